@@ -1,0 +1,419 @@
+#!/usr/bin/env python3
+"""Benchmark of the quantized decode hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one "step"): the Q4_K decode matvec sweep at batch 1 -- one y = W.x
+over each matrix of a rotation set of 16 distinct 11008x4096 and 16 distinct
+4096x4096 Q4_K matrices (557 MB > 4x the 126 MB L2, so every step streams its
+weights from HBM).  The 32 launches of a step are captured in one CUDA graph
+with programmatic dependent launch between them, like consecutive projections
+of a decode step.  Weights are synthetic (uniform 4-bit codes / 6-bit scales,
+f16 d,dmin in U[1e-4,1e-3]), x ~ N(0,1), seeded.
+
+Reported: `value` = algorithmic bytes (weights + x + y) per step / device time
+per step, device-resident inputs; `e2e` = the same through the C ABI's
+GpuDispatch surface (sb_matvec_batch: host x in, host y out, copies and the
+sync inside the timed region); `roofline` for the matvec kernel against the
+measured HBM copy bandwidth; `cpu_baseline` = the reference's AVX2 Q4_K kernel
+(restated, all host cores) on a bounded sample.  With N > 1 (torchrun) every
+rank runs its own rotation set on its own GPU (rows are independent: weak
+scaling, no collective on the data path); `value` sums all ranks over the
+slowest rank's time.
+
+--impl reference times the reference's CPU implementation of the path (the
+restated AVX2 kernel, all host threads) on the same workload, a bounded sample
+per step, and prints the same JSON line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q4_K matvec HBM GB/s (% of peak)"
+UNIT = "GB/s"
+SHAPES = [(11008, 4096), (4096, 4096)]  # BASELINE.json configs[1], Q4_K shapes
+COPIES = 16
+Q4K = 3
+
+
+def algo_bytes(rows: int, cols: int) -> int:
+    return rows * (cols // 256) * 144 + cols * 4 + rows * 4
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def profile_traffic() -> float | None:
+    """DRAM bytes per launch of the Q4_K 11008x4096 matvec from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "q4k_matvec_11008x4096.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    return None
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.p = None
+
+    def stop(self) -> dict | None:
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sms, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [t.strip() for t in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return None
+        return {"sm_mhz": float(np.median(sms)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def cpu_sample_gbs(seconds: float, threads: int) -> dict:
+    """The reference's AVX2 Q4_K matvec (gemm.rs:842-894, restated in oracle/) on the
+    host cores: both BASELINE shapes once per pass, as many passes as fit `seconds`."""
+    import oracle
+    from soso_b200 import synth
+    mats = []
+    for rows, cols in SHAPES:
+        g = synth.rng("bench", "cpu", rows, cols)
+        mats.append((synth.random_weights(Q4K, rows, cols, g), rows, cols, synth.randn(cols, g),
+                     np.empty(rows, np.float32)))
+    oracle.cpu_matvec(Q4K, mats[1][0], mats[1][1], mats[1][2], mats[1][3], threads, mats[1][4])  # warm
+    t0, passes, nbytes = time.perf_counter(), 0, 0
+    while True:
+        for w, rows, cols, x, y in mats:
+            oracle.cpu_matvec(Q4K, w, rows, cols, x, threads, y)
+            nbytes += algo_bytes(rows, cols)
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": nbytes / el / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{passes} passes of Q4_K 11008x4096 + 4096x4096 matvec ({el:.1f} s)"}
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# --------------------------------------------------------------- our arm
+def run_ours(args) -> None:
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    from soso_b200 import synth
+    from soso_b200._lib import SbMatvecOp, SbView, c_f32p, c_u8p, last_error, lib
+    L = lib()
+
+    # rotation set: COPIES distinct matrices of each shape, per rank
+    mats = []
+    for rows, cols in SHAPES:
+        for k in range(COPIES):
+            g = synth.rng("bench", rank, rows, cols, k)
+            w = synth.random_weights(Q4K, rows, cols, g)
+            x = synth.randn(cols, g)
+            mats.append((rows, cols, w, x))
+    wd = [torch.from_numpy(m[2]).to(dev) for m in mats]
+    xd = [torch.from_numpy(m[3]).to(dev) for m in mats]
+    yd = [torch.empty(m[0], device=dev, dtype=torch.float32) for m in mats]
+    step_bytes = sum(algo_bytes(m[0], m[1]) for m in mats)
+    launches_per_step = len(mats)
+
+    stream = torch.cuda.Stream(dev)
+
+    def enqueue():
+        s = torch.cuda.current_stream().cuda_stream
+        for (rows, cols, _, _), w, x, y in zip(mats, wd, xd, yd):
+            rc = L.sbk_matvec(Q4K, w.data_ptr(), rows, cols, x.data_ptr(), y.data_ptr(), 1, s)
+            if rc:
+                raise RuntimeError(f"sbk_matvec rc={rc}")
+
+    with torch.cuda.stream(stream):
+        enqueue()  # warm (sets smem attributes outside capture)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        enqueue()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    # keep the GPU busy a little longer so the sampler sees load if the region was short
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, int(200.0 / max(ms / args.steps, 1e-3)))):
+            graph.replay()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # e2e through the GpuDispatch surface: host x in, host y out, one wait per step
+    views, keys, ops = [], [], (SbMatvecOp * len(mats))()
+    hx = [np.ascontiguousarray(m[3]) for m in mats]
+    hy = [np.empty(m[0], np.float32) for m in mats]
+    import ctypes
+    h = ctypes.c_void_p()
+    if L.sb_create(local, ctypes.byref(h)) != 0:
+        raise RuntimeError(last_error())
+    ctx = h
+    for i, (rows, cols, w, _) in enumerate(mats):
+        views.append(SbView(w.ctypes.data_as(c_u8p), w.size, Q4K, rows * cols))
+        keys.append(f"bench.{i}".encode())
+    for i, (rows, cols, _, _) in enumerate(mats):
+        ops[i] = SbMatvecOp(keys[i], ctypes.pointer(views[i]), rows, cols, hx[i].ctypes.data_as(c_f32p),
+                            hy[i].ctypes.data_as(c_f32p))
+    done = (ctypes.c_uint8 * len(mats))()
+    for _ in range(max(1, args.warmup)):
+        if L.sb_matvec_batch(ctx, ops, len(mats), done) != 1:
+            raise RuntimeError(last_error())
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        L.sb_matvec_batch(ctx, ops, len(mats), done)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    L.sb_destroy(ctx)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample_gbs(args.cpu_seconds, host_threads())
+
+    if rank == 0:
+        peaks = load_peaks()
+        per_step_s = ms / 1e3 / args.steps
+        value = world * step_bytes / per_step_s / 1e9
+        per_launch_bytes = step_bytes / launches_per_step
+        achieved = per_launch_bytes / (per_step_s / launches_per_step) / 1e9
+        traffic = profile_traffic()
+        h2d = sum(m[1] * 4 for m in mats)
+        d2h = sum(m[0] * 4 for m in mats)
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "pct_of_peak": round(100.0 * value / world / peaks["hbm_gbs"], 1),
+            "config": {
+                "workload": f"Q4_K decode matvec sweep, batch 1: {COPIES}x 11008x4096 + {COPIES}x 4096x4096 "
+                            "per step (BASELINE configs[1] Q4_K shapes), one CUDA graph per step with PDL",
+                "rotation_bytes_per_gpu": int(sum(m[2].size for m in mats)),
+                "l2": "inputs larger than L2 (557 MB rotation set per GPU, each matrix read once per step)",
+                "parallelism": f"independent rotation sets per GPU x{world}",
+            },
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)",
+                         "traffic": traffic, "algorithmic_bytes_per_launch": int(per_launch_bytes),
+                         "kernel": "sb::matvec_kernel<Q4K>"},
+            "e2e": {"value": round(world * step_bytes / (e2e_s / args.steps) / 1e9, 1), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "sb_matvec_batch (GpuDispatch::matvec_lote), weights resident"},
+            "gpu_launches": args.steps * launches_per_step,
+            "clocks": clk,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        del graph
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------- reference arm
+def run_reference(args) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import oracle
+    from soso_b200 import synth
+    threads = host_threads()
+    mats = []
+    for rows, cols in SHAPES:
+        g = synth.rng("bench", "ref", rows, cols)
+        mats.append((synth.random_weights(Q4K, rows, cols, g), rows, cols, synth.randn(cols, g),
+                     np.empty(rows, np.float32)))
+    step_bytes = sum(algo_bytes(r, c) for _, r, c, _, _ in mats)
+
+    def step():
+        for w, rows, cols, x, y in mats:
+            oracle.cpu_matvec(Q4K, w, rows, cols, x, threads, y)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = step_bytes * args.steps / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "Q4_K decode matvec sweep, batch 1: one 11008x4096 + one 4096x4096 per step "
+                               "(bounded sample of BASELINE configs[1])",
+                   "parallelism": f"{threads} host threads (row_strip)"},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": "reference AVX2 Q4_K matvec (gemm.rs:842-894) restated in C, "
+                                   "row_strip-threaded (parallel.rs:22-31); one matvec per BASELINE shape per step"},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+NCU_CASES = {  # name -> (dtype, rows, cols, copies): small cases for ncu captures
+    "q4k": (Q4K, 11008, 4096, 8),
+    "q4k_4096": (Q4K, 4096, 4096, 16),
+    "q6k": (13, 4096, 11008, 6),
+    "q6k_lmhead": (13, 151936, 2048, 1),
+    "q80": (2, 4096, 4096, 8),
+}
+
+
+def run_case(name: str, launches: int) -> None:
+    """Plain launches of one kernel over a rotation of copies (for ncu); prints a check line."""
+    import torch
+
+    import oracle
+    from soso_b200 import synth
+    from soso_b200._lib import lib
+    dt, rows, cols, copies = NCU_CASES[name]
+    L = lib()
+    dev = torch.device("cuda", 0)
+    ws, xs = [], []
+    for k in range(copies):
+        g = synth.rng("case", name, k)
+        ws.append(synth.random_weights(dt, rows, cols, g))
+        xs.append(synth.randn(cols, g))
+    wd = [torch.from_numpy(w).to(dev) for w in ws]
+    xd = [torch.from_numpy(x).to(dev) for x in xs]
+    yd = torch.empty(rows, device=dev, dtype=torch.float32)
+    s = torch.cuda.current_stream().cuda_stream
+    for i in range(launches):
+        k = i % copies
+        rc = L.sbk_matvec(dt, wd[k].data_ptr(), rows, cols, xd[k].data_ptr(), yd.data_ptr(), 0, s)
+        if rc:
+            raise SystemExit(f"sbk_matvec rc={rc}")
+    torch.cuda.synchronize()
+    k = (launches - 1) % copies
+    t = oracle.matvec_f64(dt, ws[k], rows, cols, xs[k])
+    y = yd.cpu().numpy()
+    rms = float(np.sqrt(np.mean(t ** 2)))
+    err = float(np.max(np.abs(y - t) / np.maximum(np.abs(t), 1e-3 * rms)))
+    print(json.dumps({"case": name, "launches": launches, "max_rel_err": err}))
+    if err > 1e-3:
+        raise SystemExit(1)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ncu-case", choices=sorted(NCU_CASES), default=None)
+    ap.add_argument("--launches", type=int, default=12)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.ncu_case:
+        run_case(args.ncu_case, args.launches)
+        return
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,129 @@
+/*
+ * sosob200.h -- C ABI of the B200 (sm_100a) quantized decode hot path.
+ *
+ * Drop-in boundary for demonodojo/soso's `trait GpuDispatch`
+ * (crates/soso-llm-core/src/gpu.rs:338-737): a Rust `impl GpuDispatch` binds
+ * these symbols with `extern "C"`.  Plain pointers and
+ * sizes only.
+ *
+ * Two layers:
+ *   sb_*   -- the GpuDispatch surface.  Host buffers, weights resident per key
+ *             (uploaded on first sight, like CudaGpu's `pesos` map,
+ *             crates/soso-llm-api/src/cuda.rs:290, :2364-2376).  Return value:
+ *             1 = handled (outputs fully written), 0 = declined (the caller
+ *             computes on its own path), <0 = error (sb_last_error()).
+ *   sbk_*  -- the kernels themselves on DEVICE pointers, enqueued on a
+ *             caller-provided cudaStream_t (passed as void*); no host sync.
+ *             Return value: 0 = enqueued, <0 = rejected (bad shape / dtype /
+ *             alignment; nothing was launched).
+ *
+ * Weight layouts are the reference's on-disk bytes, unchanged:
+ *   Q8_0 (.som)  36 B / 32 weights: f32 scale + 32 i8   (crates/sosomodel/src/layout.rs:57-59)
+ *   Q4_K (GGML) 144 B / 256: f16 d, f16 dmin, 12 B 6-bit scales/mins, 128 B nibbles (layout.rs:63-64)
+ *   Q6_K (GGML) 210 B / 256: ql[128] qh[64] i8 sc[16] f16 d  (crates/gguf2som/src/lib.rs:1639-1661)
+ * Matrices are row-major [rows = out][cols = in]; each row is a whole number
+ * of blocks (crates/sosomodel/src/dequant.rs:47-63).
+ */
+#ifndef SOSOB200_H
+#define SOSOB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* sosomodel dtype codes (crates/sosomodel/src/layout.rs:8-12).  SB_DTYPE_Q6_K
+ * is an extension: the reference stores no Q6_K tensors (gguf2som converts
+ * them to Q8_0, crates/gguf2som/src/lib.rs:1592-1610). */
+#define SB_DTYPE_F32  1
+#define SB_DTYPE_Q8_0 2
+#define SB_DTYPE_Q4_K 3
+#define SB_DTYPE_Q6_K 13
+
+/* Mirror of `TensorView { bytes, dtype, elems }` (crates/soso-llm-core/src/layer.rs:26-31). */
+typedef struct {
+    const uint8_t *bytes;
+    size_t len;
+    uint8_t dtype;
+    size_t elems;
+} sb_view;
+
+/* Mirror of `MatvecOp` (crates/soso-llm-core/src/gpu.rs:189-196). */
+typedef struct {
+    const char *key;
+    const sb_view *view;
+    size_t rows, cols;
+    const float *x;
+    float *out;
+} sb_matvec_op;
+
+/* Mirror of `GpuStats` (crates/soso-llm-core/src/gpu.rs:17-36), the fields this backend fills. */
+typedef struct {
+    uint64_t launches;
+    uint64_t total_ns;
+    uint64_t bytes_up;
+    uint64_t bytes_down;
+} sb_stats;
+
+typedef struct sb_ctx sb_ctx;
+
+/* ---- GpuDispatch surface (host buffers) -------------------------------- */
+
+/* `CudaGpu::nueva` (crates/soso-llm-api/src/cuda.rs:440): one context per device. */
+int sb_create(int device, sb_ctx **out);
+void sb_destroy(sb_ctx *ctx);
+/* `GpuDispatch::available` (gpu.rs:339). */
+int sb_available(const sb_ctx *ctx);
+/* `GpuDispatch::dtype_soportado` (gpu.rs:343-345). */
+int sb_dtype_supported(const sb_ctx *ctx, uint8_t dtype);
+/* `GpuDispatch::matvec` (gpu.rs:432-440): out[0..rows] = W . x. */
+int sb_matvec(sb_ctx *ctx, const char *key, const sb_view *w, size_t rows, size_t cols, const float *x,
+              float *out);
+/* `GpuDispatch::matmul` (gpu.rs:443-455): out[n x rows] = X[n x cols] . W^T. */
+int sb_matmul(sb_ctx *ctx, const char *key, const sb_view *w, size_t rows, size_t cols, size_t n,
+              const float *x, float *out);
+/* `GpuDispatch::matvec_lote` (gpu.rs:694-701): independent matvecs, one wait; done[i] = 1 when ops[i] ran. */
+int sb_matvec_batch(sb_ctx *ctx, sb_matvec_op *ops, size_t nops, uint8_t *done);
+/* `GpuDispatch::rmsnorm` (gpu.rs:733-736): x *= rsqrt(mean(x^2) + eps) * w, in place. */
+int sb_rmsnorm(sb_ctx *ctx, float *x, const float *w, size_t n, float eps);
+/* Number of resident weight tensors (`CudaGpu::residentes`, used by cuda_matvec.rs:138). */
+size_t sb_resident_count(const sb_ctx *ctx);
+/* `GpuDispatch::stats` (gpu.rs:350-352). */
+int sb_get_stats(const sb_ctx *ctx, sb_stats *out);
+/* Thread-local description of the last error. */
+const char *sb_last_error(void);
+
+/* ---- kernels on device pointers --------------------------------------- */
+
+/* Bytes per row for (dtype, cols), 0 if cols is not a whole number of blocks
+ * (`sosomodel::dequant::row_bytes`, crates/sosomodel/src/dequant.rs:53-63). */
+size_t sbk_row_bytes(uint8_t dtype, size_t cols);
+
+/* y[rows] = W[rows x cols] . x[cols] for dtype Q8_0 / Q4_K / Q6_K.  Replaces
+ * `gm_matvec_q4k` / `gm_matvec_q80` (lxdde/ports/nouveau/gemma_capa.cu:433,:501)
+ * and the CPU `gemm::matvec_q4_k` / `matvec_q8_0` (crates/soso-llm-core/src/gemm.rs:295,:402).
+ * w must be 16-byte aligned.  pdl != 0 launches with programmatic dependent
+ * launch so the weight stream overlaps the previous kernel on the stream. */
+int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols, const float *x, float *y, int pdl,
+               void *stream);
+
+/* RMSNorm of `rows` rows of n floats, `gemm::rmsnorm` (crates/soso-llm-core/src/gemm.rs:93-100),
+ * optionally fused with the residual add `add_f32` (gemm.rs:265): with res != NULL,
+ * h_out = x + res and y = rmsnorm(h_out) * w; else y = rmsnorm(x) * w.  y may alias x.
+ * Replaces `gm_rmsnorm_rows` / `rmsnorm_rows_f32` (gemma_capa.cu:81-96, rmsnorm_rows.cu:13-38). */
+int sbk_rmsnorm(const float *x, const float *res, float *h_out, const float *w, float *y, size_t rows, size_t n,
+                float eps, void *stream);
+
+/* Number of SMs the kernels size their grids for. */
+int sbk_num_sms(int device);
+
+/* Device-side error word (bounded waits that gave up set it); read-and-clear. */
+int sbk_take_device_error(int device, uint32_t *code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SOSOB200_H */

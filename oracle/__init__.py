@@ -1,0 +1,199 @@
+"""CPU oracle for the quantized decode hot path -- TEST INFRASTRUCTURE ONLY.
+
+This package is the checker, never the product: only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / ``--impl reference``
+legs import it.  ``soso_b200`` (the product) never imports it and has no CPU
+fallback.
+
+The C restatement lives in ``oracle.c`` (block decoders, scalar matvecs in the
+reference's operation order, quantizers) and ``cpu_baseline.c`` (the
+reference's AVX2 kernels, threaded with ``row_strip``); ``ops.py`` restates the
+float ops (RMSNorm, RoPE, softmax/top-k, SwiGLU, attention, MoE, MLA, layer
+forward).  Each function cites the reference file:line it follows.
+
+Parity pins: ``tests/test_oracle_golden.py`` checks this oracle against the
+reference's golden vectors (crates/sosomodel/tests/dequant_golden.rs,
+crates/gguf2som/src/lib.rs:1866-1889) and against the reference's own C decoder
+``lxdde/ports/nouveau/q4k_decode.h`` compiled into ``oracle/_ref/``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libq4kref.so")
+
+F32, Q8_0, Q4_K, Q6_K = 1, 2, 3, 13
+BLOCK = {Q8_0: (32, 36), Q4_K: (256, 144), Q6_K: (256, 210)}
+
+_lib = None
+_ref = None
+
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_f64p = ctypes.POINTER(ctypes.c_double)
+
+
+def build(force: bool = False) -> None:
+    """Compile liboracle.so (and _ref/ when the reference checkout exists)."""
+    if force or not os.path.exists(LIB_PATH):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(LIB_PATH)
+        L.or_f16_to_f32.restype = ctypes.c_float
+        L.or_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.or_f32_to_f16.restype = ctypes.c_uint16
+        L.or_f32_to_f16.argtypes = [ctypes.c_float]
+        L.or_row_bytes.restype = ctypes.c_size_t
+        L.or_row_bytes.argtypes = [ctypes.c_uint8, ctypes.c_size_t]
+        L.or_q4k_scale_min.argtypes = [_u8p, ctypes.c_int, _u8p, _u8p]
+        L.or_q4k_dot_sub.restype = ctypes.c_float
+        L.or_q4k_dot_sub.argtypes = [_u8p, ctypes.c_int, _f32p]
+        L.or_q4k_dot_ref.restype = ctypes.c_float
+        L.or_q4k_dot_ref.argtypes = [_u8p, _f32p]
+        for n in ("or_dequant_q8_0", "or_dequant_q4_k", "or_dequant_q6_k"):
+            f = getattr(L, n)
+            f.restype = ctypes.c_int
+            f.argtypes = [_u8p, ctypes.c_size_t, _f32p, ctypes.c_size_t]
+        L.or_dequant.restype = ctypes.c_int
+        L.or_dequant.argtypes = [ctypes.c_uint8, _u8p, ctypes.c_size_t, _f32p, ctypes.c_size_t]
+        L.or_matvec.restype = ctypes.c_int
+        L.or_matvec.argtypes = [ctypes.c_uint8, _u8p, ctypes.c_size_t, ctypes.c_size_t, _f32p, _f32p]
+        L.or_matvec_f64.restype = ctypes.c_int
+        L.or_matvec_f64.argtypes = [ctypes.c_uint8, _u8p, ctypes.c_size_t, ctypes.c_size_t, _f32p,
+                                    ctypes.c_size_t, _f64p]
+        L.or_cpu_matvec.restype = ctypes.c_int
+        L.or_cpu_matvec.argtypes = [ctypes.c_uint8, _u8p, ctypes.c_size_t, ctypes.c_size_t, _f32p, _f32p,
+                                    ctypes.c_int]
+        for n in ("or_quantize_q8_0", "or_quantize_q4_k", "or_quantize_q6_k"):
+            f = getattr(L, n)
+            f.restype = None
+            f.argtypes = [_f32p, ctypes.c_size_t, _u8p]
+        L.or_dequant_q6_k_block.argtypes = [_u8p, _f32p]
+        L.or_row_strip.argtypes = [ctypes.c_size_t] * 3 + [ctypes.POINTER(ctypes.c_size_t)] * 2
+        _lib = L
+    return _lib
+
+
+def ref_lib():
+    """The reference's own q4k_decode.h, compiled from source; None if absent."""
+    global _ref
+    if _ref is None and os.path.exists(REF_PATH):
+        R = ctypes.CDLL(REF_PATH)
+        R.ref_q4k_f16.restype = ctypes.c_float
+        R.ref_q4k_f16.argtypes = [ctypes.c_ushort]
+        R.ref_q4k_scale_min.argtypes = [_u8p, ctypes.c_int, _u8p, _u8p]
+        R.ref_q4k_dot_sub.restype = ctypes.c_float
+        R.ref_q4k_dot_sub.argtypes = [_u8p, ctypes.c_int, _f32p]
+        R.ref_q4k_dot_block.restype = ctypes.c_float
+        R.ref_q4k_dot_block.argtypes = [_u8p, _f32p]
+        R.ref_q80_dot_block.restype = ctypes.c_float
+        R.ref_q80_dot_block.argtypes = [_u8p, _f32p]
+        _ref = R
+    return _ref
+
+
+def _u8(a: np.ndarray):
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    return a, a.ctypes.data_as(_u8p)
+
+
+def _f32(a: np.ndarray):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    return a, a.ctypes.data_as(_f32p)
+
+
+def f16_to_f32(bits: int) -> float:
+    return lib().or_f16_to_f32(bits)
+
+
+def f32_to_f16(v: float) -> int:
+    return lib().or_f32_to_f16(v)
+
+
+def row_bytes(dtype: int, cols: int) -> int | None:
+    rb = lib().or_row_bytes(dtype, cols)
+    return rb or None
+
+
+def q4k_scale_min(scales: bytes, j: int) -> tuple[int, int]:
+    s, p = _u8(np.frombuffer(bytes(scales), dtype=np.uint8))
+    sc, m = ctypes.c_uint8(), ctypes.c_uint8()
+    lib().or_q4k_scale_min(p, j, ctypes.byref(sc), ctypes.byref(m))
+    return sc.value, m.value
+
+
+def q4k_dot_ref(blk: np.ndarray, x: np.ndarray) -> float:
+    b, bp = _u8(blk)
+    xx, xp = _f32(x)
+    return lib().or_q4k_dot_ref(bp, xp)
+
+
+def dequant(dtype: int, w: np.ndarray, n: int) -> np.ndarray:
+    b, bp = _u8(w)
+    out = np.empty(n, dtype=np.float32)
+    rc = lib().or_dequant(dtype, bp, b.size, out.ctypes.data_as(_f32p), n)
+    if rc:
+        raise ValueError(f"dequant rc={rc}")
+    return out
+
+
+def matvec(dtype: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    """Reference-order f32 matvec (gemm.rs scalar kernels)."""
+    b, bp = _u8(w)
+    xx, xp = _f32(x)
+    out = np.empty(rows, dtype=np.float32)
+    rc = lib().or_matvec(dtype, bp, rows, cols, xp, out.ctypes.data_as(_f32p))
+    if rc:
+        raise ValueError(f"matvec rc={rc}")
+    return out
+
+
+def matvec_f64(dtype: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray, n: int = 1) -> np.ndarray:
+    """Exact-dequant, f64-accumulated truth; x is n vectors of cols, out n x rows."""
+    b, bp = _u8(w)
+    xx, xp = _f32(x)
+    out = np.empty(n * rows, dtype=np.float64)
+    rc = lib().or_matvec_f64(dtype, bp, rows, cols, xp, n, out.ctypes.data_as(_f64p))
+    if rc:
+        raise ValueError(f"matvec_f64 rc={rc}")
+    return out
+
+
+def cpu_matvec(dtype: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray, threads: int = 1,
+               out: np.ndarray | None = None) -> np.ndarray:
+    """The reference's AVX2 kernels (gemm.rs:806-894), row_strip-threaded."""
+    b, bp = _u8(w)
+    xx, xp = _f32(x)
+    if out is None:
+        out = np.empty(rows, dtype=np.float32)
+    rc = lib().or_cpu_matvec(dtype, bp, rows, cols, xp, out.ctypes.data_as(_f32p), threads)
+    if rc:
+        raise ValueError(f"cpu_matvec rc={rc}")
+    return out
+
+
+def quantize(dtype: int, v: np.ndarray) -> np.ndarray:
+    v, vp = _f32(v)
+    be, bb = BLOCK[dtype]
+    nb = (v.size + be - 1) // be
+    out = np.zeros(nb * bb, dtype=np.uint8)
+    fn = {Q8_0: lib().or_quantize_q8_0, Q4_K: lib().or_quantize_q4_k, Q6_K: lib().or_quantize_q6_k}[dtype]
+    fn(vp, v.size, out.ctypes.data_as(_u8p))
+    return out
+
+
+def row_strip(rows: int, i: int, n: int) -> tuple[int, int]:
+    s, e = ctypes.c_size_t(), ctypes.c_size_t()
+    lib().or_row_strip(rows, i, n, ctypes.byref(s), ctypes.byref(e))
+    return s.value, e.value

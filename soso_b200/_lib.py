@@ -1,0 +1,84 @@
+"""ctypes binding of libsosob200.so -- the only way Python reaches the kernels.
+
+There is no fallback: if the library is missing or cannot be loaded, every
+entry point raises.  The declarations follow include/sosob200.h.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import build as _build
+
+c_u8p = ctypes.POINTER(ctypes.c_uint8)
+c_f32p = ctypes.POINTER(ctypes.c_float)
+c_size = ctypes.c_size_t
+
+
+class SbView(ctypes.Structure):
+    _fields_ = [("bytes", c_u8p), ("len", c_size), ("dtype", ctypes.c_uint8), ("elems", c_size)]
+
+
+class SbMatvecOp(ctypes.Structure):
+    _fields_ = [("key", ctypes.c_char_p), ("view", ctypes.POINTER(SbView)), ("rows", c_size), ("cols", c_size),
+                ("x", c_f32p), ("out", c_f32p)]
+
+
+class SbStats(ctypes.Structure):
+    _fields_ = [("launches", ctypes.c_uint64), ("total_ns", ctypes.c_uint64), ("bytes_up", ctypes.c_uint64),
+                ("bytes_down", ctypes.c_uint64)]
+
+
+# name -> (restype, argtypes); must match include/sosob200.h
+SIGNATURES = {
+    "sb_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
+    "sb_destroy": (None, [ctypes.c_void_p]),
+    "sb_available": (ctypes.c_int, [ctypes.c_void_p]),
+    "sb_dtype_supported": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint8]),
+    "sb_matvec": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(SbView), c_size, c_size, c_f32p,
+                                 c_f32p]),
+    "sb_matmul": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(SbView), c_size, c_size, c_size,
+                                 c_f32p, c_f32p]),
+    "sb_matvec_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbMatvecOp), c_size, c_u8p]),
+    "sb_rmsnorm": (ctypes.c_int, [ctypes.c_void_p, c_f32p, c_f32p, c_size, ctypes.c_float]),
+    "sb_resident_count": (c_size, [ctypes.c_void_p]),
+    "sb_get_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbStats)]),
+    "sb_last_error": (ctypes.c_char_p, []),
+    "sbk_row_bytes": (c_size, [ctypes.c_uint8, c_size]),
+    "sbk_matvec": (ctypes.c_int, [ctypes.c_uint8, ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p,
+                                  ctypes.c_int, ctypes.c_void_p]),
+    "sbk_rmsnorm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                   ctypes.c_void_p, c_size, c_size, ctypes.c_float, ctypes.c_void_p]),
+    "sbk_num_sms": (ctypes.c_int, [ctypes.c_int]),
+    "sbk_take_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
+}
+
+_L = None
+
+
+def lib():
+    """Load (building first if the sources are newer) and declare the library."""
+    global _L
+    if _L is None:
+        path = _build.LIB
+        if not os.path.exists(path) or _build.stale():
+            try:
+                _build.build()
+            except Exception as e:  # no nvcc on this host and no prebuilt library
+                if not os.path.exists(path):
+                    raise RuntimeError(f"libsosob200.so is missing and could not be built: {e}") from e
+        L = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _L = L
+    return _L
+
+
+def last_error() -> str:
+    return (lib().sb_last_error() or b"").decode(errors="replace")
+
+
+class SbError(RuntimeError):
+    """An `Err(())` of the GpuDispatch contract: the call failed on the device."""

@@ -1,0 +1,300 @@
+// dispatch.cuh -- the GpuDispatch surface (sb_*): host buffers in, host
+// buffers out, weights resident per key.
+//
+// Mirrors CudaGpu (crates/soso-llm-api/src/cuda.rs): weights are uploaded on
+// first sight and kept under their stable key (`pesos`, cuda.rs:290); a failed
+// upload is remembered and not retried (cuda.rs:2364-2376); the device is made
+// current on every call (cuda.rs:2362); shapes a kernel does not take are
+// declined with 0 rather than failed (crates/soso-llm-api/tests/cuda_matvec.rs
+// :275-282).  Unlike the reference there is no silent fallback in here: a
+// declined op returns 0 and the caller decides.
+#pragma once
+#include <chrono>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "sosob200.h"
+
+extern "C" int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols, const float *x, float *y,
+                          int pdl, void *stream);
+extern "C" int sbk_rmsnorm(const float *x, const float *res, float *h_out, const float *w, float *y, size_t rows,
+                           size_t n, float eps, void *stream);
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(const char *where, cudaError_t e)
+{
+    t_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+    return -1;
+}
+
+int fail(const std::string &msg)
+{
+    t_last_error = msg;
+    return -1;
+}
+
+struct Resident {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    uint8_t dtype = 0;
+    bool ok = false;
+};
+
+bool kernel_dtype(uint8_t d) { return d == SB_DTYPE_Q8_0 || d == SB_DTYPE_Q4_K || d == SB_DTYPE_Q6_K; }
+
+}  // namespace
+
+struct sb_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    std::unordered_map<std::string, Resident> weights;
+    void *scratch = nullptr;  // device staging for x / out of host calls
+    size_t scratch_bytes = 0;
+    sb_stats stats = {};
+
+    int ensure_scratch(size_t bytes)
+    {
+        if (bytes <= scratch_bytes) return 0;
+        if (scratch) cudaFree(scratch);
+        scratch = nullptr;
+        scratch_bytes = 0;
+        size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+        cudaError_t e = cudaMalloc(&scratch, want);
+        if (e != cudaSuccess) return fail("cudaMalloc(scratch)", e);
+        scratch_bytes = want;
+        return 0;
+    }
+
+    // 1 = resident, 0 = declined (remembered failure or shape), <0 = error
+    int resident(const char *key, const sb_view *v, size_t rows, size_t cols, Resident **out)
+    {
+        auto it = weights.find(key);
+        if (it != weights.end()) {
+            if (!it->second.ok) return 0;
+            if (it->second.bytes != v->len || it->second.dtype != v->dtype)
+                return fail(std::string("key '") + key + "' re-used with a different tensor");
+            *out = &it->second;
+            return 1;
+        }
+        Resident r;
+        r.bytes = v->len;
+        r.dtype = v->dtype;
+        // +64 B so vectorised/bulk reads that round a range up to 16 B stay inside the allocation
+        cudaError_t e = cudaMalloc(&r.ptr, v->len + 64);
+        if (e == cudaSuccess) e = cudaMemcpy(r.ptr, v->bytes, v->len, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            if (r.ptr) cudaFree(r.ptr);
+            r.ptr = nullptr;
+            weights[key] = r;  // remembered: not retried
+            cudaGetLastError();
+            return 0;
+        }
+        r.ok = true;
+        stats.bytes_up += v->len;
+        auto res = weights.emplace(key, r);
+        *out = &res.first->second;
+        (void)rows;
+        (void)cols;
+        return 1;
+    }
+};
+
+namespace {
+
+// Shape/dtype admission shared by matvec/matmul: 1 ok, 0 decline.
+int admit(const sb_view *w, size_t rows, size_t cols)
+{
+    if (!w || !w->bytes || !kernel_dtype(w->dtype)) return 0;
+    if (w->elems != rows * cols || rows == 0) return 0;
+    size_t rb = sbk_row_bytes(w->dtype, cols);
+    if (!rb || w->len != rb * rows || cols > 65536) return 0;
+    return 1;
+}
+
+uint64_t now_ns()
+{
+    return (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+               std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+}  // namespace
+
+extern "C" int sb_create(int device, sb_ctx **out)
+{
+    if (!out) return fail("sb_create: null out");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return fail("cudaGetDeviceCount", e);
+    if (device < 0 || device >= n) return fail("sb_create: no such device");
+    if ((e = cudaSetDevice(device)) != cudaSuccess) return fail("cudaSetDevice", e);
+    cudaDeviceProp prop;
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return fail("cudaGetDeviceProperties", e);
+    if (prop.major != 10) return fail("sb_create: kernels are built for sm_100a only");
+    sb_ctx *c = new sb_ctx();
+    c->device = device;
+    if ((e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking)) != cudaSuccess) {
+        delete c;
+        return fail("cudaStreamCreate", e);
+    }
+    *out = c;
+    return 0;
+}
+
+extern "C" void sb_destroy(sb_ctx *c)
+{
+    if (!c) return;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    for (auto &kv : c->weights)
+        if (kv.second.ptr) cudaFree(kv.second.ptr);
+    if (c->scratch) cudaFree(c->scratch);
+    cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+extern "C" int sb_available(const sb_ctx *c) { return c ? 1 : 0; }
+
+extern "C" int sb_dtype_supported(const sb_ctx *c, uint8_t dtype) { return c && kernel_dtype(dtype) ? 1 : 0; }
+
+extern "C" size_t sb_resident_count(const sb_ctx *c)
+{
+    if (!c) return 0;
+    size_t n = 0;
+    for (auto &kv : c->weights) n += kv.second.ok ? 1 : 0;
+    return n;
+}
+
+extern "C" int sb_get_stats(const sb_ctx *c, sb_stats *out)
+{
+    if (!c || !out) return -1;
+    *out = c->stats;
+    return 0;
+}
+
+extern "C" const char *sb_last_error(void) { return t_last_error.c_str(); }
+
+// y (n x rows) = X (n x cols) . W^T ; n == 1 is the matvec.
+static int run_matvecs(sb_ctx *c, const char *key, const sb_view *w, size_t rows, size_t cols, size_t n,
+                       const float *x, float *out)
+{
+    if (!c) return fail("null context");
+    if (!key || !x || !out) return fail("null argument");
+    if (!admit(w, rows, cols) || n == 0) return 0;
+    std::lock_guard<std::mutex> lk(c->mu);
+    const uint64_t t0 = now_ns();
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return fail("cudaSetDevice", e);
+    Resident *r = nullptr;
+    int rc = c->resident(key, w, rows, cols, &r);
+    if (rc <= 0) return rc;
+    const size_t xb = n * cols * 4, yb = n * rows * 4, xoff = (xb + 255) & ~(size_t)255;
+    if (c->ensure_scratch(xoff + yb)) return -1;
+    float *dx = (float *)c->scratch, *dy = (float *)((char *)c->scratch + xoff);
+    if ((e = cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+        return fail("cudaMemcpyAsync(x)", e);
+    for (size_t t = 0; t < n; t++) {
+        int k = sbk_matvec(w->dtype, r->ptr, rows, cols, dx + t * cols, dy + t * rows, 0, c->stream);
+        if (k) return fail("sbk_matvec launch failed (" + std::to_string(k) + ")");
+        c->stats.launches++;
+    }
+    if ((e = cudaMemcpyAsync(out, dy, yb, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
+        return fail("cudaMemcpyAsync(out)", e);
+    if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", e);
+    c->stats.bytes_up += xb;
+    c->stats.bytes_down += yb;
+    c->stats.total_ns += now_ns() - t0;
+    return 1;
+}
+
+extern "C" int sb_matvec(sb_ctx *c, const char *key, const sb_view *w, size_t rows, size_t cols, const float *x,
+                         float *out)
+{
+    return run_matvecs(c, key, w, rows, cols, 1, x, out);
+}
+
+extern "C" int sb_matmul(sb_ctx *c, const char *key, const sb_view *w, size_t rows, size_t cols, size_t n,
+                         const float *x, float *out)
+{
+    return run_matvecs(c, key, w, rows, cols, n, x, out);
+}
+
+extern "C" int sb_matvec_batch(sb_ctx *c, sb_matvec_op *ops, size_t nops, uint8_t *done)
+{
+    if (!c) return fail("null context");
+    if (!ops || !done) return fail("null argument");
+    std::lock_guard<std::mutex> lk(c->mu);
+    const uint64_t t0 = now_ns();
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return fail("cudaSetDevice", e);
+    // pass 1: residency + scratch layout
+    std::vector<Resident *> res(nops, nullptr);
+    std::vector<size_t> xo(nops), yo(nops);
+    size_t off = 0;
+    for (size_t i = 0; i < nops; i++) {
+        done[i] = 0;
+        sb_matvec_op &op = ops[i];
+        if (!op.key || !op.x || !op.out || !admit(op.view, op.rows, op.cols)) continue;
+        int rc = c->resident(op.key, op.view, op.rows, op.cols, &res[i]);
+        if (rc < 0) return rc;
+        if (rc == 0) res[i] = nullptr;
+        if (!res[i]) continue;
+        xo[i] = off;
+        off += (op.cols * 4 + 255) & ~(size_t)255;
+        yo[i] = off;
+        off += (op.rows * 4 + 255) & ~(size_t)255;
+    }
+    if (off == 0) return 1;
+    if (c->ensure_scratch(off)) return -1;
+    char *base = (char *)c->scratch;
+    for (size_t i = 0; i < nops; i++) {
+        if (!res[i]) continue;
+        sb_matvec_op &op = ops[i];
+        if ((e = cudaMemcpyAsync(base + xo[i], op.x, op.cols * 4, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+            return fail("cudaMemcpyAsync(x)", e);
+        int k = sbk_matvec(op.view->dtype, res[i]->ptr, op.rows, op.cols, (const float *)(base + xo[i]),
+                           (float *)(base + yo[i]), 0, c->stream);
+        if (k) return fail("sbk_matvec launch failed");
+        if ((e = cudaMemcpyAsync(op.out, base + yo[i], op.rows * 4, cudaMemcpyDeviceToHost, c->stream)) !=
+            cudaSuccess)
+            return fail("cudaMemcpyAsync(out)", e);
+        c->stats.launches++;
+        c->stats.bytes_up += op.cols * 4;
+        c->stats.bytes_down += op.rows * 4;
+    }
+    if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", e);
+    for (size_t i = 0; i < nops; i++) done[i] = res[i] ? 1 : 0;
+    c->stats.total_ns += now_ns() - t0;
+    return 1;
+}
+
+extern "C" int sb_rmsnorm(sb_ctx *c, float *x, const float *w, size_t n, float eps)
+{
+    if (!c) return fail("null context");
+    if (!x || !w) return fail("null argument");
+    if (n == 0) return 0;
+    std::lock_guard<std::mutex> lk(c->mu);
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return fail("cudaSetDevice", e);
+    const size_t b = (n * 4 + 255) & ~(size_t)255;
+    if (c->ensure_scratch(2 * b)) return -1;
+    float *dx = (float *)c->scratch, *dw = (float *)((char *)c->scratch + b);
+    if ((e = cudaMemcpyAsync(dx, x, n * 4, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+        return fail("cudaMemcpyAsync", e);
+    if ((e = cudaMemcpyAsync(dw, w, n * 4, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+        return fail("cudaMemcpyAsync", e);
+    if (sbk_rmsnorm(dx, nullptr, nullptr, dw, dx, 1, n, eps, c->stream)) return fail("sbk_rmsnorm launch failed");
+    if ((e = cudaMemcpyAsync(x, dx, n * 4, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
+        return fail("cudaMemcpyAsync", e);
+    if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", e);
+    c->stats.launches++;
+    return 1;
+}

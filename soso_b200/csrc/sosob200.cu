@@ -1,0 +1,6 @@
+// sosob200.cu -- the whole device library as one translation unit (so the
+// device-side globals in common.cuh have exactly one definition).
+#include "common.cuh"
+#include "matvec.cuh"
+#include "norm.cuh"
+#include "dispatch.cuh"

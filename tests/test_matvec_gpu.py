@@ -1,0 +1,286 @@
+"""GPU parity of the sm_100a matvec kernels against the CPU oracle.
+
+Through both C-ABI layers: sb_matvec / sb_matmul (host buffers, the
+GpuDispatch surface) and sbk_matvec (device pointers).  Cases follow the
+reference's own tests (crates/sosomodel/tests/dequant_golden.rs,
+crates/soso-llm-api/tests/cuda_matvec.rs) and BASELINE.json configs 1-2.
+"""
+import ctypes
+import os
+import threading
+
+import numpy as np
+import pytest
+
+import oracle
+from soso_b200 import synth
+from soso_b200._lib import lib
+from soso_b200.dispatch import CudaGpu, MatvecOp, TensorView, try_gpu_matvec
+from soso_b200.formats import DTYPE_Q4_K, DTYPE_Q6_K, DTYPE_Q8_0, row_bytes
+from tests._util import assert_matvec_close, cerca
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "q4k_ref_blocks.npz")
+ESCALAS_F16 = [0x2400, 0x2800, 0x2C00, 0x3000]  # cuda_matvec.rs:17-18
+
+
+def view(dt, w, rows, cols):
+    return TensorView(np.ascontiguousarray(w, dtype=np.uint8), dt, rows * cols)
+
+
+def dev_matvec(dt, w, rows, cols, x, pdl=0):
+    """sbk_matvec on torch device buffers; returns y on host."""
+    import torch
+    wd = torch.from_numpy(np.ascontiguousarray(w)).cuda()
+    xd = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
+    yd = torch.full((rows,), float("nan"), device="cuda", dtype=torch.float32)
+    s = torch.cuda.current_stream()
+    rc = lib().sbk_matvec(dt, wd.data_ptr(), rows, cols, xd.data_ptr(), yd.data_ptr(), pdl, s.cuda_stream)
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+    return yd.cpu().numpy()
+
+
+# ---------------------------------------------------------------- KATs
+def test_kat_q4k_block_dot(gpu):
+    from tests.test_oracle_golden import bloque_q4k, x_256
+    out = np.zeros(1, dtype=np.float32)
+    assert gpu.matvec("kat.q4k", view(DTYPE_Q4_K, bloque_q4k(), 1, 256), 1, 256, x_256(), out)
+    assert abs(out[0] - (-15.875)) <= 1e-2
+
+
+def test_kat_q80_block_dot(gpu):
+    b = np.zeros(36, dtype=np.uint8)
+    b[0:4] = np.array([0.25], dtype=np.float32).view(np.uint8)
+    b[4:] = np.array([(i * 9 - 100) for i in range(32)]).astype(np.int8).view(np.uint8)
+    xs = np.array([((i % 13) - 6.0) * 0.125 for i in range(32)], dtype=np.float32)
+    out = np.zeros(1, dtype=np.float32)
+    assert gpu.matvec("kat.q80", view(DTYPE_Q8_0, b, 1, 32), 1, 32, xs, out)
+    assert abs(out[0] - 172.59375) <= 1e-3
+
+
+def test_kat_q6k_minus_one(gpu):
+    q6 = np.zeros(210, dtype=np.uint8)
+    q6[192:208] = 1
+    d = oracle.f32_to_f16(1.0 / 32.0)
+    q6[208], q6[209] = d & 0xFF, d >> 8
+    out = np.zeros(1, dtype=np.float32)
+    assert gpu.matvec("kat.q6k", view(DTYPE_Q6_K, q6, 1, 256), 1, 256, np.ones(256, np.float32), out)
+    assert out[0] == -256.0
+
+
+def test_reference_c_decoder_blocks(gpu):
+    """Each block of the golden npz (outputs of the reference's q4k_decode.h) as a 1x256 matvec."""
+    g = np.load(GOLD)
+    q4, x, want = g["q4"], g["x"], g["dot_block"]
+    for i in range(q4.shape[0]):
+        out = np.zeros(1, dtype=np.float32)
+        assert gpu.matvec(f"gold.{i}", view(DTYPE_Q4_K, q4[i], 1, 256), 1, 256, x[i], out)
+        t = oracle.matvec_f64(DTYPE_Q4_K, q4[i], 1, 256, x[i])[0]
+        # against f64 truth at the reference's tolerance, and near the reference's f32 value
+        assert abs(out[0] - t) <= 2e-4 * (1 + abs(t)), i
+        assert abs(out[0] - want[i]) <= 1e-3 * (1 + abs(want[i])), i
+
+
+# ----------------------------------------------- reference test recipes
+def test_cuda_matvec_recipe_q8_0(gpu):
+    """cuda_matvec.rs:58-123: Q8_0 300x3840, scale 0.02, LCG codes, x in [-1,1]."""
+    e = synth.Lcg(12345)
+    rows, cols = 300, 3840
+    w = np.empty((rows * cols // 32, 36), dtype=np.uint8)
+    w[:, 0:4] = np.array([0.02], dtype=np.float32).view(np.uint8)
+    for b in range(w.shape[0]):
+        w[b, 4:] = [e.next() & 0xFF for _ in range(32)]
+    w = w.reshape(-1)
+    x = np.array([(e.next() % 2001) / 1000.0 - 1.0 for _ in range(cols)], dtype=np.float32)
+    y = np.zeros(rows, dtype=np.float32)
+    assert gpu.matvec("q8", view(DTYPE_Q8_0, w, rows, cols), rows, cols, x, y)
+    cerca(y, oracle.matvec_f64(DTYPE_Q8_0, w, rows, cols, x), "Q8_0")
+
+
+def test_cuda_matvec_recipe_q4k_and_reject(gpu):
+    """cuda_matvec.rs:213-283: Q4_K 200x2304 (LCG bytes, f16 scale table), n = 1 and 5;
+    cols not a multiple of 256 is declined without error."""
+    e = synth.Lcg(777)
+    rows, cols = 200, 2304
+    blocks = []
+    for _ in range(rows * cols // 256):
+        b = np.empty(144, dtype=np.uint8)
+        b[0:2] = np.array([ESCALAS_F16[e.next() % 4]], dtype=np.uint16).view(np.uint8)
+        b[2:4] = np.array([ESCALAS_F16[e.next() % 4]], dtype=np.uint16).view(np.uint8)
+        b[4:] = [e.next() & 0xFF for _ in range(140)]
+        blocks.append(b)
+    w = np.concatenate(blocks)
+    v = view(DTYPE_Q4_K, w, rows, cols)
+    for n in (1, 5):
+        x = np.array([(e.next() % 2001) / 1000.0 - 1.0 for _ in range(n * cols)], dtype=np.float32)
+        y = np.zeros(n * rows, dtype=np.float32)
+        ok = gpu.matvec("k", v, rows, cols, x, y) if n == 1 else gpu.matmul("k", v, rows, cols, n, x, y)
+        assert ok
+        cerca(y, oracle.matvec_f64(DTYPE_Q4_K, w, rows, cols, x, n), f"Q4_K n={n}")
+    corto = TensorView(w[:144].copy(), DTYPE_Q4_K, 256)
+    assert not gpu.matvec("raro", corto, 2, 128, np.zeros(128, np.float32), np.zeros(2, np.float32))
+
+
+# ------------------------------------------------------ BASELINE shapes
+SHAPES = [
+    (DTYPE_Q8_0, 4096, 4096, "C1"),
+    (DTYPE_Q4_K, 4096, 4096, "C2"),
+    (DTYPE_Q4_K, 11008, 4096, "C2"),
+    (DTYPE_Q6_K, 4096, 11008, "C2"),
+    (DTYPE_Q6_K, 151936, 2048, "C2 lm_head"),
+    (DTYPE_Q8_0, 2048, 10944, "C5 dense down"),
+    (DTYPE_Q8_0, 2048, 1408, "C5 expert down"),
+    (DTYPE_Q4_K, 256, 2048, "C3 k/v"),
+    (DTYPE_Q4_K, 1408, 2048, "C5 expert gate"),
+]
+
+
+@pytest.mark.parametrize("dt,rows,cols,tag", SHAPES)
+def test_baseline_shapes(dt, rows, cols, tag):
+    g = synth.rng("test", tag, dt, rows, cols)
+    w = synth.random_weights(dt, rows, cols, g)
+    x = synth.randn(cols, g)
+    y = dev_matvec(dt, w, rows, cols, x)
+    assert not np.any(np.isnan(y)), "unwritten outputs"
+    assert_matvec_close(y, oracle.matvec_f64(dt, w, rows, cols, x), f"{tag} {rows}x{cols}")
+    yo = oracle.matvec(dt, w, rows, cols, x)  # reference-order f32, reported distance
+    assert_matvec_close(yo, oracle.matvec_f64(dt, w, rows, cols, x), "oracle f32")
+
+
+# ------------------------------------------------------------ edge shapes
+EDGE = [(dt, r, c) for dt in (DTYPE_Q4_K, DTYPE_Q6_K, DTYPE_Q8_0)
+        for r, c in ((1, 256), (1, 4096), (2, 256), (3, 512), (7, 768), (31, 256), (33, 1024), (100, 256),
+                     (149, 512), (297, 1280), (1000, 256), (5, 16384))]
+
+
+@pytest.mark.parametrize("dt,rows,cols", EDGE)
+def test_edge_shapes(dt, rows, cols):
+    g = synth.rng("edge", dt, rows, cols)
+    w = synth.random_weights(dt, rows, cols, g)
+    x = synth.randn(cols, g)
+    y = dev_matvec(dt, w, rows, cols, x, pdl=rows % 2)
+    assert not np.any(np.isnan(y))
+    assert_matvec_close(y, oracle.matvec_f64(dt, w, rows, cols, x), f"{dt} {rows}x{cols}")
+
+
+def test_quantized_real_weights():
+    """Weights from the reference quantizers (quant.rs:8-154) rather than random bytes."""
+    g = np.random.default_rng(44)
+    for dt in (DTYPE_Q4_K, DTYPE_Q8_0, DTYPE_Q6_K):
+        rows, cols = 300, 2048
+        w = oracle.quantize(dt, (g.standard_normal(rows * cols) / np.sqrt(cols)).astype(np.float32))
+        x = g.standard_normal(cols).astype(np.float32)
+        assert_matvec_close(dev_matvec(dt, w, rows, cols, x), oracle.matvec_f64(dt, w, rows, cols, x), dt)
+
+
+def test_extreme_activations():
+    """Large and tiny activations stay within tolerance (x is pre-scaled by up to 2^89)."""
+    g = np.random.default_rng(45)
+    rows, cols = 64, 1024
+    for dt in (DTYPE_Q4_K, DTYPE_Q8_0, DTYPE_Q6_K):
+        w = synth.random_weights(dt, rows, cols, g)
+        for scale in (1e-6, 1e4, 1e8):
+            x = (g.standard_normal(cols) * scale).astype(np.float32)
+            assert_matvec_close(dev_matvec(dt, w, rows, cols, x), oracle.matvec_f64(dt, w, rows, cols, x),
+                                f"{dt} x*{scale}")
+
+
+def test_deterministic_across_runs():
+    g = np.random.default_rng(46)
+    w = synth.random_weights(DTYPE_Q4_K, 4096, 4096, g)
+    x = synth.randn(4096, g)
+    a = dev_matvec(DTYPE_Q4_K, w, 4096, 4096, x)
+    b = dev_matvec(DTYPE_Q4_K, w, 4096, 4096, x, pdl=1)
+    assert np.array_equal(a, b)
+
+
+# ---------------------------------------------------- dispatch semantics
+def test_dispatch_residency_and_decline():
+    gpu = CudaGpu(0)
+    try:
+        g = np.random.default_rng(1)
+        w = synth.random_weights(DTYPE_Q4_K, 64, 512, g)
+        v = view(DTYPE_Q4_K, w, 64, 512)
+        x = synth.randn(512, g)
+        y = np.zeros(64, np.float32)
+        assert gpu.available() and gpu.dtype_soportado(DTYPE_Q4_K) and not gpu.dtype_soportado(7)
+        assert gpu.matvec("L00.attn_q", v, 64, 512, x, y)
+        assert gpu.matvec("L00.attn_q", v, 64, 512, x, y)
+        assert gpu.residentes() == 1
+        # elems mismatch / unsupported dtype: declined, not an error
+        assert not gpu.matvec("bad", TensorView(v.bytes, DTYPE_Q4_K, 7), 64, 512, x, y)
+        assert not gpu.matvec("f32", TensorView(np.zeros(16, np.uint8), 1, 4), 2, 2, x, y)
+        assert not try_gpu_matvec(gpu, "mxfp4", TensorView(np.zeros(20, np.uint8), 4, 32), 1, 32, x, y)
+        st = gpu.stats()
+        assert st.launches == 2 and st.bytes_up >= w.size
+        assert_matvec_close(y, oracle.matvec_f64(DTYPE_Q4_K, w, 64, 512, x))
+    finally:
+        gpu.close()
+
+
+def test_matvec_lote(gpu):
+    g = np.random.default_rng(2)
+    ops, refs = [], []
+    for i, (dt, r, c) in enumerate([(DTYPE_Q4_K, 300, 1024), (DTYPE_Q8_0, 100, 512), (DTYPE_Q6_K, 77, 768),
+                                    (7, 8, 256)]):
+        if dt == 7:
+            ops.append(MatvecOp(f"lote.{i}", TensorView(np.zeros(8 * 144, np.uint8), 7, 8 * 256), 8, 256,
+                                np.zeros(256, np.float32), np.zeros(8, np.float32)))
+            refs.append(None)
+            continue
+        w = synth.random_weights(dt, r, c, g)
+        x = synth.randn(c, g)
+        ops.append(MatvecOp(f"lote.{i}", view(dt, w, r, c), r, c, x, np.zeros(r, np.float32)))
+        refs.append(oracle.matvec_f64(dt, w, r, c, x))
+    hecho = [False] * len(ops)
+    gpu.matvec_lote(ops, hecho)
+    assert hecho == [True, True, True, False]
+    for op, ref in zip(ops, refs):
+        if ref is not None:
+            assert_matvec_close(op.out, ref, op.key)
+
+
+def test_rmsnorm(gpu):
+    g = np.random.default_rng(3)
+    for n in (1, 100, 2048, 4096):
+        x = g.standard_normal(n).astype(np.float32)
+        w = g.standard_normal(n).astype(np.float32)
+        # gemm.rs:93-100, sequential f32 fold
+        ss = np.float32(0)
+        for v in x:
+            ss = np.float32(ss + v * v)
+        scale = np.float32(1.0) / np.sqrt(np.float32(ss / np.float32(n)) + np.float32(1e-6))
+        ref = x * scale * w
+        y = x.copy()
+        assert gpu.rmsnorm(y, w, 1e-6)
+        assert np.max(np.abs(y - ref) / (1 + np.abs(ref))) < 1e-5
+
+
+def test_used_from_another_thread():
+    """cuda_matvec.rs:141-171: created on one thread, used on another."""
+    gpu = CudaGpu(0)
+    err = []
+
+    def run():
+        try:
+            g = np.random.default_rng(7)
+            w = synth.random_weights(DTYPE_Q4_K, 64, 256, g)
+            x = np.arange(256, dtype=np.float32) / 100.0
+            y = np.zeros(64, np.float32)
+            assert gpu.matvec("t", view(DTYPE_Q4_K, w, 64, 256), 64, 256, x, y)
+            cerca(y, oracle.matvec_f64(DTYPE_Q4_K, w, 64, 256, x), "otro hilo")
+        except Exception as ex:  # pragma: no cover
+            err.append(ex)
+
+    t = threading.Thread(target=run)
+    t.start()
+    t.join()
+    gpu.close()
+    assert not err, err
+
+
+def test_no_device_error_word():
+    code = ctypes.c_uint32(0)
+    assert lib().sbk_take_device_error(0, ctypes.byref(code)) == 0
+    assert code.value == 0
