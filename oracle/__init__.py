@@ -197,3 +197,87 @@ def row_strip(rows: int, i: int, n: int) -> tuple[int, int]:
     s, e = ctypes.c_size_t(), ctypes.c_size_t()
     lib().or_row_strip(rows, i, n, ctypes.byref(s), ctypes.byref(e))
     return s.value, e.value
+
+
+# ---------------------------------------------------------------- float ops
+def _ops_lib():
+    L = lib()
+    if not getattr(L, "_ops_ready", False):
+        L.or_rmsnorm.argtypes = [_f32p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_float]
+        L.or_rmsnorm.argtypes = [_f32p, _f32p, ctypes.c_size_t, ctypes.c_float]
+        L.or_rope_heads.argtypes = [_f32p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_float,
+                                    ctypes.c_int]
+        L.or_rope_llama_n.argtypes = [_f32p, ctypes.c_size_t, ctypes.c_float, ctypes.c_size_t]
+        L.or_topk_softmax.argtypes = [_f32p, ctypes.c_size_t, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int32), _f32p]
+        L.or_swiglu.argtypes = [_f32p, _f32p, ctypes.c_size_t]
+        _u16p = ctypes.POINTER(ctypes.c_uint16)
+        L.or_attention_decode_f16.argtypes = [_f32p, _u16p, _u16p, ctypes.c_size_t, ctypes.c_size_t,
+                                              ctypes.c_size_t, ctypes.c_size_t, _f32p]
+        L.or_argmax.restype = ctypes.c_int32
+        L.or_argmax.argtypes = [_f32p, ctypes.c_size_t]
+        L._ops_ready = True
+    return L
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """gemm.rs:93-100; returns a new array."""
+    y = np.array(x, dtype=np.float32, copy=True)
+    ww, wp = _f32(w)
+    _ops_lib().or_rmsnorm(y.ctypes.data_as(_f32p), wp, y.size, eps)
+    return y
+
+
+def rope_heads(x: np.ndarray, n_heads: int, hd: int, pos: int, theta: float, neox: bool) -> np.ndarray:
+    """gemm.rs:1452-1491 (rope_cabezas)."""
+    y = np.array(x, dtype=np.float32, copy=True)
+    _ops_lib().or_rope_heads(y.ctypes.data_as(_f32p), n_heads, hd, pos, theta, 1 if neox else 0)
+    return y
+
+
+def rope_llama_n(x: np.ndarray, pos: int, theta: float, n_rot: int) -> np.ndarray:
+    y = np.array(x, dtype=np.float32, copy=True)
+    _ops_lib().or_rope_llama_n(y.ctypes.data_as(_f32p), pos, theta, n_rot)
+    return y
+
+
+def topk_softmax(logits: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """gemm.rs:62-91; returns (idx int32[k], weights f32[k]) in rank order."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    idx = np.zeros(k, dtype=np.int32)
+    w = np.zeros(k, dtype=np.float32)
+    _ops_lib().or_topk_softmax(lg.ctypes.data_as(_f32p), lg.size, k, idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                               w.ctypes.data_as(_f32p))
+    return idx, w
+
+
+def swiglu(up: np.ndarray, gate: np.ndarray) -> np.ndarray:
+    """gemm.rs:210-226: silu(gate) * up."""
+    u = np.array(up, dtype=np.float32, copy=True)
+    g, gp = _f32(gate)
+    _ops_lib().or_swiglu(u.ctypes.data_as(_f32p), gp, u.size)
+    return u
+
+
+def attention_decode_f16(q: np.ndarray, k16: np.ndarray, v16: np.ndarray, hd: int, kv_dim: int, kv_head: int,
+                         n_tokens: int) -> np.ndarray:
+    """attn.rs:73-140 over f16 rows [token][kv_dim] (uint16 bit arrays)."""
+    qq, qp = _f32(q)
+    k = np.ascontiguousarray(k16, dtype=np.uint16)
+    v = np.ascontiguousarray(v16, dtype=np.uint16)
+    out = np.zeros(hd, dtype=np.float32)
+    _u16p = ctypes.POINTER(ctypes.c_uint16)
+    _ops_lib().or_attention_decode_f16(qp, k.ctypes.data_as(_u16p), v.ctypes.data_as(_u16p), hd, kv_dim, kv_head,
+                                       n_tokens, out.ctypes.data_as(_f32p))
+    return out
+
+
+def argmax(v: np.ndarray) -> int:
+    """runtime.rs:2021-2028 (ties -> last index)."""
+    vv, vp = _f32(v)
+    return int(_ops_lib().or_argmax(vp, vv.size))
+
+
+def f32_to_f16_array(v: np.ndarray) -> np.ndarray:
+    """f16.rs:10-37 elementwise (the reference KV-cache rounding)."""
+    L = lib()
+    return np.array([L.or_f32_to_f16(float(a)) for a in np.asarray(v, dtype=np.float32).ravel()], dtype=np.uint16)

@@ -482,3 +482,141 @@ OR_API void or_quantize_q6_k(const float *src, size_t n, uint8_t *out)
         o[209] = (uint8_t)(d_bits >> 8);
     }
 }
+
+/* ------------------------------------------------------ float ops ---- */
+
+/* crates/soso-llm-core/src/gemm.rs:93-100 (rmsnorm, in place). */
+OR_API void or_rmsnorm(float *x, const float *w, size_t n, float eps)
+{
+    float var = 0.0f;
+    for (size_t i = 0; i < n; i++) var += x[i] * x[i];
+    var /= (float)n;
+    float scale = 1.0f / sqrtf(var + eps);
+    for (size_t i = 0; i < n; i++) x[i] = x[i] * scale * w[i];
+}
+
+/* crates/soso-llm-core/src/gemm.rs:1452-1491 (rope_cabezas): cos/sin per pair
+ * once, applied to every head; NeoX pairs (i, i+half), else (2i, 2i+1). */
+OR_API void or_rope_heads(float *x, size_t n_heads, size_t hd, size_t pos, float theta, int neox)
+{
+    size_t half = hd / 2;
+    float cs[512], sn[512];
+    if (hd < 2 || half > 512) return;
+    for (size_t i = 0; i < half; i++) {
+        float freq = powf(theta, -2.0f * (float)i / (float)hd);
+        float ang = (float)pos * freq;
+        sn[i] = sinf(ang);
+        cs[i] = cosf(ang);
+    }
+    for (size_t h = 0; h < n_heads; h++) {
+        float *v = x + h * hd;
+        for (size_t i = 0; i < half; i++) {
+            size_t a = neox ? i : 2 * i, b = neox ? i + half : 2 * i + 1;
+            float va = v[a], vb = v[b];
+            v[a] = va * cs[i] - vb * sn[i];
+            v[b] = va * sn[i] + vb * cs[i];
+        }
+    }
+}
+
+/* crates/soso-llm-core/src/gemm.rs:1346 + :1500-1520 (rope_inplace_n: llama
+ * pairs over the first n_rot elements, freq = theta^(-2i/n_rot)). */
+OR_API void or_rope_llama_n(float *x, size_t pos, float theta, size_t n_rot)
+{
+    size_t half = n_rot / 2;
+    for (size_t i = 0; i < half; i++) {
+        float freq = powf(theta, -2.0f * (float)i / (float)n_rot);
+        float ang = (float)pos * freq;
+        float s = sinf(ang), c = cosf(ang);
+        float a = x[2 * i], b = x[2 * i + 1];
+        x[2 * i] = a * c - b * s;
+        x[2 * i + 1] = a * s + b * c;
+    }
+}
+
+/* crates/soso-llm-core/src/gemm.rs:62-91 (softmax_inplace + topk_softmax):
+ * softmax over all, stable sort by weight desc, keep k, renormalise. */
+OR_API void or_topk_softmax(float *logits, size_t n, size_t k, int32_t *idx, float *w)
+{
+    float mx = -INFINITY, sum = 0.0f;
+    for (size_t i = 0; i < n; i++) mx = fmaxf(mx, logits[i]);
+    for (size_t i = 0; i < n; i++) {
+        logits[i] = expf(logits[i] - mx);
+        sum += logits[i];
+    }
+    if (sum > 0.0f)
+        for (size_t i = 0; i < n; i++) logits[i] /= sum;
+    /* stable selection of the k largest (ties keep the lower index first) */
+    if (k > n) k = n;
+    unsigned char *used = (unsigned char *)calloc(n, 1);
+    for (size_t r = 0; r < k; r++) {
+        size_t best = n;
+        for (size_t i = 0; i < n; i++) {
+            if (used[i]) continue;
+            if (best == n || logits[i] > logits[best]) best = i;
+        }
+        used[best] = 1;
+        idx[r] = (int32_t)best;
+        w[r] = logits[best];
+    }
+    free(used);
+    float t = 0.0f;
+    for (size_t r = 0; r < k; r++) t += w[r];
+    if (t > 0.0f)
+        for (size_t r = 0; r < k; r++) w[r] /= t;
+}
+
+/* crates/soso-llm-core/src/gemm.rs:210-226 (silu, swiglu_inplace scalar path). */
+OR_API void or_swiglu(float *up, const float *gate, size_t n)
+{
+    for (size_t i = 0; i < n; i++) up[i] = (gate[i] / (1.0f + expf(-gate[i]))) * up[i];
+}
+
+/* crates/soso-llm-core/src/attn.rs:73-140 (attention_decode_f16_tiled_scalar):
+ * online softmax over tiles of 64 positions, f16 K/V rows [token][kv_dim]. */
+OR_API void or_attention_decode_f16(const float *q, const uint16_t *k, const uint16_t *v, size_t hd,
+                                    size_t kv_dim, size_t kv_head, size_t n_tokens, float *out)
+{
+    enum { TILE = 64 };
+    for (size_t d = 0; d < hd; d++) out[d] = 0.0f;
+    if (n_tokens == 0 || hd == 0) return;
+    float inv = 1.0f / sqrtf((float)hd), m = -INFINITY, l = 0.0f, sc[TILE];
+    for (size_t t0 = 0; t0 < n_tokens; t0 += TILE) {
+        size_t t1 = t0 + TILE < n_tokens ? t0 + TILE : n_tokens;
+        float tmax = -INFINITY;
+        for (size_t t = t0; t < t1; t++) {
+            size_t off = t * kv_dim + kv_head * hd;
+            float dot = 0.0f;
+            for (size_t d = 0; d < hd; d++) dot += q[d] * or_f16_to_f32(k[off + d]);
+            float s = dot * inv;
+            sc[t - t0] = s;
+            if (s > tmax) tmax = s;
+        }
+        float mnew = m > tmax ? m : tmax;
+        float alpha = m == -INFINITY ? 0.0f : expf(m - mnew);
+        for (size_t d = 0; d < hd; d++) out[d] *= alpha;
+        l *= alpha;
+        float ts = 0.0f;
+        for (size_t t = t0; t < t1; t++) {
+            float p = expf(sc[t - t0] - mnew);
+            ts += p;
+            size_t off = t * kv_dim + kv_head * hd;
+            for (size_t d = 0; d < hd; d++) out[d] += p * or_f16_to_f32(v[off + d]);
+        }
+        l += ts;
+        m = mnew;
+    }
+    if (l > 0.0f) {
+        float il = 1.0f / l;
+        for (size_t d = 0; d < hd; d++) out[d] *= il;
+    }
+}
+
+/* crates/soso-llm-core/src/runtime.rs:2021-2028 (argmax: max_by keeps the last of equal maxima). */
+OR_API int32_t or_argmax(const float *v, size_t n)
+{
+    size_t bi = 0;
+    for (size_t i = 1; i < n; i++)
+        if (!(v[i] < v[bi])) bi = i;  /* >= : later equal values win */
+    return n ? (int32_t)bi : 0;
+}

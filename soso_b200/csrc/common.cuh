@@ -1,6 +1,7 @@
 // common.cuh -- shared device helpers for the sm_100a decode kernels.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -20,10 +21,11 @@ __device__ __forceinline__ void set_dev_error(unsigned int code) { atomicCAS(&g_
 // Balanced [start, end) of worker i of n -- the reference's row_strip
 // (crates/soso-llm-core/src/parallel.rs:22-31), used for rows over CTAs and for
 // blocks over 8-lane workers.
-__host__ __device__ __forceinline__ void row_strip(long long rows, long long i, long long n, long long &s,
-                                                   long long &e)
+// 32-bit: every count the kernels split (rows, blocks) is below 2^31, and
+// 64-bit division is a long emulated sequence on the GPU.
+__host__ __device__ __forceinline__ void row_strip(int rows, int i, int n, int &s, int &e)
 {
-    long long base = rows / n, rem = rows % n;
+    const int base = rows / n, rem = rows - base * n;
     s = i * base + (i < rem ? i : rem);
     e = s + base + (i < rem ? 1 : 0);
 }
@@ -101,6 +103,13 @@ constexpr float TWO_P60 = 1152921504606846976.0f;  // 2^60
 
 // Sum over the 8-lane group that contains this lane.  The mask names only the
 // group, so groups of one warp may call it at different times.
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
 __device__ __forceinline__ float warp8_sum(float v)
 {
     const unsigned m = 0xffu << (threadIdx.x & 24);

@@ -24,7 +24,11 @@
 //    workers are finished by a deterministic fixup in shared memory, so the
 //    result does not depend on scheduling.
 #pragma once
+#include <mutex>
+#include <unordered_map>
+
 #include "common.cuh"
+#include "q4k_mmv.cuh"
 #include "sosob200.h"
 
 namespace sb {
@@ -38,8 +42,18 @@ constexpr int MV_WORKERS = MV_THREADS / 8;
 // Lane c (0..7) of a worker reads qs chunk c = bytes 16c..16c+15: pair p = c/2,
 // low nibbles = sub-block 2p elements l0..l0+15 (l0 = 16*(c&1)), high nibbles =
 // sub-block 2p+1 (dequant.rs:181-186: byte pair*32+l -> elems pair*64+l, +32).
+// sums[i] = x[32i] + ... + x[32i+31], one warp per chunk, coalesced loads.
+__device__ __forceinline__ void chunk_sums32(float *sums, const float *__restrict__ x, int nchunks)
+{
+    const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int i = threadIdx.x >> 5; i < nchunks; i += nw) {
+        const float v = warp_sum(x[i * 32 + lane]);
+        if (lane == 0) sums[i] = v;
+    }
+}
+
 struct Q4K {
-    static constexpr int BE = 256, BB = 144;
+    static constexpr int BE = 256, BB = 144, U = 4;
     // smem: X2 float2[nb*128] (swizzled), sx float[nb*8]
     static __host__ __device__ size_t smem_bytes(int cols) { return (size_t)cols * 4 + (size_t)cols / 32 * 4; }
 
@@ -57,18 +71,21 @@ struct Q4K {
             float slo = (l & 1) ? 0x1p81f : 0x1p89f, shi = (l & 1) ? 0x1p77f : 0x1p85f;
             X2[b * 128 + c * 16 + (((j ^ c) & 7) << 1) + (l & 1)] = make_float2(lo * slo, hi * shi);
         }
-        for (int i = threadIdx.x; i < nb * 8; i += blockDim.x) {
-            float s = 0.0f;
-            for (int k = 0; k < 32; k++) s += x[i * 32 + k];
-            sx[i] = s;
-        }
+        chunk_sums32(sx, x, nb * 8);
     }
 
-    static __device__ __forceinline__ float block_dot(const uint8_t *__restrict__ blk, int c, int bc,
-                                                      const float *smem, int cols)
+    struct Frag {
+        uint4 hdr, qv;
+    };
+    static __device__ __forceinline__ void load(Frag &f, const uint8_t *__restrict__ blk, int c)
     {
-        const uint4 hdr = ldg_stream_v4(blk);
-        const uint4 qv = ldg_stream_v4(blk + 16 + c * 16);
+        f.hdr = ldg_stream_v4(blk);
+        f.qv = ldg_stream_v4(blk + 16 + c * 16);
+    }
+
+    static __device__ __forceinline__ float dot(const Frag &f, int c, int bc, const float *smem, int cols)
+    {
+        const uint4 hdr = f.hdr, qv = f.qv;
         const float4 *X4 = reinterpret_cast<const float4 *>(smem) + bc * 64 + c * 8;
         const float *sx = smem + cols;
         float2 acc = make_float2(0.0f, 0.0f);
@@ -103,33 +120,41 @@ struct Q4K {
 // reads code word c (codes 4c..4c+3).  Codes are offset to q+128 (xor 0x80)
 // so they are non-negative bit patterns; 128*Sum(x) is removed per block.
 struct Q80 {
-    static constexpr int BE = 32, BB = 36;
-    // smem: X float[cols] (pre-scaled, natural order), sx float[cols/32]
-    static __host__ __device__ size_t smem_bytes(int cols) { return (size_t)cols * 4 + (size_t)cols / 32 * 4; }
+    static constexpr int BE = 32, BB = 36, U = 8;
+    // smem per 4-element group g (cols/4 groups, 8 floats each):
+    //   X[4g..4g+3] pre-scaled, then the accumulator seed
+    //   (-128*2^-60*(x0+x2), -128*2^-60*(x1+x3)) that removes the +128 offset
+    //   inside the lane's own sum, before it can grow.
+    static __host__ __device__ size_t smem_bytes(int cols) { return (size_t)cols / 4 * 32; }
 
     static __device__ void stage(float *smem, const float *__restrict__ x, int cols)
     {
-        float *X = smem, *sx = smem + cols;
-        for (int i = threadIdx.x; i < cols; i += blockDim.x) X[i] = x[i] * ((i & 1) ? 0x1p81f : 0x1p89f);
-        for (int i = threadIdx.x; i < cols / 32; i += blockDim.x) {
-            float s = 0.0f;
-            for (int k = 0; k < 32; k++) s += x[i * 32 + k];
-            sx[i] = s;
+        float4 *S = reinterpret_cast<float4 *>(smem);
+        for (int g = threadIdx.x; g < cols / 4; g += blockDim.x) {
+            const float x0 = x[4 * g], x1 = x[4 * g + 1], x2 = x[4 * g + 2], x3 = x[4 * g + 3];
+            S[2 * g] = make_float4(x0 * 0x1p89f, x1 * 0x1p81f, x2 * 0x1p89f, x3 * 0x1p81f);
+            S[2 * g + 1] = make_float4(-0x1p-53f * (x0 + x2), -0x1p-53f * (x1 + x3), 0.0f, 0.0f);
         }
     }
 
-    static __device__ __forceinline__ float block_dot(const uint8_t *__restrict__ blk, int c, int bc,
-                                                      const float *smem, int cols)
+    struct Frag {
+        uint32_t scale, w;
+    };
+    static __device__ __forceinline__ void load(Frag &f, const uint8_t *__restrict__ blk, int c)
     {
-        const float scale = __uint_as_float(ldg_u32(blk));
-        const uint32_t t = ldg_u32(blk + 4 + 4 * c) ^ 0x80808080u, v = t >> 16;
-        const float4 X = reinterpret_cast<const float4 *>(smem)[bc * 8 + c];
+        f.scale = ldg_u32(blk);
+        f.w = ldg_u32(blk + 4 + 4 * c);
+    }
+
+    static __device__ __forceinline__ float dot(const Frag &f, int c, int bc, const float *smem, int cols)
+    {
+        const uint32_t t = f.w ^ 0x80808080u, v = t >> 16;  // codes as q + 128
+        const float4 *S = reinterpret_cast<const float4 *>(smem) + 2 * (bc * 8 + c);
+        const float4 X = S[0], B = S[1];
         float2 acc = ffma2(make_float2(bits_f(t & 0xFFu), bits_f(t & 0xFF00u)), make_float2(X.x, X.y),
-                           make_float2(0.0f, 0.0f));
+                           make_float2(B.x, B.y));
         acc = ffma2(make_float2(bits_f(v & 0xFFu), bits_f(v & 0xFF00u)), make_float2(X.z, X.w), acc);
-        float r = scale * TWO_P60 * (acc.x + acc.y);
-        if (c == 0) r -= scale * 128.0f * smem[cols + bc];
-        return r;
+        return __uint_as_float(f.scale) * TWO_P60 * (acc.x + acc.y);
     }
 };
 
@@ -143,7 +168,7 @@ struct Q80 {
 //   Q4 (elems 128n+96+l) = B hi | (H bits 6-7)<<4     scale sc[8n + g/4 + 6]
 // codes are q+32 (unsigned); 32*Sum(x) over each 4-element group is removed.
 struct Q6K {
-    static constexpr int BE = 256, BB = 210;
+    static constexpr int BE = 256, BB = 210, U = 2;
     // smem: X float4[nb][2][8][4] (Q1..Q4 values of element 4g+k), sx4 float4[nb][2][8]
     static __host__ __device__ size_t smem_bytes(int cols) { return (size_t)cols * 4 + (size_t)cols; }
 
@@ -172,20 +197,33 @@ struct Q6K {
         }
     }
 
-    static __device__ __forceinline__ float block_dot(const uint8_t *__restrict__ blk, int g, int bc,
-                                                      const float *smem, int cols)
+    struct Frag {
+        uint32_t A[2], B[2], H[2], sa[2], sb[2];
+        unsigned short d;
+    };
+    static __device__ __forceinline__ void load(Frag &f, const uint8_t *__restrict__ blk, int g)
+    {
+#pragma unroll
+        for (int n = 0; n < 2; n++) {
+            f.A[n] = ldg_u32_a2(blk + 64 * n + 4 * g);
+            f.B[n] = ldg_u32_a2(blk + 64 * n + 32 + 4 * g);
+            f.H[n] = ldg_u32_a2(blk + 128 + 32 * n + 4 * g);
+            f.sa[n] = ldg_u32_a2(blk + 192 + 8 * n);
+            f.sb[n] = ldg_u32_a2(blk + 196 + 8 * n);
+        }
+        f.d = ldg_u16(blk + 208);
+    }
+
+    static __device__ __forceinline__ float dot(const Frag &f, int g, int bc, const float *smem, int cols)
     {
         const float4 *X = reinterpret_cast<const float4 *>(smem) + bc * 64;
         const float4 *S = reinterpret_cast<const float4 *>(smem + cols) + bc * 16;
-        const float d = __half2float(__ushort_as_half(ldg_u16(blk + 208))) * TWO_P60;
+        const float d = __half2float(__ushort_as_half(f.d)) * TWO_P60;
         const int gi = (g >> 2) * 8;
         float total = 0.0f;
 #pragma unroll
         for (int n = 0; n < 2; n++) {
-            const uint32_t A = ldg_u32_a2(blk + 64 * n + 4 * g);
-            const uint32_t B = ldg_u32_a2(blk + 64 * n + 32 + 4 * g);
-            const uint32_t H = ldg_u32_a2(blk + 128 + 32 * n + 4 * g);
-            const uint32_t sa = ldg_u32_a2(blk + 192 + 8 * n), sb = ldg_u32_a2(blk + 196 + 8 * n);
+            const uint32_t A = f.A[n], B = f.B[n], H = f.H[n], sa = f.sa[n], sb = f.sb[n];
             const uint32_t q[4] = {(A & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u),
                                    (B & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u),
                                    ((A >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u),
@@ -222,65 +260,78 @@ __global__ void __launch_bounds__(MV_THREADS) matvec_kernel(const uint8_t *__res
     extern __shared__ __align__(16) float smem[];
     __shared__ float seg_first[MV_WORKERS], seg_last[MV_WORKERS];
 
+    __shared__ int wrange[MV_WORKERS + 1];
     const int nb = cols / F::BE;
-    long long r0, r1;
+    int r0, r1;
     row_strip(rows, blockIdx.x, gridDim.x, r0, r1);
-    const long long cb0 = r0 * nb, cb1 = r1 * nb;  // this CTA's blocks
+    const int cb0 = r0 * nb, cb1 = r1 * nb;  // this CTA's blocks
 
-    if (threadIdx.x < 32) prefetch_range_l2(W, cb0 * F::BB, cb1 * F::BB);
+#ifndef SB_NO_L2PF
+    if (threadIdx.x < 32) prefetch_range_l2(W, (long long)cb0 * F::BB, (long long)cb1 * F::BB);
+#endif
+    if (threadIdx.x <= MV_WORKERS) {
+        int s0, e0;
+        row_strip(cb1 - cb0, threadIdx.x < MV_WORKERS ? threadIdx.x : MV_WORKERS - 1, MV_WORKERS, s0, e0);
+        wrange[threadIdx.x] = cb0 + (threadIdx.x < MV_WORKERS ? s0 : e0);
+    }
     griddep_wait();
     F::stage(smem, x, cols);
     __syncthreads();
     griddep_launch();
 
     const int worker = threadIdx.x >> 3, c = threadIdx.x & 7;
-    long long wb0, wb1;
-    row_strip(cb1 - cb0, worker, MV_WORKERS, wb0, wb1);
-    wb0 += cb0;
-    wb1 += cb0;
+    const int wb0 = wrange[worker], wb1 = wrange[worker + 1];
 
     if (wb0 < wb1) {
-        long long row = wb0 / nb;
-        int bc = (int)(wb0 - row * nb);
-        long long seg_start = wb0;
+        int row = wb0 / nb;
+        int bc = wb0 - row * nb;
+        int seg_start = wb0;
         float acc = 0.0f;
-        for (long long b = wb0; b < wb1; b++) {
-            acc += F::block_dot(W + b * F::BB, c, bc, smem, cols);
-            if (++bc == nb || b + 1 == wb1) {
-                const float v = warp8_sum(acc);
-                const bool starts = seg_start == row * nb, ends = bc == nb;
-                if (c == 0) {
-                    if (starts && ends) y[row] = v;
-                    else if (starts) seg_last[worker] = v;   // owner of a row that continues
-                    else seg_first[worker] = v;              // continuation (middle or last piece)
+        const uint8_t *rowp = W + (size_t)row * nb * F::BB;
+        for (int b = wb0; b < wb1; b += F::U) {
+            // issue the loads of up to U blocks before any of them is used
+            typename F::Frag fr[F::U];
+#pragma unroll
+            for (int u = 0; u < F::U; u++)
+                if (b + u < wb1) F::load(fr[u], W + (size_t)(b + u) * F::BB, c);
+#pragma unroll
+            for (int u = 0; u < F::U; u++) {
+                if (b + u < wb1) {
+                    acc += F::dot(fr[u], c, bc, smem, cols);
+                    if (++bc == nb || b + u + 1 == wb1) {
+                        const float v = warp8_sum(acc);
+                        const bool starts = seg_start == row * nb, ends = bc == nb;
+                        if (c == 0) {
+                            if (starts && ends) y[row] = v;
+                            else if (starts) seg_last[worker] = v;  // owner of a row that continues
+                            else seg_first[worker] = v;             // continuation (middle or last piece)
+                        }
+                        acc = 0.0f;
+                        bc = 0;
+                        row++;
+                        seg_start = b + u + 1;
+                    }
                 }
-                acc = 0.0f;
-                bc = 0;
-                row++;
-                seg_start = b + 1;
             }
         }
+        (void)rowp;
     }
     __syncthreads();
     // Deterministic fixup of rows split between workers: the worker holding a
     // row's first block adds the following workers' pieces in order.
     if (threadIdx.x < MV_WORKERS) {
         const int w = threadIdx.x;
-        long long a0, a1;
-        row_strip(cb1 - cb0, w, MV_WORKERS, a0, a1);
-        a0 += cb0;
-        a1 += cb0;
+        const int a0 = wrange[w], a1 = wrange[w + 1];
         if (a0 < a1) {
-            const long long last_row = (a1 - 1) / nb;
-            const long long row_end = (last_row + 1) * nb;
+            const int last_row = (a1 - 1) / nb;
+            const int row_end = (last_row + 1) * nb;
             if (a1 < row_end && last_row * nb >= a0) {
                 float total = seg_last[w];
                 for (int w2 = w + 1; w2 < MV_WORKERS; w2++) {
-                    long long b0, b1;
-                    row_strip(cb1 - cb0, w2, MV_WORKERS, b0, b1);
+                    const int b0 = wrange[w2], b1 = wrange[w2 + 1];
                     if (b0 >= b1) break;
                     total += seg_first[w2];
-                    if (b1 + cb0 >= row_end) break;
+                    if (b1 >= row_end) break;
                 }
                 y[last_row] = total;
             }
@@ -308,8 +359,8 @@ static int launch_matvec(const void *w, size_t rows, size_t cols, const float *x
             return -3;
         smem_set[dev] = smem;
     }
-    // two CTAs per SM when shared memory allows, never more CTAs than rows
-    int per_sm = smem <= 100 * 1024 ? 2 : 1;
+    // as many CTAs per SM as shared memory allows (registers cap it at 3), never more CTAs than rows
+    int per_sm = smem <= 64 * 1024 ? 3 : smem <= 100 * 1024 ? 2 : 1;
     long long grid = (long long)num_sms[dev] * per_sm;
     if ((long long)rows < grid) grid = (long long)rows;
     cudaLaunchConfig_t cfg = {};
@@ -342,15 +393,71 @@ extern "C" size_t sbk_row_bytes(uint8_t dtype, size_t cols)
     return cols / e * b;
 }
 
+namespace sb {
+// Per (device, stream) workspace for the split-row kernels, grown on demand and
+// zero-initialised.  Growing allocates: make the first call of a shape outside
+// stream capture.
+struct WsCache {
+    std::mutex mu;
+    std::unordered_map<unsigned long long, std::pair<void *, size_t>> m;
+};
+static WsCache g_ws;
+
+static void *stream_ws(cudaStream_t s, size_t bytes)
+{
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long key = ((unsigned long long)dev << 56) ^ (unsigned long long)(uintptr_t)s;
+    std::lock_guard<std::mutex> lk(g_ws.mu);
+    auto &e = g_ws.m[key];
+    if (e.second >= bytes) return e.first;
+    if (e.first) {
+        cudaStreamSynchronize(s);
+        cudaFree(e.first);
+    }
+    e.first = nullptr;
+    e.second = 0;
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    if (cudaMalloc(&e.first, want) != cudaSuccess) return nullptr;
+    cudaMemset(e.first, 0, want);
+    e.second = want;
+    return e.first;
+}
+
+static int num_sms_cached()
+{
+    static int n[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!n[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        n[dev] = v > 0 ? v : 148;
+    }
+    return n[dev];
+}
+}  // namespace sb
+
 extern "C" int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols, const float *x, float *y,
                           int pdl, void *stream)
 {
     if (!w || !x || !y || rows == 0 || rows > (1u << 30)) return -1;
     if (!sbk_row_bytes(dtype, cols) || cols > 65536) return -1;
+    if ((unsigned long long)rows * (cols / 32) >= (1ull << 31)) return -1;  // block indices are 32-bit
     if (((uintptr_t)w & 15) || ((uintptr_t)x & 15)) return -2;
     cudaStream_t s = (cudaStream_t)stream;
     switch (dtype) {
-    case SB_DTYPE_Q4_K: return sb::launch_matvec<sb::Q4K>(w, rows, cols, x, y, pdl, s);
+    case SB_DTYPE_Q4_K:
+        if (cols <= (size_t)sb::q4kmmv::MAX_COLS &&
+            sb::q4kmmv::smem_bytes((int)cols, sb::q4kmmv::max_groups_per_cta((int)rows, (int)cols,
+                                                                             sb::num_sms_cached())) <= 227 * 1024) {
+            const int grid = sb::num_sms_cached();
+            void *ws = sb::stream_ws(s, sb::q4kmmv::ws_bytes((int)rows, (int)cols, grid));
+            if (!ws) return -3;
+            return sb::q4kmmv::launch(w, (int)rows, (int)cols, x, y, ws, grid, pdl, s);
+        }
+        return sb::launch_matvec<sb::Q4K>(w, rows, cols, x, y, pdl, s);
     case SB_DTYPE_Q8_0: return sb::launch_matvec<sb::Q80>(w, rows, cols, x, y, pdl, s);
     case SB_DTYPE_Q6_K: return sb::launch_matvec<sb::Q6K>(w, rows, cols, x, y, pdl, s);
     }

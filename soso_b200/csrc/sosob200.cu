@@ -3,4 +3,5 @@
 #include "common.cuh"
 #include "matvec.cuh"
 #include "norm.cuh"
+#include "decode_ops.cuh"
 #include "dispatch.cuh"
