@@ -109,12 +109,66 @@ size_t sbk_row_bytes(uint8_t dtype, size_t cols);
 int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols, const float *x, float *y, int pdl,
                void *stream);
 
+/* One device-pointer matvec of a batch. */
+typedef struct {
+    const void *w;
+    size_t rows, cols;
+    const float *x;
+    float *y;
+} sbk_mv_op;
+
+/* Independent matvecs of one dtype in as few launches as possible (Q4_K: one
+ * launch per 40 matrices, their weight streams split across all SMs as one) --
+ * the device-pointer form of `GpuDispatch::matvec_lote` (gpu.rs:694-701) and of
+ * the reference's `Lote` batches (crates/soso-llm-core/src/layer.rs:571-641). */
+int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, int pdl, void *stream);
+
 /* RMSNorm of `rows` rows of n floats, `gemm::rmsnorm` (crates/soso-llm-core/src/gemm.rs:93-100),
  * optionally fused with the residual add `add_f32` (gemm.rs:265): with res != NULL,
  * h_out = x + res and y = rmsnorm(h_out) * w; else y = rmsnorm(x) * w.  y may alias x.
  * Replaces `gm_rmsnorm_rows` / `rmsnorm_rows_f32` (gemma_capa.cu:81-96, rmsnorm_rows.cu:13-38). */
 int sbk_rmsnorm(const float *x, const float *res, float *h_out, const float *w, float *y, size_t rows, size_t n,
                 float eps, void *stream);
+
+/* ---- decode-step kernels (device pointers; `pos` / `token` read from device memory,
+ * so a captured CUDA graph serves every step) ---------------------------------- */
+
+/* On the stacked [q | k | v] vector of one token: optional bias (add_optional_bias,
+ * crates/soso-llm-core/src/layer.rs:1146-1163), optional per-head QK-norm
+ * (layer.rs:1164-1181), RoPE (rope_cabezas, gemm.rs:1452-1491; neox != 0 pairs
+ * (i, i+d/2), else (2i, 2i+1)), then K/V appended as f16 rows at *pos of the
+ * [ctx][kv_heads*head_dim] caches (LayerKv::append_f16, kv.rs:258-275, with the
+ * reference's f32->f16 rounding, f16.rs:10-37).  q is roped in place.
+ * Replaces gm_rope + gm_kv_append (lxdde/ports/nouveau/gemma_capa.cu:99-141). */
+int sbk_rope_kv_append(float *qkv, const float *bias, const float *qnorm, const float *knorm, uint16_t *kcache,
+                       uint16_t *vcache, const int32_t *pos, size_t heads, size_t kv_heads, size_t head_dim,
+                       size_t ctx, float theta, float eps, int neox, int pdl, void *stream);
+
+/* Workspace bytes for sbk_attn_decode (zero-filled before first use; left zeroed). */
+size_t sbk_attn_ws_bytes(size_t heads, size_t kv_heads, size_t head_dim, size_t ctx);
+/* GQA decode attention of one token over positions 0..*pos of the f16 caches:
+ * softmax(q.k / sqrt(hd)) . v per query head, kv head = head / (heads/kv_heads)
+ * (attention_decode_f16_tiled_scalar, crates/soso-llm-core/src/attn.rs:73-140; split
+ * into chunks merged like combinar_trozos, attn_grupo.rs:171-203).  head_dim 128.
+ * Replaces mo_attn_split + mo_attn_combine (gemma_capa.cu:765-926). */
+int sbk_attn_decode(const float *q, const uint16_t *kcache, const uint16_t *vcache, float *out, const int32_t *pos,
+                    size_t heads, size_t kv_heads, size_t head_dim, size_t ctx, void *ws, int pdl, void *stream);
+
+/* Router: softmax over n_exp logits, stable top-k by weight, renormalised
+ * (gemm::topk_softmax, crates/soso-llm-core/src/gemm.rs:62-91); idx/wts in rank
+ * order.  Replaces mo_router (gemma_capa.cu:586-639). */
+int sbk_router_topk(const float *logits, size_t n_exp, size_t top_k, int32_t *idx, float *wts, int pdl, void *stream);
+
+/* Workspace bytes for sbk_argmax (zero-filled before first use; left zeroed). */
+size_t sbk_argmax_ws_bytes(void);
+/* Greedy token: index of the maximum, ties to the LAST index like
+ * Runtime::argmax (crates/soso-llm-core/src/runtime.rs:2021-2028). */
+int sbk_argmax(const float *v, size_t n, int32_t *out, void *ws, int pdl, void *stream);
+
+/* One embedding row (dtype F32 / Q8_0 / Q4_K / Q6_K) dequantised exactly
+ * (Runtime::embed_token, crates/soso-llm-core/src/runtime.rs:787-802). */
+int sbk_embed_row(const void *table, uint8_t dtype, size_t vocab, size_t hidden, const int32_t *token, float *out,
+                  int pdl, void *stream);
 
 /* Number of SMs the kernels size their grids for. */
 int sbk_num_sms(int device);

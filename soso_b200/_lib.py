@@ -24,6 +24,11 @@ class SbMatvecOp(ctypes.Structure):
                 ("x", c_f32p), ("out", c_f32p)]
 
 
+class SbkMvOp(ctypes.Structure):
+    _fields_ = [("w", ctypes.c_void_p), ("rows", c_size), ("cols", c_size), ("x", ctypes.c_void_p),
+                ("y", ctypes.c_void_p)]
+
+
 class SbStats(ctypes.Structure):
     _fields_ = [("launches", ctypes.c_uint64), ("total_ns", ctypes.c_uint64), ("bytes_up", ctypes.c_uint64),
                 ("bytes_down", ctypes.c_uint64)]
@@ -49,6 +54,19 @@ SIGNATURES = {
                                   ctypes.c_int, ctypes.c_void_p]),
     "sbk_rmsnorm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                    ctypes.c_void_p, c_size, c_size, ctypes.c_float, ctypes.c_void_p]),
+    "sbk_matvec_batch": (ctypes.c_int, [ctypes.c_uint8, ctypes.c_void_p, c_size, ctypes.c_int, ctypes.c_void_p]),
+    "sbk_rope_kv_append": (ctypes.c_int, [ctypes.c_void_p] * 7 + [c_size] * 4 + [ctypes.c_float, ctypes.c_float,
+                                                                          ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "sbk_attn_ws_bytes": (c_size, [c_size] * 4),
+    "sbk_attn_decode": (ctypes.c_int, [ctypes.c_void_p] * 5 + [c_size] * 4 + [ctypes.c_void_p, ctypes.c_int,
+                                                                          ctypes.c_void_p]),
+    "sbk_router_topk": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                       ctypes.c_void_p]),
+    "sbk_argmax_ws_bytes": (c_size, []),
+    "sbk_argmax": (ctypes.c_int, [ctypes.c_void_p, c_size, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                  ctypes.c_void_p]),
+    "sbk_embed_row": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint8, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p,
+                                     ctypes.c_int, ctypes.c_void_p]),
     "sbk_num_sms": (ctypes.c_int, [ctypes.c_int]),
     "sbk_take_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
 }

@@ -22,6 +22,7 @@ extern "C" int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols
                           int pdl, void *stream);
 extern "C" int sbk_rmsnorm(const float *x, const float *res, float *h_out, const float *w, float *y, size_t rows,
                            size_t n, float eps, void *stream);
+extern "C" int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, int pdl, void *stream);
 
 namespace {
 
@@ -255,20 +256,33 @@ extern "C" int sb_matvec_batch(sb_ctx *c, sb_matvec_op *ops, size_t nops, uint8_
     if (off == 0) return 1;
     if (c->ensure_scratch(off)) return -1;
     char *base = (char *)c->scratch;
+    // all inputs up, then the kernels grouped by dtype (one launch per batch of Q4_K
+    // matrices), then all outputs down, one wait
+    std::vector<sbk_mv_op> by_dtype[3];
     for (size_t i = 0; i < nops; i++) {
         if (!res[i]) continue;
         sb_matvec_op &op = ops[i];
         if ((e = cudaMemcpyAsync(base + xo[i], op.x, op.cols * 4, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
             return fail("cudaMemcpyAsync(x)", e);
-        int k = sbk_matvec(op.view->dtype, res[i]->ptr, op.rows, op.cols, (const float *)(base + xo[i]),
-                           (float *)(base + yo[i]), 0, c->stream);
-        if (k) return fail("sbk_matvec launch failed");
+        const int k = op.view->dtype == SB_DTYPE_Q4_K ? 0 : op.view->dtype == SB_DTYPE_Q6_K ? 1 : 2;
+        by_dtype[k].push_back(sbk_mv_op{res[i]->ptr, op.rows, op.cols, (const float *)(base + xo[i]),
+                                        (float *)(base + yo[i])});
+        c->stats.bytes_up += op.cols * 4;
+        c->stats.bytes_down += op.rows * 4;
+    }
+    const uint8_t dts[3] = {SB_DTYPE_Q4_K, SB_DTYPE_Q6_K, SB_DTYPE_Q8_0};
+    for (int k = 0; k < 3; k++) {
+        if (by_dtype[k].empty()) continue;
+        if (sbk_matvec_batch(dts[k], by_dtype[k].data(), by_dtype[k].size(), 0, c->stream))
+            return fail("sbk_matvec_batch launch failed");
+        c->stats.launches++;
+    }
+    for (size_t i = 0; i < nops; i++) {
+        if (!res[i]) continue;
+        sb_matvec_op &op = ops[i];
         if ((e = cudaMemcpyAsync(op.out, base + yo[i], op.rows * 4, cudaMemcpyDeviceToHost, c->stream)) !=
             cudaSuccess)
             return fail("cudaMemcpyAsync(out)", e);
-        c->stats.launches++;
-        c->stats.bytes_up += op.cols * 4;
-        c->stats.bytes_down += op.rows * 4;
     }
     if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", e);
     for (size_t i = 0; i < nops; i++) done[i] = res[i] ? 1 : 0;

@@ -448,20 +448,60 @@ extern "C" int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols
     if (((uintptr_t)w & 15) || ((uintptr_t)x & 15)) return -2;
     cudaStream_t s = (cudaStream_t)stream;
     switch (dtype) {
-    case SB_DTYPE_Q4_K:
-        if (cols <= (size_t)sb::q4kmmv::MAX_COLS &&
-            sb::q4kmmv::smem_bytes((int)cols, sb::q4kmmv::max_groups_per_cta((int)rows, (int)cols,
-                                                                             sb::num_sms_cached())) <= 227 * 1024) {
-            const int grid = sb::num_sms_cached();
-            void *ws = sb::stream_ws(s, sb::q4kmmv::ws_bytes((int)rows, (int)cols, grid));
+    case SB_DTYPE_Q4_K: {
+        const int grid = sb::num_sms_cached();
+        const sb::q4kmmv::MatOp op{w, (int)rows, (int)cols, x, y};
+        if (sb::q4kmmv::fits(&op, 1, grid)) {
+            void *ws = sb::stream_ws(s, sb::q4kmmv::ws_bytes(grid));
             if (!ws) return -3;
-            return sb::q4kmmv::launch(w, (int)rows, (int)cols, x, y, ws, grid, pdl, s);
+            return sb::q4kmmv::launch_batch(&op, 1, ws, grid, pdl, s);
         }
         return sb::launch_matvec<sb::Q4K>(w, rows, cols, x, y, pdl, s);
+    }
     case SB_DTYPE_Q8_0: return sb::launch_matvec<sb::Q80>(w, rows, cols, x, y, pdl, s);
     case SB_DTYPE_Q6_K: return sb::launch_matvec<sb::Q6K>(w, rows, cols, x, y, pdl, s);
     }
     return -1;
+}
+
+extern "C" int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, int pdl, void *stream)
+{
+    if (!ops || n == 0) return -1;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dtype == SB_DTYPE_Q4_K) {
+        const int grid = sb::num_sms_cached();
+        for (size_t i0 = 0; i0 < n; i0 += sb::q4kmmv::MAXB) {
+            const size_t nb = n - i0 < (size_t)sb::q4kmmv::MAXB ? n - i0 : (size_t)sb::q4kmmv::MAXB;
+            sb::q4kmmv::MatOp mo[sb::q4kmmv::MAXB];
+            bool ok = true;
+            for (size_t i = 0; i < nb; i++) {
+                const sbk_mv_op &o = ops[i0 + i];
+                if (!o.w || !o.x || !o.y || !o.rows || ((uintptr_t)o.w & 15) || ((uintptr_t)o.x & 15) ||
+                    sbk_row_bytes(dtype, o.cols) == 0)
+                    return -1;
+                mo[i] = sb::q4kmmv::MatOp{o.w, (int)o.rows, (int)o.cols, o.x, o.y};
+                ok = ok && o.rows < (1u << 24);
+            }
+            if (ok && sb::q4kmmv::fits(mo, (int)nb, grid)) {
+                void *ws = sb::stream_ws(s, sb::q4kmmv::ws_bytes(grid));
+                if (!ws) return -3;
+                const int rc = sb::q4kmmv::launch_batch(mo, (int)nb, ws, grid, pdl, s);
+                if (rc) return rc;
+            } else {
+                for (size_t i = 0; i < nb; i++) {
+                    const sbk_mv_op &o = ops[i0 + i];
+                    const int rc = sbk_matvec(dtype, o.w, o.rows, o.cols, o.x, o.y, pdl, stream);
+                    if (rc) return rc;
+                }
+            }
+        }
+        return 0;
+    }
+    for (size_t i = 0; i < n; i++) {
+        const int rc = sbk_matvec(dtype, ops[i].w, ops[i].rows, ops[i].cols, ops[i].x, ops[i].y, pdl, stream);
+        if (rc) return rc;
+    }
+    return 0;
 }
 
 extern "C" int sbk_num_sms(int device)

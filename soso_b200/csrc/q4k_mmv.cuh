@@ -249,19 +249,38 @@ __device__ __forceinline__ int owner_of(int unit, int total, int n)
     return unit < big ? unit / (base + 1) : rem + (base ? (unit - big) / base : 0);
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
-    q4k_mmv_kernel(const __grid_constant__ CUtensorMap wmap, int rows, int cols, const float *__restrict__ x,
-                   float *__restrict__ y, Ws ws, int max_groups)
+// One launch serves a batch of independent matvecs (the reference's
+// matvec_lote: several matvecs, one wait).  Their stages are numbered one
+// after another; the CTAs split that global range, so the batch streams as one.
+constexpr int MAXB = 40;
+
+struct __align__(64) MatDesc {
+    CUtensorMap map;        // weights as [rows][row_bytes/8] u64, box 16 x 72
+    const float *x;
+    float *y;
+    int rows, cols, spg;    // spg: stages per 16-row group
+    int st_begin, cnt_off;  // first global stage; first counter of its groups
+};
+
+struct Batch {
+    MatDesc d[MAXB];
+    int n, total;            // matrices, stages
+    int max_cols, max_groups;  // shared-memory capacities (prep, partial table)
+};
+
+__global__ void __launch_bounds__(THREADS, 1) q4k_mmv_kernel(const __grid_constant__ Batch B, Ws ws)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    const Smem s = carve(smem_raw, cols, max_groups);
-    const int nb = cols / 256;
-    const int groups = (rows + 15) >> 4, spg = (nb + SBLK - 1) / SBLK, total = groups * spg;
+    const Smem s = carve(smem_raw, B.max_cols, B.max_groups);
     int st0, st1;
-    row_strip(total, blockIdx.x, gridDim.x, st0, st1);
+    row_strip(B.total, blockIdx.x, gridDim.x, st0, st1);
     const int nst = st1 - st0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g_first = st0 / spg, g_last = (st1 - 1) / spg;  // valid when nst > 0
+    // matrices touched: m_first .. m_last
+    int m_first = 0;
+    while (m_first + 1 < B.n && B.d[m_first + 1].st_begin <= st0) m_first++;
+    int m_last = m_first;
+    while (nst > 0 && m_last + 1 < B.n && B.d[m_last + 1].st_begin < st1) m_last++;
 
     if (threadIdx.x == 0) {
         for (int k = 0; k < NSLOT; k++) {
@@ -270,14 +289,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // zero the per-group partial table
-    if (nst > 0)
-        for (int i = threadIdx.x; i < (g_last - g_first + 1) * NCW * 16; i += blockDim.x) s.part[i] = 0.0f;
     if (threadIdx.x < 16) reinterpret_cast<float *>(s.zero)[threadIdx.x] = 0.0f;
     __syncthreads();
-    // Dependents (the next x prep, then the next matvec) may launch now: they only
-    // read what this grid writes after their own griddepcontrol.wait, which waits
-    // for this grid to complete.
+    // Dependents may launch now: they only read what this grid writes after their
+    // own griddepcontrol.wait, which waits for this grid to complete.
     griddep_launch();
 
     bool failed = false;
@@ -285,17 +300,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---------------- producer: weights do not depend on the previous kernel, so the
         // whole stream runs without griddepcontrol.wait
         if (lane == 0 && nst > 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
-            int G = st0 / spg, j = st0 - G * spg, slot = 0;
+            int mi = m_first, slot = 0;
             unsigned phase = 0;  // parity of the empty-barrier phase to wait for
+            const MatDesc *d = &B.d[mi];
+            int ls = st0 - d->st_begin, G = ls / d->spg, j = ls - G * d->spg;
+            int mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&d->map) : "memory");
             for (int k = 0; k < nst; k++) {
+                if (st0 + k == mend) {  // next matrix of the batch
+                    d = &B.d[++mi];
+                    G = 0, j = 0;
+                    mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
+                    asm volatile("prefetch.tensormap [%0];" ::"l"(&d->map) : "memory");
+                }
                 if (k >= NSLOT && !mbar_wait(&s.empty[slot], phase)) {
                     failed = true;
                     break;
                 }
                 mbar_expect_tx_arrive(&s.full[slot], (unsigned)SLOTB);  // full box, zero-filled past the ends
-                tma_load_2d(s.ring + slot * SLOTB, &wmap, j * SBLK * 18, G * 16, &s.full[slot]);
-                if (++j == spg) j = 0, G++;
+                tma_load_2d(s.ring + slot * SLOTB, &d->map, j * SBLK * 18, G * 16, &s.full[slot]);
+                if (++j == d->spg) j = 0, G++;
                 if (++slot == NSLOT) {
                     slot = 0;
                     if (k >= NSLOT) phase ^= 1u;  // stages 2*NSLOT.. wait for the second use of a slot, ...
@@ -307,135 +331,165 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
         // ---------------- consumers
         const int cwg = warp - 1;  // 0 .. NCW-1
-        griddep_wait();            // x is written by the previous kernel
-        prep_x(x, cols, s.prep, cwg);
-        asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
         const int team = cwg / NCONS, cw = cwg % NCONS, g = lane >> 2, t = lane & 3, sh = 8 * t;
         const bool live = frag_live(g, t);
-        const int HB = cols / 128;
-        // lane-constant pieces of every address
-        const uint8_t *fragl = live ? s.prep + frag_lane(g, t) * 64 : s.zero;  // + hb * fstride
         const int fstride = live ? 1024 : 0;
-        const float *fbt = reinterpret_cast<const float *>(s.prep + (size_t)HB * 1024) + t, *sxt = fbt + HB * 4;
         const uint8_t *ring_lane = s.ring + g * ROWB + cw * 144;  // + slot * SLOTB
         const int qoff = 16 + t * 16;
-        float acc0 = 0.0f, acc1 = 0.0f;
-        int cur = -1;
-        int slot = team, G = (st0 + team) / spg, j = (st0 + team) - G * spg;
-        unsigned parity = 0;
-        for (int k = team; k < nst && !failed; k += NSTREAM) {
-            if (k != team) {  // advance by NSTREAM stages
-                slot += NSTREAM;
-                if (slot >= NSLOT) slot -= NSLOT, parity ^= 1u;
-                j += NSTREAM;
-                while (j >= spg) j -= spg, G++;
-            }
-            if (!mbar_wait(&s.full[slot], parity)) {
-                failed = true;
-                set_dev_error(0x52u);
-                break;
-            }
-            const int blk = j * SBLK + cw;
-            bool released = false;
-            if (G != cur) {
-                if (cur >= 0) {
-                    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-                    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-                    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-                    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-                    if (t == 0) {
-                        float *p = s.part + ((cur - g_first) * NCW + cwg) * 16;
-                        p[g] = acc0;
-                        p[g + 8] = acc1;
+        griddep_wait();  // x of every matrix is written by the previous kernel
+        for (int mi = m_first; mi <= m_last && nst > 0; mi++) {
+            const MatDesc &d = B.d[mi];
+            const int cols = d.cols, nb = cols / 256, spg = d.spg, HB = cols / 128;
+            const int mtot = spg * ((d.rows + 15) >> 4);
+            const int ka = max(st0, d.st_begin) - st0, kb = min(st1, d.st_begin + mtot) - st0;  // CTA-local stages
+            const int gs0 = (ka + st0 - d.st_begin) / spg, gs1 = (kb - 1 + st0 - d.st_begin) / spg;
+            const int ng = gs1 - gs0 + 1;
+            // x -> prep (frag, scales, sums) and a clean partial table for this segment
+            prep_x(d.x, cols, s.prep, cwg);
+            for (int i = cwg * 32 + lane; i < ng * NCW * 16; i += NCW * 32) s.part[i] = 0.0f;
+            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+            const uint8_t *fragl = live ? s.prep + frag_lane(g, t) * 64 : s.zero;
+            const float *fbt = reinterpret_cast<const float *>(s.prep + (size_t)HB * 1024) + t, *sxt = fbt + HB * 4;
+            float acc0 = 0.0f, acc1 = 0.0f;
+            int cur = -1;
+            const int k0 = ka + team;
+            int slot = k0 % NSLOT, G = (k0 + st0 - d.st_begin) / spg, j = (k0 + st0 - d.st_begin) - G * spg;
+            unsigned parity = (k0 / NSLOT) & 1;
+            for (int k = k0; k < kb && !failed; k += NSTREAM) {
+                if (k != k0) {  // advance by NSTREAM stages
+                    slot += NSTREAM;
+                    if (slot >= NSLOT) slot -= NSLOT, parity ^= 1u;
+                    j += NSTREAM;
+                    while (j >= spg) j -= spg, G++;
+                }
+                if (!mbar_wait(&s.full[slot], parity)) {
+                    failed = true;
+                    set_dev_error(0x52u);
+                    break;
+                }
+                const int blk = j * SBLK + cw;
+                bool released = false;
+                if (G != cur) {
+                    if (cur >= 0) {
+                        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+                        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+                        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+                        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+                        if (t == 0) {
+                            float *p = s.part + ((cur - gs0) * NCW + cwg) * 16;
+                            p[g] = acc0;
+                            p[g + 8] = acc1;
+                        }
                     }
+                    cur = G;
+                    acc0 = acc1 = 0.0f;
                 }
-                cur = G;
-                acc0 = acc1 = 0.0f;
-            }
-            if (blk < nb) {
-                const uint8_t *r0p = ring_lane + slot * SLOTB, *r1p = r0p + 8 * ROWB;
-                const uint4 h0 = *reinterpret_cast<const uint4 *>(r0p);
-                const uint4 h1 = *reinterpret_cast<const uint4 *>(r1p);
-                const float2 dn0 = __half22float2(*reinterpret_cast<const __half2 *>(&h0.x));
-                const float2 dn1 = __half22float2(*reinterpret_cast<const __half2 *>(&h1.x));
-                const uint32_t x0 = h0.y >> sh, y0 = h0.z >> sh, z0 = h0.w >> sh;
-                const uint32_t x1 = h1.y >> sh, y1 = h1.z >> sh, z1 = h1.w >> sh;
-                const uint8_t *fr = fragl + blk * 2 * fstride;
-                const float *fbb = fbt + blk * 8, *sxb = sxt + blk * 8;
-                uint4 qa[2], qb[2], Bv[2][4];
-#pragma unroll
-                for (int half = 0; half < 2; half++) {
-                    qa[half] = *reinterpret_cast<const uint4 *>(r0p + qoff + half * 64);
-                    qb[half] = *reinterpret_cast<const uint4 *>(r1p + qoff + half * 64);
-                }
-                // The stage's bytes are in registers: hand the slot back to the producer
-                // now (arrive has release semantics, so these reads precede its refill).
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.empty[slot]);
-                released = true;
-#pragma unroll
-                for (int half = 0; half < 2; half++) {
-                    const uint4 *fp = reinterpret_cast<const uint4 *>(fr + half * fstride);
-#pragma unroll
-                    for (int q = 0; q < 4; q++) Bv[half][q] = fp[q];
-                }
-                // four independent chains: (half, byte pair 0/2 vs 1/3)
-                float dacc[2][2][4];
-#pragma unroll
-                for (int h = 0; h < 2; h++)
-#pragma unroll
-                    for (int p = 0; p < 2; p++)
-#pragma unroll
-                        for (int i = 0; i < 4; i++) dacc[h][p][i] = 0.0f;
-#pragma unroll
-                for (int iw = 0; iw < 4; iw++) {
+                if (blk < nb) {
+                    const uint8_t *r0p = ring_lane + slot * SLOTB, *r1p = r0p + 8 * ROWB;
+                    const uint4 h0 = *reinterpret_cast<const uint4 *>(r0p);
+                    const uint4 h1 = *reinterpret_cast<const uint4 *>(r1p);
+                    uint4 qa[2], qb[2], Bv[2][4];
 #pragma unroll
                     for (int half = 0; half < 2; half++) {
-                        const uint32_t wa[4] = {qa[half].x, qa[half].y, qa[half].z, qa[half].w};
-                        const uint32_t wb[4] = {qb[half].x, qb[half].y, qb[half].z, qb[half].w};
-                        const uint32_t bb[16] = {Bv[half][0].x, Bv[half][0].y, Bv[half][0].z, Bv[half][0].w,
-                                                 Bv[half][1].x, Bv[half][1].y, Bv[half][1].z, Bv[half][1].w,
-                                                 Bv[half][2].x, Bv[half][2].y, Bv[half][2].z, Bv[half][2].w,
-                                                 Bv[half][3].x, Bv[half][3].y, Bv[half][3].z, Bv[half][3].w};
-                        const uint32_t a = wa[iw], b = wb[iw], a8 = a >> 8, b8 = b >> 8;
-                        mma_f16(dacc[half][0], a & 0x000F000Fu, b & 0x000F000Fu, a & 0x00F000F0u, b & 0x00F000F0u,
-                                bb[(2 * iw) * 2], bb[(2 * iw) * 2 + 1]);
-                        mma_f16(dacc[half][1], a8 & 0x000F000Fu, b8 & 0x000F000Fu, a8 & 0x00F000F0u,
-                                b8 & 0x00F000F0u, bb[(2 * iw + 1) * 2], bb[(2 * iw + 1) * 2 + 1]);
+                        qa[half] = *reinterpret_cast<const uint4 *>(r0p + qoff + half * 64);
+                        qb[half] = *reinterpret_cast<const uint4 *>(r1p + qoff + half * 64);
                     }
-                }
+                    // The stage's bytes are in registers: hand the slot back to the producer
+                    // now (arrive has release semantics, so these reads precede its refill).
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.empty[slot]);
+                    released = true;
+                    const float2 dn0 = __half22float2(*reinterpret_cast<const __half2 *>(&h0.x));
+                    const float2 dn1 = __half22float2(*reinterpret_cast<const __half2 *>(&h1.x));
+                    const uint32_t x0 = h0.y >> sh, y0 = h0.z >> sh, z0 = h0.w >> sh;
+                    const uint32_t x1 = h1.y >> sh, y1 = h1.z >> sh, z1 = h1.w >> sh;
+                    const uint8_t *fr = fragl + blk * 2 * fstride;
+                    const float *fbb = fbt + blk * 8, *sxb = sxt + blk * 8;
 #pragma unroll
-                for (int half = 0; half < 2; half++) {
-                    // sub-block j = 4*half + t of this block, rows g and g+8
-                    uint32_t sc0, mm0, sc1, mm1;
-                    if (half == 0) {
-                        sc0 = x0 & 63u, mm0 = y0 & 63u, sc1 = x1 & 63u, mm1 = y1 & 63u;
-                    } else {
-                        sc0 = (z0 & 15u) | ((x0 >> 2) & 48u), mm0 = ((z0 >> 4) & 15u) | ((y0 >> 2) & 48u);
-                        sc1 = (z1 & 15u) | ((x1 >> 2) & 48u), mm1 = ((z1 >> 4) & 15u) | ((y1 >> 2) & 48u);
+                    for (int half = 0; half < 2; half++) {
+                        const uint4 *fp = reinterpret_cast<const uint4 *>(fr + half * fstride);
+#pragma unroll
+                        for (int q = 0; q < 4; q++) Bv[half][q] = fp[q];
                     }
-                    const float fb = fbb[half * 4], sx = sxb[half * 4];
-                    const float S0 = ((dacc[half][0][0] + dacc[half][1][0]) + (dacc[half][0][1] + dacc[half][1][1])) * fb;
-                    const float S1 = ((dacc[half][0][2] + dacc[half][1][2]) + (dacc[half][0][3] + dacc[half][1][3])) * fb;
-                    acc0 += (dn0.x * __uint2float_rn(sc0)) * S0 - (dn0.y * __uint2float_rn(mm0)) * sx;
-                    acc1 += (dn1.x * __uint2float_rn(sc1)) * S1 - (dn1.y * __uint2float_rn(mm1)) * sx;
+                    // four independent chains: (half, byte pair 0/2 vs 1/3)
+                    float dacc[2][2][4];
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                        for (int p = 0; p < 2; p++)
+#pragma unroll
+                            for (int i = 0; i < 4; i++) dacc[h][p][i] = 0.0f;
+#pragma unroll
+                    for (int iw = 0; iw < 4; iw++) {
+#pragma unroll
+                        for (int half = 0; half < 2; half++) {
+                            const uint32_t wa[4] = {qa[half].x, qa[half].y, qa[half].z, qa[half].w};
+                            const uint32_t wb[4] = {qb[half].x, qb[half].y, qb[half].z, qb[half].w};
+                            const uint32_t bb[16] = {Bv[half][0].x, Bv[half][0].y, Bv[half][0].z, Bv[half][0].w,
+                                                     Bv[half][1].x, Bv[half][1].y, Bv[half][1].z, Bv[half][1].w,
+                                                     Bv[half][2].x, Bv[half][2].y, Bv[half][2].z, Bv[half][2].w,
+                                                     Bv[half][3].x, Bv[half][3].y, Bv[half][3].z, Bv[half][3].w};
+                            const uint32_t a = wa[iw], b = wb[iw], a8 = a >> 8, b8 = b >> 8;
+                            mma_f16(dacc[half][0], a & 0x000F000Fu, b & 0x000F000Fu, a & 0x00F000F0u,
+                                    b & 0x00F000F0u, bb[(2 * iw) * 2], bb[(2 * iw) * 2 + 1]);
+                            mma_f16(dacc[half][1], a8 & 0x000F000Fu, b8 & 0x000F000Fu, a8 & 0x00F000F0u,
+                                    b8 & 0x00F000F0u, bb[(2 * iw + 1) * 2], bb[(2 * iw + 1) * 2 + 1]);
+                        }
+                    }
+#pragma unroll
+                    for (int half = 0; half < 2; half++) {
+                        // sub-block j = 4*half + t of this block, rows g and g+8
+                        uint32_t sc0, mm0, sc1, mm1;
+                        if (half == 0) {
+                            sc0 = x0 & 63u, mm0 = y0 & 63u, sc1 = x1 & 63u, mm1 = y1 & 63u;
+                        } else {
+                            sc0 = (z0 & 15u) | ((x0 >> 2) & 48u), mm0 = ((z0 >> 4) & 15u) | ((y0 >> 2) & 48u);
+                            sc1 = (z1 & 15u) | ((x1 >> 2) & 48u), mm1 = ((z1 >> 4) & 15u) | ((y1 >> 2) & 48u);
+                        }
+                        const float fb = fbb[half * 4], sx = sxb[half * 4];
+                        const float S0 =
+                            ((dacc[half][0][0] + dacc[half][1][0]) + (dacc[half][0][1] + dacc[half][1][1])) * fb;
+                        const float S1 =
+                            ((dacc[half][0][2] + dacc[half][1][2]) + (dacc[half][0][3] + dacc[half][1][3])) * fb;
+                        acc0 += (dn0.x * __uint2float_rn(sc0)) * S0 - (dn0.y * __uint2float_rn(mm0)) * sx;
+                        acc1 += (dn1.x * __uint2float_rn(sc1)) * S1 - (dn1.y * __uint2float_rn(mm1)) * sx;
+                    }
+                }
+                if (!released) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.empty[slot]);
                 }
             }
-            if (!released) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s.empty[slot]);
+            if (cur >= 0) {
+                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+                if (t == 0) {
+                    float *p = s.part + ((cur - gs0) * NCW + cwg) * 16;
+                    p[g] = acc0;
+                    p[g + 8] = acc1;
+                }
             }
-        }
-        if (cur >= 0) {
-            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-            if (t == 0) {
-                float *p = s.part + ((cur - g_first) * NCW + cwg) * 16;
-                p[g] = acc0;
-                p[g + 8] = acc1;
+            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+            // segment epilogue: sum the consumer warps' pieces per group (fixed order)
+            const bool head_cut = mi == m_first && (st0 - d.st_begin) % spg != 0;
+            const bool tail_cut = mi == m_last && (st1 - d.st_begin) % spg != 0 && st1 < d.st_begin + mtot;
+            for (int i = cwg * 32 + lane; i < ng * 16; i += NCW * 32) {
+                const int gl = i >> 4, r = i & 15, row = (gs0 + gl) * 16 + r;
+                float v = 0.0f;
+                for (int w = 0; w < NCW; w++) v += s.part[(gl * NCW + w) * 16 + r];
+                const bool cut = (gl == 0 && head_cut) || (gl == ng - 1 && tail_cut);
+                if (!cut) {
+                    if (row < d.rows) d.y[row] = v;
+                } else {
+                    // side 0: the group holding this CTA's first stage, side 1: any other (its last)
+                    const int ga = d.st_begin + (gs0 + gl) * spg;
+                    ws.part[(blockIdx.x * 2 + ((st0 >= ga && st0 < ga + spg) ? 0 : 1)) * 16 + r] = v;
+                    __threadfence();
+                }
             }
+            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
         }
     }
     if (failed) {
@@ -446,37 +500,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     if (nst <= 0) return;
 
-    // ---------------- epilogue: sum the consumer warps' pieces per group (fixed order)
+    // ---------------- groups cut by CTA boundaries: the last CTA to arrive at a group's
+    // counter sums the pieces in CTA order.  Both sides in one round trip.
     __shared__ int last_flag[2];
-    const int ng = g_last - g_first + 1;
-    const bool head_cut = st0 % spg != 0;                      // group g_first started in an earlier CTA
-    const bool tail_cut = st1 % spg != 0 && st1 < total;        // group g_last continues in a later CTA
-    for (int i = threadIdx.x; i < ng * 16; i += blockDim.x) {
-        const int gl = i >> 4, r = i & 15, row = (g_first + gl) * 16 + r;
-        float v = 0.0f;
-        for (int w = 0; w < NCW; w++) v += s.part[(gl * NCW + w) * 16 + r];
-        const bool cut = (gl == 0 && head_cut) || (gl == ng - 1 && tail_cut);
-        if (!cut) {
-            if (row < rows) y[row] = v;
-        } else {
-            // slot 0: this CTA's first group, slot 1: its last (a single cut-both group uses slot 0)
-            ws.part[(blockIdx.x * 2 + (gl == 0 ? 0 : 1)) * 16 + r] = v;
-            __threadfence();
-        }
-    }
-    if (!head_cut && !tail_cut) return;
-    __syncthreads();
-    // groups cut by CTA boundaries: the last CTA to arrive at a group's counter sums
-    // the pieces in CTA order.  Both sides in one round trip.
+    __shared__ int side_g[2], side_ca[2], side_cb[2], side_m[2];
     if (threadIdx.x < 2) {
         const int side = threadIdx.x;
-        const int gl = side == 0 ? 0 : ng - 1;
-        const bool mine = side == 0 ? head_cut : (tail_cut && !(ng == 1 && head_cut));
+        const int mi = side == 0 ? m_first : m_last;
+        const MatDesc &d = B.d[mi];
+        const int mtot = d.spg * ((d.rows + 15) >> 4);
+        const int ls0 = st0 - d.st_begin, ls1 = st1 - d.st_begin;  // stage range relative to the matrix
+        const bool head_cut = ls0 % d.spg != 0;
+        const bool tail_cut = ls1 % d.spg != 0 && ls1 < mtot;
+        // one group cut on both sides of a one-group range is side 0's job
+        const bool single = m_first == m_last && (ls0 / d.spg) == ((ls1 - 1) / d.spg);
+        const bool mine = side == 0 ? head_cut || (single && tail_cut) : (tail_cut && !single);
         int flag = 0;
         if (mine) {
-            const int G = g_first + gl;
-            const int c_a = owner_of(G * spg, total, gridDim.x), c_b = owner_of((G + 1) * spg - 1, total, gridDim.x);
-            flag = atomicAdd(&ws.cnt[G], 1u) == (unsigned)(c_b - c_a);
+            const int G = side == 0 ? ls0 / d.spg : (ls1 - 1) / d.spg;
+            const int ga = d.st_begin + G * d.spg;
+            const int c_a = owner_of(ga, B.total, gridDim.x), c_b = owner_of(ga + d.spg - 1, B.total, gridDim.x);
+            flag = atomicAdd(&ws.cnt[d.cnt_off + G], 1u) == (unsigned)(c_b - c_a);
+            side_g[side] = G, side_ca[side] = c_a, side_cb[side] = c_b, side_m[side] = mi;
         }
         last_flag[side] = flag;
     }
@@ -485,16 +530,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int side = threadIdx.x >> 4, r = threadIdx.x & 15;
         if (last_flag[side]) {
             __threadfence();
-            const int G = g_first + (side == 0 ? 0 : ng - 1);
-            const int c_a = owner_of(G * spg, total, gridDim.x), c_b = owner_of((G + 1) * spg - 1, total, gridDim.x);
+            const MatDesc &d = B.d[side_m[side]];
+            const int G = side_g[side], ga = d.st_begin + G * d.spg, ge = ga + d.spg;
             float v = 0.0f;
-            for (int c = c_a; c <= c_b; c++) {
+            for (int c = side_ca[side]; c <= side_cb[side]; c++) {
                 int cs0, cs1;
-                row_strip(total, c, gridDim.x, cs0, cs1);
-                v += __ldcg(&ws.part[(c * 2 + ((cs0 / spg == G) ? 0 : 1)) * 16 + r]);
+                row_strip(B.total, c, gridDim.x, cs0, cs1);
+                // CTA c stored G as side 0 if its range starts inside G, else as side 1
+                v += __ldcg(&ws.part[(c * 2 + ((cs0 >= ga && cs0 < ge) ? 0 : 1)) * 16 + r]);
             }
-            if (G * 16 + r < rows) y[G * 16 + r] = v;
-            if (r == 0) ws.cnt[G] = 0u;
+            if (G * 16 + r < d.rows) d.y[G * 16 + r] = v;
+            if (r == 0) ws.cnt[d.cnt_off + G] = 0u;
         }
     }
 }
@@ -504,14 +550,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // [part: grid*2*16 f32].  Zeroed once when allocated.
 constexpr int CNT_MAX = 1 << 16;  // groups of 16 rows: up to 1M rows
 inline size_t ws_part_off() { return (size_t)CNT_MAX * 4; }
-inline size_t ws_bytes(int rows, int cols, int grid) { return ws_part_off() + (size_t)grid * 2 * 16 * 4 + 256; }
-
-inline int max_groups_per_cta(int rows, int cols, int grid)
-{
-    const int nb = cols / 256, spg = (nb + SBLK - 1) / SBLK, total = ((rows + 15) / 16) * spg;
-    const int per = (total + grid - 1) / grid;
-    return per / spg + 2;
-}
+inline size_t ws_bytes(int grid) { return ws_part_off() + (size_t)grid * 2 * 16 * 4 + 256; }
 
 // Launch on `stream`; ws must hold ws_bytes(rows, grid) bytes, zeroed before first use
 // (the kernel leaves its counters at zero).
@@ -579,14 +618,65 @@ inline int cached_map(CUtensorMap *out, const void *w, int rows, int cols)
     return 0;
 }
 
-inline int launch(const void *w, int rows, int cols, const float *x, float *y, void *ws, int grid, int pdl,
-                  cudaStream_t stream)
+struct MatOp {
+    const void *w;
+    int rows, cols;
+    const float *x;
+    float *y;
+};
+
+// Shared memory for a batch over `grid` CTAs (0 if it exceeds the SM).
+inline size_t batch_smem(const MatOp *ops, int n, int grid, int *max_cols, int *max_groups)
 {
-    CUtensorMap map;
-    const int mrc = cached_map(&map, w, rows, cols);
-    if (mrc) return mrc;
-    const int mg = max_groups_per_cta(rows, cols, grid);
-    const size_t smem = smem_bytes(cols, mg);
+    long long total = 0;
+    int mc = 0;
+    for (int i = 0; i < n; i++) {
+        const int spg = (ops[i].cols / 256 + SBLK - 1) / SBLK;
+        total += (long long)spg * ((ops[i].rows + 15) / 16);
+        mc = ops[i].cols > mc ? ops[i].cols : mc;
+    }
+    const long long per = (total + grid - 1) / grid;
+    int mg = 1;
+    for (int i = 0; i < n; i++) {
+        const int spg = (ops[i].cols / 256 + SBLK - 1) / SBLK, groups = (ops[i].rows + 15) / 16;
+        const long long g = per / spg + 2;
+        const int gi = (int)(g < groups ? g : groups);
+        mg = gi > mg ? gi : mg;
+    }
+    *max_cols = mc;
+    *max_groups = mg;
+    return (size_t)NSLOT * SLOTB + prep_bytes(mc) + 64 + (size_t)mg * NCW * 64 + 2 * NSLOT * 8 + 64;
+}
+
+// Launch a batch of up to MAXB independent Q4_K matvecs on `stream`; ws holds
+// ws_bytes() bytes, zeroed before its first use (the kernel leaves it zeroed).
+inline int launch_batch(const MatOp *ops, int n, void *ws, int grid, int pdl, cudaStream_t stream)
+{
+    if (n < 1 || n > MAXB) return -1;
+    static Batch b;  // large: built host-side, passed by value as the kernel parameter
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    int st = 0, cnt = 0;
+    for (int i = 0; i < n; i++) {
+        const MatOp &o = ops[i];
+        if (o.cols > MAX_COLS || o.cols % 256 || o.rows < 1) return -1;
+        MatDesc &d = b.d[i];
+        const int mrc = cached_map(&d.map, o.w, o.rows, o.cols);
+        if (mrc) return mrc;
+        d.x = o.x;
+        d.y = o.y;
+        d.rows = o.rows;
+        d.cols = o.cols;
+        d.spg = (o.cols / 256 + SBLK - 1) / SBLK;
+        d.st_begin = st;
+        d.cnt_off = cnt;
+        st += d.spg * ((o.rows + 15) / 16);
+        cnt += (o.rows + 15) / 16;
+    }
+    if (cnt > CNT_MAX) return -1;
+    b.n = n;
+    b.total = st;
+    const size_t smem = batch_smem(ops, n, grid, &b.max_cols, &b.max_groups);
     if (smem > 227 * 1024) return -5;
     static size_t smem_set[64];
     int dev = 0;
@@ -597,7 +687,6 @@ inline int launch(const void *w, int rows, int cols, const float *x, float *y, v
             return -3;
         smem_set[dev] = smem;
     }
-    if ((rows + 15) / 16 > CNT_MAX) return -1;
     uint8_t *wsb = reinterpret_cast<uint8_t *>(ws);
     Ws wsd;
     wsd.cnt = reinterpret_cast<unsigned *>(wsb);
@@ -612,8 +701,15 @@ inline int launch(const void *w, int rows, int cols, const float *x, float *y, v
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, q4k_mmv_kernel, map, rows, cols, x, y, wsd, mg);
-    return e == cudaSuccess ? 0 : -4;
+    return cudaLaunchKernelEx(&cfg, q4k_mmv_kernel, b, wsd) == cudaSuccess ? 0 : -4;
+}
+
+inline bool fits(const MatOp *ops, int n, int grid)
+{
+    int mc, mg;
+    for (int i = 0; i < n; i++)
+        if (ops[i].cols > MAX_COLS || ops[i].cols % 256) return false;
+    return batch_smem(ops, n, grid, &mc, &mg) <= 227 * 1024;
 }
 
 }  // namespace q4kmmv
