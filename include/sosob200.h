@@ -170,6 +170,19 @@ int sbk_argmax(const float *v, size_t n, int32_t *out, void *ws, int pdl, void *
 int sbk_embed_row(const void *table, uint8_t dtype, size_t vocab, size_t hidden, const int32_t *token, float *out,
                   int pdl, void *stream);
 
+/* y = W . x for Q4_K weights, like sbk_matvec(SB_DTYPE_Q4_K, ...) and with the
+ * same results, for callers that must not allocate device memory (a host engine
+ * that owns a fixed memory budget, or code that may run while a CUDA graph is
+ * being captured in global mode, where an allocation breaks the capture).  No
+ * counterpart in the reference.  Its scratch is a fixed 96 KiB array compiled
+ * into the library (held by every GPU that loads it until exit), so it takes
+ * rows <= 262144 (returns -8 beyond that), cols <= 8192, and no cudaMalloc,
+ * cudaFree or allocating library call is made.  The first call on a device
+ * looks the array's device address up (cudaGetSymbolAddress): make it before
+ * any stream capture.  All calls share the array and it keeps the last call's
+ * contents: calls that overlap on the GPU race, so serialise them. */
+int sbk_matvec_q4k_noalloc(const void *w, size_t rows, size_t cols, const float *x, float *y, void *stream);
+
 /* Number of SMs the kernels size their grids for. */
 int sbk_num_sms(int device);
 

@@ -67,6 +67,8 @@ SIGNATURES = {
                                   ctypes.c_void_p]),
     "sbk_embed_row": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint8, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p,
                                      ctypes.c_int, ctypes.c_void_p]),
+    "sbk_matvec_q4k_noalloc": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_void_p]),
     "sbk_num_sms": (ctypes.c_int, [ctypes.c_int]),
     "sbk_take_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
 }

@@ -704,6 +704,56 @@ inline int launch_batch(const MatOp *ops, int n, void *ws, int grid, int pdl, cu
     return cudaLaunchKernelEx(&cfg, q4k_mmv_kernel, b, wsd) == cudaSuccess ? 0 : -4;
 }
 
+// As launch_batch, with the scratch given as explicit counter / partial pointers
+// (used by the entry point that allocates nothing, whose scratch is a fixed array).
+inline int launch_batch_with(const MatOp *ops, int n, Ws wsd, int grid, int pdl, cudaStream_t stream)
+{
+    if (n < 1 || n > MAXB) return -1;
+    static Batch b;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    int st = 0, cnt = 0;
+    for (int i = 0; i < n; i++) {
+        const MatOp &o = ops[i];
+        if (o.cols > MAX_COLS || o.cols % 256 || o.rows < 1) return -1;
+        MatDesc &d = b.d[i];
+        const int mrc = cached_map(&d.map, o.w, o.rows, o.cols);
+        if (mrc) return mrc;
+        d.x = o.x;
+        d.y = o.y;
+        d.rows = o.rows;
+        d.cols = o.cols;
+        d.spg = (o.cols / 256 + SBLK - 1) / SBLK;
+        d.st_begin = st;
+        d.cnt_off = cnt;
+        st += d.spg * ((o.rows + 15) / 16);
+        cnt += (o.rows + 15) / 16;
+    }
+    b.n = n;
+    b.total = st;
+    const size_t smem = batch_smem(ops, n, grid, &b.max_cols, &b.max_groups);
+    if (smem > 227 * 1024) return -5;
+    // Read the kernel's current dynamic shared-memory limit on every call and only
+    // ever RAISE it: launch_batch keeps its own record of what it set, so this
+    // launcher neither lowers the limit under it nor trusts a record of its own.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, q4k_mmv_kernel) != cudaSuccess) return -3;
+    if ((size_t)fa.maxDynamicSharedSizeBytes < smem &&
+        cudaFuncSetAttribute(q4k_mmv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return -3;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, q4k_mmv_kernel, b, wsd) == cudaSuccess ? 0 : -4;
+}
+
 inline bool fits(const MatOp *ops, int n, int grid)
 {
     int mc, mg;

@@ -5,3 +5,4 @@
 #include "norm.cuh"
 #include "decode_ops.cuh"
 #include "dispatch.cuh"
+#include "noalloc.cuh"
