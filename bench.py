@@ -6,10 +6,11 @@
 Workload (one "step"): the Q4_K decode matvec sweep at batch 1 -- one y = W.x
 over each matrix of a rotation set of 16 distinct 11008x4096 and 16 distinct
 4096x4096 Q4_K matrices (557 MB > 4x the 126 MB L2, so every step streams its
-weights from HBM).  The 32 launches of a step are captured in one CUDA graph
-with programmatic dependent launch between them, like consecutive projections
-of a decode step.  Weights are synthetic (uniform 4-bit codes / 6-bit scales,
-f16 d,dmin in U[1e-4,1e-3]), x ~ N(0,1), seeded.
+weights from HBM).  The 32 independent matvecs of a step are one
+GpuDispatch::matvec_lote, which the library runs as ONE launch
+(sbk_matvec_batch: the weight streams of all 32 matrices split evenly over all
+SMs), captured in a CUDA graph.  Weights are synthetic (uniform 4-bit codes /
+6-bit scales, f16 d,dmin in U[1e-4,1e-3]), x ~ N(0,1), seeded.
 
 Reported: `value` = algorithmic bytes (weights + x + y) per step / device time
 per step, device-resident inputs; `e2e` = the same through the C ABI's
@@ -59,13 +60,28 @@ def load_peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def profile_traffic() -> float | None:
-    """DRAM bytes per launch of the Q4_K 11008x4096 matvec from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "q4k_matvec_11008x4096.json")
+def profile_traffic() -> int | None:
+    """DRAM bytes (read + write) per launch of the step's kernel, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "q4k_mmv_batch_sweep.txt")
     if os.path.exists(p):
         with open(p) as f:
-            return json.load(f).get("dram_bytes_per_launch")
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1].split()[0])
     return None
+
+
+def bench_mats(rank: int):
+    """The rotation set of one rank: COPIES distinct matrices of each shape, with their x."""
+    from soso_b200 import synth
+    mats = []
+    for rows, cols in SHAPES:
+        for k in range(COPIES):
+            g = synth.rng("bench", rank, rows, cols, k)
+            w = synth.random_weights(Q4K, rows, cols, g)
+            x = synth.randn(cols, g)
+            mats.append((rows, cols, w, x))
+    return mats
 
 
 def dist_env():
@@ -166,14 +182,7 @@ def run_ours(args) -> None:
     from soso_b200._lib import SbkMvOp, SbMatvecOp, SbView, c_f32p, c_u8p, last_error, lib
     L = lib()
 
-    # rotation set: COPIES distinct matrices of each shape, per rank
-    mats = []
-    for rows, cols in SHAPES:
-        for k in range(COPIES):
-            g = synth.rng("bench", rank, rows, cols, k)
-            w = synth.random_weights(Q4K, rows, cols, g)
-            x = synth.randn(cols, g)
-            mats.append((rows, cols, w, x))
+    mats = bench_mats(rank)
     wd = [torch.from_numpy(m[2]).to(dev) for m in mats]
     xd = [torch.from_numpy(m[3]).to(dev) for m in mats]
     yd = [torch.empty(m[0], device=dev, dtype=torch.float32) for m in mats]
@@ -392,6 +401,41 @@ NCU_CASES = {  # name -> (dtype, rows, cols, copies): small cases for ncu captur
 }
 
 
+def run_batch_case(launches: int) -> None:
+    """The bench step's launch (one sbk_matvec_batch over the rank-0 rotation set), repeated
+    `launches` times without a graph (for ncu); checks two outputs against the oracle."""
+    import torch
+
+    import oracle
+    from soso_b200._lib import SbkMvOp, lib
+    L = lib()
+    dev = torch.device("cuda", 0)
+    mats = bench_mats(0)
+    wd = [torch.from_numpy(m[2]).to(dev) for m in mats]
+    xd = [torch.from_numpy(m[3]).to(dev) for m in mats]
+    yd = [torch.empty(m[0], device=dev, dtype=torch.float32) for m in mats]
+    batch = (SbkMvOp * len(mats))()
+    for i, ((rows, cols, _, _), w, x, y) in enumerate(zip(mats, wd, xd, yd)):
+        batch[i] = SbkMvOp(w.data_ptr(), rows, cols, x.data_ptr(), y.data_ptr())
+    s = torch.cuda.current_stream().cuda_stream
+    for _ in range(launches):
+        rc = L.sbk_matvec_batch(Q4K, batch, len(mats), 0, s)
+        if rc:
+            raise SystemExit(f"sbk_matvec_batch rc={rc}")
+    torch.cuda.synchronize()
+    worst = 0.0
+    for i in (0, len(mats) - 1):
+        rows, cols, w, x = mats[i]
+        t = oracle.matvec_f64(Q4K, w, rows, cols, x)
+        y = yd[i].cpu().numpy()
+        rms = float(np.sqrt(np.mean(t ** 2)))
+        worst = max(worst, float(np.max(np.abs(y - t) / np.maximum(np.abs(t), 1e-3 * rms))))
+    print(json.dumps({"case": "q4k_batch", "launches": launches, "matrices": len(mats),
+                      "bytes_per_launch": sum(algo_bytes(m[0], m[1]) for m in mats), "max_rel_err": worst}))
+    if worst > 1e-3:
+        raise SystemExit(1)
+
+
 def run_case(name: str, launches: int) -> None:
     """Plain launches of one kernel over a rotation of copies (for ncu); prints a check line."""
     import torch
@@ -429,7 +473,7 @@ def run_case(name: str, launches: int) -> None:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ncu-case", choices=sorted(NCU_CASES), default=None)
+    ap.add_argument("--ncu-case", choices=sorted(NCU_CASES) + ["q4k_batch"], default=None)
     ap.add_argument("--launches", type=int, default=12)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -438,6 +482,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
+    if args.ncu_case == "q4k_batch":
+        run_batch_case(args.launches)
+        return
     if args.ncu_case:
         run_case(args.ncu_case, args.launches)
         return

@@ -10,6 +10,7 @@
 // declined op returns 0 and the caller decides.
 #pragma once
 #include <chrono>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -58,7 +59,22 @@ struct sb_ctx {
     std::unordered_map<std::string, Resident> weights;
     void *scratch = nullptr;  // device staging for x / out of host calls
     size_t scratch_bytes = 0;
+    void *host_stage = nullptr;  // pinned mirror of scratch: one DMA each way per call
+    size_t host_stage_bytes = 0;
     sb_stats stats = {};
+
+    int ensure_host_stage(size_t bytes)
+    {
+        if (bytes <= host_stage_bytes) return 0;
+        if (host_stage) cudaFreeHost(host_stage);
+        host_stage = nullptr;
+        host_stage_bytes = 0;
+        size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+        cudaError_t e = cudaHostAlloc(&host_stage, want, cudaHostAllocPortable);
+        if (e != cudaSuccess) return fail("cudaHostAlloc(stage)", e);
+        host_stage_bytes = want;
+        return 0;
+    }
 
     int ensure_scratch(size_t bytes)
     {
@@ -158,6 +174,7 @@ extern "C" void sb_destroy(sb_ctx *c)
     for (auto &kv : c->weights)
         if (kv.second.ptr) cudaFree(kv.second.ptr);
     if (c->scratch) cudaFree(c->scratch);
+    if (c->host_stage) cudaFreeHost(c->host_stage);
     cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -198,18 +215,21 @@ static int run_matvecs(sb_ctx *c, const char *key, const sb_view *w, size_t rows
     int rc = c->resident(key, w, rows, cols, &r);
     if (rc <= 0) return rc;
     const size_t xb = n * cols * 4, yb = n * rows * 4, xoff = (xb + 255) & ~(size_t)255;
-    if (c->ensure_scratch(xoff + yb)) return -1;
+    if (c->ensure_scratch(xoff + yb) || c->ensure_host_stage(xoff + yb)) return -1;
     float *dx = (float *)c->scratch, *dy = (float *)((char *)c->scratch + xoff);
-    if ((e = cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+    char *hs = (char *)c->host_stage;
+    memcpy(hs, x, xb);
+    if ((e = cudaMemcpyAsync(dx, hs, xb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(x)", e);
     for (size_t t = 0; t < n; t++) {
         int k = sbk_matvec(w->dtype, r->ptr, rows, cols, dx + t * cols, dy + t * rows, 0, c->stream);
         if (k) return fail("sbk_matvec launch failed (" + std::to_string(k) + ")");
         c->stats.launches++;
     }
-    if ((e = cudaMemcpyAsync(out, dy, yb, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
+    if ((e = cudaMemcpyAsync(hs + xoff, dy, yb, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(out)", e);
     if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", e);
+    memcpy(out, hs + xoff, yb);
     c->stats.bytes_up += xb;
     c->stats.bytes_down += yb;
     c->stats.total_ns += now_ns() - t0;
@@ -239,7 +259,7 @@ extern "C" int sb_matvec_batch(sb_ctx *c, sb_matvec_op *ops, size_t nops, uint8_
     // pass 1: residency + scratch layout
     std::vector<Resident *> res(nops, nullptr);
     std::vector<size_t> xo(nops), yo(nops);
-    size_t off = 0;
+    size_t xend = 0, yb = 0;
     for (size_t i = 0; i < nops; i++) {
         done[i] = 0;
         sb_matvec_op &op = ops[i];
@@ -248,22 +268,26 @@ extern "C" int sb_matvec_batch(sb_ctx *c, sb_matvec_op *ops, size_t nops, uint8_
         if (rc < 0) return rc;
         if (rc == 0) res[i] = nullptr;
         if (!res[i]) continue;
-        xo[i] = off;
-        off += (op.cols * 4 + 255) & ~(size_t)255;
-        yo[i] = off;
-        off += (op.rows * 4 + 255) & ~(size_t)255;
+        xo[i] = xend;
+        xend += (op.cols * 4 + 255) & ~(size_t)255;
+        yo[i] = yb;
+        yb += (op.rows * 4 + 255) & ~(size_t)255;
     }
-    if (off == 0) return 1;
-    if (c->ensure_scratch(off)) return -1;
-    char *base = (char *)c->scratch;
-    // all inputs up, then the kernels grouped by dtype (one launch per batch of Q4_K
-    // matrices), then all outputs down, one wait
+    if (xend == 0) return 1;
+    // [all x | all y], mirrored in pinned host memory: the inputs go up in one copy and
+    // the outputs come down in one copy (a pageable copy per op costs far more than the op)
+    if (c->ensure_scratch(xend + yb) || c->ensure_host_stage(xend + yb)) return -1;
+    char *base = (char *)c->scratch, *hs = (char *)c->host_stage;
+    for (size_t i = 0; i < nops; i++)
+        if (res[i]) memcpy(hs + xo[i], ops[i].x, ops[i].cols * 4);
+    if ((e = cudaMemcpyAsync(base, hs, xend, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+        return fail("cudaMemcpyAsync(x)", e);
+    // the kernels grouped by dtype (one launch per batch of Q4_K matrices), one wait
     std::vector<sbk_mv_op> by_dtype[3];
     for (size_t i = 0; i < nops; i++) {
         if (!res[i]) continue;
         sb_matvec_op &op = ops[i];
-        if ((e = cudaMemcpyAsync(base + xo[i], op.x, op.cols * 4, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
-            return fail("cudaMemcpyAsync(x)", e);
+        yo[i] += xend;
         const int k = op.view->dtype == SB_DTYPE_Q4_K ? 0 : op.view->dtype == SB_DTYPE_Q6_K ? 1 : 2;
         by_dtype[k].push_back(sbk_mv_op{res[i]->ptr, op.rows, op.cols, (const float *)(base + xo[i]),
                                         (float *)(base + yo[i])});
@@ -277,14 +301,11 @@ extern "C" int sb_matvec_batch(sb_ctx *c, sb_matvec_op *ops, size_t nops, uint8_
             return fail("sbk_matvec_batch launch failed");
         c->stats.launches++;
     }
-    for (size_t i = 0; i < nops; i++) {
-        if (!res[i]) continue;
-        sb_matvec_op &op = ops[i];
-        if ((e = cudaMemcpyAsync(op.out, base + yo[i], op.rows * 4, cudaMemcpyDeviceToHost, c->stream)) !=
-            cudaSuccess)
-            return fail("cudaMemcpyAsync(out)", e);
-    }
+    if ((e = cudaMemcpyAsync(hs + xend, base + xend, yb, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
+        return fail("cudaMemcpyAsync(out)", e);
     if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", e);
+    for (size_t i = 0; i < nops; i++)
+        if (res[i]) memcpy(ops[i].out, hs + yo[i], ops[i].rows * 4);
     for (size_t i = 0; i < nops; i++) done[i] = res[i] ? 1 : 0;
     c->stats.total_ns += now_ns() - t0;
     return 1;
@@ -299,16 +320,18 @@ extern "C" int sb_rmsnorm(sb_ctx *c, float *x, const float *w, size_t n, float e
     cudaError_t e = cudaSetDevice(c->device);
     if (e != cudaSuccess) return fail("cudaSetDevice", e);
     const size_t b = (n * 4 + 255) & ~(size_t)255;
-    if (c->ensure_scratch(2 * b)) return -1;
+    if (c->ensure_scratch(2 * b) || c->ensure_host_stage(2 * b)) return -1;
     float *dx = (float *)c->scratch, *dw = (float *)((char *)c->scratch + b);
-    if ((e = cudaMemcpyAsync(dx, x, n * 4, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
-        return fail("cudaMemcpyAsync", e);
-    if ((e = cudaMemcpyAsync(dw, w, n * 4, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+    char *hs = (char *)c->host_stage;
+    memcpy(hs, x, n * 4);
+    memcpy(hs + b, w, n * 4);
+    if ((e = cudaMemcpyAsync(dx, hs, 2 * b, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync", e);
     if (sbk_rmsnorm(dx, nullptr, nullptr, dw, dx, 1, n, eps, c->stream)) return fail("sbk_rmsnorm launch failed");
-    if ((e = cudaMemcpyAsync(x, dx, n * 4, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
+    if ((e = cudaMemcpyAsync(hs, dx, n * 4, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync", e);
     if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", e);
+    memcpy(x, hs, n * 4);
     c->stats.launches++;
     return 1;
 }
