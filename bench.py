@@ -66,6 +66,7 @@ def profile_traffic() -> int | None:
     if os.path.exists(p):
         with open(p) as f:
             for line in f:
+                line = line.strip()
                 if line.startswith("dram_bytes_per_launch:"):
                     return int(line.split(":", 1)[1].split()[0])
     return None

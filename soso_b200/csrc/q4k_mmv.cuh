@@ -1,20 +1,29 @@
-// q4k_mmv.cuh -- Q4_K decode matvec y = W.x on sm_100a: TMA bulk-copy weight
-// stream + dequantisation straight into mma.sync bf16 fragments.
+// q4k_mmv.cuh -- Q4_K decode matvec y = W.x on sm_100a: TMA tensor-copy weight
+// stream + dequantisation straight into integer tensor-core MMA fragments.
 //
 // Same block layout and per-sub-block algebra as the reference
 // (crates/sosomodel/src/dequant.rs:150-191; gemm.rs:428-461):
-//   y[r] = sum_blocks sum_j ( d*sc_j * Sum_l q_l x_l  -  dmin*m_j * Sum_l x_l )
-// Only the inner Sum_l q_l x_l is done by the tensor core; scales, mins and
-// the row accumulation are f32 on the CUDA cores.
+//   y[r] = sum_blocks ( d * sum_j sc_j * Sum_l q_l x_l  -  dmin * sum_j m_j * Sum_l x_l )
 //
-// Numerics.  A code q (0..15) enters the MMA as the f16 bit pattern q itself,
-// i.e. the subnormal q * 2^-24 -- exact, no offset to cancel.  x enters as two
-// f16 columns, hi = f16(x * 2^s) and lo = f16(x * 2^s - hi) (22 significant
-// bits), with a power-of-two scale 2^s chosen per 32-element sub-block so the
-// largest element sits just below 2^15.  Products are exact and accumulate in
-// f32 inside the MMA; the epilogue multiplies by 2^(24 - s).  Each CTA builds
-// these x-side operands (fragments, scales, sub-block sums of x) in shared
-// memory while its weight stream is already in flight.
+// Numerics.  The 4-bit codes enter a u8 x s8 -> s32 MMA (m16n8k32) as bytes:
+// one AND of a qs word gives four low-nibble codes, another four high-nibble
+// codes times 16 (not shifted; the 16 is folded into the scales).  x enters as
+// four int8 pieces per element, x * 2^(7-ex) = p0 + p1/2^7 + p2/2^14 + p3/2^21
+// with 2^ex above the block's max |x| (28 significant bits, every residual
+// exact in f32), one piece per B column.  Products and their sums are exact
+// integers; the 6-bit scales multiply them in integer arithmetic (IMAD), and
+// only the per-block result is converted to f32 and scaled by d.  The min term
+// sum_j m_j * Sum x_j is one f16 MMA per block: m as f16 subnormals (exact)
+// against the sub-block sums of x split into hi/lo f16 halves.  So the only
+// rounding is f32 rounding of a few per-block terms and of the row sum.
+//
+// Fragment layout.  A lane (g = lane/4, t = lane%4) holds rows g and g+8 and,
+// of byte pair P = 2*duo + t/2 of the block, bytes 16*(t%2)..+15.  Its k-slots
+// of an MMA are thus all in one sub-block (2P for low nibbles, 2P+1 for high);
+// B column g carries piece g%4 of x for sub-block slot g/4 and is zero where a
+// lane's k-slots belong to the other slot, so D column pair (2t, 2t+1) holds
+// pieces 2(t%2), 2(t%2)+1 of sub-block 2*(2*duo + t/2) + nib.  Eight MMAs per
+// 16-row x 256-column tile, four independent accumulators of two each.
 //
 // Work split ("stream-K", deterministic).  Rows are taken 16 at a time (a
 // "group", the MMA's M); a stage is (group, 4 consecutive blocks).  The stages
@@ -29,13 +38,10 @@
 // ring of NSLOT slots, issued before griddepcontrol.wait so the stream overlaps
 // the previous kernel under programmatic dependent launch.  12 consumer warps
 // form 3 teams of 4; team j takes stages j, j+3, ... and within a team warp w
-// takes block w of the stage, so three stages are in compute at once.  Within
-// a block the two half-blocks and the even/odd MMAs form four independent
-// accumulation chains, so the tensor-core latency overlaps.  A
-// lane (g = lane/4, t = lane%4) holds rows g and g+8, chunk t: 8 m16n8k16 MMAs
-// give, in D column pair (2t, 2t+1), the hi/lo partial sums of sub-block t of
-// that half-block for both rows.  The 576-byte smem row stride is 64 mod 128,
-// so the fragment loads are bank-conflict-free.
+// takes block w of the stage, so three stages are in compute at once.  A warp
+// copies its block's bytes to registers and releases the slot before any
+// math.  The 576-byte smem row stride is 64 mod 128, so the fragment loads are
+// bank-conflict-free.
 #pragma once
 #include <cuda.h>
 
@@ -118,85 +124,105 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Lanes of an MMA whose B column meets their own k-slots: lane (g, t) with
-// g/4 == t/2.  Only they carry x; the other 16 lanes pass zeros.  Compact id:
-__host__ __device__ __forceinline__ int frag_lane(int g, int t) { return (g >> 2) * 8 + (g & 3) * 2 + (t & 1); }
-__host__ __device__ __forceinline__ bool frag_live(int g, int t) { return (g >> 2) == (t >> 1); }
+// u8 x s8 -> s32 tensor-core MMA, m16n8k32 (integer: exact).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
-// Code registers, as f16 subnormals without shifting where possible: for a
-// qs word w (bytes b0..b3), MMA m = 2*iw + sub uses bytes (sub, sub+2):
-//   low nibbles  (w >> 8*sub) & 0x000F000F  -> q * 2^-24
-//   high nibbles (w >> 8*sub) & 0x00F000F0  -> q * 2^-20 (the factor 16 is
-//   folded into the scale of the odd, high-nibble sub-blocks)
+// Prepared x, per CTA in shared memory, per block b of 256 elements:
+//   frag [nb][4 q][16 live lanes][4] u32 -- the int8 x pieces, in the B-fragment
+//        order of the u8 x s8 MMAs (see prep_x)
+//   mfr  [nb][2 g][4 t] u32 -- f16x2 of the sub-block sums of x, hi (g = 0) and
+//        lo (g = 1) halves: the B fragment of the MMA that forms the min terms
+//   fx   [nb] f32 -- 2^(ex - 11): weight of piece 0 (and the 1/16 of the high nibbles)
+//   fm   [nb] f32 -- 2^(9 + kx): undoes the scaling of the min-term MMA
+// (rounded to 16 B: the zero area read as uint4 follows it)
+__host__ __device__ inline size_t prep_bytes(int cols) { return ((size_t)(cols / 256) * (1024 + 32 + 8) + 15) & ~(size_t)15; }
 
-// Prepared x, per CTA in shared memory:
-//   frag [HB][16 live lanes][8 MMAs][2] u32 -- (b0, b1) f16x2 of that lane; the
-//        one its column does not use is 0
-//   fb   [HB*4] f32 -- 2^(24 - s) per sub-block (2^(20 - s) for odd sub-blocks)
-//   sx   [HB*4] f32 -- sum of x per sub-block (for the -dmin*m term)
-__host__ __device__ inline size_t prep_bytes(int cols) { return (size_t)(cols / 128) * 1024 + (size_t)cols / 32 * 8; }
-
-// x -> prep.  A warp takes one half-block (128 elements, 4 sub-blocks) at a
-// time; lane l loads elements 4l..4l+3, so sub-block s = l/8 and element
-// e = 4(l%8) + i of it.  Sub-block s is the low (s even) or high (s odd)
-// nibbles of pair s/2, element e is byte e of the pair: chunk t = 2(s/2) + e/16,
-// word (e%16)/4 = l%4, byte e%4 = i: MMA m = 2(l%4) + i%2, half i/2 of the
-// f16x2; its hi piece goes to column g = 2s, lo piece to g = 2s+1, register
-// b0 (s even) or b1 (s odd).  Per-sub-block max and sum over 8 lanes.
+// x -> prep.  A warp takes one block (256 elements) at a time; lane l holds
+// elements 4l..4l+3 and 128+4l..128+4l+3.  With 2^ex > max|x| over the block,
+// each element becomes four int8 pieces, x*2^(7-ex) = p0 + p1/2^7 + p2/2^14 +
+// p3/2^21 (28 bits, each residual exact in f32).  Element e of sub-block s,
+// piece p, goes to live lane L = 2(4*((s>>1)&1) + p) + (e>>4), register
+// 4*(2*(s>>2) + (s&1)) + 2*((e>>3)&1) + ((e>>2)&1), byte e&3.
 __device__ __forceinline__ void prep_x(const float *__restrict__ x, int cols, uint8_t *prep, int cw)
 {
-    const int HB = cols / 128, l = threadIdx.x & 31, s = l >> 3, q = l & 7;
-    const int t = 2 * (s >> 1) + (q >> 2), m0 = 2 * (l & 3);
-    // u16 offsets within one half-block (512 u16) for element i = 0; i adds (i%2)*4 + i/2
-    const int o_hi = ((frag_lane(2 * s, t) * 8 + m0) * 2 + (s & 1)) * 2;
-    const int o_lo = ((frag_lane(2 * s + 1, t) * 8 + m0) * 2 + (s & 1)) * 2;
-    unsigned short *f16p = reinterpret_cast<unsigned short *>(prep);
-    float *fb = reinterpret_cast<float *>(prep + (size_t)HB * 1024);
-    // zero the frag area (half of it is never written: the b-register a column does not use)
-    uint4 *z = reinterpret_cast<uint4 *>(prep);
-    for (int i = cw * 32 + l; i < HB * 64; i += NCW * 32) z[i] = make_uint4(0, 0, 0, 0);
-    float4 v[4];
+    const int nb = cols / 256, l = threadIdx.x & 31;
+    uint32_t *frag = reinterpret_cast<uint32_t *>(prep);
+    unsigned short *mfr = reinterpret_cast<unsigned short *>(prep + (size_t)nb * 1024);
+    float *fx = reinterpret_cast<float *>(prep + (size_t)nb * 1056), *fm = fx + nb;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    for (int b = cw; b < nb; b += NCW) {
+        const float4 va = x4[b * 64 + l], vb = x4[b * 64 + 32 + l];
+        float mx = fmaxf(fmaxf(fmaxf(fabsf(va.x), fabsf(va.y)), fmaxf(fabsf(va.z), fabsf(va.w))),
+                         fmaxf(fmaxf(fabsf(vb.x), fabsf(vb.y)), fmaxf(fabsf(vb.z), fabsf(vb.w))));
+        float sa = (va.x + va.y) + (va.z + va.w), sbv = (vb.x + vb.y) + (vb.z + vb.w);
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-        const int hb = cw + r * NCW;
-        v[r] = hb < HB ? *reinterpret_cast<const float4 *>(x + hb * 128 + 4 * l) : make_float4(0, 0, 0, 0);
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-    auto one = [&](float4 a, int hb) {
-        float mx = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
-        float sm = (a.x + a.y) + (a.z + a.w);
+        for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
 #pragma unroll
         for (int o = 1; o < 8; o <<= 1) {
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            sm += __shfl_xor_sync(0xffffffffu, sm, o);
+            sa += __shfl_xor_sync(0xffffffffu, sa, o);
+            sbv += __shfl_xor_sync(0xffffffffu, sbv, o);
         }
+        // 2^ex > max|x| (ex from the biased exponent of the max), clamped for zero / non-finite input
         const uint32_t mxb = __float_as_uint(mx);
-        // 2^(E-126) > max|x| for a normal max with biased exponent E; scale it below 2^15
         int ex = (int)(mxb >> 23) - 126;
         ex = (mxb == 0u || mxb >= 0x7f800000u) ? 0 : ex < -100 ? -100 : ex > 100 ? 100 : ex;
-        const float scale = __uint_as_float((uint32_t)(127 + 15 - ex) << 23);
-        const int c = hb * 4 + s;
-        if (q == 0) {
-            fb[c] = __uint_as_float((uint32_t)(127 + 9 + ex - (s & 1) * 4) << 23);  // 2^(24 - (15 - ex)) / 16^(s&1)
-            fb[HB * 4 + c] = sm;
-        }
-        unsigned short *hp = f16p + (size_t)hb * 512;
-        const float xa[4] = {a.x, a.y, a.z, a.w};
+        const float scl = __uint_as_float((uint32_t)(127 + 7 - ex) << 23);
+        auto pieces = [&](float4 v4, int n) {
+            const int sblk = n >> 5, e = n & 31;
+            const int sig = (sblk >> 1) & 1, q = 2 * (sblk >> 2) + (sblk & 1);
+            const int word = 2 * ((e >> 3) & 1) + ((e >> 2) & 1), tp = e >> 4;
+            const float xs[4] = {v4.x, v4.y, v4.z, v4.w};
+            uint32_t pk[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float xv = xa[i] * scale;
-            const __half hi = __float2half_rn(xv), lo = __float2half_rn(xv - __half2float(hi));
-            const int d = (i & 1) * 4 + (i >> 1);
-            hp[o_hi + d] = __half_as_ushort(hi);
-            hp[o_lo + d] = __half_as_ushort(lo);
-        }
-    };
+            for (int i = 0; i < 4; i++) {
+                float v = xs[i] * scl;
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-        const int hb = cw + r * NCW;
-        if (hb < HB) one(v[r], hb);
+                for (int pc = 0; pc < 4; pc++) {
+                    float r = rintf(v);
+                    r = fminf(fmaxf(r, -127.0f), 127.0f);
+                    pk[pc] |= ((uint32_t)__float2int_rn(r) & 0xFFu) << (8 * i);
+                    v = (v - r) * 128.0f;
+                }
+            }
+#pragma unroll
+            for (int pc = 0; pc < 4; pc++) {
+                const int L = 2 * (4 * sig + pc) + tp;
+                frag[((b * 4 + q) * 16 + L) * 4 + word] = pk[pc];
+            }
+        };
+        pieces(va, 4 * l);
+        pieces(vb, 128 + 4 * l);
+        // sub-block sums -> f16 hi/lo with one power-of-two scale per block (max below 2^15)
+        float smx = fmaxf(fabsf(sa), fabsf(sbv));
+#pragma unroll
+        for (int o = 8; o < 32; o <<= 1) smx = fmaxf(smx, __shfl_xor_sync(0xffffffffu, smx, o));
+        const uint32_t smb = __float_as_uint(smx);
+        int kx = (int)(smb >> 23) - 126;
+        kx = (smb == 0u || smb >= 0x7f800000u) ? 0 : kx < -100 ? -100 : kx > 100 ? 100 : kx;
+        const float ms = __uint_as_float((uint32_t)(127 + 15 - kx) << 23);
+        if ((l & 7) == 0) {
+            const float sv[2] = {sa, sbv};
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                const int sidx = 4 * c + (l >> 3);
+                const float v = sv[c] * ms;
+                const __half hi = __float2half_rn(v), lo = __float2half_rn(v - __half2float(hi));
+                mfr[((b * 2 + 0) * 4 + (sidx >> 1)) * 2 + (sidx & 1)] = __half_as_ushort(hi);
+                mfr[((b * 2 + 1) * 4 + (sidx >> 1)) * 2 + (sidx & 1)] = __half_as_ushort(lo);
+            }
+        }
+        if (l == 0) {
+            fx[b] = __uint_as_float((uint32_t)(127 + ex - 11) << 23);
+            fm[b] = __uint_as_float((uint32_t)(127 + 9 + kx) << 23);
+        }
     }
-    for (int hb = cw + 4 * NCW; hb < HB; hb += NCW) one(*reinterpret_cast<const float4 *>(x + hb * 128 + 4 * l), hb);
 }
 
 struct Smem {
@@ -331,15 +357,20 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mmv_kernel(const __grid_consta
     } else {
         // ---------------- consumers
         const int cwg = warp - 1;  // 0 .. NCW-1
-        const int team = cwg / NCONS, cw = cwg % NCONS, g = lane >> 2, t = lane & 3, sh = 8 * t;
-        const bool live = frag_live(g, t);
-        const int fstride = live ? 1024 : 0;
+        const int team = cwg / NCONS, cw = cwg % NCONS, g = lane >> 2, t = lane & 3, q2 = t >> 1;
+        // B columns are (sub-block slot g/4, piece g%4): a lane carries x only where its
+        // k-slots (sub-block slot t/2) meet its column
+        const bool live = (g >> 2) == q2, mlive = g < 2;
         const uint8_t *ring_lane = s.ring + g * ROWB + cw * 144;  // + slot * SLOTB
-        const int qoff = 16 + t * 16;
+        const int qoff = 16 + t * 16;                               // + 64 * duo
+        const int sc_sh = 16 * q2;
+        // min-term A fragment: m of sub-blocks 2t, 2t+1 as f16 subnormals (byte -> u16 lane)
+        const uint32_t sel_m = (uint32_t)((2 * t) & 3) | 0x40u | ((uint32_t)(((2 * t) & 3) + 1) << 8) | 0x4000u;
+        const float lanefac = (t & 1) ? 1.0f / 16384.0f : 1.0f;  // pieces 2, 3 weigh 2^-14 of pieces 0, 1
         griddep_wait();  // x of every matrix is written by the previous kernel
         for (int mi = m_first; mi <= m_last && nst > 0; mi++) {
             const MatDesc &d = B.d[mi];
-            const int cols = d.cols, nb = cols / 256, spg = d.spg, HB = cols / 128;
+            const int cols = d.cols, nb = cols / 256, spg = d.spg;
             const int mtot = spg * ((d.rows + 15) >> 4);
             const int ka = max(st0, d.st_begin) - st0, kb = min(st1, d.st_begin + mtot) - st0;  // CTA-local stages
             const int gs0 = (ka + st0 - d.st_begin) / spg, gs1 = (kb - 1 + st0 - d.st_begin) / spg;
@@ -348,8 +379,14 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mmv_kernel(const __grid_consta
             prep_x(d.x, cols, s.prep, cwg);
             for (int i = cwg * 32 + lane; i < ng * NCW * 16; i += NCW * 32) s.part[i] = 0.0f;
             asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-            const uint8_t *fragl = live ? s.prep + frag_lane(g, t) * 64 : s.zero;
-            const float *fbt = reinterpret_cast<const float *>(s.prep + (size_t)HB * 1024) + t, *sxt = fbt + HB * 4;
+            // x-side fragments of this lane (lanes without x read zeros: stride 0 into s.zero)
+            const uint4 *bfl = live ? reinterpret_cast<const uint4 *>(s.prep) + 2 * g + (t & 1)
+                                    : reinterpret_cast<const uint4 *>(s.zero);
+            const int bq = live ? 16 : 0, bb = live ? 64 : 0;
+            const uint32_t *mfl = mlive ? reinterpret_cast<const uint32_t *>(s.prep + (size_t)nb * 1024) + g * 4 + t
+                                        : reinterpret_cast<const uint32_t *>(s.zero);
+            const int mb = mlive ? 8 : 0;
+            const float *fxp = reinterpret_cast<const float *>(s.prep + (size_t)nb * 1056), *fmp = fxp + nb;
             float acc0 = 0.0f, acc1 = 0.0f;
             int cur = -1;
             const int k0 = ka + team;
@@ -388,72 +425,67 @@ __global__ void __launch_bounds__(THREADS, 1) q4k_mmv_kernel(const __grid_consta
                     const uint8_t *r0p = ring_lane + slot * SLOTB, *r1p = r0p + 8 * ROWB;
                     const uint4 h0 = *reinterpret_cast<const uint4 *>(r0p);
                     const uint4 h1 = *reinterpret_cast<const uint4 *>(r1p);
-                    uint4 qa[2], qb[2], Bv[2][4];
-#pragma unroll
-                    for (int half = 0; half < 2; half++) {
-                        qa[half] = *reinterpret_cast<const uint4 *>(r0p + qoff + half * 64);
-                        qb[half] = *reinterpret_cast<const uint4 *>(r1p + qoff + half * 64);
-                    }
+                    // rows g / g+8: 16 bytes of pair 2*duo + t/2 each (bytes 16*(t&1).. of the pair)
+                    const uint4 qa0 = *reinterpret_cast<const uint4 *>(r0p + qoff);
+                    const uint4 qa1 = *reinterpret_cast<const uint4 *>(r0p + qoff + 64);
+                    const uint4 qb0 = *reinterpret_cast<const uint4 *>(r1p + qoff);
+                    const uint4 qb1 = *reinterpret_cast<const uint4 *>(r1p + qoff + 64);
                     // The stage's bytes are in registers: hand the slot back to the producer
                     // now (arrive has release semantics, so these reads precede its refill).
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&s.empty[slot]);
                     released = true;
+                    const uint4 *bp = bfl + blk * bb;
+                    const uint4 B0 = bp[0], B1 = bp[bq], B2 = bp[2 * bq], B3 = bp[3 * bq];
+                    const uint32_t mbv = mfl[blk * mb];
+                    // D[2*duo + nib]: sub-block 2*(2*duo + t/2) + nib; columns (2t, 2t+1) = pieces
+                    // 2(t&1), 2(t&1)+1; rows g (c0, c1) and g+8 (c2, c3).  Integer, exact.
+                    constexpr uint32_t LO = 0x0F0F0F0Fu, HI = 0xF0F0F0F0u;
+                    int D[4][4];
+#pragma unroll
+                    for (int a = 0; a < 4; a++)
+#pragma unroll
+                        for (int c = 0; c < 4; c++) D[a][c] = 0;
+                    mma_u8s8(D[0], qa0.x & LO, qb0.x & LO, qa0.y & LO, qb0.y & LO, B0.x, B0.y);
+                    mma_u8s8(D[1], qa0.x & HI, qb0.x & HI, qa0.y & HI, qb0.y & HI, B1.x, B1.y);
+                    mma_u8s8(D[2], qa1.x & LO, qb1.x & LO, qa1.y & LO, qb1.y & LO, B2.x, B2.y);
+                    mma_u8s8(D[3], qa1.x & HI, qb1.x & HI, qa1.y & HI, qb1.y & HI, B3.x, B3.y);
+                    mma_u8s8(D[0], qa0.z & LO, qb0.z & LO, qa0.w & LO, qb0.w & LO, B0.z, B0.w);
+                    mma_u8s8(D[1], qa0.z & HI, qb0.z & HI, qa0.w & HI, qb0.w & HI, B1.z, B1.w);
+                    mma_u8s8(D[2], qa1.z & LO, qb1.z & LO, qa1.w & LO, qb1.w & LO, B2.z, B2.w);
+                    mma_u8s8(D[3], qa1.z & HI, qb1.z & HI, qa1.w & HI, qb1.w & HI, B3.z, B3.w);
+                    // 6-bit scales and mins (dequant.rs:150-167 packing), rows g and g+8
+                    auto sc_pack = [&](const uint4 h, int (&c)[4], uint32_t &am) {
+                        const uint32_t S0 = h.y & 0x3F3F3F3Fu;
+                        const uint32_t S1 = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+                        const uint32_t M0 = h.z & 0x3F3F3F3Fu;
+                        const uint32_t M1 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+                        const uint32_t s0 = S0 >> sc_sh, s1 = S1 >> sc_sh;
+                        // low-nibble sub-blocks carry codes x1, high-nibble ones x16: scale the former by 16
+                        c[0] = (int)((s0 << 4) & 0xFF0u);
+                        c[1] = (int)((s0 >> 8) & 0xFFu);
+                        c[2] = (int)((s1 << 4) & 0xFF0u);
+                        c[3] = (int)((s1 >> 8) & 0xFFu);
+                        am = __byte_perm(t < 2 ? M0 : M1, 0u, sel_m);
+                    };
+                    int c0[4], c1[4];
+                    uint32_t am0, am1;
+                    sc_pack(h0, c0, am0);
+                    sc_pack(h1, c1, am1);
+                    // min terms: sum_j m_j * sumx_j for rows g, g+8 (column pair 0/1 = hi/lo, lane t = 0)
+                    float dm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    mma_f16(dm, am0, am1, 0u, 0u, mbv, 0u);
+                    const int I00 = c0[0] * D[0][0] + c0[1] * D[1][0] + c0[2] * D[2][0] + c0[3] * D[3][0];
+                    const int I01 = c0[0] * D[0][1] + c0[1] * D[1][1] + c0[2] * D[2][1] + c0[3] * D[3][1];
+                    const int I10 = c1[0] * D[0][2] + c1[1] * D[1][2] + c1[2] * D[2][2] + c1[3] * D[3][2];
+                    const int I11 = c1[0] * D[0][3] + c1[1] * D[1][3] + c1[2] * D[2][3] + c1[3] * D[3][3];
                     const float2 dn0 = __half22float2(*reinterpret_cast<const __half2 *>(&h0.x));
                     const float2 dn1 = __half22float2(*reinterpret_cast<const __half2 *>(&h1.x));
-                    const uint32_t x0 = h0.y >> sh, y0 = h0.z >> sh, z0 = h0.w >> sh;
-                    const uint32_t x1 = h1.y >> sh, y1 = h1.z >> sh, z1 = h1.w >> sh;
-                    const uint8_t *fr = fragl + blk * 2 * fstride;
-                    const float *fbb = fbt + blk * 8, *sxb = sxt + blk * 8;
-#pragma unroll
-                    for (int half = 0; half < 2; half++) {
-                        const uint4 *fp = reinterpret_cast<const uint4 *>(fr + half * fstride);
-#pragma unroll
-                        for (int q = 0; q < 4; q++) Bv[half][q] = fp[q];
-                    }
-                    // four independent chains: (half, byte pair 0/2 vs 1/3)
-                    float dacc[2][2][4];
-#pragma unroll
-                    for (int h = 0; h < 2; h++)
-#pragma unroll
-                        for (int p = 0; p < 2; p++)
-#pragma unroll
-                            for (int i = 0; i < 4; i++) dacc[h][p][i] = 0.0f;
-#pragma unroll
-                    for (int iw = 0; iw < 4; iw++) {
-#pragma unroll
-                        for (int half = 0; half < 2; half++) {
-                            const uint32_t wa[4] = {qa[half].x, qa[half].y, qa[half].z, qa[half].w};
-                            const uint32_t wb[4] = {qb[half].x, qb[half].y, qb[half].z, qb[half].w};
-                            const uint32_t bb[16] = {Bv[half][0].x, Bv[half][0].y, Bv[half][0].z, Bv[half][0].w,
-                                                     Bv[half][1].x, Bv[half][1].y, Bv[half][1].z, Bv[half][1].w,
-                                                     Bv[half][2].x, Bv[half][2].y, Bv[half][2].z, Bv[half][2].w,
-                                                     Bv[half][3].x, Bv[half][3].y, Bv[half][3].z, Bv[half][3].w};
-                            const uint32_t a = wa[iw], b = wb[iw], a8 = a >> 8, b8 = b >> 8;
-                            mma_f16(dacc[half][0], a & 0x000F000Fu, b & 0x000F000Fu, a & 0x00F000F0u,
-                                    b & 0x00F000F0u, bb[(2 * iw) * 2], bb[(2 * iw) * 2 + 1]);
-                            mma_f16(dacc[half][1], a8 & 0x000F000Fu, b8 & 0x000F000Fu, a8 & 0x00F000F0u,
-                                    b8 & 0x00F000F0u, bb[(2 * iw + 1) * 2], bb[(2 * iw + 1) * 2 + 1]);
-                        }
-                    }
-#pragma unroll
-                    for (int half = 0; half < 2; half++) {
-                        // sub-block j = 4*half + t of this block, rows g and g+8
-                        uint32_t sc0, mm0, sc1, mm1;
-                        if (half == 0) {
-                            sc0 = x0 & 63u, mm0 = y0 & 63u, sc1 = x1 & 63u, mm1 = y1 & 63u;
-                        } else {
-                            sc0 = (z0 & 15u) | ((x0 >> 2) & 48u), mm0 = ((z0 >> 4) & 15u) | ((y0 >> 2) & 48u);
-                            sc1 = (z1 & 15u) | ((x1 >> 2) & 48u), mm1 = ((z1 >> 4) & 15u) | ((y1 >> 2) & 48u);
-                        }
-                        const float fb = fbb[half * 4], sx = sxb[half * 4];
-                        const float S0 =
-                            ((dacc[half][0][0] + dacc[half][1][0]) + (dacc[half][0][1] + dacc[half][1][1])) * fb;
-                        const float S1 =
-                            ((dacc[half][0][2] + dacc[half][1][2]) + (dacc[half][0][3] + dacc[half][1][3])) * fb;
-                        acc0 += (dn0.x * __uint2float_rn(sc0)) * S0 - (dn0.y * __uint2float_rn(mm0)) * sx;
-                        acc1 += (dn1.x * __uint2float_rn(sc1)) * S1 - (dn1.y * __uint2float_rn(mm1)) * sx;
-                    }
+                    const float fxl = fxp[blk] * lanefac, fml = fmp[blk];
+                    acc0 += (dn0.x * fxl) * fmaf(__int2float_rn(I01), 1.0f / 128.0f, __int2float_rn(I00)) -
+                            (dn0.y * fml) * (dm[0] + dm[1]);
+                    acc1 += (dn1.x * fxl) * fmaf(__int2float_rn(I11), 1.0f / 128.0f, __int2float_rn(I10)) -
+                            (dn1.y * fml) * (dm[2] + dm[3]);
                 }
                 if (!released) {
                     __syncwarp();
