@@ -95,6 +95,69 @@ int sb_get_stats(const sb_ctx *ctx, sb_stats *out);
 /* Thread-local description of the last error. */
 const char *sb_last_error(void);
 
+/* ---- whole-token decode (device-resident model, one CUDA graph per token) -- */
+
+/* Mirror of `MatDec` (gpu.rs:92-98): one matrix of the model, rows = out, cols = in. */
+typedef struct {
+    const char *key;
+    sb_view view;
+    size_t rows, cols;
+} sb_mat;
+
+/* Mirror of `MoeDec` (gpu.rs:130-137): router [n_exp x hidden], experts[3*e + {0,1,2}] =
+ * gate, up, down of expert e; optional shared expert (3 matrices) with an optional
+ * sigmoid gate row [hidden] (layer.rs:1883-1907). */
+typedef struct {
+    size_t n_exp, top_k, ffn;
+    sb_mat router;
+    const sb_mat *experts;
+    const sb_mat *shared;
+    const float *shared_gate;
+} sb_moe_plan;
+
+/* One layer: `CapaDec` (gpu.rs:138-148) with GQA attention (`GatedDec`, gpu.rs:113-122;
+ * bias and QK-norm as layer.rs:1146-1181, RoPE as layer.rs:1184-1193) and a dense SwiGLU
+ * FFN (layer.rs:1352-1389) or, when moe != NULL, a MoE FFN. */
+typedef struct {
+    size_t heads, kv_heads, head_dim;
+    float theta;
+    int neox;
+    const float *q_norm, *k_norm; /* [head_dim] each, or NULL */
+    const float *qkv_bias;        /* [heads*hd + 2*kv_heads*hd] stacked q|k|v, or NULL */
+    const float *norm_attn, *norm_ffn;
+    sb_mat q, k, v, o;
+    sb_mat gate, up, down;
+    const sb_moe_plan *moe;
+} sb_layer_plan;
+
+/* `DecodePlan` (gpu.rs:150-158) plus the embedding table (for device-side greedy
+ * decoding; view.bytes may be NULL) and the KV context length to allocate. */
+typedef struct {
+    const sb_layer_plan *layers;
+    size_t n_layers;
+    size_t hidden, vocab, ctx;
+    float eps;
+    const float *final_norm;
+    sb_mat lm_head;
+    sb_mat embed;
+} sb_decode_plan;
+
+/* `GpuDispatch::decode_preparar` (gpu.rs:654-657): weights resident, KV caches
+ * (f16, [ctx][kv_heads*head_dim] per layer, kv.rs:21-56) and buffers allocated, the
+ * per-token CUDA graphs captured.  1 = ready, 0 = the plan has something this
+ * backend does not run, <0 = error.  Resets the KV caches. */
+int sb_decode_prepare(sb_ctx *ctx, const sb_decode_plan *plan);
+/* `GpuDispatch::decode_token` (gpu.rs:675-684): one token from its embedding row
+ * (host f32[hidden]) at position pos; logits (host f32[vocab]) out, and when
+ * kv_rows != NULL the new f16 K and V rows of every layer, in layer order
+ * ([k | v] per layer).  1 = done, 0 = not prepared, <0 = error. */
+int sb_decode_token(sb_ctx *ctx, const float *embed, size_t pos, float *logits, uint16_t *kv_rows);
+/* n greedy steps entirely on the device (graph per token, no host round trip):
+ * positions pos .. pos+n-1; the token fed at step i is prompt[i] while i < n_prompt,
+ * else the argmax of the previous step (runtime.rs:2021-2028).  tokens_out[i] = the
+ * argmax produced at step i.  Needs plan.embed.  1 = done, 0 = not prepared, <0 = error. */
+int sb_decode_greedy(sb_ctx *ctx, const int32_t *prompt, size_t n_prompt, size_t pos, size_t n, int32_t *tokens_out);
+
 /* ---- kernels on device pointers --------------------------------------- */
 
 /* Bytes per row for (dtype, cols), 0 if cols is not a whole number of blocks
@@ -153,6 +216,9 @@ size_t sbk_attn_ws_bytes(size_t heads, size_t kv_heads, size_t head_dim, size_t 
  * Replaces mo_attn_split + mo_attn_combine (gemma_capa.cu:765-926). */
 int sbk_attn_decode(const float *q, const uint16_t *kcache, const uint16_t *vcache, float *out, const int32_t *pos,
                     size_t heads, size_t kv_heads, size_t head_dim, size_t ctx, void *ws, int pdl, void *stream);
+
+/* out = silu(gate) * up, elementwise (`swiglu_inplace`, crates/soso-llm-core/src/gemm.rs:210-226). */
+int sbk_swiglu(const float *gate, const float *up, float *out, size_t n, int pdl, void *stream);
 
 /* Router: softmax over n_exp logits, stable top-k by weight, renormalised
  * (gemm::topk_softmax, crates/soso-llm-core/src/gemm.rs:62-91); idx/wts in rank

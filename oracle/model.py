@@ -1,0 +1,92 @@
+"""CPU restatement of the reference's dense decode step -- TEST INFRASTRUCTURE ONLY.
+
+The checker for soso_b200's whole-token decode engine: one token of a dense GQA
+decoder, op by op, with the oracle's restated kernels (oracle.c), in the order
+of crates/soso-llm-core/src/layer.rs:947-1398 and runtime.rs:787-802,
+1976-2028.  Only tests import this module.
+
+The model is the dict of soso_b200.decode.synth_model (reference block layouts,
+keyed like the reference's tensors); cfg is a DenseConfig.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+import oracle
+
+
+class DenseOracle:
+    def __init__(self, cfg, model: dict):
+        self.cfg = cfg
+        self.m = model
+        self.k = [np.zeros((cfg.ctx, cfg.kv_dim), np.uint16) for _ in range(cfg.n_layers)]
+        self.v = [np.zeros((cfg.ctx, cfg.kv_dim), np.uint16) for _ in range(cfg.n_layers)]
+        self._embd = None
+
+    def _mv(self, name: str, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        dt = self.cfg.dtypes[name.split(".")[-1]]
+        return oracle.matvec(dt, self.m[name], rows, cols, x)
+
+    def embed(self, token: int) -> np.ndarray:
+        """Runtime::embed_token (runtime.rs:787-802): the dequantised row."""
+        cfg = self.cfg
+        from soso_b200.formats import row_bytes
+        rb = row_bytes(cfg.dtypes["token_embd"], cfg.hidden)
+        row = self.m["token_embd"][token * rb:(token + 1) * rb]
+        return oracle.dequant(cfg.dtypes["token_embd"], row, cfg.hidden).astype(np.float32)
+
+    def step(self, h: np.ndarray, pos: int) -> np.ndarray:
+        """One token from its embedding row at `pos`; returns the logits (and keeps K/V)."""
+        cfg, m = self.cfg, self.m
+        H, qd, kvd, hd = cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.head_dim
+        group = cfg.heads // cfg.kv_heads
+        h = np.array(h, np.float32, copy=True)
+        for l in range(cfg.n_layers):
+            p = f"blk.{l}."
+            # attention block (layer.rs:1088-1283)
+            xn = oracle.rmsnorm(h, m[p + "attn_norm"], cfg.eps)
+            q = self._mv(p + "attn_q", xn, qd, H)
+            k = self._mv(p + "attn_k", xn, kvd, H)
+            v = self._mv(p + "attn_v", xn, kvd, H)
+            if p + "qkv_bias" in m:  # add_optional_bias (layer.rs:1146-1163)
+                b = m[p + "qkv_bias"]
+                q = (q + b[:qd]).astype(np.float32)
+                k = (k + b[qd:qd + kvd]).astype(np.float32)
+                v = (v + b[qd + kvd:]).astype(np.float32)
+            if p + "attn_q_norm" in m:  # FLAG_QK_NORM (layer.rs:1164-1181)
+                q = np.concatenate([oracle.rmsnorm(q[i * hd:(i + 1) * hd], m[p + "attn_q_norm"], cfg.eps)
+                                    for i in range(cfg.heads)])
+                k = np.concatenate([oracle.rmsnorm(k[i * hd:(i + 1) * hd], m[p + "attn_k_norm"], cfg.eps)
+                                    for i in range(cfg.kv_heads)])
+            q = oracle.rope_heads(q, cfg.heads, hd, pos, cfg.theta, cfg.neox)  # rope_cabezas (layer.rs:1184-1193)
+            k = oracle.rope_heads(k, cfg.kv_heads, hd, pos, cfg.theta, cfg.neox)
+            self.k[l][pos] = oracle.f32_to_f16_array(k)  # LayerKv::append_f16 (kv.rs:258-275)
+            self.v[l][pos] = oracle.f32_to_f16_array(v)
+            att = np.concatenate([
+                oracle.attention_decode_f16(q[i * hd:(i + 1) * hd], self.k[l][:pos + 1], self.v[l][:pos + 1], hd,
+                                            kvd, i // group, pos + 1)
+                for i in range(cfg.heads)])
+            o = self._mv(p + "attn_output", att, H, qd)
+            h = (h + o).astype(np.float32)  # add_f32 (layer.rs:1296)
+            # dense FFN (layer.rs:1300-1389)
+            xn = oracle.rmsnorm(h, m[p + "ffn_norm"], cfg.eps)
+            gate = self._mv(p + "ffn_gate", xn, cfg.ffn, H)
+            up = self._mv(p + "ffn_up", xn, cfg.ffn, H)
+            act = oracle.swiglu(up, gate)
+            down = self._mv(p + "ffn_down", act, H, cfg.ffn)
+            h = (h + down).astype(np.float32)  # add_assign_f32 (layer.rs:1391)
+        # logits (runtime.rs:1976-2019)
+        hn = oracle.rmsnorm(h, m["output_norm"], cfg.eps)
+        return self._mv("output", hn, cfg.vocab, H)
+
+    def greedy(self, prompt, n: int) -> tuple[np.ndarray, list]:
+        """n steps from position 0: prompt tokens first, then argmax (runtime.rs:2021-2028)."""
+        toks, logits_all = [], []
+        tok = int(prompt[0])
+        for i in range(n):
+            lg = self.step(self.embed(tok), i)
+            logits_all.append(lg)
+            a = oracle.argmax(lg)
+            toks.append(a)
+            tok = int(prompt[i + 1]) if i + 1 < len(prompt) else a
+        return np.array(toks, np.int32), logits_all

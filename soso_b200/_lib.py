@@ -34,6 +34,28 @@ class SbStats(ctypes.Structure):
                 ("bytes_down", ctypes.c_uint64)]
 
 
+class SbMat(ctypes.Structure):
+    _fields_ = [("key", ctypes.c_char_p), ("view", SbView), ("rows", c_size), ("cols", c_size)]
+
+
+class SbMoePlan(ctypes.Structure):
+    _fields_ = [("n_exp", c_size), ("top_k", c_size), ("ffn", c_size), ("router", SbMat),
+                ("experts", ctypes.POINTER(SbMat)), ("shared", ctypes.POINTER(SbMat)), ("shared_gate", c_f32p)]
+
+
+class SbLayerPlan(ctypes.Structure):
+    _fields_ = [("heads", c_size), ("kv_heads", c_size), ("head_dim", c_size), ("theta", ctypes.c_float),
+                ("neox", ctypes.c_int), ("q_norm", c_f32p), ("k_norm", c_f32p), ("qkv_bias", c_f32p),
+                ("norm_attn", c_f32p), ("norm_ffn", c_f32p), ("q", SbMat), ("k", SbMat), ("v", SbMat), ("o", SbMat),
+                ("gate", SbMat), ("up", SbMat), ("down", SbMat), ("moe", ctypes.POINTER(SbMoePlan))]
+
+
+class SbDecodePlan(ctypes.Structure):
+    _fields_ = [("layers", ctypes.POINTER(SbLayerPlan)), ("n_layers", c_size), ("hidden", c_size), ("vocab", c_size),
+                ("ctx", c_size), ("eps", ctypes.c_float), ("final_norm", c_f32p), ("lm_head", SbMat),
+                ("embed", SbMat)]
+
+
 # name -> (restype, argtypes); must match include/sosob200.h
 SIGNATURES = {
     "sb_create": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
@@ -49,7 +71,13 @@ SIGNATURES = {
     "sb_resident_count": (c_size, [ctypes.c_void_p]),
     "sb_get_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbStats)]),
     "sb_last_error": (ctypes.c_char_p, []),
+    "sb_decode_prepare": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbDecodePlan)]),
+    "sb_decode_token": (ctypes.c_int, [ctypes.c_void_p, c_f32p, c_size, c_f32p, ctypes.POINTER(ctypes.c_uint16)]),
+    "sb_decode_greedy": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), c_size, c_size, c_size,
+                                        ctypes.POINTER(ctypes.c_int32)]),
     "sbk_row_bytes": (c_size, [ctypes.c_uint8, c_size]),
+    "sbk_swiglu": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, c_size, ctypes.c_int,
+                                  ctypes.c_void_p]),
     "sbk_matvec": (ctypes.c_int, [ctypes.c_uint8, ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p,
                                   ctypes.c_int, ctypes.c_void_p]),
     "sbk_rmsnorm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,

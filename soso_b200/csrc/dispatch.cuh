@@ -52,8 +52,12 @@ bool kernel_dtype(uint8_t d) { return d == SB_DTYPE_Q8_0 || d == SB_DTYPE_Q4_K |
 
 }  // namespace
 
+struct sb_engine;                  // whole-token decode state (engine.cuh)
+void sb_engine_free(sb_engine *e);
+
 struct sb_ctx {
     int device = 0;
+    sb_engine *eng = nullptr;
     cudaStream_t stream = nullptr;
     std::mutex mu;
     std::unordered_map<std::string, Resident> weights;
@@ -171,6 +175,7 @@ extern "C" void sb_destroy(sb_ctx *c)
     if (!c) return;
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
+    if (c->eng) sb_engine_free(c->eng);
     for (auto &kv : c->weights)
         if (kv.second.ptr) cudaFree(kv.second.ptr);
     if (c->scratch) cudaFree(c->scratch);

@@ -26,10 +26,11 @@ __device__ __forceinline__ float block_sum(float v, float *red)
 }
 
 // One CTA per row.  If res != nullptr: h = x + res is written to h_out (the new
-// residual stream) and normalised into y; else y = rmsnorm(x).
+// residual stream) and normalised into y; else y = rmsnorm(x).  h_out may alias
+// res (each element is read, then written, by the same thread).
 __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_rows_kernel(const float *x,
-                                                                    const float *__restrict__ res,
-                                                                    float *__restrict__ h_out,
+                                                                    const float *res,
+                                                                    float *h_out,
                                                                     const float *__restrict__ w,
                                                                     float *y, int n, float eps)
 {

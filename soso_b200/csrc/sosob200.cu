@@ -5,4 +5,5 @@
 #include "norm.cuh"
 #include "decode_ops.cuh"
 #include "dispatch.cuh"
+#include "engine.cuh"
 #include "noalloc.cuh"

@@ -1,0 +1,173 @@
+"""Whole-token decode through the C ABI (GpuDispatch::decode_preparar / decode_token,
+crates/soso-llm-core/src/gpu.rs:654-684): model configurations, seeded synthetic
+models in the reference's block layouts, and a session object that owns the plan.
+
+The model of a config is a dict of numpy arrays keyed like the reference's
+tensors (`blk.{l}.attn_q`, ..., `output`, `token_embd`); weights are bytes in
+the reference layout, norms and biases f32.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import synth
+from ._lib import (SbDecodePlan, SbLayerPlan, SbMat, SbView, SbError, c_f32p, c_u8p, last_error, lib)
+from .formats import DTYPE_Q4_K, DTYPE_Q6_K
+
+
+@dataclass(frozen=True)
+class DenseConfig:
+    """A dense GQA decoder (Qwen2-style: q/k/v bias, NeoX RoPE, SwiGLU)."""
+    n_layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    ctx: int
+    theta: float = 1e6
+    eps: float = 1e-6
+    neox: bool = True
+    qkv_bias: bool = True
+    qk_norm: bool = False
+    # Q4_K_M mix: Q4_K everywhere, Q6_K for ffn_down and the output matrix
+    dtypes: dict = field(default_factory=lambda: {"attn_q": DTYPE_Q4_K, "attn_k": DTYPE_Q4_K, "attn_v": DTYPE_Q4_K,
+                                                  "attn_output": DTYPE_Q4_K, "ffn_gate": DTYPE_Q4_K,
+                                                  "ffn_up": DTYPE_Q4_K, "ffn_down": DTYPE_Q6_K,
+                                                  "output": DTYPE_Q6_K, "token_embd": DTYPE_Q4_K})
+
+    @property
+    def q_dim(self) -> int:
+        return self.heads * self.head_dim
+
+    @property
+    def kv_dim(self) -> int:
+        return self.kv_heads * self.head_dim
+
+
+# Qwen2.5-3B-style dense decoder, fp16 KV at 4096 context
+QWEN25_3B = DenseConfig(n_layers=36, hidden=2048, heads=16, kv_heads=2, head_dim=128, ffn=11008, vocab=151936,
+                        ctx=4096)
+# a small model of the same structure, for parity tests against the CPU oracle
+TINY = DenseConfig(n_layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1024, ctx=160)
+
+
+def shapes(cfg: DenseConfig) -> dict:
+    """tensor name suffix -> (rows, cols)"""
+    H = cfg.hidden
+    return {"attn_q": (cfg.q_dim, H), "attn_k": (cfg.kv_dim, H), "attn_v": (cfg.kv_dim, H),
+            "attn_output": (H, cfg.q_dim), "ffn_gate": (cfg.ffn, H), "ffn_up": (cfg.ffn, H),
+            "ffn_down": (H, cfg.ffn)}
+
+
+def synth_model(cfg: DenseConfig, seed: str = "model") -> dict:
+    """Seeded random-init weights of the config's architecture (synth.model_weights)."""
+    m = {}
+    H = cfg.hidden
+    for l in range(cfg.n_layers):
+        for name, (rows, cols) in shapes(cfg).items():
+            m[f"blk.{l}.{name}"] = synth.model_weights(cfg.dtypes[name], rows, cols, synth.rng(seed, l, name))
+        g = synth.rng(seed, l, "vec")
+        m[f"blk.{l}.attn_norm"] = (1.0 + 0.1 * g.standard_normal(H)).astype(np.float32)
+        m[f"blk.{l}.ffn_norm"] = (1.0 + 0.1 * g.standard_normal(H)).astype(np.float32)
+        if cfg.qkv_bias:
+            m[f"blk.{l}.qkv_bias"] = (0.1 * g.standard_normal(cfg.q_dim + 2 * cfg.kv_dim)).astype(np.float32)
+        if cfg.qk_norm:
+            m[f"blk.{l}.attn_q_norm"] = (1.0 + 0.1 * g.standard_normal(cfg.head_dim)).astype(np.float32)
+            m[f"blk.{l}.attn_k_norm"] = (1.0 + 0.1 * g.standard_normal(cfg.head_dim)).astype(np.float32)
+    g = synth.rng(seed, "out")
+    m["output_norm"] = (1.0 + 0.1 * g.standard_normal(H)).astype(np.float32)
+    m["output"] = synth.model_weights(cfg.dtypes["output"], cfg.vocab, H, synth.rng(seed, "output"))
+    m["token_embd"] = synth.model_weights(cfg.dtypes["token_embd"], cfg.vocab, H, synth.rng(seed, "embd"), std=1.0)
+    return m
+
+
+def _f32(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(c_f32p)
+
+
+class DecodeSession:
+    """A prepared whole-token decode on one device (sb_decode_prepare)."""
+
+    def __init__(self, cfg: DenseConfig, model: dict, device: int = 0, ctx_handle=None):
+        self.cfg = cfg
+        self.model = model
+        L = lib()
+        self._own = ctx_handle is None
+        if ctx_handle is None:
+            h = ctypes.c_void_p()
+            if L.sb_create(device, ctypes.byref(h)) != 0:
+                raise SbError(last_error())
+            ctx_handle = h
+        self.ctx = ctx_handle
+        self._keep = []
+        H = cfg.hidden
+        layers = (SbLayerPlan * cfg.n_layers)()
+        for l in range(cfg.n_layers):
+            lp = layers[l]
+            lp.heads, lp.kv_heads, lp.head_dim = cfg.heads, cfg.kv_heads, cfg.head_dim
+            lp.theta, lp.neox = cfg.theta, int(cfg.neox)
+            lp.q_norm = _f32(model.get(f"blk.{l}.attn_q_norm"))
+            lp.k_norm = _f32(model.get(f"blk.{l}.attn_k_norm"))
+            lp.qkv_bias = _f32(model.get(f"blk.{l}.qkv_bias"))
+            lp.norm_attn = _f32(model[f"blk.{l}.attn_norm"])
+            lp.norm_ffn = _f32(model[f"blk.{l}.ffn_norm"])
+            for fld, name in (("q", "attn_q"), ("k", "attn_k"), ("v", "attn_v"), ("o", "attn_output"),
+                              ("gate", "ffn_gate"), ("up", "ffn_up"), ("down", "ffn_down")):
+                rows, cols = shapes(cfg)[name]
+                setattr(lp, fld, self._mat(f"blk.{l}.{name}", cfg.dtypes[name], rows, cols))
+        plan = SbDecodePlan()
+        plan.layers = layers
+        plan.n_layers = cfg.n_layers
+        plan.hidden, plan.vocab, plan.ctx, plan.eps = H, cfg.vocab, cfg.ctx, cfg.eps
+        plan.final_norm = _f32(model["output_norm"])
+        plan.lm_head = self._mat("output", cfg.dtypes["output"], cfg.vocab, H)
+        plan.embed = self._mat("token_embd", cfg.dtypes["token_embd"], cfg.vocab, H)
+        self._keep += [layers, plan]
+        rc = L.sb_decode_prepare(self.ctx, ctypes.byref(plan))
+        if rc != 1:
+            raise SbError(f"sb_decode_prepare returned {rc}: {last_error()}")
+
+    def _mat(self, key: str, dtype: int, rows: int, cols: int) -> SbMat:
+        w = self.model[key]
+        k = key.encode()
+        self._keep.append(k)
+        return SbMat(k, SbView(w.ctypes.data_as(c_u8p), w.size, dtype, rows * cols), rows, cols)
+
+    def token(self, embed: np.ndarray, pos: int, kv_rows: bool = False):
+        """decode_token: logits of the token whose embedding row is `embed`, at `pos`."""
+        cfg = self.cfg
+        e = np.ascontiguousarray(embed, dtype=np.float32)
+        logits = np.empty(cfg.vocab, np.float32)
+        kv = np.empty(cfg.n_layers * 2 * cfg.kv_dim, np.uint16) if kv_rows else None
+        rc = lib().sb_decode_token(self.ctx, e.ctypes.data_as(c_f32p), pos, logits.ctypes.data_as(c_f32p),
+                                   kv.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)) if kv is not None else None)
+        if rc != 1:
+            raise SbError(f"sb_decode_token returned {rc}: {last_error()}")
+        return (logits, kv) if kv_rows else logits
+
+    def greedy(self, prompt, n: int, pos: int = 0) -> np.ndarray:
+        """n device-side steps from `pos`: prompt tokens fed first, then the argmax chain;
+        returns the argmax of every step."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.empty(n, np.int32)
+        rc = lib().sb_decode_greedy(self.ctx, p.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), p.size, pos, n,
+                                    out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+        if rc != 1:
+            raise SbError(f"sb_decode_greedy returned {rc}: {last_error()}")
+        return out
+
+    def close(self):
+        if self._own and self.ctx:
+            lib().sb_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
