@@ -305,6 +305,8 @@ def run_ours(args) -> None:
         e2e_s = float(t.item())
     L.sb_destroy(ctx)
 
+    dec = None if args.no_decode else decode_bench(local, rank)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_sample_gbs(args.cpu_seconds, host_threads())
@@ -335,7 +337,7 @@ def run_ours(args) -> None:
                          "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)",
                          "traffic": traffic, "algorithmic_bytes_per_launch": int(per_launch_bytes),
-                         "kernel": "sb::q4kmmv::q4k_mmv_kernel"},
+                         "kernel": "sb::tcmv::tc_mmv_kernel<Q4K>"},
             "e2e": {"value": round(world * step_bytes / (e2e_s / args.steps) / 1e9, 1), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "sb_matvec_batch (GpuDispatch::matvec_lote), weights resident"},
@@ -343,6 +345,11 @@ def run_ours(args) -> None:
             "single_matvec_launch": single,
             "clocks": clk,
         }
+        if dec:
+            if world > 1:
+                dec["aggregate_tok_per_s"] = round(dec["tok_per_s"] * world, 1)
+                dec["parallelism"] = f"{world} independent replicas (no tensor parallelism yet)"
+            line["decode"] = dec
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -350,6 +357,42 @@ def run_ours(args) -> None:
         import torch.distributed as dist
         del graph
         dist.destroy_process_group()
+
+
+def decode_bench(device: int, rank: int) -> dict:
+    """Qwen2.5-3B-style dense decoder (Q4_K_M mix), fp16 KV at 4096
+    context, batch-1 greedy decode of 256 tokens after a 128-token random prompt, through the
+    whole-token decode engine (sb_decode_greedy: one CUDA graph per token, tokens chained
+    on the device).  Timed: the 256 generated tokens (wall clock around the call, which
+    ends with a stream synchronize)."""
+    from soso_b200 import decode, synth
+    cfg = decode.QWEN25_3B
+    model = decode.synth_model(cfg, f"c3.{rank}")
+    sess = decode.DecodeSession(cfg, model, device=device)
+    prompt = synth.rng("prompt", "c3", rank).integers(0, cfg.vocab, 128).astype(np.int32)
+    sess.greedy(prompt[:8], 8)  # warm
+    first = sess.greedy(prompt, 128)  # the prompt, one token per step
+    n_gen = 256
+    t0 = time.perf_counter()
+    toks = sess.greedy(first[-1:], n_gen, pos=128)
+    dt = time.perf_counter() - t0
+    weights = sum(v.nbytes for k, v in model.items() if k != "token_embd" and v.dtype == np.uint8)
+    kv_per_pos = cfg.n_layers * 2 * cfg.kv_dim * 2
+    avg_ctx = 128 + (n_gen + 1) / 2.0
+    bytes_tok = weights + kv_per_pos * avg_ctx + cfg.hidden * 4
+    peaks = load_peaks()
+    tps = n_gen / dt
+    sess.close()
+    return {"config": "configs[2]: Qwen2.5-3B-style dense, 36 layers, hidden 2048, 16 q / 2 kv heads x 128, "
+                      "SwiGLU 11008, vocab 151936, Q4_K + Q6_K (ffn_down, output), fp16 KV ctx 4096",
+            "data": "synthetic random-init weights (seeded), random prompt",
+            "prompt_tokens": 128, "generated_tokens": n_gen, "tok_per_s": round(tps, 1),
+            "ms_per_token": round(1e3 * dt / n_gen, 3), "bytes_per_token": int(bytes_tok),
+            "roofline": {"bound": "hbm", "achieved_GBps": round(bytes_tok * tps / 1e9, 1),
+                         "peak_GBps": peaks["hbm_gbs"], "frac": round(bytes_tok * tps / 1e9 / peaks["hbm_gbs"], 4),
+                         "roofline_tok_per_s": round(peaks["hbm_gbs"] * 1e9 / bytes_tok, 1)},
+            "timing": "wall clock around sb_decode_greedy(256 steps); graph launches chained on one stream",
+            "last_tokens": toks[-4:].tolist()}
 
 
 # ---------------------------------------------------------- reference arm
@@ -482,6 +525,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
     args = ap.parse_args()
     if args.ncu_case == "q4k_batch":
         run_batch_case(args.launches)

@@ -41,6 +41,13 @@ extern "C" {
 #define SB_DTYPE_Q8_0 2
 #define SB_DTYPE_Q4_K 3
 #define SB_DTYPE_Q6_K 13
+/* Q6_K repacked for the device (no counterpart in the reference): the same
+ * 210-byte blocks, regrouped per row into groups of 8 blocks laid out as
+ * planes [ql 8x128][qh 8x64][scales 8x16][d 8x2] (a last partial group of m
+ * blocks the same way with m, padded to 16 bytes), so rows and fields are
+ * 16-byte aligned for TMA.  Made by sbk_q6k_pack; the host-buffer calls (sb_*)
+ * repack Q6_K weights this way when they upload them. */
+#define SB_DTYPE_Q6_K_P 14
 
 /* Mirror of `TensorView { bytes, dtype, elems }` (crates/soso-llm-core/src/layer.rs:26-31). */
 typedef struct {
@@ -164,7 +171,7 @@ int sb_decode_greedy(sb_ctx *ctx, const int32_t *prompt, size_t n_prompt, size_t
  * (`sosomodel::dequant::row_bytes`, crates/sosomodel/src/dequant.rs:53-63). */
 size_t sbk_row_bytes(uint8_t dtype, size_t cols);
 
-/* y[rows] = W[rows x cols] . x[cols] for dtype Q8_0 / Q4_K / Q6_K.  Replaces
+/* y[rows] = W[rows x cols] . x[cols] for dtype Q8_0 / Q4_K / Q6_K / Q6_K_P.  Replaces
  * `gm_matvec_q4k` / `gm_matvec_q80` (lxdde/ports/nouveau/gemma_capa.cu:433,:501)
  * and the CPU `gemm::matvec_q4_k` / `matvec_q8_0` (crates/soso-llm-core/src/gemm.rs:295,:402).
  * w must be 16-byte aligned.  pdl != 0 launches with programmatic dependent
@@ -179,6 +186,12 @@ typedef struct {
     const float *x;
     float *y;
 } sbk_mv_op;
+
+/* Repack rows x cols Q6_K weights (reference layout, device memory) into
+ * SB_DTYPE_Q6_K_P at dst (sbk_row_bytes(SB_DTYPE_Q6_K_P, cols) * rows bytes,
+ * 16-byte aligned).  No counterpart in the reference, which converts Q6_K to
+ * Q8_0 on import instead (crates/gguf2som/src/lib.rs:1592-1610). */
+int sbk_q6k_pack(const void *src, size_t rows, size_t cols, void *dst, void *stream);
 
 /* Independent matvecs of one dtype in as few launches as possible (Q4_K: one
  * launch per 40 matrices, their weight streams split across all SMs as one) --

@@ -24,6 +24,7 @@ extern "C" int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols
 extern "C" int sbk_rmsnorm(const float *x, const float *res, float *h_out, const float *w, float *y, size_t rows,
                            size_t n, float eps, void *stream);
 extern "C" int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, int pdl, void *stream);
+extern "C" int sbk_q6k_pack(const void *src, size_t rows, size_t cols, void *dst, void *stream);
 
 namespace {
 
@@ -44,7 +45,8 @@ int fail(const std::string &msg)
 struct Resident {
     void *ptr = nullptr;
     size_t bytes = 0;
-    uint8_t dtype = 0;
+    uint8_t dtype = 0;      // as given (the reference's dtype)
+    uint8_t dev_dtype = 0;  // as held on the device (Q6_K is repacked to Q6_K_P for matvecs)
     bool ok = false;
 };
 
@@ -93,8 +95,11 @@ struct sb_ctx {
         return 0;
     }
 
-    // 1 = resident, 0 = declined (remembered failure or shape), <0 = error
-    int resident(const char *key, const sb_view *v, size_t rows, size_t cols, Resident **out)
+    // 1 = resident, 0 = declined (remembered failure or shape), <0 = error.  Q6_K
+    // matrices are repacked (SB_DTYPE_Q6_K_P) unless for_matvec is false (tables read
+    // row by row, like the embedding, stay in the reference layout).
+    int resident(const char *key, const sb_view *v, size_t rows, size_t cols, Resident **out,
+                 bool for_matvec = true)
     {
         auto it = weights.find(key);
         if (it != weights.end()) {
@@ -107,9 +112,25 @@ struct sb_ctx {
         Resident r;
         r.bytes = v->len;
         r.dtype = v->dtype;
-        // +64 B so vectorised/bulk reads that round a range up to 16 B stay inside the allocation
-        cudaError_t e = cudaMalloc(&r.ptr, v->len + 64);
-        if (e == cudaSuccess) e = cudaMemcpy(r.ptr, v->bytes, v->len, cudaMemcpyHostToDevice);
+        r.dev_dtype = v->dtype;
+        const bool pack = for_matvec && v->dtype == SB_DTYPE_Q6_K && rows * cols == v->elems &&
+                          sbk_row_bytes(SB_DTYPE_Q6_K_P, cols) != 0 && cols <= 12288;
+        cudaError_t e;
+        if (pack) {
+            // upload, then repack into the resident buffer (+64 B: bulk reads round up to 16 B)
+            void *tmp = nullptr;
+            e = cudaMalloc(&tmp, v->len);
+            if (e == cudaSuccess) e = cudaMalloc(&r.ptr, sbk_row_bytes(SB_DTYPE_Q6_K_P, cols) * rows + 64);
+            if (e == cudaSuccess) e = cudaMemcpy(tmp, v->bytes, v->len, cudaMemcpyHostToDevice);
+            if (e == cudaSuccess && sbk_q6k_pack(tmp, rows, cols, r.ptr, nullptr) != 0) e = cudaErrorLaunchFailure;
+            if (e == cudaSuccess) e = cudaDeviceSynchronize();
+            if (tmp) cudaFree(tmp);
+            r.dev_dtype = SB_DTYPE_Q6_K_P;
+        } else {
+            // +64 B so vectorised/bulk reads that round a range up to 16 B stay inside the allocation
+            e = cudaMalloc(&r.ptr, v->len + 64);
+            if (e == cudaSuccess) e = cudaMemcpy(r.ptr, v->bytes, v->len, cudaMemcpyHostToDevice);
+        }
         if (e != cudaSuccess) {
             if (r.ptr) cudaFree(r.ptr);
             r.ptr = nullptr;
@@ -227,7 +248,7 @@ static int run_matvecs(sb_ctx *c, const char *key, const sb_view *w, size_t rows
     if ((e = cudaMemcpyAsync(dx, hs, xb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(x)", e);
     for (size_t t = 0; t < n; t++) {
-        int k = sbk_matvec(w->dtype, r->ptr, rows, cols, dx + t * cols, dy + t * rows, 0, c->stream);
+        int k = sbk_matvec(r->dev_dtype, r->ptr, rows, cols, dx + t * cols, dy + t * rows, 0, c->stream);
         if (k) return fail("sbk_matvec launch failed (" + std::to_string(k) + ")");
         c->stats.launches++;
     }
@@ -288,21 +309,22 @@ extern "C" int sb_matvec_batch(sb_ctx *c, sb_matvec_op *ops, size_t nops, uint8_
     if ((e = cudaMemcpyAsync(base, hs, xend, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(x)", e);
     // the kernels grouped by dtype (one launch per batch of Q4_K matrices), one wait
-    std::vector<sbk_mv_op> by_dtype[3];
+    std::vector<std::pair<uint8_t, std::vector<sbk_mv_op>>> by_dtype;
     for (size_t i = 0; i < nops; i++) {
         if (!res[i]) continue;
         sb_matvec_op &op = ops[i];
         yo[i] += xend;
-        const int k = op.view->dtype == SB_DTYPE_Q4_K ? 0 : op.view->dtype == SB_DTYPE_Q6_K ? 1 : 2;
-        by_dtype[k].push_back(sbk_mv_op{res[i]->ptr, op.rows, op.cols, (const float *)(base + xo[i]),
-                                        (float *)(base + yo[i])});
+        const uint8_t dt = res[i]->dev_dtype;
+        size_t k = 0;
+        while (k < by_dtype.size() && by_dtype[k].first != dt) k++;
+        if (k == by_dtype.size()) by_dtype.push_back({dt, {}});
+        by_dtype[k].second.push_back(sbk_mv_op{res[i]->ptr, op.rows, op.cols, (const float *)(base + xo[i]),
+                                               (float *)(base + yo[i])});
         c->stats.bytes_up += op.cols * 4;
         c->stats.bytes_down += op.rows * 4;
     }
-    const uint8_t dts[3] = {SB_DTYPE_Q4_K, SB_DTYPE_Q6_K, SB_DTYPE_Q8_0};
-    for (int k = 0; k < 3; k++) {
-        if (by_dtype[k].empty()) continue;
-        if (sbk_matvec_batch(dts[k], by_dtype[k].data(), by_dtype[k].size(), 0, c->stream))
+    for (auto &grp : by_dtype) {
+        if (sbk_matvec_batch(grp.first, grp.second.data(), grp.second.size(), 0, c->stream))
             return fail("sbk_matvec_batch launch failed");
         c->stats.launches++;
     }

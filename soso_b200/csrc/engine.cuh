@@ -169,10 +169,10 @@ int eng_mat(sb_ctx *c, const sb_mat &m, size_t rows, size_t cols, EngMat *out, b
     if (m.rows != rows || m.cols != cols) return fail(std::string("decode plan: ") + m.key + " has an unexpected shape");
     if (matvec && !admit(&m.view, rows, cols)) return 0;
     Resident *r = nullptr;
-    const int rc = c->resident(m.key, &m.view, rows, cols, &r);
+    const int rc = c->resident(m.key, &m.view, rows, cols, &r, matvec);
     if (rc <= 0) return rc;
     out->w = r->ptr;
-    out->dt = m.view.dtype;
+    out->dt = r->dev_dtype;
     out->rows = rows;
     out->cols = cols;
     return 1;

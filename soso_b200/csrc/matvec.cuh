@@ -28,7 +28,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
-#include "q4k_mmv.cuh"
+#include "tc_mmv.cuh"
 #include "sosob200.h"
 
 namespace sb {
@@ -386,6 +386,7 @@ extern "C" size_t sbk_row_bytes(uint8_t dtype, size_t cols)
     case SB_DTYPE_Q8_0: e = 32; b = 36; break;
     case SB_DTYPE_Q4_K: e = 256; b = 144; break;
     case SB_DTYPE_Q6_K: e = 256; b = 210; break;
+    case SB_DTYPE_Q6_K_P: return (cols == 0 || cols % 256) ? 0 : sb::tcmv::q6k_packed_row_bytes(cols);
     case SB_DTYPE_F32: return cols * 4;
     default: return 0;
     }
@@ -439,6 +440,45 @@ static int num_sms_cached()
 }
 }  // namespace sb
 
+namespace sb {
+// Up to MAXB matrices of format F per launch of the tensor-core kernel; with
+// `fallback`, a chunk the kernel does not take runs matrix by matrix through
+// sbk_matvec, else it is rejected (-5).
+template <class F>
+static int tc_matvec_batch(const sbk_mv_op *ops, size_t n, int pdl, cudaStream_t s, bool fallback)
+{
+    const int grid = num_sms_cached();
+    for (size_t i0 = 0; i0 < n; i0 += tcmv::MAXB) {
+        const size_t nb = n - i0 < (size_t)tcmv::MAXB ? n - i0 : (size_t)tcmv::MAXB;
+        tcmv::MatOp mo[tcmv::MAXB];
+        bool ok = true;
+        for (size_t i = 0; i < nb; i++) {
+            const sbk_mv_op &o = ops[i0 + i];
+            if (!o.w || !o.x || !o.y || !o.rows || ((uintptr_t)o.w & 15) || ((uintptr_t)o.x & 15) ||
+                sbk_row_bytes(F::DTYPE, o.cols) == 0)
+                return -1;
+            mo[i] = tcmv::MatOp{o.w, (int)o.rows, (int)o.cols, o.x, o.y};
+            ok = ok && o.rows < (1u << 24);
+        }
+        if (ok && tcmv::fits<F>(mo, (int)nb, grid)) {
+            void *ws = stream_ws(s, tcmv::ws_bytes(grid));
+            if (!ws) return -3;
+            const int rc = tcmv::launch_batch<F>(mo, (int)nb, ws, grid, pdl, s);
+            if (rc) return rc;
+        } else if (fallback) {
+            for (size_t i = 0; i < nb; i++) {
+                const sbk_mv_op &o = ops[i0 + i];
+                const int rc = launch_matvec<Q4K>(o.w, o.rows, o.cols, o.x, o.y, pdl, s);
+                if (rc) return rc;
+            }
+        } else {
+            return -5;
+        }
+    }
+    return 0;
+}
+}  // namespace sb
+
 extern "C" int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols, const float *x, float *y,
                           int pdl, void *stream)
 {
@@ -447,17 +487,10 @@ extern "C" int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols
     if ((unsigned long long)rows * (cols / 32) >= (1ull << 31)) return -1;  // block indices are 32-bit
     if (((uintptr_t)w & 15) || ((uintptr_t)x & 15)) return -2;
     cudaStream_t s = (cudaStream_t)stream;
+    const sbk_mv_op op{w, rows, cols, x, y};
     switch (dtype) {
-    case SB_DTYPE_Q4_K: {
-        const int grid = sb::num_sms_cached();
-        const sb::q4kmmv::MatOp op{w, (int)rows, (int)cols, x, y};
-        if (sb::q4kmmv::fits(&op, 1, grid)) {
-            void *ws = sb::stream_ws(s, sb::q4kmmv::ws_bytes(grid));
-            if (!ws) return -3;
-            return sb::q4kmmv::launch_batch(&op, 1, ws, grid, pdl, s);
-        }
-        return sb::launch_matvec<sb::Q4K>(w, rows, cols, x, y, pdl, s);
-    }
+    case SB_DTYPE_Q4_K: return sb::tc_matvec_batch<sb::tcmv::Q4K>(&op, 1, pdl, s, true);
+    case SB_DTYPE_Q6_K_P: return sb::tc_matvec_batch<sb::tcmv::Q6KP>(&op, 1, pdl, s, false);
     case SB_DTYPE_Q8_0: return sb::launch_matvec<sb::Q80>(w, rows, cols, x, y, pdl, s);
     case SB_DTYPE_Q6_K: return sb::launch_matvec<sb::Q6K>(w, rows, cols, x, y, pdl, s);
     }
@@ -468,40 +501,19 @@ extern "C" int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, i
 {
     if (!ops || n == 0) return -1;
     cudaStream_t s = (cudaStream_t)stream;
-    if (dtype == SB_DTYPE_Q4_K) {
-        const int grid = sb::num_sms_cached();
-        for (size_t i0 = 0; i0 < n; i0 += sb::q4kmmv::MAXB) {
-            const size_t nb = n - i0 < (size_t)sb::q4kmmv::MAXB ? n - i0 : (size_t)sb::q4kmmv::MAXB;
-            sb::q4kmmv::MatOp mo[sb::q4kmmv::MAXB];
-            bool ok = true;
-            for (size_t i = 0; i < nb; i++) {
-                const sbk_mv_op &o = ops[i0 + i];
-                if (!o.w || !o.x || !o.y || !o.rows || ((uintptr_t)o.w & 15) || ((uintptr_t)o.x & 15) ||
-                    sbk_row_bytes(dtype, o.cols) == 0)
-                    return -1;
-                mo[i] = sb::q4kmmv::MatOp{o.w, (int)o.rows, (int)o.cols, o.x, o.y};
-                ok = ok && o.rows < (1u << 24);
-            }
-            if (ok && sb::q4kmmv::fits(mo, (int)nb, grid)) {
-                void *ws = sb::stream_ws(s, sb::q4kmmv::ws_bytes(grid));
-                if (!ws) return -3;
-                const int rc = sb::q4kmmv::launch_batch(mo, (int)nb, ws, grid, pdl, s);
-                if (rc) return rc;
-            } else {
-                for (size_t i = 0; i < nb; i++) {
-                    const sbk_mv_op &o = ops[i0 + i];
-                    const int rc = sbk_matvec(dtype, o.w, o.rows, o.cols, o.x, o.y, pdl, stream);
-                    if (rc) return rc;
-                }
-            }
-        }
-        return 0;
-    }
+    if (dtype == SB_DTYPE_Q4_K) return sb::tc_matvec_batch<sb::tcmv::Q4K>(ops, n, pdl, s, true);
+    if (dtype == SB_DTYPE_Q6_K_P) return sb::tc_matvec_batch<sb::tcmv::Q6KP>(ops, n, pdl, s, false);
     for (size_t i = 0; i < n; i++) {
         const int rc = sbk_matvec(dtype, ops[i].w, ops[i].rows, ops[i].cols, ops[i].x, ops[i].y, pdl, stream);
         if (rc) return rc;
     }
     return 0;
+}
+
+extern "C" int sbk_q6k_pack(const void *src, size_t rows, size_t cols, void *dst, void *stream)
+{
+    if (((uintptr_t)dst & 15)) return -2;
+    return sb::tcmv::q6k_pack(src, rows, cols, dst, (cudaStream_t)stream);
 }
 
 extern "C" int sbk_num_sms(int device)

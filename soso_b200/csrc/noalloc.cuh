@@ -21,7 +21,7 @@
 // cudaGetSymbolAddress while that device is current, and later calls reuse it.
 // Make that first call before any stream capture.
 #pragma once
-#include "q4k_mmv.cuh"
+#include "tc_mmv.cuh"
 
 namespace sb {
 namespace noalloc {
@@ -60,20 +60,20 @@ extern "C" int sbk_matvec_q4k_noalloc(const void *w, size_t rows, size_t cols, c
     using namespace sb;
     if (!w || !x || !y || rows == 0) return -1;
     if (((uintptr_t)w & 15) || ((uintptr_t)x & 15)) return -2;
-    if (cols == 0 || cols % 256 || cols > (size_t)q4kmmv::MAX_COLS) return -1;
+    if (cols == 0 || cols % 256 || cols > (size_t)tcmv::Q4K::MAX_COLS) return -1;
     // the fixed scratch bounds the shape: one counter per 16 rows
     if ((rows + 15) / 16 > (size_t)noalloc::MAX_GROUPS) return -8;
     const int grid = num_sms_cached();
     if (grid > noalloc::MAX_CTAS) return -8;
-    const q4kmmv::MatOp op{w, (int)rows, (int)cols, x, y};
-    if (!q4kmmv::fits(&op, 1, grid)) return -5;
+    const tcmv::MatOp op{w, (int)rows, (int)cols, x, y};
+    if (!tcmv::fits<tcmv::Q4K>(&op, 1, grid)) return -5;
     void *scratch = nullptr;
     if (noalloc::scratch_ptr(&scratch)) return -3;
     cudaStream_t s = (cudaStream_t)stream;
     // counters must start at zero (a call that failed midway may have left some set)
     if (cudaMemsetAsync(scratch, 0, (rows + 15) / 16 * 4, s) != cudaSuccess) return -4;
-    q4kmmv::Ws wsd;
+    tcmv::Ws wsd;
     wsd.cnt = reinterpret_cast<unsigned *>(scratch);
     wsd.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(scratch) + noalloc::CNT_BYTES);
-    return q4kmmv::launch_batch_with(&op, 1, wsd, grid, 0, s);
+    return tcmv::launch_batch_ws<tcmv::Q4K>(&op, 1, wsd, noalloc::MAX_GROUPS, grid, 0, s);
 }

@@ -1,0 +1,133 @@
+// tc_common.cuh -- building blocks of the tensor-core matvec kernels (tc_mmv.cuh):
+// mbarrier ring primitives, the 2-D TMA tensor load (never with multicast) and
+// the warp-level MMA forms the quantized formats use.
+#pragma once
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace sb {
+namespace tcmv {
+
+constexpr unsigned SPIN_LIMIT = 1u << 26;
+
+// workspace (global): per CTA two boundary partials (16 floats each), then one counter per group
+struct Ws {
+    float *part;    // [grid][2][16]
+    unsigned *cnt;  // [groups]
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, unsigned count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx_arrive(uint64_t *b, unsigned bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *b)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+
+// Bounded wait for the phase with the given parity; false if the limit ran out.
+// (The suspend-time hint lets a waiting warp yield its issue slots.)
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity)
+{
+    const uint32_t a = smem_u32(b);
+    for (unsigned i = 0; i < SPIN_LIMIT; i++) {
+        uint32_t ok;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok)
+            : "r"(a), "r"(parity), "r"(1000u)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
+// 2-D tiled TMA load (no multicast): box at element coords (x = u64 column, y = row).
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// u8 x s8 -> s32 tensor-core MMA, m16n8k32 (integer: exact).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// s8 x s8 -> s32 tensor-core MMA, m16n8k32 (integer: exact).
+__device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Four int8 pieces of v (|v| < 128): v = p0 + p1/2^7 + p2/2^14 + p3/2^21 to 28
+// bits; every residual is exact in f32.  Byte i of pk[p] gets piece p.
+__device__ __forceinline__ void int8_pieces(float v, int i, uint32_t (&pk)[4])
+{
+#pragma unroll
+    for (int pc = 0; pc < 4; pc++) {
+        float r = rintf(v);
+        r = fminf(fmaxf(r, -127.0f), 127.0f);
+        pk[pc] |= ((uint32_t)__float2int_rn(r) & 0xFFu) << (8 * i);
+        v = (v - r) * 128.0f;
+    }
+}
+
+// 2^e with 2^e > max |v| over the warp (from the max's biased exponent), clamped for
+// zero and non-finite input.
+__device__ __forceinline__ int warp_exp_above(float mx)
+{
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const uint32_t mxb = __float_as_uint(mx);
+    const int ex = (int)(mxb >> 23) - 126;
+    return (mxb == 0u || mxb >= 0x7f800000u) ? 0 : ex < -100 ? -100 : ex > 100 ? 100 : ex;
+}
+
+// PTX prmt in its generic mode: a selector nibble with bit 3 set replicates the
+// sign bit of the selected byte (used to sign-extend one int8 into 32 bits).
+__device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t sel)
+{
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
+
+}  // namespace tcmv
+}  // namespace sb

@@ -1,0 +1,490 @@
+// tc_mmv.cuh -- decode matvec y = W.x for the quantized formats on sm_100a
+// tensor cores: a TMA weight stream through an mbarrier ring, dequantisation in
+// registers straight into MMA fragments, and a deterministic stream-K split.
+// The per-format arithmetic lives in tc_q4k.cuh (Q4_K) and tc_q6k.cuh (Q6_K,
+// repacked); this file is the machinery they share.
+//
+// Work split ("stream-K", deterministic).  Rows are taken 16 at a time (a
+// "group", the MMA's M); a stage is (group, F::SBLK consecutive blocks).  The
+// stages of all matrices of a batch, group-major, are split into one contiguous
+// range per CTA (row_strip), so every SM gets the same number of bytes whatever
+// the shapes.  A group cut by a CTA boundary is finished by whichever CTA
+// arrives last at its counter, summing the pieces in CTA order; no spinning.
+//
+// Per CTA: warp 0 is the producer -- one 2-D TMA tensor copy per stage (a
+// 16-row box of F::BOXW u64 of the weight matrix; rows past the end and columns
+// past a row's end are zero-filled by the TMA unit; no multicast) into a ring
+// of F::NSLOT slots, issued before griddepcontrol.wait so the stream overlaps
+// the previous kernel under programmatic dependent launch.  F::NCW consumer
+// warps form F::NSTREAM teams of F::NCONS; team j takes stages j, j+NSTREAM, ...
+// and within a team warp w takes block w of the stage.  A warp copies its
+// block's bytes to registers and releases the slot before any math.  Every
+// mbarrier wait is bounded and reports through the device error word.
+//
+// One launch serves a batch of independent matvecs (the reference's
+// matvec_lote, crates/soso-llm-core/src/gpu.rs:694-701: several matvecs, one
+// wait); their stages are numbered one after another, so the batch streams as one.
+#pragma once
+#include "tc_q4k.cuh"
+#include "tc_q6k.cuh"
+
+namespace sb {
+namespace tcmv {
+
+constexpr int MAXB = 40;           // matrices per launch
+constexpr int CNT_MAX = 1 << 16;   // groups of 16 rows per launch (counters in the workspace)
+
+struct __align__(64) MatDesc {
+    CUtensorMap map;        // weights as [rows][row_bytes/8] u64, box 16 x F::BOXW
+    const float *x;
+    float *y;
+    int rows, cols, spg;    // spg: stages per 16-row group
+    int st_begin, cnt_off;  // first global stage; first counter of its groups
+};
+
+struct Batch {
+    MatDesc d[MAXB];
+    int n, total;              // matrices, stages
+    int max_cols, max_groups;  // shared-memory capacities (prep, partial table)
+};
+
+template <class F>
+struct Smem {
+    uint8_t *ring;    // NSLOT * SLOTB
+    uint8_t *prep;    // F::prep_bytes(max_cols)
+    uint8_t *zero;    // 64 B of zeros: the B fragment of lanes that carry no x
+    float *part;      // [groups of this CTA][NCW][16]
+    uint64_t *full;   // [NSLOT]
+    uint64_t *empty;  // [NSLOT]
+};
+
+template <class F>
+__host__ __device__ inline size_t smem_bytes(int max_cols, int max_groups)
+{
+    return (size_t)F::NSLOT * F::SLOTB + F::prep_bytes(max_cols) + 64 + (size_t)max_groups * F::NCW * 64 +
+           2 * F::NSLOT * 8 + 64;
+}
+
+template <class F>
+__device__ __forceinline__ Smem<F> carve(uint8_t *base, int max_cols, int max_groups)
+{
+    Smem<F> s;
+    size_t o = 0;
+    s.ring = base;
+    o += (size_t)F::NSLOT * F::SLOTB;
+    s.prep = base + o;
+    o += F::prep_bytes(max_cols);
+    s.zero = base + o;
+    o += 64;
+    s.part = reinterpret_cast<float *>(base + o);
+    o += (size_t)max_groups * F::NCW * 64;
+    o = (o + 7) & ~(size_t)7;
+    s.full = reinterpret_cast<uint64_t *>(base + o);
+    s.empty = s.full + F::NSLOT;
+    return s;
+}
+
+// inverse of row_strip: which of n parts holds `unit`
+__device__ __forceinline__ int owner_of(int unit, int total, int n)
+{
+    const int base = total / n, rem = total - base * n;
+    const int big = rem * (base + 1);
+    return unit < big ? unit / (base + 1) : rem + (base ? (unit - big) / base : 0);
+}
+
+template <class F>
+__global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_constant__ Batch B, Ws ws)
+{
+    constexpr int NCW = F::NCW, NSLOT = F::NSLOT, NSTREAM = F::NSTREAM;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    const Smem<F> s = carve<F>(smem_raw, B.max_cols, B.max_groups);
+    int st0, st1;
+    row_strip(B.total, blockIdx.x, gridDim.x, st0, st1);
+    const int nst = st1 - st0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // matrices touched: m_first .. m_last
+    int m_first = 0;
+    while (m_first + 1 < B.n && B.d[m_first + 1].st_begin <= st0) m_first++;
+    int m_last = m_first;
+    while (nst > 0 && m_last + 1 < B.n && B.d[m_last + 1].st_begin < st1) m_last++;
+
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < NSLOT; k++) {
+            mbar_init(&s.full[k], 1);
+            mbar_init(&s.empty[k], F::NCONS);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x < 16) reinterpret_cast<float *>(s.zero)[threadIdx.x] = 0.0f;
+    __syncthreads();
+    // Dependents may launch now: they only read what this grid writes after their
+    // own griddepcontrol.wait, which waits for this grid to complete.
+    griddep_launch();
+
+    bool failed = false;
+    if (warp == 0) {
+        // ---------------- producer: weights do not depend on the previous kernel, so the
+        // whole stream runs without griddepcontrol.wait
+        if (lane == 0 && nst > 0) {
+            int mi = m_first, slot = 0;
+            unsigned phase = 0;  // parity of the empty-barrier phase to wait for
+            const MatDesc *d = &B.d[mi];
+            int ls = st0 - d->st_begin, G = ls / d->spg, j = ls - G * d->spg;
+            int mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&d->map) : "memory");
+            for (int k = 0; k < nst; k++) {
+                if (st0 + k == mend) {  // next matrix of the batch
+                    d = &B.d[++mi];
+                    G = 0, j = 0;
+                    mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
+                    asm volatile("prefetch.tensormap [%0];" ::"l"(&d->map) : "memory");
+                }
+                if (k >= NSLOT && !mbar_wait(&s.empty[slot], phase)) {
+                    failed = true;
+                    break;
+                }
+                mbar_expect_tx_arrive(&s.full[slot], (unsigned)F::SLOTB);  // full box, zero-filled past the ends
+                tma_load_2d(s.ring + slot * F::SLOTB, &d->map, F::stage_x(j), G * 16, &s.full[slot]);
+                if (++j == d->spg) j = 0, G++;
+                if (++slot == NSLOT) {
+                    slot = 0;
+                    if (k >= NSLOT) phase ^= 1u;  // stages 2*NSLOT.. wait for the second use of a slot, ...
+                }
+            }
+            if (failed) set_dev_error(0x51u);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- consumers
+        const int cwg = warp - 1;  // 0 .. NCW-1
+        const int team = cwg / F::NCONS, cw = cwg % F::NCONS, g = lane >> 2, t = lane & 3;
+        const typename F::Lane L = F::lane_setup(g, t);
+        griddep_wait();  // x of every matrix is written by the previous kernel
+        for (int mi = m_first; mi <= m_last && nst > 0; mi++) {
+            const MatDesc &d = B.d[mi];
+            const int nb = d.cols / 256, spg = d.spg;
+            const int mtot = spg * ((d.rows + 15) >> 4);
+            const int ka = max(st0, d.st_begin) - st0, kb = min(st1, d.st_begin + mtot) - st0;  // CTA-local stages
+            const int gs0 = (ka + st0 - d.st_begin) / spg, gs1 = (kb - 1 + st0 - d.st_begin) / spg;
+            const int ng = gs1 - gs0 + 1;
+            // x -> prep and a clean partial table for this segment
+            F::prep_x(d.x, d.cols, s.prep, cwg);
+            for (int i = cwg * 32 + lane; i < ng * NCW * 16; i += NCW * 32) s.part[i] = 0.0f;
+            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+            const typename F::Seg S = F::seg_setup(L, s.prep, s.zero, nb);
+            float acc0 = 0.0f, acc1 = 0.0f;
+            int cur = -1;
+            const int k0 = ka + team;
+            int slot = k0 % NSLOT, G = (k0 + st0 - d.st_begin) / spg, j = (k0 + st0 - d.st_begin) - G * spg;
+            unsigned parity = (k0 / NSLOT) & 1;
+            auto flush = [&]() {
+                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+                if (t == 0) {
+                    float *p = s.part + ((cur - gs0) * NCW + cwg) * 16;
+                    p[g] = acc0;
+                    p[g + 8] = acc1;
+                }
+            };
+            for (int k = k0; k < kb && !failed; k += NSTREAM) {
+                if (k != k0) {  // advance by NSTREAM stages
+                    slot += NSTREAM;
+                    if (slot >= NSLOT) slot -= NSLOT, parity ^= 1u;
+                    j += NSTREAM;
+                    while (j >= spg) j -= spg, G++;
+                }
+                if (!mbar_wait(&s.full[slot], parity)) {
+                    failed = true;
+                    set_dev_error(0x52u);
+                    break;
+                }
+                if (G != cur) {
+                    if (cur >= 0) flush();
+                    cur = G;
+                    acc0 = acc1 = 0.0f;
+                }
+                const int blk = j * F::SBLK + cw;
+                if (blk < nb) {
+                    F::block(L, S, s.ring + slot * F::SLOTB, cw, blk, nb, &s.empty[slot], acc0, acc1);
+                } else {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.empty[slot]);
+                }
+            }
+            if (cur >= 0) flush();
+            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+            // segment epilogue: sum the consumer warps' pieces per group (fixed order)
+            const bool head_cut = mi == m_first && (st0 - d.st_begin) % spg != 0;
+            const bool tail_cut = mi == m_last && (st1 - d.st_begin) % spg != 0 && st1 < d.st_begin + mtot;
+            for (int i = cwg * 32 + lane; i < ng * 16; i += NCW * 32) {
+                const int gl = i >> 4, r = i & 15, row = (gs0 + gl) * 16 + r;
+                float v = 0.0f;
+                for (int w = 0; w < NCW; w++) v += s.part[(gl * NCW + w) * 16 + r];
+                const bool cut = (gl == 0 && head_cut) || (gl == ng - 1 && tail_cut);
+                if (!cut) {
+                    if (row < d.rows) d.y[row] = v;
+                } else {
+                    // side 0: the group holding this CTA's first stage, side 1: any other (its last)
+                    const int ga = d.st_begin + (gs0 + gl) * spg;
+                    ws.part[(blockIdx.x * 2 + ((st0 >= ga && st0 < ga + spg) ? 0 : 1)) * 16 + r] = v;
+                    __threadfence();
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+        }
+    }
+    if (failed) {
+        // let every TMA copy issued into this CTA's shared memory land before exiting (bounded)
+        if (warp == 0 && lane == 0)
+            for (int k = nst > NSLOT ? nst - NSLOT : 0; k < nst; k++) mbar_wait(&s.full[k % NSLOT], (k / NSLOT) & 1);
+    }
+    __syncthreads();
+    if (nst <= 0) return;
+
+    // ---------------- groups cut by CTA boundaries: the last CTA to arrive at a group's
+    // counter sums the pieces in CTA order.  Both sides in one round trip.
+    __shared__ int last_flag[2];
+    __shared__ int side_g[2], side_ca[2], side_cb[2], side_m[2];
+    if (threadIdx.x < 2) {
+        const int side = threadIdx.x;
+        const int mi = side == 0 ? m_first : m_last;
+        const MatDesc &d = B.d[mi];
+        const int mtot = d.spg * ((d.rows + 15) >> 4);
+        const int ls0 = st0 - d.st_begin, ls1 = st1 - d.st_begin;  // stage range relative to the matrix
+        const bool head_cut = ls0 % d.spg != 0;
+        const bool tail_cut = ls1 % d.spg != 0 && ls1 < mtot;
+        // one group cut on both sides of a one-group range is side 0's job
+        const bool single = m_first == m_last && (ls0 / d.spg) == ((ls1 - 1) / d.spg);
+        const bool mine = side == 0 ? head_cut || (single && tail_cut) : (tail_cut && !single);
+        int flag = 0;
+        if (mine) {
+            const int G = side == 0 ? ls0 / d.spg : (ls1 - 1) / d.spg;
+            const int ga = d.st_begin + G * d.spg;
+            const int c_a = owner_of(ga, B.total, gridDim.x), c_b = owner_of(ga + d.spg - 1, B.total, gridDim.x);
+            flag = atomicAdd(&ws.cnt[d.cnt_off + G], 1u) == (unsigned)(c_b - c_a);
+            side_g[side] = G, side_ca[side] = c_a, side_cb[side] = c_b, side_m[side] = mi;
+        }
+        last_flag[side] = flag;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const int side = threadIdx.x >> 4, r = threadIdx.x & 15;
+        if (last_flag[side]) {
+            __threadfence();
+            const MatDesc &d = B.d[side_m[side]];
+            const int G = side_g[side], ga = d.st_begin + G * d.spg, ge = ga + d.spg;
+            float v = 0.0f;
+            for (int c = side_ca[side]; c <= side_cb[side]; c++) {
+                int cs0, cs1;
+                row_strip(B.total, c, gridDim.x, cs0, cs1);
+                // CTA c stored G as side 0 if its range starts inside G, else as side 1
+                v += __ldcg(&ws.part[(c * 2 + ((cs0 >= ga && cs0 < ge) ? 0 : 1)) * 16 + r]);
+            }
+            if (G * 16 + r < d.rows) d.y[G * 16 + r] = v;
+            if (r == 0) ws.cnt[d.cnt_off + G] = 0u;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+// Workspace layout (fixed offsets, whatever the shape, because one workspace
+// serves every launch on a stream): [cnt: CNT_MAX u32, zero between launches]
+// [part: grid*2*16 f32].  Zeroed once when allocated; the kernel leaves it zeroed.
+inline size_t ws_part_off() { return (size_t)CNT_MAX * 4; }
+inline size_t ws_bytes(int grid) { return ws_part_off() + (size_t)grid * 2 * 16 * 4 + 256; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn()
+{
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+// Weights as a [rows][row_bytes/8] u64 tensor, box = 16 rows x F::BOXW u64.
+template <class F>
+inline int make_map(CUtensorMap *m, const void *w, int rows, int cols)
+{
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return -6;
+    const cuuint64_t rb = (cuuint64_t)F::row_bytes(cols);
+    cuuint64_t dims[2] = {rb / 8, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {rb};
+    cuuint32_t box[2] = {(cuuint32_t)F::BOXW, 16};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -7;
+}
+
+// Tensor maps are pure functions of (format, pointer, shape); keep the last few.
+template <class F>
+inline int cached_map(CUtensorMap *out, const void *w, int rows, int cols)
+{
+    struct E {
+        const void *w;
+        int rows, cols;
+        CUtensorMap m;
+    };
+    static E cache[128];
+    static int next = 0;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto &e : cache)
+        if (e.w == w && e.rows == rows && e.cols == cols) {
+            *out = e.m;
+            return 0;
+        }
+    E &e = cache[next];
+    next = (next + 1) % 128;
+    const int rc = make_map<F>(&e.m, w, rows, cols);
+    if (rc) {
+        e.w = nullptr;
+        return rc;
+    }
+    e.w = w;
+    e.rows = rows;
+    e.cols = cols;
+    *out = e.m;
+    return 0;
+}
+
+struct MatOp {
+    const void *w;
+    int rows, cols;
+    const float *x;
+    float *y;
+};
+
+template <class F>
+inline int stages_per_group(int cols)
+{
+    return (cols / 256 + F::SBLK - 1) / F::SBLK;
+}
+
+// Shared memory for a batch over `grid` CTAs.
+template <class F>
+inline size_t batch_smem(const MatOp *ops, int n, int grid, int *max_cols, int *max_groups)
+{
+    long long total = 0;
+    int mc = 0;
+    for (int i = 0; i < n; i++) {
+        total += (long long)stages_per_group<F>(ops[i].cols) * ((ops[i].rows + 15) / 16);
+        mc = ops[i].cols > mc ? ops[i].cols : mc;
+    }
+    const long long per = (total + grid - 1) / grid;
+    int mg = 1;
+    for (int i = 0; i < n; i++) {
+        const int spg = stages_per_group<F>(ops[i].cols), groups = (ops[i].rows + 15) / 16;
+        const long long g = per / spg + 2;
+        const int gi = (int)(g < groups ? g : groups);
+        mg = gi > mg ? gi : mg;
+    }
+    *max_cols = mc;
+    *max_groups = mg;
+    return smem_bytes<F>(mc, mg);
+}
+
+template <class F>
+inline bool fits(const MatOp *ops, int n, int grid)
+{
+    int mc, mg;
+    for (int i = 0; i < n; i++)
+        if (ops[i].cols > F::MAX_COLS || ops[i].cols % 256 || ops[i].rows < 1) return false;
+    return batch_smem<F>(ops, n, grid, &mc, &mg) <= 227 * 1024;
+}
+
+// Launch a batch of up to MAXB independent matvecs of format F on `stream`, with
+// the scratch given as counter / partial pointers (counters zero on entry, left
+// zero); at most cnt_cap 16-row groups in the batch.
+template <class F>
+inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int grid, int pdl, cudaStream_t stream)
+{
+    if (n < 1 || n > MAXB) return -1;
+    static Batch b;  // large: built host-side, passed by value as the kernel parameter
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    int st = 0, cnt = 0;
+    for (int i = 0; i < n; i++) {
+        const MatOp &o = ops[i];
+        if (o.cols > F::MAX_COLS || o.cols % 256 || o.rows < 1) return -1;
+        MatDesc &d = b.d[i];
+        const int mrc = cached_map<F>(&d.map, o.w, o.rows, o.cols);
+        if (mrc) return mrc;
+        d.x = o.x;
+        d.y = o.y;
+        d.rows = o.rows;
+        d.cols = o.cols;
+        d.spg = stages_per_group<F>(o.cols);
+        d.st_begin = st;
+        d.cnt_off = cnt;
+        st += d.spg * ((o.rows + 15) / 16);
+        cnt += (o.rows + 15) / 16;
+    }
+    if (cnt > cnt_cap) return -1;
+    b.n = n;
+    b.total = st;
+    const size_t smem = batch_smem<F>(ops, n, grid, &b.max_cols, &b.max_groups);
+    if (smem > 227 * 1024) return -5;
+    // the kernel's dynamic shared-memory limit only ever grows (one record per device)
+    static size_t smem_set[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return -3;
+    if (smem > smem_set[dev]) {
+        if (cudaFuncSetAttribute(tc_mmv_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+            cudaSuccess)
+            return -3;
+        smem_set[dev] = smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(F::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, tc_mmv_kernel<F>, b, wsd) == cudaSuccess ? 0 : -4;
+}
+
+// As launch_batch_ws over a workspace of ws_bytes(grid) bytes.
+template <class F>
+inline int launch_batch(const MatOp *ops, int n, void *ws, int grid, int pdl, cudaStream_t stream)
+{
+    uint8_t *wsb = reinterpret_cast<uint8_t *>(ws);
+    Ws wsd;
+    wsd.cnt = reinterpret_cast<unsigned *>(wsb);
+    wsd.part = reinterpret_cast<float *>(wsb + ws_part_off());
+    return launch_batch_ws<F>(ops, n, wsd, CNT_MAX, grid, pdl, stream);
+}
+
+// Repack GGML Q6_K rows (reference layout) into the packed layout of tc_q6k.cuh.
+inline int q6k_pack(const void *src, size_t rows, size_t cols, void *dst, cudaStream_t stream)
+{
+    if (!src || !dst || !rows || cols % 256 || cols > (1u << 24) || rows > (1u << 30)) return -1;
+    const long long nb = (long long)(cols / 256), n = (long long)rows * nb;
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    q6k_pack_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint8_t *>(src), (long long)rows, (int)nb,
+                                                reinterpret_cast<uint8_t *>(dst),
+                                                (long long)q6k_packed_row_bytes(cols));
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
+}  // namespace tcmv
+}  // namespace sb
