@@ -16,8 +16,8 @@
 // past a row's end are zero-filled by the TMA unit; no multicast) into a ring
 // of F::NSLOT slots, issued before griddepcontrol.wait so the stream overlaps
 // the previous kernel under programmatic dependent launch.  F::NCW consumer
-// warps form F::NSTREAM teams of F::NCONS; team j takes stages j, j+NSTREAM, ...
-// and within a team warp w takes block w of the stage.  A warp copies its
+// warps form F::NSTREAM teams of F::NCONS; team j takes the CTA-local stages
+// k = j (mod NSTREAM), and within a team warp w takes block w of the stage.  A warp copies its
 // block's bytes to registers and releases the slot before any math.  Every
 // mbarrier wait is bounded and reports through the device error word.
 //
@@ -96,6 +96,7 @@ template <class F>
 __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_constant__ Batch B, Ws ws)
 {
     constexpr int NCW = F::NCW, NSLOT = F::NSLOT, NSTREAM = F::NSTREAM;
+    static_assert(NSLOT % NSTREAM == 0, "a ring slot must belong to one consumer team");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<F> s = carve<F>(smem_raw, B.max_cols, B.max_groups);
     int st0, st1;
@@ -174,7 +175,11 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
             const typename F::Seg S = F::seg_setup(L, s.prep, s.zero, nb);
             float acc0 = 0.0f, acc1 = 0.0f;
             int cur = -1;
-            const int k0 = ka + team;
+            // Team j takes the CTA-local stages k with k % NSTREAM == j in every segment, so
+            // (NSLOT a multiple of NSTREAM) each ring slot is only ever read by one team.  That
+            // team waited for the slot's previous phase itself, so a parity wait can never
+            // mistake the phase before an unfinished one for the awaited phase.
+            const int k0 = ka + (team - ka % NSTREAM + NSTREAM) % NSTREAM;
             int slot = k0 % NSLOT, G = (k0 + st0 - d.st_begin) / spg, j = (k0 + st0 - d.st_begin) - G * spg;
             unsigned parity = (k0 / NSLOT) & 1;
             auto flush = [&]() {

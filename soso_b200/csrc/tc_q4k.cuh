@@ -28,6 +28,9 @@
 // fragment loads are bank-conflict-free); 12 consumer warps in 3 teams of 4,
 // one block per warp per stage.
 #pragma once
+#ifndef SB_Q4K_NSLOT
+#define SB_Q4K_NSLOT 9  // ring slots (build-time tuning knob)
+#endif
 #include "tc_common.cuh"
 
 namespace sb {
@@ -40,7 +43,7 @@ struct Q4K {
     static constexpr int NSTREAM = 3;    // stages in compute at once (teams)
     static constexpr int NCW = NCONS * NSTREAM;
     static constexpr int THREADS = (NCW + 1) * 32;
-    static constexpr int NSLOT = 10;
+    static constexpr int NSLOT = SB_Q4K_NSLOT;  // a multiple of NSTREAM
     static constexpr int BOXW = SBLK * 18;  // u64 per box row (576 B)
     static constexpr int ROWB = BOXW * 8;
     static constexpr int SLOTB = 16 * ROWB;

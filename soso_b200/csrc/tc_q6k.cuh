@@ -65,7 +65,7 @@ struct Q6KP {
     static constexpr int NSTREAM = 2;
     static constexpr int NCW = NCONS * NSTREAM;
     static constexpr int THREADS = (NCW + 1) * 32;
-    static constexpr int NSLOT = 5;
+    static constexpr int NSLOT = 4;   // a multiple of NSTREAM
     static constexpr int BOXW = 212;  // u64: one group (210) + 16 bytes
     static constexpr int ROWB = BOXW * 8;
     static constexpr int SLOTB = 16 * ROWB;
