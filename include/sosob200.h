@@ -199,6 +199,28 @@ int sbk_q6k_pack(const void *src, size_t rows, size_t cols, void *dst, void *str
  * the reference's `Lote` batches (crates/soso-llm-core/src/layer.rs:571-641). */
 int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, int pdl, void *stream);
 
+/* How the input vector of a fused batch is formed as the kernel reads it, so the
+ * step that produces it costs no launch of its own (a = every op's x, which must
+ * be the same vector for the whole batch):
+ *   SBK_XS_NORM    h = a (+ res when res != NULL) and x = rmsnorm(h) * norm_w
+ *                  (gemm::rmsnorm, crates/soso-llm-core/src/gemm.rs:93-100, after the
+ *                  residual add add_f32, gemm.rs:265); when h_out != NULL it receives h
+ *                  (the new residual stream; must not alias a or res)
+ *   SBK_XS_SWIGLU  x = silu(a) * res  (swiglu_inplace, gemm.rs:210-226; a = gate, res = up)
+ * Replaces the reference's separate rmsnorm / residual-add / SwiGLU passes between
+ * matvecs (layer.rs:1284-1389). */
+enum { SBK_XS_PLAIN = 0, SBK_XS_NORM = 1, SBK_XS_SWIGLU = 2 };
+typedef struct {
+    const float *res;
+    const float *norm_w;
+    float *h_out;
+    float eps;
+    int mode;
+} sbk_xsrc;
+/* sbk_matvec_batch with the input formed as *xs says (dtype Q4_K or Q6_K_P; 16-byte
+ * aligned vectors).  Returns -5 for a dtype without the fused input forms. */
+int sbk_matvec_batch_x(uint8_t dtype, const sbk_mv_op *ops, size_t n, const sbk_xsrc *xs, int pdl, void *stream);
+
 /* RMSNorm of `rows` rows of n floats, `gemm::rmsnorm` (crates/soso-llm-core/src/gemm.rs:93-100),
  * optionally fused with the residual add `add_f32` (gemm.rs:265): with res != NULL,
  * h_out = x + res and y = rmsnorm(h_out) * w; else y = rmsnorm(x) * w.  y may alias x.
@@ -229,6 +251,16 @@ size_t sbk_attn_ws_bytes(size_t heads, size_t kv_heads, size_t head_dim, size_t 
  * Replaces mo_attn_split + mo_attn_combine (gemma_capa.cu:765-926). */
 int sbk_attn_decode(const float *q, const uint16_t *kcache, const uint16_t *vcache, float *out, const int32_t *pos,
                     size_t heads, size_t kv_heads, size_t head_dim, size_t ctx, void *ws, int pdl, void *stream);
+/* sbk_rope_kv_append and sbk_attn_decode in one launch: on the stacked, unroped
+ * [q | k | v] vector, bias / QK-norm / RoPE as sbk_rope_kv_append, this token's K/V
+ * rows appended at *pos (f16, the reference's rounding), then attention over
+ * positions 0..*pos.  qkv is not modified (the roped q lives in shared memory).
+ * Workspace as sbk_attn_decode.  Replaces gm_rope + gm_kv_append + mo_attn_split +
+ * mo_attn_combine (gemma_capa.cu:99-141, :765-926); the CPU order is layer.rs:1146-1282. */
+int sbk_attn_rope_decode(const float *qkv, const float *bias, const float *qnorm, const float *knorm,
+                         uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos, size_t heads,
+                         size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox, void *ws,
+                         int pdl, void *stream);
 
 /* out = silu(gate) * up, elementwise (`swiglu_inplace`, crates/soso-llm-core/src/gemm.rs:210-226). */
 int sbk_swiglu(const float *gate, const float *up, float *out, size_t n, int pdl, void *stream);

@@ -29,6 +29,12 @@ class SbkMvOp(ctypes.Structure):
                 ("y", ctypes.c_void_p)]
 
 
+class SbkXSrc(ctypes.Structure):
+    """sbk_xsrc: how a fused batch forms its input (mode SBK_XS_PLAIN 0 / NORM 1 / SWIGLU 2)."""
+    _fields_ = [("res", ctypes.c_void_p), ("norm_w", ctypes.c_void_p), ("h_out", ctypes.c_void_p),
+                ("eps", ctypes.c_float), ("mode", ctypes.c_int)]
+
+
 class SbStats(ctypes.Structure):
     _fields_ = [("launches", ctypes.c_uint64), ("total_ns", ctypes.c_uint64), ("bytes_up", ctypes.c_uint64),
                 ("bytes_down", ctypes.c_uint64)]
@@ -84,6 +90,11 @@ SIGNATURES = {
     "sbk_rmsnorm": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                    ctypes.c_void_p, c_size, c_size, ctypes.c_float, ctypes.c_void_p]),
     "sbk_matvec_batch": (ctypes.c_int, [ctypes.c_uint8, ctypes.c_void_p, c_size, ctypes.c_int, ctypes.c_void_p]),
+    "sbk_matvec_batch_x": (ctypes.c_int, [ctypes.c_uint8, ctypes.c_void_p, c_size, ctypes.POINTER(SbkXSrc),
+                                          ctypes.c_int, ctypes.c_void_p]),
+    "sbk_attn_rope_decode": (ctypes.c_int, [ctypes.c_void_p] * 8 + [c_size] * 4 + [ctypes.c_float, ctypes.c_float,
+                                                                           ctypes.c_int, ctypes.c_void_p,
+                                                                           ctypes.c_int, ctypes.c_void_p]),
     "sbk_rope_kv_append": (ctypes.c_int, [ctypes.c_void_p] * 7 + [c_size] * 4 + [ctypes.c_float, ctypes.c_float,
                                                                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "sbk_attn_ws_bytes": (c_size, [c_size] * 4),

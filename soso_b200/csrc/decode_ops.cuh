@@ -110,135 +110,292 @@ __global__ void rope_kv_kernel(RopeKvArgs a)
 }
 
 // ---------------------------------------------------------------- attention
-// Flash-decoding over the f16 cache, one CTA per (chunk of ATT_CH positions,
-// kv head) covering the G = heads/kv_heads query heads that share that kv
-// head, so every K/V row is read once per group (like the reference's
-// mo_attn_split, gemma_capa.cu:765-877).  Each CTA writes (acc, max, sum) for
-// its chunk; the last CTA of a kv head to finish (counter, no spinning) merges
-// the chunks in chunk order, as combinar_trozos does (attn_grupo.rs:171-203):
-// score = (q.k) / sqrt(hd), softmax over positions 0..pos inclusive.
+// Flash-decoding over the f16 cache.  One CTA per (span of positions, kv head)
+// covers the G = heads/kv_heads query heads that share that kv head, so every
+// K/V row is read once per group (like the reference's mo_attn_split,
+// gemma_capa.cu:765-877).  A span is ATT_CH positions (more when the context is
+// longer than ATT_MAXC * ATT_CH), taken ATT_CH at a time: the sub-chunk's K and V
+// rows are copied to shared memory with cp.async first (all in flight at once),
+// then scores, an online-softmax update and P.V run out of shared memory.  With
+// one span the CTA writes the output directly; otherwise each CTA writes
+// (acc, max, sum) and the last CTA of a kv head to finish (counter, no
+// spinning) merges the spans in order, as combinar_trozos does
+// (attn_grupo.rs:171-203): score = (q.k) / sqrt(hd), softmax over 0..pos.
+//
+// With `rope` set the kernel also does the step before it (layer.rs:1146-1193,
+// as rope_kv_kernel): q heads get bias, QK-norm and RoPE into shared memory,
+// and the CTA whose span holds position pos forms this token's K and V rows
+// the same way, appends them to the caches (f16, the reference's rounding) and
+// uses the rounded rows, exactly as the reference attends over its f16 cache.
 constexpr int ATT_CH = 64;
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAXG = 8;
+constexpr int ATT_MAXC = 64;  // spans per kv head at most
+constexpr int ATT_KPAD = 8;   // f16 pad per cached row in shared memory (272-byte rows)
 
 struct AttnArgs {
-    const float *q;            // [heads][hd], roped
-    const uint16_t *kc, *vc;   // [ctx][kv_dim] f16
+    const float *qkv;          // q [heads][hd]; with rope: then k [kv_heads][hd], v [kv_heads][hd]
+    const float *bias;         // rope: same layout as qkv, or null
+    const float *qnorm;        // rope: [hd] or null
+    const float *knorm;        // rope: [hd] or null
+    uint16_t *kc, *vc;         // [ctx][kv_dim] f16
     float *out;                // [heads][hd]
-    float *part;               // workspace [kv_heads][max_chunks][G][hd + 2]
+    float *part;               // workspace [kv_heads][ATT_MAXC][G][hd + 2]
     unsigned *cnt;             // workspace [kv_heads], zero between launches
     const int *pos;
-    int heads, kv_heads, kv_dim, ctx, max_chunks;
+    int heads, kv_heads, kv_dim, ctx, span;
+    float theta, eps;
+    int neox, rope;
 };
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
 
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(AttnArgs a)
 {
+    static_assert(HD == 128, "one lane per two RoPE pairs; one thread per two P.V dims of two heads");
     __shared__ float qs[ATT_MAXG][HD];
+    __shared__ __align__(16) uint16_t ks[ATT_CH][HD + ATT_KPAD];
+    __shared__ __align__(16) uint16_t vs[ATT_CH][HD + ATT_KPAD];
+    __shared__ __align__(16) uint16_t knew[HD], vnew[HD];
     __shared__ float sc[ATT_MAXG][ATT_CH];
+    __shared__ float rc[HD / 2], rs[HD / 2];
+    __shared__ float s_m[ATT_MAXG], s_l[ATT_MAXG], s_f[ATT_MAXG];
+    __shared__ float sw[ATT_MAXG][ATT_MAXC];
     __shared__ int is_last;
     griddep_wait();
     const int G = a.heads / a.kv_heads, kvh = blockIdx.y, c = blockIdx.x, tid = threadIdx.x;
-    const int seq = *a.pos + 1;
-    const int nch = (seq + ATT_CH - 1) / ATT_CH;
-    if (c >= nch || seq > a.ctx || nch > a.max_chunks) {
-        if (c == 0 && tid == 0 && (seq > a.ctx || nch > a.max_chunks)) set_dev_error(0x62u);
+    const int warp = tid >> 5, lane = tid & 31;
+    const int pos = *a.pos, seq = pos + 1;
+    const int nch = (seq + a.span - 1) / a.span;
+    if (pos < 0 || c >= nch || seq > a.ctx || nch > ATT_MAXC) {
+        if (c == 0 && tid == 0 && (pos < 0 || seq > a.ctx || nch > ATT_MAXC)) set_dev_error(0x62u);
         return;
     }
-    const int t0 = c * ATT_CH, tn = min(ATT_CH, seq - t0);
-    const float inv = 1.0f / sqrtf((float)HD);
-    for (int i = tid; i < G * HD; i += ATT_THREADS) qs[i / HD][i % HD] = a.q[(kvh * G) * HD + i];
+    const int tb = c * a.span, te = min(seq, tb + a.span);
+    const bool own_new = a.rope && c == nch - 1;  // this CTA forms and appends row pos
+    // first sub-chunk's rows in flight while q (and the new rows) are prepared
+    auto load_rows = [&](int t0, int tn) {
+        for (int i = tid; i < tn * (HD / 8); i += ATT_THREADS) {
+            const int r = i / (HD / 8), v8 = i % (HD / 8);
+            if (own_new && t0 + r == pos) continue;
+            const size_t g = (size_t)(t0 + r) * a.kv_dim + kvh * HD + v8 * 8;
+            cp_async16(&ks[r][v8 * 8], a.kc + g);
+            cp_async16(&vs[r][v8 * 8], a.vc + g);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    load_rows(tb, min(ATT_CH, te - tb));
+    // RoPE angles (rope_cabezas: freq_i = theta^(-2i/d), angle = pos * freq_i)
+    if (a.rope && tid < HD / 2) {
+        const float freq = powf(a.theta, (-2.0f * (float)tid) / (float)HD);
+        const float ang = (float)pos * freq;
+        rs[tid] = sinf(ang);
+        rc[tid] = cosf(ang);
+    }
+    if (tid < ATT_MAXG) s_m[tid] = -INFINITY, s_l[tid] = 0.0f;
     __syncthreads();
-    // scores: thread (t = tid/4, quarter dq = tid%4)
-    {
-        const int t = tid >> 2, dq = tid & 3;
-        float part[ATT_MAXG];
+    // q heads of the group (and, for own_new, this token's k and v rows): one warp per
+    // vector, lane l holds pairs l and l + 32
+    const int ntask = G + (own_new ? 2 : 0);
+    for (int task = warp; task < ntask; task += ATT_THREADS / 32) {
+        const int kind = task < G ? 0 : task - G + 1;  // 0 q, 1 k, 2 v
+        const int base = kind == 0 ? (kvh * G + task) * HD : a.heads * HD + (kind == 2 ? a.kv_dim : 0) + kvh * HD;
+        float v[4];
+        int e[4];
 #pragma unroll
-        for (int j = 0; j < ATT_MAXG; j++) part[j] = 0.0f;
-        if (t < tn) {
-            const uint16_t *krow = a.kc + (size_t)(t0 + t) * a.kv_dim + kvh * HD + dq * (HD / 4);
+        for (int h = 0; h < 2; h++) {
+            const int p = lane + 32 * h;
+            e[2 * h] = a.neox ? p : 2 * p;
+            e[2 * h + 1] = a.neox ? p + HD / 2 : 2 * p + 1;
+        }
 #pragma unroll
-            for (int v8 = 0; v8 < HD / 32; v8++) {
-                const uint4 kk = *reinterpret_cast<const uint4 *>(krow + v8 * 8);
-                const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w};
+        for (int k = 0; k < 4; k++) v[k] = a.qkv[base + e[k]];
+        if (a.rope) {
+            if (a.bias) {
 #pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&kw[e]));
-                    const int d = dq * (HD / 4) + v8 * 8 + 2 * e;
+                for (int k = 0; k < 4; k++) v[k] += a.bias[base + e[k]];
+            }
+            const float *nw = kind == 0 ? a.qnorm : kind == 1 ? a.knorm : nullptr;
+            if (nw) {
+                const float ss = warp_sum((v[0] * v[0] + v[1] * v[1]) + (v[2] * v[2] + v[3] * v[3]));
+                const float scale = 1.0f / sqrtf(ss / (float)HD + a.eps);
 #pragma unroll
-                    for (int j = 0; j < ATT_MAXG; j++)
-                        if (j < G) part[j] += qs[j][d] * kf.x + qs[j][d + 1] * kf.y;
+                for (int k = 0; k < 4; k++) v[k] = v[k] * scale * nw[e[k]];
+            }
+            if (kind < 2) {
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const float cs = rc[lane + 32 * h], sn = rs[lane + 32 * h];
+                    const float x0 = v[2 * h], x1 = v[2 * h + 1];
+                    v[2 * h] = x0 * cs - x1 * sn;
+                    v[2 * h + 1] = x0 * sn + x1 * cs;
                 }
             }
         }
+        if (kind == 0) {
 #pragma unroll
-        for (int j = 0; j < ATT_MAXG; j++) {
-            part[j] += __shfl_xor_sync(0xffffffffu, part[j], 1);
-            part[j] += __shfl_xor_sync(0xffffffffu, part[j], 2);
-        }
-        if (dq == 0)
-            for (int j = 0; j < G; j++) sc[j][t] = t < tn ? part[j] * inv : -INFINITY;
-    }
-    __syncthreads();
-    // softmax pieces: warp j owns head j
-    const int warp = tid >> 5, lane = tid & 31;
-    float *dst = a.part + ((size_t)(kvh * a.max_chunks + c) * G) * (HD + 2);
-    if (warp < G) {
-        const float s0 = sc[warp][lane], s1 = sc[warp][lane + 32];
-        float m = fmaxf(s0, s1);
+            for (int k = 0; k < 4; k++) qs[task][e[k]] = v[k];
+        } else {
+            uint16_t *row = (kind == 1 ? a.kc : a.vc) + (size_t)pos * a.kv_dim + kvh * HD;
+            uint16_t *nrow = kind == 1 ? knew : vnew;
 #pragma unroll
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const float p0 = lane < tn ? expf(s0 - m) : 0.0f, p1 = lane + 32 < tn ? expf(s1 - m) : 0.0f;
-        sc[warp][lane] = p0;
-        sc[warp][lane + 32] = p1;
-        const float l = warp_sum(p0 + p1);
-        if (lane == 0) {
-            dst[warp * (HD + 2) + HD] = m;
-            dst[warp * (HD + 2) + HD + 1] = l;
+            for (int k = 0; k < 4; k++) {
+                const uint16_t hb = f32_to_f16_ref(v[k]);
+                row[e[k]] = hb;
+                nrow[e[k]] = hb;
+            }
         }
     }
-    __syncthreads();
-    // P.V: thread -> dims (2*(tid % (HD/2)), +1), heads tid/(HD/2), + step
-    {
-        const int dp = tid % (HD / 2), j0 = tid / (HD / 2), jstep = ATT_THREADS / (HD / 2);
-        for (int j = j0; j < G; j += jstep) {
-            float ax = 0.0f, ay = 0.0f;
+    const float inv = 1.0f / sqrtf((float)HD);
+    // P.V ownership: dims 2*dp, 2*dp+1 of heads j0 and j0 + 4
+    const int dp = tid % (HD / 2), j0 = tid / (HD / 2);
+    float ax[2] = {0.0f, 0.0f}, ay[2] = {0.0f, 0.0f};
+    for (int t0 = tb; t0 < te; t0 += ATT_CH) {
+        const int tn = min(ATT_CH, te - t0);
+        if (t0 != tb) load_rows(t0, tn);
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();  // rows landed; q and the new rows written
+        if (own_new && pos >= t0 && pos < t0 + tn)
+            for (int i = tid; i < HD; i += ATT_THREADS) ks[pos - t0][i] = knew[i], vs[pos - t0][i] = vnew[i];
+        __syncthreads();
+        // scores: thread (t = tid/4, quarter dq = tid%4)
+        {
+            const int t = tid >> 2, dq = tid & 3;
+            float part[ATT_MAXG];
+#pragma unroll
+            for (int j = 0; j < ATT_MAXG; j++) part[j] = 0.0f;
+            if (t < tn) {
+#pragma unroll
+                for (int v8 = 0; v8 < HD / 32; v8++) {
+                    const uint4 kk = *reinterpret_cast<const uint4 *>(&ks[t][dq * (HD / 4) + v8 * 8]);
+                    const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+                    for (int e2 = 0; e2 < 4; e2++) {
+                        const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&kw[e2]));
+                        const int d = dq * (HD / 4) + v8 * 8 + 2 * e2;
+#pragma unroll
+                        for (int j = 0; j < ATT_MAXG; j++)
+                            if (j < G) part[j] += qs[j][d] * kf.x + qs[j][d + 1] * kf.y;
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < ATT_MAXG; j++) {
+                part[j] += __shfl_xor_sync(0xffffffffu, part[j], 1);
+                part[j] += __shfl_xor_sync(0xffffffffu, part[j], 2);
+            }
+            if (dq == 0)
+                for (int j = 0; j < G; j++) sc[j][t] = t < tn ? part[j] * inv : -INFINITY;
+        }
+        __syncthreads();
+        // online softmax: warp j owns head j
+        if (warp < G) {
+            const float s0 = sc[warp][lane], s1 = sc[warp][lane + 32];
+            float m = fmaxf(s0, s1);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float mo = s_m[warp], mn = fmaxf(mo, m);
+            const float p0 = lane < tn ? expf(s0 - mn) : 0.0f, p1 = lane + 32 < tn ? expf(s1 - mn) : 0.0f;
+            sc[warp][lane] = p0;
+            sc[warp][lane + 32] = p1;
+            const float l = warp_sum(p0 + p1);
+            __syncwarp();
+            if (lane == 0) {
+                const float f = mo == -INFINITY ? 0.0f : expf(mo - mn);
+                s_f[warp] = f;
+                s_l[warp] = s_l[warp] * f + l;
+                s_m[warp] = mn;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int j = j0 + 4 * h;
+            if (j >= G) continue;
+            const float f = s_f[j];
+            float x0 = ax[h] * f, y0 = ay[h] * f;
             for (int t = 0; t < tn; t++) {
                 const float p = sc[j][t];
-                const float2 vf = __half22float2(
-                    *reinterpret_cast<const __half2 *>(a.vc + (size_t)(t0 + t) * a.kv_dim + kvh * HD + 2 * dp));
-                ax += p * vf.x;
-                ay += p * vf.y;
+                const float2 vf = __half22float2(*reinterpret_cast<const __half2 *>(&vs[t][2 * dp]));
+                x0 += p * vf.x;
+                y0 += p * vf.y;
             }
-            dst[j * (HD + 2) + 2 * dp] = ax;
-            dst[j * (HD + 2) + 2 * dp + 1] = ay;
+            ax[h] = x0, ay[h] = y0;
         }
+        __syncthreads();  // before the next sub-chunk overwrites ks / vs / sc
     }
+    if (nch == 1) {  // the whole context in one span: normalise and store
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int j = j0 + 4 * h;
+            if (j >= G) continue;
+            const float l = s_l[j], r = l > 0.0f ? 1.0f / l : 0.0f;
+            float *o = a.out + (size_t)(kvh * G + j) * HD;
+            o[2 * dp] = l > 0.0f ? ax[h] * r : 0.0f;
+            o[2 * dp + 1] = l > 0.0f ? ay[h] * r : 0.0f;
+        }
+        griddep_launch();
+        return;
+    }
+    float *dst = a.part + ((size_t)(kvh * ATT_MAXC + c) * G) * (HD + 2);
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int j = j0 + 4 * h;
+        if (j >= G) continue;
+        dst[j * (HD + 2) + 2 * dp] = ax[h];
+        dst[j * (HD + 2) + 2 * dp + 1] = ay[h];
+    }
+    if (tid < G) dst[tid * (HD + 2) + HD] = s_m[tid], dst[tid * (HD + 2) + HD + 1] = s_l[tid];
     __threadfence();
     __syncthreads();
     if (tid == 0) is_last = atomicAdd(&a.cnt[kvh], 1u) == (unsigned)(nch - 1);
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    // merge chunks 0..nch-1 in order (combinar_trozos)
-    const float *base = a.part + (size_t)kvh * a.max_chunks * G * (HD + 2);
-    for (int i = tid; i < G * HD; i += ATT_THREADS) {
-        const int j = i / HD, d = i % HD;
-        float mmax = -INFINITY;
-        for (int cc = 0; cc < nch; cc++) {
+    // merge spans 0..nch-1 (combinar_trozos): per head, weights exp(m_c - M) from one warp,
+    // then every output element as an independent-load sum over spans
+    const float *base = a.part + (size_t)kvh * ATT_MAXC * G * (HD + 2);
+    if (warp < G) {
+        const int j = warp;
+        float M = -INFINITY;
+        for (int cc = lane; cc < nch; cc += 32) {
             const float *pc = base + ((size_t)cc * G + j) * (HD + 2);
-            if (__ldcg(pc + HD + 1) > 0.0f) mmax = fmaxf(mmax, __ldcg(pc + HD));
+            if (__ldcg(pc + HD + 1) > 0.0f) M = fmaxf(M, __ldcg(pc + HD));
         }
-        float o = 0.0f, l = 0.0f;
-        for (int cc = 0; cc < nch; cc++) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.0f;
+        for (int cc = lane; cc < nch; cc += 32) {
             const float *pc = base + ((size_t)cc * G + j) * (HD + 2);
             const float li = __ldcg(pc + HD + 1);
-            if (li <= 0.0f) continue;
-            const float w = expf(__ldcg(pc + HD) - mmax);
-            l += w * li;
-            o += w * __ldcg(pc + d);
+            const float w = li > 0.0f ? expf(__ldcg(pc + HD) - M) : 0.0f;
+            sw[j][cc] = w;
+            L += w * li;
         }
-        a.out[(kvh * G + j) * HD + d] = l > 0.0f ? o * (1.0f / l) : 0.0f;
+        L = warp_sum(L);
+        if (lane == 0) s_l[j] = L;
+    }
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += ATT_THREADS) {
+        const int j = i / HD, d = i % HD;
+        float o = 0.0f;
+        int cc = 0;
+        for (; cc + 4 <= nch; cc += 4) {
+            float v[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) v[k] = __ldcg(base + ((size_t)(cc + k) * G + j) * (HD + 2) + d);
+#pragma unroll
+            for (int k = 0; k < 4; k++) o += sw[j][cc + k] * v[k];
+        }
+        for (; cc < nch; cc++) o += sw[j][cc] * __ldcg(base + ((size_t)cc * G + j) * (HD + 2) + d);
+        const float L = s_l[j];
+        a.out[(kvh * G + j) * HD + d] = L > 0.0f ? o * (1.0f / L) : 0.0f;
     }
     if (tid == 0) a.cnt[kvh] = 0u;
     griddep_launch();
@@ -302,8 +459,14 @@ __global__ void router_topk_kernel(const float *__restrict__ logits, int n, int 
 
 // ------------------------------------------------------------------- argmax
 // Runtime::argmax (crates/soso-llm-core/src/runtime.rs:2021-2028): Rust's
-// max_by keeps the LAST of equal maxima.  Per-CTA partials, the last CTA to
-// finish reduces them (counter, no spinning).
+// max_by keeps the LAST of equal maxima.  Per-CTA partials (four independent
+// loads in flight per thread), the last CTA to finish reduces them in parallel
+// (counter, no spinning).  When `step` is set it also ends a greedy step of the
+// device-side loop: hist[i] = the argmax of step i, the next token is prompt[i+1]
+// while the prompt lasts, else that argmax; the position advances.
+constexpr int AM_THREADS = 512;
+constexpr int AM_GRID = 148;
+
 struct ArgmaxArgs {
     const float *v;
     int n;
@@ -311,6 +474,9 @@ struct ArgmaxArgs {
     int *pi;         // workspace [grid]
     unsigned *cnt;   // workspace, zero between launches
     int *out;
+    // greedy step (all null when unused)
+    int *pos, *step, *hist;
+    const int *prompt, *n_prompt;
 };
 
 __device__ __forceinline__ void amax_merge(float &bv, int &bi, float v, int i)
@@ -321,17 +487,8 @@ __device__ __forceinline__ void amax_merge(float &bv, int &bi, float v, int i)
     }
 }
 
-__global__ void argmax_kernel(ArgmaxArgs a)
+__device__ __forceinline__ void amax_block(float &bv, int &bi, float *sv, int *si)
 {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    __shared__ int is_last;
-    griddep_wait();
-    int s, e;
-    row_strip(a.n, blockIdx.x, gridDim.x, s, e);
-    float bv = -INFINITY;
-    int bi = -1;
-    for (int i = s + threadIdx.x; i < e; i += blockDim.x) amax_merge(bv, bi, a.v[i], i);
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -343,21 +500,62 @@ __global__ void argmax_kernel(ArgmaxArgs a)
         si[threadIdx.x >> 5] = bi;
     }
     __syncthreads();
+    if (threadIdx.x < 32) {
+        const int nw = blockDim.x >> 5;
+        bv = threadIdx.x < nw ? sv[threadIdx.x] : -INFINITY;
+        bi = threadIdx.x < nw ? si[threadIdx.x] : -1;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            amax_merge(bv, bi, ov, oi);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(AM_THREADS) argmax_kernel(ArgmaxArgs a)
+{
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ int is_last;
+    griddep_wait();
+    int s, e;
+    row_strip(a.n, blockIdx.x, gridDim.x, s, e);
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int i = s + threadIdx.x; i < e; i += 4 * AM_THREADS) {
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = i + k * AM_THREADS < e ? a.v[i + k * AM_THREADS] : -INFINITY;
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (i + k * AM_THREADS < e) amax_merge(bv, bi, v[k], i + k * AM_THREADS);
+    }
+    amax_block(bv, bi, sv, si);
     if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++) amax_merge(bv, bi, sv[w], si[w]);
         a.pv[blockIdx.x] = bv;
         a.pi[blockIdx.x] = bi;
         __threadfence();
         is_last = atomicAdd(a.cnt, 1u) == gridDim.x - 1;
     }
     __syncthreads();
-    if (is_last && threadIdx.x == 0) {
-        __threadfence();
-        float v = -INFINITY;
-        int i = -1;
-        for (int c = 0; c < (int)gridDim.x; c++) amax_merge(v, i, __ldcg(a.pv + c), __ldcg(a.pi + c));
-        *a.out = i < 0 ? 0 : i;
+    if (!is_last) return;
+    __threadfence();
+    bv = -INFINITY, bi = -1;
+    for (int c = threadIdx.x; c < (int)gridDim.x; c += AM_THREADS) amax_merge(bv, bi, __ldcg(a.pv + c), __ldcg(a.pi + c));
+    __syncthreads();
+    amax_block(bv, bi, sv, si);
+    if (threadIdx.x == 0) {
+        const int tok = bi < 0 ? 0 : bi;
+        *a.out = tok;
         *a.cnt = 0u;
+        if (a.step) {
+            const int i = *a.step;
+            a.hist[i] = tok;
+            if (i + 1 < *a.n_prompt) *a.out = a.prompt[i + 1];
+            *a.pos += 1;
+            *a.step = i + 1;
+        }
     }
     griddep_launch();
 }
@@ -451,26 +649,53 @@ extern "C" int sbk_rope_kv_append(float *qkv, const float *bias, const float *qn
 extern "C" size_t sbk_attn_ws_bytes(size_t heads, size_t kv_heads, size_t head_dim, size_t ctx)
 {
     const size_t G = kv_heads ? heads / kv_heads : 0;
-    const size_t chunks = (ctx + sb::ATT_CH - 1) / sb::ATT_CH;
-    return 256 + kv_heads * 4 + kv_heads * chunks * G * (head_dim + 2) * 4;
+    (void)ctx;
+    return 256 + kv_heads * 4 + 16 + kv_heads * sb::ATT_MAXC * G * (head_dim + 2) * 4;
 }
+
+namespace sb {
+inline int attn_launch(const AttnArgs &a0, size_t heads, size_t kv_heads, size_t head_dim, size_t ctx, void *ws,
+                       int pdl, cudaStream_t s)
+{
+    if (!a0.qkv || !a0.kc || !a0.vc || !a0.out || !a0.pos || !ws || !kv_heads || heads % kv_heads) return -1;
+    const size_t G = heads / kv_heads;
+    if (G > ATT_MAXG || head_dim != 128 || ctx == 0 || ctx > (1u << 24)) return -1;
+    if (((uintptr_t)a0.kc | (uintptr_t)a0.vc) & 15) return -2;
+    // positions per CTA: ATT_CH, or a multiple of it so at most ATT_MAXC spans cover ctx
+    const size_t subs = (ctx + ATT_CH - 1) / ATT_CH;
+    const int span = (int)(((subs + ATT_MAXC - 1) / ATT_MAXC) * ATT_CH);
+    const int chunks = (int)((ctx + span - 1) / span);
+    // workspace: [counters (zeroed, left zero)] [partials]
+    AttnArgs a = a0;
+    a.cnt = (unsigned *)ws;
+    float *part = (float *)((char *)ws + 256 + kv_heads * 4);
+    a.part = (float *)(((uintptr_t)part + 15) & ~(uintptr_t)15);
+    a.heads = (int)heads, a.kv_heads = (int)kv_heads, a.kv_dim = (int)(kv_heads * head_dim);
+    a.ctx = (int)ctx, a.span = span;
+    return launch_k(attn_decode_kernel<128>, dim3((unsigned)chunks, (unsigned)kv_heads), dim3(ATT_THREADS), 0, pdl,
+                    s, a);
+}
+}  // namespace sb
 
 extern "C" int sbk_attn_decode(const float *q, const uint16_t *kcache, const uint16_t *vcache, float *out,
                                const int32_t *pos, size_t heads, size_t kv_heads, size_t head_dim, size_t ctx,
                                void *ws, int pdl, void *stream)
 {
-    if (!q || !kcache || !vcache || !out || !pos || !ws || !kv_heads || heads % kv_heads) return -1;
-    const size_t G = heads / kv_heads;
-    if (G > sb::ATT_MAXG || head_dim != 128) return -1;
-    const int chunks = (int)((ctx + sb::ATT_CH - 1) / sb::ATT_CH);
-    // workspace: [counters (zeroed, left zero)] [partials]
-    unsigned *cnt = (unsigned *)ws;
-    float *part = (float *)((char *)ws + 256 + kv_heads * 4);
-    part = (float *)(((uintptr_t)part + 15) & ~(uintptr_t)15);
-    sb::AttnArgs a{q, kcache, vcache, out, part, cnt, pos, (int)heads, (int)kv_heads, (int)(kv_heads * head_dim),
-                   (int)ctx, chunks};
-    return sb::launch_k(sb::attn_decode_kernel<128>, dim3((unsigned)chunks, (unsigned)kv_heads), dim3(sb::ATT_THREADS),
-                        0, pdl, (cudaStream_t)stream, a);
+    sb::AttnArgs a = {};
+    a.qkv = q, a.kc = const_cast<uint16_t *>(kcache), a.vc = const_cast<uint16_t *>(vcache), a.out = out, a.pos = pos;
+    a.rope = 0;
+    return sb::attn_launch(a, heads, kv_heads, head_dim, ctx, ws, pdl, (cudaStream_t)stream);
+}
+
+extern "C" int sbk_attn_rope_decode(const float *qkv, const float *bias, const float *qnorm, const float *knorm,
+                                    uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos, size_t heads,
+                                    size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox,
+                                    void *ws, int pdl, void *stream)
+{
+    sb::AttnArgs a = {};
+    a.qkv = qkv, a.bias = bias, a.qnorm = qnorm, a.knorm = knorm, a.kc = kcache, a.vc = vcache, a.out = out;
+    a.pos = pos, a.theta = theta, a.eps = eps, a.neox = neox, a.rope = 1;
+    return sb::attn_launch(a, heads, kv_heads, head_dim, ctx, ws, pdl, (cudaStream_t)stream);
 }
 
 extern "C" int sbk_router_topk(const float *logits, size_t n_exp, size_t top_k, int32_t *idx, float *wts, int pdl,
@@ -481,17 +706,24 @@ extern "C" int sbk_router_topk(const float *logits, size_t n_exp, size_t top_k, 
                         (int)n_exp, (int)top_k, idx, wts);
 }
 
-extern "C" size_t sbk_argmax_ws_bytes(void) { return 256 + 148 * 8 * 2; }
+extern "C" size_t sbk_argmax_ws_bytes(void) { return 256 + sb::AM_GRID * 8 * 2; }
+
+namespace sb {
+inline int argmax_launch(const float *v, size_t n, int32_t *out, void *ws, int pdl, cudaStream_t s, int *pos,
+                         int *step, int *hist, const int *prompt, const int *n_prompt)
+{
+    if (!v || !n || !out || !ws || n > (1u << 30)) return -1;
+    unsigned *cnt = (unsigned *)ws;
+    float *pv = (float *)((char *)ws + 256);
+    int *pi = (int *)((char *)ws + 256 + AM_GRID * 8);
+    ArgmaxArgs a{v, (int)n, pv, pi, cnt, out, pos, step, hist, prompt, n_prompt};
+    return launch_k(argmax_kernel, dim3(AM_GRID), dim3(AM_THREADS), 0, pdl, s, a);
+}
+}  // namespace sb
 
 extern "C" int sbk_argmax(const float *v, size_t n, int32_t *out, void *ws, int pdl, void *stream)
 {
-    if (!v || !n || !out || !ws || n > (1u << 30)) return -1;
-    const int grid = 148;
-    unsigned *cnt = (unsigned *)ws;
-    float *pv = (float *)((char *)ws + 256);
-    int *pi = (int *)((char *)ws + 256 + grid * 8);
-    sb::ArgmaxArgs a{v, (int)n, pv, pi, cnt, out};
-    return sb::launch_k(sb::argmax_kernel, dim3(grid), dim3(256), 0, pdl, (cudaStream_t)stream, a);
+    return sb::argmax_launch(v, n, out, ws, pdl, (cudaStream_t)stream, nullptr, nullptr, nullptr, nullptr, nullptr);
 }
 
 extern "C" int sbk_embed_row(const void *table, uint8_t dtype, size_t vocab, size_t hidden, const int32_t *token,

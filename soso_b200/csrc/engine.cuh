@@ -13,13 +13,19 @@
 // token = argmax(logits) (runtime.rs:1976-2028).  The residual add of each
 // block is fused into the RMSNorm that follows it.
 //
-// Per token: 9 launches per layer + 4, all captured once; independent matvecs
-// of one input (q/k/v, gate/up) share one launch (sbk_matvec_batch).
+// Per token: 5 launches per layer + 2, all captured once.  Independent matvecs
+// of one input (q/k/v, gate/up) share one launch (sbk_matvec_batch_x), and the
+// elementwise steps are folded into the launches around them: the residual add
+// and RMSNorm into the preparation of the next matvec's input, SwiGLU into the
+// down projection's, bias / QK-norm / RoPE / KV append into attention, and the
+// end of a greedy step into argmax.  The residual stream alternates between two
+// buffers (a matvec's CTAs read one while CTA 0 writes the other).
 #pragma once
 #include <algorithm>
 #include <vector>
 
 #include "dispatch.cuh"
+#include "decode_ops.cuh"
 
 extern "C" int sbk_embed_row(const void *table, uint8_t dtype, size_t vocab, size_t hidden, const int32_t *token,
                              float *out, int pdl, void *stream);
@@ -33,6 +39,10 @@ extern "C" int sbk_attn_decode(const float *q, const uint16_t *kcache, const uin
                                void *ws, int pdl, void *stream);
 extern "C" size_t sbk_argmax_ws_bytes(void);
 extern "C" int sbk_argmax(const float *v, size_t n, int32_t *out, void *ws, int pdl, void *stream);
+extern "C" int sbk_attn_rope_decode(const float *qkv, const float *bias, const float *qnorm, const float *knorm,
+                                    uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos, size_t heads,
+                                    size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox,
+                                    void *ws, int pdl, void *stream);
 
 namespace sb {
 
@@ -45,20 +55,6 @@ __global__ void swiglu_kernel(const float *__restrict__ g, const float *__restri
         o[i] = x / (1.0f + expf(-x)) * u[i];
     }
     griddep_launch();
-}
-
-// End of a greedy step: record the argmax of step i; the token fed next is
-// prompt[i+1] while the prompt lasts, else that argmax; advance the position.
-__global__ void advance_kernel(int *pos, int *tok, const int *prompt, const int *n_prompt, int *hist, int *step)
-{
-    griddep_wait();
-    if (threadIdx.x == 0 && blockIdx.x == 0) {
-        const int i = *step;
-        hist[i] = *tok;
-        if (i + 1 < *n_prompt) *tok = prompt[i + 1];
-        *pos += 1;
-        *step = i + 1;
-    }
 }
 
 // New K/V rows (at *pos) of every layer into one contiguous [layer][k | v] buffer.
@@ -109,11 +105,6 @@ struct EngMat {
     size_t rows = 0, cols = 0;
 };
 
-struct MvGroup {
-    uint8_t dt;
-    std::vector<sbk_mv_op> ops;
-};
-
 struct EngLayer {
     EngMat q, k, v, o, g, u, d;
     size_t heads = 0, kvh = 0, hd = 0, qd = 0, kvd = 0, ffn = 0;
@@ -121,7 +112,6 @@ struct EngLayer {
     int neox = 0;
     float *qn = nullptr, *kn = nullptr, *bias = nullptr, *na = nullptr, *nf = nullptr;
     uint16_t *kc = nullptr, *vc = nullptr;
-    std::vector<MvGroup> qkv, gu;
 };
 
 }  // namespace
@@ -132,7 +122,7 @@ struct sb_engine {
     float eps = 0.0f;
     EngMat lm, emb;
     float *fnorm = nullptr;
-    float *h = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *ob = nullptr, *gu = nullptr, *act = nullptr,
+    float *h = nullptr, *h2 = nullptr, *tmp = nullptr, *qkv = nullptr, *att = nullptr, *ob = nullptr, *gu = nullptr,
           *logits = nullptr;
     int *ints = nullptr;  // pos, tok, step, n_prompt
     int *prompt = nullptr, *hist = nullptr;
@@ -190,20 +180,36 @@ int upload_f32(sb_engine *e, const float *src, size_t n, float **dst)
     return 0;
 }
 
-void add_op(std::vector<MvGroup> &gs, const EngMat &m, const float *x, float *y)
-{
-    for (auto &g : gs)
-        if (g.dt == m.dt) {
-            g.ops.push_back(sbk_mv_op{m.w, m.rows, m.cols, x, y});
-            return;
-        }
-    gs.push_back(MvGroup{m.dt, {sbk_mv_op{m.w, m.rows, m.cols, x, y}}});
-}
+bool fused_dtype(uint8_t dt) { return dt == SB_DTYPE_Q4_K || dt == SB_DTYPE_Q6_K_P; }
 
-int run_groups(const std::vector<MvGroup> &gs, cudaStream_t s, size_t *launches)
+// The matvecs `ms` (one input vector a, outputs ys) with the input formed as xs says:
+// one fused launch per dtype where the kernel has the fused input forms, else the
+// input is materialised first (sbk_rmsnorm / sbk_swiglu into `tmp`).
+int run_mv(sb_engine *e, const EngMat *const *ms, float *const *ys, int n, const float *a, const sbk_xsrc &xs,
+           cudaStream_t s, size_t *launches)
 {
-    for (const auto &g : gs) {
-        const int rc = sbk_matvec_batch(g.dt, g.ops.data(), g.ops.size(), 1, s);
+    bool done[8] = {false};
+    for (int i = 0; i < n; i++) {
+        if (done[i]) continue;
+        const uint8_t dt = ms[i]->dt;
+        sbk_mv_op ops[8];
+        int k = 0;
+        for (int j = i; j < n; j++)
+            if (!done[j] && ms[j]->dt == dt) ops[k++] = sbk_mv_op{ms[j]->w, ms[j]->rows, ms[j]->cols, a, ys[j]}, done[j] = true;
+        int rc;
+        if (fused_dtype(dt) || xs.mode == SBK_XS_PLAIN) {
+            rc = xs.mode == SBK_XS_PLAIN ? sbk_matvec_batch(dt, ops, k, 1, s) : sbk_matvec_batch_x(dt, ops, k, &xs, 1, s);
+        } else {
+            const size_t cols = ops[0].cols;
+            if (xs.mode == SBK_XS_NORM)
+                rc = sbk_rmsnorm(a, xs.res, xs.res ? xs.h_out : nullptr, xs.norm_w, e->tmp, 1, cols, xs.eps, s);
+            else
+                rc = sbk_swiglu(a, xs.res, e->tmp, cols, 1, s);
+            if (rc) return rc;
+            *launches += 1;
+            for (int j = 0; j < k; j++) ops[j].x = e->tmp;
+            rc = sbk_matvec_batch(dt, ops, k, 1, s);
+        }
         if (rc) return rc;
         *launches += 1;
     }
@@ -216,37 +222,61 @@ int run_groups(const std::vector<MvGroup> &gs, cudaStream_t s, size_t *launches)
         if (_rc) return fail(std::string("decode step: ") + #x + " rejected (" + std::to_string(_rc) + ")"); \
         n++;                                                                                                 \
     } while (0)
+#define ENG_MV(...)                                                                                          \
+    do {                                                                                                     \
+        const int _rc = run_mv(e, __VA_ARGS__, s, &n);                                                        \
+        if (_rc) return fail(std::string("decode step: matvec launch rejected (") + std::to_string(_rc) + ")"); \
+    } while (0)
 
 // One token, enqueued on s.  greedy: embedding row from the device token, and
-// argmax + advance at the end.
+// argmax (which also ends the step) at the end.
 int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
 {
     size_t n = 0;
     int *pos = e->ints, *tok = e->ints + 1, *step = e->ints + 2, *np = e->ints + 3;
+    float *hc = e->h, *ho = e->h2;  // residual stream: current / the other buffer
     if (greedy) ENG_CHECK(sbk_embed_row(e->emb.w, e->emb.dt, e->V, e->H, tok, e->h, 1, s));
     for (size_t l = 0; l < e->L.size(); l++) {
         EngLayer &L = e->L[l];
-        if (l == 0)
-            ENG_CHECK(sbk_rmsnorm(e->h, nullptr, nullptr, L.na, e->xn, 1, e->H, e->eps, s));
-        else
-            ENG_CHECK(sbk_rmsnorm(e->ob, e->h, e->h, L.na, e->xn, 1, e->H, e->eps, s));
-        if (run_groups(L.qkv, s, &n)) return fail("decode step: q/k/v matvec batch rejected");
-        ENG_CHECK(sbk_rope_kv_append(e->qkv, L.bias, L.qn, L.kn, L.kc, L.vc, pos, L.heads, L.kvh, L.hd, e->ctx,
-                                     L.theta, e->eps, L.neox, 1, s));
-        ENG_CHECK(sbk_attn_decode(e->qkv, L.kc, L.vc, e->att, pos, L.heads, L.kvh, L.hd, e->ctx, e->attn_ws, 1, s));
-        ENG_CHECK(sbk_matvec(L.o.dt, L.o.w, L.o.rows, L.o.cols, e->att, e->ob, 1, s));
-        ENG_CHECK(sbk_rmsnorm(e->ob, e->h, e->h, L.nf, e->xn, 1, e->H, e->eps, s));
-        if (run_groups(L.gu, s, &n)) return fail("decode step: gate/up matvec batch rejected");
-        ENG_CHECK(sbk_swiglu(e->gu, e->gu + L.ffn, e->act, L.ffn, 1, s));
-        ENG_CHECK(sbk_matvec(L.d.dt, L.d.w, L.d.rows, L.d.cols, e->act, e->ob, 1, s));
+        // attention block: h (+ previous down output) -> rmsnorm -> q|k|v
+        {
+            const sbk_xsrc xs{l ? e->ob : nullptr, L.na, l ? ho : nullptr, e->eps, SBK_XS_NORM};
+            const EngMat *ms[3] = {&L.q, &L.k, &L.v};
+            float *ys[3] = {e->qkv, e->qkv + L.qd, e->qkv + L.qd + L.kvd};
+            ENG_MV(ms, ys, 3, hc, xs);
+            if (l) std::swap(hc, ho);
+        }
+        ENG_CHECK(sbk_attn_rope_decode(e->qkv, L.bias, L.qn, L.kn, L.kc, L.vc, e->att, pos, L.heads, L.kvh, L.hd,
+                                       e->ctx, L.theta, e->eps, L.neox, e->attn_ws, 1, s));
+        {
+            const sbk_xsrc xs{nullptr, nullptr, nullptr, 0.0f, SBK_XS_PLAIN};
+            const EngMat *ms[1] = {&L.o};
+            float *ys[1] = {e->ob};
+            ENG_MV(ms, ys, 1, e->att, xs);
+        }
+        // FFN block: h + attention output -> rmsnorm -> gate|up; silu(gate) * up -> down
+        {
+            const sbk_xsrc xs{e->ob, L.nf, ho, e->eps, SBK_XS_NORM};
+            const EngMat *ms[2] = {&L.g, &L.u};
+            float *ys[2] = {e->gu, e->gu + L.ffn};
+            ENG_MV(ms, ys, 2, hc, xs);
+            std::swap(hc, ho);
+        }
+        {
+            const sbk_xsrc xs{e->gu + L.ffn, nullptr, nullptr, 0.0f, SBK_XS_SWIGLU};
+            const EngMat *ms[1] = {&L.d};
+            float *ys[1] = {e->ob};
+            ENG_MV(ms, ys, 1, e->gu, xs);
+        }
     }
-    ENG_CHECK(sbk_rmsnorm(e->ob, e->h, e->h, e->fnorm, e->xn, 1, e->H, e->eps, s));
-    ENG_CHECK(sbk_matvec(e->lm.dt, e->lm.w, e->V, e->H, e->xn, e->logits, 1, s));
+    {
+        const sbk_xsrc xs{e->ob, e->fnorm, nullptr, e->eps, SBK_XS_NORM};
+        const EngMat *ms[1] = {&e->lm};
+        float *ys[1] = {e->logits};
+        ENG_MV(ms, ys, 1, hc, xs);
+    }
     if (greedy) {
-        ENG_CHECK(sbk_argmax(e->logits, e->V, tok, e->am_ws, 1, s));
-        sb::advance_kernel<<<1, 32, 0, s>>>(pos, tok, e->prompt, np, e->hist, step);
-        if (cudaGetLastError() != cudaSuccess) return fail("decode step: advance launch failed");
-        n++;
+        ENG_CHECK(sb::argmax_launch(e->logits, e->V, tok, e->am_ws, 1, s, pos, step, e->hist, e->prompt, np));
     } else {
         const sb::KvRowsArgs a{(const uint16_t *const *)e->kv_meta,
                                (const uint16_t *const *)e->kv_meta + e->L.size(),
@@ -346,12 +376,12 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
     // activations (each padded to 64 floats)
     auto fbuf = [&](size_t n) { return (float *)e->dalloc(((n + 63) & ~(size_t)63) * 4, &err); };
     e->h = fbuf(H);
-    e->xn = fbuf(H);
+    e->h2 = fbuf(H);
     e->qkv = fbuf(e->qkv_max);
     e->att = fbuf(e->qkv_max);
     e->ob = fbuf(H);
     e->gu = fbuf(2 * e->ffn_max);
-    e->act = fbuf(e->ffn_max);
+    e->tmp = fbuf(std::max(e->ffn_max, std::max(H, e->qkv_max)));
     e->logits = fbuf(e->V);
     e->ints = (int *)e->dalloc(64, &err);
     e->prompt = (int *)e->dalloc(e->ctx * 4, &err);
@@ -374,14 +404,6 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         }
         if ((err = cudaMemcpy(e->kv_meta, m.data(), meta, cudaMemcpyHostToDevice)) != cudaSuccess)
             return bail(fail("cudaMemcpy(kv meta)", err));
-    }
-    for (size_t l = 0; l < nl; l++) {
-        EngLayer &L = e->L[l];
-        add_op(L.qkv, L.q, e->xn, e->qkv);
-        add_op(L.qkv, L.k, e->xn, e->qkv + L.qd);
-        add_op(L.qkv, L.v, e->xn, e->qkv + L.qd + L.kvd);
-        add_op(L.gu, L.g, e->xn, e->gu);
-        add_op(L.gu, L.u, e->xn, e->gu + L.ffn);
     }
     // zeroed state; one eager token of each kind (sets kernel attributes, creates the
     // per-stream matvec workspace outside any capture), then capture, then re-zero

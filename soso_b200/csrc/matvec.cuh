@@ -445,8 +445,10 @@ namespace sb {
 // `fallback`, a chunk the kernel does not take runs matrix by matrix through
 // sbk_matvec, else it is rejected (-5).
 template <class F>
-static int tc_matvec_batch(const sbk_mv_op *ops, size_t n, int pdl, cudaStream_t s, bool fallback)
+static int tc_matvec_batch(const sbk_mv_op *ops, size_t n, int pdl, cudaStream_t s, bool fallback,
+                           const tcmv::XSrc *xs = nullptr)
 {
+    if (xs && xs->mode != tcmv::XS_PLAIN) fallback = false;  // the CUDA-core kernel has no fused input forms
     const int grid = num_sms_cached();
     for (size_t i0 = 0; i0 < n; i0 += tcmv::MAXB) {
         const size_t nb = n - i0 < (size_t)tcmv::MAXB ? n - i0 : (size_t)tcmv::MAXB;
@@ -463,7 +465,7 @@ static int tc_matvec_batch(const sbk_mv_op *ops, size_t n, int pdl, cudaStream_t
         if (ok && tcmv::fits<F>(mo, (int)nb, grid)) {
             void *ws = stream_ws(s, tcmv::ws_bytes(grid));
             if (!ws) return -3;
-            const int rc = tcmv::launch_batch<F>(mo, (int)nb, ws, grid, pdl, s);
+            const int rc = tcmv::launch_batch<F>(mo, (int)nb, ws, grid, pdl, s, xs);
             if (rc) return rc;
         } else if (fallback) {
             for (size_t i = 0; i < nb; i++) {
@@ -508,6 +510,17 @@ extern "C" int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, i
         if (rc) return rc;
     }
     return 0;
+}
+
+extern "C" int sbk_matvec_batch_x(uint8_t dtype, const sbk_mv_op *ops, size_t n, const sbk_xsrc *xs, int pdl,
+                                  void *stream)
+{
+    if (!ops || n == 0 || !xs) return -1;
+    const sb::tcmv::XSrc x{xs->res, xs->norm_w, xs->h_out, xs->eps, xs->mode};
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dtype == SB_DTYPE_Q4_K) return sb::tc_matvec_batch<sb::tcmv::Q4K>(ops, n, pdl, s, true, &x);
+    if (dtype == SB_DTYPE_Q6_K_P) return sb::tc_matvec_batch<sb::tcmv::Q6KP>(ops, n, pdl, s, false, &x);
+    return -5;
 }
 
 extern "C" int sbk_q6k_pack(const void *src, size_t rows, size_t cols, void *dst, void *stream)

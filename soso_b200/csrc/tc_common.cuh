@@ -54,13 +54,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity)
     return false;
 }
 
+// L2 policy for streamed weights: each byte is read once per token, so let it be
+// the first to go and keep activations, KV rows and code resident in L2.
+__device__ __forceinline__ uint64_t l2_evict_first()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // 2-D tiled TMA load (no multicast): box at element coords (x = u64 column, y = row).
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
+                                            uint64_t policy)
 {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];" ::"r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+        "[%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
 
@@ -128,6 +138,50 @@ __device__ __forceinline__ uint32_t prmt_b32(uint32_t a, uint32_t b, uint32_t se
 }
 
 __device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
+
+// How the input vector of the matvecs of one launch is formed while it is prepared,
+// so that the step producing it needs no launch of its own.  With a = the matrix's x:
+//   XS_PLAIN   x = a
+//   XS_NORM    h = a (+ b when b is set: the residual add, gemm.rs:265-290),
+//              x = h * (1 / sqrtf(sum(h^2) / n + eps)) * w   (gemm::rmsnorm, gemm.rs:93-100);
+//              CTA 0 also stores h to h_out when set (the new residual stream; h_out
+//              must not alias a or b, which other CTAs are still reading)
+//   XS_SWIGLU  x = silu(a) * b, silu(v) = v / (1 + expf(-v))  (gemm.rs:210-226; a = gate, b = up)
+enum { XS_PLAIN = 0, XS_NORM = 1, XS_SWIGLU = 2 };
+
+struct XSrc {
+    const float *b;
+    const float *w;
+    float *h_out;
+    float eps;
+    int mode;
+};
+
+// Element loader of the preparation: float4 i of the (transformed) input vector.
+struct XLoad {
+    const float4 *a, *b, *w;
+    float scale;
+    int mode;
+    __device__ __forceinline__ float4 operator()(int i) const
+    {
+        float4 v = a[i];
+        if (mode == XS_NORM) {
+            if (b) {
+                const float4 r = b[i];
+                v.x += r.x, v.y += r.y, v.z += r.z, v.w += r.w;
+            }
+            const float4 g = w[i];
+            v.x = v.x * scale * g.x, v.y = v.y * scale * g.y, v.z = v.z * scale * g.z, v.w = v.w * scale * g.w;
+        } else if (mode == XS_SWIGLU) {
+            const float4 u = b[i];
+            v.x = v.x / (1.0f + expf(-v.x)) * u.x;
+            v.y = v.y / (1.0f + expf(-v.y)) * u.y;
+            v.z = v.z / (1.0f + expf(-v.z)) * u.z;
+            v.w = v.w / (1.0f + expf(-v.w)) * u.w;
+        }
+        return v;
+    }
+};
 
 }  // namespace tcmv
 }  // namespace sb

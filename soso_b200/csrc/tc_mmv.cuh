@@ -44,8 +44,11 @@ struct __align__(64) MatDesc {
 
 struct Batch {
     MatDesc d[MAXB];
+    XSrc xs;                   // how every matrix's x is formed (tc_common.cuh)
     int n, total;              // matrices, stages
     int max_cols, max_groups;  // shared-memory capacities (prep, partial table)
+    int split_groups;          // 1: CTAs take whole 16-row groups (no cut groups, no fix-up)
+    int total_groups;
 };
 
 template <class F>
@@ -54,6 +57,7 @@ struct Smem {
     uint8_t *prep;    // F::prep_bytes(max_cols)
     uint8_t *zero;    // 64 B of zeros: the B fragment of lanes that carry no x
     float *part;      // [groups of this CTA][NCW][16]
+    float *red;       // [64]: the sum of squares of an XS_NORM input, per consumer warp
     uint64_t *full;   // [NSLOT]
     uint64_t *empty;  // [NSLOT]
 };
@@ -61,7 +65,7 @@ struct Smem {
 template <class F>
 __host__ __device__ inline size_t smem_bytes(int max_cols, int max_groups)
 {
-    return (size_t)F::NSLOT * F::SLOTB + F::prep_bytes(max_cols) + 64 + (size_t)max_groups * F::NCW * 64 +
+    return (size_t)F::NSLOT * F::SLOTB + F::prep_bytes(max_cols) + 64 + (size_t)max_groups * F::NCW * 64 + 256 +
            2 * F::NSLOT * 8 + 64;
 }
 
@@ -78,10 +82,21 @@ __device__ __forceinline__ Smem<F> carve(uint8_t *base, int max_cols, int max_gr
     o += 64;
     s.part = reinterpret_cast<float *>(base + o);
     o += (size_t)max_groups * F::NCW * 64;
+    s.red = reinterpret_cast<float *>(base + o);
+    o += 256;
     o = (o + 7) & ~(size_t)7;
     s.full = reinterpret_cast<uint64_t *>(base + o);
     s.empty = s.full + F::NSLOT;
     return s;
+}
+
+// First stage of 16-row group g of the batch (groups numbered across matrices).
+__device__ __forceinline__ int stage_of_group(const Batch &B, int g)
+{
+    if (g >= B.total_groups) return B.total;
+    int i = 0;
+    while (i + 1 < B.n && B.d[i + 1].cnt_off <= g) i++;
+    return B.d[i].st_begin + (g - B.d[i].cnt_off) * B.d[i].spg;
 }
 
 // inverse of row_strip: which of n parts holds `unit`
@@ -100,7 +115,14 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<F> s = carve<F>(smem_raw, B.max_cols, B.max_groups);
     int st0, st1;
-    row_strip(B.total, blockIdx.x, gridDim.x, st0, st1);
+    if (B.split_groups) {
+        int g0, g1;
+        row_strip(B.total_groups, blockIdx.x, gridDim.x, g0, g1);
+        st0 = stage_of_group(B, g0);
+        st1 = stage_of_group(B, g1);
+    } else {
+        row_strip(B.total, blockIdx.x, gridDim.x, st0, st1);
+    }
     const int nst = st1 - st0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // matrices touched: m_first .. m_last
@@ -129,6 +151,7 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
         if (lane == 0 && nst > 0) {
             int mi = m_first, slot = 0;
             unsigned phase = 0;  // parity of the empty-barrier phase to wait for
+            const uint64_t pol = l2_evict_first();
             const MatDesc *d = &B.d[mi];
             int ls = st0 - d->st_begin, G = ls / d->spg, j = ls - G * d->spg;
             int mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
@@ -145,7 +168,7 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
                     break;
                 }
                 mbar_expect_tx_arrive(&s.full[slot], (unsigned)F::SLOTB);  // full box, zero-filled past the ends
-                tma_load_2d(s.ring + slot * F::SLOTB, &d->map, F::stage_x(j), G * 16, &s.full[slot]);
+                tma_load_2d(s.ring + slot * F::SLOTB, &d->map, F::stage_x(j), G * 16, &s.full[slot], pol);
                 if (++j == d->spg) j = 0, G++;
                 if (++slot == NSLOT) {
                     slot = 0;
@@ -161,6 +184,8 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
         const int team = cwg / F::NCONS, cw = cwg % F::NCONS, g = lane >> 2, t = lane & 3;
         const typename F::Lane L = F::lane_setup(g, t);
         griddep_wait();  // x of every matrix is written by the previous kernel
+        const float *prev_x = nullptr;
+        int prev_cols = 0;
         for (int mi = m_first; mi <= m_last && nst > 0; mi++) {
             const MatDesc &d = B.d[mi];
             const int nb = d.cols / 256, spg = d.spg;
@@ -168,8 +193,35 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
             const int ka = max(st0, d.st_begin) - st0, kb = min(st1, d.st_begin + mtot) - st0;  // CTA-local stages
             const int gs0 = (ka + st0 - d.st_begin) / spg, gs1 = (kb - 1 + st0 - d.st_begin) / spg;
             const int ng = gs1 - gs0 + 1;
-            // x -> prep and a clean partial table for this segment
-            F::prep_x(d.x, d.cols, s.prep, cwg);
+            // x -> prep (unless the previous segment prepared the same x) and a clean
+            // partial table for this segment
+            if (d.x != prev_x || d.cols != prev_cols) {
+                XLoad X{reinterpret_cast<const float4 *>(d.x), reinterpret_cast<const float4 *>(B.xs.b),
+                        reinterpret_cast<const float4 *>(B.xs.w), 1.0f, B.xs.mode};
+                if (B.xs.mode == XS_NORM) {
+                    // sum of squares of h = a (+ b), fixed order; CTA 0 stores h
+                    float ss = 0.0f;
+                    float4 *ho = blockIdx.x == 0 ? reinterpret_cast<float4 *>(B.xs.h_out) : nullptr;
+                    for (int i = cwg * 32 + lane; i < d.cols / 4; i += NCW * 32) {
+                        float4 v = X.a[i];
+                        if (X.b) {
+                            const float4 r = X.b[i];
+                            v.x += r.x, v.y += r.y, v.z += r.z, v.w += r.w;
+                        }
+                        if (ho) ho[i] = v;
+                        ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+                    }
+                    ss = warp_sum(ss);
+                    if (lane == 0) s.red[cwg] = ss;
+                    asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+                    float tot = 0.0f;
+                    for (int w = 0; w < NCW; w++) tot += s.red[w];
+                    X.scale = 1.0f / sqrtf(tot / (float)d.cols + B.xs.eps);
+                }
+                F::prep_x(X, d.cols, s.prep, cwg);
+                prev_x = d.x;
+                prev_cols = d.cols;
+            }
             for (int i = cwg * 32 + lane; i < ng * NCW * 16; i += NCW * 32) s.part[i] = 0.0f;
             asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
             const typename F::Seg S = F::seg_setup(L, s.prep, s.zero, nb);
@@ -415,8 +467,28 @@ inline bool fits(const MatOp *ops, int n, int grid)
 // Launch a batch of up to MAXB independent matvecs of format F on `stream`, with
 // the scratch given as counter / partial pointers (counters zero on entry, left
 // zero); at most cnt_cap 16-row groups in the batch.
+// Stages of the busiest CTA when whole groups are split evenly over `grid` CTAs.
+inline int group_split_max(const Batch &b, int grid)
+{
+    int mx = 0;
+    auto stage_of = [&](int g) {
+        if (g >= b.total_groups) return b.total;
+        int i = 0;
+        while (i + 1 < b.n && b.d[i + 1].cnt_off <= g) i++;
+        return b.d[i].st_begin + (g - b.d[i].cnt_off) * b.d[i].spg;
+    };
+    for (int c = 0; c < grid; c++) {
+        const int base = b.total_groups / grid, rem = b.total_groups % grid;
+        const int g0 = c * base + (c < rem ? c : rem), g1 = g0 + base + (c < rem ? 1 : 0);
+        const int st = stage_of(g1) - stage_of(g0);
+        mx = st > mx ? st : mx;
+    }
+    return mx;
+}
+
 template <class F>
-inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int grid, int pdl, cudaStream_t stream)
+inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int grid, int pdl, cudaStream_t stream,
+                           const XSrc *xs = nullptr)
 {
     if (n < 1 || n > MAXB) return -1;
     static Batch b;  // large: built host-side, passed by value as the kernel parameter
@@ -442,7 +514,30 @@ inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int gri
     if (cnt > cnt_cap) return -1;
     b.n = n;
     b.total = st;
-    const size_t smem = batch_smem<F>(ops, n, grid, &b.max_cols, &b.max_groups);
+    b.total_groups = cnt;
+    b.xs = xs ? *xs : XSrc{nullptr, nullptr, nullptr, 0.0f, XS_PLAIN};
+    if (b.xs.mode != XS_PLAIN) {
+        // one input vector for the whole batch (h_out is written once, from it)
+        for (int i = 1; i < n; i++)
+            if (ops[i].x != ops[0].x || ops[i].cols != ops[0].cols) return -1;
+        if ((b.xs.mode == XS_NORM && !b.xs.w) || (b.xs.mode == XS_SWIGLU && !b.xs.b)) return -1;
+        if (b.xs.mode != XS_NORM && b.xs.mode != XS_SWIGLU) return -1;
+        if (((uintptr_t)b.xs.b | (uintptr_t)b.xs.w | (uintptr_t)b.xs.h_out) & 15) return -2;
+    }
+    // Whole groups per CTA when that costs at most one stage more on the busiest CTA
+    // and the stream-K split is short (latency-bound): no cross-CTA fix-up at all.
+    const int smax = (st + grid - 1) / grid, gmax = group_split_max(b, grid);
+    b.split_groups = gmax <= smax || (gmax <= smax + 1 && smax <= 4);
+    size_t smem = batch_smem<F>(ops, n, grid, &b.max_cols, &b.max_groups);
+    if (b.split_groups) {
+        const int need = (cnt + grid - 1) / grid + 1;
+        if (need > b.max_groups && smem_bytes<F>(b.max_cols, need) <= 227 * 1024) {
+            b.max_groups = need;
+            smem = smem_bytes<F>(b.max_cols, need);
+        } else if (need > b.max_groups) {
+            b.split_groups = 0;
+        }
+    }
     if (smem > 227 * 1024) return -5;
     // the kernel's dynamic shared-memory limit only ever grows (one record per device)
     static size_t smem_set[64];
@@ -470,13 +565,14 @@ inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int gri
 
 // As launch_batch_ws over a workspace of ws_bytes(grid) bytes.
 template <class F>
-inline int launch_batch(const MatOp *ops, int n, void *ws, int grid, int pdl, cudaStream_t stream)
+inline int launch_batch(const MatOp *ops, int n, void *ws, int grid, int pdl, cudaStream_t stream,
+                        const XSrc *xs = nullptr)
 {
     uint8_t *wsb = reinterpret_cast<uint8_t *>(ws);
     Ws wsd;
     wsd.cnt = reinterpret_cast<unsigned *>(wsb);
     wsd.part = reinterpret_cast<float *>(wsb + ws_part_off());
-    return launch_batch_ws<F>(ops, n, wsd, CNT_MAX, grid, pdl, stream);
+    return launch_batch_ws<F>(ops, n, wsd, CNT_MAX, grid, pdl, stream, xs);
 }
 
 // Repack GGML Q6_K rows (reference layout) into the packed layout of tc_q6k.cuh.

@@ -47,7 +47,7 @@ struct Q4K {
     static constexpr int BOXW = SBLK * 18;  // u64 per box row (576 B)
     static constexpr int ROWB = BOXW * 8;
     static constexpr int SLOTB = 16 * ROWB;
-    static constexpr int MAX_COLS = 8192;
+    static constexpr int MAX_COLS = 16384;
 
     __host__ __device__ static size_t row_bytes(int cols) { return (size_t)(cols / 256) * 144; }
     __host__ __device__ static int stage_x(int j) { return j * SBLK * 18; }  // u64 column of stage j
@@ -68,15 +68,14 @@ struct Q4K {
     // 4l..4l+3 and 128+4l..128+4l+3.  Element e of sub-block s, piece p, goes to
     // live lane L = 2(4*((s>>1)&1) + p) + (e>>4), register
     // 4*(2*(s>>2) + (s&1)) + 2*((e>>3)&1) + ((e>>2)&1), byte e&3.
-    __device__ static void prep_x(const float *__restrict__ x, int cols, uint8_t *prep, int cw)
+    __device__ static void prep_x(const XLoad &X, int cols, uint8_t *prep, int cw)
     {
         const int nb = cols / 256, l = threadIdx.x & 31;
         uint32_t *frag = reinterpret_cast<uint32_t *>(prep);
         unsigned short *mfr = reinterpret_cast<unsigned short *>(prep + (size_t)nb * 1024);
         float *fx = reinterpret_cast<float *>(prep + (size_t)nb * 1056), *fm = fx + nb;
-        const float4 *x4 = reinterpret_cast<const float4 *>(x);
         for (int b = cw; b < nb; b += NCW) {
-            const float4 va = x4[b * 64 + l], vb = x4[b * 64 + 32 + l];
+            const float4 va = X(b * 64 + l), vb = X(b * 64 + 32 + l);
             const float mx = fmaxf(fmaxf(fmaxf(fabsf(va.x), fabsf(va.y)), fmaxf(fabsf(va.z), fabsf(va.w))),
                                    fmaxf(fmaxf(fabsf(vb.x), fabsf(vb.y)), fmaxf(fabsf(vb.z), fabsf(vb.w))));
             float sa = (va.x + va.y) + (va.z + va.w), sbv = (vb.x + vb.y) + (vb.z + vb.w);
