@@ -216,6 +216,13 @@ typedef struct {
     float *h_out;
     float eps;
     int mode;
+    /* SBK_XS_NORM after a MoE FFN: with ny > 0 the residual is a weighted set of
+     * vectors, h = (sum over i = 0..ny-1, in order, of yw[i] * ys[i*ystride ..]) + a
+     * (the expert combine of layer.rs:1922-1933, then add_assign_f32 :1389); res unused.
+     * ny <= 16; yw is read on the device (it may be written by an earlier kernel). */
+    const float *ys;
+    const float *yw;
+    int ny, ystride;
 } sbk_xsrc;
 /* sbk_matvec_batch with the input formed as *xs says (dtype Q4_K or Q6_K_P; 16-byte
  * aligned vectors).  Returns -5 for a dtype without the fused input forms. */

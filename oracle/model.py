@@ -24,7 +24,7 @@ class DenseOracle:
         self._embd = None
 
     def _mv(self, name: str, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
-        dt = self.cfg.dtypes[name.split(".")[-1]]
+        dt = self.cfg.dtypes[name.split(".")[-1]]  # by tensor kind (experts share their kind's dtype)
         return oracle.matvec(dt, self.m[name], rows, cols, x)
 
     def embed(self, token: int) -> np.ndarray:
@@ -68,8 +68,11 @@ class DenseOracle:
                 for i in range(cfg.heads)])
             o = self._mv(p + "attn_output", att, H, qd)
             h = (h + o).astype(np.float32)  # add_f32 (layer.rs:1296)
-            # dense FFN (layer.rs:1300-1389)
             xn = oracle.rmsnorm(h, m[p + "ffn_norm"], cfg.eps)
+            if getattr(cfg, "n_exp", 0) and l >= cfg.first_moe:
+                h = (self._moe(p, xn, l) + h).astype(np.float32)  # hidden = moe_acc; += residual (:1389)
+                continue
+            # dense FFN (layer.rs:1300-1389)
             gate = self._mv(p + "ffn_gate", xn, cfg.ffn, H)
             up = self._mv(p + "ffn_up", xn, cfg.ffn, H)
             act = oracle.swiglu(up, gate)
@@ -78,6 +81,34 @@ class DenseOracle:
         # logits (runtime.rs:1976-2019)
         hn = oracle.rmsnorm(h, m["output_norm"], cfg.eps)
         return self._mv("output", hn, cfg.vocab, H)
+
+    def _moe(self, p: str, xn: np.ndarray, l: int) -> np.ndarray:
+        """forward_moe_ffn / moe_expertos_agrupados (layer.rs:1938-1972, :1862-1935): router
+        logits, topk_softmax (gemm.rs:62-91), per chosen expert down(swiglu(up, gate)) summed
+        in rank order with its weight, then the shared expert weighted by
+        sigmoid(ffn_gate_inp_shexp . xn) (or 1)."""
+        cfg, m, H = self.cfg, self.m, self.cfg.hidden
+        logits = self._mv(p + "ffn_gate_inp", xn, cfg.n_exp, H)
+        self.last_route = oracle.topk_softmax(logits, cfg.top_k)
+        idx, wts = self.last_route
+        acc = np.zeros(H, np.float32)
+        for e, w in zip(idx, wts):
+            q = f"{p}E{int(e):03d}."
+            gate = self._mv(q + "ffn_gate", xn, cfg.moe_ffn, H)
+            up = self._mv(q + "ffn_up", xn, cfg.moe_ffn, H)
+            down = self._mv(q + "ffn_down", oracle.swiglu(up, gate), H, cfg.moe_ffn)
+            acc = (acc + down * np.float32(w)).astype(np.float32)
+        if cfg.shared_ffn:
+            q = f"{p}S00."
+            gate = self._mv(q + "ffn_gate", xn, cfg.shared_ffn, H)
+            up = self._mv(q + "ffn_up", xn, cfg.shared_ffn, H)
+            down = self._mv(q + "ffn_down", oracle.swiglu(up, gate), H, cfg.shared_ffn)
+            pg = np.float32(1.0)
+            if cfg.shared_gate:
+                d = np.float32(np.dot(m[p + "ffn_gate_inp_shexp"].astype(np.float64), xn.astype(np.float64)))
+                pg = np.float32(1.0 / (1.0 + np.exp(-np.float64(d))))
+            acc = (acc + down * pg).astype(np.float32)
+        return acc
 
     def greedy(self, prompt, n: int) -> tuple[np.ndarray, list]:
         """n steps from position 0: prompt tokens first, then argmax (runtime.rs:2021-2028)."""

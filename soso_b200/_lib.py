@@ -32,7 +32,8 @@ class SbkMvOp(ctypes.Structure):
 class SbkXSrc(ctypes.Structure):
     """sbk_xsrc: how a fused batch forms its input (mode SBK_XS_PLAIN 0 / NORM 1 / SWIGLU 2)."""
     _fields_ = [("res", ctypes.c_void_p), ("norm_w", ctypes.c_void_p), ("h_out", ctypes.c_void_p),
-                ("eps", ctypes.c_float), ("mode", ctypes.c_int)]
+                ("eps", ctypes.c_float), ("mode", ctypes.c_int), ("ys", ctypes.c_void_p), ("yw", ctypes.c_void_p),
+                ("ny", ctypes.c_int), ("ystride", ctypes.c_int)]
 
 
 class SbStats(ctypes.Structure):

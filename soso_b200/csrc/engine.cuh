@@ -79,6 +79,106 @@ __global__ void kv_rows_kernel(KvRowsArgs a)
     }
 }
 
+// MoE routing of one token on the device, between the router matvec and the expert
+// matvecs: softmax over all experts, stable top-k by weight, renormalised
+// (gemm::topk_softmax, crates/soso-llm-core/src/gemm.rs:62-91, as router_topk_kernel),
+// the shared expert's weight sigmoid(gate_row . x) or 1 (layer.rs:1883-1907), and the
+// expert choice written into the device-side batches of the two expert launches
+// (their matrices point at the chosen experts' tensor maps).  One CTA.
+struct RouteArgs {
+    const float *logits;
+    int n_exp, k;
+    int *idx;
+    float *wts;             // [k] routed weights, then the shared expert's weight
+    const float *sg_row;    // shared expert gate row [H], or null (weight 1)
+    const float *h;         // residual stream after attention (x = rmsnorm(h) * nw)
+    const float *nw;
+    float eps;
+    int H, has_shared;
+    tcmv::Batch *gu, *dn;   // gu.d[2i] / d[2i+1] = gate / up of choice i; dn.d[i] = its down
+    const CUtensorMap *maps;  // [n_exp][3]: gate, up, down
+};
+
+__global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
+{
+    __shared__ float p[1024];
+    __shared__ float red[32];
+    __shared__ float topw[64];
+    __shared__ int topi[64];
+    griddep_wait();
+    const int tid = threadIdx.x, n = a.n_exp;
+    float m = -INFINITY;
+    for (int i = tid; i < n; i += blockDim.x) m = fmaxf(m, a.logits[i]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    m = -INFINITY;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int i = tid; i < n; i += blockDim.x) {
+        p[i] = expf(a.logits[i] - m);
+        sum += p[i];
+    }
+    sum = warp_sum(sum);
+    if ((tid & 31) == 0) red[tid >> 5] = sum;
+    __syncthreads();
+    sum = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) sum += red[w];
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x)
+        if (sum > 0.0f) p[i] = p[i] / sum;
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) {
+        const float v = p[i];
+        int r = 0;
+        for (int j = 0; j < n; j++) {
+            const float u = p[j];
+            r += (u > v) || (u == v && j < i);
+        }
+        if (r < a.k) topi[r] = i, topw[r] = v;
+    }
+    // shared expert gate: sigmoid(row . rmsnorm(h) * nw), the dot in warp 0
+    float sg = 1.0f;
+    if (a.has_shared && a.sg_row) {
+        float ss = 0.0f, dot = 0.0f;
+        for (int i = tid; i < a.H; i += blockDim.x) ss += a.h[i] * a.h[i];
+        ss = warp_sum(ss);
+        __syncthreads();
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        ss = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) ss += red[w];
+        const float scale = 1.0f / sqrtf(ss / (float)a.H + a.eps);
+        __syncthreads();
+        for (int i = tid; i < a.H; i += blockDim.x) dot += a.sg_row[i] * (a.h[i] * scale * a.nw[i]);
+        dot = warp_sum(dot);
+        if ((tid & 31) == 0) red[tid >> 5] = dot;
+        __syncthreads();
+        dot = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) dot += red[w];
+        sg = 1.0f / (1.0f + expf(-dot));
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.0f;
+        for (int r = 0; r < a.k; r++) t += topw[r];
+        for (int r = 0; r < a.k; r++) {
+            a.wts[r] = t > 0.0f ? topw[r] / t : topw[r];
+            a.idx[r] = topi[r];
+        }
+        if (a.has_shared) a.wts[a.k] = sg;
+    }
+    if (tid < a.k) {
+        const int e = topi[tid];
+        a.gu->d[2 * tid].mapp = a.maps + 3 * e;
+        a.gu->d[2 * tid + 1].mapp = a.maps + 3 * e + 1;
+        a.dn->d[tid].mapp = a.maps + 3 * e + 2;
+    }
+    griddep_launch();
+}
+
 }  // namespace sb
 
 extern "C" int sbk_swiglu(const float *gate, const float *up, float *out, size_t n, int pdl, void *stream)
@@ -112,6 +212,17 @@ struct EngLayer {
     int neox = 0;
     float *qn = nullptr, *kn = nullptr, *bias = nullptr, *na = nullptr, *nf = nullptr;
     uint16_t *kc = nullptr, *vc = nullptr;
+    // MoE FFN (sb_moe_plan): router, n_exp experts (gate, up, down), optional shared expert
+    bool moe = false, has_sh = false;
+    size_t n_exp = 0, top_k = 0, effn = 0, sffn = 0;
+    EngMat router, sh[3];
+    std::vector<EngMat> ex;            // [n_exp][3]
+    float *sg = nullptr;               // shared expert gate row, or null (weight 1)
+    CUtensorMap *maps = nullptr;       // device [n_exp][3]: the experts' tensor maps
+    sb::tcmv::Batch *gu_b = nullptr;   // device batches of the two expert launches (built on
+    sb::tcmv::Batch *dn_b = nullptr;   //   the first enqueue; the route kernel picks the maps)
+    size_t gu_smem = 0, dn_smem = 0;
+    const float *built_for = nullptr;  // residual buffer the batches read
 };
 
 }  // namespace
@@ -124,6 +235,10 @@ struct sb_engine {
     float *fnorm = nullptr;
     float *h = nullptr, *h2 = nullptr, *tmp = nullptr, *qkv = nullptr, *att = nullptr, *ob = nullptr, *gu = nullptr,
           *logits = nullptr;
+    // MoE: router logits, chosen experts and weights, gate|up per choice, down outputs per choice
+    float *rlog = nullptr, *wts = nullptr, *egu = nullptr, *ys = nullptr;
+    int *ridx = nullptr;
+    size_t moe_slots = 0, moe_ffn = 0, n_exp_max = 0;
     int *ints = nullptr;  // pos, tok, step, n_prompt
     int *prompt = nullptr, *hist = nullptr;
     void *attn_ws = nullptr, *am_ws = nullptr;
@@ -201,6 +316,7 @@ int run_mv(sb_engine *e, const EngMat *const *ms, float *const *ys, int n, const
             rc = xs.mode == SBK_XS_PLAIN ? sbk_matvec_batch(dt, ops, k, 1, s) : sbk_matvec_batch_x(dt, ops, k, &xs, 1, s);
         } else {
             const size_t cols = ops[0].cols;
+            if (xs.ny) return -5;  // the weighted residual set exists only in the fused form
             if (xs.mode == SBK_XS_NORM)
                 rc = sbk_rmsnorm(a, xs.res, xs.res ? xs.h_out : nullptr, xs.norm_w, e->tmp, 1, cols, xs.eps, s);
             else
@@ -213,6 +329,87 @@ int run_mv(sb_engine *e, const EngMat *const *ms, float *const *ys, int n, const
         if (rc) return rc;
         *launches += 1;
     }
+    return 0;
+}
+
+// Build (once, eagerly, outside any capture) the two device-side batches of a MoE layer:
+// gate|up of every choice (input rmsnorm(hc) * ffn_norm) and their downs (input
+// silu(gate) * up per choice), plus the shared expert last.  Matrices of routed choices
+// start out pointing at expert 0; route_kernel points them at the chosen experts.
+template <class FG, class FD>
+int build_moe_batches(sb_engine *e, EngLayer &L, const float *hc)
+{
+    using namespace sb::tcmv;
+    const int grid = sb::num_sms_cached();
+    const int k = (int)L.top_k, ns = k + (L.has_sh ? 1 : 0);
+    MatOpX gu[MAXB], dn[MAXB];
+    for (int i = 0; i < ns; i++) {
+        const bool shared = i == k;
+        const EngMat &g = shared ? L.sh[0] : L.ex[0], &u = shared ? L.sh[1] : L.ex[1], &d = shared ? L.sh[2] : L.ex[2];
+        float *gi = e->egu + (size_t)(2 * i) * e->moe_ffn, *ui = e->egu + (size_t)(2 * i + 1) * e->moe_ffn;
+        gu[2 * i] = MatOpX{MatOp{g.w, (int)g.rows, (int)g.cols, hc, gi}, nullptr, nullptr};
+        gu[2 * i + 1] = MatOpX{MatOp{u.w, (int)u.rows, (int)u.cols, hc, ui}, nullptr, nullptr};
+        dn[i] = MatOpX{MatOp{d.w, (int)d.rows, (int)d.cols, gi, e->ys + (size_t)i * e->H}, ui, nullptr};
+    }
+    XSrc xg{};
+    xg.w = L.nf, xg.eps = e->eps, xg.mode = XS_NORM;
+    XSrc xd{};
+    xd.mode = XS_SWIGLU;
+    Batch hb;
+    memset(&hb, 0, sizeof(hb));
+    cudaError_t err;
+    int rc = build_batch<FG>(gu, 2 * ns, CNT_MAX, grid, &xg, &hb, &L.gu_smem);
+    if (rc) return fail("decode plan: expert gate/up batch rejected (" + std::to_string(rc) + ")");
+    if (!L.gu_b && !(L.gu_b = (Batch *)e->dalloc(sizeof(Batch), &err))) return fail("cudaMalloc(batch)", err);
+    if ((err = cudaMemcpy(L.gu_b, &hb, sizeof(Batch), cudaMemcpyHostToDevice)) != cudaSuccess)
+        return fail("cudaMemcpy(batch)", err);
+    memset(&hb, 0, sizeof(hb));
+    rc = build_batch<FD>(dn, ns, CNT_MAX, grid, &xd, &hb, &L.dn_smem);
+    if (rc) return fail("decode plan: expert down batch rejected (" + std::to_string(rc) + ")");
+    if (!L.dn_b && !(L.dn_b = (Batch *)e->dalloc(sizeof(Batch), &err))) return fail("cudaMalloc(batch)", err);
+    if ((err = cudaMemcpy(L.dn_b, &hb, sizeof(Batch), cudaMemcpyHostToDevice)) != cudaSuccess)
+        return fail("cudaMemcpy(batch)", err);
+    L.built_for = hc;
+    return 0;
+}
+
+template <class F>
+int launch_moe_batch(sb::tcmv::Batch *b, size_t smem, cudaStream_t s)
+{
+    using namespace sb::tcmv;
+    const int grid = sb::num_sms_cached();
+    void *ws = sb::stream_ws(s, ws_bytes(grid));
+    if (!ws) return -3;
+    Ws w;
+    w.cnt = reinterpret_cast<unsigned *>(ws);
+    w.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + ws_part_off());
+    return launch_dev_batch<F>(b, smem, w, grid, 1, s);
+}
+
+int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, bool build, size_t *n)
+{
+    const uint8_t gdt = L.ex[0].dt, ddt = L.ex[2].dt;
+    int rc = 0;
+    if (build) {
+        if (gdt == SB_DTYPE_Q4_K && ddt == SB_DTYPE_Q4_K) rc = build_moe_batches<sb::tcmv::Q4K, sb::tcmv::Q4K>(e, L, hc);
+        else if (gdt == SB_DTYPE_Q4_K && ddt == SB_DTYPE_Q6_K_P) rc = build_moe_batches<sb::tcmv::Q4K, sb::tcmv::Q6KP>(e, L, hc);
+        else if (gdt == SB_DTYPE_Q6_K_P && ddt == SB_DTYPE_Q6_K_P) rc = build_moe_batches<sb::tcmv::Q6KP, sb::tcmv::Q6KP>(e, L, hc);
+        else if (gdt == SB_DTYPE_Q6_K_P && ddt == SB_DTYPE_Q4_K) rc = build_moe_batches<sb::tcmv::Q6KP, sb::tcmv::Q4K>(e, L, hc);
+        else return fail("decode plan: expert dtypes without a tensor-core kernel");
+        if (rc) return rc;
+    }
+    sb::RouteArgs ra{e->rlog, (int)L.n_exp, (int)L.top_k, e->ridx, e->wts, L.sg, hc, L.nf, e->eps, (int)e->H,
+                     L.has_sh ? 1 : 0, L.gu_b, L.dn_b, L.maps};
+    if ((rc = sb::launch_k(sb::route_kernel, dim3(1), dim3(256), 0, 1, s, ra))) return rc;
+    *n += 1;
+    rc = gdt == SB_DTYPE_Q4_K ? launch_moe_batch<sb::tcmv::Q4K>(L.gu_b, L.gu_smem, s)
+                              : launch_moe_batch<sb::tcmv::Q6KP>(L.gu_b, L.gu_smem, s);
+    if (rc) return rc;
+    *n += 1;
+    rc = ddt == SB_DTYPE_Q4_K ? launch_moe_batch<sb::tcmv::Q4K>(L.dn_b, L.dn_smem, s)
+                              : launch_moe_batch<sb::tcmv::Q6KP>(L.dn_b, L.dn_smem, s);
+    if (rc) return rc;
+    *n += 1;
     return 0;
 }
 
@@ -236,41 +433,67 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
     int *pos = e->ints, *tok = e->ints + 1, *step = e->ints + 2, *np = e->ints + 3;
     float *hc = e->h, *ho = e->h2;  // residual stream: current / the other buffer
     if (greedy) ENG_CHECK(sbk_embed_row(e->emb.w, e->emb.dt, e->V, e->H, tok, e->h, 1, s));
+    int moe_ny = 0;  // > 0: the last FFN was MoE; its result is the weighted set ys / wts
+    auto norm_src = [&](const float *w, float *h_out) {
+        sbk_xsrc xs{};
+        xs.norm_w = w, xs.h_out = h_out, xs.eps = e->eps, xs.mode = SBK_XS_NORM;
+        if (moe_ny) xs.ys = e->ys, xs.yw = e->wts, xs.ny = moe_ny, xs.ystride = (int)e->H;
+        else xs.res = e->ob;
+        return xs;
+    };
     for (size_t l = 0; l < e->L.size(); l++) {
         EngLayer &L = e->L[l];
-        // attention block: h (+ previous down output) -> rmsnorm -> q|k|v
+        // attention block: h (+ previous FFN output) -> rmsnorm -> q|k|v
         {
-            const sbk_xsrc xs{l ? e->ob : nullptr, L.na, l ? ho : nullptr, e->eps, SBK_XS_NORM};
+            sbk_xsrc xs = norm_src(L.na, l ? ho : nullptr);
+            if (!l) xs.res = nullptr;
             const EngMat *ms[3] = {&L.q, &L.k, &L.v};
             float *ys[3] = {e->qkv, e->qkv + L.qd, e->qkv + L.qd + L.kvd};
             ENG_MV(ms, ys, 3, hc, xs);
             if (l) std::swap(hc, ho);
+            moe_ny = 0;
         }
         ENG_CHECK(sbk_attn_rope_decode(e->qkv, L.bias, L.qn, L.kn, L.kc, L.vc, e->att, pos, L.heads, L.kvh, L.hd,
                                        e->ctx, L.theta, e->eps, L.neox, e->attn_ws, 1, s));
         {
-            const sbk_xsrc xs{nullptr, nullptr, nullptr, 0.0f, SBK_XS_PLAIN};
+            const sbk_xsrc xs{};
             const EngMat *ms[1] = {&L.o};
             float *ys[1] = {e->ob};
             ENG_MV(ms, ys, 1, e->att, xs);
         }
-        // FFN block: h + attention output -> rmsnorm -> gate|up; silu(gate) * up -> down
+        if (L.moe) {
+            // MoE FFN: h + attention output -> rmsnorm -> router logits; route; experts
+            {
+                const sbk_xsrc xs = norm_src(L.nf, ho);
+                const EngMat *ms[1] = {&L.router};
+                float *ys[1] = {e->rlog};
+                ENG_MV(ms, ys, 1, hc, xs);
+                std::swap(hc, ho);
+            }
+            const bool build = L.built_for == nullptr;
+            if (!build && L.built_for != hc) return fail("decode step: MoE batches built for another buffer");
+            if (moe_dispatch(e, L, hc, s, build, &n)) return fail("decode step: MoE launch rejected");
+            moe_ny = (int)(L.top_k + (L.has_sh ? 1 : 0));
+            continue;
+        }
+        // dense FFN block: h + attention output -> rmsnorm -> gate|up; silu(gate) * up -> down
         {
-            const sbk_xsrc xs{e->ob, L.nf, ho, e->eps, SBK_XS_NORM};
+            const sbk_xsrc xs = norm_src(L.nf, ho);
             const EngMat *ms[2] = {&L.g, &L.u};
             float *ys[2] = {e->gu, e->gu + L.ffn};
             ENG_MV(ms, ys, 2, hc, xs);
             std::swap(hc, ho);
         }
         {
-            const sbk_xsrc xs{e->gu + L.ffn, nullptr, nullptr, 0.0f, SBK_XS_SWIGLU};
+            sbk_xsrc xs{};
+            xs.res = e->gu + L.ffn, xs.mode = SBK_XS_SWIGLU;
             const EngMat *ms[1] = {&L.d};
             float *ys[1] = {e->ob};
             ENG_MV(ms, ys, 1, e->gu, xs);
         }
     }
     {
-        const sbk_xsrc xs{e->ob, e->fnorm, nullptr, e->eps, SBK_XS_NORM};
+        const sbk_xsrc xs = norm_src(e->fnorm, nullptr);
         const EngMat *ms[1] = {&e->lm};
         float *ys[1] = {e->logits};
         ENG_MV(ms, ys, 1, hc, xs);
@@ -341,19 +564,65 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
     for (size_t l = 0; l < p->n_layers; l++) {
         const sb_layer_plan &lp = p->layers[l];
         EngLayer &L = e->L[l];
-        if (lp.moe) return bail(0);  // MoE layers: not run by this engine
         if (!lp.norm_attn || !lp.norm_ffn) return bail(fail("decode plan: layer without norms"));
         L.heads = lp.heads, L.kvh = lp.kv_heads, L.hd = lp.head_dim, L.theta = lp.theta, L.neox = lp.neox;
-        if (!L.heads || !L.kvh || L.heads % L.kvh || L.hd != 128) return bail(0);
-        L.qd = L.heads * L.hd, L.kvd = L.kvh * L.hd, L.ffn = lp.gate.rows;
+        if (!L.heads || !L.kvh || L.heads % L.kvh || L.hd != 128 || L.heads / L.kvh > 8) return bail(0);
+        L.qd = L.heads * L.hd, L.kvd = L.kvh * L.hd;
         int rc;
         if ((rc = eng_mat(c, lp.q, L.qd, H, &L.q, true)) != 1) return bail(rc);
         if ((rc = eng_mat(c, lp.k, L.kvd, H, &L.k, true)) != 1) return bail(rc);
         if ((rc = eng_mat(c, lp.v, L.kvd, H, &L.v, true)) != 1) return bail(rc);
         if ((rc = eng_mat(c, lp.o, H, L.qd, &L.o, true)) != 1) return bail(rc);
-        if ((rc = eng_mat(c, lp.gate, L.ffn, H, &L.g, true)) != 1) return bail(rc);
-        if ((rc = eng_mat(c, lp.up, L.ffn, H, &L.u, true)) != 1) return bail(rc);
-        if ((rc = eng_mat(c, lp.down, H, L.ffn, &L.d, true)) != 1) return bail(rc);
+        if (lp.moe) {
+            // MoE FFN: every expert resident, its tensor map in a device table
+            const sb_moe_plan &mp = *lp.moe;
+            if (!mp.n_exp || !mp.top_k || mp.top_k > mp.n_exp || mp.top_k > 16 || mp.n_exp > 1024 || !mp.experts ||
+                !mp.ffn || mp.ffn % 256)
+                return bail(0);
+            L.moe = true, L.n_exp = mp.n_exp, L.top_k = mp.top_k, L.effn = mp.ffn;
+            L.has_sh = mp.shared != nullptr;
+            if (2 * (L.top_k + (L.has_sh ? 1 : 0)) > (size_t)sb::tcmv::MAXB) return bail(0);
+            if ((rc = eng_mat(c, mp.router, L.n_exp, H, &L.router, true)) != 1) return bail(rc);
+            L.ex.resize(3 * L.n_exp);
+            std::vector<CUtensorMap> maps(3 * L.n_exp);
+            for (size_t x = 0; x < L.n_exp; x++) {
+                const size_t r[3] = {L.effn, L.effn, H}, cc[3] = {H, H, L.effn};
+                for (int k = 0; k < 3; k++) {
+                    EngMat &m = L.ex[3 * x + k];
+                    if ((rc = eng_mat(c, mp.experts[3 * x + k], r[k], cc[k], &m, true)) != 1) return bail(rc);
+                    if (m.dt != L.ex[k].dt) return bail(0);  // one dtype per matrix kind
+                    const int mr = m.dt == SB_DTYPE_Q4_K
+                                       ? sb::tcmv::make_map<sb::tcmv::Q4K>(&maps[3 * x + k], m.w, (int)m.rows, (int)m.cols)
+                                   : m.dt == SB_DTYPE_Q6_K_P
+                                       ? sb::tcmv::make_map<sb::tcmv::Q6KP>(&maps[3 * x + k], m.w, (int)m.rows, (int)m.cols)
+                                       : 1;
+                    if (mr > 0) return bail(0);  // expert dtype without a tensor-core kernel
+                    if (mr < 0) return bail(fail("decode plan: tensor map of an expert rejected"));
+                }
+            }
+            if (L.has_sh) {
+                L.sffn = mp.shared[0].rows;
+                const size_t r[3] = {L.sffn, L.sffn, H}, cc[3] = {H, H, L.sffn};
+                for (int k = 0; k < 3; k++) {
+                    if ((rc = eng_mat(c, mp.shared[k], r[k], cc[k], &L.sh[k], true)) != 1) return bail(rc);
+                    if (L.sh[k].dt != L.ex[k].dt) return bail(0);
+                }
+                if (upload_f32(e, mp.shared_gate, H, &L.sg)) return bail(-1);
+            }
+            L.maps = (CUtensorMap *)e->dalloc(maps.size() * sizeof(CUtensorMap), &err);
+            if (err != cudaSuccess) return bail(fail("cudaMalloc(tensor maps)", err));
+            if ((err = cudaMemcpy(L.maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice)) !=
+                cudaSuccess)
+                return bail(fail("cudaMemcpy(tensor maps)", err));
+            e->moe_slots = std::max(e->moe_slots, L.top_k + (L.has_sh ? 1 : 0));
+            e->moe_ffn = std::max(e->moe_ffn, std::max(L.effn, L.sffn));
+            e->n_exp_max = std::max(e->n_exp_max, L.n_exp);
+        } else {
+            L.ffn = lp.gate.rows;
+            if ((rc = eng_mat(c, lp.gate, L.ffn, H, &L.g, true)) != 1) return bail(rc);
+            if ((rc = eng_mat(c, lp.up, L.ffn, H, &L.u, true)) != 1) return bail(rc);
+            if ((rc = eng_mat(c, lp.down, H, L.ffn, &L.d, true)) != 1) return bail(rc);
+        }
         if (upload_f32(e, lp.norm_attn, H, &L.na) || upload_f32(e, lp.norm_ffn, H, &L.nf) ||
             upload_f32(e, lp.q_norm, L.hd, &L.qn) || upload_f32(e, lp.k_norm, L.hd, &L.kn) ||
             upload_f32(e, lp.qkv_bias, L.qd + 2 * L.kvd, &L.bias))
@@ -383,6 +652,14 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
     e->gu = fbuf(2 * e->ffn_max);
     e->tmp = fbuf(std::max(e->ffn_max, std::max(H, e->qkv_max)));
     e->logits = fbuf(e->V);
+    if (e->moe_slots) {
+        e->rlog = fbuf(e->n_exp_max);
+        e->wts = fbuf(e->moe_slots);
+        e->ridx = (int *)fbuf(e->moe_slots);
+        e->moe_ffn = (e->moe_ffn + 63) & ~(size_t)63;
+        e->egu = fbuf(2 * e->moe_slots * e->moe_ffn);
+        e->ys = fbuf(e->moe_slots * H);
+    }
     e->ints = (int *)e->dalloc(64, &err);
     e->prompt = (int *)e->dalloc(e->ctx * 4, &err);
     e->hist = (int *)e->dalloc(e->ctx * 4, &err);

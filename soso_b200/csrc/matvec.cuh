@@ -516,7 +516,7 @@ extern "C" int sbk_matvec_batch_x(uint8_t dtype, const sbk_mv_op *ops, size_t n,
                                   void *stream)
 {
     if (!ops || n == 0 || !xs) return -1;
-    const sb::tcmv::XSrc x{xs->res, xs->norm_w, xs->h_out, xs->eps, xs->mode};
+    const sb::tcmv::XSrc x{xs->res, xs->norm_w, xs->h_out, xs->eps, xs->mode, xs->ys, xs->yw, xs->ny, xs->ystride};
     cudaStream_t s = (cudaStream_t)stream;
     if (dtype == SB_DTYPE_Q4_K) return sb::tc_matvec_batch<sb::tcmv::Q4K>(ops, n, pdl, s, true, &x);
     if (dtype == SB_DTYPE_Q6_K_P) return sb::tc_matvec_batch<sb::tcmv::Q6KP>(ops, n, pdl, s, false, &x);

@@ -155,24 +155,50 @@ struct XSrc {
     float *h_out;
     float eps;
     int mode;
+    // XS_NORM with a weighted set of residual vectors (a MoE layer's expert outputs):
+    // h = (sum_k yw[k] * ys[k * ystride + e], k = 0..ny-1 in order) + a   (layer.rs:1922-1933,
+    // then add_assign_f32 :1389); used instead of b when ny > 0
+    const float *ys;
+    const float *yw;
+    int ny, ystride;
 };
+
+constexpr int XS_MAXY = 16;
 
 // Element loader of the preparation: float4 i of the (transformed) input vector.
 struct XLoad {
     const float4 *a, *b, *w;
+    const float4 *ys;
     float scale;
-    int mode;
-    __device__ __forceinline__ float4 operator()(int i) const
+    int mode, ny, ys4;
+    float yw[XS_MAXY];
+
+    __device__ __forceinline__ float4 h(int i) const
     {
         float4 v = a[i];
-        if (mode == XS_NORM) {
-            if (b) {
-                const float4 r = b[i];
-                v.x += r.x, v.y += r.y, v.z += r.z, v.w += r.w;
+        if (ny) {
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int k = 0; k < ny; k++) {
+                const float4 y = ys[k * ys4 + i];
+                acc.x += y.x * yw[k], acc.y += y.y * yw[k], acc.z += y.z * yw[k], acc.w += y.w * yw[k];
             }
+            v.x = acc.x + v.x, v.y = acc.y + v.y, v.z = acc.z + v.z, v.w = acc.w + v.w;
+        } else if (b) {
+            const float4 r = b[i];
+            v.x += r.x, v.y += r.y, v.z += r.z, v.w += r.w;
+        }
+        return v;
+    }
+    __device__ __forceinline__ float4 operator()(int i) const
+    {
+        if (mode == XS_NORM) {
+            float4 v = h(i);
             const float4 g = w[i];
             v.x = v.x * scale * g.x, v.y = v.y * scale * g.y, v.z = v.z * scale * g.z, v.w = v.w * scale * g.w;
-        } else if (mode == XS_SWIGLU) {
+            return v;
+        }
+        float4 v = a[i];
+        if (mode == XS_SWIGLU) {
             const float4 u = b[i];
             v.x = v.x / (1.0f + expf(-v.x)) * u.x;
             v.y = v.y / (1.0f + expf(-v.y)) * u.y;

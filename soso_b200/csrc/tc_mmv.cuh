@@ -35,8 +35,10 @@ constexpr int MAXB = 40;           // matrices per launch
 constexpr int CNT_MAX = 1 << 16;   // groups of 16 rows per launch (counters in the workspace)
 
 struct __align__(64) MatDesc {
-    CUtensorMap map;        // weights as [rows][row_bytes/8] u64, box 16 x F::BOXW
+    CUtensorMap map;          // weights as [rows][row_bytes/8] u64, box 16 x F::BOXW
+    const CUtensorMap *mapp;  // when set: the map to use instead (a table entry chosen on the device)
     const float *x;
+    const float *xb;          // XS_SWIGLU: this matrix's b (else the batch's)
     float *y;
     int rows, cols, spg;    // spg: stages per 16-row group
     int st_begin, cnt_off;  // first global stage; first counter of its groups
@@ -107,9 +109,12 @@ __device__ __forceinline__ int owner_of(int unit, int total, int n)
     return unit < big ? unit / (base + 1) : rem + (base ? (unit - big) / base : 0);
 }
 
-template <class F>
-__global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_constant__ Batch B, Ws ws)
+template <class F, bool DEV>
+__device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
 {
+    // A batch in device memory may have been written by the previous kernel (the expert
+    // choice): everyone, the producer included, waits for it before reading the batch.
+    if (DEV) griddep_wait();
     constexpr int NCW = F::NCW, NSLOT = F::NSLOT, NSTREAM = F::NSTREAM;
     static_assert(NSLOT % NSTREAM == 0, "a ring slot must belong to one consumer team");
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -153,22 +158,24 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
             unsigned phase = 0;  // parity of the empty-barrier phase to wait for
             const uint64_t pol = l2_evict_first();
             const MatDesc *d = &B.d[mi];
+            const CUtensorMap *mp = d->mapp ? d->mapp : &d->map;
             int ls = st0 - d->st_begin, G = ls / d->spg, j = ls - G * d->spg;
             int mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&d->map) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(mp) : "memory");
             for (int k = 0; k < nst; k++) {
                 if (st0 + k == mend) {  // next matrix of the batch
                     d = &B.d[++mi];
+                    mp = d->mapp ? d->mapp : &d->map;
                     G = 0, j = 0;
                     mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
-                    asm volatile("prefetch.tensormap [%0];" ::"l"(&d->map) : "memory");
+                    asm volatile("prefetch.tensormap [%0];" ::"l"(mp) : "memory");
                 }
                 if (k >= NSLOT && !mbar_wait(&s.empty[slot], phase)) {
                     failed = true;
                     break;
                 }
                 mbar_expect_tx_arrive(&s.full[slot], (unsigned)F::SLOTB);  // full box, zero-filled past the ends
-                tma_load_2d(s.ring + slot * F::SLOTB, &d->map, F::stage_x(j), G * 16, &s.full[slot], pol);
+                tma_load_2d(s.ring + slot * F::SLOTB, mp, F::stage_x(j), G * 16, &s.full[slot], pol);
                 if (++j == d->spg) j = 0, G++;
                 if (++slot == NSLOT) {
                     slot = 0;
@@ -196,18 +203,22 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
             // x -> prep (unless the previous segment prepared the same x) and a clean
             // partial table for this segment
             if (d.x != prev_x || d.cols != prev_cols) {
-                XLoad X{reinterpret_cast<const float4 *>(d.x), reinterpret_cast<const float4 *>(B.xs.b),
-                        reinterpret_cast<const float4 *>(B.xs.w), 1.0f, B.xs.mode};
+                XLoad X;
+                X.a = reinterpret_cast<const float4 *>(d.x);
+                X.b = reinterpret_cast<const float4 *>(d.xb ? d.xb : B.xs.b);
+                X.w = reinterpret_cast<const float4 *>(B.xs.w);
+                X.ys = reinterpret_cast<const float4 *>(B.xs.ys);
+                X.scale = 1.0f;
+                X.mode = B.xs.mode;
+                X.ny = B.xs.mode == XS_NORM ? B.xs.ny : 0;
+                X.ys4 = B.xs.ystride / 4;
+                for (int k = 0; k < X.ny; k++) X.yw[k] = B.xs.yw[k];
                 if (B.xs.mode == XS_NORM) {
-                    // sum of squares of h = a (+ b), fixed order; CTA 0 stores h
+                    // sum of squares of h = a (+ b or the weighted residuals), fixed order; CTA 0 stores h
                     float ss = 0.0f;
                     float4 *ho = blockIdx.x == 0 ? reinterpret_cast<float4 *>(B.xs.h_out) : nullptr;
                     for (int i = cwg * 32 + lane; i < d.cols / 4; i += NCW * 32) {
-                        float4 v = X.a[i];
-                        if (X.b) {
-                            const float4 r = X.b[i];
-                            v.x += r.x, v.y += r.y, v.z += r.z, v.w += r.w;
-                        }
+                        const float4 v = X.h(i);
                         if (ho) ho[i] = v;
                         ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
                     }
@@ -343,6 +354,20 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
             if (r == 0) ws.cnt[d.cnt_off + G] = 0u;
         }
     }
+}
+
+template <class F>
+__global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_constant__ Batch B, Ws ws)
+{
+    tc_mmv_body<F, false>(B, ws);
+}
+
+// The same with the batch in device memory (written by an earlier kernel on the stream,
+// e.g. the expert choice of a MoE router); its matrices name their maps through mapp.
+template <class F>
+__global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_dev_kernel(const Batch *__restrict__ B, Ws ws)
+{
+    tc_mmv_body<F, true>(*B, ws);
 }
 
 // ------------------------------------------------------------------ host side
@@ -486,22 +511,31 @@ inline int group_split_max(const Batch &b, int grid)
     return mx;
 }
 
+struct MatOpX {  // a MatOp with a per-matrix second input (XS_SWIGLU) and an optional map table entry
+    MatOp op;
+    const float *xb;
+    const CUtensorMap *mapp;
+};
+
+// Fill *b (every field) for n matrices over `grid` CTAs; *smem = its dynamic shared memory.
+// With `uniform_x` false the matrices may have different inputs (XS_PLAIN / XS_SWIGLU).
 template <class F>
-inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int grid, int pdl, cudaStream_t stream,
-                           const XSrc *xs = nullptr)
+inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XSrc *xs, Batch *bp, size_t *smem_out)
 {
     if (n < 1 || n > MAXB) return -1;
-    static Batch b;  // large: built host-side, passed by value as the kernel parameter
-    static std::mutex mu;
-    std::lock_guard<std::mutex> lk(mu);
+    Batch &b = *bp;
     int st = 0, cnt = 0;
+    MatOp plain[MAXB];
     for (int i = 0; i < n; i++) {
-        const MatOp &o = ops[i];
+        const MatOp &o = ops[i].op;
+        plain[i] = o;
         if (o.cols > F::MAX_COLS || o.cols % 256 || o.rows < 1) return -1;
         MatDesc &d = b.d[i];
         const int mrc = cached_map<F>(&d.map, o.w, o.rows, o.cols);
         if (mrc) return mrc;
+        d.mapp = ops[i].mapp;
         d.x = o.x;
+        d.xb = ops[i].xb;
         d.y = o.y;
         d.rows = o.rows;
         d.cols = o.cols;
@@ -515,20 +549,28 @@ inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int gri
     b.n = n;
     b.total = st;
     b.total_groups = cnt;
-    b.xs = xs ? *xs : XSrc{nullptr, nullptr, nullptr, 0.0f, XS_PLAIN};
+    b.xs = xs ? *xs : XSrc{};
     if (b.xs.mode != XS_PLAIN) {
-        // one input vector for the whole batch (h_out is written once, from it)
-        for (int i = 1; i < n; i++)
-            if (ops[i].x != ops[0].x || ops[i].cols != ops[0].cols) return -1;
-        if ((b.xs.mode == XS_NORM && !b.xs.w) || (b.xs.mode == XS_SWIGLU && !b.xs.b)) return -1;
         if (b.xs.mode != XS_NORM && b.xs.mode != XS_SWIGLU) return -1;
-        if (((uintptr_t)b.xs.b | (uintptr_t)b.xs.w | (uintptr_t)b.xs.h_out) & 15) return -2;
+        if (b.xs.mode == XS_NORM) {
+            // one input vector for the whole batch (h_out is written once, from it)
+            for (int i = 1; i < n; i++)
+                if (ops[i].op.x != ops[0].op.x || ops[i].op.cols != ops[0].op.cols) return -1;
+            if (!b.xs.w || b.xs.ny < 0 || b.xs.ny > XS_MAXY || (b.xs.ny && (!b.xs.ys || !b.xs.yw))) return -1;
+            if (b.xs.ny && b.xs.ystride % 4) return -2;
+        } else {
+            for (int i = 0; i < n; i++)
+                if (!ops[i].xb && !b.xs.b) return -1;
+        }
+        if (((uintptr_t)b.xs.b | (uintptr_t)b.xs.w | (uintptr_t)b.xs.h_out | (uintptr_t)b.xs.ys) & 15) return -2;
     }
+    for (int i = 0; i < n; i++)
+        if ((uintptr_t)ops[i].xb & 15) return -2;
     // Whole groups per CTA when that costs at most one stage more on the busiest CTA
     // and the stream-K split is short (latency-bound): no cross-CTA fix-up at all.
     const int smax = (st + grid - 1) / grid, gmax = group_split_max(b, grid);
     b.split_groups = gmax <= smax || (gmax <= smax + 1 && smax <= 4);
-    size_t smem = batch_smem<F>(ops, n, grid, &b.max_cols, &b.max_groups);
+    size_t smem = batch_smem<F>(plain, n, grid, &b.max_cols, &b.max_groups);
     if (b.split_groups) {
         const int need = (cnt + grid - 1) / grid + 1;
         if (need > b.max_groups && smem_bytes<F>(b.max_cols, need) <= 227 * 1024) {
@@ -539,28 +581,78 @@ inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int gri
         }
     }
     if (smem > 227 * 1024) return -5;
-    // the kernel's dynamic shared-memory limit only ever grows (one record per device)
-    static size_t smem_set[64];
+    *smem_out = smem;
+    return 0;
+}
+
+// Raise a kernel's dynamic shared-memory limit to `smem` (only ever grows; one record per
+// device and kernel).
+template <class K>
+inline int ensure_smem(K kernel, size_t smem, size_t *rec)
+{
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return -3;
-    if (smem > smem_set[dev]) {
-        if (cudaFuncSetAttribute(tc_mmv_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-            cudaSuccess)
+    if (smem > rec[dev]) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return -3;
-        smem_set[dev] = smem;
+        rec[dev] = smem;
     }
+    return 0;
+}
+
+inline cudaLaunchConfig_t mmv_config(int grid, int threads, size_t smem, int pdl, cudaStream_t stream,
+                                     cudaLaunchAttribute *attr)
+{
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(F::THREADS);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
+    return cfg;
+}
+
+// Launch a batch of up to MAXB independent matvecs of format F on `stream`, with
+// the scratch given as counter / partial pointers (counters zero on entry, left
+// zero); at most cnt_cap 16-row groups in the batch.
+template <class F>
+inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int grid, int pdl, cudaStream_t stream,
+                           const XSrc *xs = nullptr)
+{
+    if (n < 1 || n > MAXB) return -1;
+    static Batch b;  // large: built host-side, passed by value as the kernel parameter
+    static std::mutex mu;
+    static size_t smem_rec[64];
+    std::lock_guard<std::mutex> lk(mu);
+    MatOpX ox[MAXB];
+    for (int i = 0; i < n; i++) ox[i] = MatOpX{ops[i], nullptr, nullptr};
+    size_t smem = 0;
+    int rc = build_batch<F>(ox, n, cnt_cap, grid, xs, &b, &smem);
+    if (rc) return rc;
+    if ((rc = ensure_smem(tc_mmv_kernel<F>, smem, smem_rec))) return rc;
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = mmv_config(grid, F::THREADS, smem, pdl, stream, attr);
     return cudaLaunchKernelEx(&cfg, tc_mmv_kernel<F>, b, wsd) == cudaSuccess ? 0 : -4;
+}
+
+// Launch a batch held in device memory (dev, a copy of a batch made by build_batch, whose
+// mapp / x / y fields an earlier kernel on the stream may have rewritten; shapes and the
+// split must stay as built).  smem as build_batch returned it.
+template <class F>
+inline int launch_dev_batch(const Batch *dev, size_t smem, Ws wsd, int grid, int pdl, cudaStream_t stream)
+{
+    static size_t smem_rec[64];
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    int rc = ensure_smem(tc_mmv_dev_kernel<F>, smem, smem_rec);
+    if (rc) return rc;
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = mmv_config(grid, F::THREADS, smem, pdl, stream, attr);
+    return cudaLaunchKernelEx(&cfg, tc_mmv_dev_kernel<F>, dev, wsd) == cudaSuccess ? 0 : -4;
 }
 
 // As launch_batch_ws over a workspace of ws_bytes(grid) bytes.

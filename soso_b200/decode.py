@@ -14,7 +14,8 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import synth
-from ._lib import (SbDecodePlan, SbLayerPlan, SbMat, SbView, SbError, c_f32p, c_u8p, last_error, lib)
+from ._lib import (SbDecodePlan, SbLayerPlan, SbMat, SbMoePlan, SbView, SbError, c_f32p, c_u8p, last_error,
+                   lib)
 from .formats import DTYPE_Q4_K, DTYPE_Q6_K
 
 
@@ -34,6 +35,15 @@ class DenseConfig:
     neox: bool = True
     qkv_bias: bool = True
     qk_norm: bool = False
+    # MoE FFN on layers >= first_moe when n_exp > 0 (forward_moe_ffn, layer.rs:1938-2109):
+    # n_exp routed experts of width moe_ffn, top_k chosen per token, and an optional shared
+    # expert of width shared_ffn (gated by sigmoid(ffn_gate_inp_shexp . x) when shared_gate)
+    n_exp: int = 0
+    top_k: int = 0
+    moe_ffn: int = 0
+    first_moe: int = 0
+    shared_ffn: int = 0
+    shared_gate: bool = False
     # Q4_K_M mix: Q4_K everywhere, Q6_K for ffn_down and the output matrix
     dtypes: dict = field(default_factory=lambda: {"attn_q": DTYPE_Q4_K, "attn_k": DTYPE_Q4_K, "attn_v": DTYPE_Q4_K,
                                                   "attn_output": DTYPE_Q4_K, "ffn_gate": DTYPE_Q4_K,
@@ -48,12 +58,29 @@ class DenseConfig:
     def kv_dim(self) -> int:
         return self.kv_heads * self.head_dim
 
+    def is_moe(self, layer: int) -> bool:
+        return self.n_exp > 0 and layer >= self.first_moe
+
 
 # Qwen2.5-3B-style dense decoder, fp16 KV at 4096 context
 QWEN25_3B = DenseConfig(n_layers=36, hidden=2048, heads=16, kv_heads=2, head_dim=128, ffn=11008, vocab=151936,
                         ctx=4096)
 # a small model of the same structure, for parity tests against the CPU oracle
 TINY = DenseConfig(n_layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1024, ctx=160)
+
+_ALL_Q4K = {k: DTYPE_Q4_K for k in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down",
+                                    "output", "token_embd", "ffn_gate_inp")}
+# Qwen3-30B-A3B-style MoE decoder, all Q4_K, QK-norm, fp16 KV at 2048
+QWEN3_30B_A3B = DenseConfig(n_layers=48, hidden=2048, heads=32, kv_heads=4, head_dim=128, ffn=0, vocab=151936,
+                            ctx=2048, qkv_bias=False, qk_norm=True, n_exp=128, top_k=8, moe_ffn=768,
+                            dtypes=dict(_ALL_Q4K))
+# small MoE models of the same structure for parity tests: one dense layer first, then MoE
+# layers with a gated shared expert (TINY_MOE) or none (TINY_MOE_NS)
+TINY_MOE = DenseConfig(n_layers=3, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1024, ctx=96,
+                       qkv_bias=False, qk_norm=True, n_exp=16, top_k=4, moe_ffn=256, first_moe=1, shared_ffn=512,
+                       shared_gate=True, dtypes=dict(_ALL_Q4K, ffn_down=DTYPE_Q6_K, output=DTYPE_Q6_K))
+TINY_MOE_NS = DenseConfig(n_layers=2, hidden=512, heads=8, kv_heads=2, head_dim=128, ffn=0, vocab=1024, ctx=96,
+                          qkv_bias=False, qk_norm=True, n_exp=32, top_k=8, moe_ffn=256, dtypes=dict(_ALL_Q4K))
 
 
 def shapes(cfg: DenseConfig) -> dict:
@@ -70,7 +97,26 @@ def synth_model(cfg: DenseConfig, seed: str = "model") -> dict:
     H = cfg.hidden
     for l in range(cfg.n_layers):
         for name, (rows, cols) in shapes(cfg).items():
+            if cfg.is_moe(l) and name.startswith("ffn_"):
+                continue
             m[f"blk.{l}.{name}"] = synth.model_weights(cfg.dtypes[name], rows, cols, synth.rng(seed, l, name))
+        if cfg.is_moe(l):
+            # router rows scaled so the logits are about N(0, 1)
+            m[f"blk.{l}.ffn_gate_inp"] = synth.model_weights(cfg.dtypes["ffn_gate_inp"], cfg.n_exp, H,
+                                                              synth.rng(seed, l, "router"), std=1.0 / np.sqrt(H))
+            for e in range(cfg.n_exp):
+                for name, (rows, cols) in (("ffn_gate", (cfg.moe_ffn, H)), ("ffn_up", (cfg.moe_ffn, H)),
+                                           ("ffn_down", (H, cfg.moe_ffn))):
+                    m[f"blk.{l}.E{e:03d}.{name}"] = synth.model_weights(cfg.dtypes[name], rows, cols,
+                                                                         synth.rng(seed, l, e, name))
+            if cfg.shared_ffn:
+                for name, (rows, cols) in (("ffn_gate", (cfg.shared_ffn, H)), ("ffn_up", (cfg.shared_ffn, H)),
+                                           ("ffn_down", (H, cfg.shared_ffn))):
+                    m[f"blk.{l}.S00.{name}"] = synth.model_weights(cfg.dtypes[name], rows, cols,
+                                                                    synth.rng(seed, l, "shared", name))
+                if cfg.shared_gate:
+                    m[f"blk.{l}.ffn_gate_inp_shexp"] = (synth.rng(seed, l, "sg").standard_normal(H) /
+                                                        np.sqrt(H)).astype(np.float32)
         g = synth.rng(seed, l, "vec")
         m[f"blk.{l}.attn_norm"] = (1.0 + 0.1 * g.standard_normal(H)).astype(np.float32)
         m[f"blk.{l}.ffn_norm"] = (1.0 + 0.1 * g.standard_normal(H)).astype(np.float32)
@@ -118,8 +164,12 @@ class DecodeSession:
             lp.norm_ffn = _f32(model[f"blk.{l}.ffn_norm"])
             for fld, name in (("q", "attn_q"), ("k", "attn_k"), ("v", "attn_v"), ("o", "attn_output"),
                               ("gate", "ffn_gate"), ("up", "ffn_up"), ("down", "ffn_down")):
+                if cfg.is_moe(l) and name.startswith("ffn_"):
+                    continue
                 rows, cols = shapes(cfg)[name]
                 setattr(lp, fld, self._mat(f"blk.{l}.{name}", cfg.dtypes[name], rows, cols))
+            if cfg.is_moe(l):
+                lp.moe = ctypes.pointer(self._moe_plan(l))
         plan = SbDecodePlan()
         plan.layers = layers
         plan.n_layers = cfg.n_layers
@@ -131,6 +181,30 @@ class DecodeSession:
         rc = L.sb_decode_prepare(self.ctx, ctypes.byref(plan))
         if rc != 1:
             raise SbError(f"sb_decode_prepare returned {rc}: {last_error()}")
+
+    def _moe_plan(self, l: int) -> SbMoePlan:
+        """MoeDec (gpu.rs:130-137) of layer l: router, experts [gate, up, down] each, shared expert."""
+        cfg, H = self.cfg, self.cfg.hidden
+        mp = SbMoePlan()
+        mp.n_exp, mp.top_k, mp.ffn = cfg.n_exp, cfg.top_k, cfg.moe_ffn
+        mp.router = self._mat(f"blk.{l}.ffn_gate_inp", cfg.dtypes["ffn_gate_inp"], cfg.n_exp, H)
+        ex = (SbMat * (3 * cfg.n_exp))()
+        for e in range(cfg.n_exp):
+            for k, (name, rows, cols) in enumerate((("ffn_gate", cfg.moe_ffn, H), ("ffn_up", cfg.moe_ffn, H),
+                                                     ("ffn_down", H, cfg.moe_ffn))):
+                ex[3 * e + k] = self._mat(f"blk.{l}.E{e:03d}.{name}", cfg.dtypes[name], rows, cols)
+        mp.experts = ex
+        if cfg.shared_ffn:
+            sh = (SbMat * 3)()
+            for k, (name, rows, cols) in enumerate((("ffn_gate", cfg.shared_ffn, H), ("ffn_up", cfg.shared_ffn, H),
+                                                     ("ffn_down", H, cfg.shared_ffn))):
+                sh[k] = self._mat(f"blk.{l}.S00.{name}", cfg.dtypes[name], rows, cols)
+            mp.shared = sh
+            self._keep.append(sh)
+            if cfg.shared_gate:
+                mp.shared_gate = _f32(self.model[f"blk.{l}.ffn_gate_inp_shexp"])
+        self._keep += [ex, mp]
+        return mp
 
     def _mat(self, key: str, dtype: int, rows: int, cols: int) -> SbMat:
         w = self.model[key]

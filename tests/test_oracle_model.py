@@ -16,3 +16,15 @@ def test_tiny_model_steps_are_finite_and_deterministic():
     # logits are O(1)..O(10), not collapsed: the synthetic weights keep activations sane
     s = np.std(la[-1])
     assert 0.05 < s < 100
+
+
+def test_tiny_moe_model_steps_route_and_stay_finite():
+    cfg = decode.TINY_MOE
+    model = decode.synth_model(cfg, "tinymoe")
+    orc = DenseOracle(cfg, model)
+    prompt = synth.rng("prompt", "tinymoe").integers(0, cfg.vocab, 3).astype(np.int32)
+    toks, lg = orc.greedy(prompt, 4)
+    assert all(np.isfinite(x).all() for x in lg)
+    idx, wts = orc.last_route
+    assert len(set(idx.tolist())) == cfg.top_k and abs(float(np.sum(wts)) - 1.0) < 1e-5
+    assert np.all(np.diff(wts) <= 0)  # rank order: weights descending
