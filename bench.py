@@ -305,7 +305,8 @@ def run_ours(args) -> None:
         e2e_s = float(t.item())
     L.sb_destroy(ctx)
 
-    dec = None if args.no_decode else decode_bench(local, rank)
+    dec = None if args.no_decode else decode_bench(local, rank, "dense")
+    dec_moe = None if args.no_decode else decode_bench(local, rank, "moe")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -350,6 +351,11 @@ def run_ours(args) -> None:
                 dec["aggregate_tok_per_s"] = round(dec["tok_per_s"] * world, 1)
                 dec["parallelism"] = f"{world} independent replicas (no tensor parallelism yet)"
             line["decode"] = dec
+        if dec_moe:
+            if world > 1:
+                dec_moe["aggregate_tok_per_s"] = round(dec_moe["tok_per_s"] * world, 1)
+                dec_moe["parallelism"] = f"{world} independent replicas (no expert parallelism yet)"
+            line["decode_moe"] = dec_moe
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -359,32 +365,45 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
-def decode_bench(device: int, rank: int) -> dict:
-    """Qwen2.5-3B-style dense decoder (Q4_K_M mix), fp16 KV at 4096
-    context, batch-1 greedy decode of 256 tokens after a 128-token random prompt, through the
-    whole-token decode engine (sb_decode_greedy: one CUDA graph per token, tokens chained
-    on the device).  Timed: the 256 generated tokens (wall clock around the call, which
-    ends with a stream synchronize)."""
+def decode_bench(device: int, rank: int, which: str = "dense") -> dict:
+    """Whole-token decode through the engine (sb_decode_greedy: one CUDA graph per token,
+    tokens chained on the device), batch-1 greedy decode of 256 tokens after a 128-token
+    random prompt.  which = "dense": BASELINE.json configs[2] (Qwen2.5-3B-style, Q4_K_M mix,
+    fp16 KV at 4096); "moe": configs[3] (Qwen3-30B-A3B-style, 128 experts top-8, all Q4_K,
+    fp16 KV at 2048).  Timed: the 256 generated tokens (wall clock around the call, which
+    ends with a stream synchronize).  Bytes per token = weights read per token (attention,
+    router, the top-k experts' matrices, output matrix) + the KV rows read at the average
+    position."""
     from soso_b200 import decode, synth
-    cfg = decode.QWEN25_3B
-    model = decode.synth_model(cfg, f"c3.{rank}")
+    cfg = decode.QWEN25_3B if which == "dense" else decode.QWEN3_30B_A3B
+    model = decode.synth_model(cfg, f"c{'3' if which == 'dense' else '4'}.{rank}")
     sess = decode.DecodeSession(cfg, model, device=device)
-    prompt = synth.rng("prompt", "c3", rank).integers(0, cfg.vocab, 128).astype(np.int32)
+    prompt = synth.rng("prompt", which, rank).integers(0, cfg.vocab, 128).astype(np.int32)
     sess.greedy(prompt[:8], 8)  # warm
     first = sess.greedy(prompt, 128)  # the prompt, one token per step
     n_gen = 256
     t0 = time.perf_counter()
     toks = sess.greedy(first[-1:], n_gen, pos=128)
     dt = time.perf_counter() - t0
-    weights = sum(v.nbytes for k, v in model.items() if k != "token_embd" and v.dtype == np.uint8)
+    weights = 0
+    for k, v in model.items():
+        if k == "token_embd" or v.dtype != np.uint8:
+            continue
+        if ".E" in k:  # routed experts: top_k of n_exp read per token
+            weights += v.nbytes * cfg.top_k / cfg.n_exp
+        else:
+            weights += v.nbytes
     kv_per_pos = cfg.n_layers * 2 * cfg.kv_dim * 2
     avg_ctx = 128 + (n_gen + 1) / 2.0
     bytes_tok = weights + kv_per_pos * avg_ctx + cfg.hidden * 4
     peaks = load_peaks()
     tps = n_gen / dt
     sess.close()
-    return {"config": "configs[2]: Qwen2.5-3B-style dense, 36 layers, hidden 2048, 16 q / 2 kv heads x 128, "
-                      "SwiGLU 11008, vocab 151936, Q4_K + Q6_K (ffn_down, output), fp16 KV ctx 4096",
+    desc = ("configs[2]: Qwen2.5-3B-style dense, 36 layers, hidden 2048, 16 q / 2 kv heads x 128, SwiGLU 11008, "
+            "vocab 151936, Q4_K + Q6_K (ffn_down, output), fp16 KV ctx 4096") if which == "dense" else (
+            "configs[3]: Qwen3-30B-A3B-style MoE, 48 layers, hidden 2048, 32 q / 4 kv heads x 128, QK-norm, "
+            "128 experts x SwiGLU 768, softmax top-8, vocab 151936, all Q4_K, fp16 KV ctx 2048")
+    return {"config": desc,
             "data": "synthetic random-init weights (seeded), random prompt",
             "prompt_tokens": 128, "generated_tokens": n_gen, "tok_per_s": round(tps, 1),
             "ms_per_token": round(1e3 * dt / n_gen, 3), "bytes_per_token": int(bytes_tok),
