@@ -228,6 +228,21 @@ typedef struct {
  * aligned vectors).  Returns -5 for a dtype without the fused input forms. */
 int sbk_matvec_batch_x(uint8_t dtype, const sbk_mv_op *ops, size_t n, const sbk_xsrc *xs, int pdl, void *stream);
 
+/* Batched prefill GEMM on the tcgen05 tensor cores: y[n x rows] = x[n x cols] . W^T for
+ * Q4_K weights (device pointers, x and y f32, row-major).  W is dequantised to 16-bit
+ * operands in shared memory tile by tile, x is rounded likewise (into ws), accumulation is
+ * f32 in tensor memory.  Replaces the reference's block-prefill GEMM iq_matmul_mma
+ * (lxdde/ports/nouveau/matvec_iq.cu:731-816, :966; f16 mma.sync) and the CPU
+ * matvec_q4_k_batch (crates/soso-llm-core/src/gemm.rs:495-546) behind
+ * GpuDispatch::matmul (crates/soso-llm-core/src/gpu.rs:443-455).  ws: at least
+ * sbk_matmul_ws_bytes(n, cols) bytes, 16-byte aligned.  -5: dtype not supported. */
+size_t sbk_matmul_ws_bytes(size_t n, size_t cols);
+/* prec: SBK_PREC_BF16 (weights and x as bf16, 8 significant bits) or SBK_PREC_F16 (as f16,
+ * 11 bits: the precision of the reference's f16 mma.sync prefill). */
+enum { SBK_PREC_BF16 = 0, SBK_PREC_F16 = 1 };
+int sbk_matmul(uint8_t dtype, const void *w, size_t rows, size_t cols, size_t n, const float *x, float *y, void *ws,
+               int prec, int pdl, void *stream);
+
 /* RMSNorm of `rows` rows of n floats, `gemm::rmsnorm` (crates/soso-llm-core/src/gemm.rs:93-100),
  * optionally fused with the residual add `add_f32` (gemm.rs:265): with res != NULL,
  * h_out = x + res and y = rmsnorm(h_out) * w; else y = rmsnorm(x) * w.  y may alias x.

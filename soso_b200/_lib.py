@@ -111,6 +111,9 @@ SIGNATURES = {
     "sbk_matvec_q4k_noalloc": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_void_p]),
     "sbk_num_sms": (ctypes.c_int, [ctypes.c_int]),
+    "sbk_matmul_ws_bytes": (c_size, [c_size, c_size]),
+    "sbk_matmul": (ctypes.c_int, [ctypes.c_uint8, ctypes.c_void_p, c_size, c_size, c_size, ctypes.c_void_p,
+                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "sbk_take_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
 }
 

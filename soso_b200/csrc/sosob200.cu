@@ -7,3 +7,4 @@
 #include "dispatch.cuh"
 #include "engine.cuh"
 #include "noalloc.cuh"
+#include "prefill.cuh"

@@ -39,10 +39,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *b)
 
 // Bounded wait for the phase with the given parity; false if the limit ran out.
 // (The suspend-time hint lets a waiting warp yield its issue slots.)
-__device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity)
+__device__ __forceinline__ bool mbar_wait(uint64_t *b, unsigned parity, unsigned limit = SPIN_LIMIT)
 {
     const uint32_t a = smem_u32(b);
-    for (unsigned i = 0; i < SPIN_LIMIT; i++) {
+    for (unsigned i = 0; i < limit; i++) {
         uint32_t ok;
         asm volatile(
             "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
