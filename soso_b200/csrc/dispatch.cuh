@@ -54,6 +54,8 @@ bool kernel_dtype(uint8_t d) { return d == SB_DTYPE_Q8_0 || d == SB_DTYPE_Q4_K |
 
 }  // namespace
 
+constexpr size_t PREFILL_MIN_TOKENS = 16;  // sb_matmul: from this many tokens on, the tcgen05 GEMM
+
 struct sb_engine;                  // whole-token decode state (engine.cuh)
 void sb_engine_free(sb_engine *e);
 
@@ -241,16 +243,28 @@ static int run_matvecs(sb_ctx *c, const char *key, const sb_view *w, size_t rows
     int rc = c->resident(key, w, rows, cols, &r);
     if (rc <= 0) return rc;
     const size_t xb = n * cols * 4, yb = n * rows * 4, xoff = (xb + 255) & ~(size_t)255;
-    if (c->ensure_scratch(xoff + yb) || c->ensure_host_stage(xoff + yb)) return -1;
+    const size_t yoff = xoff + ((yb + 255) & ~(size_t)255);
+    // batches of tokens go to the tensor-core prefill GEMM (f16 operands: the precision of
+    // the reference's own mma.sync prefill), single tokens to the matvec
+    const bool gemm = n >= PREFILL_MIN_TOKENS && r->dev_dtype == SB_DTYPE_Q4_K;
+    const size_t wsb = gemm ? sbk_matmul_ws_bytes(n, cols) : 0;
+    if (c->ensure_scratch(yoff + wsb) || c->ensure_host_stage(xoff + yb)) return -1;
     float *dx = (float *)c->scratch, *dy = (float *)((char *)c->scratch + xoff);
     char *hs = (char *)c->host_stage;
     memcpy(hs, x, xb);
     if ((e = cudaMemcpyAsync(dx, hs, xb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(x)", e);
-    for (size_t t = 0; t < n; t++) {
-        int k = sbk_matvec(r->dev_dtype, r->ptr, rows, cols, dx + t * cols, dy + t * rows, 0, c->stream);
-        if (k) return fail("sbk_matvec launch failed (" + std::to_string(k) + ")");
-        c->stats.launches++;
+    if (gemm) {
+        int k = sbk_matmul(r->dev_dtype, r->ptr, rows, cols, n, dx, dy, (char *)c->scratch + yoff, SBK_PREC_F16, 0,
+                           c->stream);
+        if (k) return fail("sbk_matmul launch failed (" + std::to_string(k) + ")");
+        c->stats.launches += 2;
+    } else {
+        for (size_t t = 0; t < n; t++) {
+            int k = sbk_matvec(r->dev_dtype, r->ptr, rows, cols, dx + t * cols, dy + t * rows, 0, c->stream);
+            if (k) return fail("sbk_matvec launch failed (" + std::to_string(k) + ")");
+            c->stats.launches++;
+        }
     }
     if ((e = cudaMemcpyAsync(hs + xoff, dy, yb, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(out)", e);

@@ -13,18 +13,19 @@
 // tokens) output tile over the whole K, so every weight byte is read and
 // dequantised once per 256 tokens.
 //
-// Warp roles (6 warps):
+// Warp roles (10 warps):
 //   warp 0     TMA producer: raw weight blocks (one 256-column block column per
 //              4 stages) and the X tile of every 64-column stage
 //   warp 1     owns the tensor-memory allocation; one elected lane issues the
 //              tcgen05.mma of a stage (4 x K16) and commits it to the stage's
 //              `empty` barrier, and after the last stage to `acc_full`
-//   warps 2-5  dequantise: thread r takes weight row r of the tile, one 64-column
-//              stage at a time (Q4_K: one byte pair, sub-blocks 2p and 2p+1),
-//              writing bf16 rows in the 128-byte-swizzled K-major layout the MMA
+//   warps 2-9  dequantise: two threads per weight row of the tile, one 64-column
+//              stage at a time (Q4_K: one byte pair, sub-block 2p or 2p+1 each),
+//              writing 16-bit rows in the 128-byte-swizzled K-major layout the MMA
 //              descriptor describes; then the epilogue: tcgen05.ld of their
-//              32 lanes (warp w reads lanes 32*(w%4)..), stores of Y (a warp
-//              writes 32 consecutive rows of one token: coalesced).
+//              32 lanes (warp w reads lanes 32*(w%4)..; the two warps of a lane
+//              quadrant split the columns), stores of Y (a warp writes 32
+//              consecutive rows of one token: coalesced).
 // Every mbarrier wait is bounded and reports through the device error word; the
 // tensor memory is always freed after the last commit has landed.
 #pragma once
@@ -41,7 +42,8 @@ constexpr int BK = 64;        // columns per stage: one 128-byte swizzle atom of
 constexpr int NST = 3;        // stages in flight
 constexpr int RAWK = 256;     // columns per raw weight block column (one Q4_K block)
 constexpr int NRAW = 2;       // raw weight block columns in flight
-constexpr int THREADS = 192;
+constexpr int NDQ = 8;        // dequantising / epilogue warps: two threads per weight row
+constexpr int THREADS = (2 + NDQ) * 32;
 constexpr int X_BYTES = BN * BK * 2;   // 32 KiB
 constexpr int W_BYTES = BM * BK * 2;   // 16 KiB
 constexpr int TMEM_COLS = 256;
@@ -147,41 +149,35 @@ __device__ __forceinline__ uint32_t pack16(float a, float b)
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// Q4_K, one byte pair p of the block in `blk` (144 bytes): 64 weights of sub-blocks 2p (low
-// nibbles, columns 0..31) and 2p+1 (high nibbles, columns 32..63) as d*sc*q - dmin*m
-// (crates/sosomodel/src/dequant.rs:150-248), rounded to the operand type and written into
-// this row of the swizzled stage tile.
+// Q4_K, one byte pair p of the block in `blk` (144 bytes), nibble half h: the 32 weights of
+// sub-block 2p + h (h = 0: low nibbles, columns 0..31 of the stage; 1: high nibbles,
+// columns 32..63) as d*sc*q - dmin*m (crates/sosomodel/src/dequant.rs:150-248), rounded to
+// the operand type and written into this row of the swizzled stage tile.
 template <bool F16>
-__device__ __forceinline__ void q4k_pair_to_16(const uint8_t *blk, int p, uint8_t *row, int r)
+__device__ __forceinline__ void q4k_half_to_16(const uint8_t *blk, int p, int h, uint8_t *row, int r)
 {
     const float d = __half2float(*reinterpret_cast<const __half *>(blk));
     const float dmin = __half2float(*reinterpret_cast<const __half *>(blk + 2));
     const uint8_t *sc = blk + 4;
-    float a[2], b[2];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int j = 2 * p + h;
-        unsigned s_, m_;
-        if (j < 4) s_ = sc[j] & 63, m_ = sc[j + 4] & 63;
-        else s_ = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4), m_ = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-        a[h] = d * (float)s_;
-        b[h] = dmin * (float)m_;
-    }
+    const int j = 2 * p + h;
+    unsigned s_, m_;
+    if (j < 4) s_ = sc[j] & 63, m_ = sc[j + 4] & 63;
+    else s_ = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4), m_ = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    const float a = d * (float)s_, b = dmin * (float)m_;
     const uint4 *q4 = reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
 #pragma unroll
-    for (int half = 0; half < 2; half++) {  // 16 bytes -> weights 16*half .. +15 (low) and 32 + ... (high)
+    for (int half = 0; half < 2; half++) {  // 16 bytes -> weights 16*half .. +15 of the sub-block
         const uint4 qv = q4[half];
         const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-        for (int h = 0; h < 2; h++) {  // h = 0: low nibbles (sub-block 2p), 1: high (2p+1)
+        {
             uint32_t out[8];
 #pragma unroll
             for (int wd = 0; wd < 4; wd++) {
                 const uint32_t v = h ? (qw[wd] >> 4) & 0x0F0F0F0Fu : qw[wd] & 0x0F0F0F0Fu;
                 const float q0 = (float)(v & 0xFF), q1 = (float)((v >> 8) & 0xFF), q2 = (float)((v >> 16) & 0xFF),
                             q3 = (float)(v >> 24);
-                out[2 * wd] = pack16<F16>(a[h] * q0 - b[h], a[h] * q1 - b[h]);
-                out[2 * wd + 1] = pack16<F16>(a[h] * q2 - b[h], a[h] * q3 - b[h]);
+                out[2 * wd] = pack16<F16>(a * q0 - b, a * q1 - b);
+                out[2 * wd + 1] = pack16<F16>(a * q2 - b, a * q3 - b);
             }
             // columns 32*h + 16*half .. +15 = 16-byte chunks c0, c0 + 1 of the 128-byte row
             const int c0 = 4 * h + 2 * half;
@@ -212,12 +208,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < NST; i++) {
             tcmv::mbar_init(&s.x_full[i], 1);
-            tcmv::mbar_init(&s.w_full[i], 4);
+            tcmv::mbar_init(&s.w_full[i], NDQ);
             tcmv::mbar_init(&s.st_empty[i], 1);
         }
         for (int i = 0; i < NRAW; i++) {
             tcmv::mbar_init(&s.raw_full[i], 1);
-            tcmv::mbar_init(&s.raw_empty[i], 4);
+            tcmv::mbar_init(&s.raw_empty[i], NDQ);
         }
         tcmv::mbar_init(s.acc_full, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -284,8 +280,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         __syncwarp();
     } else {
-        // dequantisers: thread r = weight row r of the tile
-        const int r = threadIdx.x - 64;
+        // dequantisers: thread t takes weight row t % 128, nibble half t / 128
+        const int r = (threadIdx.x - 64) & (BM - 1), hh = (threadIdx.x - 64) / BM;
         for (int ks = 0; ks < KS && !failed; ks++) {
             const int st = ks % NST, rk = ks / 4, rs = rk % NRAW, p = ks % 4;
             if (p == 0 && !tcmv::mbar_wait(&s.raw_full[rs], (rk / NRAW) & 1, WAIT)) failed = true;
@@ -294,7 +290,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 set_dev_error(0x73u);
                 break;
             }
-            q4k_pair_to_16<F16>(s.raw[rs] + r * RAW_ROWB, p, s.w[st] + r * 128, r);
+            q4k_half_to_16<F16>(s.raw[rs] + r * RAW_ROWB, p, hh, s.w[st] + r * 128, r);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
             __syncwarp();
             if (lane == 0) {
@@ -306,7 +302,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (tcmv::mbar_wait(s.acc_full, 0, WAIT)) {
             fence_after_sync();
             const int q = warp & 3, row = row0 + 32 * q + lane;
-            for (int c = 0; c < BN; c += 32) {
+            const int c0 = ((warp - 2) / 4) * (BN * 4 / NDQ);  // warps of one lane quadrant split the columns
+            for (int c = c0; c < c0 + BN * 4 / NDQ; c += 32) {
                 float v[32];
                 tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
                 if (row < a.rows) {

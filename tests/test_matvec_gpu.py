@@ -122,6 +122,31 @@ def test_cuda_matvec_recipe_q4k_and_reject(gpu):
     assert not gpu.matvec("raro", corto, 2, 128, np.zeros(128, np.float32), np.zeros(2, np.float32))
 
 
+def test_cuda_matmul_recipe_tensor_core_path(gpu):
+    """cuda_matvec.rs:245-272 with n large enough for the tensor-core prefill GEMM
+    (GpuDispatch::matmul, f16 operands, f32 accumulation), graded like the reference's own
+    f16 path: max |y - r| / (1 + rms(r)) < 8e-3."""
+    e = synth.Lcg(778)
+    rows, cols = 200, 2304
+    blocks = []
+    for _ in range(rows * cols // 256):
+        b = np.empty(144, dtype=np.uint8)
+        b[0:2] = np.array([ESCALAS_F16[e.next() % 4]], dtype=np.uint16).view(np.uint8)
+        b[2:4] = np.array([ESCALAS_F16[e.next() % 4]], dtype=np.uint16).view(np.uint8)
+        b[4:] = [e.next() & 0xFF for _ in range(140)]
+        blocks.append(b)
+    w = np.concatenate(blocks)
+    v = view(DTYPE_Q4_K, w, rows, cols)
+    for n in (16, 64, 300):
+        x = np.array([(e.next() % 2001) / 1000.0 - 1.0 for _ in range(n * cols)], dtype=np.float32)
+        y = np.zeros(n * rows, dtype=np.float32)
+        assert gpu.matmul("kmm", v, rows, cols, n, x, y)
+        r = oracle.matvec_f64(DTYPE_Q4_K, w, rows, cols, x, n)
+        rms = float(np.sqrt(np.mean(r ** 2)))
+        peor = float(np.max(np.abs(y - r))) / (1.0 + rms)
+        assert peor < 8e-3, f"Q4_K n={n}: {peor}"
+
+
 # ------------------------------------------------------ BASELINE shapes
 SHAPES = [
     (DTYPE_Q8_0, 4096, 4096, "C1"),
