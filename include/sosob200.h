@@ -122,6 +122,16 @@ typedef struct {
     const float *shared_gate;
 } sb_moe_plan;
 
+/* Multi-head latent attention of one layer (arch.rs:51-202, attn.rs:306-404): q_down
+ * [q_rank x hidden], q_up [heads*(qk_nope+qk_rope) x q_rank], kv_down [kv_rank x hidden],
+ * k_up [kv_heads*(qk_nope+qk_rope) x kv_rank], v_up [kv_heads*v_dim x kv_rank]; q rows per
+ * head are nope then rope.  The layer's KV cache is the reference's latent cache
+ * ([ctx][kv_rank] f16, kv.rs:293-315) plus the rope keys [ctx][kv_heads][qk_rope] f32. */
+typedef struct {
+    size_t q_rank, kv_rank, qk_nope, qk_rope, v_dim;
+    sb_mat q_down, q_up, kv_down, k_up, v_up;
+} sb_mla_plan;
+
 /* One layer: `CapaDec` (gpu.rs:138-148) with GQA attention (`GatedDec`, gpu.rs:113-122;
  * bias and QK-norm as layer.rs:1146-1181, RoPE as layer.rs:1184-1193) and a dense SwiGLU
  * FFN (layer.rs:1352-1389) or, when moe != NULL, a MoE FFN. */
@@ -135,6 +145,7 @@ typedef struct {
     sb_mat q, k, v, o;
     sb_mat gate, up, down;
     const sb_moe_plan *moe;
+    const sb_mla_plan *mla; /* when set: MLA attention (q, k, v unused; o = attn_output) */
 } sb_layer_plan;
 
 /* `DecodePlan` (gpu.rs:150-158) plus the embedding table (for device-side greedy
@@ -297,6 +308,24 @@ size_t sbk_argmax_ws_bytes(void);
 /* Greedy token: index of the maximum, ties to the LAST index like
  * Runtime::argmax (crates/soso-llm-core/src/runtime.rs:2021-2028). */
 int sbk_argmax(const float *v, size_t n, int32_t *out, void *ws, int pdl, void *stream);
+
+/* MLA decode in the absorbed form (mathematically the reference's re-expansion,
+ * attention_decode_mla_latent, crates/soso-llm-core/src/attn.rs:306-404; the reference
+ * has no GPU kernel for MLA).  sbk_mla_absorb, one CTA per head: appends this token's
+ * latent row c (f16, the reference's rounding) at *pos, its rope keys
+ * rope_pos(W_kr . c) per kv head, the roped q slice qr[heads][qk_rope] and the absorbed
+ * query qt[heads][kv_rank] = W_kn^T q_nope (W_kn, W_kr = head's nope / rope rows of the
+ * Q4_K k_up).  sbk_mla_attn: cbar[heads][kv_rank] = sum_t softmax_t(qt.c_t + qr.kr_t) c_t
+ * / scaled by 1/sqrt(qk_nope+qk_rope); the output of a head is then W_v,h . cbar_h.
+ * heads <= 16, kv_rank a multiple of 512 (<= 1024), qk_rope even (<= 128).  ws: at least
+ * sbk_mla_ws_bytes(heads, kv_rank), zero-filled before first use (left zeroed). */
+size_t sbk_mla_ws_bytes(size_t heads, size_t kv_rank);
+int sbk_mla_absorb(const float *q, const float *c, const void *k_up, uint8_t k_up_dtype, uint16_t *latent,
+                   float *krope, float *qt, float *qr, const int32_t *pos, size_t heads, size_t kv_heads,
+                   size_t kv_rank, size_t qk_nope, size_t qk_rope, size_t ctx, float theta, int pdl, void *stream);
+int sbk_mla_attn(const float *qt, const float *qr, const uint16_t *latent, const float *krope, float *cbar,
+                 const int32_t *pos, size_t heads, size_t kv_heads, size_t kv_rank, size_t qk_nope, size_t qk_rope,
+                 size_t ctx, void *ws, int pdl, void *stream);
 
 /* One embedding row (dtype F32 / Q8_0 / Q4_K / Q6_K) dequantised exactly
  * (Runtime::embed_token, crates/soso-llm-core/src/runtime.rs:787-802). */

@@ -22,6 +22,7 @@ class DenseOracle:
         self.k = [np.zeros((cfg.ctx, cfg.kv_dim), np.uint16) for _ in range(cfg.n_layers)]
         self.v = [np.zeros((cfg.ctx, cfg.kv_dim), np.uint16) for _ in range(cfg.n_layers)]
         self._embd = None
+        self._mla_kv = [dict() for _ in range(cfg.n_layers)]  # (layer) t -> expanded (k, v) of latent row t
 
     def _mv(self, name: str, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
         dt = self.cfg.dtypes[name.split(".")[-1]]  # by tensor kind (experts share their kind's dtype)
@@ -43,6 +44,30 @@ class DenseOracle:
         h = np.array(h, np.float32, copy=True)
         for l in range(cfg.n_layers):
             p = f"blk.{l}."
+            if getattr(cfg, "mla", False):
+                h = (h + self._mla(p, oracle.rmsnorm(h, m[p + "attn_norm"], cfg.eps), l, pos)).astype(np.float32)
+            else:
+                h = self._gqa(p, h, l, pos)
+            xn = oracle.rmsnorm(h, m[p + "ffn_norm"], cfg.eps)
+            if getattr(cfg, "n_exp", 0) and l >= cfg.first_moe:
+                h = (self._moe(p, xn, l) + h).astype(np.float32)  # hidden = moe_acc; += residual (:1389)
+                continue
+            # dense FFN (layer.rs:1300-1389)
+            gate = self._mv(p + "ffn_gate", xn, cfg.ffn, H)
+            up = self._mv(p + "ffn_up", xn, cfg.ffn, H)
+            act = oracle.swiglu(up, gate)
+            down = self._mv(p + "ffn_down", act, H, cfg.ffn)
+            h = (h + down).astype(np.float32)  # add_assign_f32 (layer.rs:1391)
+        # logits (runtime.rs:1976-2019)
+        hn = oracle.rmsnorm(h, m["output_norm"], cfg.eps)
+        return self._mv("output", hn, cfg.vocab, H)
+
+    def _gqa(self, p: str, h: np.ndarray, l: int, pos: int) -> np.ndarray:
+        """GQA attention block (layer.rs:1088-1296): returns h + attention output."""
+        cfg, m = self.cfg, self.m
+        H, qd, kvd, hd = cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.head_dim
+        group = cfg.heads // cfg.kv_heads
+        if True:
             # attention block (layer.rs:1088-1283)
             xn = oracle.rmsnorm(h, m[p + "attn_norm"], cfg.eps)
             q = self._mv(p + "attn_q", xn, qd, H)
@@ -67,20 +92,48 @@ class DenseOracle:
                                             kvd, i // group, pos + 1)
                 for i in range(cfg.heads)])
             o = self._mv(p + "attn_output", att, H, qd)
-            h = (h + o).astype(np.float32)  # add_f32 (layer.rs:1296)
-            xn = oracle.rmsnorm(h, m[p + "ffn_norm"], cfg.eps)
-            if getattr(cfg, "n_exp", 0) and l >= cfg.first_moe:
-                h = (self._moe(p, xn, l) + h).astype(np.float32)  # hidden = moe_acc; += residual (:1389)
-                continue
-            # dense FFN (layer.rs:1300-1389)
-            gate = self._mv(p + "ffn_gate", xn, cfg.ffn, H)
-            up = self._mv(p + "ffn_up", xn, cfg.ffn, H)
-            act = oracle.swiglu(up, gate)
-            down = self._mv(p + "ffn_down", act, H, cfg.ffn)
-            h = (h + down).astype(np.float32)  # add_assign_f32 (layer.rs:1391)
-        # logits (runtime.rs:1976-2019)
-        hn = oracle.rmsnorm(h, m["output_norm"], cfg.eps)
-        return self._mv("output", hn, cfg.vocab, H)
+            return (h + o).astype(np.float32)  # add_f32 (layer.rs:1296)
+
+    def _mla(self, p: str, xn: np.ndarray, l: int, pos: int) -> np.ndarray:
+        """forward_mla_attn (arch.rs:51-202) with attention_decode_mla_latent (attn.rs:306-404),
+        restated with q and k rows per head of qk_nope + qk_rope (nope first): the latent row
+        c = kv_down . xn is cached as f16; every cached row is re-expanded k = k_up . c_t (RoPE,
+        llama pairs, on each head's rope slice at position t) and v = v_up . c_t; softmax in the
+        reference's order; returns the attention output projected by attn_output."""
+        cfg, m, H = self.cfg, self.m, self.cfg.hidden
+        qk = cfg.qk_nope + cfg.qk_rope
+        group = cfg.heads // cfg.kv_heads
+        cq = self._mv(p + "attn_q_down", xn, cfg.q_rank, H)
+        q = self._mv(p + "attn_q_up", cq, cfg.heads * qk, cfg.q_rank)
+        c = self._mv(p + "attn_kv_down", xn, cfg.kv_rank, H)
+        for hh in range(cfg.heads):
+            s0 = hh * qk + cfg.qk_nope
+            q[s0:s0 + cfg.qk_rope] = oracle.rope_llama_n(q[s0:s0 + cfg.qk_rope], pos, cfg.theta, cfg.qk_rope)
+        self.k[l][pos] = oracle.f32_to_f16_array(c)  # append_mla_latent (kv.rs:293-315)
+        cache = self._mla_kv[l]
+        for t in range(pos + 1):
+            if t not in cache:
+                ct = self.k[l][t].view(np.float16).astype(np.float32)
+                kf = self._mv(p + "attn_k_up", ct, cfg.kv_heads * qk, cfg.kv_rank)
+                for g in range(cfg.kv_heads):
+                    s0 = g * qk + cfg.qk_nope
+                    kf[s0:s0 + cfg.qk_rope] = oracle.rope_llama_n(kf[s0:s0 + cfg.qk_rope], t, cfg.theta, cfg.qk_rope)
+                vf = self._mv(p + "attn_v_up", ct, cfg.kv_heads * cfg.v_dim, cfg.kv_rank)
+                cache[t] = (kf, vf)
+        inv = np.float32(1.0 / np.sqrt(np.float32(qk)))
+        att = np.zeros(cfg.heads * cfg.v_dim, np.float32)
+        for hh in range(cfg.heads):
+            g = hh // group
+            qh = q[hh * qk:(hh + 1) * qk]
+            lg = np.array([np.float32(np.dot(qh, cache[t][0][g * qk:(g + 1) * qk])) * inv for t in range(pos + 1)],
+                          np.float32)
+            lg = np.exp(lg - lg.max()).astype(np.float32)
+            lg = (lg / lg.sum()).astype(np.float32)
+            out = np.zeros(cfg.v_dim, np.float32)
+            for t in range(pos + 1):
+                out = (out + lg[t] * cache[t][1][g * cfg.v_dim:(g + 1) * cfg.v_dim]).astype(np.float32)
+            att[hh * cfg.v_dim:(hh + 1) * cfg.v_dim] = out
+        return self._mv(p + "attn_output", att, H, cfg.q_dim)
 
     def _moe(self, p: str, xn: np.ndarray, l: int) -> np.ndarray:
         """forward_moe_ffn / moe_expertos_agrupados (layer.rs:1938-1972, :1862-1935): router

@@ -50,11 +50,17 @@ class SbMoePlan(ctypes.Structure):
                 ("experts", ctypes.POINTER(SbMat)), ("shared", ctypes.POINTER(SbMat)), ("shared_gate", c_f32p)]
 
 
+class SbMlaPlan(ctypes.Structure):
+    _fields_ = [("q_rank", c_size), ("kv_rank", c_size), ("qk_nope", c_size), ("qk_rope", c_size), ("v_dim", c_size),
+                ("q_down", SbMat), ("q_up", SbMat), ("kv_down", SbMat), ("k_up", SbMat), ("v_up", SbMat)]
+
+
 class SbLayerPlan(ctypes.Structure):
     _fields_ = [("heads", c_size), ("kv_heads", c_size), ("head_dim", c_size), ("theta", ctypes.c_float),
                 ("neox", ctypes.c_int), ("q_norm", c_f32p), ("k_norm", c_f32p), ("qkv_bias", c_f32p),
                 ("norm_attn", c_f32p), ("norm_ffn", c_f32p), ("q", SbMat), ("k", SbMat), ("v", SbMat), ("o", SbMat),
-                ("gate", SbMat), ("up", SbMat), ("down", SbMat), ("moe", ctypes.POINTER(SbMoePlan))]
+                ("gate", SbMat), ("up", SbMat), ("down", SbMat), ("moe", ctypes.POINTER(SbMoePlan)),
+                ("mla", ctypes.POINTER(SbMlaPlan))]
 
 
 class SbDecodePlan(ctypes.Structure):
@@ -112,6 +118,11 @@ SIGNATURES = {
                                               ctypes.c_void_p]),
     "sbk_num_sms": (ctypes.c_int, [ctypes.c_int]),
     "sbk_matmul_ws_bytes": (c_size, [c_size, c_size]),
+    "sbk_mla_ws_bytes": (c_size, [c_size, c_size]),
+    "sbk_mla_absorb": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_uint8] + [ctypes.c_void_p] * 5 +
+                       [c_size] * 6 + [ctypes.c_float, ctypes.c_int, ctypes.c_void_p]),
+    "sbk_mla_attn": (ctypes.c_int, [ctypes.c_void_p] * 6 + [c_size] * 6 + [ctypes.c_void_p, ctypes.c_int,
+                                                                         ctypes.c_void_p]),
     "sbk_matmul": (ctypes.c_int, [ctypes.c_uint8, ctypes.c_void_p, c_size, c_size, c_size, ctypes.c_void_p,
                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "sbk_take_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),

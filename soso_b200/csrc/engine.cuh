@@ -57,26 +57,20 @@ __global__ void swiglu_kernel(const float *__restrict__ g, const float *__restri
     griddep_launch();
 }
 
-// New K/V rows (at *pos) of every layer into one contiguous [layer][k | v] buffer.
-struct KvRowsArgs {
-    const uint16_t *const *kc;
-    const uint16_t *const *vc;
-    const int *kvd;
-    const long long *off;
-    int n_layers;
-    const int *pos;
-    uint16_t *out;
+// This token's cache rows of every layer into one contiguous buffer, in layer order:
+// [k | v] for an attention layer, the latent row for an MLA layer.  One CTA per segment.
+struct KvSeg {
+    const uint16_t *src;  // cache [ctx][width]
+    long long dst_off;
+    int width, pad;
 };
 
-__global__ void kv_rows_kernel(KvRowsArgs a)
+__global__ void kv_rows_kernel(const KvSeg *segs, const int *pos, uint16_t *out)
 {
     griddep_wait();
-    const int l = blockIdx.x, d = a.kvd[l], p = *a.pos;
-    uint16_t *o = a.out + a.off[l];
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        o[i] = a.kc[l][(long long)p * d + i];
-        o[d + i] = a.vc[l][(long long)p * d + i];
-    }
+    const KvSeg g = segs[blockIdx.x];
+    const long long p = *pos;
+    for (int i = threadIdx.x; i < g.width; i += blockDim.x) out[g.dst_off + i] = g.src[p * g.width + i];
 }
 
 // MoE routing of one token on the device, between the router matvec and the expert
@@ -223,6 +217,12 @@ struct EngLayer {
     sb::tcmv::Batch *dn_b = nullptr;   //   the first enqueue; the route kernel picks the maps)
     size_t gu_smem = 0, dn_smem = 0;
     const float *built_for = nullptr;  // residual buffer the batches read
+    // MLA attention (sb_mla_plan): latent cache + rope keys instead of K/V rows
+    bool mla = false;
+    size_t q_rank = 0, kv_rank = 0, qk_nope = 0, qk_rope = 0, v_dim = 0;
+    EngMat q_down, q_up, kv_down, k_up, v_up;
+    uint16_t *latent = nullptr;
+    float *krope = nullptr;
 };
 
 }  // namespace
@@ -239,11 +239,17 @@ struct sb_engine {
     float *rlog = nullptr, *wts = nullptr, *egu = nullptr, *ys = nullptr;
     int *ridx = nullptr;
     size_t moe_slots = 0, moe_ffn = 0, n_exp_max = 0;
+    // MLA: q_down | kv_down outputs, q_up output, absorbed query, roped q slice, latent sums
+    float *mcq = nullptr, *mc = nullptr, *mq = nullptr, *mqt = nullptr, *mqr = nullptr, *mcbar = nullptr;
+    size_t mla_q = 0, mla_r = 0, mla_qq = 0, mla_hr = 0, mla_hp = 0;
+    void *mla_ws = nullptr;
+    size_t mla_ws_bytes = 0;
+    void *kv_segs = nullptr;
+    size_t n_kv_segs = 0;
     int *ints = nullptr;  // pos, tok, step, n_prompt
     int *prompt = nullptr, *hist = nullptr;
     void *attn_ws = nullptr, *am_ws = nullptr;
     uint16_t *kv_rows = nullptr;
-    void *kv_meta = nullptr;
     std::vector<void *> allocs;
     cudaGraphExec_t g_tok = nullptr, g_greedy = nullptr;
     size_t launches_per_token = 0;
@@ -443,18 +449,53 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
     };
     for (size_t l = 0; l < e->L.size(); l++) {
         EngLayer &L = e->L[l];
-        // attention block: h (+ previous FFN output) -> rmsnorm -> q|k|v
-        {
-            sbk_xsrc xs = norm_src(L.na, l ? ho : nullptr);
-            if (!l) xs.res = nullptr;
-            const EngMat *ms[3] = {&L.q, &L.k, &L.v};
-            float *ys[3] = {e->qkv, e->qkv + L.qd, e->qkv + L.qd + L.kvd};
-            ENG_MV(ms, ys, 3, hc, xs);
-            if (l) std::swap(hc, ho);
-            moe_ny = 0;
+        if (L.mla) {
+            // MLA block: h (+ previous FFN output) -> rmsnorm -> q_down | kv_down; q_up;
+            // absorbed query + latent / rope-key append; attention over the latent cache;
+            // per head W_v,h . cbar_h
+            {
+                sbk_xsrc xs = norm_src(L.na, l ? ho : nullptr);
+                if (!l) xs.res = nullptr;
+                const EngMat *ms[2] = {&L.q_down, &L.kv_down};
+                float *ys[2] = {e->mcq, e->mc};
+                ENG_MV(ms, ys, 2, hc, xs);
+                if (l) std::swap(hc, ho);
+                moe_ny = 0;
+            }
+            {
+                const sbk_xsrc xs{};
+                const EngMat *ms[1] = {&L.q_up};
+                float *ys[1] = {e->mq};
+                ENG_MV(ms, ys, 1, e->mcq, xs);
+            }
+            ENG_CHECK(sbk_mla_absorb(e->mq, e->mc, L.k_up.w, L.k_up.dt, L.latent, L.krope, e->mqt, e->mqr, pos,
+                                     L.heads, L.kvh, L.kv_rank, L.qk_nope, L.qk_rope, e->ctx, L.theta, 1, s));
+            ENG_CHECK(sbk_mla_attn(e->mqt, e->mqr, L.latent, L.krope, e->mcbar, pos, L.heads, L.kvh, L.kv_rank,
+                                   L.qk_nope, L.qk_rope, e->ctx, e->mla_ws, 1, s));
+            {
+                const size_t rb = sbk_row_bytes(L.v_up.dt, L.kv_rank);
+                sbk_mv_op ops[sb::mla::MAXH];
+                for (size_t h = 0; h < L.heads; h++) {
+                    const size_t kvh = h / (L.heads / L.kvh);
+                    ops[h] = sbk_mv_op{(const uint8_t *)L.v_up.w + kvh * L.v_dim * rb, L.v_dim, L.kv_rank,
+                                       e->mcbar + h * L.kv_rank, e->att + h * L.v_dim};
+                }
+                ENG_CHECK(sbk_matvec_batch(L.v_up.dt, ops, L.heads, 1, s));
+            }
+        } else {
+            // attention block: h (+ previous FFN output) -> rmsnorm -> q|k|v
+            {
+                sbk_xsrc xs = norm_src(L.na, l ? ho : nullptr);
+                if (!l) xs.res = nullptr;
+                const EngMat *ms[3] = {&L.q, &L.k, &L.v};
+                float *ys[3] = {e->qkv, e->qkv + L.qd, e->qkv + L.qd + L.kvd};
+                ENG_MV(ms, ys, 3, hc, xs);
+                if (l) std::swap(hc, ho);
+                moe_ny = 0;
+            }
+            ENG_CHECK(sbk_attn_rope_decode(e->qkv, L.bias, L.qn, L.kn, L.kc, L.vc, e->att, pos, L.heads, L.kvh, L.hd,
+                                           e->ctx, L.theta, e->eps, L.neox, e->attn_ws, 1, s));
         }
-        ENG_CHECK(sbk_attn_rope_decode(e->qkv, L.bias, L.qn, L.kn, L.kc, L.vc, e->att, pos, L.heads, L.kvh, L.hd,
-                                       e->ctx, L.theta, e->eps, L.neox, e->attn_ws, 1, s));
         {
             const sbk_xsrc xs{};
             const EngMat *ms[1] = {&L.o};
@@ -501,13 +542,7 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
     if (greedy) {
         ENG_CHECK(sb::argmax_launch(e->logits, e->V, tok, e->am_ws, 1, s, pos, step, e->hist, e->prompt, np));
     } else {
-        const sb::KvRowsArgs a{(const uint16_t *const *)e->kv_meta,
-                               (const uint16_t *const *)e->kv_meta + e->L.size(),
-                               (const int *)((const uint16_t *const *)e->kv_meta + 2 * e->L.size()),
-                               (const long long *)((const char *)e->kv_meta + 2 * e->L.size() * 8 +
-                                                   ((e->L.size() * 4 + 7) & ~(size_t)7)),
-                               (int)e->L.size(), pos, e->kv_rows};
-        sb::kv_rows_kernel<<<(unsigned)e->L.size(), 256, 0, s>>>(a);
+        sb::kv_rows_kernel<<<(unsigned)e->n_kv_segs, 256, 0, s>>>((const sb::KvSeg *)e->kv_segs, pos, e->kv_rows);
         if (cudaGetLastError() != cudaSuccess) return fail("decode step: kv rows launch failed");
         n++;
     }
@@ -566,13 +601,42 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         EngLayer &L = e->L[l];
         if (!lp.norm_attn || !lp.norm_ffn) return bail(fail("decode plan: layer without norms"));
         L.heads = lp.heads, L.kvh = lp.kv_heads, L.hd = lp.head_dim, L.theta = lp.theta, L.neox = lp.neox;
-        if (!L.heads || !L.kvh || L.heads % L.kvh || L.hd != 128 || L.heads / L.kvh > 8) return bail(0);
-        L.qd = L.heads * L.hd, L.kvd = L.kvh * L.hd;
         int rc;
-        if ((rc = eng_mat(c, lp.q, L.qd, H, &L.q, true)) != 1) return bail(rc);
-        if ((rc = eng_mat(c, lp.k, L.kvd, H, &L.k, true)) != 1) return bail(rc);
-        if ((rc = eng_mat(c, lp.v, L.kvd, H, &L.v, true)) != 1) return bail(rc);
-        if ((rc = eng_mat(c, lp.o, H, L.qd, &L.o, true)) != 1) return bail(rc);
+        if (lp.mla) {
+            // MLA: latent cache + rope keys; attention output heads * v_dim wide
+            const sb_mla_plan &ml = *lp.mla;
+            L.mla = true, L.q_rank = ml.q_rank, L.kv_rank = ml.kv_rank, L.qk_nope = ml.qk_nope;
+            L.qk_rope = ml.qk_rope, L.v_dim = ml.v_dim;
+            if (!L.heads || !L.kvh || L.heads % L.kvh || L.heads > (size_t)sb::mla::MAXH || L.kv_rank % 512 ||
+                L.kv_rank > (size_t)sb::mla::MAXR || !L.qk_nope || !L.qk_rope || L.qk_rope % 2 ||
+                L.qk_rope > (size_t)sb::mla::MAXRP || !L.v_dim || !L.q_rank)
+                return bail(0);
+            const size_t qk = L.qk_nope + L.qk_rope;
+            L.qd = L.heads * L.v_dim;  // attention output width
+            if ((rc = eng_mat(c, ml.q_down, L.q_rank, H, &L.q_down, true)) != 1) return bail(rc);
+            if ((rc = eng_mat(c, ml.q_up, L.heads * qk, L.q_rank, &L.q_up, true)) != 1) return bail(rc);
+            if ((rc = eng_mat(c, ml.kv_down, L.kv_rank, H, &L.kv_down, true)) != 1) return bail(rc);
+            if ((rc = eng_mat(c, ml.k_up, L.kvh * qk, L.kv_rank, &L.k_up, true)) != 1) return bail(rc);
+            if ((rc = eng_mat(c, ml.v_up, L.kvh * L.v_dim, L.kv_rank, &L.v_up, true)) != 1) return bail(rc);
+            if (L.k_up.dt != SB_DTYPE_Q4_K) return bail(0);  // the absorption reads Q4_K rows
+            if ((rc = eng_mat(c, lp.o, H, L.qd, &L.o, true)) != 1) return bail(rc);
+            L.latent = (uint16_t *)e->dalloc(e->ctx * L.kv_rank * 2, &err);
+            if (err == cudaSuccess) L.krope = (float *)e->dalloc(e->ctx * L.kvh * L.qk_rope * 4, &err);
+            if (err != cudaSuccess) return bail(fail("cudaMalloc(latent cache)", err));
+            e->mla_q = std::max(e->mla_q, L.q_rank);
+            e->mla_r = std::max(e->mla_r, L.kv_rank);
+            e->mla_qq = std::max(e->mla_qq, L.heads * qk);
+            e->mla_hr = std::max(e->mla_hr, L.heads * L.kv_rank);
+            e->mla_hp = std::max(e->mla_hp, L.heads * L.qk_rope);
+            e->mla_ws_bytes = std::max(e->mla_ws_bytes, sbk_mla_ws_bytes(L.heads, L.kv_rank));
+        } else {
+            if (!L.heads || !L.kvh || L.heads % L.kvh || L.hd != 128 || L.heads / L.kvh > 8) return bail(0);
+            L.qd = L.heads * L.hd, L.kvd = L.kvh * L.hd;
+            if ((rc = eng_mat(c, lp.q, L.qd, H, &L.q, true)) != 1) return bail(rc);
+            if ((rc = eng_mat(c, lp.k, L.kvd, H, &L.k, true)) != 1) return bail(rc);
+            if ((rc = eng_mat(c, lp.v, L.kvd, H, &L.v, true)) != 1) return bail(rc);
+            if ((rc = eng_mat(c, lp.o, H, L.qd, &L.o, true)) != 1) return bail(rc);
+        }
         if (lp.moe) {
             // MoE FFN: every expert resident, its tensor map in a device table
             const sb_moe_plan &mp = *lp.moe;
@@ -627,13 +691,18 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             upload_f32(e, lp.q_norm, L.hd, &L.qn) || upload_f32(e, lp.k_norm, L.hd, &L.kn) ||
             upload_f32(e, lp.qkv_bias, L.qd + 2 * L.kvd, &L.bias))
             return bail(-1);
-        L.kc = (uint16_t *)e->dalloc(e->ctx * L.kvd * 2, &err);
-        if (err == cudaSuccess) L.vc = (uint16_t *)e->dalloc(e->ctx * L.kvd * 2, &err);
-        if (err != cudaSuccess) return bail(fail("cudaMalloc(kv cache)", err));
+        if (L.mla) {
+            e->kv_rows_total += L.kv_rank;
+            e->qkv_max = std::max(e->qkv_max, L.qd);
+        } else {
+            L.kc = (uint16_t *)e->dalloc(e->ctx * L.kvd * 2, &err);
+            if (err == cudaSuccess) L.vc = (uint16_t *)e->dalloc(e->ctx * L.kvd * 2, &err);
+            if (err != cudaSuccess) return bail(fail("cudaMalloc(kv cache)", err));
+            e->qkv_max = std::max(e->qkv_max, L.qd + 2 * L.kvd);
+            e->kv_rows_total += 2 * L.kvd;
+            attn_ws = std::max(attn_ws, sbk_attn_ws_bytes(L.heads, L.kvh, L.hd, e->ctx));
+        }
         e->ffn_max = std::max(e->ffn_max, L.ffn);
-        e->qkv_max = std::max(e->qkv_max, L.qd + 2 * L.kvd);
-        e->kv_rows_total += 2 * L.kvd;
-        attn_ws = std::max(attn_ws, sbk_attn_ws_bytes(L.heads, L.kvh, L.hd, e->ctx));
     }
     int rc;
     if ((rc = eng_mat(c, p->lm_head, e->V, H, &e->lm, true)) != 1) return bail(rc);
@@ -660,37 +729,56 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         e->egu = fbuf(2 * e->moe_slots * e->moe_ffn);
         e->ys = fbuf(e->moe_slots * H);
     }
+    if (e->mla_r) {
+        e->mcq = fbuf(e->mla_q);
+        e->mc = fbuf(e->mla_r);
+        e->mq = fbuf(e->mla_qq);
+        e->mqt = fbuf(e->mla_hr);
+        e->mqr = fbuf(e->mla_hp);
+        e->mcbar = fbuf(e->mla_hr);
+        e->mla_ws = e->dalloc(e->mla_ws_bytes, &err);
+    }
     e->ints = (int *)e->dalloc(64, &err);
     e->prompt = (int *)e->dalloc(e->ctx * 4, &err);
     e->hist = (int *)e->dalloc(e->ctx * 4, &err);
     e->attn_ws = e->dalloc(attn_ws, &err);
     e->am_ws = e->dalloc(sbk_argmax_ws_bytes(), &err);
     e->kv_rows = (uint16_t *)e->dalloc(e->kv_rows_total * 2, &err);
-    const size_t nl = e->L.size(), meta = 2 * nl * 8 + ((nl * 4 + 7) & ~(size_t)7) + nl * 8;
-    e->kv_meta = e->dalloc(meta, &err);
-    if (err != cudaSuccess) return bail(fail("cudaMalloc(decode buffers)", err));
     {
-        std::vector<char> m(meta, 0);
-        const uint16_t **kc = (const uint16_t **)m.data(), **vc = kc + nl;
-        int *kvd = (int *)(m.data() + 2 * nl * 8);
-        long long *off = (long long *)(m.data() + 2 * nl * 8 + ((nl * 4 + 7) & ~(size_t)7));
+        std::vector<sb::KvSeg> segs;
         long long o = 0;
-        for (size_t l = 0; l < nl; l++) {
-            kc[l] = e->L[l].kc, vc[l] = e->L[l].vc, kvd[l] = (int)e->L[l].kvd, off[l] = o;
-            o += 2 * (long long)e->L[l].kvd;
+        for (auto &L : e->L) {
+            if (L.mla) {
+                segs.push_back(sb::KvSeg{L.latent, o, (int)L.kv_rank, 0});
+                o += (long long)L.kv_rank;
+            } else {
+                segs.push_back(sb::KvSeg{L.kc, o, (int)L.kvd, 0});
+                segs.push_back(sb::KvSeg{L.vc, o + (long long)L.kvd, (int)L.kvd, 0});
+                o += 2 * (long long)L.kvd;
+            }
         }
-        if ((err = cudaMemcpy(e->kv_meta, m.data(), meta, cudaMemcpyHostToDevice)) != cudaSuccess)
-            return bail(fail("cudaMemcpy(kv meta)", err));
+        e->n_kv_segs = segs.size();
+        e->kv_segs = e->dalloc(segs.size() * sizeof(sb::KvSeg), &err);
+        if (err != cudaSuccess) return bail(fail("cudaMalloc(kv segments)", err));
+        if ((err = cudaMemcpy(e->kv_segs, segs.data(), segs.size() * sizeof(sb::KvSeg), cudaMemcpyHostToDevice)) !=
+            cudaSuccess)
+            return bail(fail("cudaMemcpy(kv segments)", err));
     }
     // zeroed state; one eager token of each kind (sets kernel attributes, creates the
     // per-stream matvec workspace outside any capture), then capture, then re-zero
     auto zero_state = [&]() {
         cudaError_t z = cudaMemsetAsync(e->ints, 0, 64, c->stream);
         for (auto &L : e->L) {
+            if (L.mla) {
+                if (z == cudaSuccess) z = cudaMemsetAsync(L.latent, 0, e->ctx * L.kv_rank * 2, c->stream);
+                if (z == cudaSuccess) z = cudaMemsetAsync(L.krope, 0, e->ctx * L.kvh * L.qk_rope * 4, c->stream);
+                continue;
+            }
             if (z == cudaSuccess) z = cudaMemsetAsync(L.kc, 0, e->ctx * L.kvd * 2, c->stream);
             if (z == cudaSuccess) z = cudaMemsetAsync(L.vc, 0, e->ctx * L.kvd * 2, c->stream);
         }
-        if (z == cudaSuccess) z = cudaMemsetAsync(e->attn_ws, 0, attn_ws, c->stream);
+        if (z == cudaSuccess && e->mla_ws) z = cudaMemsetAsync(e->mla_ws, 0, e->mla_ws_bytes, c->stream);
+        if (z == cudaSuccess && attn_ws) z = cudaMemsetAsync(e->attn_ws, 0, attn_ws, c->stream);
         if (z == cudaSuccess) z = cudaMemsetAsync(e->am_ws, 0, sbk_argmax_ws_bytes(), c->stream);
         if (z == cudaSuccess) z = cudaMemsetAsync(e->h, 0, H * 4, c->stream);
         if (z == cudaSuccess) z = cudaStreamSynchronize(c->stream);

@@ -4,6 +4,7 @@
 #include "matvec.cuh"
 #include "norm.cuh"
 #include "decode_ops.cuh"
+#include "mla.cuh"
 #include "dispatch.cuh"
 #include "engine.cuh"
 #include "noalloc.cuh"

@@ -14,8 +14,8 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import synth
-from ._lib import (SbDecodePlan, SbLayerPlan, SbMat, SbMoePlan, SbView, SbError, c_f32p, c_u8p, last_error,
-                   lib)
+from ._lib import (SbDecodePlan, SbLayerPlan, SbMat, SbMlaPlan, SbMoePlan, SbView, SbError, c_f32p, c_u8p,
+                   last_error, lib)
 from .formats import DTYPE_Q4_K, DTYPE_Q6_K
 
 
@@ -38,6 +38,14 @@ class DenseConfig:
     # MoE FFN on layers >= first_moe when n_exp > 0 (forward_moe_ffn, layer.rs:1938-2109):
     # n_exp routed experts of width moe_ffn, top_k chosen per token, and an optional shared
     # expert of width shared_ffn (gated by sigmoid(ffn_gate_inp_shexp . x) when shared_gate)
+    # MLA attention (arch.rs:51-202) on every layer when mla: q_down / q_up (q-LoRA),
+    # kv_down to a kv_rank latent, k_up / v_up; q and k rows per head nope then rope
+    mla: bool = False
+    q_rank: int = 0
+    kv_rank: int = 0
+    qk_nope: int = 0
+    qk_rope: int = 0
+    v_dim: int = 0
     n_exp: int = 0
     top_k: int = 0
     moe_ffn: int = 0
@@ -52,11 +60,13 @@ class DenseConfig:
 
     @property
     def q_dim(self) -> int:
-        return self.heads * self.head_dim
+        """width of the attention output (heads * v_dim for MLA)"""
+        return self.heads * (self.v_dim if self.mla else self.head_dim)
 
     @property
     def kv_dim(self) -> int:
-        return self.kv_heads * self.head_dim
+        """width of one layer's cache row (the latent row for MLA)"""
+        return self.kv_rank if self.mla else self.kv_heads * self.head_dim
 
     def is_moe(self, layer: int) -> bool:
         return self.n_exp > 0 and layer >= self.first_moe
@@ -69,7 +79,8 @@ QWEN25_3B = DenseConfig(n_layers=36, hidden=2048, heads=16, kv_heads=2, head_dim
 TINY = DenseConfig(n_layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1024, ctx=160)
 
 _ALL_Q4K = {k: DTYPE_Q4_K for k in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down",
-                                    "output", "token_embd", "ffn_gate_inp")}
+                                    "output", "token_embd", "ffn_gate_inp", "attn_q_down", "attn_q_up",
+                                    "attn_kv_down", "attn_k_up", "attn_v_up")}
 # Qwen3-30B-A3B-style MoE decoder, all Q4_K, QK-norm, fp16 KV at 2048
 QWEN3_30B_A3B = DenseConfig(n_layers=48, hidden=2048, heads=32, kv_heads=4, head_dim=128, ffn=0, vocab=151936,
                             ctx=2048, qkv_bias=False, qk_norm=True, n_exp=128, top_k=8, moe_ffn=768,
@@ -79,6 +90,12 @@ QWEN3_30B_A3B = DenseConfig(n_layers=48, hidden=2048, heads=32, kv_heads=4, head
 TINY_MOE = DenseConfig(n_layers=3, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1024, ctx=96,
                        qkv_bias=False, qk_norm=True, n_exp=16, top_k=4, moe_ffn=256, first_moe=1, shared_ffn=512,
                        shared_gate=True, dtypes=dict(_ALL_Q4K, ffn_down=DTYPE_Q6_K, output=DTYPE_Q6_K))
+# a small MLA + MoE model (configs[4]'s structure): MLA on every layer, a dense FFN first,
+# then MoE layers with an ungated shared expert
+TINY_MLA = DenseConfig(n_layers=3, hidden=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=1024, ctx=96,
+                       theta=1e4, neox=False, qkv_bias=False, mla=True, q_rank=256, kv_rank=512, qk_nope=64,
+                       qk_rope=32, v_dim=128, n_exp=8, top_k=2, moe_ffn=256, first_moe=1, shared_ffn=512,
+                       dtypes=dict(_ALL_Q4K))
 TINY_MOE_NS = DenseConfig(n_layers=2, hidden=512, heads=8, kv_heads=2, head_dim=128, ffn=0, vocab=1024, ctx=96,
                           qkv_bias=False, qk_norm=True, n_exp=32, top_k=8, moe_ffn=256, dtypes=dict(_ALL_Q4K))
 
@@ -86,6 +103,12 @@ TINY_MOE_NS = DenseConfig(n_layers=2, hidden=512, heads=8, kv_heads=2, head_dim=
 def shapes(cfg: DenseConfig) -> dict:
     """tensor name suffix -> (rows, cols)"""
     H = cfg.hidden
+    if cfg.mla:
+        qk = cfg.qk_nope + cfg.qk_rope
+        return {"attn_q_down": (cfg.q_rank, H), "attn_q_up": (cfg.heads * qk, cfg.q_rank),
+                "attn_kv_down": (cfg.kv_rank, H), "attn_k_up": (cfg.kv_heads * qk, cfg.kv_rank),
+                "attn_v_up": (cfg.kv_heads * cfg.v_dim, cfg.kv_rank), "attn_output": (H, cfg.q_dim),
+                "ffn_gate": (cfg.ffn, H), "ffn_up": (cfg.ffn, H), "ffn_down": (H, cfg.ffn)}
     return {"attn_q": (cfg.q_dim, H), "attn_k": (cfg.kv_dim, H), "attn_v": (cfg.kv_dim, H),
             "attn_output": (H, cfg.q_dim), "ffn_gate": (cfg.ffn, H), "ffn_up": (cfg.ffn, H),
             "ffn_down": (H, cfg.ffn)}
@@ -164,12 +187,22 @@ class DecodeSession:
             lp.norm_ffn = _f32(model[f"blk.{l}.ffn_norm"])
             for fld, name in (("q", "attn_q"), ("k", "attn_k"), ("v", "attn_v"), ("o", "attn_output"),
                               ("gate", "ffn_gate"), ("up", "ffn_up"), ("down", "ffn_down")):
-                if cfg.is_moe(l) and name.startswith("ffn_"):
+                if (cfg.is_moe(l) and name.startswith("ffn_")) or (cfg.mla and name in ("attn_q", "attn_k", "attn_v")):
                     continue
                 rows, cols = shapes(cfg)[name]
                 setattr(lp, fld, self._mat(f"blk.{l}.{name}", cfg.dtypes[name], rows, cols))
             if cfg.is_moe(l):
                 lp.moe = ctypes.pointer(self._moe_plan(l))
+            if cfg.mla:
+                mp = SbMlaPlan()
+                mp.q_rank, mp.kv_rank, mp.qk_nope, mp.qk_rope, mp.v_dim = (cfg.q_rank, cfg.kv_rank, cfg.qk_nope,
+                                                                          cfg.qk_rope, cfg.v_dim)
+                for fld in ("q_down", "q_up", "kv_down", "k_up", "v_up"):
+                    name = "attn_" + fld
+                    rows, cols = shapes(cfg)[name]
+                    setattr(mp, fld, self._mat(f"blk.{l}.{name}", cfg.dtypes[name], rows, cols))
+                self._keep.append(mp)
+                lp.mla = ctypes.pointer(mp)
         plan = SbDecodePlan()
         plan.layers = layers
         plan.n_layers = cfg.n_layers

@@ -1,0 +1,57 @@
+"""MLA decode (absorbed form) on the whole-token engine against the CPU restatement of the
+reference's MLA (forward_mla_attn + attention_decode_mla_latent, arch.rs:51-202,
+attn.rs:306-404, re-expanding K and V from the latent cache at every step).
+
+Bars: identical greedy top-1 tokens; logits within 1e-2
+relative (per logit, |gpu - cpu| <= 1e-2 * max(|cpu|, rms)); the appended latent rows
+within one f16 rounding step of the oracle's.
+"""
+import numpy as np
+import pytest
+
+from oracle.model import DenseOracle
+from soso_b200 import decode, synth
+
+pytestmark = pytest.mark.gpu
+LOGIT_REL = 1e-2
+
+
+def logits_close(g, t):
+    rms = float(np.sqrt(np.mean(t.astype(np.float64) ** 2)))
+    return float((np.abs(g.astype(np.float64) - t) / np.maximum(np.abs(t), rms)).max())
+
+
+@pytest.fixture(scope="module")
+def mla_model():
+    cfg = decode.TINY_MLA
+    return cfg, decode.synth_model(cfg, "tinymla")
+
+
+def test_mla_greedy_matches_oracle(gpu, mla_model):
+    cfg, model = mla_model
+    prompt = synth.rng("prompt", "mla").integers(0, cfg.vocab, 8).astype(np.int32)
+    sess = decode.DecodeSession(cfg, model)
+    try:
+        got = sess.greedy(prompt, 40)
+    finally:
+        sess.close()
+    want, logits = DenseOracle(cfg, model).greedy(prompt, 40)
+    gaps = [float(np.sort(lg)[-1] - np.sort(lg)[-2]) for lg in logits]
+    assert np.array_equal(got, want), (np.nonzero(got != want)[0][:5], min(gaps))
+
+
+def test_mla_decode_token_logits_and_latent_rows(gpu, mla_model):
+    cfg, model = mla_model
+    sess = decode.DecodeSession(cfg, model)
+    orc = DenseOracle(cfg, model)
+    try:
+        for pos, t in enumerate(synth.rng("toks", "mla").integers(0, cfg.vocab, 12)):
+            e = orc.embed(int(t))
+            lg, kv = sess.token(e, pos, kv_rows=True)
+            assert logits_close(lg, orc.step(e, pos)) <= LOGIT_REL, pos
+            for l in range(cfg.n_layers):
+                got = kv[l * cfg.kv_rank:(l + 1) * cfg.kv_rank].view(np.float16).astype(np.float32)
+                want = orc.k[l][pos].view(np.float16).astype(np.float32)
+                assert np.max(np.abs(got - want)) <= 2e-3 * max(1.0, float(np.abs(want).max())), (pos, l)
+    finally:
+        sess.close()

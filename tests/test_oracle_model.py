@@ -28,3 +28,27 @@ def test_tiny_moe_model_steps_route_and_stay_finite():
     idx, wts = orc.last_route
     assert len(set(idx.tolist())) == cfg.top_k and abs(float(np.sum(wts)) - 1.0) < 1e-5
     assert np.all(np.diff(wts) <= 0)  # rank order: weights descending
+
+
+def test_tiny_mla_model_steps_are_finite_and_deterministic():
+    cfg = decode.TINY_MLA
+    model = decode.synth_model(cfg, "tinymla")
+    prompt = synth.rng("prompt", "tinymla").integers(0, cfg.vocab, 3).astype(np.int32)
+    a, la = DenseOracle(cfg, model).greedy(prompt, 5)
+    b, _ = DenseOracle(cfg, model).greedy(prompt, 5)
+    assert np.array_equal(a, b) and all(np.isfinite(x).all() for x in la)
+
+
+def test_mla_absorbed_form_equals_reexpansion():
+    """The identity the MLA kernels rest on (f64, random data): q.(W_kn c) == (W_kn^T q).c and
+    sum_t p_t (W_v c_t) == W_v (sum_t p_t c_t)."""
+    g = np.random.default_rng(5)
+    nope, rank, vdim, T = 64, 512, 128, 9
+    wkn = g.standard_normal((nope, rank))
+    wv = g.standard_normal((vdim, rank))
+    q = g.standard_normal(nope)
+    c = g.standard_normal((T, rank))
+    p = g.random(T)
+    p /= p.sum()
+    assert np.allclose([q @ (wkn @ c[t]) for t in range(T)], c @ (wkn.T @ q))
+    assert np.allclose(sum(p[t] * (wv @ c[t]) for t in range(T)), wv @ (p @ c))
