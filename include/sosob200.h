@@ -48,6 +48,11 @@ extern "C" {
  * 16-byte aligned for TMA.  Made by sbk_q6k_pack; the host-buffer calls (sb_*)
  * repack Q6_K weights this way when they upload them. */
 #define SB_DTYPE_Q6_K_P 14
+/* Q8_0 with every row padded to a multiple of 16 bytes (zeros after the last block) so
+ * rows start 16-byte aligned for TMA; the same 36-byte blocks.  Rows of a multiple of 128
+ * weights need no padding (SB_DTYPE_Q8_0 rows are read as they are).  Made by sbk_q80_pad;
+ * the host-buffer calls (sb_*) hold Q8_0 weights this way.  No counterpart in the reference. */
+#define SB_DTYPE_Q8_0_R 15
 
 /* Mirror of `TensorView { bytes, dtype, elems }` (crates/soso-llm-core/src/layer.rs:26-31). */
 typedef struct {
@@ -203,6 +208,9 @@ typedef struct {
  * 16-byte aligned).  No counterpart in the reference, which converts Q6_K to
  * Q8_0 on import instead (crates/gguf2som/src/lib.rs:1592-1610). */
 int sbk_q6k_pack(const void *src, size_t rows, size_t cols, void *dst, void *stream);
+/* Copy rows x cols Q8_0 weights (reference layout, device memory) to SB_DTYPE_Q8_0_R at dst
+ * (sbk_row_bytes(SB_DTYPE_Q8_0_R, cols) * rows bytes, 16-byte aligned). */
+int sbk_q80_pad(const void *src, size_t rows, size_t cols, void *dst, void *stream);
 
 /* Independent matvecs of one dtype in as few launches as possible (Q4_K: one
  * launch per 40 matrices, their weight streams split across all SMs as one) --

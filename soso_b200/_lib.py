@@ -90,6 +90,7 @@ SIGNATURES = {
                                         ctypes.POINTER(ctypes.c_int32)]),
     "sbk_row_bytes": (c_size, [ctypes.c_uint8, c_size]),
     "sbk_q6k_pack": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p]),
+    "sbk_q80_pad": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p]),
     "sbk_swiglu": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, c_size, ctypes.c_int,
                                   ctypes.c_void_p]),
     "sbk_matvec": (ctypes.c_int, [ctypes.c_uint8, ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p,

@@ -25,6 +25,7 @@ extern "C" int sbk_rmsnorm(const float *x, const float *res, float *h_out, const
                            size_t n, float eps, void *stream);
 extern "C" int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, int pdl, void *stream);
 extern "C" int sbk_q6k_pack(const void *src, size_t rows, size_t cols, void *dst, void *stream);
+extern "C" int sbk_q80_pad(const void *src, size_t rows, size_t cols, void *dst, void *stream);
 
 namespace {
 
@@ -117,8 +118,21 @@ struct sb_ctx {
         r.dev_dtype = v->dtype;
         const bool pack = for_matvec && v->dtype == SB_DTYPE_Q6_K && rows * cols == v->elems &&
                           sbk_row_bytes(SB_DTYPE_Q6_K_P, cols) != 0 && cols <= 12288;
+        // Q8_0 is held with 16-byte-aligned rows (SB_DTYPE_Q8_0_R) for the tensor-core kernel
+        // (a plain copy when the rows are aligned already), so one resident form serves all
+        const bool pad = for_matvec && v->dtype == SB_DTYPE_Q8_0 && rows * cols == v->elems &&
+                         sbk_row_bytes(SB_DTYPE_Q8_0_R, cols) != 0 && cols <= 16384;
         cudaError_t e;
-        if (pack) {
+        if (pad) {
+            void *tmp = nullptr;
+            e = cudaMalloc(&tmp, v->len);
+            if (e == cudaSuccess) e = cudaMalloc(&r.ptr, sbk_row_bytes(SB_DTYPE_Q8_0_R, cols) * rows + 64);
+            if (e == cudaSuccess) e = cudaMemcpy(tmp, v->bytes, v->len, cudaMemcpyHostToDevice);
+            if (e == cudaSuccess && sbk_q80_pad(tmp, rows, cols, r.ptr, nullptr) != 0) e = cudaErrorLaunchFailure;
+            if (e == cudaSuccess) e = cudaDeviceSynchronize();
+            if (tmp) cudaFree(tmp);
+            r.dev_dtype = SB_DTYPE_Q8_0_R;
+        } else if (pack) {
             // upload, then repack into the resident buffer (+64 B: bulk reads round up to 16 B)
             void *tmp = nullptr;
             e = cudaMalloc(&tmp, v->len);

@@ -301,7 +301,10 @@ int upload_f32(sb_engine *e, const float *src, size_t n, float **dst)
     return 0;
 }
 
-bool fused_dtype(uint8_t dt) { return dt == SB_DTYPE_Q4_K || dt == SB_DTYPE_Q6_K_P; }
+bool fused_dtype(uint8_t dt)
+{
+    return dt == SB_DTYPE_Q4_K || dt == SB_DTYPE_Q6_K_P || dt == SB_DTYPE_Q8_0 || dt == SB_DTYPE_Q8_0_R;
+}
 
 // The matvecs `ms` (one input vector a, outputs ys) with the input formed as xs says:
 // one fused launch per dtype where the kernel has the fused input forms, else the
@@ -397,7 +400,10 @@ int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, boo
     const uint8_t gdt = L.ex[0].dt, ddt = L.ex[2].dt;
     int rc = 0;
     if (build) {
-        if (gdt == SB_DTYPE_Q4_K && ddt == SB_DTYPE_Q4_K) rc = build_moe_batches<sb::tcmv::Q4K, sb::tcmv::Q4K>(e, L, hc);
+        const bool d80 = ddt == SB_DTYPE_Q8_0 || ddt == SB_DTYPE_Q8_0_R;
+        if (gdt == SB_DTYPE_Q4_K && d80) rc = build_moe_batches<sb::tcmv::Q4K, sb::tcmv::Q80>(e, L, hc);
+        else if (gdt == SB_DTYPE_Q6_K_P && d80) rc = build_moe_batches<sb::tcmv::Q6KP, sb::tcmv::Q80>(e, L, hc);
+        else if (gdt == SB_DTYPE_Q4_K && ddt == SB_DTYPE_Q4_K) rc = build_moe_batches<sb::tcmv::Q4K, sb::tcmv::Q4K>(e, L, hc);
         else if (gdt == SB_DTYPE_Q4_K && ddt == SB_DTYPE_Q6_K_P) rc = build_moe_batches<sb::tcmv::Q4K, sb::tcmv::Q6KP>(e, L, hc);
         else if (gdt == SB_DTYPE_Q6_K_P && ddt == SB_DTYPE_Q6_K_P) rc = build_moe_batches<sb::tcmv::Q6KP, sb::tcmv::Q6KP>(e, L, hc);
         else if (gdt == SB_DTYPE_Q6_K_P && ddt == SB_DTYPE_Q4_K) rc = build_moe_batches<sb::tcmv::Q6KP, sb::tcmv::Q4K>(e, L, hc);
@@ -412,8 +418,9 @@ int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, boo
                               : launch_moe_batch<sb::tcmv::Q6KP>(L.gu_b, L.gu_smem, s);
     if (rc) return rc;
     *n += 1;
-    rc = ddt == SB_DTYPE_Q4_K ? launch_moe_batch<sb::tcmv::Q4K>(L.dn_b, L.dn_smem, s)
-                              : launch_moe_batch<sb::tcmv::Q6KP>(L.dn_b, L.dn_smem, s);
+    rc = ddt == SB_DTYPE_Q4_K   ? launch_moe_batch<sb::tcmv::Q4K>(L.dn_b, L.dn_smem, s)
+         : ddt == SB_DTYPE_Q6_K_P ? launch_moe_batch<sb::tcmv::Q6KP>(L.dn_b, L.dn_smem, s)
+                                  : launch_moe_batch<sb::tcmv::Q80>(L.dn_b, L.dn_smem, s);
     if (rc) return rc;
     *n += 1;
     return 0;
@@ -641,7 +648,7 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             // MoE FFN: every expert resident, its tensor map in a device table
             const sb_moe_plan &mp = *lp.moe;
             if (!mp.n_exp || !mp.top_k || mp.top_k > mp.n_exp || mp.top_k > 16 || mp.n_exp > 1024 || !mp.experts ||
-                !mp.ffn || mp.ffn % 256)
+                !mp.ffn || mp.ffn % 32)
                 return bail(0);
             L.moe = true, L.n_exp = mp.n_exp, L.top_k = mp.top_k, L.effn = mp.ffn;
             L.has_sh = mp.shared != nullptr;
@@ -655,11 +662,14 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
                     EngMat &m = L.ex[3 * x + k];
                     if ((rc = eng_mat(c, mp.experts[3 * x + k], r[k], cc[k], &m, true)) != 1) return bail(rc);
                     if (m.dt != L.ex[k].dt) return bail(0);  // one dtype per matrix kind
-                    const int mr = m.dt == SB_DTYPE_Q4_K
-                                       ? sb::tcmv::make_map<sb::tcmv::Q4K>(&maps[3 * x + k], m.w, (int)m.rows, (int)m.cols)
-                                   : m.dt == SB_DTYPE_Q6_K_P
-                                       ? sb::tcmv::make_map<sb::tcmv::Q6KP>(&maps[3 * x + k], m.w, (int)m.rows, (int)m.cols)
-                                       : 1;
+                    const int mr =
+                        m.dt == SB_DTYPE_Q4_K
+                            ? sb::tcmv::make_map<sb::tcmv::Q4K>(&maps[3 * x + k], m.w, (int)m.rows, (int)m.cols)
+                        : m.dt == SB_DTYPE_Q6_K_P
+                            ? sb::tcmv::make_map<sb::tcmv::Q6KP>(&maps[3 * x + k], m.w, (int)m.rows, (int)m.cols)
+                        : (m.dt == SB_DTYPE_Q8_0_R || (m.dt == SB_DTYPE_Q8_0 && m.cols % 128 == 0)) && k == 2
+                            ? sb::tcmv::make_map<sb::tcmv::Q80>(&maps[3 * x + k], m.w, (int)m.rows, (int)m.cols)
+                            : 1;
                     if (mr > 0) return bail(0);  // expert dtype without a tensor-core kernel
                     if (mr < 0) return bail(fail("decode plan: tensor map of an expert rejected"));
                 }

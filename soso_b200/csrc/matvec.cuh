@@ -387,6 +387,7 @@ extern "C" size_t sbk_row_bytes(uint8_t dtype, size_t cols)
     case SB_DTYPE_Q4_K: e = 256; b = 144; break;
     case SB_DTYPE_Q6_K: e = 256; b = 210; break;
     case SB_DTYPE_Q6_K_P: return (cols == 0 || cols % 256) ? 0 : sb::tcmv::q6k_packed_row_bytes(cols);
+    case SB_DTYPE_Q8_0_R: return (cols == 0 || cols % 32) ? 0 : sb::tcmv::q80_row_bytes_padded(cols);
     case SB_DTYPE_F32: return cols * 4;
     default: return 0;
     }
@@ -444,7 +445,7 @@ namespace sb {
 // Up to MAXB matrices of format F per launch of the tensor-core kernel; with
 // `fallback`, a chunk the kernel does not take runs matrix by matrix through
 // sbk_matvec, else it is rejected (-5).
-template <class F>
+template <class F, class FB = Q4K>
 static int tc_matvec_batch(const sbk_mv_op *ops, size_t n, int pdl, cudaStream_t s, bool fallback,
                            const tcmv::XSrc *xs = nullptr)
 {
@@ -470,7 +471,7 @@ static int tc_matvec_batch(const sbk_mv_op *ops, size_t n, int pdl, cudaStream_t
         } else if (fallback) {
             for (size_t i = 0; i < nb; i++) {
                 const sbk_mv_op &o = ops[i0 + i];
-                const int rc = launch_matvec<Q4K>(o.w, o.rows, o.cols, o.x, o.y, pdl, s);
+                const int rc = launch_matvec<FB>(o.w, o.rows, o.cols, o.x, o.y, pdl, s);
                 if (rc) return rc;
             }
         } else {
@@ -493,7 +494,11 @@ extern "C" int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols
     switch (dtype) {
     case SB_DTYPE_Q4_K: return sb::tc_matvec_batch<sb::tcmv::Q4K>(&op, 1, pdl, s, true);
     case SB_DTYPE_Q6_K_P: return sb::tc_matvec_batch<sb::tcmv::Q6KP>(&op, 1, pdl, s, false);
-    case SB_DTYPE_Q8_0: return sb::launch_matvec<sb::Q80>(w, rows, cols, x, y, pdl, s);
+    case SB_DTYPE_Q8_0:
+        // rows of a multiple of 128 weights are 16-byte aligned: the tensor-core kernel reads them
+        if (cols % 128 == 0) return sb::tc_matvec_batch<sb::tcmv::Q80, sb::Q80>(&op, 1, pdl, s, true);
+        return sb::launch_matvec<sb::Q80>(w, rows, cols, x, y, pdl, s);
+    case SB_DTYPE_Q8_0_R: return sb::tc_matvec_batch<sb::tcmv::Q80, sb::Q80>(&op, 1, pdl, s, false);
     case SB_DTYPE_Q6_K: return sb::launch_matvec<sb::Q6K>(w, rows, cols, x, y, pdl, s);
     }
     return -1;
@@ -505,6 +510,12 @@ extern "C" int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, i
     cudaStream_t s = (cudaStream_t)stream;
     if (dtype == SB_DTYPE_Q4_K) return sb::tc_matvec_batch<sb::tcmv::Q4K>(ops, n, pdl, s, true);
     if (dtype == SB_DTYPE_Q6_K_P) return sb::tc_matvec_batch<sb::tcmv::Q6KP>(ops, n, pdl, s, false);
+    if (dtype == SB_DTYPE_Q8_0_R) return sb::tc_matvec_batch<sb::tcmv::Q80, sb::Q80>(ops, n, pdl, s, false);
+    if (dtype == SB_DTYPE_Q8_0) {
+        bool aligned = true;
+        for (size_t i = 0; i < n; i++) aligned = aligned && ops[i].cols % 128 == 0;
+        if (aligned) return sb::tc_matvec_batch<sb::tcmv::Q80, sb::Q80>(ops, n, pdl, s, true);
+    }
     for (size_t i = 0; i < n; i++) {
         const int rc = sbk_matvec(dtype, ops[i].w, ops[i].rows, ops[i].cols, ops[i].x, ops[i].y, pdl, stream);
         if (rc) return rc;
@@ -520,7 +531,24 @@ extern "C" int sbk_matvec_batch_x(uint8_t dtype, const sbk_mv_op *ops, size_t n,
     cudaStream_t s = (cudaStream_t)stream;
     if (dtype == SB_DTYPE_Q4_K) return sb::tc_matvec_batch<sb::tcmv::Q4K>(ops, n, pdl, s, true, &x);
     if (dtype == SB_DTYPE_Q6_K_P) return sb::tc_matvec_batch<sb::tcmv::Q6KP>(ops, n, pdl, s, false, &x);
+    if (dtype == SB_DTYPE_Q8_0_R) return sb::tc_matvec_batch<sb::tcmv::Q80, sb::Q80>(ops, n, pdl, s, false, &x);
+    if (dtype == SB_DTYPE_Q8_0) {
+        for (size_t i = 0; i < n; i++)
+            if (ops[i].cols % 128) return -5;  // unaligned rows: pad them first (sbk_q80_pad)
+        return sb::tc_matvec_batch<sb::tcmv::Q80, sb::Q80>(ops, n, pdl, s, false, &x);
+    }
     return -5;
+}
+
+extern "C" int sbk_q80_pad(const void *src, size_t rows, size_t cols, void *dst, void *stream)
+{
+    if (!src || !dst || !rows || cols % 32 || cols > (1u << 24) || rows > (1u << 30)) return -1;
+    if ((uintptr_t)dst & 15) return -2;
+    const int rb = (int)(cols / 32 * 36), rbp = (int)sb::tcmv::q80_row_bytes_padded(cols);
+    const long long n = (long long)rows * rbp;
+    sb::tcmv::q80_pad_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const uint8_t *>(src), (long long)rows, rb, reinterpret_cast<uint8_t *>(dst), rbp);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
 extern "C" int sbk_q6k_pack(const void *src, size_t rows, size_t cols, void *dst, void *stream)

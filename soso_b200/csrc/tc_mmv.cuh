@@ -27,6 +27,7 @@
 #pragma once
 #include "tc_q4k.cuh"
 #include "tc_q6k.cuh"
+#include "tc_q80.cuh"
 
 namespace sb {
 namespace tcmv {
@@ -195,7 +196,7 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
         int prev_cols = 0;
         for (int mi = m_first; mi <= m_last && nst > 0; mi++) {
             const MatDesc &d = B.d[mi];
-            const int nb = d.cols / 256, spg = d.spg;
+            const int nb = F::units(d.cols), spg = d.spg;
             const int mtot = spg * ((d.rows + 15) >> 4);
             const int ka = max(st0, d.st_begin) - st0, kb = min(st1, d.st_begin + mtot) - st0;  // CTA-local stages
             const int gs0 = (ka + st0 - d.st_begin) / spg, gs1 = (kb - 1 + st0 - d.st_begin) / spg;
@@ -235,7 +236,7 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
             }
             for (int i = cwg * 32 + lane; i < ng * NCW * 16; i += NCW * 32) s.part[i] = 0.0f;
             asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-            const typename F::Seg S = F::seg_setup(L, s.prep, s.zero, nb);
+            const typename F::Seg S = F::seg_setup(L, s.prep, s.zero, nb, d.cols);
             float acc0 = 0.0f, acc1 = 0.0f;
             int cur = -1;
             // Team j takes the CTA-local stages k with k % NSTREAM == j in every segment, so
@@ -454,7 +455,7 @@ struct MatOp {
 template <class F>
 inline int stages_per_group(int cols)
 {
-    return (cols / 256 + F::SBLK - 1) / F::SBLK;
+    return (F::units(cols) + F::SBLK - 1) / F::SBLK;
 }
 
 // Shared memory for a batch over `grid` CTAs.
@@ -485,7 +486,7 @@ inline bool fits(const MatOp *ops, int n, int grid)
 {
     int mc, mg;
     for (int i = 0; i < n; i++)
-        if (ops[i].cols > F::MAX_COLS || ops[i].cols % 256 || ops[i].rows < 1) return false;
+        if (ops[i].cols > F::MAX_COLS || ops[i].cols % F::COLS_MULT || ops[i].rows < 1) return false;
     return batch_smem<F>(ops, n, grid, &mc, &mg) <= 227 * 1024;
 }
 
@@ -529,7 +530,7 @@ inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XS
     for (int i = 0; i < n; i++) {
         const MatOp &o = ops[i].op;
         plain[i] = o;
-        if (o.cols > F::MAX_COLS || o.cols % 256 || o.rows < 1) return -1;
+        if (o.cols > F::MAX_COLS || o.cols % F::COLS_MULT || o.rows < 1) return -1;
         MatDesc &d = b.d[i];
         const int mrc = cached_map<F>(&d.map, o.w, o.rows, o.cols);
         if (mrc) return mrc;

@@ -49,6 +49,8 @@ struct Q4K {
     static constexpr int SLOTB = 16 * ROWB;
     static constexpr int MAX_COLS = 16384;
 
+    static constexpr int COLS_MULT = 256;
+    __host__ __device__ static int units(int cols) { return cols / 256; }
     __host__ __device__ static size_t row_bytes(int cols) { return (size_t)(cols / 256) * 144; }
     __host__ __device__ static int stage_x(int j) { return j * SBLK * 18; }  // u64 column of stage j
 
@@ -154,7 +156,7 @@ struct Q4K {
         int mb;
         const float *fxp, *fmp;
     };
-    __device__ static Seg seg_setup(const Lane &L, const uint8_t *prep, const uint8_t *zero, int nb)
+    __device__ static Seg seg_setup(const Lane &L, const uint8_t *prep, const uint8_t *zero, int nb, int)
     {
         Seg s;
         // lanes without x read zeros: stride 0 into the zero area

@@ -71,6 +71,8 @@ struct Q6KP {
     static constexpr int SLOTB = 16 * ROWB;
     static constexpr int MAX_COLS = 12288;
 
+    static constexpr int COLS_MULT = 256;
+    __host__ __device__ static int units(int cols) { return cols / 256; }
     __host__ __device__ static size_t row_bytes(int cols) { return q6k_packed_row_bytes((size_t)cols); }
     __host__ __device__ static int stage_x(int j) { return j * 210; }
 
@@ -157,7 +159,7 @@ struct Q6KP {
         const uint32_t *ofl;
         const float *fxp;
     };
-    __device__ static Seg seg_setup(const Lane &L, const uint8_t *prep, const uint8_t *zero, int nb)
+    __device__ static Seg seg_setup(const Lane &L, const uint8_t *prep, const uint8_t *zero, int nb, int)
     {
         Seg s;
         s.bfl = L.live ? reinterpret_cast<const uint4 *>(prep) + 2 * L.g + L.tp : reinterpret_cast<const uint4 *>(zero);

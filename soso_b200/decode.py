@@ -16,7 +16,7 @@ import numpy as np
 from . import synth
 from ._lib import (SbDecodePlan, SbLayerPlan, SbMat, SbMlaPlan, SbMoePlan, SbView, SbError, c_f32p, c_u8p,
                    last_error, lib)
-from .formats import DTYPE_Q4_K, DTYPE_Q6_K
+from .formats import DTYPE_Q4_K, DTYPE_Q6_K, DTYPE_Q8_0
 
 
 @dataclass(frozen=True)
@@ -92,10 +92,19 @@ TINY_MOE = DenseConfig(n_layers=3, hidden=512, heads=4, kv_heads=2, head_dim=128
                        shared_gate=True, dtypes=dict(_ALL_Q4K, ffn_down=DTYPE_Q6_K, output=DTYPE_Q6_K))
 # a small MLA + MoE model (configs[4]'s structure): MLA on every layer, a dense FFN first,
 # then MoE layers with an ungated shared expert
+# (down projections Q8_0 like configs[4]'s, the experts' 160 wide: rows padded on upload)
 TINY_MLA = DenseConfig(n_layers=3, hidden=512, heads=4, kv_heads=4, head_dim=128, ffn=1024, vocab=1024, ctx=96,
                        theta=1e4, neox=False, qkv_bias=False, mla=True, q_rank=256, kv_rank=512, qk_nope=64,
-                       qk_rope=32, v_dim=128, n_exp=8, top_k=2, moe_ffn=256, first_moe=1, shared_ffn=512,
-                       dtypes=dict(_ALL_Q4K))
+                       qk_rope=32, v_dim=128, n_exp=8, top_k=2, moe_ffn=160, first_moe=1, shared_ffn=512,
+                       dtypes=dict(_ALL_Q4K, ffn_down=DTYPE_Q8_0))
+# DeepSeek-V2-Lite-style MLA + MoE (q-LoRA rank 512 synthesized, as the
+# reference's MLA requires it), layer 0 dense FFN 10944, then 64 routed experts (top-6, 1408)
+# plus the 2 shared experts (held as one expert of 2816, ungated); down projections Q8_0
+# (1408 / 10944 are not whole Q4_K blocks), all else Q4_K; RoPE theta 1e4, llama pairs
+DEEPSEEK_V2_LITE = DenseConfig(n_layers=27, hidden=2048, heads=16, kv_heads=16, head_dim=128, ffn=10944,
+                               vocab=102400, ctx=2048, theta=1e4, neox=False, qkv_bias=False, mla=True, q_rank=512,
+                               kv_rank=512, qk_nope=128, qk_rope=64, v_dim=128, n_exp=64, top_k=6, moe_ffn=1408,
+                               first_moe=1, shared_ffn=2816, dtypes=dict(_ALL_Q4K, ffn_down=DTYPE_Q8_0))
 TINY_MOE_NS = DenseConfig(n_layers=2, hidden=512, heads=8, kv_heads=2, head_dim=128, ffn=0, vocab=1024, ctx=96,
                           qkv_bias=False, qk_norm=True, n_exp=32, top_k=8, moe_ffn=256, dtypes=dict(_ALL_Q4K))
 

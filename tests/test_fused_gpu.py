@@ -117,10 +117,10 @@ def test_fused_input_rejections():
     for xs in (XSrc(None, None, None, 1e-6, 1), XSrc(None, None, None, 0.0, 7)):
         rc, _, _ = run_x(DTYPE_Q4_K, [(256, 2048)], a, xs, "rej")
         assert rc == -1
-    # a dtype without the fused forms
+    # a dtype without the fused forms (reference-layout Q6_K) is rejected before any launch
     ops = (SbkMvOp * 1)(SbkMvOp(16, 4, 256, 16, 16))
     xs = XSrc(None, 16, None, 1e-6, 1)
-    assert lib().sbk_matvec_batch_x(2, ops, 1, ctypes.byref(xs), 0, None) == -5
+    assert lib().sbk_matvec_batch_x(13, ops, 1, ctypes.byref(xs), 0, None) == -5
 
 
 @pytest.mark.parametrize("heads,kv_heads,neox,qk_norm,bias,pos", [
