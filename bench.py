@@ -305,8 +305,17 @@ def run_ours(args) -> None:
         e2e_s = float(t.item())
     L.sb_destroy(ctx)
 
-    dec = None if args.no_decode else decode_bench(local, rank, "dense")
-    dec_moe = None if args.no_decode else decode_bench(local, rank, "moe")
+    # the other BASELINE configs on this GPU: C1 (Q8_0 matvec), the decode models (C3 dense; C4
+    # MoE and C5 MLA+MoE at N=1 only: each rank would hold its own 11-16 GB synthetic model),
+    # and the tcgen05 prefill GEMM on C5's prefill shapes
+    extra = {}
+    if not args.no_decode:
+        extra["c1_q8_0_matvec"] = q80_bench(dev)
+        extra["decode"] = decode_bench(local, rank, "dense")
+        if world == 1:
+            extra["decode_moe"] = decode_bench(local, rank, "moe")
+            extra["decode_mla"] = decode_bench(local, rank, "mla")
+            extra["prefill"] = prefill_bench(dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -346,16 +355,11 @@ def run_ours(args) -> None:
             "single_matvec_launch": single,
             "clocks": clk,
         }
-        if dec:
-            if world > 1:
-                dec["aggregate_tok_per_s"] = round(dec["tok_per_s"] * world, 1)
-                dec["parallelism"] = f"{world} independent replicas (no tensor parallelism yet)"
-            line["decode"] = dec
-        if dec_moe:
-            if world > 1:
-                dec_moe["aggregate_tok_per_s"] = round(dec_moe["tok_per_s"] * world, 1)
-                dec_moe["parallelism"] = f"{world} independent replicas (no expert parallelism yet)"
-            line["decode_moe"] = dec_moe
+        for k, v in extra.items():
+            if k.startswith("decode") and world > 1:
+                v["aggregate_tok_per_s"] = round(v["tok_per_s"] * world, 1)
+                v["parallelism"] = f"{world} independent replicas"
+            line[k] = v
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -375,8 +379,8 @@ def decode_bench(device: int, rank: int, which: str = "dense") -> dict:
     router, the top-k experts' matrices, output matrix) + the KV rows read at the average
     position."""
     from soso_b200 import decode, synth
-    cfg = decode.QWEN25_3B if which == "dense" else decode.QWEN3_30B_A3B
-    model = decode.synth_model(cfg, f"c{'3' if which == 'dense' else '4'}.{rank}")
+    cfg = {"dense": decode.QWEN25_3B, "moe": decode.QWEN3_30B_A3B, "mla": decode.DEEPSEEK_V2_LITE}[which]
+    model = decode.synth_model(cfg, f"{which}.{rank}")
     sess = decode.DecodeSession(cfg, model, device=device)
     prompt = synth.rng("prompt", which, rank).integers(0, cfg.vocab, 128).astype(np.int32)
     sess.greedy(prompt[:8], 8)  # warm
@@ -393,16 +397,23 @@ def decode_bench(device: int, rank: int, which: str = "dense") -> dict:
             weights += v.nbytes * cfg.top_k / cfg.n_exp
         else:
             weights += v.nbytes
-    kv_per_pos = cfg.n_layers * 2 * cfg.kv_dim * 2
+    # cache bytes read per cached position: K and V rows (f16), or the latent row (f16) and the
+    # rope keys (f32) of an MLA layer
+    kv_per_pos = (cfg.n_layers * (cfg.kv_rank * 2 + cfg.kv_heads * cfg.qk_rope * 4) if cfg.mla
+                  else cfg.n_layers * 2 * cfg.kv_dim * 2)
     avg_ctx = 128 + (n_gen + 1) / 2.0
     bytes_tok = weights + kv_per_pos * avg_ctx + cfg.hidden * 4
     peaks = load_peaks()
     tps = n_gen / dt
     sess.close()
-    desc = ("configs[2]: Qwen2.5-3B-style dense, 36 layers, hidden 2048, 16 q / 2 kv heads x 128, SwiGLU 11008, "
-            "vocab 151936, Q4_K + Q6_K (ffn_down, output), fp16 KV ctx 4096") if which == "dense" else (
-            "configs[3]: Qwen3-30B-A3B-style MoE, 48 layers, hidden 2048, 32 q / 4 kv heads x 128, QK-norm, "
-            "128 experts x SwiGLU 768, softmax top-8, vocab 151936, all Q4_K, fp16 KV ctx 2048")
+    desc = {"dense": "configs[2]: Qwen2.5-3B-style dense, 36 layers, hidden 2048, 16 q / 2 kv heads x 128, SwiGLU "
+                     "11008, vocab 151936, Q4_K + Q6_K (ffn_down, output), fp16 KV ctx 4096",
+            "moe": "configs[3]: Qwen3-30B-A3B-style MoE, 48 layers, hidden 2048, 32 q / 4 kv heads x 128, QK-norm, "
+                   "128 experts x SwiGLU 768, softmax top-8, vocab 151936, all Q4_K, fp16 KV ctx 2048",
+            "mla": "configs[4]: DeepSeek-V2-Lite-style MLA + MoE, 27 layers, hidden 2048, 16 heads, kv_lora 512, "
+                   "qk_nope 128 + qk_rope 64, v_head 128, q-LoRA 512 (synthesized), layer 0 dense FFN 10944, then "
+                   "64 experts top-6 x 1408 + shared 2816, vocab 102400, Q4_K (down projections Q8_0), latent "
+                   "f16 cache ctx 2048"}[which]
     return {"config": desc,
             "data": "synthetic random-init weights (seeded), random prompt",
             "prompt_tokens": 128, "generated_tokens": n_gen, "tok_per_s": round(tps, 1),
@@ -412,6 +423,110 @@ def decode_bench(device: int, rank: int, which: str = "dense") -> dict:
                          "roofline_tok_per_s": round(peaks["hbm_gbs"] * 1e9 / bytes_tok, 1)},
             "timing": "wall clock around sb_decode_greedy(256 steps); graph launches chained on one stream",
             "last_tokens": toks[-4:].tolist()}
+
+
+def q80_bench(dev) -> dict:
+    """the Q8_0 4096x4096 matvec (.som blocks, f32 scale), batch 1, on
+    the tensor-core kernel; a CUDA graph of launches over 32 distinct copies (604 MB > L2)."""
+    import torch
+
+    from soso_b200 import synth
+    from soso_b200._lib import lib
+    L = lib()
+    rows, cols, copies, reps = 4096, 4096, 32, 5
+    ws_ = [torch.from_numpy(synth.random_weights(2, rows, cols, synth.rng("c1", k))).to(dev) for k in range(copies)]
+    x = torch.randn(cols, device=dev)
+    y = torch.empty(rows, device=dev)
+    s = torch.cuda.Stream(dev)
+
+    def enq(st):
+        for k in range(copies):
+            if L.sbk_matvec(2, ws_[k].data_ptr(), rows, cols, x.data_ptr(), y.data_ptr(), 1, st):
+                raise RuntimeError("sbk_matvec(Q8_0) rejected")
+    with torch.cuda.stream(s):
+        enq(s.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        enq(torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+    nbytes = rows * cols // 32 * 36 + cols * 4 + rows * 4
+    peaks = load_peaks()
+    return {"config": "configs[0]: Q8_0 4096x4096 (.som 36-byte blocks), x f32, batch 1",
+            "kernel": "sb::tcmv::tc_mmv_kernel<Q80> (one launch per matvec, PDL chain)",
+            "us_per_matvec": round(us, 2), "GBps": round(nbytes / us / 1e3, 1),
+            "frac_of_hbm": round(nbytes / us / 1e3 / peaks["hbm_gbs"], 4),
+            "l2": f"{copies} distinct copies ({copies * rows * cols // 32 * 36 // 2**20} MiB) rotated"}
+
+
+def prefill_bench(dev) -> dict:
+    """The tcgen05 prefill GEMM (sbk_matmul, bf16 operands) on the
+    Q4_K matrices of one configs[4] 512-token prefill layer: q_down, kv_down (512 x 2048),
+    q_up (3072 x 512), the dense FFN gate/up (10944 x 2048) and an expert gate/up
+    (1408 x 2048); each timed alone in a CUDA graph over 4 distinct copies."""
+    import torch
+
+    from soso_b200 import synth
+    from soso_b200._lib import lib
+    L = lib()
+    peaks_tf = 1633.9
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            peaks_tf = float(json.load(f).get("bf16_tflops", peaks_tf))
+    n = 512
+    out = {}
+    tot_fl, tot_us = 0.0, 0.0
+    for name, rows, cols in (("q_down|kv_down", 512, 2048), ("q_up", 3072, 512), ("ffn_gate|up", 10944, 2048),
+                             ("expert_gate|up", 1408, 2048)):
+        copies = 4
+        ws_ = [torch.from_numpy(synth.random_weights(3, rows, cols, synth.rng("pf", name, k))).to(dev)
+               for k in range(copies)]
+        x = torch.randn(n, cols, device=dev)
+        y = torch.empty(n, rows, device=dev)
+        wsb = torch.empty(int(L.sbk_matmul_ws_bytes(n, cols)), dtype=torch.uint8, device=dev)
+        s = torch.cuda.Stream(dev)
+
+        def enq(st):
+            for k in range(copies):
+                if L.sbk_matmul(3, ws_[k].data_ptr(), rows, cols, n, x.data_ptr(), y.data_ptr(), wsb.data_ptr(), 0, 1,
+                                st):
+                    raise RuntimeError("sbk_matmul rejected")
+        with torch.cuda.stream(s):
+            enq(s.cuda_stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            enq(torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (10 * copies)
+        fl = 2.0 * n * rows * cols
+        tot_fl += fl
+        tot_us += us
+        out[f"{name} {rows}x{cols}"] = {"us": round(us, 1), "TFLOPs": round(fl / us / 1e6, 1)}
+    return {"config": "configs[4] prefill, 512 tokens: Q4_K GEMMs of one layer, bf16 operands, f32 accumulation "
+                      "in tensor memory (conversion of x to bf16 included)",
+            "kernel": "sb::pf::pf_gemm_q4k_kernel (tcgen05.mma kind::f16, M=128 N=256)",
+            "shapes": out, "TFLOPs": round(tot_fl / tot_us / 1e6, 1),
+            "frac_of_bf16_peak": round(tot_fl / tot_us / 1e6 / peaks_tf, 4),
+            "peak_source": "measured (MEASURED_PEAKS.json bf16_tflops, burst)"}
 
 
 # ---------------------------------------------------------- reference arm
