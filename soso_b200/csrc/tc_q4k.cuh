@@ -31,6 +31,9 @@
 #ifndef SB_Q4K_NSLOT
 #define SB_Q4K_NSLOT 9  // ring slots (build-time tuning knob)
 #endif
+#ifndef SB_Q4K_NSTREAM
+#define SB_Q4K_NSTREAM 3  // consumer teams (build-time tuning knob)
+#endif
 #include "tc_common.cuh"
 
 namespace sb {
@@ -40,7 +43,7 @@ struct Q4K {
     static constexpr uint8_t DTYPE = 3;  // SB_DTYPE_Q4_K
     static constexpr int SBLK = 4;       // blocks per stage
     static constexpr int NCONS = 4;      // consumer warps per stage (one block each)
-    static constexpr int NSTREAM = 3;    // stages in compute at once (teams)
+    static constexpr int NSTREAM = SB_Q4K_NSTREAM;  // stages in compute at once (teams)
     static constexpr int NCW = NCONS * NSTREAM;
     static constexpr int THREADS = (NCW + 1) * 32;
     static constexpr int NSLOT = SB_Q4K_NSLOT;  // a multiple of NSTREAM

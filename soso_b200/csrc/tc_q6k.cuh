@@ -27,6 +27,12 @@
 // 16 consumer warps in 2 teams of 8, one block per warp per stage.  The box
 // row is 1696 bytes (one group + 16, == 32 mod 128: conflict-free 8-byte loads).
 #pragma once
+#ifndef SB_Q6K_NSLOT
+#define SB_Q6K_NSLOT 4  // ring slots (build-time tuning knob)
+#endif
+#ifndef SB_Q6K_NSTREAM
+#define SB_Q6K_NSTREAM 2  // consumer teams (build-time tuning knob)
+#endif
 #include "tc_common.cuh"
 
 namespace sb {
@@ -62,10 +68,10 @@ struct Q6KP {
     static constexpr uint8_t DTYPE = 14;  // SB_DTYPE_Q6_K_P
     static constexpr int SBLK = 8;        // blocks per stage (one group)
     static constexpr int NCONS = 8;
-    static constexpr int NSTREAM = 2;
+    static constexpr int NSTREAM = SB_Q6K_NSTREAM;
     static constexpr int NCW = NCONS * NSTREAM;
     static constexpr int THREADS = (NCW + 1) * 32;
-    static constexpr int NSLOT = 4;   // a multiple of NSTREAM
+    static constexpr int NSLOT = SB_Q6K_NSLOT;  // a multiple of NSTREAM
     static constexpr int BOXW = 212;  // u64: one group (210) + 16 bytes
     static constexpr int ROWB = BOXW * 8;
     static constexpr int SLOTB = 16 * ROWB;
