@@ -181,6 +181,22 @@ int sb_decode_token(sb_ctx *ctx, const float *embed, size_t pos, float *logits, 
  * argmax produced at step i.  Needs plan.embed.  1 = done, 0 = not prepared, <0 = error. */
 int sb_decode_greedy(sb_ctx *ctx, const int32_t *prompt, size_t n_prompt, size_t pos, size_t n, int32_t *tokens_out);
 
+/* ---- tensor-parallel groups (no counterpart in the reference, whose multi-machine mode
+ * is a TCP layer pipeline, crates/soso-llm-core/src/pipeline.rs) -------------------------
+ * One process per GPU of one node.  Each rank creates its group exchange area, the ranks
+ * swap the returned CUDA IPC handles over their own host channel (soso_b200 uses
+ * torch.distributed), each opens the others', and then sb_decode_prepare shards the plan
+ * it is given (the full model) across the group: attention heads and FFN rows of the
+ * dense layers (column shards of attn_output / ffn_down, whose partial sums every rank
+ * adds in rank order inside the next matvec's input preparation) and vocabulary rows of
+ * the output matrix (the greedy token is the largest of the ranks' maxima).  With a group
+ * of world > 1, sb_decode_prepare returns before its warm-up token: call
+ * sb_decode_finish on every rank after a host barrier; only sb_decode_greedy runs. */
+size_t sb_group_handle_bytes(void);
+int sb_group_create(sb_ctx *ctx, int rank, int world, void *handle_out);
+int sb_group_open(sb_ctx *ctx, const void *handles /* world x sb_group_handle_bytes(), rank order */);
+int sb_decode_finish(sb_ctx *ctx);
+
 /* ---- kernels on device pointers --------------------------------------- */
 
 /* Bytes per row for (dtype, cols), 0 if cols is not a whole number of blocks

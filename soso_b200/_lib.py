@@ -86,6 +86,10 @@ SIGNATURES = {
     "sb_last_error": (ctypes.c_char_p, []),
     "sb_decode_prepare": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbDecodePlan)]),
     "sb_decode_token": (ctypes.c_int, [ctypes.c_void_p, c_f32p, c_size, c_f32p, ctypes.POINTER(ctypes.c_uint16)]),
+    "sb_group_handle_bytes": (c_size, []),
+    "sb_group_create": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "sb_group_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "sb_decode_finish": (ctypes.c_int, [ctypes.c_void_p]),
     "sb_decode_greedy": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), c_size, c_size, c_size,
                                         ctypes.POINTER(ctypes.c_int32)]),
     "sbk_row_bytes": (c_size, [ctypes.c_uint8, c_size]),

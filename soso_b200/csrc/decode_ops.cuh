@@ -8,6 +8,7 @@
 // CUDA graph serves every step.
 #pragma once
 #include "common.cuh"
+#include "group.cuh"
 
 namespace sb {
 
@@ -477,6 +478,11 @@ struct ArgmaxArgs {
     // greedy step (all null when unused)
     int *pos, *step, *hist;
     const int *prompt, *n_prompt;
+    // tensor-parallel: v is this rank's vocabulary slice starting at `base`; the slice's
+    // (max, index) goes to every rank's exchange area (pub.dst[p] -> 2 x u32) and
+    // argmax_gather_kernel finishes the step
+    int base;
+    grp::Pub pub;
 };
 
 __device__ __forceinline__ void amax_merge(float &bv, int &bi, float v, int i)
@@ -545,7 +551,17 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(ArgmaxArgs a)
     for (int c = threadIdx.x; c < (int)gridDim.x; c += AM_THREADS) amax_merge(bv, bi, __ldcg(a.pv + c), __ldcg(a.pi + c));
     __syncthreads();
     amax_block(bv, bi, sv, si);
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0 && a.pub.n) {
+        const unsigned vb = __float_as_uint(bv), ib = (unsigned)(a.base + (bi < 0 ? 0 : bi));
+        for (int p = 0; p < a.pub.n; p++) {
+            unsigned *d = reinterpret_cast<unsigned *>(a.pub.dst[p]);
+            d[0] = vb;
+            d[1] = ib;
+        }
+        __threadfence_system();
+        for (int p = 0; p < a.pub.n; p++) atomicAdd_system(a.pub.cnt[p], 1u);
+        *a.cnt = 0u;
+    } else if (threadIdx.x == 0) {
         const int tok = bi < 0 ? 0 : bi;
         *a.out = tok;
         *a.cnt = 0u;
@@ -558,6 +574,39 @@ __global__ void __launch_bounds__(AM_THREADS) argmax_kernel(ArgmaxArgs a)
         }
     }
     griddep_launch();
+}
+
+// End of a tensor-parallel greedy step: wait for every rank's (max, index) of its vocabulary
+// slice, take the largest (ties to the larger index, as Runtime::argmax), record it and feed
+// the next token as argmax_kernel does, then start the next epoch.  One thread.
+struct GatherArgs {
+    void *area;              // own exchange area
+    const unsigned *cnt;     // counters of the argmax exchange point, [n]
+    unsigned *epoch;
+    int n;
+    int *out, *pos, *step, *hist;
+    const int *prompt, *n_prompt;
+};
+
+__global__ void argmax_gather_kernel(GatherArgs a)
+{
+    griddep_wait();
+    if (threadIdx.x != 0) return;
+    const unsigned e = *a.epoch;
+    grp::wait_counts(a.cnt, a.n, e);
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int s = 0; s < a.n; s++) {
+        const unsigned *sl = grp::arg_slot(a.area, s);
+        amax_merge(bv, bi, __uint_as_float(__ldcg(sl)), (int)__ldcg(sl + 1));
+    }
+    const int tok = bi < 0 ? 0 : bi;
+    const int i = *a.step;
+    a.hist[i] = tok;
+    *a.out = i + 1 < *a.n_prompt ? a.prompt[i + 1] : tok;
+    *a.pos += 1;
+    *a.step = i + 1;
+    *a.epoch = e + 1;
 }
 
 // -------------------------------------------------------------------- embed
@@ -716,7 +765,7 @@ inline int argmax_launch(const float *v, size_t n, int32_t *out, void *ws, int p
     unsigned *cnt = (unsigned *)ws;
     float *pv = (float *)((char *)ws + 256);
     int *pi = (int *)((char *)ws + 256 + AM_GRID * 8);
-    ArgmaxArgs a{v, (int)n, pv, pi, cnt, out, pos, step, hist, prompt, n_prompt};
+    ArgmaxArgs a{v, (int)n, pv, pi, cnt, out, pos, step, hist, prompt, n_prompt, 0, grp::Pub{}};
     return launch_k(argmax_kernel, dim3(AM_GRID), dim3(AM_THREADS), 0, pdl, s, a);
 }
 }  // namespace sb

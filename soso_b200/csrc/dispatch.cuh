@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "group.cuh"
 #include "sosob200.h"
 
 extern "C" int sbk_matvec(uint8_t dtype, const void *w, size_t rows, size_t cols, const float *x, float *y,
@@ -71,6 +72,7 @@ struct sb_ctx {
     void *host_stage = nullptr;  // pinned mirror of scratch: one DMA each way per call
     size_t host_stage_bytes = 0;
     sb_stats stats = {};
+    sb_group *grp = nullptr;  // tensor-parallel group (sb_group_create / sb_group_open)
 
     int ensure_host_stage(size_t bytes)
     {
@@ -217,8 +219,66 @@ extern "C" void sb_destroy(sb_ctx *c)
         if (kv.second.ptr) cudaFree(kv.second.ptr);
     if (c->scratch) cudaFree(c->scratch);
     if (c->host_stage) cudaFreeHost(c->host_stage);
+    if (c->grp) {
+        for (int p = 0; p < c->grp->world; p++)
+            if (p != c->grp->rank && c->grp->peer[p]) cudaIpcCloseMemHandle(c->grp->peer[p]);
+        if (c->grp->area) cudaFree(c->grp->area);
+        if (c->grp->epoch) cudaFree(c->grp->epoch);
+        if (c->grp->ones) cudaFree(c->grp->ones);
+        delete c->grp;
+    }
     cudaStreamDestroy(c->stream);
     delete c;
+}
+
+extern "C" size_t sb_group_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int sb_group_create(sb_ctx *c, int rank, int world, void *handle_out)
+{
+    if (!c || !handle_out) return fail("null argument");
+    if (world < 1 || world > sb::grp::MAXG || rank < 0 || rank >= world) return fail("sb_group_create: bad rank/world");
+    std::lock_guard<std::mutex> lk(c->mu);
+    if (c->grp) return fail("sb_group_create: the context already has a group");
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return fail("cudaSetDevice", e);
+    sb_group *g = new sb_group();
+    g->rank = rank, g->world = world;
+    const float ones[sb::grp::MAXG] = {1, 1, 1, 1, 1, 1, 1, 1};
+    const unsigned one = 1;
+    if ((e = cudaMalloc(&g->area, sb::grp::AREA_BYTES)) == cudaSuccess &&
+        (e = cudaMemset(g->area, 0, sb::grp::AREA_BYTES)) == cudaSuccess &&
+        (e = cudaMalloc(&g->epoch, 64)) == cudaSuccess &&
+        (e = cudaMemcpy(g->epoch, &one, 4, cudaMemcpyHostToDevice)) == cudaSuccess &&
+        (e = cudaMalloc(&g->ones, sizeof(ones))) == cudaSuccess &&
+        (e = cudaMemcpy(g->ones, ones, sizeof(ones), cudaMemcpyHostToDevice)) == cudaSuccess &&
+        (e = cudaIpcGetMemHandle((cudaIpcMemHandle_t *)handle_out, g->area)) == cudaSuccess) {
+        g->peer[rank] = g->area;
+        c->grp = g;
+        return 0;
+    }
+    if (g->area) cudaFree(g->area);
+    if (g->epoch) cudaFree(g->epoch);
+    if (g->ones) cudaFree(g->ones);
+    delete g;
+    return fail("sb_group_create", e);
+}
+
+extern "C" int sb_group_open(sb_ctx *c, const void *handles)
+{
+    if (!c || !handles) return fail("null argument");
+    std::lock_guard<std::mutex> lk(c->mu);
+    sb_group *g = c->grp;
+    if (!g) return fail("sb_group_open: no group (sb_group_create first)");
+    cudaError_t e = cudaSetDevice(c->device);
+    if (e != cudaSuccess) return fail("cudaSetDevice", e);
+    const cudaIpcMemHandle_t *h = (const cudaIpcMemHandle_t *)handles;
+    for (int p = 0; p < g->world; p++) {
+        if (p == g->rank || g->peer[p]) continue;
+        if ((e = cudaIpcOpenMemHandle(&g->peer[p], h[p], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess)
+            return fail("cudaIpcOpenMemHandle", e);
+    }
+    g->opened = true;
+    return 0;
 }
 
 extern "C" int sb_available(const sb_ctx *c) { return c ? 1 : 0; }

@@ -246,6 +246,11 @@ struct sb_engine {
     size_t mla_ws_bytes = 0;
     void *kv_segs = nullptr;
     size_t n_kv_segs = 0;
+    // tensor parallelism (sb_group of world > 1): this rank's vocabulary slice of the output
+    sb_group *tp = nullptr;
+    size_t vbase = 0, vn = 0;
+    size_t attn_ws_bytes = 0;
+    bool pending_finish = false;  // sb_decode_finish still to run (warm-up + capture)
     int *ints = nullptr;  // pos, tok, step, n_prompt
     int *prompt = nullptr, *hist = nullptr;
     void *attn_ws = nullptr, *am_ws = nullptr;
@@ -289,6 +294,46 @@ int eng_mat(sb_ctx *c, const sb_mat &m, size_t rows, size_t cols, EngMat *out, b
     return 1;
 }
 
+// Rows [r0, r0 + nr) of a plan matrix (a tensor-parallel shard), resident under its own key.
+int eng_mat_rows(sb_ctx *c, const sb_mat &m, size_t rows, size_t cols, size_t r0, size_t nr, EngMat *out)
+{
+    if (!m.key || !m.view.bytes) return fail("decode plan: matrix without key or bytes");
+    if (m.rows != rows || m.cols != cols) return fail(std::string("decode plan: ") + m.key + " has an unexpected shape");
+    if (!admit(&m.view, rows, cols) || r0 + nr > rows || !nr) return 0;
+    const size_t rb = sbk_row_bytes(m.view.dtype, cols);
+    sb_view v = m.view;
+    v.bytes += r0 * rb;
+    v.len = nr * rb;
+    v.elems = nr * cols;
+    const std::string key = std::string(m.key) + "#rows" + std::to_string(r0) + "+" + std::to_string(nr);
+    Resident *r = nullptr;
+    const int rc = c->resident(key.c_str(), &v, nr, cols, &r, true);
+    if (rc <= 0) return rc;
+    *out = EngMat{r->ptr, r->dev_dtype, nr, cols};
+    return 1;
+}
+
+// Columns [c0, c0 + nc) of a plan matrix (whole blocks: a tensor-parallel shard of its input
+// dimension), gathered row by row on the host, resident under its own key.
+int eng_mat_cols(sb_ctx *c, const sb_mat &m, size_t rows, size_t cols, size_t c0, size_t nc, EngMat *out)
+{
+    if (!m.key || !m.view.bytes) return fail("decode plan: matrix without key or bytes");
+    if (m.rows != rows || m.cols != cols) return fail(std::string("decode plan: ") + m.key + " has an unexpected shape");
+    if (!admit(&m.view, rows, cols) || c0 + nc > cols || !nc) return 0;
+    const uint8_t dt = m.view.dtype;
+    const size_t rb = sbk_row_bytes(dt, cols), ob = c0 ? sbk_row_bytes(dt, c0) : 0, sb_ = sbk_row_bytes(dt, nc);
+    if (!sb_ || (c0 && !ob)) return 0;  // not on block boundaries
+    std::vector<uint8_t> tmp(rows * sb_);
+    for (size_t r = 0; r < rows; r++) memcpy(tmp.data() + r * sb_, m.view.bytes + r * rb + ob, sb_);
+    sb_view v{tmp.data(), tmp.size(), dt, rows * nc};
+    const std::string key = std::string(m.key) + "#cols" + std::to_string(c0) + "+" + std::to_string(nc);
+    Resident *r = nullptr;
+    const int rc = c->resident(key.c_str(), &v, rows, nc, &r, true);
+    if (rc <= 0) return rc;
+    *out = EngMat{r->ptr, r->dev_dtype, rows, nc};
+    return 1;
+}
+
 int upload_f32(sb_engine *e, const float *src, size_t n, float **dst)
 {
     *dst = nullptr;
@@ -310,8 +355,21 @@ bool fused_dtype(uint8_t dt)
 // one fused launch per dtype where the kernel has the fused input forms, else the
 // input is materialised first (sbk_rmsnorm / sbk_swiglu into `tmp`).
 int run_mv(sb_engine *e, const EngMat *const *ms, float *const *ys, int n, const float *a, const sbk_xsrc &xs,
-           cudaStream_t s, size_t *launches)
+           cudaStream_t s, size_t *launches, const sb::grp::Pub *pub = nullptr, const sb::grp::Wait *wait = nullptr)
 {
+    if ((pub && pub->n) || (wait && wait->n)) {
+        // tensor-parallel forms: one dtype, the tensor-core kernels only
+        sbk_mv_op ops[8];
+        for (int j = 0; j < n; j++) {
+            if (ms[j]->dt != ms[0]->dt) return -5;
+            ops[j] = sbk_mv_op{ms[j]->w, ms[j]->rows, ms[j]->cols, a, ys[j]};
+        }
+        const sb::tcmv::XSrc x{xs.res, xs.norm_w, xs.h_out, xs.eps, xs.mode, xs.ys, xs.yw, xs.ny, xs.ystride};
+        const int rc = sb::matvec_batch_group(ms[0]->dt, ops, n, x, pub, wait, s);
+        if (rc) return rc;
+        *launches += 1;
+        return 0;
+    }
     bool done[8] = {false};
     for (int i = 0; i < n; i++) {
         if (done[i]) continue;
@@ -437,6 +495,11 @@ int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, boo
         const int _rc = run_mv(e, __VA_ARGS__, s, &n);                                                        \
         if (_rc) return fail(std::string("decode step: matvec launch rejected (") + std::to_string(_rc) + ")"); \
     } while (0)
+#define ENG_MV_G(PUB, WAIT, ...)                                                                             \
+    do {                                                                                                     \
+        const int _rc = run_mv(e, __VA_ARGS__, s, &n, PUB, WAIT);                                             \
+        if (_rc) return fail(std::string("decode step: matvec launch rejected (") + std::to_string(_rc) + ")"); \
+    } while (0)
 
 // One token, enqueued on s.  greedy: embedding row from the device token, and
 // argmax (which also ends the step) at the end.
@@ -447,10 +510,29 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
     float *hc = e->h, *ho = e->h2;  // residual stream: current / the other buffer
     if (greedy) ENG_CHECK(sbk_embed_row(e->emb.w, e->emb.dt, e->V, e->H, tok, e->h, 1, s));
     int moe_ny = 0;  // > 0: the last FFN was MoE; its result is the weighted set ys / wts
+    // tensor parallelism: exchange point x of this token (2l: attn_output partial sums of
+    // layer l, 2l+1: ffn_down partial sums, 2L: the vocabulary-slice maxima)
+    sb_group *const g = e->tp;
+    const int G = g ? g->world : 1, grid = sb::num_sms_cached();
+    int xprev = -1;  // the exchange point holding the pending residual (-1: none)
+    auto pub_of = [&](int x) {
+        sb::grp::Pub pb{};
+        pb.n = G;
+        for (int p = 0; p < G; p++)
+            pb.dst[p] = sb::grp::data_slot(g->peer[p], x, g->rank), pb.cnt[p] = sb::grp::cnt_slot(g->peer[p], x, g->rank);
+        return pb;
+    };
+    auto wait_of = [&](int x) {
+        sb::grp::Wait w{};
+        if (g && x >= 0) w = sb::grp::Wait{sb::grp::cnt_slot(g->area, x, 0), g->epoch, G, grid};
+        return w;
+    };
     auto norm_src = [&](const float *w, float *h_out) {
         sbk_xsrc xs{};
         xs.norm_w = w, xs.h_out = h_out, xs.eps = e->eps, xs.mode = SBK_XS_NORM;
-        if (moe_ny) xs.ys = e->ys, xs.yw = e->wts, xs.ny = moe_ny, xs.ystride = (int)e->H;
+        if (g && xprev >= 0)
+            xs.ys = sb::grp::data_slot(g->area, xprev, 0), xs.yw = g->ones, xs.ny = G, xs.ystride = sb::grp::XW;
+        else if (moe_ny) xs.ys = e->ys, xs.yw = e->wts, xs.ny = moe_ny, xs.ystride = (int)e->H;
         else xs.res = e->ob;
         return xs;
     };
@@ -496,9 +578,11 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
                 if (!l) xs.res = nullptr;
                 const EngMat *ms[3] = {&L.q, &L.k, &L.v};
                 float *ys[3] = {e->qkv, e->qkv + L.qd, e->qkv + L.qd + L.kvd};
-                ENG_MV(ms, ys, 3, hc, xs);
+                const sb::grp::Wait w = wait_of(l ? xprev : -1);
+                ENG_MV_G(nullptr, &w, ms, ys, 3, hc, xs);
                 if (l) std::swap(hc, ho);
                 moe_ny = 0;
+                xprev = -1;
             }
             ENG_CHECK(sbk_attn_rope_decode(e->qkv, L.bias, L.qn, L.kn, L.kc, L.vc, e->att, pos, L.heads, L.kvh, L.hd,
                                            e->ctx, L.theta, e->eps, L.neox, e->attn_ws, 1, s));
@@ -507,7 +591,13 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
             const sbk_xsrc xs{};
             const EngMat *ms[1] = {&L.o};
             float *ys[1] = {e->ob};
-            ENG_MV(ms, ys, 1, e->att, xs);
+            if (g) {  // this rank's heads' share of attn_output: to every rank
+                const sb::grp::Pub pb = pub_of((int)(2 * l));
+                ENG_MV_G(&pb, nullptr, ms, ys, 1, e->att, xs);
+                xprev = (int)(2 * l);
+            } else {
+                ENG_MV(ms, ys, 1, e->att, xs);
+            }
         }
         if (L.moe) {
             // MoE FFN: h + attention output -> rmsnorm -> router logits; route; experts
@@ -529,25 +619,50 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
             const sbk_xsrc xs = norm_src(L.nf, ho);
             const EngMat *ms[2] = {&L.g, &L.u};
             float *ys[2] = {e->gu, e->gu + L.ffn};
-            ENG_MV(ms, ys, 2, hc, xs);
+            const sb::grp::Wait w = wait_of(xprev);
+            ENG_MV_G(nullptr, &w, ms, ys, 2, hc, xs);
             std::swap(hc, ho);
+            xprev = -1;
         }
         {
             sbk_xsrc xs{};
             xs.res = e->gu + L.ffn, xs.mode = SBK_XS_SWIGLU;
             const EngMat *ms[1] = {&L.d};
             float *ys[1] = {e->ob};
-            ENG_MV(ms, ys, 1, e->gu, xs);
+            if (g) {  // this rank's share of ffn_down: to every rank
+                const sb::grp::Pub pb = pub_of((int)(2 * l + 1));
+                ENG_MV_G(&pb, nullptr, ms, ys, 1, e->gu, xs);
+                xprev = (int)(2 * l + 1);
+            } else {
+                ENG_MV(ms, ys, 1, e->gu, xs);
+            }
         }
     }
     {
         const sbk_xsrc xs = norm_src(e->fnorm, nullptr);
         const EngMat *ms[1] = {&e->lm};
         float *ys[1] = {e->logits};
-        ENG_MV(ms, ys, 1, hc, xs);
+        const sb::grp::Wait w = wait_of(xprev);
+        ENG_MV_G(nullptr, &w, ms, ys, 1, hc, xs);
     }
-    if (greedy) {
-        ENG_CHECK(sb::argmax_launch(e->logits, e->V, tok, e->am_ws, 1, s, pos, step, e->hist, e->prompt, np));
+    if (greedy && g) {
+        // the maximum of this rank's vocabulary slice to every rank, then the global one
+        const int xa = (int)(2 * e->L.size());
+        sb::grp::Pub pb{};
+        pb.n = G;
+        for (int p = 0; p < G; p++)
+            pb.dst[p] = reinterpret_cast<float *>(sb::grp::arg_slot(g->peer[p], g->rank)),
+            pb.cnt[p] = sb::grp::cnt_slot(g->peer[p], xa, g->rank);
+        unsigned *cnt = (unsigned *)e->am_ws;
+        float *pv = (float *)((char *)e->am_ws + 256);
+        int *pi = (int *)((char *)e->am_ws + 256 + sb::AM_GRID * 8);
+        sb::ArgmaxArgs aa{e->logits, (int)e->vn, pv, pi, cnt, tok, nullptr, nullptr, nullptr, nullptr, nullptr,
+                          (int)e->vbase, pb};
+        ENG_CHECK(sb::launch_k(sb::argmax_kernel, dim3(sb::AM_GRID), dim3(sb::AM_THREADS), 0, 1, s, aa));
+        sb::GatherArgs ga{g->area, sb::grp::cnt_slot(g->area, xa, 0), g->epoch, G, tok, pos, step, e->hist, e->prompt, np};
+        ENG_CHECK(sb::launch_k(sb::argmax_gather_kernel, dim3(1), dim3(32), 0, 1, s, ga));
+    } else if (greedy) {
+        ENG_CHECK(sb::argmax_launch(e->logits, e->vn, tok, e->am_ws, 1, s, pos, step, e->hist, e->prompt, np));
     } else {
         sb::kv_rows_kernel<<<(unsigned)e->n_kv_segs, 256, 0, s>>>((const sb::KvSeg *)e->kv_segs, pos, e->kv_rows);
         if (cudaGetLastError() != cudaSuccess) return fail("decode step: kv rows launch failed");
@@ -575,6 +690,28 @@ int capture(sb_engine *e, cudaStream_t s, bool greedy, cudaGraphExec_t *out)
     return 0;
 }
 
+// Positions, tokens, KV caches and the split-K workspaces back to zero (the group's epoch
+// and exchange counters are never reset).
+cudaError_t engine_zero(sb_engine *e, cudaStream_t s)
+{
+    cudaError_t z = cudaMemsetAsync(e->ints, 0, 64, s);
+    for (auto &L : e->L) {
+        if (L.mla) {
+            if (z == cudaSuccess) z = cudaMemsetAsync(L.latent, 0, e->ctx * L.kv_rank * 2, s);
+            if (z == cudaSuccess) z = cudaMemsetAsync(L.krope, 0, e->ctx * L.kvh * L.qk_rope * 4, s);
+            continue;
+        }
+        if (z == cudaSuccess) z = cudaMemsetAsync(L.kc, 0, e->ctx * L.kvd * 2, s);
+        if (z == cudaSuccess) z = cudaMemsetAsync(L.vc, 0, e->ctx * L.kvd * 2, s);
+    }
+    if (z == cudaSuccess && e->mla_ws) z = cudaMemsetAsync(e->mla_ws, 0, e->mla_ws_bytes, s);
+    if (z == cudaSuccess && e->attn_ws_bytes) z = cudaMemsetAsync(e->attn_ws, 0, e->attn_ws_bytes, s);
+    if (z == cudaSuccess) z = cudaMemsetAsync(e->am_ws, 0, sbk_argmax_ws_bytes(), s);
+    if (z == cudaSuccess) z = cudaMemsetAsync(e->h, 0, e->H * 4, s);
+    if (z == cudaSuccess) z = cudaStreamSynchronize(s);
+    return z;
+}
+
 }  // namespace
 
 extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
@@ -600,6 +737,10 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
     e->V = p->vocab;
     e->ctx = p->ctx;
     e->eps = p->eps;
+    sb_group *const g = (c->grp && c->grp->world > 1) ? c->grp : nullptr;
+    if (g && !g->opened) return bail(fail("decode plan: the group is not open (sb_group_open)"));
+    if (g && p->hidden > (size_t)sb::grp::XW) return bail(0);
+    e->tp = g;
     const size_t H = e->H;
     size_t attn_ws = 0;
     e->L.resize(p->n_layers);
@@ -609,6 +750,8 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         if (!lp.norm_attn || !lp.norm_ffn) return bail(fail("decode plan: layer without norms"));
         L.heads = lp.heads, L.kvh = lp.kv_heads, L.hd = lp.head_dim, L.theta = lp.theta, L.neox = lp.neox;
         int rc;
+        if (g && (lp.mla || lp.moe)) return bail(0);  // the tensor-parallel engine runs dense GQA layers
+        std::vector<float> tp_bias;                   // this rank's slice of the q|k|v bias
         if (lp.mla) {
             // MLA: latent cache + rope keys; attention output heads * v_dim wide
             const sb_mla_plan &ml = *lp.mla;
@@ -636,6 +779,29 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             e->mla_hr = std::max(e->mla_hr, L.heads * L.kv_rank);
             e->mla_hp = std::max(e->mla_hp, L.heads * L.qk_rope);
             e->mla_ws_bytes = std::max(e->mla_ws_bytes, sbk_mla_ws_bytes(L.heads, L.kv_rank));
+        } else if (g) {
+            // tensor-parallel attention: this rank's query heads, the kv heads they read, the
+            // matching columns of attn_output (its partial sums go through the exchange)
+            const size_t G = g->world, r = g->rank;
+            if (!L.heads || !L.kvh || L.heads % L.kvh || L.hd != 128 || L.heads % G) return bail(0);
+            const size_t gs = L.heads / L.kvh, hp = L.heads / G;
+            size_t kvl;
+            if (hp % gs == 0) kvl = hp / gs;
+            else if (gs % hp == 0) kvl = 1;
+            else return bail(0);
+            if (hp / kvl > 8) return bail(0);
+            const size_t q0 = r * hp, kv0 = q0 / gs, qdg = L.heads * L.hd, kvdg = L.kvh * L.hd;
+            L.heads = hp, L.kvh = kvl, L.qd = hp * L.hd, L.kvd = kvl * L.hd;
+            if ((rc = eng_mat_rows(c, lp.q, qdg, H, q0 * L.hd, L.qd, &L.q)) != 1) return bail(rc);
+            if ((rc = eng_mat_rows(c, lp.k, kvdg, H, kv0 * L.hd, L.kvd, &L.k)) != 1) return bail(rc);
+            if ((rc = eng_mat_rows(c, lp.v, kvdg, H, kv0 * L.hd, L.kvd, &L.v)) != 1) return bail(rc);
+            if ((rc = eng_mat_cols(c, lp.o, H, qdg, q0 * L.hd, L.qd, &L.o)) != 1) return bail(rc);
+            if (lp.qkv_bias) {
+                const float *b0 = lp.qkv_bias;
+                tp_bias.insert(tp_bias.end(), b0 + q0 * L.hd, b0 + q0 * L.hd + L.qd);
+                tp_bias.insert(tp_bias.end(), b0 + qdg + kv0 * L.hd, b0 + qdg + kv0 * L.hd + L.kvd);
+                tp_bias.insert(tp_bias.end(), b0 + qdg + kvdg + kv0 * L.hd, b0 + qdg + kvdg + kv0 * L.hd + L.kvd);
+            }
         } else {
             if (!L.heads || !L.kvh || L.heads % L.kvh || L.hd != 128 || L.heads / L.kvh > 8) return bail(0);
             L.qd = L.heads * L.hd, L.kvd = L.kvh * L.hd;
@@ -691,6 +857,18 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             e->moe_slots = std::max(e->moe_slots, L.top_k + (L.has_sh ? 1 : 0));
             e->moe_ffn = std::max(e->moe_ffn, std::max(L.effn, L.sffn));
             e->n_exp_max = std::max(e->n_exp_max, L.n_exp);
+        } else if (g) {
+            // tensor-parallel FFN: whole 256-column blocks of the intermediate dimension per rank
+            const size_t ffn_g = lp.gate.rows;
+            if (ffn_g % 256) return bail(0);
+            int b0, b1;
+            sb::row_strip((int)(ffn_g / 256), g->rank, g->world, b0, b1);
+            if (b1 <= b0) return bail(0);
+            const size_t f0 = 256 * (size_t)b0;
+            L.ffn = 256 * (size_t)(b1 - b0);
+            if ((rc = eng_mat_rows(c, lp.gate, ffn_g, H, f0, L.ffn, &L.g)) != 1) return bail(rc);
+            if ((rc = eng_mat_rows(c, lp.up, ffn_g, H, f0, L.ffn, &L.u)) != 1) return bail(rc);
+            if ((rc = eng_mat_cols(c, lp.down, H, ffn_g, f0, L.ffn, &L.d)) != 1) return bail(rc);
         } else {
             L.ffn = lp.gate.rows;
             if ((rc = eng_mat(c, lp.gate, L.ffn, H, &L.g, true)) != 1) return bail(rc);
@@ -699,7 +877,7 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         }
         if (upload_f32(e, lp.norm_attn, H, &L.na) || upload_f32(e, lp.norm_ffn, H, &L.nf) ||
             upload_f32(e, lp.q_norm, L.hd, &L.qn) || upload_f32(e, lp.k_norm, L.hd, &L.kn) ||
-            upload_f32(e, lp.qkv_bias, L.qd + 2 * L.kvd, &L.bias))
+            upload_f32(e, g ? (tp_bias.empty() ? nullptr : tp_bias.data()) : lp.qkv_bias, L.qd + 2 * L.kvd, &L.bias))
             return bail(-1);
         if (L.mla) {
             e->kv_rows_total += L.kv_rank;
@@ -715,7 +893,15 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         e->ffn_max = std::max(e->ffn_max, L.ffn);
     }
     int rc;
-    if ((rc = eng_mat(c, p->lm_head, e->V, H, &e->lm, true)) != 1) return bail(rc);
+    if (g) {  // this rank's rows of the output matrix
+        int v0, v1;
+        sb::row_strip((int)e->V, g->rank, g->world, v0, v1);
+        e->vbase = (size_t)v0, e->vn = (size_t)(v1 - v0);
+        if ((rc = eng_mat_rows(c, p->lm_head, e->V, H, e->vbase, e->vn, &e->lm)) != 1) return bail(rc);
+    } else {
+        e->vbase = 0, e->vn = e->V;
+        if ((rc = eng_mat(c, p->lm_head, e->V, H, &e->lm, true)) != 1) return bail(rc);
+    }
     if (p->embed.view.bytes) {
         if (!sbk_row_bytes(p->embed.view.dtype, H) && p->embed.view.dtype != SB_DTYPE_F32) return bail(0);
         if ((rc = eng_mat(c, p->embed, e->V, H, &e->emb, false)) != 1) return bail(rc);
@@ -774,34 +960,44 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             cudaSuccess)
             return bail(fail("cudaMemcpy(kv segments)", err));
     }
-    // zeroed state; one eager token of each kind (sets kernel attributes, creates the
-    // per-stream matvec workspace outside any capture), then capture, then re-zero
-    auto zero_state = [&]() {
-        cudaError_t z = cudaMemsetAsync(e->ints, 0, 64, c->stream);
-        for (auto &L : e->L) {
-            if (L.mla) {
-                if (z == cudaSuccess) z = cudaMemsetAsync(L.latent, 0, e->ctx * L.kv_rank * 2, c->stream);
-                if (z == cudaSuccess) z = cudaMemsetAsync(L.krope, 0, e->ctx * L.kvh * L.qk_rope * 4, c->stream);
-                continue;
-            }
-            if (z == cudaSuccess) z = cudaMemsetAsync(L.kc, 0, e->ctx * L.kvd * 2, c->stream);
-            if (z == cudaSuccess) z = cudaMemsetAsync(L.vc, 0, e->ctx * L.kvd * 2, c->stream);
-        }
-        if (z == cudaSuccess && e->mla_ws) z = cudaMemsetAsync(e->mla_ws, 0, e->mla_ws_bytes, c->stream);
-        if (z == cudaSuccess && attn_ws) z = cudaMemsetAsync(e->attn_ws, 0, attn_ws, c->stream);
-        if (z == cudaSuccess) z = cudaMemsetAsync(e->am_ws, 0, sbk_argmax_ws_bytes(), c->stream);
-        if (z == cudaSuccess) z = cudaMemsetAsync(e->h, 0, H * 4, c->stream);
-        if (z == cudaSuccess) z = cudaStreamSynchronize(c->stream);
-        return z;
-    };
-    if ((err = zero_state()) != cudaSuccess) return bail(fail("decode state reset", err));
+    // zeroed state; one eager token of each kind (sets kernel attributes, builds the MoE
+    // batches, creates the per-stream matvec workspace outside any capture), then capture,
+    // then re-zero.  With a tensor-parallel group the warm-up token exchanges with the other
+    // ranks, so it waits for sb_decode_finish (called on every rank after a host barrier).
+    e->attn_ws_bytes = attn_ws;
+    if (g) {
+        e->pending_finish = true;
+        c->eng = e;
+        return 1;
+    }
+    if ((err = engine_zero(e, c->stream)) != cudaSuccess) return bail(fail("decode state reset", err));
     if ((rc = enqueue_token(e, c->stream, false))) return bail(rc);
     if (e->emb.w && (rc = enqueue_token(e, c->stream, true))) return bail(rc);
     if ((err = cudaStreamSynchronize(c->stream)) != cudaSuccess) return bail(fail("decode warm-up", err));
     if ((rc = capture(e, c->stream, false, &e->g_tok))) return bail(rc);
     if (e->emb.w && (rc = capture(e, c->stream, true, &e->g_greedy))) return bail(rc);
-    if ((err = zero_state()) != cudaSuccess) return bail(fail("decode state reset", err));
+    if ((err = engine_zero(e, c->stream)) != cudaSuccess) return bail(fail("decode state reset", err));
     c->eng = e;
+    return 1;
+}
+
+extern "C" int sb_decode_finish(sb_ctx *c)
+{
+    if (!c) return fail("null context");
+    std::lock_guard<std::mutex> lk(c->mu);
+    sb_engine *e = c->eng;
+    if (!e) return 0;
+    if (!e->pending_finish) return 1;
+    cudaError_t err = cudaSetDevice(c->device);
+    if (err != cudaSuccess) return fail("cudaSetDevice", err);
+    int rc;
+    if ((err = engine_zero(e, c->stream)) != cudaSuccess) return fail("decode state reset", err);
+    if (!e->emb.w) return fail("sb_decode_finish: a tensor-parallel engine needs the embedding table");
+    if ((rc = enqueue_token(e, c->stream, true))) return rc;
+    if ((err = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("decode warm-up", err);
+    if ((rc = capture(e, c->stream, true, &e->g_greedy))) return rc;
+    if ((err = engine_zero(e, c->stream)) != cudaSuccess) return fail("decode state reset", err);
+    e->pending_finish = false;
     return 1;
 }
 
@@ -811,7 +1007,7 @@ extern "C" int sb_decode_token(sb_ctx *c, const float *embed, size_t pos, float 
     if (!embed || !logits) return fail("null argument");
     std::lock_guard<std::mutex> lk(c->mu);
     sb_engine *e = c->eng;
-    if (!e || !e->g_tok) return 0;
+    if (!e || !e->g_tok || e->tp) return 0;  // a tensor-parallel engine holds a slice of the logits
     if (pos >= e->ctx) return fail("sb_decode_token: position beyond the prepared context");
     const uint64_t t0 = now_ns();
     cudaError_t err = cudaSetDevice(c->device);
@@ -847,6 +1043,7 @@ extern "C" int sb_decode_greedy(sb_ctx *c, const int32_t *prompt, size_t n_promp
     if (!prompt || !n_prompt || !tokens_out) return fail("null argument");
     std::lock_guard<std::mutex> lk(c->mu);
     sb_engine *e = c->eng;
+    if (e && e->pending_finish) return fail("sb_decode_greedy: call sb_decode_finish first (tensor-parallel group)");
     if (!e || !e->g_greedy) return 0;
     if (n == 0) return 1;
     if (pos + n > e->ctx || n_prompt > e->ctx) return fail("sb_decode_greedy: beyond the prepared context");

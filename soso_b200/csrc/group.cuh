@@ -1,0 +1,100 @@
+// group.cuh -- tensor-parallel groups of GPUs of one node: the exchange areas through
+// which a kernel hands its share of a result to every rank of the group.
+//
+// The reference runs on one device (its multi-machine mode is a TCP layer pipeline,
+// crates/soso-llm-core/src/pipeline.rs); the sharded decode here is new.  One process
+// drives one GPU; every rank allocates one exchange area and the ranks swap CUDA IPC
+// handles to it (through whatever host channel they share: torch.distributed in
+// soso_b200), so each rank can store into every peer's area over NVLink.
+//
+// A publishing kernel (a matvec whose rows are this rank's share of a sum, or the
+// argmax of this rank's slice of the vocabulary) stores its values into slot [rank]
+// of every rank's area, fences, and adds 1 per CTA to that area's counter of
+// (exchange point k, source rank).  A consuming kernel waits, with a bounded spin,
+// until every source's counter has reached epoch * (CTAs per publisher) and then sums
+// the slots in rank order (a fixed order: every rank forms bit-identical sums).
+// Exchange points are numbered within a token; data slots alternate by the parity of
+// k, which is enough because no rank can publish exchange k + 2 before every rank has
+// consumed exchange k (it needs their k + 1 shares first).  Counters only grow: the
+// epoch (tokens started on this group, device memory) scales their targets, so nothing
+// is ever reset between tokens.
+#pragma once
+#include "common.cuh"
+
+namespace sb {
+namespace grp {
+
+constexpr int MAXG = 8;          // ranks
+constexpr int XW = 16384;        // floats per data slot (hidden size at most)
+constexpr int NX = 512;          // exchange points per token
+constexpr unsigned WAIT_LIMIT = 1u << 26;
+
+// [data: 2][MAXG][XW] f32 | [arg: MAXG][2] u32 | [cnt: NX][MAXG] u32
+constexpr size_t DATA_BYTES = (size_t)2 * MAXG * XW * 4;
+constexpr size_t ARG_OFF = DATA_BYTES;
+constexpr size_t CNT_OFF = ARG_OFF + (size_t)MAXG * 8;
+constexpr size_t AREA_BYTES = CNT_OFF + (size_t)NX * MAXG * 4;
+
+__host__ __device__ inline float *data_slot(void *area, int k, int src)
+{
+    return reinterpret_cast<float *>(area) + ((size_t)(k & 1) * MAXG + src) * XW;
+}
+__host__ __device__ inline unsigned *arg_slot(void *area, int src)
+{
+    return reinterpret_cast<unsigned *>(reinterpret_cast<char *>(area) + ARG_OFF) + 2 * src;
+}
+__host__ __device__ inline unsigned *cnt_slot(void *area, int k, int src)
+{
+    return reinterpret_cast<unsigned *>(reinterpret_cast<char *>(area) + CNT_OFF) + (size_t)k * MAXG + src;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait until cnt[s] >= target for s < n; false (and the device error word set)
+// if the limit ran out.
+__device__ inline bool wait_counts(const unsigned *cnt, int n, unsigned target)
+{
+    for (int s = 0; s < n; s++) {
+        unsigned it = 0;
+        while (ld_acquire_sys(cnt + s) < target) {
+            if (++it > WAIT_LIMIT) {
+                set_dev_error(0x91u);
+                return false;
+            }
+            __nanosleep(100);
+        }
+    }
+    return true;
+}
+
+// Where a kernel publishes its share of exchange point k.
+struct Pub {
+    float *dst[MAXG];       // data slot [rank] of every rank's area
+    unsigned *cnt[MAXG];    // counter (k, rank) of every rank's area
+    int n;                  // ranks (0: not publishing)
+};
+
+// What a kernel waits for before reading exchange point k from its own area.
+struct Wait {
+    const unsigned *cnt;    // counters (k, 0..n-1) of the own area
+    const unsigned *epoch;  // device epoch (tokens started)
+    int n;                  // ranks (0: nothing to wait for)
+    int per;                // counter increments per source per token (publisher CTAs)
+};
+
+}  // namespace grp
+}  // namespace sb
+
+struct sb_group {
+    int rank = 0, world = 1;
+    void *area = nullptr;                       // own exchange area (cudaMalloc)
+    void *peer[sb::grp::MAXG] = {};             // every rank's area as mapped here (peer[rank] = area)
+    unsigned *epoch = nullptr;                  // device: tokens started on this group
+    float *ones = nullptr;                      // device: MAXG x 1.0f (weights of the rank sum)
+    bool opened = false;
+};

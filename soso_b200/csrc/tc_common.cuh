@@ -1,5 +1,5 @@
 // tc_common.cuh -- building blocks of the tensor-core matvec kernels (tc_mmv.cuh):
-// mbarrier ring primitives, the 2-D TMA tensor load (never with multicast) and
+// mbarrier ring primitives, the 2-D TMA tensor load (into this CTA only) and
 // the warp-level MMA forms the quantized formats use.
 #pragma once
 #include <cuda.h>
@@ -63,7 +63,7 @@ __device__ __forceinline__ uint64_t l2_evict_first()
     return p;
 }
 
-// 2-D tiled TMA load (no multicast): box at element coords (x = u64 column, y = row).
+// 2-D tiled TMA load into this CTA: box at element coords (x = u64 column, y = row).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar,
                                             uint64_t policy)
 {
@@ -179,7 +179,7 @@ struct XLoad {
         if (ny) {
             float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             for (int k = 0; k < ny; k++) {
-                const float4 y = ys[k * ys4 + i];
+                const float4 y = __ldcg(ys + k * ys4 + i);  // may be written by peers: read at L2
                 acc.x += y.x * yw[k], acc.y += y.y * yw[k], acc.z += y.z * yw[k], acc.w += y.w * yw[k];
             }
             v.x = acc.x + v.x, v.y = acc.y + v.y, v.z = acc.z + v.z, v.w = acc.w + v.w;

@@ -13,7 +13,7 @@
 //
 // Per CTA: warp 0 is the producer -- one 2-D TMA tensor copy per stage (a
 // 16-row box of F::BOXW u64 of the weight matrix; rows past the end and columns
-// past a row's end are zero-filled by the TMA unit; no multicast) into a ring
+// past a row's end are zero-filled by the TMA unit; each CTA loads only its own tiles) into a ring
 // of F::NSLOT slots, issued before griddepcontrol.wait so the stream overlaps
 // the previous kernel under programmatic dependent launch.  F::NCW consumer
 // warps form F::NSTREAM teams of F::NCONS; team j takes the CTA-local stages
@@ -28,6 +28,7 @@
 #include "tc_q4k.cuh"
 #include "tc_q6k.cuh"
 #include "tc_q80.cuh"
+#include "group.cuh"
 
 namespace sb {
 namespace tcmv {
@@ -52,6 +53,8 @@ struct Batch {
     int max_cols, max_groups;  // shared-memory capacities (prep, partial table)
     int split_groups;          // 1: CTAs take whole 16-row groups (no cut groups, no fix-up)
     int total_groups;
+    grp::Pub pub;              // also store matrix 0's rows into the group's exchange areas
+    grp::Wait wait;            // wait for an exchange point before reading the input
 };
 
 template <class F>
@@ -192,6 +195,11 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
         const int team = cwg / F::NCONS, cw = cwg % F::NCONS, g = lane >> 2, t = lane & 3;
         const typename F::Lane L = F::lane_setup(g, t);
         griddep_wait();  // x of every matrix is written by the previous kernel
+        if (B.wait.n) {  // the input's residual set comes from every rank of the group
+            if (cwg == 0 && lane == 0)
+                if (!grp::wait_counts(B.wait.cnt, B.wait.n, *B.wait.epoch * (unsigned)B.wait.per)) failed = true;
+            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+        }
         const float *prev_x = nullptr;
         int prev_cols = 0;
         for (int mi = m_first; mi <= m_last && nst > 0; mi++) {
@@ -293,7 +301,10 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
                 for (int w = 0; w < NCW; w++) v += s.part[(gl * NCW + w) * 16 + r];
                 const bool cut = (gl == 0 && head_cut) || (gl == ng - 1 && tail_cut);
                 if (!cut) {
-                    if (row < d.rows) d.y[row] = v;
+                    if (row < d.rows) {
+                        d.y[row] = v;
+                        for (int p = 0; p < B.pub.n; p++) B.pub.dst[p][row] = v;
+                    }
                 } else {
                     // side 0: the group holding this CTA's first stage, side 1: any other (its last)
                     const int ga = d.st_begin + (gs0 + gl) * spg;
@@ -308,6 +319,13 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
         // let every TMA copy issued into this CTA's shared memory land before exiting (bounded)
         if (warp == 0 && lane == 0)
             for (int k = nst > NSLOT ? nst - NSLOT : 0; k < nst; k++) mbar_wait(&s.full[k % NSLOT], (k / NSLOT) & 1);
+    }
+    if (B.pub.n) {
+        // every row this CTA owns is in the peers' areas: count the CTA (all CTAs count,
+        // so the consumers' target is epoch * grid whatever the split)
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x < B.pub.n) atomicAdd_system(B.pub.cnt[threadIdx.x], 1u);
     }
     __syncthreads();
     if (nst <= 0) return;
@@ -551,6 +569,8 @@ inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XS
     b.total = st;
     b.total_groups = cnt;
     b.xs = xs ? *xs : XSrc{};
+    b.pub = grp::Pub{};
+    b.wait = grp::Wait{};
     if (b.xs.mode != XS_PLAIN) {
         if (b.xs.mode != XS_NORM && b.xs.mode != XS_SWIGLU) return -1;
         if (b.xs.mode == XS_NORM) {
@@ -622,7 +642,7 @@ inline cudaLaunchConfig_t mmv_config(int grid, int threads, size_t smem, int pdl
 // zero); at most cnt_cap 16-row groups in the batch.
 template <class F>
 inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int grid, int pdl, cudaStream_t stream,
-                           const XSrc *xs = nullptr)
+                           const XSrc *xs = nullptr, const grp::Pub *pub = nullptr, const grp::Wait *wait = nullptr)
 {
     if (n < 1 || n > MAXB) return -1;
     static Batch b;  // large: built host-side, passed by value as the kernel parameter
@@ -634,6 +654,19 @@ inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int gri
     size_t smem = 0;
     int rc = build_batch<F>(ox, n, cnt_cap, grid, xs, &b, &smem);
     if (rc) return rc;
+    if (wait) b.wait = *wait;
+    if (pub && pub->n) {
+        // a published matrix's rows must be final in the CTA that computes them: whole groups
+        if (n != 1) return -1;
+        b.pub = *pub;
+        if (!b.split_groups) {
+            const int need = (b.total_groups + grid - 1) / grid + 1;
+            if (need > b.max_groups) b.max_groups = need;
+            smem = smem_bytes<F>(b.max_cols, b.max_groups);
+            if (smem > 227 * 1024) return -5;
+            b.split_groups = 1;
+        }
+    }
     if ((rc = ensure_smem(tc_mmv_kernel<F>, smem, smem_rec))) return rc;
     cudaLaunchAttribute attr[1];
     const cudaLaunchConfig_t cfg = mmv_config(grid, F::THREADS, smem, pdl, stream, attr);
@@ -659,13 +692,13 @@ inline int launch_dev_batch(const Batch *dev, size_t smem, Ws wsd, int grid, int
 // As launch_batch_ws over a workspace of ws_bytes(grid) bytes.
 template <class F>
 inline int launch_batch(const MatOp *ops, int n, void *ws, int grid, int pdl, cudaStream_t stream,
-                        const XSrc *xs = nullptr)
+                        const XSrc *xs = nullptr, const grp::Pub *pub = nullptr, const grp::Wait *wait = nullptr)
 {
     uint8_t *wsb = reinterpret_cast<uint8_t *>(ws);
     Ws wsd;
     wsd.cnt = reinterpret_cast<unsigned *>(wsb);
     wsd.part = reinterpret_cast<float *>(wsb + ws_part_off());
-    return launch_batch_ws<F>(ops, n, wsd, CNT_MAX, grid, pdl, stream, xs);
+    return launch_batch_ws<F>(ops, n, wsd, CNT_MAX, grid, pdl, stream, xs, pub, wait);
 }
 
 // Repack GGML Q6_K rows (reference layout) into the packed layout of tc_q6k.cuh.

@@ -171,7 +171,10 @@ def _f32(a: np.ndarray | None):
 class DecodeSession:
     """A prepared whole-token decode on one device (sb_decode_prepare)."""
 
-    def __init__(self, cfg: DenseConfig, model: dict, device: int = 0, ctx_handle=None):
+    def __init__(self, cfg: DenseConfig, model: dict, device: int = 0, ctx_handle=None, group=None):
+        """group = (rank, world, all_gather): tensor-parallel decode across `world` processes
+        (soso_b200.tp); all_gather(bytes) -> every rank's bytes, and it doubles as the host
+        barrier before the first (exchanging) warm-up token."""
         self.cfg = cfg
         self.model = model
         L = lib()
@@ -182,6 +185,9 @@ class DecodeSession:
                 raise SbError(last_error())
             ctx_handle = h
         self.ctx = ctx_handle
+        if group is not None and group[1] > 1:
+            from . import tp
+            tp.open_group(self.ctx, group[0], group[1], group[2])
         self._keep = []
         H = cfg.hidden
         layers = (SbLayerPlan * cfg.n_layers)()
@@ -223,6 +229,11 @@ class DecodeSession:
         rc = L.sb_decode_prepare(self.ctx, ctypes.byref(plan))
         if rc != 1:
             raise SbError(f"sb_decode_prepare returned {rc}: {last_error()}")
+        if group is not None and group[1] > 1:
+            group[2](b"prepared")  # every rank has its shards resident: the warm-up may exchange
+            rc = L.sb_decode_finish(self.ctx)
+            if rc != 1:
+                raise SbError(f"sb_decode_finish returned {rc}: {last_error()}")
 
     def _moe_plan(self, l: int) -> SbMoePlan:
         """MoeDec (gpu.rs:130-137) of layer l: router, experts [gate, up, down] each, shared expert."""
