@@ -624,6 +624,46 @@ def run_batch_case(launches: int) -> None:
         raise SystemExit(1)
 
 
+def run_prefill_case(launches: int) -> None:
+    """The tcgen05 prefill GEMM on configs[4]'s dense FFN gate shape (10944 x 2048, 512 tokens,
+    bf16 operands), `launches` times without a graph (for ncu); checks one output row."""
+    import torch
+
+    import oracle
+    from soso_b200 import synth
+    from soso_b200._lib import lib
+    L = lib()
+    rows, cols, n = 10944, 2048, 512
+    g = synth.rng("ncu", "prefill")
+    w = synth.random_weights(Q4K, rows, cols, g)
+    x = g.standard_normal((n, cols)).astype(np.float32)
+    wd, xd = torch.from_numpy(w).cuda(), torch.from_numpy(x).cuda()
+    y = torch.empty(n, rows, device="cuda")
+    ws = torch.empty(int(L.sbk_matmul_ws_bytes(n, cols)), dtype=torch.uint8, device="cuda")
+    for _ in range(launches):
+        if L.sbk_matmul(Q4K, wd.data_ptr(), rows, cols, n, xd.data_ptr(), y.data_ptr(), ws.data_ptr(), 0, 0,
+                        torch.cuda.current_stream().cuda_stream):
+            raise SystemExit("sbk_matmul rejected")
+    torch.cuda.synchronize()
+    t = oracle.matvec_f64(Q4K, w, rows, cols, x[7])
+    err = float(np.max(np.abs(y[7].cpu().numpy() - t)) / np.sqrt(np.mean(t ** 2)))
+    print(json.dumps({"case": "prefill", "launches": launches, "max_err_over_rms": err}))
+    if err > 3e-2:
+        raise SystemExit(1)
+
+
+def run_decode_case(tokens: int) -> None:
+    """A 4-layer slice of configs[2] (the dense decoder) through the whole-token engine:
+    `tokens` greedy steps (eager warm-up, then graph replays) -- for an ncu launch list."""
+    from soso_b200 import decode
+    cfg = decode.DenseConfig(n_layers=4, hidden=2048, heads=16, kv_heads=2, head_dim=128, ffn=11008, vocab=151936,
+                             ctx=4096)
+    sess = decode.DecodeSession(cfg, decode.synth_model(cfg, "ncu"))
+    toks = sess.greedy(np.arange(8, dtype=np.int32), tokens)
+    sess.close()
+    print(json.dumps({"case": "decode", "tokens": toks.tolist()}))
+
+
 def run_case(name: str, launches: int) -> None:
     """Plain launches of one kernel over a rotation of copies (for ncu); prints a check line."""
     import torch
@@ -661,7 +701,7 @@ def run_case(name: str, launches: int) -> None:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ncu-case", choices=sorted(NCU_CASES) + ["q4k_batch"], default=None)
+    ap.add_argument("--ncu-case", choices=sorted(NCU_CASES) + ["q4k_batch", "prefill", "decode"], default=None)
     ap.add_argument("--launches", type=int, default=12)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -673,6 +713,12 @@ def main():
     args = ap.parse_args()
     if args.ncu_case == "q4k_batch":
         run_batch_case(args.launches)
+        return
+    if args.ncu_case == "prefill":
+        run_prefill_case(args.launches)
+        return
+    if args.ncu_case == "decode":
+        run_decode_case(args.launches)
         return
     if args.ncu_case:
         run_case(args.ncu_case, args.launches)

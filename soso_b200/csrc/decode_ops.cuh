@@ -133,6 +133,10 @@ constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAXG = 8;
 constexpr int ATT_MAXC = 64;  // spans per kv head at most
 constexpr int ATT_KPAD = 8;   // f16 pad per cached row in shared memory (272-byte rows)
+// q in shared memory: 8 floats of padding after every 32, so the four quarter-dims a warp
+// reads at once (32 floats apart) fall in different banks
+constexpr int ATT_QS = 160;   // floats per head row (128 + 4 * 8)
+__host__ __device__ constexpr int att_qi(int d) { return d + ((d >> 5) << 3); }
 
 struct AttnArgs {
     const float *qkv;          // q [heads][hd]; with rope: then k [kv_heads][hd], v [kv_heads][hd]
@@ -160,7 +164,7 @@ template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(AttnArgs a)
 {
     static_assert(HD == 128, "one lane per two RoPE pairs; one thread per two P.V dims of two heads");
-    __shared__ float qs[ATT_MAXG][HD];
+    __shared__ float qs[ATT_MAXG][ATT_QS];
     __shared__ __align__(16) uint16_t ks[ATT_CH][HD + ATT_KPAD];
     __shared__ __align__(16) uint16_t vs[ATT_CH][HD + ATT_KPAD];
     __shared__ __align__(16) uint16_t knew[HD], vnew[HD];
@@ -241,7 +245,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(AttnArgs a)
         }
         if (kind == 0) {
 #pragma unroll
-            for (int k = 0; k < 4; k++) qs[task][e[k]] = v[k];
+            for (int k = 0; k < 4; k++) qs[task][att_qi(e[k])] = v[k];
         } else {
             uint16_t *row = (kind == 1 ? a.kc : a.vc) + (size_t)pos * a.kv_dim + kvh * HD;
             uint16_t *nrow = kind == 1 ? knew : vnew;
@@ -279,10 +283,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(AttnArgs a)
 #pragma unroll
                     for (int e2 = 0; e2 < 4; e2++) {
                         const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&kw[e2]));
-                        const int d = dq * (HD / 4) + v8 * 8 + 2 * e2;
+                        const int d = att_qi(dq * (HD / 4) + v8 * 8 + 2 * e2);
 #pragma unroll
                         for (int j = 0; j < ATT_MAXG; j++)
-                            if (j < G) part[j] += qs[j][d] * kf.x + qs[j][d + 1] * kf.y;
+                            if (j < G) {
+                                const float2 qv = *reinterpret_cast<const float2 *>(&qs[j][d]);
+                                part[j] += qv.x * kf.x + qv.y * kf.y;
+                            }
                     }
                 }
             }
@@ -362,41 +369,53 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(AttnArgs a)
     // merge spans 0..nch-1 (combinar_trozos): per head, weights exp(m_c - M) from one warp,
     // then every output element as an independent-load sum over spans
     const float *base = a.part + (size_t)kvh * ATT_MAXC * G * (HD + 2);
+    // (m, l) of every span read once (two spans per lane at most: ATT_MAXC = 64)
     if (warp < G) {
         const int j = warp;
-        float M = -INFINITY;
-        for (int cc = lane; cc < nch; cc += 32) {
+        float mv[2], lv[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int cc = lane + 32 * u;
             const float *pc = base + ((size_t)cc * G + j) * (HD + 2);
-            if (__ldcg(pc + HD + 1) > 0.0f) M = fmaxf(M, __ldcg(pc + HD));
+            lv[u] = cc < nch ? __ldcg(pc + HD + 1) : 0.0f;
+            mv[u] = cc < nch ? __ldcg(pc + HD) : -INFINITY;
         }
+        float M = fmaxf(lv[0] > 0.0f ? mv[0] : -INFINITY, lv[1] > 0.0f ? mv[1] : -INFINITY);
 #pragma unroll
         for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         float L = 0.0f;
-        for (int cc = lane; cc < nch; cc += 32) {
-            const float *pc = base + ((size_t)cc * G + j) * (HD + 2);
-            const float li = __ldcg(pc + HD + 1);
-            const float w = li > 0.0f ? expf(__ldcg(pc + HD) - M) : 0.0f;
-            sw[j][cc] = w;
-            L += w * li;
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int cc = lane + 32 * u;
+            const float w = lv[u] > 0.0f ? expf(mv[u] - M) : 0.0f;
+            if (cc < nch) sw[j][cc] = w;
+            L += w * lv[u];
         }
         L = warp_sum(L);
         if (lane == 0) s_l[j] = L;
     }
     __syncthreads();
-    for (int i = tid; i < G * HD; i += ATT_THREADS) {
-        const int j = i / HD, d = i % HD;
-        float o = 0.0f;
-        int cc = 0;
-        for (; cc + 4 <= nch; cc += 4) {
-            float v[4];
+    // every thread sums its G*HD/ATT_THREADS outputs together, span by span, so the loads of
+    // one span (and of the next few) are all in flight at once
+    constexpr int PER = ATT_MAXG * HD / ATT_THREADS;  // 4
+    float o[PER];
 #pragma unroll
-            for (int k = 0; k < 4; k++) v[k] = __ldcg(base + ((size_t)(cc + k) * G + j) * (HD + 2) + d);
+    for (int u = 0; u < PER; u++) o[u] = 0.0f;
+#pragma unroll 4
+    for (int cc = 0; cc < nch; cc++) {
 #pragma unroll
-            for (int k = 0; k < 4; k++) o += sw[j][cc + k] * v[k];
+        for (int u = 0; u < PER; u++) {
+            const int i = tid + u * ATT_THREADS, j = i / HD, d = i % HD;
+            if (j < G) o[u] += sw[j][cc] * __ldcg(base + ((size_t)cc * G + j) * (HD + 2) + d);
         }
-        for (; cc < nch; cc++) o += sw[j][cc] * __ldcg(base + ((size_t)cc * G + j) * (HD + 2) + d);
-        const float L = s_l[j];
-        a.out[(kvh * G + j) * HD + d] = L > 0.0f ? o * (1.0f / L) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+        const int i = tid + u * ATT_THREADS, j = i / HD, d = i % HD;
+        if (j < G) {
+            const float L = s_l[j];
+            a.out[(kvh * G + j) * HD + d] = L > 0.0f ? o[u] * (1.0f / L) : 0.0f;
+        }
     }
     if (tid == 0) a.cnt[kvh] = 0u;
     griddep_launch();
