@@ -104,17 +104,23 @@ __device__ __forceinline__ void mma_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Four int8 pieces of v (|v| < 128): v = p0 + p1/2^7 + p2/2^14 + p3/2^21 to 28
-// bits; every residual is exact in f32.  Byte i of pk[p] gets piece p.
-__device__ __forceinline__ void int8_pieces(float v, int i, uint32_t (&pk)[4])
+// Four int8 pieces of each of four values (|v| < 128): v = p0 + p1/2^7 + p2/2^14 + p3/2^21
+// to 28 bits.  v * 2^21 is rounded to an integer i (|i| < 2^28, exact scaling); p0 = i >> 21
+// (-128..127) and p1, p2, p3 are the next 7-bit fields of i (0..127), so
+// i = p0*2^21 + p1*2^14 + p2*2^7 + p3 exactly.  Byte k of pk[p] gets piece p of value k.
+__device__ __forceinline__ void int8_pieces4(float4 v, uint32_t (&pk)[4])
 {
+    const int i[4] = {__float2int_rn(v.x * 2097152.0f), __float2int_rn(v.y * 2097152.0f),
+                      __float2int_rn(v.z * 2097152.0f), __float2int_rn(v.w * 2097152.0f)};
+    uint32_t p0 = 0u, p1 = 0u, p2 = 0u, p3 = 0u;
 #pragma unroll
-    for (int pc = 0; pc < 4; pc++) {
-        float r = rintf(v);
-        r = fminf(fmaxf(r, -127.0f), 127.0f);
-        pk[pc] |= ((uint32_t)__float2int_rn(r) & 0xFFu) << (8 * i);
-        v = (v - r) * 128.0f;
+    for (int k = 0; k < 4; k++) {
+        p0 |= (uint32_t)((i[k] >> 21) & 255) << (8 * k);
+        p1 |= (uint32_t)((i[k] >> 14) & 127) << (8 * k);
+        p2 |= (uint32_t)((i[k] >> 7) & 127) << (8 * k);
+        p3 |= (uint32_t)(i[k] & 127) << (8 * k);
     }
+    pk[0] = p0, pk[1] = p1, pk[2] = p2, pk[3] = p3;
 }
 
 // 2^e with 2^e > max |v| over the warp (from the max's biased exponent), clamped for

@@ -8,8 +8,8 @@
 // one AND of a qs word gives four low-nibble codes, another four high-nibble
 // codes times 16 (not shifted; the 16 is folded into the scales).  x enters as
 // four int8 pieces per element, x * 2^(7-ex) = p0 + p1/2^7 + p2/2^14 + p3/2^21
-// with 2^ex above the block's max |x| (28 significant bits, every residual
-// exact in f32), one piece per B column.  Products and their sums are exact
+// with 2^ex above the block's max |x| (x * 2^(7-ex) rounded once to a multiple of
+// 2^-21, then split into exact integer fields), one piece per B column.  Products and their sums are exact
 // integers; the 6-bit scales multiply them in integer arithmetic (IMAD), and
 // only the per-block result is converted to f32 and scaled by d.  The min term
 // sum_j m_j * Sum x_j is one f16 MMA per block: m as f16 subnormals (exact)
@@ -95,11 +95,8 @@ struct Q4K {
                 const int sblk = n >> 5, e = n & 31;
                 const int sig = (sblk >> 1) & 1, q = 2 * (sblk >> 2) + (sblk & 1);
                 const int word = 2 * ((e >> 3) & 1) + ((e >> 2) & 1), tp = e >> 4;
-                uint32_t pk[4] = {0u, 0u, 0u, 0u};
-                int8_pieces(v4.x * scl, 0, pk);
-                int8_pieces(v4.y * scl, 1, pk);
-                int8_pieces(v4.z * scl, 2, pk);
-                int8_pieces(v4.w * scl, 3, pk);
+                uint32_t pk[4];
+                int8_pieces4(make_float4(v4.x * scl, v4.y * scl, v4.z * scl, v4.w * scl), pk);
 #pragma unroll
                 for (int pc = 0; pc < 4; pc++) {
                     const int L = 2 * (4 * sig + pc) + tp;

@@ -111,11 +111,8 @@ struct Q6KP {
 #pragma unroll
             for (int bsel = 0; bsel < 2; bsel++) {
                 const float4 v4 = bsel ? vb : va;
-                uint32_t pk[4] = {0u, 0u, 0u, 0u};
-                int8_pieces(v4.x * scl, 0, pk);
-                int8_pieces(v4.y * scl, 1, pk);
-                int8_pieces(v4.z * scl, 2, pk);
-                int8_pieces(v4.w * scl, 3, pk);
+                uint32_t pk[4];
+                int8_pieces4(make_float4(v4.x * scl, v4.y * scl, v4.z * scl, v4.w * scl), pk);
                 const int word = 2 * (mi & 1) + bsel;
 #pragma unroll
                 for (int pc = 0; pc < 4; pc++) {
@@ -131,7 +128,7 @@ struct Q6KP {
                 const int s = l >> 1;
 #pragma unroll
                 for (int pc = 0; pc < 4; pc++) {
-                    const int hi = sx[pc] >> 6, lo = sx[pc] & 63;  // sx = 64 hi + lo, |sx| <= 2032
+                    const int hi = sx[pc] >> 6, lo = sx[pc] & 63;  // sx = 64 hi + lo, |sx| <= 2048
                     ofr[(b * 32 + (2 * pc) * 4 + (s >> 2)) * 4 + (s & 3)] = (int8_t)hi;
                     ofr[(b * 32 + (2 * pc + 1) * 4 + (s >> 2)) * 4 + (s & 3)] = (int8_t)lo;
                 }

@@ -73,11 +73,8 @@ struct Q80 {
             const float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
             const int ex = warp_exp_above(mx);
             const float scl = pow2f(7 - ex);
-            uint32_t pk[4] = {0u, 0u, 0u, 0u};
-            int8_pieces(v.x * scl, 0, pk);
-            int8_pieces(v.y * scl, 1, pk);
-            int8_pieces(v.z * scl, 2, pk);
-            int8_pieces(v.w * scl, 3, pk);
+            uint32_t pk[4];
+            int8_pieces4(make_float4(v.x * scl, v.y * scl, v.z * scl, v.w * scl), pk);
             const int b = l >> 3, q = l & 7;
 #pragma unroll
             for (int pc = 0; pc < 4; pc++) frag[((u * 4 + b) * 4 + pc) * 8 + q] = pk[pc];
