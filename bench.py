@@ -305,16 +305,16 @@ def run_ours(args) -> None:
         e2e_s = float(t.item())
     L.sb_destroy(ctx)
 
-    # the other BASELINE configs on this GPU: C1 (Q8_0 matvec), the decode models (C3 dense; C4
-    # MoE and C5 MLA+MoE at N=1 only: each rank would hold its own 11-16 GB synthetic model),
-    # and the tcgen05 prefill GEMM on C5's prefill shapes
+    # the other BASELINE configs: C1 (Q8_0 matvec), the decode models (C3 dense, C4 MoE, C5
+    # MLA+MoE; one model split over the ranks at N > 1), and the tcgen05 prefill GEMM on C5's
+    # prefill shapes (N = 1)
     extra = {}
     if not args.no_decode:
         extra["c1_q8_0_matvec"] = q80_bench(dev)
         extra["decode"] = decode_bench(local, rank, "dense", world)
+        extra["decode_moe"] = decode_bench(local, rank, "moe", world)
+        extra["decode_mla"] = decode_bench(local, rank, "mla", world)
         if world == 1:
-            extra["decode_moe"] = decode_bench(local, rank, "moe")
-            extra["decode_mla"] = decode_bench(local, rank, "mla")
             extra["prefill"] = prefill_bench(dev)
 
     cpu = None
@@ -366,6 +366,45 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def weight_bytes_per_token(cfg) -> float:
+    """Weight bytes one decode token reads (reference layouts): every layer's attention and
+    dense FFN or router + top_k routed experts + shared expert, and the output matrix; the
+    same whatever the split over GPUs."""
+    from soso_b200 import decode
+    from soso_b200.formats import row_bytes
+    H, total = cfg.hidden, 0.0
+    for l in range(cfg.n_layers):
+        for name, (rows, cols) in decode.shapes(cfg).items():
+            if cfg.is_moe(l) and name.startswith("ffn_"):
+                continue
+            total += rows * row_bytes(cfg.dtypes[name], cols)
+        if cfg.is_moe(l):
+            total += cfg.n_exp * row_bytes(cfg.dtypes["ffn_gate_inp"], H)
+            f = cfg.top_k * cfg.moe_ffn + cfg.shared_ffn
+            total += 2 * f * row_bytes(cfg.dtypes["ffn_gate"], H)
+            total += H * (cfg.top_k * row_bytes(cfg.dtypes["ffn_down"], cfg.moe_ffn)
+                          + (row_bytes(cfg.dtypes["ffn_down"], cfg.shared_ffn) if cfg.shared_ffn else 0))
+    return total + cfg.vocab * row_bytes(cfg.dtypes["output"], H)
+
+
+def parallelism(cfg, world: int) -> str:
+    """How the library splits a decode model over `world` GPUs (soso_b200.tp)."""
+    from soso_b200 import tp
+    parts = []
+    parts.append(f"attention tp{world} (query heads)" if tp.attention_split(cfg, world) else
+                 "attention whole on every rank")
+    if cfg.ffn and cfg.ffn % 256 == 0:
+        parts.append(f"dense FFN tp{world} (256-column blocks)")
+    elif cfg.ffn:
+        parts.append("dense FFN whole on every rank")
+    if cfg.n_exp:
+        parts.append(f"experts ep{world} (expert IDs split, router on every rank"
+                     + (", shared expert on rank layer % world" if cfg.shared_ffn else "") + ")")
+    parts.append("vocabulary rows split")
+    return "; ".join(parts) + ("; partial sums and expert outputs exchanged through peer memory inside the "
+                               "matvec kernels")
+
+
 def decode_bench(device: int, rank: int, which: str = "dense", world: int = 1) -> dict:
     """Whole-token decode through the engine (sb_decode_greedy: one CUDA graph per token,
     tokens chained on the device), batch-1 greedy decode of 256 tokens after a 128-token
@@ -382,7 +421,8 @@ def decode_bench(device: int, rank: int, which: str = "dense", world: int = 1) -
         from soso_b200 import tp
         group = (rank, world, tp.torch_all_gather())
     seed = f"{which}.{rank if group is None else 0}"
-    model = decode.synth_model(cfg, seed)
+    # under expert parallelism a rank makes only the experts it holds (same bytes as whole)
+    model = decode.synth_model(cfg, seed, held=(rank, world) if group and cfg.n_exp else None)
     sess = decode.DecodeSession(cfg, model, device=device, group=group)
     prompt = synth.rng("prompt", which, 0 if group else rank).integers(0, cfg.vocab, 128).astype(np.int32)
     sess.greedy(prompt[:8], 8)  # warm
@@ -395,14 +435,7 @@ def decode_bench(device: int, rank: int, which: str = "dense", world: int = 1) -
     dt = time.perf_counter() - t0
     if group:
         dt = max(float(v) for v in group[2](repr(dt).encode()))  # the slowest rank
-    weights = 0
-    for k, v in model.items():
-        if k == "token_embd" or v.dtype != np.uint8:
-            continue
-        if ".E" in k:  # routed experts: top_k of n_exp read per token
-            weights += v.nbytes * cfg.top_k / cfg.n_exp
-        else:
-            weights += v.nbytes
+    weights = weight_bytes_per_token(cfg)
     # cache bytes read per cached position: K and V rows (f16), or the latent row (f16) and the
     # rope keys (f32) of an MLA layer
     kv_per_pos = (cfg.n_layers * (cfg.kv_rank * 2 + cfg.kv_heads * cfg.qk_rope * 4) if cfg.mla
@@ -430,8 +463,7 @@ def decode_bench(device: int, rank: int, which: str = "dense", world: int = 1) -
                          "roofline_tok_per_s": round(hbm * 1e9 / bytes_tok, 1)},
             "timing": "wall clock around sb_decode_greedy(256 steps); graph launches chained on one stream"
                       + ("; max over ranks" if group else ""),
-            "parallelism": f"tp{world} (attention heads, FFN blocks and vocabulary sharded; partial sums exchanged "
-                           "through peer memory inside the matvec kernels)" if group else "1 GPU",
+            "parallelism": parallelism(cfg, world) if group else "1 GPU",
             "last_tokens": toks[-4:].tolist()}
 
 

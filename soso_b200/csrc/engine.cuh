@@ -77,8 +77,12 @@ __global__ void kv_rows_kernel(const KvSeg *segs, const int *pos, uint16_t *out)
 // matvecs: softmax over all experts, stable top-k by weight, renormalised
 // (gemm::topk_softmax, crates/soso-llm-core/src/gemm.rs:62-91, as router_topk_kernel),
 // the shared expert's weight sigmoid(gate_row . x) or 1 (layer.rs:1883-1907), and the
-// expert choice written into the device-side batches of the two expert launches
-// (their matrices point at the chosen experts' tensor maps).  One CTA.
+// expert choice written into the device-side batches of the two expert launches.
+// The choices whose experts are resident here (all of them on one GPU; the rank's range
+// of expert IDs under expert parallelism) are taken in choice order; with m of them the
+// launches run batch m of their k + 1 prepared batches, whose first m matrices (pairs for
+// gate|up) now point at those experts' tensor maps and, for the downs, publish to the
+// exchange slot of their choice.  One CTA.
 struct RouteArgs {
     const float *logits;
     int n_exp, k;
@@ -89,8 +93,12 @@ struct RouteArgs {
     const float *nw;
     float eps;
     int H, has_shared;
-    tcmv::Batch *gu, *dn;   // gu.d[2i] / d[2i+1] = gate / up of choice i; dn.d[i] = its down
-    const CUtensorMap *maps;  // [n_exp][3]: gate, up, down
+    tcmv::Batch *gu, *dn;   // [k + 1] each: batch m runs m resident choices (+ the shared
+                            // expert, when it is computed here, as matrix m)
+    int *sel;               // the batch index m, for both launches
+    const CUtensorMap *maps;  // [hi - lo][3]: gate, up, down of the resident experts
+    int lo, hi;             // resident experts [lo, hi)
+    int xw;                 // floats between exchange slots: the down of choice r publishes at r * xw
 };
 
 __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
@@ -99,6 +107,8 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
     __shared__ float red[32];
     __shared__ float topw[64];
     __shared__ int topi[64];
+    __shared__ int own[64];
+    __shared__ int s_m;
     griddep_wait();
     const int tid = threadIdx.x, n = a.n_exp;
     float m = -INFINITY;
@@ -163,12 +173,21 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
             a.idx[r] = topi[r];
         }
         if (a.has_shared) a.wts[a.k] = sg;
+        int mo = 0;
+        for (int r = 0; r < a.k; r++)
+            if (topi[r] >= a.lo && topi[r] < a.hi) own[mo++] = r;
+        s_m = mo;
+        *a.sel = mo;
     }
-    if (tid < a.k) {
-        const int e = topi[tid];
-        a.gu->d[2 * tid].mapp = a.maps + 3 * e;
-        a.gu->d[2 * tid + 1].mapp = a.maps + 3 * e + 1;
-        a.dn->d[tid].mapp = a.maps + 3 * e + 2;
+    __syncthreads();
+    const int mo = s_m;  // resident choices: batch mo of the k + 1
+    if (tid < mo) {
+        const int r = own[tid], e = topi[r] - a.lo;
+        tcmv::Batch *gu = a.gu + mo, *dn = a.dn + mo;
+        gu->d[2 * tid].mapp = a.maps + 3 * e;
+        gu->d[2 * tid + 1].mapp = a.maps + 3 * e + 1;
+        dn->d[tid].mapp = a.maps + 3 * e + 2;
+        dn->d[tid].pub_off = r * a.xw;
     }
     griddep_launch();
 }
@@ -210,13 +229,18 @@ struct EngLayer {
     bool moe = false, has_sh = false;
     size_t n_exp = 0, top_k = 0, effn = 0, sffn = 0;
     EngMat router, sh[3];
-    std::vector<EngMat> ex;            // [n_exp][3]
+    std::vector<EngMat> ex;            // [hi - lo][3]: the resident experts
+    size_t ex_lo = 0, ex_hi = 0;       // resident experts (all, or this rank's IDs)
+    bool sh_here = false;              // the shared expert is computed on this GPU
     float *sg = nullptr;               // shared expert gate row, or null (weight 1)
-    CUtensorMap *maps = nullptr;       // device [n_exp][3]: the experts' tensor maps
-    sb::tcmv::Batch *gu_b = nullptr;   // device batches of the two expert launches (built on
-    sb::tcmv::Batch *dn_b = nullptr;   //   the first enqueue; the route kernel picks the maps)
+    CUtensorMap *maps = nullptr;       // device [hi - lo][3]: the resident experts' tensor maps
+    sb::tcmv::Batch *gu_b = nullptr;   // device batches of the two expert launches, [top_k + 1]
+    sb::tcmv::Batch *dn_b = nullptr;   //   each (built on the first enqueue; the route kernel
+    int *sel = nullptr;                //   picks one and its maps, and writes its index here)
     size_t gu_smem = 0, dn_smem = 0;
     const float *built_for = nullptr;  // residual buffer the batches read
+    // tensor parallelism: attention heads / FFN blocks sharded (else computed whole here)
+    bool tp_attn = false, tp_ffn = false;
     // MLA attention (sb_mla_plan): latent cache + rope keys instead of K/V rows
     bool mla = false;
     size_t q_rank = 0, kv_rank = 0, qk_nope = 0, qk_rope = 0, v_dim = 0;
@@ -399,49 +423,74 @@ int run_mv(sb_engine *e, const EngMat *const *ms, float *const *ys, int n, const
     return 0;
 }
 
-// Build (once, eagerly, outside any capture) the two device-side batches of a MoE layer:
-// gate|up of every choice (input rmsnorm(hc) * ffn_norm) and their downs (input
-// silu(gate) * up per choice), plus the shared expert last.  Matrices of routed choices
-// start out pointing at expert 0; route_kernel points them at the chosen experts.
+// Build (once, eagerly, outside any capture) the device-side batches of a MoE layer's two
+// expert launches, one pair per count m of routed choices resident here (only m = top_k on
+// one GPU): gate|up of each (input rmsnorm(hc) * ffn_norm) and their downs (input
+// silu(gate) * up per choice), with the shared expert last when it is computed here.
+// Matrices of routed choices start out pointing at the first resident expert; route_kernel
+// points them at the chosen ones.  Under expert parallelism (pub set) every down batch
+// publishes its rows to the exchange slot of its choice (the shared expert's: slot top_k).
 template <class FG, class FD>
-int build_moe_batches(sb_engine *e, EngLayer &L, const float *hc)
+int build_moe_batches(sb_engine *e, EngLayer &L, const float *hc, const sb::grp::Pub *pub)
 {
     using namespace sb::tcmv;
     const int grid = sb::num_sms_cached();
-    const int k = (int)L.top_k, ns = k + (L.has_sh ? 1 : 0);
-    MatOpX gu[MAXB], dn[MAXB];
-    for (int i = 0; i < ns; i++) {
-        const bool shared = i == k;
-        const EngMat &g = shared ? L.sh[0] : L.ex[0], &u = shared ? L.sh[1] : L.ex[1], &d = shared ? L.sh[2] : L.ex[2];
-        float *gi = e->egu + (size_t)(2 * i) * e->moe_ffn, *ui = e->egu + (size_t)(2 * i + 1) * e->moe_ffn;
-        gu[2 * i] = MatOpX{MatOp{g.w, (int)g.rows, (int)g.cols, hc, gi}, nullptr, nullptr};
-        gu[2 * i + 1] = MatOpX{MatOp{u.w, (int)u.rows, (int)u.cols, hc, ui}, nullptr, nullptr};
-        dn[i] = MatOpX{MatOp{d.w, (int)d.rows, (int)d.cols, gi, e->ys + (size_t)i * e->H}, ui, nullptr};
-    }
+    const int k = (int)L.top_k, sh = L.sh_here ? 1 : 0;
+    const int m0 = pub ? 0 : k;
     XSrc xg{};
     xg.w = L.nf, xg.eps = e->eps, xg.mode = XS_NORM;
     XSrc xd{};
     xd.mode = XS_SWIGLU;
-    Batch hb;
-    memset(&hb, 0, sizeof(hb));
+    std::vector<Batch> hg(k + 1), hd(k + 1);
+    memset(hg.data(), 0, hg.size() * sizeof(Batch));
+    memset(hd.data(), 0, hd.size() * sizeof(Batch));
+    size_t gs = 0, ds = 0;
+    for (int m = m0; m <= k; m++) {
+        const int ns = m + sh;
+        size_t sg = 0, sd = 0;
+        if (!ns) {
+            empty_batch<FG>(&hg[m], xg, &sg);
+            empty_batch<FD>(&hd[m], xd, &sd);
+        } else {
+            MatOpX gu[MAXB], dn[MAXB];
+            for (int i = 0; i < ns; i++) {
+                const bool shared = i == m;
+                const EngMat &g = shared ? L.sh[0] : L.ex[0], &u = shared ? L.sh[1] : L.ex[1];
+                const EngMat &d = shared ? L.sh[2] : L.ex[2];
+                float *gi = e->egu + (size_t)(2 * i) * e->moe_ffn, *ui = e->egu + (size_t)(2 * i + 1) * e->moe_ffn;
+                gu[2 * i] = MatOpX{MatOp{g.w, (int)g.rows, (int)g.cols, hc, gi}, nullptr, nullptr};
+                gu[2 * i + 1] = MatOpX{MatOp{u.w, (int)u.rows, (int)u.cols, hc, ui}, nullptr, nullptr};
+                dn[i] = MatOpX{MatOp{d.w, (int)d.rows, (int)d.cols, gi, e->ys + (size_t)(shared ? k : i) * e->H}, ui,
+                               nullptr};
+            }
+            int rc = build_batch<FG>(gu, 2 * ns, CNT_MAX, grid, &xg, &hg[m], &sg);
+            if (rc) return fail("decode plan: expert gate/up batch rejected (" + std::to_string(rc) + ")");
+            rc = build_batch<FD>(dn, ns, CNT_MAX, grid, &xd, &hd[m], &sd);
+            if (!rc && pub) rc = whole_groups<FD>(&hd[m], grid, &sd);
+            if (rc) return fail("decode plan: expert down batch rejected (" + std::to_string(rc) + ")");
+            if (sh) hd[m].d[m].pub_off = k * sb::grp::XW;
+        }
+        if (pub) hd[m].pub = *pub;
+        gs = std::max(gs, sg);
+        ds = std::max(ds, sd);
+    }
     cudaError_t err;
-    int rc = build_batch<FG>(gu, 2 * ns, CNT_MAX, grid, &xg, &hb, &L.gu_smem);
-    if (rc) return fail("decode plan: expert gate/up batch rejected (" + std::to_string(rc) + ")");
-    if (!L.gu_b && !(L.gu_b = (Batch *)e->dalloc(sizeof(Batch), &err))) return fail("cudaMalloc(batch)", err);
-    if ((err = cudaMemcpy(L.gu_b, &hb, sizeof(Batch), cudaMemcpyHostToDevice)) != cudaSuccess)
+    if (!L.gu_b) {
+        L.gu_b = (Batch *)e->dalloc((k + 1) * sizeof(Batch), &err);
+        if (err == cudaSuccess) L.dn_b = (Batch *)e->dalloc((k + 1) * sizeof(Batch), &err);
+        if (err == cudaSuccess) L.sel = (int *)e->dalloc(16, &err);
+        if (err != cudaSuccess) return fail("cudaMalloc(batch)", err);
+    }
+    if ((err = cudaMemcpy(L.gu_b, hg.data(), (k + 1) * sizeof(Batch), cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (err = cudaMemcpy(L.dn_b, hd.data(), (k + 1) * sizeof(Batch), cudaMemcpyHostToDevice)) != cudaSuccess)
         return fail("cudaMemcpy(batch)", err);
-    memset(&hb, 0, sizeof(hb));
-    rc = build_batch<FD>(dn, ns, CNT_MAX, grid, &xd, &hb, &L.dn_smem);
-    if (rc) return fail("decode plan: expert down batch rejected (" + std::to_string(rc) + ")");
-    if (!L.dn_b && !(L.dn_b = (Batch *)e->dalloc(sizeof(Batch), &err))) return fail("cudaMalloc(batch)", err);
-    if ((err = cudaMemcpy(L.dn_b, &hb, sizeof(Batch), cudaMemcpyHostToDevice)) != cudaSuccess)
-        return fail("cudaMemcpy(batch)", err);
+    L.gu_smem = gs, L.dn_smem = ds;
     L.built_for = hc;
     return 0;
 }
 
 template <class F>
-int launch_moe_batch(sb::tcmv::Batch *b, size_t smem, cudaStream_t s)
+int launch_moe_batch(sb::tcmv::Batch *b, const int *sel, size_t smem, cudaStream_t s)
 {
     using namespace sb::tcmv;
     const int grid = sb::num_sms_cached();
@@ -450,35 +499,39 @@ int launch_moe_batch(sb::tcmv::Batch *b, size_t smem, cudaStream_t s)
     Ws w;
     w.cnt = reinterpret_cast<unsigned *>(ws);
     w.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + ws_part_off());
-    return launch_dev_batch<F>(b, smem, w, grid, 1, s);
+    return launch_dev_batch<F>(b, sel, smem, w, grid, 1, s);
 }
 
-int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, bool build, size_t *n)
+// The MoE FFN after its router matvec: route, expert gate|up, expert downs.  pub: where the
+// downs publish (expert parallelism), else null.
+int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, bool build, size_t *n,
+                 const sb::grp::Pub *pub)
 {
     const uint8_t gdt = L.ex[0].dt, ddt = L.ex[2].dt;
     int rc = 0;
     if (build) {
         const bool d80 = ddt == SB_DTYPE_Q8_0 || ddt == SB_DTYPE_Q8_0_R;
-        if (gdt == SB_DTYPE_Q4_K && d80) rc = build_moe_batches<sb::tcmv::Q4K, sb::tcmv::Q80>(e, L, hc);
-        else if (gdt == SB_DTYPE_Q6_K_P && d80) rc = build_moe_batches<sb::tcmv::Q6KP, sb::tcmv::Q80>(e, L, hc);
-        else if (gdt == SB_DTYPE_Q4_K && ddt == SB_DTYPE_Q4_K) rc = build_moe_batches<sb::tcmv::Q4K, sb::tcmv::Q4K>(e, L, hc);
-        else if (gdt == SB_DTYPE_Q4_K && ddt == SB_DTYPE_Q6_K_P) rc = build_moe_batches<sb::tcmv::Q4K, sb::tcmv::Q6KP>(e, L, hc);
-        else if (gdt == SB_DTYPE_Q6_K_P && ddt == SB_DTYPE_Q6_K_P) rc = build_moe_batches<sb::tcmv::Q6KP, sb::tcmv::Q6KP>(e, L, hc);
-        else if (gdt == SB_DTYPE_Q6_K_P && ddt == SB_DTYPE_Q4_K) rc = build_moe_batches<sb::tcmv::Q6KP, sb::tcmv::Q4K>(e, L, hc);
+        using namespace sb::tcmv;
+        if (gdt == SB_DTYPE_Q4_K && d80) rc = build_moe_batches<Q4K, Q80>(e, L, hc, pub);
+        else if (gdt == SB_DTYPE_Q6_K_P && d80) rc = build_moe_batches<Q6KP, Q80>(e, L, hc, pub);
+        else if (gdt == SB_DTYPE_Q4_K && ddt == SB_DTYPE_Q4_K) rc = build_moe_batches<Q4K, Q4K>(e, L, hc, pub);
+        else if (gdt == SB_DTYPE_Q4_K && ddt == SB_DTYPE_Q6_K_P) rc = build_moe_batches<Q4K, Q6KP>(e, L, hc, pub);
+        else if (gdt == SB_DTYPE_Q6_K_P && ddt == SB_DTYPE_Q6_K_P) rc = build_moe_batches<Q6KP, Q6KP>(e, L, hc, pub);
+        else if (gdt == SB_DTYPE_Q6_K_P && ddt == SB_DTYPE_Q4_K) rc = build_moe_batches<Q6KP, Q4K>(e, L, hc, pub);
         else return fail("decode plan: expert dtypes without a tensor-core kernel");
         if (rc) return rc;
     }
     sb::RouteArgs ra{e->rlog, (int)L.n_exp, (int)L.top_k, e->ridx, e->wts, L.sg, hc, L.nf, e->eps, (int)e->H,
-                     L.has_sh ? 1 : 0, L.gu_b, L.dn_b, L.maps};
+                     L.has_sh ? 1 : 0, L.gu_b, L.dn_b, L.sel, L.maps, (int)L.ex_lo, (int)L.ex_hi, sb::grp::XW};
     if ((rc = sb::launch_k(sb::route_kernel, dim3(1), dim3(256), 0, 1, s, ra))) return rc;
     *n += 1;
-    rc = gdt == SB_DTYPE_Q4_K ? launch_moe_batch<sb::tcmv::Q4K>(L.gu_b, L.gu_smem, s)
-                              : launch_moe_batch<sb::tcmv::Q6KP>(L.gu_b, L.gu_smem, s);
+    rc = gdt == SB_DTYPE_Q4_K ? launch_moe_batch<sb::tcmv::Q4K>(L.gu_b, L.sel, L.gu_smem, s)
+                              : launch_moe_batch<sb::tcmv::Q6KP>(L.gu_b, L.sel, L.gu_smem, s);
     if (rc) return rc;
     *n += 1;
-    rc = ddt == SB_DTYPE_Q4_K   ? launch_moe_batch<sb::tcmv::Q4K>(L.dn_b, L.dn_smem, s)
-         : ddt == SB_DTYPE_Q6_K_P ? launch_moe_batch<sb::tcmv::Q6KP>(L.dn_b, L.dn_smem, s)
-                                  : launch_moe_batch<sb::tcmv::Q80>(L.dn_b, L.dn_smem, s);
+    rc = ddt == SB_DTYPE_Q4_K   ? launch_moe_batch<sb::tcmv::Q4K>(L.dn_b, L.sel, L.dn_smem, s)
+         : ddt == SB_DTYPE_Q6_K_P ? launch_moe_batch<sb::tcmv::Q6KP>(L.dn_b, L.sel, L.dn_smem, s)
+                                  : launch_moe_batch<sb::tcmv::Q80>(L.dn_b, L.sel, L.dn_smem, s);
     if (rc) return rc;
     *n += 1;
     return 0;
@@ -503,23 +556,34 @@ int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, boo
 
 // One token, enqueued on s.  greedy: embedding row from the device token, and
 // argmax (which also ends the step) at the end.
+//
+// The residual stream: h (hc) plus what the last block produced, added in the preparation
+// of the next block's input (rmsnorm(h + y) * w).  y is the attention or dense FFN output
+// (ob), or the weighted expert outputs (ys, wts) of a MoE FFN, or, on a group of GPUs, the
+// slots of an exchange point: the ranks' partial sums (tensor parallelism, weights 1) or
+// the routed experts' outputs by choice (expert parallelism, the routing weights).
 int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
 {
     size_t n = 0;
     int *pos = e->ints, *tok = e->ints + 1, *step = e->ints + 2, *np = e->ints + 3;
     float *hc = e->h, *ho = e->h2;  // residual stream: current / the other buffer
     if (greedy) ENG_CHECK(sbk_embed_row(e->emb.w, e->emb.dt, e->V, e->H, tok, e->h, 1, s));
-    int moe_ny = 0;  // > 0: the last FFN was MoE; its result is the weighted set ys / wts
-    // tensor parallelism: exchange point x of this token (2l: attn_output partial sums of
-    // layer l, 2l+1: ffn_down partial sums, 2L: the vocabulary-slice maxima)
+    int moe_ny = 0;  // > 0: the last FFN was MoE, computed here; its result is the weighted set ys / wts
+    // Exchange points of this token are numbered in the order they are published: the data
+    // slots alternate with that number's parity, which is safe because no rank publishes
+    // point x + 2 before every rank has read point x (to publish x + 1, every rank has read x
+    // first, and x + 2 comes after waiting for all of x + 1).
     sb_group *const g = e->tp;
     const int G = g ? g->world : 1, grid = sb::num_sms_cached();
-    int xprev = -1;  // the exchange point holding the pending residual (-1: none)
-    auto pub_of = [&](int x) {
+    int nx = 0;                  // exchange points published so far
+    int xprev = -1;              // the exchange point holding the pending residual (-1: none)
+    const float *xw = nullptr;   // its slots' weights
+    int xny = 0;                 // and count
+    auto pub_slot = [&](int x, int slot) {
         sb::grp::Pub pb{};
         pb.n = G;
         for (int p = 0; p < G; p++)
-            pb.dst[p] = sb::grp::data_slot(g->peer[p], x, g->rank), pb.cnt[p] = sb::grp::cnt_slot(g->peer[p], x, g->rank);
+            pb.dst[p] = sb::grp::data_slot(g->peer[p], x, slot), pb.cnt[p] = sb::grp::cnt_slot(g->peer[p], x, g->rank);
         return pb;
     };
     auto wait_of = [&](int x) {
@@ -531,11 +595,13 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
         sbk_xsrc xs{};
         xs.norm_w = w, xs.h_out = h_out, xs.eps = e->eps, xs.mode = SBK_XS_NORM;
         if (g && xprev >= 0)
-            xs.ys = sb::grp::data_slot(g->area, xprev, 0), xs.yw = g->ones, xs.ny = G, xs.ystride = sb::grp::XW;
+            xs.ys = sb::grp::data_slot(g->area, xprev, 0), xs.yw = xw, xs.ny = xny, xs.ystride = sb::grp::XW;
         else if (moe_ny) xs.ys = e->ys, xs.yw = e->wts, xs.ny = moe_ny, xs.ystride = (int)e->H;
         else xs.res = e->ob;
         return xs;
     };
+    // consume the pending residual (after the launch that read it)
+    auto consumed = [&]() { moe_ny = 0, xprev = -1, xw = nullptr, xny = 0; };
     for (size_t l = 0; l < e->L.size(); l++) {
         EngLayer &L = e->L[l];
         if (L.mla) {
@@ -547,9 +613,10 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
                 if (!l) xs.res = nullptr;
                 const EngMat *ms[2] = {&L.q_down, &L.kv_down};
                 float *ys[2] = {e->mcq, e->mc};
-                ENG_MV(ms, ys, 2, hc, xs);
+                const sb::grp::Wait w = wait_of(l ? xprev : -1);
+                ENG_MV_G(nullptr, &w, ms, ys, 2, hc, xs);
                 if (l) std::swap(hc, ho);
-                moe_ny = 0;
+                consumed();
             }
             {
                 const sbk_xsrc xs{};
@@ -581,8 +648,7 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
                 const sb::grp::Wait w = wait_of(l ? xprev : -1);
                 ENG_MV_G(nullptr, &w, ms, ys, 3, hc, xs);
                 if (l) std::swap(hc, ho);
-                moe_ny = 0;
-                xprev = -1;
+                consumed();
             }
             ENG_CHECK(sbk_attn_rope_decode(e->qkv, L.bias, L.qn, L.kn, L.kc, L.vc, e->att, pos, L.heads, L.kvh, L.hd,
                                            e->ctx, L.theta, e->eps, L.neox, e->attn_ws, 1, s));
@@ -591,10 +657,10 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
             const sbk_xsrc xs{};
             const EngMat *ms[1] = {&L.o};
             float *ys[1] = {e->ob};
-            if (g) {  // this rank's heads' share of attn_output: to every rank
-                const sb::grp::Pub pb = pub_of((int)(2 * l));
+            if (L.tp_attn) {  // this rank's heads' share of attn_output: to every rank
+                const sb::grp::Pub pb = pub_slot(nx, g->rank);
                 ENG_MV_G(&pb, nullptr, ms, ys, 1, e->att, xs);
-                xprev = (int)(2 * l);
+                xprev = nx++, xw = g->ones, xny = G;
             } else {
                 ENG_MV(ms, ys, 1, e->att, xs);
             }
@@ -605,13 +671,22 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
                 const sbk_xsrc xs = norm_src(L.nf, ho);
                 const EngMat *ms[1] = {&L.router};
                 float *ys[1] = {e->rlog};
-                ENG_MV(ms, ys, 1, hc, xs);
+                const sb::grp::Wait w = wait_of(xprev);
+                ENG_MV_G(nullptr, &w, ms, ys, 1, hc, xs);
                 std::swap(hc, ho);
+                consumed();
             }
             const bool build = L.built_for == nullptr;
             if (!build && L.built_for != hc) return fail("decode step: MoE batches built for another buffer");
-            if (moe_dispatch(e, L, hc, s, build, &n)) return fail("decode step: MoE launch rejected");
-            moe_ny = (int)(L.top_k + (L.has_sh ? 1 : 0));
+            const int ny = (int)(L.top_k + (L.has_sh ? 1 : 0));
+            if (g) {  // expert parallelism: every choice's output to its slot of every rank's area
+                const sb::grp::Pub pb = pub_slot(nx, 0);
+                if (moe_dispatch(e, L, hc, s, build, &n, &pb)) return fail("decode step: MoE launch rejected");
+                xprev = nx++, xw = e->wts, xny = ny;
+            } else {
+                if (moe_dispatch(e, L, hc, s, build, &n, nullptr)) return fail("decode step: MoE launch rejected");
+                moe_ny = ny;
+            }
             continue;
         }
         // dense FFN block: h + attention output -> rmsnorm -> gate|up; silu(gate) * up -> down
@@ -622,17 +697,17 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
             const sb::grp::Wait w = wait_of(xprev);
             ENG_MV_G(nullptr, &w, ms, ys, 2, hc, xs);
             std::swap(hc, ho);
-            xprev = -1;
+            consumed();
         }
         {
             sbk_xsrc xs{};
             xs.res = e->gu + L.ffn, xs.mode = SBK_XS_SWIGLU;
             const EngMat *ms[1] = {&L.d};
             float *ys[1] = {e->ob};
-            if (g) {  // this rank's share of ffn_down: to every rank
-                const sb::grp::Pub pb = pub_of((int)(2 * l + 1));
+            if (L.tp_ffn) {  // this rank's share of ffn_down: to every rank
+                const sb::grp::Pub pb = pub_slot(nx, g->rank);
                 ENG_MV_G(&pb, nullptr, ms, ys, 1, e->gu, xs);
-                xprev = (int)(2 * l + 1);
+                xprev = nx++, xw = g->ones, xny = G;
             } else {
                 ENG_MV(ms, ys, 1, e->gu, xs);
             }
@@ -647,7 +722,7 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
     }
     if (greedy && g) {
         // the maximum of this rank's vocabulary slice to every rank, then the global one
-        const int xa = (int)(2 * e->L.size());
+        const int xa = nx;
         sb::grp::Pub pb{};
         pb.n = G;
         for (int p = 0; p < G; p++)
@@ -739,7 +814,7 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
     e->eps = p->eps;
     sb_group *const g = (c->grp && c->grp->world > 1) ? c->grp : nullptr;
     if (g && !g->opened) return bail(fail("decode plan: the group is not open (sb_group_open)"));
-    if (g && p->hidden > (size_t)sb::grp::XW) return bail(0);
+    if (g && (p->hidden > (size_t)sb::grp::XW || 2 * p->n_layers + 1 > (size_t)sb::grp::NX)) return bail(0);
     e->tp = g;
     const size_t H = e->H;
     size_t attn_ws = 0;
@@ -750,8 +825,15 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         if (!lp.norm_attn || !lp.norm_ffn) return bail(fail("decode plan: layer without norms"));
         L.heads = lp.heads, L.kvh = lp.kv_heads, L.hd = lp.head_dim, L.theta = lp.theta, L.neox = lp.neox;
         int rc;
-        if (g && (lp.mla || lp.moe)) return bail(0);  // the tensor-parallel engine runs dense GQA layers
-        std::vector<float> tp_bias;                   // this rank's slice of the q|k|v bias
+        std::vector<float> tp_bias;  // this rank's slice of the q|k|v bias
+        // tensor-parallel attention when the query heads split evenly and each rank's heads
+        // read whole kv heads (or share one); else (and for MLA) every rank computes it whole
+        size_t tp_hp = 0, tp_kvl = 0;
+        if (g && !lp.mla && L.heads && L.kvh && L.heads % L.kvh == 0 && L.hd == 128 && L.heads % g->world == 0) {
+            const size_t gs = L.heads / L.kvh, hp = L.heads / g->world;
+            const size_t kvl = hp % gs == 0 ? hp / gs : gs % hp == 0 ? 1 : 0;
+            if (kvl && hp / kvl <= 8) tp_hp = hp, tp_kvl = kvl;
+        }
         if (lp.mla) {
             // MLA: latent cache + rope keys; attention output heads * v_dim wide
             const sb_mla_plan &ml = *lp.mla;
@@ -779,17 +861,11 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             e->mla_hr = std::max(e->mla_hr, L.heads * L.kv_rank);
             e->mla_hp = std::max(e->mla_hp, L.heads * L.qk_rope);
             e->mla_ws_bytes = std::max(e->mla_ws_bytes, sbk_mla_ws_bytes(L.heads, L.kv_rank));
-        } else if (g) {
+        } else if (tp_hp) {
             // tensor-parallel attention: this rank's query heads, the kv heads they read, the
             // matching columns of attn_output (its partial sums go through the exchange)
-            const size_t G = g->world, r = g->rank;
-            if (!L.heads || !L.kvh || L.heads % L.kvh || L.hd != 128 || L.heads % G) return bail(0);
-            const size_t gs = L.heads / L.kvh, hp = L.heads / G;
-            size_t kvl;
-            if (hp % gs == 0) kvl = hp / gs;
-            else if (gs % hp == 0) kvl = 1;
-            else return bail(0);
-            if (hp / kvl > 8) return bail(0);
+            const size_t r = g->rank, gs = L.heads / L.kvh, hp = tp_hp, kvl = tp_kvl;
+            L.tp_attn = true;
             const size_t q0 = r * hp, kv0 = q0 / gs, qdg = L.heads * L.hd, kvdg = L.kvh * L.hd;
             L.heads = hp, L.kvh = kvl, L.qd = hp * L.hd, L.kvd = kvl * L.hd;
             if ((rc = eng_mat_rows(c, lp.q, qdg, H, q0 * L.hd, L.qd, &L.q)) != 1) return bail(rc);
@@ -818,15 +894,32 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
                 return bail(0);
             L.moe = true, L.n_exp = mp.n_exp, L.top_k = mp.top_k, L.effn = mp.ffn;
             L.has_sh = mp.shared != nullptr;
-            if (2 * (L.top_k + (L.has_sh ? 1 : 0)) > (size_t)sb::tcmv::MAXB) return bail(0);
+            if (2 * (L.top_k + (L.has_sh ? 1 : 0)) > (size_t)sb::tcmv::MAXB ||
+                L.top_k + (L.has_sh ? 1 : 0) > (size_t)sb::tcmv::XS_MAXY)
+                return bail(0);
+            if (g && L.top_k + 1 > (size_t)sb::grp::DSL) return bail(0);
+            // the router on every rank; the experts resident here: all of them, or under
+            // expert parallelism this rank's range of expert IDs (row_strip), and the shared
+            // expert on rank l % world
             if ((rc = eng_mat(c, mp.router, L.n_exp, H, &L.router, true)) != 1) return bail(rc);
-            L.ex.resize(3 * L.n_exp);
-            std::vector<CUtensorMap> maps(3 * L.n_exp);
-            for (size_t x = 0; x < L.n_exp; x++) {
+            if (g) {
+                int lo, hi;
+                sb::row_strip((int)L.n_exp, g->rank, g->world, lo, hi);
+                if (hi <= lo) return bail(0);
+                L.ex_lo = (size_t)lo, L.ex_hi = (size_t)hi;
+                L.sh_here = L.has_sh && l % g->world == (size_t)g->rank;
+            } else {
+                L.ex_lo = 0, L.ex_hi = L.n_exp;
+                L.sh_here = L.has_sh;
+            }
+            const size_t nl = L.ex_hi - L.ex_lo;
+            L.ex.resize(3 * nl);
+            std::vector<CUtensorMap> maps(3 * nl);
+            for (size_t x = 0; x < nl; x++) {
                 const size_t r[3] = {L.effn, L.effn, H}, cc[3] = {H, H, L.effn};
                 for (int k = 0; k < 3; k++) {
                     EngMat &m = L.ex[3 * x + k];
-                    if ((rc = eng_mat(c, mp.experts[3 * x + k], r[k], cc[k], &m, true)) != 1) return bail(rc);
+                    if ((rc = eng_mat(c, mp.experts[3 * (L.ex_lo + x) + k], r[k], cc[k], &m, true)) != 1) return bail(rc);
                     if (m.dt != L.ex[k].dt) return bail(0);  // one dtype per matrix kind
                     const int mr =
                         m.dt == SB_DTYPE_Q4_K
@@ -840,7 +933,9 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
                     if (mr < 0) return bail(fail("decode plan: tensor map of an expert rejected"));
                 }
             }
-            if (L.has_sh) {
+            if (L.has_sh && !L.sh_here) {
+                if (upload_f32(e, mp.shared_gate, H, &L.sg)) return bail(-1);
+            } else if (L.has_sh) {
                 L.sffn = mp.shared[0].rows;
                 const size_t r[3] = {L.sffn, L.sffn, H}, cc[3] = {H, H, L.sffn};
                 for (int k = 0; k < 3; k++) {
@@ -857,13 +952,13 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             e->moe_slots = std::max(e->moe_slots, L.top_k + (L.has_sh ? 1 : 0));
             e->moe_ffn = std::max(e->moe_ffn, std::max(L.effn, L.sffn));
             e->n_exp_max = std::max(e->n_exp_max, L.n_exp);
-        } else if (g) {
-            // tensor-parallel FFN: whole 256-column blocks of the intermediate dimension per rank
+        } else if (g && lp.gate.rows % 256 == 0 && lp.gate.rows / 256 >= (size_t)g->world) {
+            // tensor-parallel FFN: whole 256-column blocks of the intermediate dimension per
+            // rank (other widths: every rank computes the FFN whole)
             const size_t ffn_g = lp.gate.rows;
-            if (ffn_g % 256) return bail(0);
             int b0, b1;
             sb::row_strip((int)(ffn_g / 256), g->rank, g->world, b0, b1);
-            if (b1 <= b0) return bail(0);
+            L.tp_ffn = true;
             const size_t f0 = 256 * (size_t)b0;
             L.ffn = 256 * (size_t)(b1 - b0);
             if ((rc = eng_mat_rows(c, lp.gate, ffn_g, H, f0, L.ffn, &L.g)) != 1) return bail(rc);
@@ -877,7 +972,8 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         }
         if (upload_f32(e, lp.norm_attn, H, &L.na) || upload_f32(e, lp.norm_ffn, H, &L.nf) ||
             upload_f32(e, lp.q_norm, L.hd, &L.qn) || upload_f32(e, lp.k_norm, L.hd, &L.kn) ||
-            upload_f32(e, g ? (tp_bias.empty() ? nullptr : tp_bias.data()) : lp.qkv_bias, L.qd + 2 * L.kvd, &L.bias))
+            upload_f32(e, L.tp_attn ? (tp_bias.empty() ? nullptr : tp_bias.data()) : lp.qkv_bias, L.qd + 2 * L.kvd,
+                       &L.bias))
             return bail(-1);
         if (L.mla) {
             e->kv_rows_total += L.kv_rank;

@@ -8,11 +8,14 @@
 // soso_b200), so each rank can store into every peer's area over NVLink.
 //
 // A publishing kernel (a matvec whose rows are this rank's share of a sum, or the
-// argmax of this rank's slice of the vocabulary) stores its values into slot [rank]
-// of every rank's area, fences, and adds 1 per CTA to that area's counter of
-// (exchange point k, source rank).  A consuming kernel waits, with a bounded spin,
-// until every source's counter has reached epoch * (CTAs per publisher) and then sums
-// the slots in rank order (a fixed order: every rank forms bit-identical sums).
+// argmax of this rank's slice of the vocabulary) stores its values into a data slot of
+// every rank's area, fences, and adds 1 per CTA to that area's counter of (exchange
+// point k, source rank).  Tensor-parallel partial sums go to slot [rank]; the outputs
+// of routed experts (expert parallelism) go to slot [choice], the expert's position in
+// the token's top-k, whichever rank owns the expert.  A consuming kernel waits, with a
+// bounded spin, until every source's counter has reached epoch * (CTAs per publisher)
+// and then sums the slots in slot order with its weights (a fixed order: every rank
+// forms bit-identical sums).
 // Exchange points are numbered within a token; data slots alternate by the parity of
 // k, which is enough because no rank can publish exchange k + 2 before every rank has
 // consumed exchange k (it needs their k + 1 shares first).  Counters only grow: the
@@ -25,19 +28,20 @@ namespace sb {
 namespace grp {
 
 constexpr int MAXG = 8;          // ranks
+constexpr int DSL = 24;          // data slots per parity (ranks, or top-k choices + a shared expert)
 constexpr int XW = 16384;        // floats per data slot (hidden size at most)
 constexpr int NX = 512;          // exchange points per token
 constexpr unsigned WAIT_LIMIT = 1u << 26;
 
-// [data: 2][MAXG][XW] f32 | [arg: MAXG][2] u32 | [cnt: NX][MAXG] u32
-constexpr size_t DATA_BYTES = (size_t)2 * MAXG * XW * 4;
+// [data: 2][DSL][XW] f32 | [arg: MAXG][2] u32 | [cnt: NX][MAXG] u32
+constexpr size_t DATA_BYTES = (size_t)2 * DSL * XW * 4;
 constexpr size_t ARG_OFF = DATA_BYTES;
 constexpr size_t CNT_OFF = ARG_OFF + (size_t)MAXG * 8;
 constexpr size_t AREA_BYTES = CNT_OFF + (size_t)NX * MAXG * 4;
 
-__host__ __device__ inline float *data_slot(void *area, int k, int src)
+__host__ __device__ inline float *data_slot(void *area, int k, int slot)
 {
-    return reinterpret_cast<float *>(area) + ((size_t)(k & 1) * MAXG + src) * XW;
+    return reinterpret_cast<float *>(area) + ((size_t)(k & 1) * DSL + slot) * XW;
 }
 __host__ __device__ inline unsigned *arg_slot(void *area, int src)
 {
@@ -74,7 +78,7 @@ __device__ inline bool wait_counts(const unsigned *cnt, int n, unsigned target)
 
 // Where a kernel publishes its share of exchange point k.
 struct Pub {
-    float *dst[MAXG];       // data slot [rank] of every rank's area
+    float *dst[MAXG];       // a data slot of every rank's area (matrix i of a batch adds its pub_off)
     unsigned *cnt[MAXG];    // counter (k, rank) of every rank's area
     int n;                  // ranks (0: not publishing)
 };

@@ -25,6 +25,8 @@
 // matvec_lote, crates/soso-llm-core/src/gpu.rs:694-701: several matvecs, one
 // wait); their stages are numbered one after another, so the batch streams as one.
 #pragma once
+#include <cstring>
+
 #include "tc_q4k.cuh"
 #include "tc_q6k.cuh"
 #include "tc_q80.cuh"
@@ -44,6 +46,7 @@ struct __align__(64) MatDesc {
     float *y;
     int rows, cols, spg;    // spg: stages per 16-row group
     int st_begin, cnt_off;  // first global stage; first counter of its groups
+    int pub_off;            // where this matrix's rows go in the batch's exchange slots (floats)
 };
 
 struct Batch {
@@ -53,7 +56,7 @@ struct Batch {
     int max_cols, max_groups;  // shared-memory capacities (prep, partial table)
     int split_groups;          // 1: CTAs take whole 16-row groups (no cut groups, no fix-up)
     int total_groups;
-    grp::Pub pub;              // also store matrix 0's rows into the group's exchange areas
+    grp::Pub pub;              // also store every matrix's rows into the group's exchange areas
     grp::Wait wait;            // wait for an exchange point before reading the input
 };
 
@@ -303,7 +306,7 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
                 if (!cut) {
                     if (row < d.rows) {
                         d.y[row] = v;
-                        for (int p = 0; p < B.pub.n; p++) B.pub.dst[p][row] = v;
+                        for (int p = 0; p < B.pub.n; p++) B.pub.dst[p][d.pub_off + row] = v;
                     }
                 } else {
                     // side 0: the group holding this CTA's first stage, side 1: any other (its last)
@@ -383,10 +386,18 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
 
 // The same with the batch in device memory (written by an earlier kernel on the stream,
 // e.g. the expert choice of a MoE router); its matrices name their maps through mapp.
+// With `sel` set, the batch is B[*sel], one of several prepared batches (the number of
+// routed experts this rank owns picks the one whose split fits).
 template <class F>
-__global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_dev_kernel(const Batch *__restrict__ B, Ws ws)
+__global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_dev_kernel(const Batch *__restrict__ B,
+                                                                   const int *__restrict__ sel, Ws ws)
 {
-    tc_mmv_body<F, true>(*B, ws);
+    if (sel) {
+        griddep_wait();  // *sel is written by the previous kernel
+        tc_mmv_body<F, true>(B[*sel], ws);
+    } else {
+        tc_mmv_body<F, true>(*B, ws);
+    }
 }
 
 // ------------------------------------------------------------------ host side
@@ -561,6 +572,7 @@ inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XS
         d.spg = stages_per_group<F>(o.cols);
         d.st_begin = st;
         d.cnt_off = cnt;
+        d.pub_off = 0;
         st += d.spg * ((o.rows + 15) / 16);
         cnt += (o.rows + 15) / 16;
     }
@@ -604,6 +616,32 @@ inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XS
     if (smem > 227 * 1024) return -5;
     *smem_out = smem;
     return 0;
+}
+
+// A published matrix's rows must be final in the CTA that computes them: switch a batch
+// to whole 16-row groups per CTA (no groups cut between CTAs), growing *smem to match.
+template <class F>
+inline int whole_groups(Batch *b, int grid, size_t *smem)
+{
+    if (b->split_groups) return 0;
+    const int need = (b->total_groups + grid - 1) / grid + 1;
+    if (need > b->max_groups) b->max_groups = need;
+    *smem = smem_bytes<F>(b->max_cols, b->max_groups);
+    if (*smem > 227 * 1024) return -5;
+    b->split_groups = 1;
+    return 0;
+}
+
+// A batch of no matrices (every CTA only takes part in the publication, if any); *smem
+// is what its launch needs at least.
+template <class F>
+inline void empty_batch(Batch *b, const XSrc &xs, size_t *smem)
+{
+    memset(b, 0, sizeof(Batch));
+    b->xs = xs;
+    b->split_groups = 1;
+    b->max_groups = 1;
+    *smem = smem_bytes<F>(0, 1);
 }
 
 // Raise a kernel's dynamic shared-memory limit to `smem` (only ever grows; one record per
@@ -656,16 +694,9 @@ inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int gri
     if (rc) return rc;
     if (wait) b.wait = *wait;
     if (pub && pub->n) {
-        // a published matrix's rows must be final in the CTA that computes them: whole groups
         if (n != 1) return -1;
         b.pub = *pub;
-        if (!b.split_groups) {
-            const int need = (b.total_groups + grid - 1) / grid + 1;
-            if (need > b.max_groups) b.max_groups = need;
-            smem = smem_bytes<F>(b.max_cols, b.max_groups);
-            if (smem > 227 * 1024) return -5;
-            b.split_groups = 1;
-        }
+        if ((rc = whole_groups<F>(&b, grid, &smem))) return rc;
     }
     if ((rc = ensure_smem(tc_mmv_kernel<F>, smem, smem_rec))) return rc;
     cudaLaunchAttribute attr[1];
@@ -674,10 +705,12 @@ inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int gri
 }
 
 // Launch a batch held in device memory (dev, a copy of a batch made by build_batch, whose
-// mapp / x / y fields an earlier kernel on the stream may have rewritten; shapes and the
-// split must stay as built).  smem as build_batch returned it.
+// mapp / x / y / pub_off fields an earlier kernel on the stream may have rewritten; shapes
+// and the split must stay as built), or dev[*sel] when sel is set.  smem: at least what
+// build_batch returned for every batch that may be chosen.
 template <class F>
-inline int launch_dev_batch(const Batch *dev, size_t smem, Ws wsd, int grid, int pdl, cudaStream_t stream)
+inline int launch_dev_batch(const Batch *dev, const int *sel, size_t smem, Ws wsd, int grid, int pdl,
+                            cudaStream_t stream)
 {
     static size_t smem_rec[64];
     static std::mutex mu;
@@ -686,7 +719,7 @@ inline int launch_dev_batch(const Batch *dev, size_t smem, Ws wsd, int grid, int
     if (rc) return rc;
     cudaLaunchAttribute attr[1];
     const cudaLaunchConfig_t cfg = mmv_config(grid, F::THREADS, smem, pdl, stream, attr);
-    return cudaLaunchKernelEx(&cfg, tc_mmv_dev_kernel<F>, dev, wsd) == cudaSuccess ? 0 : -4;
+    return cudaLaunchKernelEx(&cfg, tc_mmv_dev_kernel<F>, dev, sel, wsd) == cudaSuccess ? 0 : -4;
 }
 
 // As launch_batch_ws over a workspace of ws_bytes(grid) bytes.

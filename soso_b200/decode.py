@@ -123,10 +123,17 @@ def shapes(cfg: DenseConfig) -> dict:
             "ffn_down": (H, cfg.ffn)}
 
 
-def synth_model(cfg: DenseConfig, seed: str = "model") -> dict:
-    """Seeded random-init weights of the config's architecture (synth.model_weights)."""
+def synth_model(cfg: DenseConfig, seed: str = "model", held=None) -> dict:
+    """Seeded random-init weights of the config's architecture (synth.model_weights).
+    held = (rank, world): leave out the experts that rank does not hold under expert
+    parallelism (soso_b200.tp: routed experts by ID range, shared experts by layer); every
+    tensor that is made has the same bytes either way."""
     m = {}
     H = cfg.hidden
+    ex_lo, ex_hi = 0, cfg.n_exp
+    if held is not None and cfg.n_exp:
+        from .tp import row_strip
+        ex_lo, ex_hi = row_strip(cfg.n_exp, held[0], held[1])
     for l in range(cfg.n_layers):
         for name, (rows, cols) in shapes(cfg).items():
             if cfg.is_moe(l) and name.startswith("ffn_"):
@@ -136,7 +143,7 @@ def synth_model(cfg: DenseConfig, seed: str = "model") -> dict:
             # router rows scaled so the logits are about N(0, 1)
             m[f"blk.{l}.ffn_gate_inp"] = synth.model_weights(cfg.dtypes["ffn_gate_inp"], cfg.n_exp, H,
                                                               synth.rng(seed, l, "router"), std=1.0 / np.sqrt(H))
-            for e in range(cfg.n_exp):
+            for e in range(ex_lo, ex_hi):
                 for name, (rows, cols) in (("ffn_gate", (cfg.moe_ffn, H)), ("ffn_up", (cfg.moe_ffn, H)),
                                            ("ffn_down", (H, cfg.moe_ffn))):
                     m[f"blk.{l}.E{e:03d}.{name}"] = synth.model_weights(cfg.dtypes[name], rows, cols,
@@ -144,6 +151,8 @@ def synth_model(cfg: DenseConfig, seed: str = "model") -> dict:
             if cfg.shared_ffn:
                 for name, (rows, cols) in (("ffn_gate", (cfg.shared_ffn, H)), ("ffn_up", (cfg.shared_ffn, H)),
                                            ("ffn_down", (H, cfg.shared_ffn))):
+                    if held is not None and l % held[1] != held[0]:
+                        continue
                     m[f"blk.{l}.S00.{name}"] = synth.model_weights(cfg.dtypes[name], rows, cols,
                                                                     synth.rng(seed, l, "shared", name))
                 if cfg.shared_gate:
@@ -172,9 +181,11 @@ class DecodeSession:
     """A prepared whole-token decode on one device (sb_decode_prepare)."""
 
     def __init__(self, cfg: DenseConfig, model: dict, device: int = 0, ctx_handle=None, group=None):
-        """group = (rank, world, all_gather): tensor-parallel decode across `world` processes
-        (soso_b200.tp); all_gather(bytes) -> every rank's bytes, and it doubles as the host
-        barrier before the first (exchanging) warm-up token."""
+        """group = (rank, world, all_gather): decode across `world` processes, sharded as
+        soso_b200.tp describes; all_gather(bytes) -> every rank's bytes, and it doubles as
+        the host barrier before the first (exchanging) warm-up token.  Under expert
+        parallelism `model` may leave out the experts this rank does not hold
+        (synth_model(..., held=(rank, world)))."""
         self.cfg = cfg
         self.model = model
         L = lib()
@@ -260,7 +271,9 @@ class DecodeSession:
         return mp
 
     def _mat(self, key: str, dtype: int, rows: int, cols: int) -> SbMat:
-        w = self.model[key]
+        w = self.model.get(key)
+        if w is None:  # not held by this rank (expert parallelism): the library does not read it
+            return SbMat(None, SbView(None, 0, dtype, rows * cols), rows, cols)
         k = key.encode()
         self._keep.append(k)
         return SbMat(k, SbView(w.ctypes.data_as(c_u8p), w.size, dtype, rows * cols), rows, cols)

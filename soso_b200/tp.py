@@ -1,13 +1,19 @@
-"""Tensor-parallel decode plumbing: one process per GPU, torch.distributed for the host
-channel (the library's exchange areas are opened by CUDA IPC handles the ranks swap here).
+"""Multi-GPU decode plumbing: one process per GPU, torch.distributed for the host channel
+(the library's exchange areas are opened by CUDA IPC handles the ranks swap here).
 
 The sharding itself happens inside the library (sb_decode_prepare with a group); the rules
 are restated here, for the host side and its tests:
-  * attention: query heads split evenly (heads % world == 0); a rank reads the kv heads of
-    its query heads (whole groups of them, or the one kv head they share);
-  * attn_output: the columns of the rank's heads (its share of the sum);
-  * FFN: whole 256-column blocks of the intermediate dimension, split like row_strip
-    (crates/soso-llm-core/src/parallel.rs:22-31); gate/up rows and ffn_down columns alike;
+  * attention (GQA): query heads split evenly when heads % world == 0 and each rank's heads
+    read whole kv heads (or share one); a rank holds its heads' q/k/v rows and the matching
+    columns of attn_output (its share of the sum).  Otherwise, and for MLA, every rank
+    computes attention whole;
+  * dense FFN: whole 256-column blocks of the intermediate dimension, split like row_strip
+    (crates/soso-llm-core/src/parallel.rs:22-31), gate/up rows and ffn_down columns alike,
+    when there are at least `world` blocks; otherwise every rank computes it whole;
+  * MoE FFN (expert parallelism): the router on every rank (every rank routes identically);
+    expert IDs split like row_strip, a rank runs the chosen experts it holds and sends each
+    one's output to the choice's slot of every rank; the shared expert lives on rank
+    layer % world;
   * output matrix: vocabulary rows split like row_strip; the greedy token is the largest
     of the ranks' maxima (ties to the larger index, as Runtime::argmax).
 """
@@ -28,29 +34,45 @@ def row_strip(n: int, i: int, parts: int) -> tuple[int, int]:
 
 @dataclass(frozen=True)
 class Shard:
-    heads: tuple[int, int]      # [first, end) query heads
-    kv_heads: tuple[int, int]   # [first, end) kv heads read
-    ffn: tuple[int, int]        # [first, end) intermediate columns (FFN)
-    vocab: tuple[int, int]      # [first, end) output rows
+    heads: tuple[int, int] | None     # [first, end) query heads (None: attention computed whole)
+    kv_heads: tuple[int, int] | None  # [first, end) kv heads read
+    ffn: tuple[int, int] | None       # [first, end) intermediate columns of the dense FFN (None: whole)
+    vocab: tuple[int, int]            # [first, end) output rows
+    experts: tuple[int, int] | None   # [first, end) expert IDs held (MoE layers)
+
+
+def attention_split(cfg, world: int):
+    """(query heads per rank, kv heads per rank) of a tensor-parallel attention, or None when
+    every rank computes attention whole."""
+    if cfg.mla or world < 2 or cfg.heads % cfg.kv_heads or cfg.head_dim != 128 or cfg.heads % world:
+        return None
+    gs, hp = cfg.heads // cfg.kv_heads, cfg.heads // world
+    kvl = hp // gs if hp % gs == 0 else 1 if gs % hp == 0 else 0
+    if not kvl or hp // kvl > 8:
+        return None
+    return hp, kvl
 
 
 def shard(cfg, rank: int, world: int) -> Shard:
-    """The slice of a dense GQA model that rank `rank` of `world` holds (as the library cuts it)."""
-    if cfg.heads % world:
-        raise ValueError("query heads must split evenly across the group")
-    gs, hp = cfg.heads // cfg.kv_heads, cfg.heads // world
-    if hp % gs == 0:
-        kvl = hp // gs
-    elif gs % hp == 0:
-        kvl = 1
-    else:
-        raise ValueError("query heads per rank and the GQA group size must divide one another")
-    q0 = rank * hp
-    kv0 = q0 // gs
-    if cfg.ffn % 256:
-        raise ValueError("the FFN width must be whole 256-column blocks")
-    b0, b1 = row_strip(cfg.ffn // 256, rank, world)
-    return Shard((q0, q0 + hp), (kv0, kv0 + kvl), (256 * b0, 256 * b1), row_strip(cfg.vocab, rank, world))
+    """The slice of a model that rank `rank` of `world` holds (as the library cuts it)."""
+    heads = kv = ffn = experts = None
+    a = attention_split(cfg, world)
+    if a:
+        hp, kvl = a
+        q0 = rank * hp
+        kv0 = q0 // (cfg.heads // cfg.kv_heads)
+        heads, kv = (q0, q0 + hp), (kv0, kv0 + kvl)
+    if world > 1 and cfg.ffn and cfg.ffn % 256 == 0 and cfg.ffn // 256 >= world:
+        b0, b1 = row_strip(cfg.ffn // 256, rank, world)
+        ffn = (256 * b0, 256 * b1)
+    if cfg.n_exp:
+        experts = row_strip(cfg.n_exp, rank, world)
+    return Shard(heads, kv, ffn, row_strip(cfg.vocab, rank, world), experts)
+
+
+def shared_expert_rank(layer: int, world: int) -> int:
+    """The rank that computes layer `layer`'s shared expert."""
+    return layer % world
 
 
 def open_group(ctx, rank: int, world: int, all_gather) -> None:

@@ -1,5 +1,5 @@
-"""Worker of tests/test_tp_gpu.py: tensor-parallel greedy decode of a small dense model on
-every rank of a torchrun group, checked on rank 0 against the CPU oracle.  Prints one JSON
+"""Worker of tests/test_tp_gpu.py: greedy decode of a small model split over every rank of a
+torchrun group (tensor / expert parallelism), checked on rank 0 against the CPU oracle.  Prints one JSON
 line per rank; exits non-zero on a mismatch."""
 import json
 import os
@@ -25,7 +25,7 @@ def main():
     name = sys.argv[1] if len(sys.argv) > 1 else "TINY"
     steps = int(sys.argv[2]) if len(sys.argv) > 2 else 48
     cfg = getattr(decode, name)
-    model = decode.synth_model(cfg, name.lower())
+    model = decode.synth_model(cfg, name.lower())  # whole: rank 0's oracle reads every expert
     prompt = synth.rng("prompt", "tp").integers(0, cfg.vocab, 8).astype(np.int32)
     sess = decode.DecodeSession(cfg, model, device=local, group=(rank, world, tp.torch_all_gather()))
     got = sess.greedy(prompt, steps)
