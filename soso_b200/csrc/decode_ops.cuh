@@ -9,6 +9,7 @@
 #pragma once
 #include "common.cuh"
 #include "group.cuh"
+#include "tc_common.cuh"
 
 namespace sb {
 
@@ -111,32 +112,48 @@ __global__ void rope_kv_kernel(RopeKvArgs a)
 }
 
 // ---------------------------------------------------------------- attention
-// Flash-decoding over the f16 cache.  One CTA per (span of positions, kv head)
-// covers the G = heads/kv_heads query heads that share that kv head, so every
-// K/V row is read once per group (like the reference's mo_attn_split,
-// gemma_capa.cu:765-877).  A span is ATT_CH positions (more when the context is
-// longer than ATT_MAXC * ATT_CH), taken ATT_CH at a time: the sub-chunk's K and V
-// rows are copied to shared memory with cp.async first (all in flight at once),
-// then scores, an online-softmax update and P.V run out of shared memory.  With
-// one span the CTA writes the output directly; otherwise each CTA writes
-// (acc, max, sum) and the last CTA of a kv head to finish (counter, no
-// spinning) merges the spans in order, as combinar_trozos does
-// (attn_grupo.rs:171-203): score = (q.k) / sqrt(hd), softmax over 0..pos.
+// Flash-decoding over the f16 cache.  The CTAs of one kv head form a thread-block
+// cluster of ATT_SPANS; CTA c takes span c of the positions 0..pos (spans of a
+// multiple of ATT_MIN positions, as many as the context needs up to ATT_SPANS) for
+// the G = heads/kv_heads query heads that share the kv head, so every K/V row is
+// read once per group (like the reference's mo_attn_split, gemma_capa.cu:765-877).
+// A span is taken ATT_CH positions at a time through two shared-memory buffers: the
+// rows of the next sub-chunk are copied (one bulk copy per row, completion counted
+// on an mbarrier) while the current one is computed.  Per sub-chunk, scores
+// S = K.q and the output update O += V^T.P run on the tensor cores (mma.sync
+// m16n8k16, f32 accumulation) with q and P each split into two f16 parts (hi + lo,
+// 22 significant bits; K and V are f16 already), around an online softmax per head
+// in f32.  The spans are merged as combinar_trozos does (attn_grupo.rs:171-203) --
+// weights exp(m_c - M), sum of l_c, in span order -- by the cluster itself: every
+// CTA reads its share of the outputs from all CTAs' shared memory.
 //
 // With `rope` set the kernel also does the step before it (layer.rs:1146-1193,
-// as rope_kv_kernel): q heads get bias, QK-norm and RoPE into shared memory,
-// and the CTA whose span holds position pos forms this token's K and V rows
-// the same way, appends them to the caches (f16, the reference's rounding) and
-// uses the rounded rows, exactly as the reference attends over its f16 cache.
-constexpr int ATT_CH = 64;
+// as rope_kv_kernel): q heads get bias, QK-norm and RoPE, and the CTA whose span
+// holds position pos forms this token's K and V rows the same way, appends them to
+// the caches (f16, the reference's rounding) and uses the rounded rows, exactly as
+// the reference attends over its f16 cache.
+//
+// Everything that does not depend on the previous kernel happens before
+// griddepcontrol.wait: the position (written before this kernel's stream position
+// by another kernel than the previous one: in the decode graph, the previous
+// token's last kernel), the cached rows of earlier positions, the RoPE angles,
+// biases and norm weights.
+constexpr int ATT_CH = 64;       // positions per sub-chunk (one K/V buffer)
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAXG = 8;
-constexpr int ATT_MAXC = 64;  // spans per kv head at most
-constexpr int ATT_KPAD = 8;   // f16 pad per cached row in shared memory (272-byte rows)
-// q in shared memory: 8 floats of padding after every 32, so the four quarter-dims a warp
-// reads at once (32 floats apart) fall in different banks
-constexpr int ATT_QS = 160;   // floats per head row (128 + 4 * 8)
-__host__ __device__ constexpr int att_qi(int d) { return d + ((d >> 5) << 3); }
+constexpr int ATT_SPANS = 16;    // CTAs per kv head: one cluster
+constexpr int ATT_MIN = 16;      // positions per span at least
+constexpr int ATT_HD = 128;
+constexpr int ATT_RS = ATT_HD + 8;  // f16 per K/V/q row in shared memory (272 B: ldmatrix rows conflict-free)
+constexpr int ATT_PS = ATT_CH + 8;  // f16 per P row (144 B)
+
+// Positions per span for a context of seq positions.
+__host__ __device__ inline int att_span(int seq)
+{
+    const int per = (seq + ATT_SPANS - 1) / ATT_SPANS;
+    const int span = (per + ATT_MIN - 1) / ATT_MIN * ATT_MIN;
+    return span > ATT_MIN ? span : ATT_MIN;
+}
 
 struct AttnArgs {
     const float *qkv;          // q [heads][hd]; with rope: then k [kv_heads][hd], v [kv_heads][hd]
@@ -145,98 +162,174 @@ struct AttnArgs {
     const float *knorm;        // rope: [hd] or null
     uint16_t *kc, *vc;         // [ctx][kv_dim] f16
     float *out;                // [heads][hd]
-    float *part;               // workspace [kv_heads][ATT_MAXC][G][hd + 2]
-    unsigned *cnt;             // workspace [kv_heads], zero between launches
     const int *pos;
-    int heads, kv_heads, kv_dim, ctx, span;
+    int heads, kv_heads, kv_dim, ctx;
     float theta, eps;
     int neox, rope;
 };
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+struct AttSmem {
+    uint16_t k[2][ATT_CH][ATT_RS];
+    uint16_t v[2][ATT_CH][ATT_RS];
+    uint16_t qh[ATT_MAXG][ATT_RS], ql[ATT_MAXG][ATT_RS];  // q = qh + ql (f16 parts)
+    uint16_t ph[ATT_MAXG][ATT_PS], pl[ATT_MAXG][ATT_PS];  // P = ph + pl
+    float sc[ATT_MAXG][ATT_CH];
+    float acc[ATT_MAXG][ATT_HD];                          // this span's unnormalised output
+    float m[ATT_MAXG], l[ATT_MAXG], f[ATT_MAXG];
+    uint16_t knew[ATT_HD], vnew[ATT_HD];
+    float rc[ATT_HD / 2], rs[ATT_HD / 2];
+    uint64_t bar[2];
+};
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar)
 {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-                 "l"(src)
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tcmv::smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(tcmv::smem_u32(bar))
                  : "memory");
 }
 
-template <int HD>
-__global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(AttnArgs a)
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p)
 {
-    static_assert(HD == 128, "one lane per two RoPE pairs; one thread per two P.V dims of two heads");
-    __shared__ float qs[ATT_MAXG][ATT_QS];
-    __shared__ __align__(16) uint16_t ks[ATT_CH][HD + ATT_KPAD];
-    __shared__ __align__(16) uint16_t vs[ATT_CH][HD + ATT_KPAD];
-    __shared__ __align__(16) uint16_t knew[HD], vnew[HD];
-    __shared__ float sc[ATT_MAXG][ATT_CH];
-    __shared__ float rc[HD / 2], rs[HD / 2];
-    __shared__ float s_m[ATT_MAXG], s_l[ATT_MAXG], s_f[ATT_MAXG];
-    __shared__ float sw[ATT_MAXG][ATT_MAXC];
-    __shared__ int is_last;
-    griddep_wait();
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(tcmv::smem_u32(p)));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(tcmv::smem_u32(p)));
+}
+
+__device__ __forceinline__ float cluster_ld_f32(const void *p, int rank)
+{
+    uint32_t ra;
+    float v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(tcmv::smem_u32(p)), "r"(rank));
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void cluster_sync()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// f32 -> f16 hi part and the f16 rounding of the rest
+__device__ __forceinline__ void split_f16(float x, uint16_t &hi, uint16_t &lo)
+{
+    const __half h = __float2half_rn(x);
+    hi = __half_as_ushort(h);
+    lo = __half_as_ushort(__float2half_rn(x - __half2float(h)));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(AttnArgs a)
+{
+    static_assert(HD == ATT_HD, "one lane per two RoPE pairs; 8 warps x 16 output dims");
+    extern __shared__ __align__(128) uint8_t att_raw[];
+    AttSmem &s = *reinterpret_cast<AttSmem *>(att_raw);
     const int G = a.heads / a.kv_heads, kvh = blockIdx.y, c = blockIdx.x, tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31;
-    const int pos = *a.pos, seq = pos + 1;
-    const int nch = (seq + a.span - 1) / a.span;
-    if (pos < 0 || c >= nch || seq > a.ctx || nch > ATT_MAXC) {
-        if (c == 0 && tid == 0 && (pos < 0 || seq > a.ctx || nch > ATT_MAXC)) set_dev_error(0x62u);
+    const int warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
+    const int pos = __ldcg(a.pos), seq = pos + 1;
+    if (pos < 0 || seq > a.ctx) {  // the same for every CTA: all leave
+        if (c == 0 && kvh == 0 && tid == 0) set_dev_error(0x62u);
         return;
     }
-    const int tb = c * a.span, te = min(seq, tb + a.span);
+    const int span = att_span(seq), nch = (seq + span - 1) / span;
+    const bool active = c < nch;
+    const int tb = c * span, te = active ? min(seq, tb + span) : tb;
+    const int nsub = active ? (te - tb + ATT_CH - 1) / ATT_CH : 0;
     const bool own_new = a.rope && c == nch - 1;  // this CTA forms and appends row pos
-    // first sub-chunk's rows in flight while q (and the new rows) are prepared
-    auto load_rows = [&](int t0, int tn) {
-        for (int i = tid; i < tn * (HD / 8); i += ATT_THREADS) {
-            const int r = i / (HD / 8), v8 = i % (HD / 8);
-            if (own_new && t0 + r == pos) continue;
-            const size_t g = (size_t)(t0 + r) * a.kv_dim + kvh * HD + v8 * 8;
-            cp_async16(&ks[r][v8 * 8], a.kc + g);
-            cp_async16(&vs[r][v8 * 8], a.vc + g);
+    if (nch == 1 && !active) return;              // no merge to take part in
+    // the next kernel may be scheduled now; it reads the output only after its own wait
+    griddep_launch();
+    if (tid == 0) {
+        tcmv::mbar_init(&s.bar[0], 1);
+        tcmv::mbar_init(&s.bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // q and P rows of absent heads stay zero; no head has a running max yet
+    for (int i = tid; i < (ATT_MAXG - G) * ATT_RS; i += ATT_THREADS)
+        (&s.qh[G][0])[i] = 0, (&s.ql[G][0])[i] = 0;
+    for (int i = tid; i < (ATT_MAXG - G) * ATT_PS; i += ATT_THREADS) (&s.ph[G][0])[i] = 0, (&s.pl[G][0])[i] = 0;
+    if (tid < ATT_MAXG) s.m[tid] = -INFINITY, s.l[tid] = 0.0f, s.f[tid] = 0.0f;
+    __syncthreads();
+    // rows of sub-chunk i into buffer i & 1 (warp 0); row pos is this token's, formed below
+    auto issue = [&](int i) {
+        const int t0 = tb + i * ATT_CH, tn = min(ATT_CH, te - t0), b = i & 1;
+        const bool skip = own_new && pos >= t0 && pos < t0 + tn;
+        if (lane == 0) tcmv::mbar_expect_tx_arrive(&s.bar[b], (unsigned)(tn - (skip ? 1 : 0)) * HD * 4);
+        __syncwarp();
+        for (int r = lane; r < tn; r += 32) {
+            if (skip && t0 + r == pos) continue;
+            const size_t g = (size_t)(t0 + r) * a.kv_dim + (size_t)kvh * HD;
+            bulk_g2s(&s.k[b][r][0], a.kc + g, HD * 2, &s.bar[b]);
+            bulk_g2s(&s.v[b][r][0], a.vc + g, HD * 2, &s.bar[b]);
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    load_rows(tb, min(ATT_CH, te - tb));
+    if (warp == 0) {
+        if (nsub > 0) issue(0);
+        if (nsub > 1) issue(1);
+    }
+    int issued = nsub < 2 ? nsub : 2;
     // RoPE angles (rope_cabezas: freq_i = theta^(-2i/d), angle = pos * freq_i)
-    if (a.rope && tid < HD / 2) {
+    if (active && a.rope && tid < HD / 2) {
         const float freq = powf(a.theta, (-2.0f * (float)tid) / (float)HD);
         const float ang = (float)pos * freq;
-        rs[tid] = sinf(ang);
-        rc[tid] = cosf(ang);
+        s.rs[tid] = sinf(ang);
+        s.rc[tid] = cosf(ang);
     }
-    if (tid < ATT_MAXG) s_m[tid] = -INFINITY, s_l[tid] = 0.0f;
-    __syncthreads();
     // q heads of the group (and, for own_new, this token's k and v rows): one warp per
-    // vector, lane l holds pairs l and l + 32
-    const int ntask = G + (own_new ? 2 : 0);
-    for (int task = warp; task < ntask; task += ATT_THREADS / 32) {
+    // vector, lane l holds pairs l and l + 32; a warp has two vectors at most
+    const int ntask = active ? G + (own_new ? 2 : 0) : 0;
+    int e[4];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int p = lane + 32 * h;
+        e[2 * h] = a.neox ? p : 2 * p;
+        e[2 * h + 1] = a.neox ? p + HD / 2 : 2 * p + 1;
+    }
+    float cb[2][4], cn[2][4];  // bias and norm weight of each of this warp's vectors
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++) {
+        const int task = warp + tt * (ATT_THREADS / 32);
         const int kind = task < G ? 0 : task - G + 1;  // 0 q, 1 k, 2 v
         const int base = kind == 0 ? (kvh * G + task) * HD : a.heads * HD + (kind == 2 ? a.kv_dim : 0) + kvh * HD;
-        float v[4];
-        int e[4];
+        const float *nw = kind == 0 ? a.qnorm : kind == 1 ? a.knorm : nullptr;
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int p = lane + 32 * h;
-            e[2 * h] = a.neox ? p : 2 * p;
-            e[2 * h + 1] = a.neox ? p + HD / 2 : 2 * p + 1;
+        for (int k = 0; k < 4; k++) {
+            cb[tt][k] = task < ntask && a.rope && a.bias ? a.bias[base + e[k]] : 0.0f;
+            cn[tt][k] = task < ntask && a.rope && nw ? nw[e[k]] : 1.0f;
         }
+    }
+    griddep_wait();  // q|k|v are written by the previous kernel
+    __syncthreads();
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++) {
+        const int task = warp + tt * (ATT_THREADS / 32);
+        if (task >= ntask) break;
+        const int kind = task < G ? 0 : task - G + 1;
+        const int base = kind == 0 ? (kvh * G + task) * HD : a.heads * HD + (kind == 2 ? a.kv_dim : 0) + kvh * HD;
+        float v[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) v[k] = a.qkv[base + e[k]];
         if (a.rope) {
-            if (a.bias) {
 #pragma unroll
-                for (int k = 0; k < 4; k++) v[k] += a.bias[base + e[k]];
-            }
-            const float *nw = kind == 0 ? a.qnorm : kind == 1 ? a.knorm : nullptr;
-            if (nw) {
+            for (int k = 0; k < 4; k++) v[k] += cb[tt][k];
+            const bool normed = kind == 0 ? a.qnorm != nullptr : kind == 1 ? a.knorm != nullptr : false;
+            if (normed) {
                 const float ss = warp_sum((v[0] * v[0] + v[1] * v[1]) + (v[2] * v[2] + v[3] * v[3]));
                 const float scale = 1.0f / sqrtf(ss / (float)HD + a.eps);
 #pragma unroll
-                for (int k = 0; k < 4; k++) v[k] = v[k] * scale * nw[e[k]];
+                for (int k = 0; k < 4; k++) v[k] = v[k] * scale * cn[tt][k];
             }
             if (kind < 2) {
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
-                    const float cs = rc[lane + 32 * h], sn = rs[lane + 32 * h];
+                    const float cs = s.rc[lane + 32 * h], sn = s.rs[lane + 32 * h];
                     const float x0 = v[2 * h], x1 = v[2 * h + 1];
                     v[2 * h] = x0 * cs - x1 * sn;
                     v[2 * h + 1] = x0 * sn + x1 * cs;
@@ -245,10 +338,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(AttnArgs a)
         }
         if (kind == 0) {
 #pragma unroll
-            for (int k = 0; k < 4; k++) qs[task][att_qi(e[k])] = v[k];
+            for (int k = 0; k < 4; k++) split_f16(v[k], s.qh[task][e[k]], s.ql[task][e[k]]);
         } else {
             uint16_t *row = (kind == 1 ? a.kc : a.vc) + (size_t)pos * a.kv_dim + kvh * HD;
-            uint16_t *nrow = kind == 1 ? knew : vnew;
+            uint16_t *nrow = kind == 1 ? s.knew : s.vnew;
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const uint16_t hb = f32_to_f16_ref(v[k]);
@@ -257,168 +350,152 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(AttnArgs a)
             }
         }
     }
+    __syncthreads();
     const float inv = 1.0f / sqrtf((float)HD);
-    // P.V ownership: dims 2*dp, 2*dp+1 of heads j0 and j0 + 4
-    const int dp = tid % (HD / 2), j0 = tid / (HD / 2);
-    float ax[2] = {0.0f, 0.0f}, ay[2] = {0.0f, 0.0f};
-    for (int t0 = tb; t0 < te; t0 += ATT_CH) {
-        const int tn = min(ATT_CH, te - t0);
-        if (t0 != tb) load_rows(t0, tn);
-        asm volatile("cp.async.wait_all;" ::: "memory");
-        __syncthreads();  // rows landed; q and the new rows written
+    // O^T accumulator of warp w: dims 16w + g8 (+ 8) x heads 2*t4, 2*t4 + 1
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int mi = lane >> 3, mr = lane & 7;  // ldmatrix: matrix and row this lane addresses
+    bool failed = false;
+    int done = 0;
+    for (int i = 0; i < nsub; i++) {
+        const int t0 = tb + i * ATT_CH, tn = min(ATT_CH, te - t0), b = i & 1;
+        if (!tcmv::mbar_wait(&s.bar[b], (unsigned)(i >> 1) & 1u)) failed = true;
+        if (__syncthreads_or(failed)) {
+            failed = true;
+            break;
+        }
+        done = i + 1;
         if (own_new && pos >= t0 && pos < t0 + tn)
-            for (int i = tid; i < HD; i += ATT_THREADS) ks[pos - t0][i] = knew[i], vs[pos - t0][i] = vnew[i];
+            for (int d = tid; d < HD; d += ATT_THREADS) s.k[b][pos - t0][d] = s.knew[d], s.v[b][pos - t0][d] = s.vnew[d];
+        // rows past the sub-chunk: zero V (P is zero there; stale rows could hold non-finite values)
+        for (int idx = tid; idx < (ATT_CH - tn) * (HD / 2); idx += ATT_THREADS)
+            reinterpret_cast<uint32_t *>(&s.v[b][tn + idx / (HD / 2)][0])[idx % (HD / 2)] = 0u;
         __syncthreads();
-        // scores: thread (t = tid/4, quarter dq = tid%4)
-        {
-            const int t = tid >> 2, dq = tid & 3;
-            float part[ATT_MAXG];
+        // scores: warp w < 4 takes positions 16w..16w+15 (rows of the MMA), heads as columns
+        if (warp < 4) {
+            const int p0 = warp * 16;
+            float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (p0 < tn) {
 #pragma unroll
-            for (int j = 0; j < ATT_MAXG; j++) part[j] = 0.0f;
-            if (t < tn) {
-#pragma unroll
-                for (int v8 = 0; v8 < HD / 32; v8++) {
-                    const uint4 kk = *reinterpret_cast<const uint4 *>(&ks[t][dq * (HD / 4) + v8 * 8]);
-                    const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w};
-#pragma unroll
-                    for (int e2 = 0; e2 < 4; e2++) {
-                        const float2 kf = __half22float2(*reinterpret_cast<const __half2 *>(&kw[e2]));
-                        const int d = att_qi(dq * (HD / 4) + v8 * 8 + 2 * e2);
-#pragma unroll
-                        for (int j = 0; j < ATT_MAXG; j++)
-                            if (j < G) {
-                                const float2 qv = *reinterpret_cast<const float2 *>(&qs[j][d]);
-                                part[j] += qv.x * kf.x + qv.y * kf.y;
-                            }
-                    }
+                for (int k0 = 0; k0 < HD; k0 += 16) {
+                    uint32_t af[4];
+                    ldsm_x4(af, &s.k[b][p0 + (mi & 1) * 8 + mr][k0 + (mi >> 1) * 8]);
+                    const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(&s.qh[g8][k0 + 2 * t4]);
+                    const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(&s.qh[g8][k0 + 2 * t4 + 8]);
+                    const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(&s.ql[g8][k0 + 2 * t4]);
+                    const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(&s.ql[g8][k0 + 2 * t4 + 8]);
+                    tcmv::mma_f16(d, af[0], af[1], af[2], af[3], bh0, bh1);
+                    tcmv::mma_f16(d, af[0], af[1], af[2], af[3], bl0, bl1);
                 }
             }
-#pragma unroll
-            for (int j = 0; j < ATT_MAXG; j++) {
-                part[j] += __shfl_xor_sync(0xffffffffu, part[j], 1);
-                part[j] += __shfl_xor_sync(0xffffffffu, part[j], 2);
+            const int pa = p0 + g8, pb = pa + 8, h0 = 2 * t4, h1 = h0 + 1;
+            if (h0 < G) {
+                s.sc[h0][pa] = pa < tn ? d[0] * inv : -INFINITY;
+                s.sc[h0][pb] = pb < tn ? d[2] * inv : -INFINITY;
             }
-            if (dq == 0)
-                for (int j = 0; j < G; j++) sc[j][t] = t < tn ? part[j] * inv : -INFINITY;
+            if (h1 < G) {
+                s.sc[h1][pa] = pa < tn ? d[1] * inv : -INFINITY;
+                s.sc[h1][pb] = pb < tn ? d[3] * inv : -INFINITY;
+            }
         }
         __syncthreads();
-        // online softmax: warp j owns head j
+        // online softmax: warp j owns head j; P as f16 parts
         if (warp < G) {
-            const float s0 = sc[warp][lane], s1 = sc[warp][lane + 32];
+            const float s0 = s.sc[warp][lane], s1 = s.sc[warp][lane + 32];
             float m = fmaxf(s0, s1);
 #pragma unroll
             for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            const float mo = s_m[warp], mn = fmaxf(mo, m);
+            const float mo = s.m[warp], mn = fmaxf(mo, m);
             const float p0 = lane < tn ? expf(s0 - mn) : 0.0f, p1 = lane + 32 < tn ? expf(s1 - mn) : 0.0f;
-            sc[warp][lane] = p0;
-            sc[warp][lane + 32] = p1;
+            split_f16(p0, s.ph[warp][lane], s.pl[warp][lane]);
+            split_f16(p1, s.ph[warp][lane + 32], s.pl[warp][lane + 32]);
             const float l = warp_sum(p0 + p1);
-            __syncwarp();
             if (lane == 0) {
                 const float f = mo == -INFINITY ? 0.0f : expf(mo - mn);
-                s_f[warp] = f;
-                s_l[warp] = s_l[warp] * f + l;
-                s_m[warp] = mn;
+                s.f[warp] = f;
+                s.l[warp] = s.l[warp] * f + l;
+                s.m[warp] = mn;
             }
         }
         __syncthreads();
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int j = j0 + 4 * h;
-            if (j >= G) continue;
-            const float f = s_f[j];
-            float x0 = ax[h] * f, y0 = ay[h] * f;
-            for (int t = 0; t < tn; t++) {
-                const float p = sc[j][t];
-                const float2 vf = __half22float2(*reinterpret_cast<const __half2 *>(&vs[t][2 * dp]));
-                x0 += p * vf.x;
-                y0 += p * vf.y;
+        // O^T (dims x heads) = f * O^T + V^T . P^T: warp w takes dims 16w..16w+15
+        {
+            const float fa = s.f[2 * t4], fb = s.f[2 * t4 + 1];
+            acc[0] *= fa, acc[1] *= fb, acc[2] *= fa, acc[3] *= fb;
+            const int d0 = warp * 16;
+            for (int k0 = 0; k0 < tn; k0 += 16) {
+                uint32_t af[4];
+                ldsm_x4_t(af, &s.v[b][k0 + (mi >> 1) * 8 + mr][d0 + (mi & 1) * 8]);
+                const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(&s.ph[g8][k0 + 2 * t4]);
+                const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(&s.ph[g8][k0 + 2 * t4 + 8]);
+                const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(&s.pl[g8][k0 + 2 * t4]);
+                const uint32_t bl1 = *reinterpret_cast<const uint32_t *>(&s.pl[g8][k0 + 2 * t4 + 8]);
+                tcmv::mma_f16(acc, af[0], af[1], af[2], af[3], bh0, bh1);
+                tcmv::mma_f16(acc, af[0], af[1], af[2], af[3], bl0, bl1);
             }
-            ax[h] = x0, ay[h] = y0;
         }
-        __syncthreads();  // before the next sub-chunk overwrites ks / vs / sc
-    }
-    if (nch == 1) {  // the whole context in one span: normalise and store
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int j = j0 + 4 * h;
-            if (j >= G) continue;
-            const float l = s_l[j], r = l > 0.0f ? 1.0f / l : 0.0f;
-            float *o = a.out + (size_t)(kvh * G + j) * HD;
-            o[2 * dp] = l > 0.0f ? ax[h] * r : 0.0f;
-            o[2 * dp + 1] = l > 0.0f ? ay[h] * r : 0.0f;
+        __syncthreads();  // buffer b, the scores and P are free again
+        if (warp == 0 && i + 2 < nsub) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(i + 2);
         }
-        griddep_launch();
-        return;
+        if (i + 2 < nsub) issued = i + 3;
     }
-    float *dst = a.part + ((size_t)(kvh * ATT_MAXC + c) * G) * (HD + 2);
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const int j = j0 + 4 * h;
-        if (j >= G) continue;
-        dst[j * (HD + 2) + 2 * dp] = ax[h];
-        dst[j * (HD + 2) + 2 * dp + 1] = ay[h];
-    }
-    if (tid < G) dst[tid * (HD + 2) + HD] = s_m[tid], dst[tid * (HD + 2) + HD + 1] = s_l[tid];
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) is_last = atomicAdd(&a.cnt[kvh], 1u) == (unsigned)(nch - 1);
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    // merge spans 0..nch-1 (combinar_trozos): per head, weights exp(m_c - M) from one warp,
-    // then every output element as an independent-load sum over spans
-    const float *base = a.part + (size_t)kvh * ATT_MAXC * G * (HD + 2);
-    // (m, l) of every span read once (two spans per lane at most: ATT_MAXC = 64)
-    if (warp < G) {
-        const int j = warp;
-        float mv[2], lv[2];
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int cc = lane + 32 * u;
-            const float *pc = base + ((size_t)cc * G + j) * (HD + 2);
-            lv[u] = cc < nch ? __ldcg(pc + HD + 1) : 0.0f;
-            mv[u] = cc < nch ? __ldcg(pc + HD) : -INFINITY;
+    if (failed) {
+        // let the copies issued into this CTA's shared memory land before leaving (bounded)
+        if (tid == 0) {
+            set_dev_error(0x64u);
+            for (int i = done; i < issued; i++) tcmv::mbar_wait(&s.bar[i & 1], (unsigned)(i >> 1) & 1u);
         }
-        float M = fmaxf(lv[0] > 0.0f ? mv[0] : -INFINITY, lv[1] > 0.0f ? mv[1] : -INFINITY);
-#pragma unroll
-        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float L = 0.0f;
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int cc = lane + 32 * u;
-            const float w = lv[u] > 0.0f ? expf(mv[u] - M) : 0.0f;
-            if (cc < nch) sw[j][cc] = w;
-            L += w * lv[u];
-        }
-        L = warp_sum(L);
-        if (lane == 0) s_l[j] = L;
+        __syncthreads();
     }
-    __syncthreads();
-    // every thread sums its G*HD/ATT_THREADS outputs together, span by span, so the loads of
-    // one span (and of the next few) are all in flight at once
-    constexpr int PER = ATT_MAXG * HD / ATT_THREADS;  // 4
-    float o[PER];
-#pragma unroll
-    for (int u = 0; u < PER; u++) o[u] = 0.0f;
-#pragma unroll 4
-    for (int cc = 0; cc < nch; cc++) {
-#pragma unroll
-        for (int u = 0; u < PER; u++) {
-            const int i = tid + u * ATT_THREADS, j = i / HD, d = i % HD;
-            if (j < G) o[u] += sw[j][cc] * __ldcg(base + ((size_t)cc * G + j) * (HD + 2) + d);
+    {
+        const int d0 = warp * 16 + g8, h0 = 2 * t4;
+        if (nch == 1) {  // the whole context in one span: normalise and store
+            if (h0 < G) {
+                const float l = s.l[h0], r = l > 0.0f ? 1.0f / l : 0.0f;
+                a.out[(size_t)(kvh * G + h0) * HD + d0] = l > 0.0f ? acc[0] * r : 0.0f;
+                a.out[(size_t)(kvh * G + h0) * HD + d0 + 8] = l > 0.0f ? acc[2] * r : 0.0f;
+            }
+            if (h0 + 1 < G) {
+                const float l = s.l[h0 + 1], r = l > 0.0f ? 1.0f / l : 0.0f;
+                a.out[(size_t)(kvh * G + h0 + 1) * HD + d0] = l > 0.0f ? acc[1] * r : 0.0f;
+                a.out[(size_t)(kvh * G + h0 + 1) * HD + d0 + 8] = l > 0.0f ? acc[3] * r : 0.0f;
+            }
+            return;
         }
+        s.acc[h0][d0] = acc[0];
+        s.acc[h0 + 1][d0] = acc[1];
+        s.acc[h0][d0 + 8] = acc[2];
+        s.acc[h0 + 1][d0 + 8] = acc[3];
     }
+    // merge the spans (combinar_trozos): every CTA of the cluster forms G*HD/ATT_SPANS of
+    // the outputs from all CTAs' (m, l, acc), in span order
+    cluster_sync();
+    const int per = G * HD / ATT_SPANS;
+    if (tid < per) {
+        const int o = c * per + tid, j = o / HD, d = o % HD;
+        float mv[ATT_SPANS], lv[ATT_SPANS], av[ATT_SPANS];
 #pragma unroll
-    for (int u = 0; u < PER; u++) {
-        const int i = tid + u * ATT_THREADS, j = i / HD, d = i % HD;
-        if (j < G) {
-            const float L = s_l[j];
-            a.out[(kvh * G + j) * HD + d] = L > 0.0f ? o[u] * (1.0f / L) : 0.0f;
+        for (int cc = 0; cc < ATT_SPANS; cc++) {
+            mv[cc] = cc < nch ? cluster_ld_f32(&s.m[j], cc) : -INFINITY;
+            lv[cc] = cc < nch ? cluster_ld_f32(&s.l[j], cc) : 0.0f;
+            av[cc] = cc < nch ? cluster_ld_f32(&s.acc[j][d], cc) : 0.0f;
         }
+        float M = -INFINITY;
+#pragma unroll
+        for (int cc = 0; cc < ATT_SPANS; cc++)
+            if (lv[cc] > 0.0f) M = fmaxf(M, mv[cc]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < ATT_SPANS; cc++) {
+            const float w = lv[cc] > 0.0f ? expf(mv[cc] - M) : 0.0f;
+            L += w * lv[cc];
+            O += w * av[cc];
+        }
+        a.out[(size_t)(kvh * G + j) * HD + d] = L > 0.0f ? O * (1.0f / L) : 0.0f;
     }
-    if (tid == 0) a.cnt[kvh] = 0u;
-    griddep_launch();
+    cluster_sync();  // no CTA leaves while the others still read its shared memory
 }
 
 // ------------------------------------------------------------------- router
@@ -634,6 +711,7 @@ __global__ void argmax_gather_kernel(GatherArgs a)
 __global__ void embed_kernel(const uint8_t *__restrict__ table, int dtype, int vocab, int h, const int *tok,
                              float *__restrict__ out)
 {
+    griddep_launch();  // the next kernel reads the row only after its own wait
     griddep_wait();
     const int t = *tok;
     if (t < 0 || t >= vocab) {
@@ -671,7 +749,6 @@ __global__ void embed_kernel(const uint8_t *__restrict__ table, int dtype, int v
         }
         out[e] = v;
     }
-    griddep_launch();
 }
 
 }  // namespace sb
@@ -716,32 +793,53 @@ extern "C" int sbk_rope_kv_append(float *qkv, const float *bias, const float *qn
 
 extern "C" size_t sbk_attn_ws_bytes(size_t heads, size_t kv_heads, size_t head_dim, size_t ctx)
 {
-    const size_t G = kv_heads ? heads / kv_heads : 0;
-    (void)ctx;
-    return 256 + kv_heads * 4 + 16 + kv_heads * sb::ATT_MAXC * G * (head_dim + 2) * 4;
+    // the spans are merged inside each kv head's cluster: no workspace is used (kept for the
+    // interface: a caller may pass any buffer)
+    (void)heads, (void)kv_heads, (void)head_dim, (void)ctx;
+    return 256;
 }
 
 namespace sb {
 inline int attn_launch(const AttnArgs &a0, size_t heads, size_t kv_heads, size_t head_dim, size_t ctx, void *ws,
                        int pdl, cudaStream_t s)
 {
-    if (!a0.qkv || !a0.kc || !a0.vc || !a0.out || !a0.pos || !ws || !kv_heads || heads % kv_heads) return -1;
+    (void)ws;
+    if (!a0.qkv || !a0.kc || !a0.vc || !a0.out || !a0.pos || !kv_heads || heads % kv_heads) return -1;
     const size_t G = heads / kv_heads;
-    if (G > ATT_MAXG || head_dim != 128 || ctx == 0 || ctx > (1u << 24)) return -1;
+    if (G > ATT_MAXG || head_dim != ATT_HD || ctx == 0 || ctx > (1u << 24) || kv_heads > 65535) return -1;
     if (((uintptr_t)a0.kc | (uintptr_t)a0.vc) & 15) return -2;
-    // positions per CTA: ATT_CH, or a multiple of it so at most ATT_MAXC spans cover ctx
-    const size_t subs = (ctx + ATT_CH - 1) / ATT_CH;
-    const int span = (int)(((subs + ATT_MAXC - 1) / ATT_MAXC) * ATT_CH);
-    const int chunks = (int)((ctx + span - 1) / span);
-    // workspace: [counters (zeroed, left zero)] [partials]
+    // one cluster of ATT_SPANS CTAs per kv head (a non-portable cluster size)
+    static size_t smem_rec[64];
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64) return -3;
+        if (!smem_rec[dev]) {
+            if (cudaFuncSetAttribute(attn_decode_kernel<ATT_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)sizeof(AttSmem)) != cudaSuccess ||
+                cudaFuncSetAttribute(attn_decode_kernel<ATT_HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+                    cudaSuccess)
+                return -3;
+            smem_rec[dev] = sizeof(AttSmem);
+        }
+    }
     AttnArgs a = a0;
-    a.cnt = (unsigned *)ws;
-    float *part = (float *)((char *)ws + 256 + kv_heads * 4);
-    a.part = (float *)(((uintptr_t)part + 15) & ~(uintptr_t)15);
     a.heads = (int)heads, a.kv_heads = (int)kv_heads, a.kv_dim = (int)(kv_heads * head_dim);
-    a.ctx = (int)ctx, a.span = span;
-    return launch_k(attn_decode_kernel<128>, dim3((unsigned)chunks, (unsigned)kv_heads), dim3(ATT_THREADS), 0, pdl,
-                    s, a);
+    a.ctx = (int)ctx;
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3((unsigned)ATT_SPANS, (unsigned)kv_heads);
+    c.blockDim = dim3(ATT_THREADS);
+    c.dynamicSmemBytes = sizeof(AttSmem);
+    c.stream = s;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = ATT_SPANS, at[0].val.clusterDim.y = 1, at[0].val.clusterDim.z = 1;
+    at[1] = pdl_attr();
+    c.attrs = at;
+    c.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&c, attn_decode_kernel<ATT_HD>, a) == cudaSuccess ? 0 : -4;
 }
 }  // namespace sb
 

@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
     __shared__ int topi[64];
     __shared__ int own[64];
     __shared__ int s_m;
+    griddep_launch();  // the expert launches read the batches only after their own wait
     griddep_wait();
     const int tid = threadIdx.x, n = a.n_exp;
     float m = -INFINITY;
@@ -189,7 +190,6 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
         dn->d[tid].mapp = a.maps + 3 * e + 2;
         dn->d[tid].pub_off = r * a.xw;
     }
-    griddep_launch();
 }
 
 }  // namespace sb

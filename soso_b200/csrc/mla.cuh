@@ -67,6 +67,7 @@ struct AbsorbArgs {
 __global__ void __launch_bounds__(THREADS) absorb_kernel(AbsorbArgs a)
 {
     extern __shared__ __align__(16) uint8_t sm[];
+    griddep_launch();  // the next kernel reads this one's output only after its own wait
     griddep_wait();
     const int h = blockIdx.x, tid = threadIdx.x, qk_per = a.qk_nope + a.qk_rope;
     const int pos = *a.pos;
@@ -126,7 +127,6 @@ __global__ void __launch_bounds__(THREADS) absorb_kernel(AbsorbArgs a)
         dst[2 * i] = x0 * cs - x1 * sn;
         dst[2 * i + 1] = x0 * sn + x1 * cs;
     }
-    griddep_launch();
 }
 
 struct AttnArgs {
@@ -154,13 +154,16 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(AttnArgs a)
     __shared__ float sc[MAXH][CH];
     __shared__ float sw[MAXH][MAXC];
     __shared__ int is_last;
-    griddep_wait();
+    // the position was written by the previous token's last kernel (complete before this
+    // token's first kernel passed its wait): spans without work leave before waiting
     const int c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int pos = *a.pos, seq = pos + 1, nch = (seq + a.span - 1) / a.span;
+    const int pos = __ldcg(a.pos), seq = pos + 1, nch = (seq + a.span - 1) / a.span;
     if (pos < 0 || seq > a.ctx || nch > MAXC || c >= nch) {
         if (c == 0 && tid == 0 && (pos < 0 || seq > a.ctx || nch > MAXC)) set_dev_error(0x82u);
         return;
     }
+    griddep_launch();
+    griddep_wait();  // the absorbed query and this token's latent row come from the previous kernel
     const int R = a.kv_rank, RP = a.qk_rope, H = a.heads, LS = R + 8;  // padded latent row (halfs)
     float *qt = reinterpret_cast<float *>(sm);                // [H][R]
     float *qr = qt + (size_t)H * R;                           // [H][RP]
@@ -261,7 +264,6 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(AttnArgs a)
                 a.cbar[(size_t)h * R + j + 1] = acc[h][k][1] * r;
             }
         }
-        griddep_launch();
         return;
     }
     float *dst = a.part + (size_t)c * H * (R + 2);
@@ -314,7 +316,6 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(AttnArgs a)
         a.cbar[i] = L > 0.0f ? o * (1.0f / L) : 0.0f;
     }
     if (tid == 0) *a.cnt = 0u;
-    griddep_launch();
 }
 
 inline size_t absorb_smem(int kv_rank, int qk_per) { return (size_t)qk_per * (kv_rank / 256) * 144 + (kv_rank + qk_per) * 4 + 16; }

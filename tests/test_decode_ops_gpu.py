@@ -62,7 +62,8 @@ def test_rope_kv_append(heads, kv_heads, neox, qk_norm, bias):
     assert (kr[:pos] == 0).all() and (kr[pos + 1:] == 0).all()
 
 
-@pytest.mark.parametrize("heads,kv_heads,seq", [(16, 2, 1), (16, 2, 100), (16, 2, 4096), (32, 4, 777), (8, 8, 65)])
+@pytest.mark.parametrize("heads,kv_heads,seq", [(16, 2, 1), (16, 2, 16), (16, 2, 17), (16, 2, 100), (16, 2, 513),
+                                                (16, 2, 2049), (16, 2, 4096), (32, 4, 777), (8, 8, 65)])
 def test_attention_decode(heads, kv_heads, seq):
     import torch
     hd, ctx = 128, 4096
