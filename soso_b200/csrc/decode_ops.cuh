@@ -9,7 +9,7 @@
 #pragma once
 #include "common.cuh"
 #include "group.cuh"
-#include "tc_common.cuh"
+#include "tc_mmv.cuh"
 
 namespace sb {
 
@@ -118,14 +118,16 @@ __global__ void rope_kv_kernel(RopeKvArgs a)
 // the G = heads/kv_heads query heads that share the kv head, so every K/V row is
 // read once per group (like the reference's mo_attn_split, gemma_capa.cu:765-877).
 // A span is taken ATT_CH positions at a time through two shared-memory buffers: the
-// rows of the next sub-chunk are copied (one bulk copy per row, completion counted
-// on an mbarrier) while the current one is computed.  Per sub-chunk, scores
+// rows of the next sub-chunk arrive by TMA (2-D tiles of the cache, 64 rows x 64 dims,
+// 128-byte swizzle; completion counted on an mbarrier) while the current one is
+// computed.  Per sub-chunk, scores
 // S = K.q and the output update O += V^T.P run on the tensor cores (mma.sync
 // m16n8k16, f32 accumulation) with q and P each split into two f16 parts (hi + lo,
 // 22 significant bits; K and V are f16 already), around an online softmax per head
 // in f32.  The spans are merged as combinar_trozos does (attn_grupo.rs:171-203) --
 // weights exp(m_c - M), sum of l_c, in span order -- by the cluster itself: every
-// CTA reads its share of the outputs from all CTAs' shared memory.
+// CTA stores each CTA's share of its partial output into that CTA's shared memory,
+// and after one cluster barrier each CTA forms its share of the outputs locally.
 //
 // With `rope` set the kernel also does the step before it (layer.rs:1146-1193,
 // as rope_kv_kernel): q heads get bias, QK-norm and RoPE, and the CTA whose span
@@ -136,8 +138,9 @@ __global__ void rope_kv_kernel(RopeKvArgs a)
 // Everything that does not depend on the previous kernel happens before
 // griddepcontrol.wait: the position (written before this kernel's stream position
 // by another kernel than the previous one: in the decode graph, the previous
-// token's last kernel), the cached rows of earlier positions, the RoPE angles,
-// biases and norm weights.
+// token's last kernel), the cached rows of earlier positions (the tile holding row
+// pos is loaded too; that row is replaced in shared memory by the one this kernel
+// forms), the RoPE angles, biases and norm weights.
 constexpr int ATT_CH = 64;       // positions per sub-chunk (one K/V buffer)
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_MAXG = 8;
@@ -156,6 +159,7 @@ __host__ __device__ inline int att_span(int seq)
 }
 
 struct AttnArgs {
+    CUtensorMap kmap, vmap;    // the caches as [ctx][kv_dim] u16, box ATT_CH rows x 64 dims, 128-byte swizzle
     const float *qkv;          // q [heads][hd]; with rope: then k [kv_heads][hd], v [kv_heads][hd]
     const float *bias;         // rope: same layout as qkv, or null
     const float *qnorm;        // rope: [hd] or null
@@ -169,24 +173,37 @@ struct AttnArgs {
 };
 
 struct AttSmem {
-    uint16_t k[2][ATT_CH][ATT_RS];
-    uint16_t v[2][ATT_CH][ATT_RS];
+    uint8_t kb[2][2][ATT_CH * 128];  // [buffer][dims 0-63 | 64-127]: 64 rows x 128 B, 128-byte swizzle
+    uint8_t vb[2][2][ATT_CH * 128];
     uint16_t qh[ATT_MAXG][ATT_RS], ql[ATT_MAXG][ATT_RS];  // q = qh + ql (f16 parts)
     uint16_t ph[ATT_MAXG][ATT_PS], pl[ATT_MAXG][ATT_PS];  // P = ph + pl
     float sc[ATT_MAXG][ATT_CH];
-    float acc[ATT_MAXG][ATT_HD];                          // this span's unnormalised output
+    // merge: this CTA's share of the outputs (ATT_MAXG * ATT_HD / ATT_SPANS at most) as each
+    // span left it, and every span's (max, sum) per head
+    float racc[ATT_SPANS][ATT_MAXG * ATT_HD / ATT_SPANS];
+    float rm[ATT_SPANS][ATT_MAXG], rl[ATT_SPANS][ATT_MAXG];
     float m[ATT_MAXG], l[ATT_MAXG], f[ATT_MAXG];
     uint16_t knew[ATT_HD], vnew[ATT_HD];
     float rc[ATT_HD / 2], rs[ATT_HD / 2];
     uint64_t bar[2];
 };
 
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar)
+// Byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t att_swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
+
+// Address of dims d0..d0+7 (d0 a multiple of 8) of tile row `row` in a [2 halves][8 KB] buffer.
+__device__ __forceinline__ const uint8_t *att_at(const uint8_t (*buf)[ATT_CH * 128], int row, int d0)
 {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     tcmv::smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(tcmv::smem_u32(bar))
-                 : "memory");
+    return buf[d0 >> 6] + att_swz(row, (d0 & 63) >> 3);
+}
+
+__device__ __forceinline__ void tma_tile_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(tcmv::smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(tcmv::smem_u32(bar))
+        : "memory");
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p)
@@ -203,13 +220,22 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p)
                  : "r"(tcmv::smem_u32(p)));
 }
 
-__device__ __forceinline__ float cluster_ld_f32(const void *p, int rank)
+// Store v at `p` (this CTA's address of a shared variable) in CTA `rank` of the cluster.
+__device__ __forceinline__ void cluster_st_f32(const void *p, int rank, float v)
 {
     uint32_t ra;
-    float v;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(tcmv::smem_u32(p)), "r"(rank));
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-    return v;
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void cluster_arrive_relaxed()
+{
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait()
+{
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void cluster_sync()
@@ -226,11 +252,12 @@ __device__ __forceinline__ void split_f16(float x, uint16_t &hi, uint16_t &lo)
 }
 
 template <int HD>
-__global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(AttnArgs a)
+__global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __grid_constant__ AttnArgs a)
 {
     static_assert(HD == ATT_HD, "one lane per two RoPE pairs; 8 warps x 16 output dims");
-    extern __shared__ __align__(128) uint8_t att_raw[];
-    AttSmem &s = *reinterpret_cast<AttSmem *>(att_raw);
+    extern __shared__ __align__(1024) uint8_t att_raw[];
+    // the swizzled tiles want 1024-byte-aligned addresses (the launch adds 1024 bytes of slack)
+    AttSmem &s = *reinterpret_cast<AttSmem *>(att_raw + ((1024u - (tcmv::smem_u32(att_raw) & 1023u)) & 1023u));
     const int G = a.heads / a.kv_heads, kvh = blockIdx.y, c = blockIdx.x, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
     const int pos = __ldcg(a.pos), seq = pos + 1;
@@ -246,6 +273,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(AttnArgs a)
     if (nch == 1 && !active) return;              // no merge to take part in
     // the next kernel may be scheduled now; it reads the output only after its own wait
     griddep_launch();
+    // (a CTA's shared memory may be written by the others only once every CTA of the
+    // cluster is running: the first phase of the cluster barrier, waited for before the merge)
+    if (nch > 1) cluster_arrive_relaxed();
     if (tid == 0) {
         tcmv::mbar_init(&s.bar[0], 1);
         tcmv::mbar_init(&s.bar[1], 1);
@@ -257,20 +287,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(AttnArgs a)
     for (int i = tid; i < (ATT_MAXG - G) * ATT_PS; i += ATT_THREADS) (&s.ph[G][0])[i] = 0, (&s.pl[G][0])[i] = 0;
     if (tid < ATT_MAXG) s.m[tid] = -INFINITY, s.l[tid] = 0.0f, s.f[tid] = 0.0f;
     __syncthreads();
-    // rows of sub-chunk i into buffer i & 1 (warp 0); row pos is this token's, formed below
+    // rows t0..t0+63 of sub-chunk i into buffer i & 1 (thread 0): four 64 x 64 tiles (rows
+    // past ctx read as zero; rows past the sub-chunk are not used)
     auto issue = [&](int i) {
-        const int t0 = tb + i * ATT_CH, tn = min(ATT_CH, te - t0), b = i & 1;
-        const bool skip = own_new && pos >= t0 && pos < t0 + tn;
-        if (lane == 0) tcmv::mbar_expect_tx_arrive(&s.bar[b], (unsigned)(tn - (skip ? 1 : 0)) * HD * 4);
-        __syncwarp();
-        for (int r = lane; r < tn; r += 32) {
-            if (skip && t0 + r == pos) continue;
-            const size_t g = (size_t)(t0 + r) * a.kv_dim + (size_t)kvh * HD;
-            bulk_g2s(&s.k[b][r][0], a.kc + g, HD * 2, &s.bar[b]);
-            bulk_g2s(&s.v[b][r][0], a.vc + g, HD * 2, &s.bar[b]);
+        const int t0 = tb + i * ATT_CH, b = i & 1;
+        tcmv::mbar_expect_tx_arrive(&s.bar[b], 4u * ATT_CH * 128);
+        for (int h = 0; h < 2; h++) {
+            tma_tile_2d(s.kb[b][h], &a.kmap, kvh * HD + 64 * h, t0, &s.bar[b]);
+            tma_tile_2d(s.vb[b][h], &a.vmap, kvh * HD + 64 * h, t0, &s.bar[b]);
         }
     };
-    if (warp == 0) {
+    if (tid == 0) {
         if (nsub > 0) issue(0);
         if (nsub > 1) issue(1);
     }
@@ -365,11 +392,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(AttnArgs a)
             break;
         }
         done = i + 1;
-        if (own_new && pos >= t0 && pos < t0 + tn)
-            for (int d = tid; d < HD; d += ATT_THREADS) s.k[b][pos - t0][d] = s.knew[d], s.v[b][pos - t0][d] = s.vnew[d];
-        // rows past the sub-chunk: zero V (P is zero there; stale rows could hold non-finite values)
-        for (int idx = tid; idx < (ATT_CH - tn) * (HD / 2); idx += ATT_THREADS)
-            reinterpret_cast<uint32_t *>(&s.v[b][tn + idx / (HD / 2)][0])[idx % (HD / 2)] = 0u;
+        if (own_new && pos >= t0 && pos < t0 + tn && tid < HD) {  // this token's rows
+            const int r = pos - t0, d = tid;
+            const uint32_t o = att_swz(r, (d & 63) >> 3) + (d & 7) * 2;
+            *reinterpret_cast<uint16_t *>(s.kb[b][d >> 6] + o) = s.knew[d];
+            *reinterpret_cast<uint16_t *>(s.vb[b][d >> 6] + o) = s.vnew[d];
+        }
+        // rows past the sub-chunk: zero V (P is zero there; other rows could hold non-finite values)
+        for (int idx = tid; idx < (ATT_CH - tn) * 64; idx += ATT_THREADS) {
+            const int r = tn + idx / 64, w = idx % 64;
+            reinterpret_cast<uint32_t *>(s.vb[b][w >> 5] + r * 128)[w & 31] = 0u;
+        }
         __syncthreads();
         // scores: warp w < 4 takes positions 16w..16w+15 (rows of the MMA), heads as columns
         if (warp < 4) {
@@ -379,7 +412,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(AttnArgs a)
 #pragma unroll
                 for (int k0 = 0; k0 < HD; k0 += 16) {
                     uint32_t af[4];
-                    ldsm_x4(af, &s.k[b][p0 + (mi & 1) * 8 + mr][k0 + (mi >> 1) * 8]);
+                    ldsm_x4(af, att_at(s.kb[b], p0 + (mi & 1) * 8 + mr, k0 + (mi >> 1) * 8));
                     const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(&s.qh[g8][k0 + 2 * t4]);
                     const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(&s.qh[g8][k0 + 2 * t4 + 8]);
                     const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(&s.ql[g8][k0 + 2 * t4]);
@@ -425,7 +458,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(AttnArgs a)
             const int d0 = warp * 16;
             for (int k0 = 0; k0 < tn; k0 += 16) {
                 uint32_t af[4];
-                ldsm_x4_t(af, &s.v[b][k0 + (mi >> 1) * 8 + mr][d0 + (mi & 1) * 8]);
+                ldsm_x4_t(af, att_at(s.vb[b], k0 + (mi >> 1) * 8 + mr, d0 + (mi & 1) * 8));
                 const uint32_t bh0 = *reinterpret_cast<const uint32_t *>(&s.ph[g8][k0 + 2 * t4]);
                 const uint32_t bh1 = *reinterpret_cast<const uint32_t *>(&s.ph[g8][k0 + 2 * t4 + 8]);
                 const uint32_t bl0 = *reinterpret_cast<const uint32_t *>(&s.pl[g8][k0 + 2 * t4]);
@@ -435,7 +468,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(AttnArgs a)
             }
         }
         __syncthreads();  // buffer b, the scores and P are free again
-        if (warp == 0 && i + 2 < nsub) {
+        if (tid == 0 && i + 2 < nsub) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             issue(i + 2);
         }
@@ -464,38 +497,42 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(AttnArgs a)
             }
             return;
         }
-        s.acc[h0][d0] = acc[0];
-        s.acc[h0 + 1][d0] = acc[1];
-        s.acc[h0][d0 + 8] = acc[2];
-        s.acc[h0 + 1][d0 + 8] = acc[3];
     }
-    // merge the spans (combinar_trozos): every CTA of the cluster forms G*HD/ATT_SPANS of
-    // the outputs from all CTAs' (m, l, acc), in span order
-    cluster_sync();
+    // merge the spans (combinar_trozos): CTA r of the cluster forms outputs r*per .. r*per+per-1
+    // (o = head * HD + dim); every active span stores its share of each CTA's outputs and
+    // its (max, sum) per head there, then after one cluster barrier each CTA merges locally
     const int per = G * HD / ATT_SPANS;
+    cluster_wait();
+    if (active) {
+        const int d0 = warp * 16 + g8, h0 = 2 * t4;
+        const float v4[4] = {acc[0], acc[1], acc[2], acc[3]};
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int h = h0 + (k & 1), d = d0 + 8 * (k >> 1);
+            if (h >= G) continue;
+            const int o = h * HD + d;
+            cluster_st_f32(&s.racc[c][o % per], o / per, v4[k]);
+        }
+        if (tid < ATT_SPANS * G) {
+            const int r = tid / G, j = tid % G;
+            cluster_st_f32(&s.rm[c][j], r, s.m[j]);
+            cluster_st_f32(&s.rl[c][j], r, s.l[j]);
+        }
+    }
+    cluster_sync();
     if (tid < per) {
         const int o = c * per + tid, j = o / HD, d = o % HD;
-        float mv[ATT_SPANS], lv[ATT_SPANS], av[ATT_SPANS];
-#pragma unroll
-        for (int cc = 0; cc < ATT_SPANS; cc++) {
-            mv[cc] = cc < nch ? cluster_ld_f32(&s.m[j], cc) : -INFINITY;
-            lv[cc] = cc < nch ? cluster_ld_f32(&s.l[j], cc) : 0.0f;
-            av[cc] = cc < nch ? cluster_ld_f32(&s.acc[j][d], cc) : 0.0f;
-        }
         float M = -INFINITY;
-#pragma unroll
-        for (int cc = 0; cc < ATT_SPANS; cc++)
-            if (lv[cc] > 0.0f) M = fmaxf(M, mv[cc]);
+        for (int cc = 0; cc < nch; cc++)
+            if (s.rl[cc][j] > 0.0f) M = fmaxf(M, s.rm[cc][j]);
         float L = 0.0f, O = 0.0f;
-#pragma unroll
-        for (int cc = 0; cc < ATT_SPANS; cc++) {
-            const float w = lv[cc] > 0.0f ? expf(mv[cc] - M) : 0.0f;
-            L += w * lv[cc];
-            O += w * av[cc];
+        for (int cc = 0; cc < nch; cc++) {
+            const float lv = s.rl[cc][j], w = lv > 0.0f ? expf(s.rm[cc][j] - M) : 0.0f;
+            L += w * lv;
+            O += w * s.racc[cc][tid];
         }
         a.out[(size_t)(kvh * G + j) * HD + d] = L > 0.0f ? O * (1.0f / L) : 0.0f;
     }
-    cluster_sync();  // no CTA leaves while the others still read its shared memory
 }
 
 // ------------------------------------------------------------------- router
@@ -800,6 +837,21 @@ extern "C" size_t sbk_attn_ws_bytes(size_t heads, size_t kv_heads, size_t head_d
 }
 
 namespace sb {
+// The cache of one layer as a 2-D tensor for the attention kernel's TMA tiles.
+inline int attn_map(CUtensorMap *m, const uint16_t *cache, size_t kv_dim, size_t ctx)
+{
+    tcmv::EncodeTiledFn fn = tcmv::encode_fn();
+    if (!fn) return -6;
+    cuuint64_t dims[2] = {(cuuint64_t)kv_dim, (cuuint64_t)ctx};
+    cuuint64_t strides[1] = {(cuuint64_t)kv_dim * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)ATT_CH};
+    cuuint32_t es[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t *>(cache), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -7;
+}
+
 inline int attn_launch(const AttnArgs &a0, size_t heads, size_t kv_heads, size_t head_dim, size_t ctx, void *ws,
                        int pdl, cudaStream_t s)
 {
@@ -818,7 +870,7 @@ inline int attn_launch(const AttnArgs &a0, size_t heads, size_t kv_heads, size_t
         if (dev < 0 || dev >= 64) return -3;
         if (!smem_rec[dev]) {
             if (cudaFuncSetAttribute(attn_decode_kernel<ATT_HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)sizeof(AttSmem)) != cudaSuccess ||
+                                     (int)sizeof(AttSmem) + 1024) != cudaSuccess ||
                 cudaFuncSetAttribute(attn_decode_kernel<ATT_HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
                     cudaSuccess)
                 return -3;
@@ -828,10 +880,13 @@ inline int attn_launch(const AttnArgs &a0, size_t heads, size_t kv_heads, size_t
     AttnArgs a = a0;
     a.heads = (int)heads, a.kv_heads = (int)kv_heads, a.kv_dim = (int)(kv_heads * head_dim);
     a.ctx = (int)ctx;
+    int rc = attn_map(&a.kmap, a.kc, kv_heads * head_dim, ctx);
+    if (!rc) rc = attn_map(&a.vmap, a.vc, kv_heads * head_dim, ctx);
+    if (rc) return rc;
     cudaLaunchConfig_t c = {};
     c.gridDim = dim3((unsigned)ATT_SPANS, (unsigned)kv_heads);
     c.blockDim = dim3(ATT_THREADS);
-    c.dynamicSmemBytes = sizeof(AttSmem);
+    c.dynamicSmemBytes = sizeof(AttSmem) + 1024;
     c.stream = s;
     cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
