@@ -116,6 +116,96 @@ __device__ __forceinline__ int owner_of(int unit, int total, int n)
     return unit < big ? unit / (base + 1) : rem + (base ? (unit - big) / base : 0);
 }
 
+// x of one segment -> the prepared fragments (s.prep), by the NCW consumer warps (named
+// barrier 1).  Warp w takes units w, w + NCW, ...; the x values of PREP_U of its units are
+// loaded before any of them is used, so one memory round trip serves them all.  XS_NORM
+// (rmsnorm of h = a + b, or a + the weighted set): when every unit fits one such round, the
+// sum of squares comes from the same loads -- per warp over its units, then over the warps
+// in order -- and h, w are used from registers; wider inputs take a first pass for the sum.
+// h_out (CTA 0 only): the new residual stream, each element stored once.
+constexpr int PREP_U = 2;
+
+template <class F>
+__device__ __forceinline__ void prep_segment(XLoad &X, int cols, float *h_out, float eps, const Smem<F> &s, int cwg,
+                                             int lane)
+{
+    constexpr int NCW = F::NCW, XPL = F::XPL;
+    const int nu = F::units(cols), nv4 = cols / 4;
+    const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float4 *ho = reinterpret_cast<float4 *>(h_out);
+    if (X.mode == XS_NORM && nu <= PREP_U * NCW) {
+        float4 v[PREP_U][XPL], w[PREP_U][XPL];
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < PREP_U; j++)
+#pragma unroll
+            for (int k = 0; k < XPL; k++) {
+                const int u = cwg + j * NCW, i = F::xidx(u, lane, k);
+                const bool in = u < nu && i < nv4;
+                v[j][k] = in ? X.h(i) : zero;
+                w[j][k] = in ? X.w[i] : zero;
+            }
+#pragma unroll
+        for (int j = 0; j < PREP_U; j++)
+#pragma unroll
+            for (int k = 0; k < XPL; k++) {
+                const float4 h = v[j][k];
+                ss += (h.x * h.x + h.y * h.y) + (h.z * h.z + h.w * h.w);
+                const int u = cwg + j * NCW, i = F::xidx(u, lane, k);
+                if (ho && u < nu && i < nv4) ho[i] = h;
+            }
+        ss = warp_sum(ss);
+        if (lane == 0) s.red[cwg] = ss;
+        asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+        float tot = 0.0f;
+        for (int q = 0; q < NCW; q++) tot += s.red[q];
+        const float scale = 1.0f / sqrtf(tot / (float)cols + eps);
+#pragma unroll
+        for (int j = 0; j < PREP_U; j++) {
+            const int u = cwg + j * NCW;
+            if (u >= nu) break;
+#pragma unroll
+            for (int k = 0; k < XPL; k++) {
+                const float4 h = v[j][k], g = w[j][k];
+                v[j][k] = make_float4(h.x * scale * g.x, h.y * scale * g.y, h.z * scale * g.z, h.w * scale * g.w);
+            }
+            F::prep_unit(u, nu, v[j], s.prep);
+        }
+        return;
+    }
+    if (X.mode == XS_NORM) {
+        // sum of squares of h = a (+ b or the weighted residuals) first, in a fixed order
+        float ss = 0.0f;
+        for (int i = cwg * 32 + lane; i < nv4; i += NCW * 32) {
+            const float4 v = X.h(i);
+            if (ho) ho[i] = v;
+            ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) s.red[cwg] = ss;
+        asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+        float tot = 0.0f;
+        for (int q = 0; q < NCW; q++) tot += s.red[q];
+        X.scale = 1.0f / sqrtf(tot / (float)cols + eps);
+    }
+    for (int u0 = cwg; u0 < nu; u0 += PREP_U * NCW) {
+        float4 v[PREP_U][XPL];
+#pragma unroll
+        for (int j = 0; j < PREP_U; j++)
+#pragma unroll
+            for (int k = 0; k < XPL; k++) {
+                const int u = u0 + j * NCW, i = F::xidx(u, lane, k);
+                v[j][k] = u < nu && i < nv4 ? X(i) : zero;
+            }
+#pragma unroll
+        for (int j = 0; j < PREP_U; j++) {
+            const int u = u0 + j * NCW;
+            if (u >= nu) break;
+            F::prep_unit(u, nu, v[j], s.prep);
+        }
+    }
+}
+
 template <class F, bool DEV>
 __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
 {
@@ -225,23 +315,7 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
                 X.ny = B.xs.mode == XS_NORM ? B.xs.ny : 0;
                 X.ys4 = B.xs.ystride / 4;
                 for (int k = 0; k < X.ny; k++) X.yw[k] = B.xs.yw[k];
-                if (B.xs.mode == XS_NORM) {
-                    // sum of squares of h = a (+ b or the weighted residuals), fixed order; CTA 0 stores h
-                    float ss = 0.0f;
-                    float4 *ho = blockIdx.x == 0 ? reinterpret_cast<float4 *>(B.xs.h_out) : nullptr;
-                    for (int i = cwg * 32 + lane; i < d.cols / 4; i += NCW * 32) {
-                        const float4 v = X.h(i);
-                        if (ho) ho[i] = v;
-                        ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
-                    }
-                    ss = warp_sum(ss);
-                    if (lane == 0) s.red[cwg] = ss;
-                    asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-                    float tot = 0.0f;
-                    for (int w = 0; w < NCW; w++) tot += s.red[w];
-                    X.scale = 1.0f / sqrtf(tot / (float)d.cols + B.xs.eps);
-                }
-                F::prep_x(X, d.cols, s.prep, cwg);
+                prep_segment<F>(X, d.cols, blockIdx.x == 0 ? B.xs.h_out : nullptr, B.xs.eps, s, cwg, lane);
                 prev_x = d.x;
                 prev_cols = d.cols;
             }

@@ -69,18 +69,20 @@ struct Q4K {
         return ((size_t)(cols / 256) * (1024 + 32 + 8) + 15) & ~(size_t)15;
     }
 
-    // x -> prep.  A warp takes one block at a time; lane l holds elements
-    // 4l..4l+3 and 128+4l..128+4l+3.  Element e of sub-block s, piece p, goes to
+    // x -> prep, one block b (unit) per warp at a time; lane l holds elements 4l..4l+3
+    // (v[0]) and 128+4l..128+4l+3 (v[1]).  Element e of sub-block s, piece p, goes to
     // live lane L = 2(4*((s>>1)&1) + p) + (e>>4), register
     // 4*(2*(s>>2) + (s&1)) + 2*((e>>3)&1) + ((e>>2)&1), byte e&3.
-    __device__ static void prep_x(const XLoad &X, int cols, uint8_t *prep, int cw)
+    static constexpr int XPL = 2;  // float4 of x per lane per unit
+    __device__ static int xidx(int b, int l, int k) { return b * 64 + 32 * k + l; }
+    __device__ static void prep_unit(int b, int nb, const float4 (&v)[XPL], uint8_t *prep)
     {
-        const int nb = cols / 256, l = threadIdx.x & 31;
+        const int l = threadIdx.x & 31;
         uint32_t *frag = reinterpret_cast<uint32_t *>(prep);
         unsigned short *mfr = reinterpret_cast<unsigned short *>(prep + (size_t)nb * 1024);
         float *fx = reinterpret_cast<float *>(prep + (size_t)nb * 1056), *fm = fx + nb;
-        for (int b = cw; b < nb; b += NCW) {
-            const float4 va = X(b * 64 + l), vb = X(b * 64 + 32 + l);
+        {
+            const float4 va = v[0], vb = v[1];
             const float mx = fmaxf(fmaxf(fmaxf(fabsf(va.x), fabsf(va.y)), fmaxf(fabsf(va.z), fabsf(va.w))),
                                    fmaxf(fmaxf(fabsf(vb.x), fabsf(vb.y)), fmaxf(fabsf(vb.z), fabsf(vb.w))));
             float sa = (va.x + va.y) + (va.z + va.w), sbv = (vb.x + vb.y) + (vb.z + vb.w);
@@ -113,8 +115,8 @@ struct Q4K {
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     const int sidx = 4 * c + (l >> 3);
-                    const float v = sv[c] * ms;
-                    const __half hi = __float2half_rn(v), lo = __float2half_rn(v - __half2float(hi));
+                    const float sm = sv[c] * ms;
+                    const __half hi = __float2half_rn(sm), lo = __float2half_rn(sm - __half2float(hi));
                     mfr[((b * 2 + 0) * 4 + (sidx >> 1)) * 2 + (sidx & 1)] = __half_as_ushort(hi);
                     mfr[((b * 2 + 1) * 4 + (sidx >> 1)) * 2 + (sidx & 1)] = __half_as_ushort(lo);
                 }

@@ -93,16 +93,18 @@ struct Q6KP {
     // Lane l holds elements 8l..8l+7 of the block: half n = l/16, k = (l/4)%4,
     // t = l%4 (l = 8t.. of the 32), so its pieces go to live lane 2(4*(t/2) + p) +
     // (t%2), register 4*((4n + k)/2) + 2*((4n + k)&1) + (4-element half), byte.
-    __device__ static void prep_x(const XLoad &X, int cols, uint8_t *prep, int cw)
+    static constexpr int XPL = 2;  // float4 of x per lane per unit: v[0] = elements 8l..8l+3, v[1] = 8l+4..8l+7
+    __device__ static int xidx(int b, int l, int k) { return b * 64 + 2 * l + k; }
+    __device__ static void prep_unit(int b, int nb, const float4 (&v)[XPL], uint8_t *prep)
     {
-        const int nb = cols / 256, l = threadIdx.x & 31;
+        const int l = threadIdx.x & 31;
         uint32_t *frag = reinterpret_cast<uint32_t *>(prep);
         int8_t *ofr = reinterpret_cast<int8_t *>(prep + (size_t)nb * 1024);
         float *fx = reinterpret_cast<float *>(prep + (size_t)nb * 1152);
         const int n = l >> 4, kk = (l >> 2) & 3, te = l & 3, sig = te >> 1, tp = te & 1;
         const int mi = 4 * n + kk, q = mi >> 1;
-        for (int b = cw; b < nb; b += NCW) {
-            const float4 va = X(b * 64 + 2 * l), vb = X(b * 64 + 2 * l + 1);
+        {
+            const float4 va = v[0], vb = v[1];
             const float mx = fmaxf(fmaxf(fmaxf(fabsf(va.x), fabsf(va.y)), fmaxf(fabsf(va.z), fabsf(va.w))),
                                    fmaxf(fmaxf(fabsf(vb.x), fabsf(vb.y)), fmaxf(fabsf(vb.z), fabsf(vb.w))));
             const int ex = warp_exp_above(mx);

@@ -60,16 +60,16 @@ struct Q80 {
     // then fx [u] f32 = 2^(ex - 7), the weight of piece 0.
     __host__ __device__ static size_t prep_bytes(int cols) { return ((size_t)units(cols) * 516 + 15) & ~(size_t)15; }
 
-    // Lane l holds elements 4l..4l+3 of the unit: block l/8, quad l%8.
-    __device__ static void prep_x(const XLoad &X, int cols, uint8_t *prep, int cw)
+    // Lane l holds elements 4l..4l+3 of the unit (v[0], zero past the row's end): block l/8, quad l%8.
+    static constexpr int XPL = 1;
+    __device__ static int xidx(int u, int l, int) { return u * 32 + l; }
+    __device__ static void prep_unit(int u, int nu, const float4 (&vx)[XPL], uint8_t *prep)
     {
-        const int nu = units(cols), l = threadIdx.x & 31;
+        const int l = threadIdx.x & 31;
         uint32_t *frag = reinterpret_cast<uint32_t *>(prep);
         float *fx = reinterpret_cast<float *>(prep + (size_t)nu * 512);
-        const int nv4 = cols / 4;
-        for (int u = cw; u < nu; u += NCW) {
-            const int i4 = u * 32 + l;
-            const float4 v = i4 < nv4 ? X(i4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        {
+            const float4 v = vx[0];
             const float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
             const int ex = warp_exp_above(mx);
             const float scl = pow2f(7 - ex);
