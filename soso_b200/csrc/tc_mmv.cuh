@@ -49,15 +49,21 @@ struct __align__(64) MatDesc {
     int pub_off;            // where this matrix's rows go in the batch's exchange slots (floats)
 };
 
+constexpr int MAXGRID = 160;       // CTAs per launch at most (the per-CTA table)
+
+// A batch as every CTA reads it: the header and this CTA's entry of the per-CTA table
+// come first (a few cache lines, no dependent lookups before the weight stream starts),
+// then the matrices.
 struct Batch {
-    MatDesc d[MAXB];
-    XSrc xs;                   // how every matrix's x is formed (tc_common.cuh)
     int n, total;              // matrices, stages
     int max_cols, max_groups;  // shared-memory capacities (prep, partial table)
     int split_groups;          // 1: CTAs take whole 16-row groups (no cut groups, no fix-up)
     int total_groups;
+    XSrc xs;                   // how every matrix's x is formed (tc_common.cuh)
     grp::Pub pub;              // also store every matrix's rows into the group's exchange areas
     grp::Wait wait;            // wait for an exchange point before reading the input
+    int4 cta[MAXGRID];         // per CTA: first stage, end stage, first and last matrix touched
+    MatDesc d[MAXB];
 };
 
 template <class F>
@@ -66,7 +72,7 @@ struct Smem {
     uint8_t *prep;    // F::prep_bytes(max_cols)
     uint8_t *zero;    // 64 B of zeros: the B fragment of lanes that carry no x
     float *part;      // [groups of this CTA][NCW][16]
-    float *red;       // [64]: the sum of squares of an XS_NORM input, per consumer warp
+    float *red;       // [64]: the sum of squares of an XS_NORM input, per unit or per consumer warp
     uint64_t *full;   // [NSLOT]
     uint64_t *empty;  // [NSLOT]
 };
@@ -99,15 +105,6 @@ __device__ __forceinline__ Smem<F> carve(uint8_t *base, int max_cols, int max_gr
     return s;
 }
 
-// First stage of 16-row group g of the batch (groups numbered across matrices).
-__device__ __forceinline__ int stage_of_group(const Batch &B, int g)
-{
-    if (g >= B.total_groups) return B.total;
-    int i = 0;
-    while (i + 1 < B.n && B.d[i + 1].cnt_off <= g) i++;
-    return B.d[i].st_begin + (g - B.d[i].cnt_off) * B.d[i].spg;
-}
-
 // inverse of row_strip: which of n parts holds `unit`
 __device__ __forceinline__ int owner_of(int unit, int total, int n)
 {
@@ -122,7 +119,9 @@ __device__ __forceinline__ int owner_of(int unit, int total, int n)
 // (rmsnorm of h = a + b, or a + the weighted set): when every unit fits one such round, the
 // sum of squares comes from the same loads -- per warp over its units, then over the warps
 // in order -- and h, w are used from registers; wider inputs take a first pass for the sum.
-// h_out (CTA 0 only): the new residual stream, each element stored once.
+// h_out (CTA 0 only): the new residual stream, each element stored once.  Every CTA reads
+// the same x: each starts at a different unit (a rotation by its index), so that at any
+// moment the CTAs ask the L2 for different lines instead of all for the same ones.
 constexpr int PREP_U = 2;
 
 template <class F>
@@ -131,38 +130,44 @@ __device__ __forceinline__ void prep_segment(XLoad &X, int cols, float *h_out, f
 {
     constexpr int NCW = F::NCW, XPL = F::XPL;
     const int nu = F::units(cols), nv4 = cols / 4;
+    const int rot = (int)((blockIdx.x * 5u) % (unsigned)nu);  // unit u -> slot (u + rot) % nu
+    auto unit = [&](int q) { return q < nu ? (q + rot < nu ? q + rot : q + rot - nu) : nu; };
     const float4 zero = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float4 *ho = reinterpret_cast<float4 *>(h_out);
     if (X.mode == XS_NORM && nu <= PREP_U * NCW) {
         float4 v[PREP_U][XPL], w[PREP_U][XPL];
-        float ss = 0.0f;
 #pragma unroll
         for (int j = 0; j < PREP_U; j++)
 #pragma unroll
             for (int k = 0; k < XPL; k++) {
-                const int u = cwg + j * NCW, i = F::xidx(u, lane, k);
+                const int u = unit(cwg + j * NCW), i = F::xidx(u, lane, k);
                 const bool in = u < nu && i < nv4;
                 v[j][k] = in ? X.h(i) : zero;
                 w[j][k] = in ? X.w[i] : zero;
             }
+        // sum of squares per unit (lanes in a fixed order), then over the units in order: the
+        // same in every CTA whatever the rotation
 #pragma unroll
-        for (int j = 0; j < PREP_U; j++)
+        for (int j = 0; j < PREP_U; j++) {
+            const int u = unit(cwg + j * NCW);
+            float ss = 0.0f;
 #pragma unroll
             for (int k = 0; k < XPL; k++) {
                 const float4 h = v[j][k];
                 ss += (h.x * h.x + h.y * h.y) + (h.z * h.z + h.w * h.w);
-                const int u = cwg + j * NCW, i = F::xidx(u, lane, k);
+                const int i = F::xidx(u, lane, k);
                 if (ho && u < nu && i < nv4) ho[i] = h;
             }
-        ss = warp_sum(ss);
-        if (lane == 0) s.red[cwg] = ss;
+            ss = warp_sum(ss);
+            if (lane == 0 && u < nu) s.red[u] = ss;
+        }
         asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
         float tot = 0.0f;
-        for (int q = 0; q < NCW; q++) tot += s.red[q];
+        for (int q = 0; q < nu; q++) tot += s.red[q];
         const float scale = 1.0f / sqrtf(tot / (float)cols + eps);
 #pragma unroll
         for (int j = 0; j < PREP_U; j++) {
-            const int u = cwg + j * NCW;
+            const int u = unit(cwg + j * NCW);
             if (u >= nu) break;
 #pragma unroll
             for (int k = 0; k < XPL; k++) {
@@ -194,12 +199,12 @@ __device__ __forceinline__ void prep_segment(XLoad &X, int cols, float *h_out, f
         for (int j = 0; j < PREP_U; j++)
 #pragma unroll
             for (int k = 0; k < XPL; k++) {
-                const int u = u0 + j * NCW, i = F::xidx(u, lane, k);
+                const int u = unit(u0 + j * NCW), i = F::xidx(u, lane, k);
                 v[j][k] = u < nu && i < nv4 ? X(i) : zero;
             }
 #pragma unroll
         for (int j = 0; j < PREP_U; j++) {
-            const int u = u0 + j * NCW;
+            const int u = unit(u0 + j * NCW);
             if (u >= nu) break;
             F::prep_unit(u, nu, v[j], s.prep);
         }
@@ -216,22 +221,10 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
     static_assert(NSLOT % NSTREAM == 0, "a ring slot must belong to one consumer team");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<F> s = carve<F>(smem_raw, B.max_cols, B.max_groups);
-    int st0, st1;
-    if (B.split_groups) {
-        int g0, g1;
-        row_strip(B.total_groups, blockIdx.x, gridDim.x, g0, g1);
-        st0 = stage_of_group(B, g0);
-        st1 = stage_of_group(B, g1);
-    } else {
-        row_strip(B.total, blockIdx.x, gridDim.x, st0, st1);
-    }
+    const int4 cr = B.cta[blockIdx.x];  // (built on the host: fill_cta)
+    const int st0 = cr.x, st1 = cr.y, m_first = cr.z, m_last = cr.w;
     const int nst = st1 - st0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // matrices touched: m_first .. m_last
-    int m_first = 0;
-    while (m_first + 1 < B.n && B.d[m_first + 1].st_begin <= st0) m_first++;
-    int m_last = m_first;
-    while (nst > 0 && m_last + 1 < B.n && B.d[m_last + 1].st_begin < st1) m_last++;
 
     if (threadIdx.x == 0) {
         for (int k = 0; k < NSLOT; k++) {
@@ -404,6 +397,7 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
         __syncthreads();
         if (threadIdx.x < B.pub.n) atomicAdd_system(B.pub.cnt[threadIdx.x], 1u);
     }
+    if (B.split_groups) return;  // whole groups: every row is final in the CTA that formed it
     __syncthreads();
     if (nst <= 0) return;
 
@@ -441,8 +435,7 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
             const int G = side_g[side], ga = d.st_begin + G * d.spg, ge = ga + d.spg;
             float v = 0.0f;
             for (int c = side_ca[side]; c <= side_cb[side]; c++) {
-                int cs0, cs1;
-                row_strip(B.total, c, gridDim.x, cs0, cs1);
+                const int cs0 = B.cta[c].x;
                 // CTA c stored G as side 0 if its range starts inside G, else as side 1
                 v += __ldcg(&ws.part[(c * 2 + ((cs0 >= ga && cs0 < ge) ? 0 : 1)) * 16 + r]);
             }
@@ -621,6 +614,35 @@ struct MatOpX {  // a MatOp with a per-matrix second input (XS_SWIGLU) and an op
     const CUtensorMap *mapp;
 };
 
+// The per-CTA table of a batch over `grid` CTAs: each CTA's stage range (whole groups or an
+// even stage split, as split_groups says) and the matrices it touches.
+inline int fill_cta(Batch *b, int grid)
+{
+    if (grid < 1 || grid > MAXGRID) return -1;
+    auto stage_of = [&](int g) {
+        if (g >= b->total_groups) return b->total;
+        int i = 0;
+        while (i + 1 < b->n && b->d[i + 1].cnt_off <= g) i++;
+        return b->d[i].st_begin + (g - b->d[i].cnt_off) * b->d[i].spg;
+    };
+    for (int c = 0; c < grid; c++) {
+        int st0, st1;
+        if (b->split_groups) {
+            int g0, g1;
+            row_strip(b->total_groups, c, grid, g0, g1);
+            st0 = stage_of(g0), st1 = stage_of(g1);
+        } else {
+            row_strip(b->total, c, grid, st0, st1);
+        }
+        int mf = 0;
+        while (mf + 1 < b->n && b->d[mf + 1].st_begin <= st0) mf++;
+        int ml = mf;
+        while (st1 > st0 && ml + 1 < b->n && b->d[ml + 1].st_begin < st1) ml++;
+        b->cta[c] = make_int4(st0, st1, mf, ml);
+    }
+    return 0;
+}
+
 // Fill *b (every field) for n matrices over `grid` CTAs; *smem = its dynamic shared memory.
 // With `uniform_x` false the matrices may have different inputs (XS_PLAIN / XS_SWIGLU).
 template <class F>
@@ -689,7 +711,7 @@ inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XS
     }
     if (smem > 227 * 1024) return -5;
     *smem_out = smem;
-    return 0;
+    return fill_cta(&b, grid);
 }
 
 // A published matrix's rows must be final in the CTA that computes them: switch a batch
@@ -703,7 +725,7 @@ inline int whole_groups(Batch *b, int grid, size_t *smem)
     *smem = smem_bytes<F>(b->max_cols, b->max_groups);
     if (*smem > 227 * 1024) return -5;
     b->split_groups = 1;
-    return 0;
+    return fill_cta(b, grid);
 }
 
 // A batch of no matrices (every CTA only takes part in the publication, if any); *smem
