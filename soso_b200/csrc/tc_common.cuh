@@ -127,9 +127,9 @@ __device__ __forceinline__ void int8_pieces4(float4 v, uint32_t (&pk)[4])
 // zero and non-finite input.
 __device__ __forceinline__ int warp_exp_above(float mx)
 {
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const uint32_t mxb = __float_as_uint(mx);
+    // mx >= 0 (an absolute value): its bits order like the values, so one integer
+    // reduction over the warp gives the maximum
+    const uint32_t mxb = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
     const int ex = (int)(mxb >> 23) - 126;
     return (mxb == 0u || mxb >= 0x7f800000u) ? 0 : ex < -100 ? -100 : ex > 100 ? 100 : ex;
 }

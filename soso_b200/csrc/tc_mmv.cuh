@@ -280,6 +280,12 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
         const int cwg = warp - 1;  // 0 .. NCW-1
         const int team = cwg / F::NCONS, cw = cwg % F::NCONS, g = lane >> 2, t = lane & 3;
         const typename F::Lane L = F::lane_setup(g, t);
+        {
+            // this CTA's first matrix descriptor into the constant cache while the previous
+            // kernel finishes (the asm keeps the load before the wait)
+            const float *x_first = nst > 0 ? B.d[m_first].x : nullptr;
+            asm volatile("" ::"l"(x_first));
+        }
         griddep_wait();  // x of every matrix is written by the previous kernel
         if (B.wait.n) {  // the input's residual set comes from every rank of the group
             if (cwg == 0 && lane == 0)
