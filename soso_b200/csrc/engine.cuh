@@ -220,6 +220,7 @@ struct EngMat {
 
 struct EngLayer {
     EngMat q, k, v, o, g, u, d;
+    EngMat gu2;  // gate and up as one matrix of 16-row group pairs (its launch forms silu(gate) * up)
     size_t heads = 0, kvh = 0, hd = 0, qd = 0, kvd = 0, ffn = 0;
     float theta = 0.0f;
     int neox = 0;
@@ -358,6 +359,38 @@ int eng_mat_cols(sb_ctx *c, const sb_mat &m, size_t rows, size_t cols, size_t c0
     return 1;
 }
 
+// Rows [r0, r0 + nr) of a gate and an up matrix as one matrix of 16-row groups of each in
+// turn (gate rows 16p.., then up rows 16p.., for p = 0, 1, ...): the launch over it forms
+// silu(gate) * up in its epilogue.  Resident under its own key; 0 when the pair does not
+// qualify (different dtypes, rows not whole groups, a format without the tensor-core kernel).
+int eng_mat_pairs(sb_ctx *c, const sb_mat &g, const sb_mat &u, size_t rows, size_t cols, size_t r0, size_t nr,
+                  EngMat *out)
+{
+    if (!g.key || !u.key || !g.view.bytes || !u.view.bytes) return fail("decode plan: matrix without key or bytes");
+    if (g.rows != rows || g.cols != cols || u.rows != rows || u.cols != cols)
+        return fail(std::string("decode plan: ") + g.key + " / " + u.key + " have unexpected shapes");
+    const uint8_t dt = g.view.dtype;
+    if (dt != u.view.dtype || nr % 16 || !nr || r0 + nr > rows || !admit(&g.view, rows, cols) ||
+        !admit(&u.view, rows, cols))
+        return 0;
+    if (dt != SB_DTYPE_Q4_K && dt != SB_DTYPE_Q6_K && dt != SB_DTYPE_Q8_0) return 0;
+    const size_t rb = sbk_row_bytes(dt, cols);
+    if (!rb) return 0;
+    std::vector<uint8_t> tmp(2 * nr * rb);
+    for (size_t p = 0; p < nr / 16; p++) {
+        memcpy(tmp.data() + (2 * p) * 16 * rb, g.view.bytes + (r0 + 16 * p) * rb, 16 * rb);
+        memcpy(tmp.data() + (2 * p + 1) * 16 * rb, u.view.bytes + (r0 + 16 * p) * rb, 16 * rb);
+    }
+    sb_view v{tmp.data(), tmp.size(), dt, 2 * nr * cols};
+    const std::string key = std::string(g.key) + "|" + u.key + "#pairs" + std::to_string(r0) + "+" + std::to_string(nr);
+    Resident *r = nullptr;
+    const int rc = c->resident(key.c_str(), &v, 2 * nr, cols, &r, true);
+    if (rc <= 0) return rc;
+    if (r->dev_dtype != SB_DTYPE_Q4_K && r->dev_dtype != SB_DTYPE_Q6_K_P && r->dev_dtype != SB_DTYPE_Q8_0_R) return 0;
+    *out = EngMat{r->ptr, r->dev_dtype, 2 * nr, cols};
+    return 1;
+}
+
 int upload_f32(sb_engine *e, const float *src, size_t n, float **dst)
 {
     *dst = nullptr;
@@ -379,9 +412,10 @@ bool fused_dtype(uint8_t dt)
 // one fused launch per dtype where the kernel has the fused input forms, else the
 // input is materialised first (sbk_rmsnorm / sbk_swiglu into `tmp`).
 int run_mv(sb_engine *e, const EngMat *const *ms, float *const *ys, int n, const float *a, const sbk_xsrc &xs,
-           cudaStream_t s, size_t *launches, const sb::grp::Pub *pub = nullptr, const sb::grp::Wait *wait = nullptr)
+           cudaStream_t s, size_t *launches, const sb::grp::Pub *pub = nullptr, const sb::grp::Wait *wait = nullptr,
+           bool pairs = false)
 {
-    if ((pub && pub->n) || (wait && wait->n)) {
+    if ((pub && pub->n) || (wait && wait->n) || pairs) {
         // tensor-parallel forms: one dtype, the tensor-core kernels only
         sbk_mv_op ops[8];
         for (int j = 0; j < n; j++) {
@@ -389,7 +423,7 @@ int run_mv(sb_engine *e, const EngMat *const *ms, float *const *ys, int n, const
             ops[j] = sbk_mv_op{ms[j]->w, ms[j]->rows, ms[j]->cols, a, ys[j]};
         }
         const sb::tcmv::XSrc x{xs.res, xs.norm_w, xs.h_out, xs.eps, xs.mode, xs.ys, xs.yw, xs.ny, xs.ystride};
-        const int rc = sb::matvec_batch_group(ms[0]->dt, ops, n, x, pub, wait, s);
+        const int rc = sb::matvec_batch_group(ms[0]->dt, ops, n, x, pub, wait, s, pairs);
         if (rc) return rc;
         *launches += 1;
         return 0;
@@ -690,7 +724,17 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
             continue;
         }
         // dense FFN block: h + attention output -> rmsnorm -> gate|up; silu(gate) * up -> down
-        {
+        // (with the gate/up pairs matrix, its launch forms silu(gate) * up itself)
+        if (L.gu2.w) {
+            const sbk_xsrc xs = norm_src(L.nf, ho);
+            const EngMat *ms[1] = {&L.gu2};
+            float *ys[1] = {e->gu};
+            const sb::grp::Wait w = wait_of(xprev);
+            const int rc = run_mv(e, ms, ys, 1, hc, xs, s, &n, nullptr, &w, true);
+            if (rc) return fail("decode step: gate/up launch rejected (" + std::to_string(rc) + ")");
+            std::swap(hc, ho);
+            consumed();
+        } else {
             const sbk_xsrc xs = norm_src(L.nf, ho);
             const EngMat *ms[2] = {&L.g, &L.u};
             float *ys[2] = {e->gu, e->gu + L.ffn};
@@ -701,7 +745,7 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
         }
         {
             sbk_xsrc xs{};
-            xs.res = e->gu + L.ffn, xs.mode = SBK_XS_SWIGLU;
+            if (!L.gu2.w) xs.res = e->gu + L.ffn, xs.mode = SBK_XS_SWIGLU;
             const EngMat *ms[1] = {&L.d};
             float *ys[1] = {e->ob};
             if (L.tp_ffn) {  // this rank's share of ffn_down: to every rank
@@ -961,13 +1005,15 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             L.tp_ffn = true;
             const size_t f0 = 256 * (size_t)b0;
             L.ffn = 256 * (size_t)(b1 - b0);
-            if ((rc = eng_mat_rows(c, lp.gate, ffn_g, H, f0, L.ffn, &L.g)) != 1) return bail(rc);
-            if ((rc = eng_mat_rows(c, lp.up, ffn_g, H, f0, L.ffn, &L.u)) != 1) return bail(rc);
+            if ((rc = eng_mat_pairs(c, lp.gate, lp.up, ffn_g, H, f0, L.ffn, &L.gu2)) < 0) return bail(rc);
+            if (rc != 1 && (rc = eng_mat_rows(c, lp.gate, ffn_g, H, f0, L.ffn, &L.g)) != 1) return bail(rc);
+            if (!L.gu2.w && (rc = eng_mat_rows(c, lp.up, ffn_g, H, f0, L.ffn, &L.u)) != 1) return bail(rc);
             if ((rc = eng_mat_cols(c, lp.down, H, ffn_g, f0, L.ffn, &L.d)) != 1) return bail(rc);
         } else {
             L.ffn = lp.gate.rows;
-            if ((rc = eng_mat(c, lp.gate, L.ffn, H, &L.g, true)) != 1) return bail(rc);
-            if ((rc = eng_mat(c, lp.up, L.ffn, H, &L.u, true)) != 1) return bail(rc);
+            if ((rc = eng_mat_pairs(c, lp.gate, lp.up, L.ffn, H, 0, L.ffn, &L.gu2)) < 0) return bail(rc);
+            if (rc != 1 && (rc = eng_mat(c, lp.gate, L.ffn, H, &L.g, true)) != 1) return bail(rc);
+            if (!L.gu2.w && (rc = eng_mat(c, lp.up, L.ffn, H, &L.u, true)) != 1) return bail(rc);
             if ((rc = eng_mat(c, lp.down, H, L.ffn, &L.d, true)) != 1) return bail(rc);
         }
         if (upload_f32(e, lp.norm_attn, H, &L.na) || upload_f32(e, lp.norm_ffn, H, &L.nf) ||

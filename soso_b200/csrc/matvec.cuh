@@ -448,8 +448,9 @@ namespace sb {
 template <class F, class FB = Q4K>
 static int tc_matvec_batch(const sbk_mv_op *ops, size_t n, int pdl, cudaStream_t s, bool fallback,
                            const tcmv::XSrc *xs = nullptr, const grp::Pub *pub = nullptr,
-                           const grp::Wait *wait = nullptr)
+                           const grp::Wait *wait = nullptr, bool pairs = false)
 {
+    if (pairs) fallback = false;
     if ((pub && pub->n) || (wait && wait->n)) fallback = false;
     if (xs && xs->mode != tcmv::XS_PLAIN) fallback = false;  // the CUDA-core kernel has no fused input forms
     const int grid = num_sms_cached();
@@ -468,7 +469,7 @@ static int tc_matvec_batch(const sbk_mv_op *ops, size_t n, int pdl, cudaStream_t
         if (ok && tcmv::fits<F>(mo, (int)nb, grid)) {
             void *ws = stream_ws(s, tcmv::ws_bytes(grid));
             if (!ws) return -3;
-            const int rc = tcmv::launch_batch<F>(mo, (int)nb, ws, grid, pdl, s, xs, pub, wait);
+            const int rc = tcmv::launch_batch<F>(mo, (int)nb, ws, grid, pdl, s, xs, pub, wait, pairs);
             if (rc) return rc;
         } else if (fallback) {
             for (size_t i = 0; i < nb; i++) {
@@ -528,12 +529,15 @@ extern "C" int sbk_matvec_batch(uint8_t dtype, const sbk_mv_op *ops, size_t n, i
 namespace sb {
 // sbk_matvec_batch_x with the group forms: wait for an exchange point before reading the
 // input, and/or publish the (single) matrix's rows to the group (engine.cuh).
+// pairs: one matrix whose rows are 16-row groups of a gate and an up projection in turn;
+// its output is silu(gate) * up (rows / 2 entries).
 inline int matvec_batch_group(uint8_t dtype, const sbk_mv_op *ops, size_t n, const tcmv::XSrc &x,
-                              const grp::Pub *pub, const grp::Wait *wait, cudaStream_t s)
+                              const grp::Pub *pub, const grp::Wait *wait, cudaStream_t s, bool pairs = false)
 {
-    if (dtype == SB_DTYPE_Q4_K) return tc_matvec_batch<tcmv::Q4K>(ops, n, 1, s, false, &x, pub, wait);
-    if (dtype == SB_DTYPE_Q6_K_P) return tc_matvec_batch<tcmv::Q6KP>(ops, n, 1, s, false, &x, pub, wait);
-    if (dtype == SB_DTYPE_Q8_0_R) return tc_matvec_batch<tcmv::Q80, Q80>(ops, n, 1, s, false, &x, pub, wait);
+    if (dtype == SB_DTYPE_Q4_K) return tc_matvec_batch<tcmv::Q4K>(ops, n, 1, s, false, &x, pub, wait, pairs);
+    if (dtype == SB_DTYPE_Q6_K_P) return tc_matvec_batch<tcmv::Q6KP>(ops, n, 1, s, false, &x, pub, wait, pairs);
+    if (dtype == SB_DTYPE_Q8_0_R)
+        return tc_matvec_batch<tcmv::Q80, Q80>(ops, n, 1, s, false, &x, pub, wait, pairs);
     return -5;
 }
 }  // namespace sb

@@ -47,6 +47,7 @@ struct __align__(64) MatDesc {
     int rows, cols, spg;    // spg: stages per 16-row group
     int st_begin, cnt_off;  // first global stage; first counter of its groups
     int pub_off;            // where this matrix's rows go in the batch's exchange slots (floats)
+    int pairs;              // 1: rows are 16-row groups of gate and up in turn; y[i] = silu(gate_i) * up_i
 };
 
 constexpr int MAXGRID = 160;       // CTAs per launch at most (the per-CTA table)
@@ -58,6 +59,7 @@ struct Batch {
     int n, total;              // matrices, stages
     int max_cols, max_groups;  // shared-memory capacities (prep, partial table)
     int split_groups;          // 1: CTAs take whole 16-row groups (no cut groups, no fix-up)
+    int pair_split;            // 1: ... two groups at a time (a matrix of gate/up group pairs)
     int total_groups;
     XSrc xs;                   // how every matrix's x is formed (tc_common.cuh)
     grp::Pub pub;              // also store every matrix's rows into the group's exchange areas
@@ -122,7 +124,10 @@ __device__ __forceinline__ int owner_of(int unit, int total, int n)
 // h_out (CTA 0 only): the new residual stream, each element stored once.  Every CTA reads
 // the same x: each starts at a different unit (a rotation by its index), so that at any
 // moment the CTAs ask the L2 for different lines instead of all for the same ones.
-constexpr int PREP_U = 2;
+#ifndef SB_PREP_U
+#define SB_PREP_U 2  // units per warp per load round (build-time tuning knob)
+#endif
+constexpr int PREP_U = SB_PREP_U;
 
 template <class F>
 __device__ __forceinline__ void prep_segment(XLoad &X, int cols, float *h_out, float eps, const Smem<F> &s, int cwg,
@@ -371,6 +376,21 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
             // segment epilogue: sum the consumer warps' pieces per group (fixed order)
             const bool head_cut = mi == m_first && (st0 - d.st_begin) % spg != 0;
             const bool tail_cut = mi == m_last && (st1 - d.st_begin) % spg != 0 && st1 < d.st_begin + mtot;
+            if (d.pairs) {
+                // gate/up group pairs (whole in this CTA): y = silu(gate) * up (gemm.rs:210-226,
+                // the same f32 steps as the XS_SWIGLU input form)
+                for (int i = cwg * 32 + lane; i < (ng >> 1) * 16; i += NCW * 32) {
+                    const int pl = i >> 4, r = i & 15, row = ((gs0 >> 1) + pl) * 16 + r;
+                    float vg = 0.0f, vu = 0.0f;
+                    for (int w = 0; w < NCW; w++) {
+                        vg += s.part[(2 * pl * NCW + w) * 16 + r];
+                        vu += s.part[((2 * pl + 1) * NCW + w) * 16 + r];
+                    }
+                    if (2 * row < d.rows) d.y[row] = vg / (1.0f + expf(-vg)) * vu;
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+                continue;
+            }
             for (int i = cwg * 32 + lane; i < ng * 16; i += NCW * 32) {
                 const int gl = i >> 4, r = i & 15, row = (gs0 + gl) * 16 + r;
                 float v = 0.0f;
@@ -618,6 +638,7 @@ struct MatOpX {  // a MatOp with a per-matrix second input (XS_SWIGLU) and an op
     MatOp op;
     const float *xb;
     const CUtensorMap *mapp;
+    int pairs = 0;   // gate/up group pairs: y has rows / 2 entries (MatDesc::pairs)
 };
 
 // The per-CTA table of a batch over `grid` CTAs: each CTA's stage range (whole groups or an
@@ -635,7 +656,12 @@ inline int fill_cta(Batch *b, int grid)
         int st0, st1;
         if (b->split_groups) {
             int g0, g1;
-            row_strip(b->total_groups, c, grid, g0, g1);
+            if (b->pair_split) {
+                row_strip(b->total_groups / 2, c, grid, g0, g1);
+                g0 *= 2, g1 *= 2;
+            } else {
+                row_strip(b->total_groups, c, grid, g0, g1);
+            }
             st0 = stage_of(g0), st1 = stage_of(g1);
         } else {
             row_strip(b->total, c, grid, st0, st1);
@@ -675,6 +701,8 @@ inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XS
         d.st_begin = st;
         d.cnt_off = cnt;
         d.pub_off = 0;
+        d.pairs = ops[i].pairs;
+        if (d.pairs && (n != 1 || o.rows % 32)) return -1;
         st += d.spg * ((o.rows + 15) / 16);
         cnt += (o.rows + 15) / 16;
     }
@@ -705,13 +733,16 @@ inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XS
     // and the stream-K split is short (latency-bound): no cross-CTA fix-up at all.
     const int smax = (st + grid - 1) / grid, gmax = group_split_max(b, grid);
     b.split_groups = gmax <= smax || (gmax <= smax + 1 && smax <= 4);
+    b.pair_split = ops[0].pairs;
+    if (b.pair_split) b.split_groups = 1;  // a pair's two groups finish in one CTA
     size_t smem = batch_smem<F>(plain, n, grid, &b.max_cols, &b.max_groups);
     if (b.split_groups) {
-        const int need = (cnt + grid - 1) / grid + 1;
+        const int need = b.pair_split ? 2 * ((cnt / 2 + grid - 1) / grid) + 2 : (cnt + grid - 1) / grid + 1;
         if (need > b.max_groups && smem_bytes<F>(b.max_cols, need) <= 227 * 1024) {
             b.max_groups = need;
             smem = smem_bytes<F>(b.max_cols, need);
         } else if (need > b.max_groups) {
+            if (b.pair_split) return -5;
             b.split_groups = 0;
         }
     }
@@ -782,7 +813,8 @@ inline cudaLaunchConfig_t mmv_config(int grid, int threads, size_t smem, int pdl
 // zero); at most cnt_cap 16-row groups in the batch.
 template <class F>
 inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int grid, int pdl, cudaStream_t stream,
-                           const XSrc *xs = nullptr, const grp::Pub *pub = nullptr, const grp::Wait *wait = nullptr)
+                           const XSrc *xs = nullptr, const grp::Pub *pub = nullptr, const grp::Wait *wait = nullptr,
+                           bool pairs = false)
 {
     if (n < 1 || n > MAXB) return -1;
     static Batch b;  // large: built host-side, passed by value as the kernel parameter
@@ -790,7 +822,7 @@ inline int launch_batch_ws(const MatOp *ops, int n, Ws wsd, int cnt_cap, int gri
     static size_t smem_rec[64];
     std::lock_guard<std::mutex> lk(mu);
     MatOpX ox[MAXB];
-    for (int i = 0; i < n; i++) ox[i] = MatOpX{ops[i], nullptr, nullptr};
+    for (int i = 0; i < n; i++) ox[i] = MatOpX{ops[i], nullptr, nullptr, pairs ? 1 : 0};
     size_t smem = 0;
     int rc = build_batch<F>(ox, n, cnt_cap, grid, xs, &b, &smem);
     if (rc) return rc;
@@ -827,13 +859,14 @@ inline int launch_dev_batch(const Batch *dev, const int *sel, size_t smem, Ws ws
 // As launch_batch_ws over a workspace of ws_bytes(grid) bytes.
 template <class F>
 inline int launch_batch(const MatOp *ops, int n, void *ws, int grid, int pdl, cudaStream_t stream,
-                        const XSrc *xs = nullptr, const grp::Pub *pub = nullptr, const grp::Wait *wait = nullptr)
+                        const XSrc *xs = nullptr, const grp::Pub *pub = nullptr, const grp::Wait *wait = nullptr,
+                        bool pairs = false)
 {
     uint8_t *wsb = reinterpret_cast<uint8_t *>(ws);
     Ws wsd;
     wsd.cnt = reinterpret_cast<unsigned *>(wsb);
     wsd.part = reinterpret_cast<float *>(wsb + ws_part_off());
-    return launch_batch_ws<F>(ops, n, wsd, CNT_MAX, grid, pdl, stream, xs, pub, wait);
+    return launch_batch_ws<F>(ops, n, wsd, CNT_MAX, grid, pdl, stream, xs, pub, wait, pairs);
 }
 
 // Repack GGML Q6_K rows (reference layout) into the packed layout of tc_q6k.cuh.
