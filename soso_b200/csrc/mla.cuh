@@ -33,21 +33,6 @@ constexpr int MAXC = 64;      // spans per step
 constexpr int MAXR = 1024;    // kv_rank
 constexpr int MAXRP = 128;    // qk_rope
 
-// One Q4_K weight: element e (0..255) of the 144-byte block (dequant.rs:150-248).
-__device__ __forceinline__ float q4k_elem(const uint8_t *blk, int e)
-{
-    const float d = __half2float(*reinterpret_cast<const __half *>(blk));
-    const float dmin = __half2float(*reinterpret_cast<const __half *>(blk + 2));
-    const uint8_t *sc = blk + 4;
-    const int j = e >> 5, l = e & 31, pair = e >> 6;
-    unsigned s_, m_;
-    if (j < 4) s_ = sc[j] & 63, m_ = sc[j + 4] & 63;
-    else s_ = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4), m_ = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-    const uint8_t qb = blk[16 + pair * 32 + l];
-    const float q = (float)((j & 1) ? (qb >> 4) : (qb & 15));
-    return (d * (float)s_) * q - dmin * (float)m_;
-}
-
 struct AbsorbArgs {
     const float *q;        // [heads][qk_per], nope first (q_up output)
     const float *c;        // [kv_rank] (kv_down output)
@@ -64,7 +49,7 @@ struct AbsorbArgs {
 // CTA h: head h's absorbed query and roped q slice; for h < kv_heads also kv head h's
 // rope key at pos; CTA 0 appends the latent row.  The rows of k_up that head h needs are
 // staged in shared memory first.
-__global__ void __launch_bounds__(THREADS) absorb_kernel(AbsorbArgs a)
+__global__ void __launch_bounds__(THREADS, 1) absorb_kernel(AbsorbArgs a)
 {
     extern __shared__ __align__(16) uint8_t sm[];
     griddep_launch();  // the next kernel reads this one's output only after its own wait
@@ -76,10 +61,13 @@ __global__ void __launch_bounds__(THREADS) absorb_kernel(AbsorbArgs a)
         return;
     }
     const int group = a.heads / a.kv_heads, kvh = h / group;
-    const int rb = (a.kv_rank / 256) * 144;  // bytes per k_up row
+    const int nbk = a.kv_rank / 256, rb = nbk * 144;  // Q4_K blocks / bytes per k_up row
+    const int nsb = nbk * 8;                          // sub-blocks per row
     uint8_t *rows = sm;                                           // [qk_per][rb]
-    float *cf = reinterpret_cast<float *>(sm + (size_t)qk_per * rb);  // [kv_rank]
-    float *qs = cf + a.kv_rank;                                   // [qk_per]
+    float *ds = reinterpret_cast<float *>(sm + (size_t)qk_per * rb);  // [qk_per][nsb]: d * scale
+    float *dm = ds + (size_t)qk_per * nsb;                            // [qk_per][nsb]: dmin * min
+    float *cf = dm + (size_t)qk_per * nsb;                            // [kv_rank]
+    float *qs = cf + a.kv_rank;                                       // [qk_per]
     // stage head kvh's rows of k_up (contiguous: qk_per rows)
     const uint4 *src = reinterpret_cast<const uint4 *>(a.k_up + (size_t)kvh * qk_per * rb);
     for (int i = tid; i < qk_per * rb / 16; i += THREADS) reinterpret_cast<uint4 *>(rows)[i] = src[i];
@@ -91,6 +79,21 @@ __global__ void __launch_bounds__(THREADS) absorb_kernel(AbsorbArgs a)
     }
     for (int i = tid; i < qk_per; i += THREADS) qs[i] = a.q[(size_t)h * qk_per + i];
     __syncthreads();
+    // per (row, sub-block): d * scale and dmin * min, the two products of every weight of the
+    // sub-block (dequant.rs:150-248: w = (d * sc) * q - dmin * m)
+    for (int idx = tid; idx < qk_per * nsb; idx += THREADS) {
+        const int i = idx / nsb, sbi = idx - i * nsb, j = sbi & 7;
+        const uint8_t *blk = rows + (size_t)i * rb + (sbi >> 3) * 144;
+        const float d = __half2float(*reinterpret_cast<const __half *>(blk));
+        const float dmin = __half2float(*reinterpret_cast<const __half *>(blk + 2));
+        const uint8_t *sc = blk + 4;
+        unsigned s_, m_;
+        if (j < 4) s_ = sc[j] & 63, m_ = sc[j + 4] & 63;
+        else s_ = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4), m_ = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+        ds[idx] = d * (float)s_;
+        dm[idx] = dmin * (float)m_;
+    }
+    __syncthreads();
     // roped q slice (pairs 2i, 2i+1)
     for (int i = tid; i < a.qk_rope / 2; i += THREADS) {
         const float freq = powf(a.theta, -2.0f * (float)i / (float)a.qk_rope);
@@ -99,22 +102,41 @@ __global__ void __launch_bounds__(THREADS) absorb_kernel(AbsorbArgs a)
         a.qr[(size_t)h * a.qk_rope + 2 * i] = x0 * cs - x1 * sn;
         a.qr[(size_t)h * a.qk_rope + 2 * i + 1] = x0 * sn + x1 * cs;
     }
-    // absorbed query: qt[j] = sum_i W_kn[i][j] * q_nope[i], i in row order
-    for (int j = tid; j < a.kv_rank; j += THREADS) {
-        const int b = j >> 8, e = j & 255;
-        float acc = 0.0f;
-        for (int i = 0; i < a.qk_nope; i++) acc += q4k_elem(rows + (size_t)i * rb + b * 144, e) * qs[i];
-        a.qt[(size_t)h * a.kv_rank + j] = acc;
+    // absorbed query: qt[j] = sum_i W_kn[i][j] * q_nope[i], i in row order.  Thread t takes
+    // code byte t of the row (block t / 128): its two weights, elements e and e + 32 of the
+    // block, share the byte (low / high nibble, sub-blocks 2p and 2p + 1).
+    for (int t = tid; t < nbk * 128; t += THREADS) {
+        const int b = t >> 7, bi = t & 127, pair = bi >> 5, l = bi & 31;
+        const int s0 = b * 8 + 2 * pair, j0 = b * 256 + pair * 64 + l;
+        const uint8_t *qp = rows + b * 144 + 16 + bi;
+        float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < a.qk_nope; i++) {
+            const float q0 = (float)(qp[(size_t)i * rb] & 15), q1 = (float)(qp[(size_t)i * rb] >> 4);
+            const float *dsi = ds + (size_t)i * nsb, *dmi = dm + (size_t)i * nsb;
+            acc0 += (dsi[s0] * q0 - dmi[s0]) * qs[i];
+            acc1 += (dsi[s0 + 1] * q1 - dmi[s0 + 1]) * qs[i];
+        }
+        a.qt[(size_t)h * a.kv_rank + j0] = acc0;
+        a.qt[(size_t)h * a.kv_rank + j0 + 32] = acc1;
     }
     if (h >= a.kv_heads) return;
     // rope key of kv head h at pos: rows qk_nope.. of its k_up rows times the latent row,
-    // one warp per row (lanes over the columns, fixed order), then the rotation
+    // one warp per row (lanes over the code bytes, fixed order), then the rotation
     __shared__ float kr[MAXRP];
     const int warp = tid >> 5, lane = tid & 31;
     for (int i = warp; i < a.qk_rope; i += THREADS / 32) {
-        const uint8_t *row = rows + (size_t)(a.qk_nope + i) * rb;
+        const int row = a.qk_nope + i;
+        const uint8_t *rw = rows + (size_t)row * rb;
+        const float *dsi = ds + (size_t)row * nsb, *dmi = dm + (size_t)row * nsb;
         float acc = 0.0f;
-        for (int j = lane; j < a.kv_rank; j += 32) acc += q4k_elem(row + (j >> 8) * 144, j & 255) * cf[j];
+        for (int t = lane; t < nbk * 128; t += 32) {
+            const int b = t >> 7, bi = t & 127, pair = bi >> 5, l = bi & 31;
+            const int s0 = b * 8 + 2 * pair, j0 = b * 256 + pair * 64 + l;
+            const uint8_t qb = rw[b * 144 + 16 + bi];
+            acc += (dsi[s0] * (float)(qb & 15) - dmi[s0]) * cf[j0];
+            acc += (dsi[s0 + 1] * (float)(qb >> 4) - dmi[s0 + 1]) * cf[j0 + 32];
+        }
         acc = warp_sum(acc);
         if (lane == 0) kr[i] = acc;
     }
@@ -318,7 +340,277 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(AttnArgs a)
     if (tid == 0) *a.cnt = 0u;
 }
 
-inline size_t absorb_smem(int kv_rank, int qk_per) { return (size_t)qk_per * (kv_rank / 256) * 144 + (kv_rank + qk_per) * 4 + 16; }
+// ---------------------------------------------------------------- tensor-core form
+// The same attention for kv_rank = 512 (DeepSeek-V2-Lite's latent) on the tensor cores,
+// as the GQA kernel does it (decode_ops.cuh): the CTAs of one 16-CTA cluster take spans of
+// the positions (att_span); latent sub-chunks of 32 rows arrive by TMA (eight 32 x 64 tiles,
+// 128-byte swizzle) into two buffers; the main score term qt_h . c_t and the update
+// cbar_h += sum_t p_t c_t are mma.sync.m16n8k16 with the 16 heads as the M rows, qt and P
+// split into f16 hi + lo parts (c_t is f16 already); the rope term qr_h . kr_t (f32 keys)
+// runs on the CUDA cores; spans merge through the cluster's shared memory.
+constexpr int TC_R = 512;
+constexpr int TC_T = 32;  // positions per sub-chunk
+
+struct TcArgs {
+    CUtensorMap lmap;  // latent [ctx][512] u16, box 32 rows x 64 dims, 128-byte swizzle
+    const float *qt;   // [heads][512]
+    const float *qr;   // [heads][qk_rope]
+    const float *krope;
+    float *cbar;
+    const int *pos;
+    int heads, kv_heads, qk_rope, ctx;
+    float scale;
+};
+
+struct TcSmem {
+    uint8_t lb[2][TC_R / 64][TC_T * 128];  // [buffer][64-dim box]: 32 rows x 128 B, swizzled
+    uint16_t qh[MAXH][TC_R + 8], ql[MAXH][TC_R + 8];
+    uint16_t ph[MAXH][TC_T + 8], pl[MAXH][TC_T + 8];
+    float qr[MAXH][MAXRP];
+    float sc[2][MAXH][TC_T];  // main term, latent dims 0-255 / 256-511
+    float sr[MAXH][TC_T];     // rope term
+    float racc[ATT_SPANS][MAXH * TC_R / ATT_SPANS];
+    float rm[ATT_SPANS][MAXH], rl[ATT_SPANS][MAXH];
+    float m[MAXH], l[MAXH], f[MAXH];
+    uint64_t bar[2];
+};
+
+// Address of dims d0..d0+7 (d0 a multiple of 8) of sub-chunk row `row`.
+__device__ __forceinline__ const uint8_t *tc_at(const uint8_t (*buf)[TC_T * 128], int row, int d0)
+{
+    return buf[d0 >> 6] + att_swz(row, (d0 & 63) >> 3);
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(tcmv::smem_u32(p)));
+}
+
+__global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_constant__ TcArgs a)
+{
+    extern __shared__ __align__(1024) uint8_t tc_raw[];
+    TcSmem &s = *reinterpret_cast<TcSmem *>(tc_raw + ((1024u - (tcmv::smem_u32(tc_raw) & 1023u)) & 1023u));
+    const int H = a.heads, group = a.heads / a.kv_heads, RP = a.qk_rope;
+    const int c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g8 = lane >> 2, t4 = lane & 3;
+    const int pos = __ldcg(a.pos), seq = pos + 1;
+    if (pos < 0 || seq > a.ctx) {  // the same for every CTA: all leave
+        if (c == 0 && tid == 0) set_dev_error(0x82u);
+        return;
+    }
+    const int span = att_span(seq), nch = (seq + span - 1) / span;
+    const bool active = c < nch;
+    const int tb = c * span, te = active ? min(seq, tb + span) : tb;
+    const int nsub = active ? (te - tb + TC_T - 1) / TC_T : 0;
+    const bool late = c == nch - 1;  // holds row pos, which the previous kernel appends
+    if (nch == 1 && !active) return;
+    griddep_launch();
+    if (nch > 1) cluster_arrive_relaxed();
+    if (tid == 0) {
+        tcmv::mbar_init(&s.bar[0], 1);
+        tcmv::mbar_init(&s.bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = tid; i < (MAXH - H) * (TC_R + 8); i += THREADS) (&s.qh[H][0])[i] = 0, (&s.ql[H][0])[i] = 0;
+    for (int i = tid; i < (MAXH - H) * (TC_T + 8); i += THREADS) (&s.ph[H][0])[i] = 0, (&s.pl[H][0])[i] = 0;
+    if (tid < MAXH) s.m[tid] = -INFINITY, s.l[tid] = 0.0f, s.f[tid] = 0.0f;
+    __syncthreads();
+    auto issue = [&](int i) {  // thread 0: rows t0.. of sub-chunk i into buffer i & 1
+        const int t0 = tb + i * TC_T, b = i & 1;
+        tcmv::mbar_expect_tx_arrive(&s.bar[b], (unsigned)(TC_R / 64) * TC_T * 128);
+        for (int q = 0; q < TC_R / 64; q++) tma_tile_2d(s.lb[b][q], &a.lmap, 64 * q, t0, &s.bar[b]);
+    };
+    if (tid == 0 && !late) {
+        if (nsub > 0) issue(0);
+        if (nsub > 1) issue(1);
+    }
+    griddep_wait();  // qt, qr, this token's latent row and rope key come from the previous kernel
+    if (tid == 0 && late) {
+        if (nsub > 0) issue(0);
+        if (nsub > 1) issue(1);
+    }
+    int issued = nsub < 2 ? nsub : 2;
+    if (active) {
+        for (int i = tid; i < H * TC_R; i += THREADS) {
+            const int h = i / TC_R, d = i - h * TC_R;
+            split_f16(a.qt[i], s.qh[h][d], s.ql[h][d]);
+        }
+        for (int i = tid; i < H * RP; i += THREADS) s.qr[i / RP][i % RP] = a.qr[i];
+    }
+    __syncthreads();
+    float acc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+    const int mi = lane >> 3, mr = lane & 7;
+    bool failed = false;
+    int done = 0;
+    for (int i = 0; i < nsub; i++) {
+        const int t0 = tb + i * TC_T, tn = min(TC_T, te - t0), b = i & 1;
+        // rope term (the keys stay in global memory): thread -> head tid / 16, positions tid % 16 (+ 16)
+        {
+            const int h = tid >> 4, tt = tid & 15;
+            if (h < H) {
+                const float *q = s.qr[h];
+#pragma unroll
+                for (int k = 0; k < 2; k++) {
+                    const int t = tt + 16 * k;
+                    float r = 0.0f;
+                    if (t < tn) {
+                        const float4 *kp =
+                            reinterpret_cast<const float4 *>(a.krope + ((size_t)(t0 + t) * a.kv_heads + h / group) * RP);
+                        for (int j = 0; j < RP / 4; j++) {
+                            const float4 kv = __ldcg(kp + j);
+                            r += q[4 * j] * kv.x + q[4 * j + 1] * kv.y + q[4 * j + 2] * kv.z + q[4 * j + 3] * kv.w;
+                        }
+                    }
+                    s.sr[h][t] = r;
+                }
+            }
+        }
+        if (!tcmv::mbar_wait(&s.bar[b], (unsigned)(i >> 1) & 1u)) failed = true;
+        if (__syncthreads_or(failed)) {
+            failed = true;
+            break;
+        }
+        done = i + 1;
+        // rows past the sub-chunk: zero (P is zero there; other rows could hold non-finite values)
+        for (int idx = tid; idx < (TC_T - tn) * (TC_R / 2); idx += THREADS) {
+            const int r = tn + idx / (TC_R / 2), w = idx % (TC_R / 2);
+            reinterpret_cast<uint32_t *>(s.lb[b][w >> 5] + r * 128)[w & 31] = 0u;
+        }
+        __syncthreads();
+        // main term: warp w takes positions 8(w & 3) .. +8 and latent dims 256(w >> 2) .. +256
+        {
+            const int n0 = 8 * (warp & 3), kh = warp >> 2;
+            float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (n0 < tn) {
+#pragma unroll 4
+                for (int ks = 0; ks < 16; ks++) {
+                    const int k0 = kh * 256 + ks * 16;
+                    uint32_t ah[4], al[4], bf[2];
+                    ldsm_x4(ah, &s.qh[(mi & 1) * 8 + mr][k0 + (mi >> 1) * 8]);
+                    ldsm_x4(al, &s.ql[(mi & 1) * 8 + mr][k0 + (mi >> 1) * 8]);
+                    ldsm_x2(bf, tc_at(s.lb[b], n0 + mr, k0 + ((lane >> 3) & 1) * 8));
+                    tcmv::mma_f16(d, ah[0], ah[1], ah[2], ah[3], bf[0], bf[1]);
+                    tcmv::mma_f16(d, al[0], al[1], al[2], al[3], bf[0], bf[1]);
+                }
+            }
+            // d: (head g8 | g8 + 8) x (position n0 + 2 t4 | + 1)
+            s.sc[kh][g8][n0 + 2 * t4] = d[0];
+            s.sc[kh][g8][n0 + 2 * t4 + 1] = d[1];
+            s.sc[kh][g8 + 8][n0 + 2 * t4] = d[2];
+            s.sc[kh][g8 + 8][n0 + 2 * t4 + 1] = d[3];
+        }
+        __syncthreads();
+        // online softmax: warp w takes heads w and w + 8, lane = position
+        for (int hh = warp; hh < H; hh += THREADS / 32) {
+            const float sv = lane < tn ? ((s.sc[0][hh][lane] + s.sc[1][hh][lane]) + s.sr[hh][lane]) * a.scale : -INFINITY;
+            float mx = sv;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            const float mo = s.m[hh], mn = fmaxf(mo, mx);
+            const float p = lane < tn ? expf(sv - mn) : 0.0f;
+            split_f16(p, s.ph[hh][lane], s.pl[hh][lane]);
+            const float l = warp_sum(p);
+            if (lane == 0) {
+                const float f = mo == -INFINITY ? 0.0f : expf(mo - mn);
+                s.f[hh] = f;
+                s.l[hh] = s.l[hh] * f + l;
+                s.m[hh] = mn;
+            }
+        }
+        __syncthreads();
+        // cbar (heads x dims) = f * cbar + P . C: warp w takes latent dims 64w .. 64w + 63
+        {
+            const float fa = s.f[g8], fb = s.f[g8 + 8];
+#pragma unroll
+            for (int nt = 0; nt < 8; nt++) acc[nt][0] *= fa, acc[nt][1] *= fa, acc[nt][2] *= fb, acc[nt][3] *= fb;
+            for (int k0 = 0; k0 < tn; k0 += 16) {
+                uint32_t ph[4], pl[4];
+                ldsm_x4(ph, &s.ph[(mi & 1) * 8 + mr][k0 + (mi >> 1) * 8]);
+                ldsm_x4(pl, &s.pl[(mi & 1) * 8 + mr][k0 + (mi >> 1) * 8]);
+#pragma unroll
+                for (int nt = 0; nt < 8; nt += 2) {
+                    const int n0 = warp * 64 + nt * 8;
+                    uint32_t bt[4];
+                    ldsm_x4_t(bt, tc_at(s.lb[b], k0 + (mi & 1) * 8 + mr, n0 + (mi >> 1) * 8));
+                    tcmv::mma_f16(acc[nt], ph[0], ph[1], ph[2], ph[3], bt[0], bt[1]);
+                    tcmv::mma_f16(acc[nt], pl[0], pl[1], pl[2], pl[3], bt[0], bt[1]);
+                    tcmv::mma_f16(acc[nt + 1], ph[0], ph[1], ph[2], ph[3], bt[2], bt[3]);
+                    tcmv::mma_f16(acc[nt + 1], pl[0], pl[1], pl[2], pl[3], bt[2], bt[3]);
+                }
+            }
+        }
+        __syncthreads();  // buffer b, the scores and P are free again
+        if (tid == 0 && i + 2 < nsub) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(i + 2);
+        }
+        if (i + 2 < nsub) issued = i + 3;
+    }
+    if (failed) {
+        if (tid == 0) {
+            set_dev_error(0x83u);
+            for (int i = done; i < issued; i++) tcmv::mbar_wait(&s.bar[i & 1], (unsigned)(i >> 1) & 1u);
+        }
+        __syncthreads();
+    }
+    if (nch == 1) {  // the whole context in one span: normalise and store
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++) {
+            const int d = warp * 64 + nt * 8 + 2 * t4;
+#pragma unroll
+            for (int hb = 0; hb < 2; hb++) {
+                const int h = g8 + 8 * hb;
+                if (h >= H) continue;
+                const float l = s.l[h], r = l > 0.0f ? 1.0f / l : 0.0f;
+                a.cbar[(size_t)h * TC_R + d] = l > 0.0f ? acc[nt][2 * hb] * r : 0.0f;
+                a.cbar[(size_t)h * TC_R + d + 1] = l > 0.0f ? acc[nt][2 * hb + 1] * r : 0.0f;
+            }
+        }
+        return;
+    }
+    // merge the spans (combinar_trozos): CTA r forms outputs r*per .. (o = head * 512 + dim)
+    const int per = H * TC_R / ATT_SPANS;
+    cluster_wait();
+    if (active) {
+#pragma unroll
+        for (int nt = 0; nt < 8; nt++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int h = g8 + 8 * (k >> 1), d = warp * 64 + nt * 8 + 2 * t4 + (k & 1);
+                if (h >= H) continue;
+                const int o = h * TC_R + d;
+                cluster_st_f32(&s.racc[c][o % per], o / per, acc[nt][k]);
+            }
+        if (tid < ATT_SPANS * H) {
+            const int r = tid / H, j = tid % H;
+            cluster_st_f32(&s.rm[c][j], r, s.m[j]);
+            cluster_st_f32(&s.rl[c][j], r, s.l[j]);
+        }
+    }
+    cluster_sync();
+    for (int q = tid; q < per; q += THREADS) {
+        const int o = c * per + q, j = o / TC_R;
+        float M = -INFINITY;
+        for (int cc = 0; cc < nch; cc++)
+            if (s.rl[cc][j] > 0.0f) M = fmaxf(M, s.rm[cc][j]);
+        float L = 0.0f, O = 0.0f;
+        for (int cc = 0; cc < nch; cc++) {
+            const float lv = s.rl[cc][j], w = lv > 0.0f ? expf(s.rm[cc][j] - M) : 0.0f;
+            L += w * lv;
+            O += w * s.racc[cc][q];
+        }
+        a.cbar[o] = L > 0.0f ? O * (1.0f / L) : 0.0f;
+    }
+}
+
+inline size_t absorb_smem(int kv_rank, int qk_per)
+{
+    return (size_t)qk_per * (kv_rank / 256) * 144 + (size_t)2 * qk_per * (kv_rank / 256) * 8 * 4 + (kv_rank + qk_per) * 4 +
+           16;
+}
 inline size_t attn_smem(int heads, int kv_heads, int kv_rank, int qk_rope)
 {
     return ((size_t)heads * kv_rank + (size_t)heads * qk_rope + (size_t)CH * kv_heads * qk_rope) * 4 +
@@ -364,6 +656,53 @@ extern "C" int sbk_mla_attn(const float *qt, const float *qr, const uint16_t *la
         qk_rope > MAXRP || !ctx || ctx > (1u << 24))
         return -1;
     if (((uintptr_t)latent | (uintptr_t)ws) & 15) return -2;
+    if (kv_rank == TC_R && qk_rope % 4 == 0) {
+        // the tensor-core form: one cluster of ATT_SPANS CTAs (a non-portable cluster size)
+        static size_t tc_rec[64];
+        static std::mutex mu;
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            int dev = 0;
+            cudaGetDevice(&dev);
+            if (dev < 0 || dev >= 64) return -3;
+            if (!tc_rec[dev]) {
+                if (cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(TcSmem) + 1024) != cudaSuccess ||
+                    cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+                        cudaSuccess)
+                    return -3;
+                tc_rec[dev] = 1;
+            }
+        }
+        TcArgs t{};
+        {
+            sb::tcmv::EncodeTiledFn fn = sb::tcmv::encode_fn();
+            if (!fn) return -6;
+            cuuint64_t dims[2] = {(cuuint64_t)TC_R, (cuuint64_t)ctx};
+            cuuint64_t strides[1] = {(cuuint64_t)TC_R * 2};
+            cuuint32_t box[2] = {64, (cuuint32_t)TC_T};
+            cuuint32_t es[2] = {1, 1};
+            if (fn(&t.lmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t *>(latent), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return -7;
+        }
+        t.qt = qt, t.qr = qr, t.krope = krope, t.cbar = cbar, t.pos = pos;
+        t.heads = (int)heads, t.kv_heads = (int)kv_heads, t.qk_rope = (int)qk_rope, t.ctx = (int)ctx;
+        t.scale = 1.0f / sqrtf((float)(qk_nope + qk_rope));
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3((unsigned)sb::ATT_SPANS);
+        lc.blockDim = dim3(THREADS);
+        lc.dynamicSmemBytes = sizeof(TcSmem) + 1024;
+        lc.stream = (cudaStream_t)stream;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = sb::ATT_SPANS, at[0].val.clusterDim.y = 1, at[0].val.clusterDim.z = 1;
+        at[1] = sb::pdl_attr();
+        lc.attrs = at;
+        lc.numAttrs = pdl ? 2 : 1;
+        return cudaLaunchKernelEx(&lc, attn_tc_kernel, t) == cudaSuccess ? 0 : -4;
+    }
     const size_t smem = attn_smem((int)heads, (int)kv_heads, (int)kv_rank, (int)qk_rope);
     if (smem > 227 * 1024) return -1;
     static size_t rec[64];
