@@ -96,8 +96,9 @@ struct RouteArgs {
     tcmv::Batch *gu, *dn;   // [k + 1] each: batch m runs m resident choices (+ the shared
                             // expert, when it is computed here, as matrix m)
     int *sel;               // the batch index m, for both launches
-    const CUtensorMap *maps;  // [hi - lo][3]: gate, up, down of the resident experts
+    const CUtensorMap *maps;  // [hi - lo][3]: gate, up, down of the resident experts (pairs: gate/up, -, down)
     int lo, hi;             // resident experts [lo, hi)
+    int pairs;              // gate|up launches run one gate/up pair matrix per choice
     int xw;                 // floats between exchange slots: the down of choice r publishes at r * xw
 };
 
@@ -185,8 +186,12 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
     if (tid < mo) {
         const int r = own[tid], e = topi[r] - a.lo;
         tcmv::Batch *gu = a.gu + mo, *dn = a.dn + mo;
-        gu->d[2 * tid].mapp = a.maps + 3 * e;
-        gu->d[2 * tid + 1].mapp = a.maps + 3 * e + 1;
+        if (a.pairs) {
+            gu->d[tid].mapp = a.maps + 3 * e;
+        } else {
+            gu->d[2 * tid].mapp = a.maps + 3 * e;
+            gu->d[2 * tid + 1].mapp = a.maps + 3 * e + 1;
+        }
         dn->d[tid].mapp = a.maps + 3 * e + 2;
         dn->d[tid].pub_off = r * a.xw;
     }
@@ -232,6 +237,7 @@ struct EngLayer {
     EngMat router, sh[3];
     std::vector<EngMat> ex;            // [hi - lo][3]: the resident experts
     size_t ex_lo = 0, ex_hi = 0;       // resident experts (all, or this rank's IDs)
+    bool ex_pairs = false;             // ex[3x] (and sh[0]) is the gate/up pair matrix, ex[3x + 1] unused
     bool sh_here = false;              // the shared expert is computed on this GPU
     float *sg = nullptr;               // shared expert gate row, or null (weight 1)
     CUtensorMap *maps = nullptr;       // device [hi - lo][3]: the resident experts' tensor maps
@@ -474,7 +480,7 @@ int build_moe_batches(sb_engine *e, EngLayer &L, const float *hc, const sb::grp:
     XSrc xg{};
     xg.w = L.nf, xg.eps = e->eps, xg.mode = XS_NORM;
     XSrc xd{};
-    xd.mode = XS_SWIGLU;
+    xd.mode = L.ex_pairs ? XS_PLAIN : XS_SWIGLU;
     std::vector<Batch> hg(k + 1), hd(k + 1);
     memset(hg.data(), 0, hg.size() * sizeof(Batch));
     memset(hd.data(), 0, hd.size() * sizeof(Batch));
@@ -492,12 +498,17 @@ int build_moe_batches(sb_engine *e, EngLayer &L, const float *hc, const sb::grp:
                 const EngMat &g = shared ? L.sh[0] : L.ex[0], &u = shared ? L.sh[1] : L.ex[1];
                 const EngMat &d = shared ? L.sh[2] : L.ex[2];
                 float *gi = e->egu + (size_t)(2 * i) * e->moe_ffn, *ui = e->egu + (size_t)(2 * i + 1) * e->moe_ffn;
+                float *yi = e->ys + (size_t)(shared ? k : i) * e->H;
+                if (L.ex_pairs) {  // one pair matrix per choice; its output is silu(gate) * up
+                    gu[i] = MatOpX{MatOp{g.w, (int)g.rows, (int)g.cols, hc, gi}, nullptr, nullptr, 1};
+                    dn[i] = MatOpX{MatOp{d.w, (int)d.rows, (int)d.cols, gi, yi}, nullptr, nullptr};
+                    continue;
+                }
                 gu[2 * i] = MatOpX{MatOp{g.w, (int)g.rows, (int)g.cols, hc, gi}, nullptr, nullptr};
                 gu[2 * i + 1] = MatOpX{MatOp{u.w, (int)u.rows, (int)u.cols, hc, ui}, nullptr, nullptr};
-                dn[i] = MatOpX{MatOp{d.w, (int)d.rows, (int)d.cols, gi, e->ys + (size_t)(shared ? k : i) * e->H}, ui,
-                               nullptr};
+                dn[i] = MatOpX{MatOp{d.w, (int)d.rows, (int)d.cols, gi, yi}, ui, nullptr};
             }
-            int rc = build_batch<FG>(gu, 2 * ns, CNT_MAX, grid, &xg, &hg[m], &sg);
+            int rc = build_batch<FG>(gu, L.ex_pairs ? ns : 2 * ns, CNT_MAX, grid, &xg, &hg[m], &sg);
             if (rc) return fail("decode plan: expert gate/up batch rejected (" + std::to_string(rc) + ")");
             rc = build_batch<FD>(dn, ns, CNT_MAX, grid, &xd, &hd[m], &sd);
             if (!rc && pub) rc = whole_groups<FD>(&hd[m], grid, &sd);
@@ -556,7 +567,8 @@ int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, boo
         if (rc) return rc;
     }
     sb::RouteArgs ra{e->rlog, (int)L.n_exp, (int)L.top_k, e->ridx, e->wts, L.sg, hc, L.nf, e->eps, (int)e->H,
-                     L.has_sh ? 1 : 0, L.gu_b, L.dn_b, L.sel, L.maps, (int)L.ex_lo, (int)L.ex_hi, sb::grp::XW};
+                     L.has_sh ? 1 : 0, L.gu_b, L.dn_b, L.sel, L.maps, (int)L.ex_lo, (int)L.ex_hi, L.ex_pairs ? 1 : 0,
+                     sb::grp::XW};
     if ((rc = sb::launch_k(sb::route_kernel, dim3(1), dim3(256), 0, 1, s, ra))) return rc;
     *n += 1;
     rc = gdt == SB_DTYPE_Q4_K ? launch_moe_batch<sb::tcmv::Q4K>(L.gu_b, L.sel, L.gu_smem, s)
@@ -959,11 +971,32 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             const size_t nl = L.ex_hi - L.ex_lo;
             L.ex.resize(3 * nl);
             std::vector<CUtensorMap> maps(3 * nl);
+            // gate and up of each expert as one matrix of 16-row group pairs (its launch forms
+            // silu(gate) * up) when both are of one tensor-core format
+            {
+                auto pairable = [&](const sb_mat &g, const sb_mat &u, size_t f) {
+                    const uint8_t dt = g.view.dtype;
+                    return g.view.bytes && u.view.bytes && dt == u.view.dtype && f % 16 == 0 &&
+                           (dt == SB_DTYPE_Q4_K || dt == SB_DTYPE_Q6_K || dt == SB_DTYPE_Q8_0);
+                };
+                L.ex_pairs = pairable(mp.experts[3 * L.ex_lo], mp.experts[3 * L.ex_lo + 1], L.effn) &&
+                             (!L.sh_here || pairable(mp.shared[0], mp.shared[1], mp.shared[0].rows));
+            }
             for (size_t x = 0; x < nl; x++) {
                 const size_t r[3] = {L.effn, L.effn, H}, cc[3] = {H, H, L.effn};
                 for (int k = 0; k < 3; k++) {
                     EngMat &m = L.ex[3 * x + k];
-                    if ((rc = eng_mat(c, mp.experts[3 * (L.ex_lo + x) + k], r[k], cc[k], &m, true)) != 1) return bail(rc);
+                    if (L.ex_pairs && k == 1) {  // (the pair matrix's slot repeated)
+                        m = L.ex[3 * x];
+                        maps[3 * x + 1] = maps[3 * x];
+                        continue;
+                    }
+                    if (L.ex_pairs && k == 0) {
+                        const sb_mat &eg = mp.experts[3 * (L.ex_lo + x)], &eu = mp.experts[3 * (L.ex_lo + x) + 1];
+                        if ((rc = eng_mat_pairs(c, eg, eu, L.effn, H, 0, L.effn, &m)) != 1) return bail(rc);
+                    } else if ((rc = eng_mat(c, mp.experts[3 * (L.ex_lo + x) + k], r[k], cc[k], &m, true)) != 1) {
+                        return bail(rc);
+                    }
                     if (m.dt != L.ex[k].dt) return bail(0);  // one dtype per matrix kind
                     const int mr =
                         m.dt == SB_DTYPE_Q4_K
@@ -983,7 +1016,15 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
                 L.sffn = mp.shared[0].rows;
                 const size_t r[3] = {L.sffn, L.sffn, H}, cc[3] = {H, H, L.sffn};
                 for (int k = 0; k < 3; k++) {
-                    if ((rc = eng_mat(c, mp.shared[k], r[k], cc[k], &L.sh[k], true)) != 1) return bail(rc);
+                    if (L.ex_pairs && k == 1) {
+                        L.sh[1] = L.sh[0];
+                        continue;
+                    }
+                    if (L.ex_pairs && k == 0)
+                        rc = eng_mat_pairs(c, mp.shared[0], mp.shared[1], L.sffn, H, 0, L.sffn, &L.sh[0]);
+                    else
+                        rc = eng_mat(c, mp.shared[k], r[k], cc[k], &L.sh[k], true);
+                    if (rc != 1) return bail(rc);
                     if (L.sh[k].dt != L.ex[k].dt) return bail(0);
                 }
                 if (upload_f32(e, mp.shared_gate, H, &L.sg)) return bail(-1);

@@ -702,7 +702,7 @@ inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XS
         d.cnt_off = cnt;
         d.pub_off = 0;
         d.pairs = ops[i].pairs;
-        if (d.pairs && (n != 1 || o.rows % 32)) return -1;
+        if (ops[i].pairs != ops[0].pairs || (d.pairs && o.rows % 32)) return -1;  // all pair matrices or none
         st += d.spg * ((o.rows + 15) / 16);
         cnt += (o.rows + 15) / 16;
     }
