@@ -270,7 +270,9 @@ int sbk_matvec_batch_x(uint8_t dtype, const sbk_mv_op *ops, size_t n, const sbk_
  * (lxdde/ports/nouveau/matvec_iq.cu:731-816, :966; f16 mma.sync) and the CPU
  * matvec_q4_k_batch (crates/soso-llm-core/src/gemm.rs:495-546) behind
  * GpuDispatch::matmul (crates/soso-llm-core/src/gpu.rs:443-455).  ws: at least
- * sbk_matmul_ws_bytes(n, cols) bytes, 16-byte aligned.  -5: dtype not supported. */
+ * sbk_matmul_ws_bytes(n, cols) bytes, 16-byte aligned (X as 16-bit operands, then ~21 MB
+ * for the partial sums when too few output tiles make the GEMM split K into slices).
+ * -5: dtype not supported. */
 size_t sbk_matmul_ws_bytes(size_t n, size_t cols);
 /* prec: SBK_PREC_BF16 (weights and x as bf16, 8 significant bits) or SBK_PREC_F16 (as f16,
  * 11 bits: the precision of the reference's f16 mma.sync prefill). */

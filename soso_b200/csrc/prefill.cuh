@@ -193,8 +193,24 @@ __device__ __forceinline__ void q4k_half_to_16(const uint8_t *blk, int p, int h,
 
 struct Args {
     int rows, cols, n;
-    float *y;  // [n][rows]
+    float *y;      // [n][rows]
+    int kslices;   // > 1: CTA z takes K slice z (whole 256-column blocks) and writes part[z]
+    float *part;   // [kslices][n][rows]
 };
+
+// Partial sums of the K slices -> Y, in slice order.
+__global__ void pf_reduce_kernel(const float *__restrict__ part, float *__restrict__ y, long long total, int kslices)
+{
+    griddep_wait();
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        float v = part[i];
+        for (int z = 1; z < kslices; z++) v += part[(long long)z * total + i];
+        y[i] = v;
+    }
+}
+
+constexpr int MAX_SPLIT_CTAS = 160;  // CTAs of a K-split launch at most (bounds the partials)
+constexpr size_t PART_BYTES = (size_t)MAX_SPLIT_CTAS * BM * BN * 4;
 
 template <bool F16>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -204,7 +220,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const Smem s = carve(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = blockIdx.x * BM, tok0 = blockIdx.y * BN;
-    const int KS = a.cols / BK;  // stages
+    const int KS = a.cols / BK / a.kslices;  // stages of this CTA's K slice
+    const int ks0 = (int)blockIdx.z * KS;     // its first stage (a multiple of 4: whole blocks)
     if (threadIdx.x == 0) {
         for (int i = 0; i < NST; i++) {
             tcmv::mbar_init(&s.x_full[i], 1);
@@ -244,7 +261,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         break;
                     }
                     tcmv::mbar_expect_tx_arrive(&s.raw_full[rs], (unsigned)RAW_BYTES);
-                    tcmv::tma_load_2d(s.raw[rs], &wmap, rk * (RAW_ROWB / 8), row0, &s.raw_full[rs], pol);
+                    tcmv::tma_load_2d(s.raw[rs], &wmap, (rk + ks0 / 4) * (RAW_ROWB / 8), row0, &s.raw_full[rs], pol);
                 }
                 if (ks >= NST && !tcmv::mbar_wait(&s.st_empty[st], ((ks / NST) - 1) & 1, WAIT)) {
                     failed = true;
@@ -254,7 +271,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 asm volatile(
                     "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
                     "{%2, %3}], [%4];" ::"r"(tcmv::smem_u32(s.x[st])),
-                    "l"(&xmap), "r"(ks * BK), "r"(tok0), "r"(tcmv::smem_u32(&s.x_full[st]))
+                    "l"(&xmap), "r"((ks0 + ks) * BK), "r"(tok0), "r"(tcmv::smem_u32(&s.x_full[st]))
                     : "memory");
             }
             if (failed) set_dev_error(0x71u);
@@ -302,6 +319,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (tcmv::mbar_wait(s.acc_full, 0, WAIT)) {
             fence_after_sync();
             const int q = warp & 3, row = row0 + 32 * q + lane;
+            float *dst = a.kslices > 1 ? a.part + (size_t)blockIdx.z * a.n * a.rows : a.y;
             const int c0 = ((warp - 2) / 4) * (BN * 4 / NDQ);  // warps of one lane quadrant split the columns
             for (int c = c0; c < c0 + BN * 4 / NDQ; c += 32) {
                 float v[32];
@@ -310,7 +328,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
                         const int tok = tok0 + c + i;
-                        if (tok < a.n) a.y[(size_t)tok * a.rows + row] = v[i];
+                        if (tok < a.n) dst[(size_t)tok * a.rows + row] = v[i];
                     }
                 }
             }
@@ -402,17 +420,35 @@ int matmul(const void *w, size_t rows, size_t cols, size_t n, const float *x, fl
         std::lock_guard<std::mutex> lk(mu);
         if ((rc = tcmv::ensure_smem(pf_gemm_q4k_kernel<F16>, smem_bytes(), smem_rec))) return rc;
     }
-    Args a{(int)rows, (int)cols, (int)n, y};
-    c.gridDim = dim3((unsigned)((rows + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
+    // too few output tiles to fill the GPU: split K into slices of whole blocks (each CTA one
+    // slice of one tile, partial sums reduced in slice order by a second launch)
+    const int tiles = (int)(((rows + BM - 1) / BM) * ((n + BN - 1) / BN)), nblk = (int)(cols / 256);
+    const int sms = num_sms_cached() < MAX_SPLIT_CTAS ? num_sms_cached() : MAX_SPLIT_CTAS;
+    int ksl = 1;
+    // (not for K of one or two blocks: there the extra reduction launch costs more than it saves)
+    while (nblk >= 4 && 2 * ksl <= nblk && nblk % (2 * ksl) == 0 && tiles * 2 * ksl <= sms) ksl *= 2;
+    float *part = reinterpret_cast<float *>(reinterpret_cast<char *>(ws) + ((n * cols * 2 + 255) & ~(size_t)255));
+    Args a{(int)rows, (int)cols, (int)n, y, ksl, part};
+    c.gridDim = dim3((unsigned)((rows + BM - 1) / BM), (unsigned)((n + BN - 1) / BN), (unsigned)ksl);
     c.blockDim = dim3(THREADS);
     c.dynamicSmemBytes = smem_bytes();
     c.numAttrs = 1;  // X comes from the conversion just launched
-    return cudaLaunchKernelEx(&c, pf_gemm_q4k_kernel<F16>, wm, xm, a) == cudaSuccess ? 0 : -4;
+    if (cudaLaunchKernelEx(&c, pf_gemm_q4k_kernel<F16>, wm, xm, a) != cudaSuccess) return -4;
+    if (ksl == 1) return 0;
+    const long long total = (long long)n * (long long)rows;
+    c.gridDim = dim3((unsigned)(((total + 255) / 256) < 1184 ? (total + 255) / 256 : 1184));
+    c.blockDim = dim3(256);
+    c.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&c, pf_reduce_kernel, (const float *)part, y, total, ksl) == cudaSuccess ? 0 : -4;
 }
 }  // namespace pf
 }  // namespace sb
 
-extern "C" size_t sbk_matmul_ws_bytes(size_t n, size_t cols) { return n * cols * 2 + 256; }
+extern "C" size_t sbk_matmul_ws_bytes(size_t n, size_t cols)
+{
+    // X as 16-bit operands, then the partial sums of a K-split launch (bounded by its CTAs)
+    return ((n * cols * 2 + 255) & ~(size_t)255) + sb::pf::PART_BYTES + 256;
+}
 
 extern "C" int sbk_matmul(uint8_t dtype, const void *w, size_t rows, size_t cols, size_t n, const float *x, float *y,
                           void *ws, int prec, int pdl, void *stream)
