@@ -696,6 +696,20 @@ def run_decode_case(tokens: int) -> None:
     print(json.dumps({"case": "decode", "tokens": toks.tolist()}))
 
 
+def run_decode_mla_case(tokens: int) -> None:
+    """A 3-layer slice of configs[4] (MLA attention; a dense FFN, then two MoE layers) through
+    the whole-token engine: `tokens` greedy steps after a 64-token prompt -- for ncu captures
+    of the MLA kernels."""
+    import dataclasses
+
+    from soso_b200 import decode
+    cfg = dataclasses.replace(decode.DEEPSEEK_V2_LITE, n_layers=3)
+    sess = decode.DecodeSession(cfg, decode.synth_model(cfg, "ncu"))
+    toks = sess.greedy(np.arange(64, dtype=np.int32), 64 + tokens)
+    sess.close()
+    print(json.dumps({"case": "decode_mla", "tokens": toks[-4:].tolist()}))
+
+
 def run_case(name: str, launches: int) -> None:
     """Plain launches of one kernel over a rotation of copies (for ncu); prints a check line."""
     import torch
@@ -733,7 +747,7 @@ def run_case(name: str, launches: int) -> None:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ncu-case", choices=sorted(NCU_CASES) + ["q4k_batch", "prefill", "decode"], default=None)
+    ap.add_argument("--ncu-case", choices=sorted(NCU_CASES) + ["q4k_batch", "prefill", "decode", "decode_mla"], default=None)
     ap.add_argument("--launches", type=int, default=12)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -748,6 +762,9 @@ def main():
         return
     if args.ncu_case == "prefill":
         run_prefill_case(args.launches)
+        return
+    if args.ncu_case == "decode_mla":
+        run_decode_mla_case(args.launches)
         return
     if args.ncu_case == "decode":
         run_decode_case(args.launches)

@@ -337,13 +337,13 @@ int sbk_argmax(const float *v, size_t n, int32_t *out, void *ws, int pdl, void *
 
 /* MLA decode in the absorbed form (mathematically the reference's re-expansion,
  * attention_decode_mla_latent, crates/soso-llm-core/src/attn.rs:306-404; the reference
- * has no GPU kernel for MLA).  sbk_mla_absorb, one CTA per head: appends this token's
+ * has no GPU kernel for MLA).  sbk_mla_absorb, kv_rank / 64 CTAs per head: appends this token's
  * latent row c (f16, the reference's rounding) at *pos, its rope keys
  * rope_pos(W_kr . c) per kv head, the roped q slice qr[heads][qk_rope] and the absorbed
  * query qt[heads][kv_rank] = W_kn^T q_nope (W_kn, W_kr = head's nope / rope rows of the
  * Q4_K k_up).  sbk_mla_attn: cbar[heads][kv_rank] = sum_t softmax_t(qt.c_t + qr.kr_t) c_t
  * / scaled by 1/sqrt(qk_nope+qk_rope); the output of a head is then W_v,h . cbar_h.
- * heads <= 16, kv_rank a multiple of 512 (<= 1024), qk_rope even (<= 128).  ws: at least
+ * heads <= 16, kv_rank a multiple of 512 (<= 1024), qk_nope <= 256, qk_rope even (<= 128).  ws: at least
  * sbk_mla_ws_bytes(heads, kv_rank), zero-filled before first use (left zeroed). */
 size_t sbk_mla_ws_bytes(size_t heads, size_t kv_rank);
 int sbk_mla_absorb(const float *q, const float *c, const void *k_up, uint8_t k_up_dtype, uint16_t *latent,

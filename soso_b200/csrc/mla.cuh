@@ -46,108 +46,171 @@ struct AbsorbArgs {
     float theta;
 };
 
-// CTA h: head h's absorbed query and roped q slice; for h < kv_heads also kv head h's
-// rope key at pos; CTA 0 appends the latent row.  The rows of k_up that head h needs are
-// staged in shared memory first.
-__global__ void __launch_bounds__(THREADS, 1) absorb_kernel(AbsorbArgs a)
+constexpr int AB_THREADS = 256;
+constexpr int AB_ROWS = 8;  // qk_nope rows per thread: qk_nope <= 32 * AB_ROWS
+
+// d * scale and dmin * min of sub-block j (0-7) of a Q4_K block whose first 16 bytes are
+// `hd` (d, dmin, 12 scale bytes): the 6-bit scale / min unpacking of get_scale_min_k4
+// (dequant.rs:150-248: w = (d * sc) * q - dmin * m).
+__device__ __forceinline__ void q4k_sub(const uint4 &hd, int j, float &ds, float &dm)
 {
-    extern __shared__ __align__(16) uint8_t sm[];
+    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffffu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+    const int sh = 8 * (j & 3);
+    const unsigned by = (hd.y >> sh) & 255u, bz = (hd.z >> sh) & 255u, bw = (hd.w >> sh) & 255u;
+    unsigned s_, m_;
+    if (j < 4) s_ = by & 63u, m_ = bz & 63u;
+    else s_ = (bw & 15u) | ((by >> 6) << 4), m_ = (bw >> 4) | ((bz >> 6) << 4);
+    ds = d * (float)s_;
+    dm = dmin * (float)m_;
+}
+
+// Grid (kv_rank / 64, heads): CTA (p, h) forms qt_h over latent columns 64p .. 64p + 63 --
+// the two sub-blocks (2 * pair, 2 * pair + 1) of Q4_K block p / 4 whose weights share the
+// 32 code bytes pair * 32 .. (low / high nibble) -- for every nope row, and for h < kv_heads
+// the rope keys of kv head h's rope rows RPC * p .. RPC * p + RPC - 1 (RPC even, so each
+// rotated pair stays in one CTA).  CTAs (p, 0) append latent columns 64p .. ; CTA (0, h)
+// ropes head h's q slice.  The k_up codes do not depend on the previous kernel: every
+// thread loads its share into registers before the dependency wait.
+//
+// qt: thread (row r0 = tid / 8, code word w4 = tid % 8) holds rows r0, r0 + 32, .. and
+// code bytes 4 w4 .. 4 w4 + 3 (8 weights per row); its sums run over its rows in order,
+// then over the 4 row groups of a warp (shuffle tree) and the 8 warps (in warp order).
+__global__ void __launch_bounds__(AB_THREADS) absorb_kernel(AbsorbArgs a)
+{
+    __shared__ float red[AB_THREADS / 32][64];
+    __shared__ float kr[MAXRP];
     griddep_launch();  // the next kernel reads this one's output only after its own wait
-    griddep_wait();
-    const int h = blockIdx.x, tid = threadIdx.x, qk_per = a.qk_nope + a.qk_rope;
+    const int p = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int qk_per = a.qk_nope + a.qk_rope, kvh = h / (a.heads / a.kv_heads);
+    const int nbk = a.kv_rank / 256, rb = nbk * 144, np = nbk * 4;
+    const int b = p >> 2, pair = p & 3;
+    const uint8_t *W = a.k_up + (size_t)kvh * qk_per * rb;
+    const int w4 = tid & 7, r0 = tid >> 3;
+    uint4 hd[AB_ROWS];
+    uint32_t cw[AB_ROWS];
+#pragma unroll
+    for (int k = 0; k < AB_ROWS; k++) {
+        const int r = r0 + 32 * k;
+        if (r < a.qk_nope) {
+            const uint8_t *blk = W + (size_t)r * rb + b * 144;
+            hd[k] = __ldg(reinterpret_cast<const uint4 *>(blk));
+            cw[k] = __ldg(reinterpret_cast<const uint32_t *>(blk + 16 + pair * 32 + 4 * w4));
+        }
+    }
+    // rope rows: warp i takes row RPC * p + i (one row per warp covers RPC <= 8; more rows
+    // are loaded after the wait).  Lane chunk t8 = 8 code bytes 8 (t8 % 16) .. of block t8 / 16.
+    const int rpc = ((a.qk_rope + np - 1) / np + 1) & ~1, rlo = rpc * p, rhi = min(a.qk_rope, rlo + rpc);
+    const bool rope = h < a.kv_heads && rlo < rhi;
+    const uint8_t *WR = a.k_up + (size_t)h * qk_per * rb;  // kv head h's rows (rope keys)
+    uint4 rh[2];
+    uint2 rc[2];
+#define SB_ROPE_LOAD(i)                                                                     \
+    {                                                                                       \
+        const uint8_t *rw = WR + (size_t)(a.qk_nope + rlo + (i)) * rb;                      \
+        _Pragma("unroll") for (int j = 0; j < 2; j++) {                                     \
+            const int t8 = lane + 32 * j;                                                   \
+            if (t8 < nbk * 16) {                                                            \
+                const uint8_t *blk = rw + (t8 >> 4) * 144;                                  \
+                rh[j] = __ldg(reinterpret_cast<const uint4 *>(blk));                        \
+                rc[j] = __ldg(reinterpret_cast<const uint2 *>(blk + 16 + 8 * (t8 & 15)));   \
+            }                                                                               \
+        }                                                                                   \
+    }
+    if (rope && warp < rhi - rlo) SB_ROPE_LOAD(warp)
+    griddep_wait();  // q (q_up) and c (kv_down) come from the previous kernels
     const int pos = *a.pos;
     if (pos < 0 || pos >= a.ctx) {
-        if (h == 0 && tid == 0) set_dev_error(0x81u);
+        if (p == 0 && h == 0 && tid == 0) set_dev_error(0x81u);
         return;
     }
-    const int group = a.heads / a.kv_heads, kvh = h / group;
-    const int nbk = a.kv_rank / 256, rb = nbk * 144;  // Q4_K blocks / bytes per k_up row
-    const int nsb = nbk * 8;                          // sub-blocks per row
-    uint8_t *rows = sm;                                           // [qk_per][rb]
-    float *ds = reinterpret_cast<float *>(sm + (size_t)qk_per * rb);  // [qk_per][nsb]: d * scale
-    float *dm = ds + (size_t)qk_per * nsb;                            // [qk_per][nsb]: dmin * min
-    float *cf = dm + (size_t)qk_per * nsb;                            // [kv_rank]
-    float *qs = cf + a.kv_rank;                                       // [qk_per]
-    // stage head kvh's rows of k_up (contiguous: qk_per rows)
-    const uint4 *src = reinterpret_cast<const uint4 *>(a.k_up + (size_t)kvh * qk_per * rb);
-    for (int i = tid; i < qk_per * rb / 16; i += THREADS) reinterpret_cast<uint4 *>(rows)[i] = src[i];
-    // the latent row as the cache holds it (f16, the reference's rounding)
-    for (int j = tid; j < a.kv_rank; j += THREADS) {
-        const uint16_t hb = f32_to_f16_ref(a.c[j]);
-        cf[j] = f16_to_f32(hb);
-        if (h == 0) a.latent[(size_t)pos * a.kv_rank + j] = hb;
-    }
-    for (int i = tid; i < qk_per; i += THREADS) qs[i] = a.q[(size_t)h * qk_per + i];
-    __syncthreads();
-    // per (row, sub-block): d * scale and dmin * min, the two products of every weight of the
-    // sub-block (dequant.rs:150-248: w = (d * sc) * q - dmin * m)
-    for (int idx = tid; idx < qk_per * nsb; idx += THREADS) {
-        const int i = idx / nsb, sbi = idx - i * nsb, j = sbi & 7;
-        const uint8_t *blk = rows + (size_t)i * rb + (sbi >> 3) * 144;
-        const float d = __half2float(*reinterpret_cast<const __half *>(blk));
-        const float dmin = __half2float(*reinterpret_cast<const __half *>(blk + 2));
-        const uint8_t *sc = blk + 4;
-        unsigned s_, m_;
-        if (j < 4) s_ = sc[j] & 63, m_ = sc[j + 4] & 63;
-        else s_ = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4), m_ = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
-        ds[idx] = d * (float)s_;
-        dm[idx] = dmin * (float)m_;
-    }
-    __syncthreads();
-    // roped q slice (pairs 2i, 2i+1)
-    for (int i = tid; i < a.qk_rope / 2; i += THREADS) {
-        const float freq = powf(a.theta, -2.0f * (float)i / (float)a.qk_rope);
-        const float ang = (float)pos * freq, sn = sinf(ang), cs = cosf(ang);
-        const float x0 = qs[a.qk_nope + 2 * i], x1 = qs[a.qk_nope + 2 * i + 1];
-        a.qr[(size_t)h * a.qk_rope + 2 * i] = x0 * cs - x1 * sn;
-        a.qr[(size_t)h * a.qk_rope + 2 * i + 1] = x0 * sn + x1 * cs;
-    }
-    // absorbed query: qt[j] = sum_i W_kn[i][j] * q_nope[i], i in row order.  Thread t takes
-    // code byte t of the row (block t / 128): its two weights, elements e and e + 32 of the
-    // block, share the byte (low / high nibble, sub-blocks 2p and 2p + 1).
-    for (int t = tid; t < nbk * 128; t += THREADS) {
-        const int b = t >> 7, bi = t & 127, pair = bi >> 5, l = bi & 31;
-        const int s0 = b * 8 + 2 * pair, j0 = b * 256 + pair * 64 + l;
-        const uint8_t *qp = rows + b * 144 + 16 + bi;
-        float acc0 = 0.0f, acc1 = 0.0f;
-#pragma unroll 8
-        for (int i = 0; i < a.qk_nope; i++) {
-            const float q0 = (float)(qp[(size_t)i * rb] & 15), q1 = (float)(qp[(size_t)i * rb] >> 4);
-            const float *dsi = ds + (size_t)i * nsb, *dmi = dm + (size_t)i * nsb;
-            acc0 += (dsi[s0] * q0 - dmi[s0]) * qs[i];
-            acc1 += (dsi[s0 + 1] * q1 - dmi[s0 + 1]) * qs[i];
+    if (h == 0 && tid < 64) a.latent[(size_t)pos * a.kv_rank + 64 * p + tid] = f32_to_f16_ref(a.c[64 * p + tid]);
+    if (p == 0) {  // roped q slice (pairs 2i, 2i + 1)
+        for (int i = tid; i < a.qk_rope / 2; i += AB_THREADS) {
+            const float freq = powf(a.theta, -2.0f * (float)i / (float)a.qk_rope);
+            const float ang = (float)pos * freq, sn = sinf(ang), cs = cosf(ang);
+            const float x0 = a.q[(size_t)h * qk_per + a.qk_nope + 2 * i];
+            const float x1 = a.q[(size_t)h * qk_per + a.qk_nope + 2 * i + 1];
+            a.qr[(size_t)h * a.qk_rope + 2 * i] = x0 * cs - x1 * sn;
+            a.qr[(size_t)h * a.qk_rope + 2 * i + 1] = x0 * sn + x1 * cs;
         }
-        a.qt[(size_t)h * a.kv_rank + j0] = acc0;
-        a.qt[(size_t)h * a.kv_rank + j0 + 32] = acc1;
     }
-    if (h >= a.kv_heads) return;
-    // rope key of kv head h at pos: rows qk_nope.. of its k_up rows times the latent row,
-    // one warp per row (lanes over the code bytes, fixed order), then the rotation
-    __shared__ float kr[MAXRP];
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int i = warp; i < a.qk_rope; i += THREADS / 32) {
-        const int row = a.qk_nope + i;
-        const uint8_t *rw = rows + (size_t)row * rb;
-        const float *dsi = ds + (size_t)row * nsb, *dmi = dm + (size_t)row * nsb;
-        float acc = 0.0f;
-        for (int t = lane; t < nbk * 128; t += 32) {
-            const int b = t >> 7, bi = t & 127, pair = bi >> 5, l = bi & 31;
-            const int s0 = b * 8 + 2 * pair, j0 = b * 256 + pair * 64 + l;
-            const uint8_t qb = rw[b * 144 + 16 + bi];
-            acc += (dsi[s0] * (float)(qb & 15) - dmi[s0]) * cf[j0];
-            acc += (dsi[s0 + 1] * (float)(qb >> 4) - dmi[s0 + 1]) * cf[j0 + 32];
+    // absorbed query: qt[j] = sum_i W_kn[i][j] * q_nope[i]
+    float lo[4] = {0.0f, 0.0f, 0.0f, 0.0f}, hi[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int k = 0; k < AB_ROWS; k++) {
+        const int r = r0 + 32 * k;
+        if (r < a.qk_nope) {
+            const float qv = __ldcg(a.q + (size_t)h * qk_per + r);
+            float ds0, dm0, ds1, dm1;
+            q4k_sub(hd[k], 2 * pair, ds0, dm0);
+            q4k_sub(hd[k], 2 * pair + 1, ds1, dm1);
+#pragma unroll
+            for (int n = 0; n < 4; n++) {
+                const unsigned byte = (cw[k] >> (8 * n)) & 255u;
+                lo[n] += (ds0 * (float)(byte & 15u) - dm0) * qv;
+                hi[n] += (ds1 * (float)(byte >> 4) - dm1) * qv;
+            }
         }
-        acc = warp_sum(acc);
-        if (lane == 0) kr[i] = acc;
     }
+#pragma unroll
+    for (int n = 0; n < 4; n++) {
+#pragma unroll
+        for (int o = 8; o <= 16; o <<= 1) {
+            lo[n] += __shfl_xor_sync(0xffffffffu, lo[n], o);
+            hi[n] += __shfl_xor_sync(0xffffffffu, hi[n], o);
+        }
+    }
+    if (lane < 8) {
+#pragma unroll
+        for (int n = 0; n < 4; n++) red[warp][4 * w4 + n] = lo[n], red[warp][32 + 4 * w4 + n] = hi[n];
+    }
+    // rope keys of kv head h: rows of W_kr times the latent row as the cache holds it (f16)
+    if (rope) {
+        for (int i = warp; i < rhi - rlo; i += AB_THREADS / 32) {
+            if (i >= AB_THREADS / 32) SB_ROPE_LOAD(i)
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int t8 = lane + 32 * j;
+                if (t8 < nbk * 16) {
+                    const int c8 = t8 & 15, pr = c8 >> 2;
+                    const int col = (t8 >> 4) * 256 + pr * 64 + 8 * (c8 & 3);
+                    float ds0, dm0, ds1, dm1;
+                    q4k_sub(rh[j], 2 * pr, ds0, dm0);
+                    q4k_sub(rh[j], 2 * pr + 1, ds1, dm1);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        const unsigned byte = ((e < 4 ? rc[j].x : rc[j].y) >> (8 * (e & 3))) & 255u;
+                        const float c0 = f16_to_f32(f32_to_f16_ref(__ldcg(a.c + col + e)));
+                        const float c1 = f16_to_f32(f32_to_f16_ref(__ldcg(a.c + col + 32 + e)));
+                        acc += (ds0 * (float)(byte & 15u) - dm0) * c0;
+                        acc += (ds1 * (float)(byte >> 4) - dm1) * c1;
+                    }
+                }
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) kr[i] = acc;
+        }
+    }
+#undef SB_ROPE_LOAD
     __syncthreads();
-    for (int i = tid; i < a.qk_rope / 2; i += THREADS) {
-        const float freq = powf(a.theta, -2.0f * (float)i / (float)a.qk_rope);
-        const float ang = (float)pos * freq, sn = sinf(ang), cs = cosf(ang);
-        const float x0 = kr[2 * i], x1 = kr[2 * i + 1];
-        float *dst = a.krope + ((size_t)pos * a.kv_heads + h) * a.qk_rope;
-        dst[2 * i] = x0 * cs - x1 * sn;
-        dst[2 * i + 1] = x0 * sn + x1 * cs;
+    if (tid < 64) {
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < AB_THREADS / 32; w++) v += red[w][tid];
+        a.qt[(size_t)h * a.kv_rank + b * 256 + pair * 64 + tid] = v;
+    }
+    if (rope) {
+        for (int i = tid; i < (rhi - rlo) / 2; i += AB_THREADS) {
+            const int g = rlo / 2 + i;  // pair index within the rope slice
+            const float freq = powf(a.theta, -2.0f * (float)g / (float)a.qk_rope);
+            const float ang = (float)pos * freq, sn = sinf(ang), cs = cosf(ang);
+            const float x0 = kr[2 * i], x1 = kr[2 * i + 1];
+            float *dst = a.krope + ((size_t)pos * a.kv_heads + h) * a.qk_rope + 2 * g;
+            dst[0] = x0 * cs - x1 * sn;
+            dst[1] = x0 * sn + x1 * cs;
+        }
     }
 }
 
@@ -353,6 +416,7 @@ constexpr int TC_T = 32;  // positions per sub-chunk
 
 struct TcArgs {
     CUtensorMap lmap;  // latent [ctx][512] u16, box 32 rows x 64 dims, 128-byte swizzle
+    const uint16_t *latent;  // the same rows (row pos is read again after the dependency wait)
     const float *qt;   // [heads][512]
     const float *qr;   // [heads][qk_rope]
     const float *krope;
@@ -371,9 +435,19 @@ struct TcSmem {
     float sr[MAXH][TC_T];     // rope term
     float racc[ATT_SPANS][MAXH * TC_R / ATT_SPANS];
     float rm[ATT_SPANS][MAXH], rl[ATT_SPANS][MAXH];
+    float mw[ATT_SPANS][MAXH], minv[MAXH];  // merge: weight of span cc for head j, 1 / sum
     float m[MAXH], l[MAXH], f[MAXH];
     uint64_t bar[2];
 };
+
+constexpr int TC_KR4 = 16;  // rope-key float4s per row held in registers (all of qk_rope <= 64)
+
+__device__ __forceinline__ void cluster_st_f32x2(const void *p, int rank, float v0, float v1)
+{
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(tcmv::smem_u32(p)), "r"(rank));
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(ra), "f"(v0), "f"(v1) : "memory");
+}
 
 // Address of dims d0..d0+7 (d0 a multiple of 8) of sub-chunk row `row`.
 __device__ __forceinline__ const uint8_t *tc_at(const uint8_t (*buf)[TC_T * 128], int row, int d0)
@@ -388,6 +462,12 @@ __device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void *p)
                  : "r"(tcmv::smem_u32(p)));
 }
 
+// Everything that does not come from the previous kernel is requested before the dependency
+// wait: the latent sub-chunks (TMA) and the first sub-chunk's rope keys (registers) -- rows
+// before pos were appended by earlier tokens, which completed before this token's kernels
+// started.  Row pos itself is appended by the previous kernel: the CTA holding it loads the
+// row again after the wait and writes it over what the prefetch saw (latent tile in shared
+// memory, rope-key registers).
 __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_constant__ TcArgs a)
 {
     extern __shared__ __align__(1024) uint8_t tc_raw[];
@@ -421,22 +501,68 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_consta
         tcmv::mbar_expect_tx_arrive(&s.bar[b], (unsigned)(TC_R / 64) * TC_T * 128);
         for (int q = 0; q < TC_R / 64; q++) tma_tile_2d(s.lb[b][q], &a.lmap, 64 * q, t0, &s.bar[b]);
     };
-    if (tid == 0 && !late) {
+    if (tid == 0) {
         if (nsub > 0) issue(0);
         if (nsub > 1) issue(1);
     }
-    griddep_wait();  // qt, qr, this token's latent row and rope key come from the previous kernel
-    if (tid == 0 && late) {
-        if (nsub > 0) issue(0);
-        if (nsub > 1) issue(1);
+    // rope keys: thread -> head rh, positions rt and rt + 16 of a sub-chunk; kreg holds the
+    // first TC_KR4 float4s of each of the two rows (L2 loads: row pos is reloaded below)
+    const int rh = tid >> 4, rt = tid & 15;
+    float4 kreg[2][TC_KR4];
+#define SB_KR_LOAD(T0, TN)                                                                          \
+    _Pragma("unroll") for (int k = 0; k < 2; k++) {                                                 \
+        if (rh < H && rt + 16 * k < (TN)) {                                                         \
+            const float4 *kp = reinterpret_cast<const float4 *>(                                   \
+                a.krope + ((size_t)((T0) + rt + 16 * k) * a.kv_heads + rh / group) * RP);          \
+            _Pragma("unroll") for (int j = 0; j < TC_KR4; j++) if (4 * j < RP) kreg[k][j] = __ldcg(kp + j); \
+        }                                                                                           \
+    }
+    if (nsub > 0) SB_KR_LOAD(tb, min(TC_T, te - tb))
+    griddep_wait();  // qt, qr, this token's latent row and rope keys come from the previous kernel
+    uint4 prow = make_uint4(0u, 0u, 0u, 0u);
+    if (active && late) {
+        if (tid < TC_R / 8) prow = __ldcg(reinterpret_cast<const uint4 *>(a.latent + (size_t)pos * TC_R) + tid);
+        const int tp = pos - tb;  // the prefetched rope row of position pos, if sub-chunk 0 holds it
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            if (rh < H && tp == rt + 16 * k) {
+                const float4 *kp =
+                    reinterpret_cast<const float4 *>(a.krope + ((size_t)pos * a.kv_heads + rh / group) * RP);
+#pragma unroll
+                for (int j = 0; j < TC_KR4; j++)
+                    if (4 * j < RP) kreg[k][j] = __ldcg(kp + j);
+            }
+        }
     }
     int issued = nsub < 2 ? nsub : 2;
     if (active) {
-        for (int i = tid; i < H * TC_R; i += THREADS) {
-            const int h = i / TC_R, d = i - h * TC_R;
-            split_f16(a.qt[i], s.qh[h][d], s.ql[h][d]);
+        float4 qv[(MAXH * TC_R / 4 + THREADS - 1) / THREADS], rv[(MAXH * MAXRP / 4 + THREADS - 1) / THREADS];
+        const float4 *q4 = reinterpret_cast<const float4 *>(a.qt), *r4 = reinterpret_cast<const float4 *>(a.qr);
+#pragma unroll
+        for (int k = 0; k < (MAXH * TC_R / 4 + THREADS - 1) / THREADS; k++)
+            if (tid + THREADS * k < H * TC_R / 4) qv[k] = __ldcg(q4 + tid + THREADS * k);
+#pragma unroll
+        for (int k = 0; k < (MAXH * MAXRP / 4 + THREADS - 1) / THREADS; k++)
+            if (tid + THREADS * k < H * RP / 4) rv[k] = __ldcg(r4 + tid + THREADS * k);
+#pragma unroll
+        for (int k = 0; k < (MAXH * TC_R / 4 + THREADS - 1) / THREADS; k++) {
+            const int i = tid + THREADS * k;
+            if (i < H * TC_R / 4) {
+                const int h = i / (TC_R / 4), d = 4 * (i % (TC_R / 4));
+                split_f16(qv[k].x, s.qh[h][d], s.ql[h][d]);
+                split_f16(qv[k].y, s.qh[h][d + 1], s.ql[h][d + 1]);
+                split_f16(qv[k].z, s.qh[h][d + 2], s.ql[h][d + 2]);
+                split_f16(qv[k].w, s.qh[h][d + 3], s.ql[h][d + 3]);
+            }
         }
-        for (int i = tid; i < H * RP; i += THREADS) s.qr[i / RP][i % RP] = a.qr[i];
+#pragma unroll
+        for (int k = 0; k < (MAXH * MAXRP / 4 + THREADS - 1) / THREADS; k++) {
+            const int i = tid + THREADS * k;
+            if (i < H * RP / 4) {
+                const int h = (4 * i) / RP, d = (4 * i) % RP;
+                s.qr[h][d] = rv[k].x, s.qr[h][d + 1] = rv[k].y, s.qr[h][d + 2] = rv[k].z, s.qr[h][d + 3] = rv[k].w;
+            }
+        }
     }
     __syncthreads();
     float acc[8][4];
@@ -447,27 +573,32 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_consta
     int done = 0;
     for (int i = 0; i < nsub; i++) {
         const int t0 = tb + i * TC_T, tn = min(TC_T, te - t0), b = i & 1;
-        // rope term (the keys stay in global memory): thread -> head tid / 16, positions tid % 16 (+ 16)
-        {
-            const int h = tid >> 4, tt = tid & 15;
-            if (h < H) {
-                const float *q = s.qr[h];
+        // rope term from the registers (f32 keys): s.sr[head][position]
+        if (rh < H) {
+            const float *q = s.qr[rh];
 #pragma unroll
-                for (int k = 0; k < 2; k++) {
-                    const int t = tt + 16 * k;
-                    float r = 0.0f;
-                    if (t < tn) {
-                        const float4 *kp =
-                            reinterpret_cast<const float4 *>(a.krope + ((size_t)(t0 + t) * a.kv_heads + h / group) * RP);
-                        for (int j = 0; j < RP / 4; j++) {
-                            const float4 kv = __ldcg(kp + j);
+            for (int k = 0; k < 2; k++) {
+                const int t = rt + 16 * k;
+                float r = 0.0f;
+                if (t < tn) {
+#pragma unroll
+                    for (int j = 0; j < TC_KR4; j++)
+                        if (4 * j < RP) {
+                            const float4 kv = kreg[k][j];
                             r += q[4 * j] * kv.x + q[4 * j + 1] * kv.y + q[4 * j + 2] * kv.z + q[4 * j + 3] * kv.w;
                         }
+                    const float4 *kp =
+                        reinterpret_cast<const float4 *>(a.krope + ((size_t)(t0 + t) * a.kv_heads + rh / group) * RP);
+                    for (int j = TC_KR4; 4 * j < RP; j++) {
+                        const float4 kv = __ldcg(kp + j);
+                        r += q[4 * j] * kv.x + q[4 * j + 1] * kv.y + q[4 * j + 2] * kv.z + q[4 * j + 3] * kv.w;
                     }
-                    s.sr[h][t] = r;
                 }
+                s.sr[rh][t] = r;
             }
         }
+        // the next sub-chunk's keys: in flight during this one's tensor-core work
+        if (i + 1 < nsub) SB_KR_LOAD(t0 + TC_T, min(TC_T, te - t0 - TC_T))
         if (!tcmv::mbar_wait(&s.bar[b], (unsigned)(i >> 1) & 1u)) failed = true;
         if (__syncthreads_or(failed)) {
             failed = true;
@@ -479,6 +610,9 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_consta
             const int r = tn + idx / (TC_R / 2), w = idx % (TC_R / 2);
             reinterpret_cast<uint32_t *>(s.lb[b][w >> 5] + r * 128)[w & 31] = 0u;
         }
+        // row pos as the previous kernel wrote it (dims 8 tid .. 8 tid + 7)
+        if (late && tid < TC_R / 8 && pos >= t0 && pos < t0 + tn)
+            *reinterpret_cast<uint4 *>(s.lb[b][tid >> 3] + att_swz(pos - t0, tid & 7)) = prow;
         __syncthreads();
         // main term: warp w takes positions 8(w & 3) .. +8 and latent dims 256(w >> 2) .. +256
         {
@@ -549,6 +683,7 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_consta
         }
         if (i + 2 < nsub) issued = i + 3;
     }
+#undef SB_KR_LOAD
     if (failed) {
         if (tid == 0) {
             set_dev_error(0x83u);
@@ -578,11 +713,11 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_consta
 #pragma unroll
         for (int nt = 0; nt < 8; nt++)
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const int h = g8 + 8 * (k >> 1), d = warp * 64 + nt * 8 + 2 * t4 + (k & 1);
+            for (int hb = 0; hb < 2; hb++) {
+                const int h = g8 + 8 * hb, d = warp * 64 + nt * 8 + 2 * t4;
                 if (h >= H) continue;
-                const int o = h * TC_R + d;
-                cluster_st_f32(&s.racc[c][o % per], o / per, acc[nt][k]);
+                const int o = h * TC_R + d;  // o, o + 1: the same CTA (per is even)
+                cluster_st_f32x2(&s.racc[c][o % per], o / per, acc[nt][2 * hb], acc[nt][2 * hb + 1]);
             }
         if (tid < ATT_SPANS * H) {
             const int r = tid / H, j = tid % H;
@@ -591,26 +726,28 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_consta
         }
     }
     cluster_sync();
-    for (int q = tid; q < per; q += THREADS) {
-        const int o = c * per + q, j = o / TC_R;
+    if (tid < H) {  // per head: the span weights exp(m_cc - M) and 1 / sum_cc weight * l_cc
+        const int j = tid;
         float M = -INFINITY;
         for (int cc = 0; cc < nch; cc++)
             if (s.rl[cc][j] > 0.0f) M = fmaxf(M, s.rm[cc][j]);
-        float L = 0.0f, O = 0.0f;
+        float L = 0.0f;
         for (int cc = 0; cc < nch; cc++) {
             const float lv = s.rl[cc][j], w = lv > 0.0f ? expf(s.rm[cc][j] - M) : 0.0f;
+            s.mw[cc][j] = w;
             L += w * lv;
-            O += w * s.racc[cc][q];
         }
-        a.cbar[o] = L > 0.0f ? O * (1.0f / L) : 0.0f;
+        s.minv[j] = L > 0.0f ? 1.0f / L : 0.0f;
+    }
+    __syncthreads();
+    for (int q = tid; q < per; q += THREADS) {
+        const int o = c * per + q, j = o / TC_R;
+        float O = 0.0f;
+        for (int cc = 0; cc < nch; cc++) O += s.mw[cc][j] * s.racc[cc][q];
+        a.cbar[o] = s.minv[j] > 0.0f ? O * s.minv[j] : 0.0f;
     }
 }
 
-inline size_t absorb_smem(int kv_rank, int qk_per)
-{
-    return (size_t)qk_per * (kv_rank / 256) * 144 + (size_t)2 * qk_per * (kv_rank / 256) * 8 * 4 + (kv_rank + qk_per) * 4 +
-           16;
-}
 inline size_t attn_smem(int heads, int kv_heads, int kv_rank, int qk_rope)
 {
     return ((size_t)heads * kv_rank + (size_t)heads * qk_rope + (size_t)CH * kv_heads * qk_rope) * 4 +
@@ -634,16 +771,13 @@ extern "C" int sbk_mla_absorb(const float *q, const float *c, const void *k_up, 
     if (!q || !c || !k_up || !latent || !krope || !qt || !qr || !pos) return -1;
     if (k_up_dtype != SB_DTYPE_Q4_K) return -5;
     if (!heads || !kv_heads || heads % kv_heads || heads > MAXH || kv_rank % 256 || kv_rank > MAXR || !qk_nope ||
-        !qk_rope || qk_rope % 2 || qk_rope > MAXRP || !ctx)
+        qk_nope > 32 * AB_ROWS || !qk_rope || qk_rope % 2 || qk_rope > MAXRP || !ctx)
         return -1;
     if (((uintptr_t)k_up) & 15) return -2;
-    const size_t smem = absorb_smem((int)kv_rank, (int)(qk_nope + qk_rope));
-    if (smem > 227 * 1024) return -1;
-    static size_t rec[64];
-    if (sb::tcmv::ensure_smem(absorb_kernel, smem, rec)) return -3;
     AbsorbArgs a{q, c, (const uint8_t *)k_up, latent, krope, qt, qr, pos, (int)heads, (int)kv_heads, (int)kv_rank,
                  (int)qk_nope, (int)qk_rope, (int)ctx, theta};
-    return sb::launch_k(absorb_kernel, dim3((unsigned)heads), dim3(THREADS), smem, pdl, (cudaStream_t)stream, a);
+    return sb::launch_k(absorb_kernel, dim3((unsigned)(kv_rank / 64), (unsigned)heads), dim3(AB_THREADS), 0, pdl,
+                        (cudaStream_t)stream, a);
 }
 
 extern "C" int sbk_mla_attn(const float *qt, const float *qr, const uint16_t *latent, const float *krope, float *cbar,
@@ -656,7 +790,7 @@ extern "C" int sbk_mla_attn(const float *qt, const float *qr, const uint16_t *la
         qk_rope > MAXRP || !ctx || ctx > (1u << 24))
         return -1;
     if (((uintptr_t)latent | (uintptr_t)ws) & 15) return -2;
-    if (kv_rank == TC_R && qk_rope % 4 == 0) {
+    if (kv_rank == TC_R && qk_rope % 4 == 0 && !(((uintptr_t)qt | (uintptr_t)qr | (uintptr_t)krope) & 15)) {
         // the tensor-core form: one cluster of ATT_SPANS CTAs (a non-portable cluster size)
         static size_t tc_rec[64];
         static std::mutex mu;
@@ -687,7 +821,7 @@ extern "C" int sbk_mla_attn(const float *qt, const float *qr, const uint16_t *la
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
                 return -7;
         }
-        t.qt = qt, t.qr = qr, t.krope = krope, t.cbar = cbar, t.pos = pos;
+        t.latent = latent, t.qt = qt, t.qr = qr, t.krope = krope, t.cbar = cbar, t.pos = pos;
         t.heads = (int)heads, t.kv_heads = (int)kv_heads, t.qk_rope = (int)qk_rope, t.ctx = (int)ctx;
         t.scale = 1.0f / sqrtf((float)(qk_nope + qk_rope));
         cudaLaunchConfig_t lc = {};
