@@ -80,6 +80,8 @@ __global__ void __launch_bounds__(AB_THREADS) absorb_kernel(AbsorbArgs a)
 {
     __shared__ float red[AB_THREADS / 32][64];
     __shared__ float kr[MAXRP];
+    __shared__ float cs[MAXR];            // the latent row as the cache holds it (f16 values)
+    __shared__ float qs[32 * AB_ROWS];    // q_nope of head h
     griddep_launch();  // the next kernel reads this one's output only after its own wait
     const int p = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int qk_per = a.qk_nope + a.qk_rope, kvh = h / (a.heads / a.kv_heads);
@@ -124,7 +126,13 @@ __global__ void __launch_bounds__(AB_THREADS) absorb_kernel(AbsorbArgs a)
         if (p == 0 && h == 0 && tid == 0) set_dev_error(0x81u);
         return;
     }
-    if (h == 0 && tid < 64) a.latent[(size_t)pos * a.kv_rank + 64 * p + tid] = f32_to_f16_ref(a.c[64 * p + tid]);
+    // one round of loads: the latent row (f16 rounding, the reference's) and q_nope
+    for (int j = tid; j < a.kv_rank; j += AB_THREADS) {
+        const uint16_t hb = f32_to_f16_ref(__ldcg(a.c + j));
+        cs[j] = f16_to_f32(hb);
+        if (h == 0 && (j >> 6) == p) a.latent[(size_t)pos * a.kv_rank + j] = hb;
+    }
+    for (int i = tid; i < a.qk_nope; i += AB_THREADS) qs[i] = __ldcg(a.q + (size_t)h * qk_per + i);
     if (p == 0) {  // roped q slice (pairs 2i, 2i + 1)
         for (int i = tid; i < a.qk_rope / 2; i += AB_THREADS) {
             const float freq = powf(a.theta, -2.0f * (float)i / (float)a.qk_rope);
@@ -135,13 +143,14 @@ __global__ void __launch_bounds__(AB_THREADS) absorb_kernel(AbsorbArgs a)
             a.qr[(size_t)h * a.qk_rope + 2 * i + 1] = x0 * sn + x1 * cs;
         }
     }
+    __syncthreads();
     // absorbed query: qt[j] = sum_i W_kn[i][j] * q_nope[i]
     float lo[4] = {0.0f, 0.0f, 0.0f, 0.0f}, hi[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int k = 0; k < AB_ROWS; k++) {
         const int r = r0 + 32 * k;
         if (r < a.qk_nope) {
-            const float qv = __ldcg(a.q + (size_t)h * qk_per + r);
+            const float qv = qs[r];
             float ds0, dm0, ds1, dm1;
             q4k_sub(hd[k], 2 * pair, ds0, dm0);
             q4k_sub(hd[k], 2 * pair + 1, ds1, dm1);
@@ -182,8 +191,7 @@ __global__ void __launch_bounds__(AB_THREADS) absorb_kernel(AbsorbArgs a)
 #pragma unroll
                     for (int e = 0; e < 8; e++) {
                         const unsigned byte = ((e < 4 ? rc[j].x : rc[j].y) >> (8 * (e & 3))) & 255u;
-                        const float c0 = f16_to_f32(f32_to_f16_ref(__ldcg(a.c + col + e)));
-                        const float c1 = f16_to_f32(f32_to_f16_ref(__ldcg(a.c + col + 32 + e)));
+                        const float c0 = cs[col + e], c1 = cs[col + 32 + e];
                         acc += (ds0 * (float)(byte & 15u) - dm0) * c0;
                         acc += (ds1 * (float)(byte >> 4) - dm1) * c1;
                     }
