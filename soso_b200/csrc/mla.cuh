@@ -450,11 +450,12 @@ struct TcSmem {
 
 constexpr int TC_KR4 = 16;  // rope-key float4s per row held in registers (all of qk_rope <= 64)
 
-__device__ __forceinline__ void cluster_st_f32x2(const void *p, int rank, float v0, float v1)
+__device__ __forceinline__ void cluster_st_f32x4(const void *p, int rank, float4 v)
 {
     uint32_t ra;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(tcmv::smem_u32(p)), "r"(rank));
-    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(ra), "f"(v0), "f"(v1) : "memory");
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(ra), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
 }
 
 // Address of dims d0..d0+7 (d0 a multiple of 8) of sub-chunk row `row`.
@@ -714,19 +715,30 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_consta
         }
         return;
     }
-    // merge the spans (combinar_trozos): CTA r forms outputs r*per .. (o = head * 512 + dim)
+    // merge the spans (combinar_trozos): CTA r forms outputs r*per .. (o = head * 512 + dim).
+    // The partial sums go through latent buffer 0 (free after the loop) first, so that each
+    // warp's push is 512 contiguous bytes into one CTA (a fragment spans 8 heads: 8 CTAs).
     const int per = H * TC_R / ATT_SPANS;
-    cluster_wait();
+    float *stage = reinterpret_cast<float *>(&s.lb[0][0][0]);
+    static_assert(sizeof(s.lb[0]) >= MAXH * TC_R * 4, "partial sums fit one latent buffer");
     if (active) {
 #pragma unroll
         for (int nt = 0; nt < 8; nt++)
 #pragma unroll
             for (int hb = 0; hb < 2; hb++) {
                 const int h = g8 + 8 * hb, d = warp * 64 + nt * 8 + 2 * t4;
-                if (h >= H) continue;
-                const int o = h * TC_R + d;  // o, o + 1: the same CTA (per is even)
-                cluster_st_f32x2(&s.racc[c][o % per], o / per, acc[nt][2 * hb], acc[nt][2 * hb + 1]);
+                if (h < H)
+                    *reinterpret_cast<float2 *>(stage + h * TC_R + d) = make_float2(acc[nt][2 * hb], acc[nt][2 * hb + 1]);
             }
+    }
+    __syncthreads();
+    cluster_wait();
+    if (active) {
+        const int per4 = per / 4;
+        for (int f = tid; f < H * TC_R / 4; f += THREADS) {
+            const int r = f / per4, q = f - r * per4;
+            cluster_st_f32x4(&s.racc[c][4 * q], r, *reinterpret_cast<const float4 *>(stage + 4 * f));
+        }
         if (tid < ATT_SPANS * H) {
             const int r = tid / H, j = tid % H;
             cluster_st_f32(&s.rm[c][j], r, s.m[j]);
