@@ -746,18 +746,23 @@ __global__ void __launch_bounds__(THREADS, 1) attn_tc_kernel(const __grid_consta
         }
     }
     cluster_sync();
-    if (tid < H) {  // per head: the span weights exp(m_cc - M) and 1 / sum_cc weight * l_cc
-        const int j = tid;
-        float M = -INFINITY;
-        for (int cc = 0; cc < nch; cc++)
-            if (s.rl[cc][j] > 0.0f) M = fmaxf(M, s.rm[cc][j]);
-        float L = 0.0f;
-        for (int cc = 0; cc < nch; cc++) {
-            const float lv = s.rl[cc][j], w = lv > 0.0f ? expf(s.rm[cc][j] - M) : 0.0f;
+    {  // thread (head j, span cc): the span weight exp(m_cc - M) and 1 / sum_cc weight * l_cc,
+       // max and sum over the 16 spans of a half-warp by shuffles
+        static_assert(MAXH * ATT_SPANS == THREADS, "one thread per (head, span)");
+        const int j = tid >> 4, cc = tid & 15;
+        const bool ok = j < H && cc < nch && s.rl[cc][j] > 0.0f;
+        const float lv = ok ? s.rl[cc][j] : 0.0f, mv = ok ? s.rm[cc][j] : -INFINITY;
+        float M = mv;
+#pragma unroll
+        for (int o = 8; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float w = ok ? expf(mv - M) : 0.0f;
+        float L = w * lv;
+#pragma unroll
+        for (int o = 8; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (j < H) {
             s.mw[cc][j] = w;
-            L += w * lv;
+            if (cc == 0) s.minv[j] = L > 0.0f ? 1.0f / L : 0.0f;
         }
-        s.minv[j] = L > 0.0f ? 1.0f / L : 0.0f;
     }
     __syncthreads();
     for (int q = tid; q < per; q += THREADS) {
