@@ -896,7 +896,7 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             L.mla = true, L.q_rank = ml.q_rank, L.kv_rank = ml.kv_rank, L.qk_nope = ml.qk_nope;
             L.qk_rope = ml.qk_rope, L.v_dim = ml.v_dim;
             if (!L.heads || !L.kvh || L.heads % L.kvh || L.heads > (size_t)sb::mla::MAXH || L.kv_rank % 512 ||
-                L.kv_rank > (size_t)sb::mla::MAXR || !L.qk_nope || L.qk_nope > 32 * (size_t)sb::mla::AB_ROWS ||
+                L.kv_rank > (size_t)sb::mla::MAXR || !L.qk_nope || L.qk_nope > (size_t)sb::mla::AB_RG * sb::mla::AB_ROWS ||
                 !L.qk_rope || L.qk_rope % 2 ||
                 L.qk_rope > (size_t)sb::mla::MAXRP || !L.v_dim || !L.q_rank)
                 return bail(0);

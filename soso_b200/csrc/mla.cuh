@@ -46,8 +46,10 @@ struct AbsorbArgs {
     float theta;
 };
 
-constexpr int AB_THREADS = 256;
-constexpr int AB_ROWS = 8;  // qk_nope rows per thread: qk_nope <= 32 * AB_ROWS
+constexpr int AB_THREADS = 512;
+constexpr int AB_WARPS = AB_THREADS / 32;
+constexpr int AB_RG = AB_THREADS / 8;  // row groups (8 threads a row)
+constexpr int AB_ROWS = 4;             // qk_nope rows per thread: qk_nope <= AB_RG * AB_ROWS
 
 // d * scale and dmin * min of sub-block j (0-7) of a Q4_K block whose first 16 bytes are
 // `hd` (d, dmin, 12 scale bytes): the 6-bit scale / min unpacking of get_scale_min_k4
@@ -73,15 +75,16 @@ __device__ __forceinline__ void q4k_sub(const uint4 &hd, int j, float &ds, float
 // ropes head h's q slice.  The k_up codes do not depend on the previous kernel: every
 // thread loads its share into registers before the dependency wait.
 //
-// qt: thread (row r0 = tid / 8, code word w4 = tid % 8) holds rows r0, r0 + 32, .. and
+// qt: thread (row r0 = tid / 8, code word w4 = tid % 8) holds rows r0, r0 + 64, .. and
 // code bytes 4 w4 .. 4 w4 + 3 (8 weights per row); its sums run over its rows in order,
-// then over the 4 row groups of a warp (shuffle tree) and the 8 warps (in warp order).
+// then over the 4 row groups of a warp (shuffle tree) and the 16 warps (in warp order).
+// Rope row i of the CTA: warps i % 8 and i % 8 + 8 take the two halves of its code bytes.
 __global__ void __launch_bounds__(AB_THREADS) absorb_kernel(AbsorbArgs a)
 {
-    __shared__ float red[AB_THREADS / 32][64];
-    __shared__ float kr[MAXRP];
-    __shared__ float cs[MAXR];            // the latent row as the cache holds it (f16 values)
-    __shared__ float qs[32 * AB_ROWS];    // q_nope of head h
+    __shared__ float red[AB_WARPS][64];
+    __shared__ float krp[2][MAXRP];
+    __shared__ float cs[MAXR];         // the latent row as the cache holds it (f16 values)
+    __shared__ float qs[AB_RG * AB_ROWS];  // q_nope of head h
     griddep_launch();  // the next kernel reads this one's output only after its own wait
     const int p = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int qk_per = a.qk_nope + a.qk_rope, kvh = h / (a.heads / a.kv_heads);
@@ -93,62 +96,69 @@ __global__ void __launch_bounds__(AB_THREADS) absorb_kernel(AbsorbArgs a)
     uint32_t cw[AB_ROWS];
 #pragma unroll
     for (int k = 0; k < AB_ROWS; k++) {
-        const int r = r0 + 32 * k;
+        const int r = r0 + AB_RG * k;
         if (r < a.qk_nope) {
             const uint8_t *blk = W + (size_t)r * rb + b * 144;
             hd[k] = __ldg(reinterpret_cast<const uint4 *>(blk));
             cw[k] = __ldg(reinterpret_cast<const uint32_t *>(blk + 16 + pair * 32 + 4 * w4));
         }
     }
-    // rope rows: warp i takes row RPC * p + i (one row per warp covers RPC <= 8; more rows
-    // are loaded after the wait).  Lane chunk t8 = 8 code bytes 8 (t8 % 16) .. of block t8 / 16.
+    // rope rows: warp w takes rows w % 8, w % 8 + 8, .. of the CTA, code-byte half w / 8
+    // (lane chunk t8 = lane + 32 * half: 8 code bytes 8 (t8 % 16) .. of block t8 / 16)
     const int rpc = ((a.qk_rope + np - 1) / np + 1) & ~1, rlo = rpc * p, rhi = min(a.qk_rope, rlo + rpc);
     const bool rope = h < a.kv_heads && rlo < rhi;
     const uint8_t *WR = a.k_up + (size_t)h * qk_per * rb;  // kv head h's rows (rope keys)
-    uint4 rh[2];
-    uint2 rc[2];
-#define SB_ROPE_LOAD(i)                                                                     \
-    {                                                                                       \
-        const uint8_t *rw = WR + (size_t)(a.qk_nope + rlo + (i)) * rb;                      \
-        _Pragma("unroll") for (int j = 0; j < 2; j++) {                                     \
-            const int t8 = lane + 32 * j;                                                   \
-            if (t8 < nbk * 16) {                                                            \
-                const uint8_t *blk = rw + (t8 >> 4) * 144;                                  \
-                rh[j] = __ldg(reinterpret_cast<const uint4 *>(blk));                        \
-                rc[j] = __ldg(reinterpret_cast<const uint2 *>(blk + 16 + 8 * (t8 & 15)));   \
-            }                                                                               \
-        }                                                                                   \
+    const int rw0 = warp & 7, t8 = lane + 32 * (warp >> 3);
+    const bool rlane = t8 < nbk * 16;
+    uint4 rh = make_uint4(0u, 0u, 0u, 0u);
+    uint2 rc = make_uint2(0u, 0u);
+    if (rope && rw0 < rhi - rlo && rlane) {
+        const uint8_t *blk = WR + (size_t)(a.qk_nope + rlo + rw0) * rb + (t8 >> 4) * 144;
+        rh = __ldg(reinterpret_cast<const uint4 *>(blk));
+        rc = __ldg(reinterpret_cast<const uint2 *>(blk + 16 + 8 * (t8 & 15)));
     }
-    if (rope && warp < rhi - rlo) SB_ROPE_LOAD(warp)
     griddep_wait();  // q (q_up) and c (kv_down) come from the previous kernels
-    const int pos = *a.pos;
+    // one round of loads: pos, the latent row, q_nope and (CTA 0 of the head) the q rope pairs
+    const int pos = __ldcg(a.pos);
+    float cv[MAXR / AB_THREADS];
+#pragma unroll
+    for (int k = 0; k < MAXR / AB_THREADS; k++) {
+        const int j = tid + AB_THREADS * k;
+        cv[k] = j < a.kv_rank ? __ldcg(a.c + j) : 0.0f;
+    }
+    const float qn = tid < a.qk_nope ? __ldcg(a.q + (size_t)h * qk_per + tid) : 0.0f;
+    const bool qrope = p == 0 && tid < a.qk_rope / 2;
+    float x0 = 0.0f, x1 = 0.0f;
+    if (qrope) {
+        x0 = __ldcg(a.q + (size_t)h * qk_per + a.qk_nope + 2 * tid);
+        x1 = __ldcg(a.q + (size_t)h * qk_per + a.qk_nope + 2 * tid + 1);
+    }
     if (pos < 0 || pos >= a.ctx) {
         if (p == 0 && h == 0 && tid == 0) set_dev_error(0x81u);
         return;
     }
-    // one round of loads: the latent row (f16 rounding, the reference's) and q_nope
-    for (int j = tid; j < a.kv_rank; j += AB_THREADS) {
-        const uint16_t hb = f32_to_f16_ref(__ldcg(a.c + j));
-        cs[j] = f16_to_f32(hb);
-        if (h == 0 && (j >> 6) == p) a.latent[(size_t)pos * a.kv_rank + j] = hb;
-    }
-    for (int i = tid; i < a.qk_nope; i += AB_THREADS) qs[i] = __ldcg(a.q + (size_t)h * qk_per + i);
-    if (p == 0) {  // roped q slice (pairs 2i, 2i + 1)
-        for (int i = tid; i < a.qk_rope / 2; i += AB_THREADS) {
-            const float freq = powf(a.theta, -2.0f * (float)i / (float)a.qk_rope);
-            const float ang = (float)pos * freq, sn = sinf(ang), cs = cosf(ang);
-            const float x0 = a.q[(size_t)h * qk_per + a.qk_nope + 2 * i];
-            const float x1 = a.q[(size_t)h * qk_per + a.qk_nope + 2 * i + 1];
-            a.qr[(size_t)h * a.qk_rope + 2 * i] = x0 * cs - x1 * sn;
-            a.qr[(size_t)h * a.qk_rope + 2 * i + 1] = x0 * sn + x1 * cs;
+#pragma unroll
+    for (int k = 0; k < MAXR / AB_THREADS; k++) {
+        const int j = tid + AB_THREADS * k;
+        if (j < a.kv_rank) {
+            const uint16_t hb = f32_to_f16_ref(cv[k]);
+            cs[j] = f16_to_f32(hb);
+            if (h == 0 && (j >> 6) == p) a.latent[(size_t)pos * a.kv_rank + j] = hb;
         }
+    }
+    if (tid < a.qk_nope) qs[tid] = qn;
+    if (qrope) {  // roped q slice (pairs 2i, 2i + 1)
+        const float freq = powf(a.theta, -2.0f * (float)tid / (float)a.qk_rope);
+        const float ang = (float)pos * freq, sn = sinf(ang), cs_ = cosf(ang);
+        a.qr[(size_t)h * a.qk_rope + 2 * tid] = x0 * cs_ - x1 * sn;
+        a.qr[(size_t)h * a.qk_rope + 2 * tid + 1] = x0 * sn + x1 * cs_;
     }
     __syncthreads();
     // absorbed query: qt[j] = sum_i W_kn[i][j] * q_nope[i]
     float lo[4] = {0.0f, 0.0f, 0.0f, 0.0f}, hi[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int k = 0; k < AB_ROWS; k++) {
-        const int r = r0 + 32 * k;
+        const int r = r0 + AB_RG * k;
         if (r < a.qk_nope) {
             const float qv = qs[r];
             float ds0, dm0, ds1, dm1;
@@ -176,48 +186,46 @@ __global__ void __launch_bounds__(AB_THREADS) absorb_kernel(AbsorbArgs a)
     }
     // rope keys of kv head h: rows of W_kr times the latent row as the cache holds it (f16)
     if (rope) {
-        for (int i = warp; i < rhi - rlo; i += AB_THREADS / 32) {
-            if (i >= AB_THREADS / 32) SB_ROPE_LOAD(i)
+        for (int i = rw0; i < rhi - rlo; i += 8) {
+            if (i >= 8 && rlane) {
+                const uint8_t *blk = WR + (size_t)(a.qk_nope + rlo + i) * rb + (t8 >> 4) * 144;
+                rh = __ldg(reinterpret_cast<const uint4 *>(blk));
+                rc = __ldg(reinterpret_cast<const uint2 *>(blk + 16 + 8 * (t8 & 15)));
+            }
             float acc = 0.0f;
+            if (rlane) {
+                const int c8 = t8 & 15, pr = c8 >> 2;
+                const int col = (t8 >> 4) * 256 + pr * 64 + 8 * (c8 & 3);
+                float ds0, dm0, ds1, dm1;
+                q4k_sub(rh, 2 * pr, ds0, dm0);
+                q4k_sub(rh, 2 * pr + 1, ds1, dm1);
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int t8 = lane + 32 * j;
-                if (t8 < nbk * 16) {
-                    const int c8 = t8 & 15, pr = c8 >> 2;
-                    const int col = (t8 >> 4) * 256 + pr * 64 + 8 * (c8 & 3);
-                    float ds0, dm0, ds1, dm1;
-                    q4k_sub(rh[j], 2 * pr, ds0, dm0);
-                    q4k_sub(rh[j], 2 * pr + 1, ds1, dm1);
-#pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        const unsigned byte = ((e < 4 ? rc[j].x : rc[j].y) >> (8 * (e & 3))) & 255u;
-                        const float c0 = cs[col + e], c1 = cs[col + 32 + e];
-                        acc += (ds0 * (float)(byte & 15u) - dm0) * c0;
-                        acc += (ds1 * (float)(byte >> 4) - dm1) * c1;
-                    }
+                for (int e = 0; e < 8; e++) {
+                    const unsigned byte = ((e < 4 ? rc.x : rc.y) >> (8 * (e & 3))) & 255u;
+                    acc += (ds0 * (float)(byte & 15u) - dm0) * cs[col + e];
+                    acc += (ds1 * (float)(byte >> 4) - dm1) * cs[col + 32 + e];
                 }
             }
             acc = warp_sum(acc);
-            if (lane == 0) kr[i] = acc;
+            if (lane == 0) krp[warp >> 3][i] = acc;
         }
     }
-#undef SB_ROPE_LOAD
     __syncthreads();
     if (tid < 64) {
         float v = 0.0f;
 #pragma unroll
-        for (int w = 0; w < AB_THREADS / 32; w++) v += red[w][tid];
+        for (int w = 0; w < AB_WARPS; w++) v += red[w][tid];
         a.qt[(size_t)h * a.kv_rank + b * 256 + pair * 64 + tid] = v;
     }
     if (rope) {
         for (int i = tid; i < (rhi - rlo) / 2; i += AB_THREADS) {
             const int g = rlo / 2 + i;  // pair index within the rope slice
             const float freq = powf(a.theta, -2.0f * (float)g / (float)a.qk_rope);
-            const float ang = (float)pos * freq, sn = sinf(ang), cs = cosf(ang);
-            const float x0 = kr[2 * i], x1 = kr[2 * i + 1];
+            const float ang = (float)pos * freq, sn = sinf(ang), cs_ = cosf(ang);
+            const float k0 = krp[0][2 * i] + krp[1][2 * i], k1 = krp[0][2 * i + 1] + krp[1][2 * i + 1];
             float *dst = a.krope + ((size_t)pos * a.kv_heads + h) * a.qk_rope + 2 * g;
-            dst[0] = x0 * cs - x1 * sn;
-            dst[1] = x0 * sn + x1 * cs;
+            dst[0] = k0 * cs_ - k1 * sn;
+            dst[1] = k0 * sn + k1 * cs_;
         }
     }
 }
@@ -796,7 +804,7 @@ extern "C" int sbk_mla_absorb(const float *q, const float *c, const void *k_up, 
     if (!q || !c || !k_up || !latent || !krope || !qt || !qr || !pos) return -1;
     if (k_up_dtype != SB_DTYPE_Q4_K) return -5;
     if (!heads || !kv_heads || heads % kv_heads || heads > MAXH || kv_rank % 256 || kv_rank > MAXR || !qk_nope ||
-        qk_nope > 32 * AB_ROWS || !qk_rope || qk_rope % 2 || qk_rope > MAXRP || !ctx)
+        qk_nope > AB_RG * AB_ROWS || !qk_rope || qk_rope % 2 || qk_rope > MAXRP || !ctx)
         return -1;
     if (((uintptr_t)k_up) & 15) return -2;
     AbsorbArgs a{q, c, (const uint8_t *)k_up, latent, krope, qt, qr, pos, (int)heads, (int)kv_heads, (int)kv_rank,
