@@ -60,3 +60,32 @@ def test_product_has_no_oracle_dependency():
             txt = open(f, errors="replace").read()
             assert "import oracle" not in txt and "from oracle" not in txt, f
             assert "liboracle" not in txt, f
+
+
+def test_mla_shape_rejections_need_no_gpu():
+    """sbk_mla_absorb / sbk_mla_attn validate before touching the device (every call here
+    has exactly one bad argument; the valid remainder is DeepSeek-V2-Lite's shape)."""
+    from soso_b200.formats import DTYPE_Q4_K
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+
+    def absorb(k_up=p, dt=DTYPE_Q4_K, heads=16, kv_heads=16, kv_rank=512, qk_nope=128, qk_rope=64, q=p):
+        return L.sbk_mla_absorb(q, p, k_up, dt, p, p, p, p, p, heads, kv_heads, kv_rank, qk_nope, qk_rope, 2048,
+                                1e4, 0, None)
+
+    assert absorb(q=None) == -1
+    assert absorb(dt=8) == -5                  # k_up must be Q4_K
+    assert absorb(heads=17, kv_heads=17) == -1  # more heads than the kernels hold
+    assert absorb(heads=16, kv_heads=3) == -1  # heads not a multiple of kv_heads
+    assert absorb(kv_rank=300) == -1           # latent not whole Q4_K blocks
+    assert absorb(qk_nope=257) == -1           # more nope rows than a thread's share covers
+    assert absorb(qk_rope=63) == -1            # rope pairs
+    assert absorb(k_up=ctypes.c_void_p(8)) == -2
+
+    def attn(latent=p, kv_rank=512, qk_rope=64, ws=p):
+        return L.sbk_mla_attn(p, p, latent, p, p, p, 16, 16, kv_rank, 128, qk_rope, 2048, ws, 0, None)
+
+    assert attn(ws=None) == -1
+    assert attn(kv_rank=256) == -1             # attention wants kv_rank a multiple of 512
+    assert attn(qk_rope=256) == -1
+    assert attn(latent=ctypes.c_void_p(8)) == -2
