@@ -300,6 +300,15 @@ int sbk_rmsnorm(const float *x, const float *res, float *h_out, const float *w, 
 int sbk_rope_kv_append(float *qkv, const float *bias, const float *qnorm, const float *knorm, uint16_t *kcache,
                        uint16_t *vcache, const int32_t *pos, size_t heads, size_t kv_heads, size_t head_dim,
                        size_t ctx, float theta, float eps, int neox, int pdl, void *stream);
+/* The same with gm_rope's frequency factors (lxdde/ports/nouveau/gemma_capa.cu:99-125),
+ * how the reference runs YaRN on the GPU: factors[head_dim/2] (device, or NULL) divide
+ * the pair frequencies -- the divisors of yarn_factores, crates/soso-llm-core/src/
+ * gemm.rs:1413-1428 -- and mscale (> 0; 1 + 0.1 ln(factor) for YaRN) multiplies cos and
+ * sin.  factors NULL and mscale 1 are sbk_rope_kv_append exactly. */
+int sbk_rope_kv_append_yarn(float *qkv, const float *bias, const float *qnorm, const float *knorm, uint16_t *kcache,
+                            uint16_t *vcache, const int32_t *pos, size_t heads, size_t kv_heads, size_t head_dim,
+                            size_t ctx, float theta, float eps, int neox, const float *factors, float mscale,
+                            int pdl, void *stream);
 
 /* Workspace bytes for sbk_attn_decode (zero-filled before first use; left zeroed). */
 size_t sbk_attn_ws_bytes(size_t heads, size_t kv_heads, size_t head_dim, size_t ctx);

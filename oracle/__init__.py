@@ -240,6 +240,94 @@ def rope_llama_n(x: np.ndarray, pos: int, theta: float, n_rot: int) -> np.ndarra
     return y
 
 
+# ---- YaRN RoPE (f32 throughout, as the reference).  Parity unpinned: the reference's
+# tests hold no YaRN values; the two forms below are checked against each other, which is
+# the reference's own claim (yarn_factores "reproduces rope_neox_yarn", gemm.rs:1412-1413).
+_F = np.float32
+
+
+def _yarn_corr_dims(n_dims: int, orig_ctx: int, theta: float, beta_fast: float, beta_slow: float):
+    """yarn_corr_dims (crates/soso-llm-core/src/gemm.rs:1430-1441)."""
+    def dim(n_rot):
+        return _F(n_dims) * np.log(_F(orig_ctx) / (_F(n_rot) * _F(2.0) * _F(np.pi))) / (_F(2.0) * np.log(_F(theta)))
+    start = max(np.floor(dim(beta_fast)), _F(0.0))
+    end = min(np.ceil(dim(beta_slow)), _F(n_dims - 1))
+    return _F(start), _F(end)
+
+
+def _yarn_ramp(low, high, pair: int):
+    """yarn_ramp (gemm.rs:1443-1446)."""
+    y = (_F(pair) - low) / max(high - low, _F(0.001))
+    return _F(1.0) - _F(min(max(y, _F(0.0)), _F(1.0)))
+
+
+def yarn_factors(head_dim: int, theta: float, factor: float, orig_ctx: int, beta_fast: float,
+                 beta_slow: float) -> tuple[np.ndarray, np.float32]:
+    """yarn_factores (gemm.rs:1413-1428): per pair i the divisor of its RoPE frequency,
+    1 / (freq_scale (1 - ramp_i) + ramp_i) with freq_scale = 1 / factor, and the magnitude
+    mscale = 1 + 0.1 ln(factor) that multiplies cos and sin -- what the reference passes to
+    its GPU rope (gm_rope, lxdde/ports/nouveau/gemma_capa.cu:99-125; moe_gpu.rs:182)."""
+    low, high = _yarn_corr_dims(head_dim, orig_ctx, theta, beta_fast, beta_slow)
+    fs = _F(1.0) / _F(factor)
+    f = np.array([_F(1.0) / (fs * (_F(1.0) - _yarn_ramp(low, high, i)) + _yarn_ramp(low, high, i))
+                  for i in range(head_dim // 2)], dtype=np.float32)
+    return f, _F(_F(1.0) + _F(0.1) * np.log(_F(factor)))
+
+
+def rope_neox_yarn(x: np.ndarray, n_heads: int, hd: int, pos: int, theta: float, factor: float, orig_ctx: int,
+                   beta_fast: float, beta_slow: float) -> np.ndarray:
+    """rope_neox_yarn (gemm.rs:1372-1410), the reference's CPU YaRN: per pair the angle
+    blends interpolation (pos theta^(-2i/d) / factor) and extrapolation by the ramp, the
+    angle advancing by repeated multiplication; cos and sin scaled by mscale; NeoX pairs
+    (i, i + d/2) of every head.  Does nothing when YaRN is inactive (factor <= 1)."""
+    y = np.array(x, dtype=np.float32, copy=True)
+    if hd < 2 or n_heads == 0 or not (factor > 1.0 and orig_ctx > 0):
+        return y
+    half = hd // 2
+    fs = _F(1.0) / _F(factor)
+    low, high = _yarn_corr_dims(hd, orig_ctx, theta, beta_fast, beta_slow)
+    theta_scale = np.power(_F(theta), _F(-2.0) / _F(hd))
+    mscale = _F(_F(1.0) + _F(0.1) * np.log(_F(factor)))
+    cs, sn = np.empty(half, np.float32), np.empty(half, np.float32)
+    ang = _F(pos)
+    for i in range(half):
+        mix = _yarn_ramp(low, high, i)
+        ext = ang
+        a = (fs * ext) * (_F(1.0) - mix) + ext * mix
+        cs[i], sn[i] = np.cos(_F(a)) * mscale, np.sin(_F(a)) * mscale
+        ang = _F(ang * theta_scale)
+    for h in range(n_heads):
+        v = y[h * hd:(h + 1) * hd]
+        a0, b0 = v[:half].copy(), v[half:].copy()
+        v[:half] = a0 * cs - b0 * sn
+        v[half:] = a0 * sn + b0 * cs
+    return y
+
+
+def rope_heads_div(x: np.ndarray, n_heads: int, hd: int, pos: int, theta: float, neox: bool,
+                   factors: np.ndarray | None, mscale: float) -> np.ndarray:
+    """The reference's GPU rope with per-frequency divisors (gm_rope,
+    lxdde/ports/nouveau/gemma_capa.cu:99-125): freq_i = exp(-ln(theta) 2i / d) / factors[i],
+    angle pos freq_i, cos and sin times mscale; NeoX pairs (i, i + d/2) or llama pairs
+    (2i, 2i + 1)."""
+    y = np.array(x, dtype=np.float32, copy=True)
+    half = hd // 2
+    i = np.arange(half, dtype=np.float32)
+    freq = np.exp(-np.log(_F(theta)) * (_F(2.0) * i) / _F(hd)).astype(np.float32)
+    if factors is not None:
+        freq = (freq / np.asarray(factors, np.float32)).astype(np.float32)
+    ang = (_F(pos) * freq).astype(np.float32)
+    c, s = (np.cos(ang) * _F(mscale)).astype(np.float32), (np.sin(ang) * _F(mscale)).astype(np.float32)
+    e0 = np.arange(half) if neox else 2 * np.arange(half)
+    e1 = e0 + half if neox else e0 + 1
+    for h in range(n_heads):
+        v = y[h * hd:(h + 1) * hd]
+        a0, b0 = v[e0].copy(), v[e1].copy()
+        v[e0] = a0 * c - b0 * s
+        v[e1] = a0 * s + b0 * c
+    return y
+
+
 def topk_softmax(logits: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
     """gemm.rs:62-91; returns (idx int32[k], weights f32[k]) in rank order."""
     lg = np.array(logits, dtype=np.float32, copy=True)

@@ -109,6 +109,9 @@ SIGNATURES = {
                                                                            ctypes.c_int, ctypes.c_void_p]),
     "sbk_rope_kv_append": (ctypes.c_int, [ctypes.c_void_p] * 7 + [c_size] * 4 + [ctypes.c_float, ctypes.c_float,
                                                                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "sbk_rope_kv_append_yarn": (ctypes.c_int, [ctypes.c_void_p] * 7 + [c_size] * 4 +
+                                [ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_float,
+                                 ctypes.c_int, ctypes.c_void_p]),
     "sbk_attn_ws_bytes": (c_size, [c_size] * 4),
     "sbk_attn_decode": (ctypes.c_int, [ctypes.c_void_p] * 5 + [c_size] * 4 + [ctypes.c_void_p, ctypes.c_int,
                                                                           ctypes.c_void_p]),

@@ -54,6 +54,8 @@ struct RopeKvArgs {
     int heads, kv_heads, hd, ctx;
     float theta, eps;
     int neox;
+    const float *factors;  // [hd / 2] divisors of the pair frequencies (YaRN) or null
+    float mscale;          // multiplies cos and sin (1: plain RoPE)
 };
 
 __global__ void rope_kv_kernel(RopeKvArgs a)
@@ -91,9 +93,10 @@ __global__ void rope_kv_kernel(RopeKvArgs a)
         v1 = v1 * scale * nw[e1];
     }
     if (kind < 2) {
-        const float freq = powf(a.theta, (-2.0f * (float)i) / (float)a.hd);
+        float freq = powf(a.theta, (-2.0f * (float)i) / (float)a.hd);
+        if (a.factors) freq /= a.factors[i];  // YaRN: the reference's gm_rope (gemma_capa.cu:99-125)
         const float ang = (float)pos * freq;
-        const float s = sinf(ang), c = cosf(ang);
+        const float s = sinf(ang) * a.mscale, c = cosf(ang) * a.mscale;  // mscale 1: exact
         const float r0 = v0 * c - v1 * s, r1 = v0 * s + v1 * c;
         if (kind == 0) {
             a.qkv[base + e0] = r0;
@@ -815,15 +818,30 @@ inline int launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, int
 }
 }  // namespace sb
 
+extern "C" int sbk_rope_kv_append_yarn(float *qkv, const float *bias, const float *qnorm, const float *knorm,
+                                       uint16_t *kcache, uint16_t *vcache, const int32_t *pos, size_t heads,
+                                       size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox,
+                                       const float *factors, float mscale, int pdl, void *stream);
+
 extern "C" int sbk_rope_kv_append(float *qkv, const float *bias, const float *qnorm, const float *knorm,
                                   uint16_t *kcache, uint16_t *vcache, const int32_t *pos, size_t heads,
                                   size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox,
                                   int pdl, void *stream)
 {
+    return sbk_rope_kv_append_yarn(qkv, bias, qnorm, knorm, kcache, vcache, pos, heads, kv_heads, head_dim, ctx,
+                                   theta, eps, neox, nullptr, 1.0f, pdl, stream);
+}
+
+extern "C" int sbk_rope_kv_append_yarn(float *qkv, const float *bias, const float *qnorm, const float *knorm,
+                                       uint16_t *kcache, uint16_t *vcache, const int32_t *pos, size_t heads,
+                                       size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox,
+                                       const float *factors, float mscale, int pdl, void *stream)
+{
     if (!qkv || !kcache || !vcache || !pos || !heads || !kv_heads) return -1;
     if (head_dim < 64 || head_dim > 512 || (head_dim / 2) % 32 || heads % kv_heads) return -1;
-    sb::RopeKvArgs a{qkv, bias, qnorm, knorm, kcache, vcache, pos, (int)heads, (int)kv_heads, (int)head_dim,
-                     (int)ctx, theta, eps, neox};
+    if (!(mscale > 0.0f) || !isfinite(mscale)) return -1;
+    sb::RopeKvArgs a{qkv,          bias,         qnorm,       knorm, kcache, vcache, pos,     (int)heads,
+                     (int)kv_heads, (int)head_dim, (int)ctx,    theta, eps,    neox,   factors, mscale};
     return sb::launch_k(sb::rope_kv_kernel, dim3((unsigned)(heads + 2 * kv_heads)), dim3((unsigned)head_dim / 2), 0,
                         pdl, (cudaStream_t)stream, a);
 }

@@ -62,6 +62,44 @@ def test_rope_kv_append(heads, kv_heads, neox, qk_norm, bias):
     assert (kr[:pos] == 0).all() and (kr[pos + 1:] == 0).all()
 
 
+@pytest.mark.parametrize("heads,kv_heads,neox", [(16, 2, 1), (8, 8, 0)])
+def test_rope_kv_append_yarn(heads, kv_heads, neox):
+    """gm_rope's frequency factors (gemma_capa.cu:99-125) from yarn_factores (gemm.rs:1413-1428,
+    Mellum's YaRN: factor 16 over 8192 positions) against the oracle's restatement of gm_rope;
+    with no factors and mscale 1 the result is bit-equal to sbk_rope_kv_append."""
+    import torch
+    hd, ctx, pos, theta, eps = 128, 64, 37, 1e6, 1e-6
+    g = np.random.default_rng(100 + heads)
+    qd, kvd = heads * hd, kv_heads * hd
+    qkv = g.standard_normal(qd + 2 * kvd).astype(np.float32)
+    f, ms = oracle.yarn_factors(hd, theta, 16.0, 8192, 32.0, 1.0)
+    q = oracle.rope_heads_div(qkv[:qd], heads, hd, pos, theta, bool(neox), f, ms)
+    k = oracle.rope_heads_div(qkv[qd:qd + kvd], kv_heads, hd, pos, theta, bool(neox), f, ms)
+    dpos, df = cuda(np.array([pos], dtype=np.int32)), cuda(f)
+
+    def run(entry, *extra):
+        d = cuda(qkv)
+        kc = torch.zeros(ctx * kvd, dtype=torch.int16, device="cuda")
+        vc = torch.zeros(ctx * kvd, dtype=torch.int16, device="cuda")
+        rc = entry(d.data_ptr(), None, None, None, kc.data_ptr(), vc.data_ptr(), dpos.data_ptr(), heads, kv_heads, hd,
+                   ctx, theta, eps, neox, *extra, 0, stream())
+        assert rc == 0, rc
+        torch.cuda.synchronize()
+        return d.cpu().numpy(), kc.cpu().numpy().view(np.uint16).reshape(ctx, kvd)
+
+    gq, kr = run(lib().sbk_rope_kv_append_yarn, df.data_ptr(), float(ms))
+    assert np.max(np.abs(gq[:qd] - q) / (1 + np.abs(q))) < 5e-5
+    kf = np.array([oracle.f16_to_f32(int(u)) for u in kr[pos]], dtype=np.float32)
+    kreff = np.array([oracle.f16_to_f32(int(u)) for u in oracle.f32_to_f16_array(k)], dtype=np.float32)
+    assert np.max(np.abs(kf - kreff) / (1e-3 + np.abs(kreff))) < 2e-3
+    a = run(lib().sbk_rope_kv_append_yarn, None, 1.0)
+    b = run(lib().sbk_rope_kv_append)
+    assert np.array_equal(a[0].view(np.uint32), b[0].view(np.uint32)) and np.array_equal(a[1], b[1])
+    assert lib().sbk_rope_kv_append_yarn(dpos.data_ptr(), None, None, None, dpos.data_ptr(), dpos.data_ptr(),
+                                         dpos.data_ptr(), heads, kv_heads, hd, ctx, theta, eps, neox, None, 0.0, 0,
+                                         stream()) == -1  # mscale must be positive
+
+
 @pytest.mark.parametrize("heads,kv_heads,seq", [(16, 2, 1), (16, 2, 16), (16, 2, 17), (16, 2, 100), (16, 2, 513),
                                                 (16, 2, 2049), (16, 2, 4096), (32, 4, 777), (8, 8, 65)])
 def test_attention_decode(heads, kv_heads, seq):
