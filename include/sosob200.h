@@ -329,6 +329,12 @@ int sbk_attn_rope_decode(const float *qkv, const float *bias, const float *qnorm
                          uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos, size_t heads,
                          size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox, void *ws,
                          int pdl, void *stream);
+/* The same with YaRN: factors / mscale as sbk_rope_kv_append_yarn (gm_rope's frequency
+ * divisors, gemma_capa.cu:99-125); factors NULL is sbk_attn_rope_decode exactly. */
+int sbk_attn_rope_decode_yarn(const float *qkv, const float *bias, const float *qnorm, const float *knorm,
+                              uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos, size_t heads,
+                              size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox,
+                              const float *factors, float mscale, void *ws, int pdl, void *stream);
 
 /* out = silu(gate) * up, elementwise (`swiglu_inplace`, crates/soso-llm-core/src/gemm.rs:210-226). */
 int sbk_swiglu(const float *gate, const float *up, float *out, size_t n, int pdl, void *stream);

@@ -107,6 +107,9 @@ SIGNATURES = {
     "sbk_attn_rope_decode": (ctypes.c_int, [ctypes.c_void_p] * 8 + [c_size] * 4 + [ctypes.c_float, ctypes.c_float,
                                                                            ctypes.c_int, ctypes.c_void_p,
                                                                            ctypes.c_int, ctypes.c_void_p]),
+    "sbk_attn_rope_decode_yarn": (ctypes.c_int, [ctypes.c_void_p] * 8 + [c_size] * 4 +
+                                  [ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p, ctypes.c_float,
+                                   ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "sbk_rope_kv_append": (ctypes.c_int, [ctypes.c_void_p] * 7 + [c_size] * 4 + [ctypes.c_float, ctypes.c_float,
                                                                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "sbk_rope_kv_append_yarn": (ctypes.c_int, [ctypes.c_void_p] * 7 + [c_size] * 4 +

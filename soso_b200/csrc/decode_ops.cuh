@@ -173,6 +173,8 @@ struct AttnArgs {
     int heads, kv_heads, kv_dim, ctx;
     float theta, eps;
     int neox, rope;
+    const float *factors;      // rope: [hd / 2] YaRN divisors of the pair frequencies, or null
+    float mscale;              // rope with factors: multiplies cos and sin
 };
 
 struct AttSmem {
@@ -307,10 +309,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
     int issued = nsub < 2 ? nsub : 2;
     // RoPE angles (rope_cabezas: freq_i = theta^(-2i/d), angle = pos * freq_i)
     if (active && a.rope && tid < HD / 2) {
-        const float freq = powf(a.theta, (-2.0f * (float)tid) / (float)HD);
+        float freq = powf(a.theta, (-2.0f * (float)tid) / (float)HD);
+        if (a.factors) freq /= a.factors[tid];  // YaRN as gm_rope takes it (gemma_capa.cu:99-125)
         const float ang = (float)pos * freq;
-        s.rs[tid] = sinf(ang);
-        s.rc[tid] = cosf(ang);
+        s.rs[tid] = a.factors ? sinf(ang) * a.mscale : sinf(ang);
+        s.rc[tid] = a.factors ? cosf(ang) * a.mscale : cosf(ang);
     }
     // q heads of the group (and, for own_new, this token's k and v rows): one warp per
     // vector, lane l holds pairs l and l + 32; a warp has two vectors at most
@@ -926,14 +929,32 @@ extern "C" int sbk_attn_decode(const float *q, const uint16_t *kcache, const uin
     return sb::attn_launch(a, heads, kv_heads, head_dim, ctx, ws, pdl, (cudaStream_t)stream);
 }
 
+extern "C" int sbk_attn_rope_decode_yarn(const float *qkv, const float *bias, const float *qnorm, const float *knorm,
+                                         uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos,
+                                         size_t heads, size_t kv_heads, size_t head_dim, size_t ctx, float theta,
+                                         float eps, int neox, const float *factors, float mscale, void *ws, int pdl,
+                                         void *stream);
+
 extern "C" int sbk_attn_rope_decode(const float *qkv, const float *bias, const float *qnorm, const float *knorm,
                                     uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos, size_t heads,
                                     size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox,
                                     void *ws, int pdl, void *stream)
 {
+    return sbk_attn_rope_decode_yarn(qkv, bias, qnorm, knorm, kcache, vcache, out, pos, heads, kv_heads, head_dim,
+                                     ctx, theta, eps, neox, nullptr, 1.0f, ws, pdl, stream);
+}
+
+extern "C" int sbk_attn_rope_decode_yarn(const float *qkv, const float *bias, const float *qnorm, const float *knorm,
+                                         uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos,
+                                         size_t heads, size_t kv_heads, size_t head_dim, size_t ctx, float theta,
+                                         float eps, int neox, const float *factors, float mscale, void *ws, int pdl,
+                                         void *stream)
+{
+    if (!(mscale > 0.0f) || !isfinite(mscale)) return -1;
     sb::AttnArgs a = {};
     a.qkv = qkv, a.bias = bias, a.qnorm = qnorm, a.knorm = knorm, a.kc = kcache, a.vc = vcache, a.out = out;
     a.pos = pos, a.theta = theta, a.eps = eps, a.neox = neox, a.rope = 1;
+    a.factors = factors, a.mscale = mscale;
     return sb::attn_launch(a, heads, kv_heads, head_dim, ctx, ws, pdl, (cudaStream_t)stream);
 }
 

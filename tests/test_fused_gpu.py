@@ -176,3 +176,43 @@ def test_attn_rope_decode(heads, kv_heads, neox, qk_norm, bias, pos):
             # attention over the cache the GPU wrote (its own rounding of row pos)
             r = oracle.attention_decode_f16(q[h * hd:(h + 1) * hd], kr, vr, hd, kvd, h // G, pos + 1)
             assert np.max(np.abs(o[h * hd:(h + 1) * hd] - r)) < 2e-4 * (1 + np.max(np.abs(r))), h
+
+
+@pytest.mark.parametrize("heads,kv_heads,neox,pos", [(16, 2, 1, 37), (16, 2, 1, 700), (8, 8, 0, 129)])
+def test_attn_rope_decode_yarn(heads, kv_heads, neox, pos):
+    """The fused RoPE with YaRN divisors (Mellum's: factor 16 over 8192 positions; gm_rope,
+    gemma_capa.cu:99-125) against the oracle's gm_rope restatement and the f16 attention over
+    the cache the kernel wrote."""
+    import torch
+    hd, ctx, theta, eps = 128, 1024, 1e4, 1e-6
+    g = np.random.default_rng(7 * pos + heads)
+    qd, kvd = heads * hd, kv_heads * hd
+    qkv = g.standard_normal(qd + 2 * kvd).astype(np.float32)
+    kc = np.zeros((ctx, kvd), np.uint16)
+    vc = np.zeros((ctx, kvd), np.uint16)
+    kc[:pos] = oracle.f32_to_f16_array(g.standard_normal(pos * kvd).astype(np.float32)).reshape(pos, kvd)
+    vc[:pos] = oracle.f32_to_f16_array(g.standard_normal(pos * kvd).astype(np.float32)).reshape(pos, kvd)
+    f, ms = oracle.yarn_factors(hd, theta, 16.0, 8192, 32.0, 1.0)
+    q = oracle.rope_heads_div(qkv[:qd], heads, hd, pos, theta, bool(neox), f, ms)
+    k = oracle.rope_heads_div(qkv[qd:qd + kvd], kv_heads, hd, pos, theta, bool(neox), f, ms)
+    kt = oracle.f32_to_f16_array(k).view(np.float16).astype(np.float32)
+    dk, dv, dq, df = cuda(kc.view(np.int16)), cuda(vc.view(np.int16)), cuda(qkv), cuda(f)
+    ws = torch.zeros(lib().sbk_attn_ws_bytes(heads, kv_heads, hd, ctx), dtype=torch.uint8, device="cuda")
+    out = torch.zeros(qd, device="cuda")
+    dpos = cuda(np.array([pos], dtype=np.int32))
+    rc = lib().sbk_attn_rope_decode_yarn(dq.data_ptr(), None, None, None, dk.data_ptr(), dv.data_ptr(), out.data_ptr(),
+                                         dpos.data_ptr(), heads, kv_heads, hd, ctx, theta, eps, neox, df.data_ptr(),
+                                         float(ms), ws.data_ptr(), 1, stream())
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+    kr = dk.cpu().numpy().view(np.uint16).reshape(ctx, kvd)
+    vr = dv.cpu().numpy().view(np.uint16).reshape(ctx, kvd)
+    kf = kr[pos].view(np.float16).astype(np.float32)
+    # f32 angles of up to pos radians: the divided frequencies differ from the oracle's by an ulp
+    tol = 2e-3 + 2e-7 * pos
+    assert np.max(np.abs(kf - kt) / (1e-3 + np.abs(kt))) < tol
+    o = out.cpu().numpy()
+    G = heads // kv_heads
+    for h in range(heads):
+        r = oracle.attention_decode_f16(q[h * hd:(h + 1) * hd], kr, vr, hd, kvd, h // G, pos + 1)
+        assert np.max(np.abs(o[h * hd:(h + 1) * hd] - r)) < (2e-4 + 2e-7 * pos) * (1 + np.max(np.abs(r))), h
