@@ -151,6 +151,12 @@ typedef struct {
     sb_mat gate, up, down;
     const sb_moe_plan *moe;
     const sb_mla_plan *mla; /* when set: MLA attention (q, k, v unused; o = attn_output) */
+    /* YaRN RoPE of this layer (layer.rs:1184-1193 takes it on full-attention layers), as
+     * the reference's GPU rope takes it (gm_rope, gemma_capa.cu:99-125): head_dim/2
+     * divisors of the pair frequencies (yarn_factores, gemm.rs:1413-1428) and the mscale
+     * that multiplies cos and sin (> 0); NULL = plain RoPE.  GQA layers only. */
+    const float *rope_factors;
+    float rope_mscale;
 } sb_layer_plan;
 
 /* `DecodePlan` (gpu.rs:150-158) plus the embedding table (for device-side greedy

@@ -83,8 +83,12 @@ class DenseOracle:
                                     for i in range(cfg.heads)])
                 k = np.concatenate([oracle.rmsnorm(k[i * hd:(i + 1) * hd], m[p + "attn_k_norm"], cfg.eps)
                                     for i in range(cfg.kv_heads)])
-            q = oracle.rope_heads(q, cfg.heads, hd, pos, cfg.theta, cfg.neox)  # rope_cabezas (layer.rs:1184-1193)
-            k = oracle.rope_heads(k, cfg.kv_heads, hd, pos, cfg.theta, cfg.neox)
+            if cfg.yarn:  # rope_neox_yarn on full-attention layers (layer.rs:1184-1189)
+                q = oracle.rope_neox_yarn(q, cfg.heads, hd, pos, cfg.theta, *cfg.yarn)
+                k = oracle.rope_neox_yarn(k, cfg.kv_heads, hd, pos, cfg.theta, *cfg.yarn)
+            else:
+                q = oracle.rope_heads(q, cfg.heads, hd, pos, cfg.theta, cfg.neox)  # rope_cabezas (layer.rs:1190-1193)
+                k = oracle.rope_heads(k, cfg.kv_heads, hd, pos, cfg.theta, cfg.neox)
             self.k[l][pos] = oracle.f32_to_f16_array(k)  # LayerKv::append_f16 (kv.rs:258-275)
             self.v[l][pos] = oracle.f32_to_f16_array(v)
             att = np.concatenate([

@@ -60,7 +60,7 @@ class SbLayerPlan(ctypes.Structure):
                 ("neox", ctypes.c_int), ("q_norm", c_f32p), ("k_norm", c_f32p), ("qkv_bias", c_f32p),
                 ("norm_attn", c_f32p), ("norm_ffn", c_f32p), ("q", SbMat), ("k", SbMat), ("v", SbMat), ("o", SbMat),
                 ("gate", SbMat), ("up", SbMat), ("down", SbMat), ("moe", ctypes.POINTER(SbMoePlan)),
-                ("mla", ctypes.POINTER(SbMlaPlan))]
+                ("mla", ctypes.POINTER(SbMlaPlan)), ("rope_factors", c_f32p), ("rope_mscale", ctypes.c_float)]
 
 
 class SbDecodePlan(ctypes.Structure):

@@ -39,10 +39,11 @@ extern "C" int sbk_attn_decode(const float *q, const uint16_t *kcache, const uin
                                void *ws, int pdl, void *stream);
 extern "C" size_t sbk_argmax_ws_bytes(void);
 extern "C" int sbk_argmax(const float *v, size_t n, int32_t *out, void *ws, int pdl, void *stream);
-extern "C" int sbk_attn_rope_decode(const float *qkv, const float *bias, const float *qnorm, const float *knorm,
-                                    uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos, size_t heads,
-                                    size_t kv_heads, size_t head_dim, size_t ctx, float theta, float eps, int neox,
-                                    void *ws, int pdl, void *stream);
+extern "C" int sbk_attn_rope_decode_yarn(const float *qkv, const float *bias, const float *qnorm, const float *knorm,
+                                         uint16_t *kcache, uint16_t *vcache, float *out, const int32_t *pos,
+                                         size_t heads, size_t kv_heads, size_t head_dim, size_t ctx, float theta,
+                                         float eps, int neox, const float *factors, float mscale, void *ws, int pdl,
+                                         void *stream);
 
 namespace sb {
 
@@ -230,6 +231,8 @@ struct EngLayer {
     float theta = 0.0f;
     int neox = 0;
     float *qn = nullptr, *kn = nullptr, *bias = nullptr, *na = nullptr, *nf = nullptr;
+    float *rf = nullptr;  // YaRN divisors [hd / 2] or null
+    float rms = 1.0f;     // YaRN mscale
     uint16_t *kc = nullptr, *vc = nullptr;
     // MoE FFN (sb_moe_plan): router, n_exp experts (gate, up, down), optional shared expert
     bool moe = false, has_sh = false;
@@ -696,8 +699,8 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
                 if (l) std::swap(hc, ho);
                 consumed();
             }
-            ENG_CHECK(sbk_attn_rope_decode(e->qkv, L.bias, L.qn, L.kn, L.kc, L.vc, e->att, pos, L.heads, L.kvh, L.hd,
-                                           e->ctx, L.theta, e->eps, L.neox, e->attn_ws, 1, s));
+            ENG_CHECK(sbk_attn_rope_decode_yarn(e->qkv, L.bias, L.qn, L.kn, L.kc, L.vc, e->att, pos, L.heads, L.kvh,
+                                                L.hd, e->ctx, L.theta, e->eps, L.neox, L.rf, L.rms, e->attn_ws, 1, s));
         }
         {
             const sbk_xsrc xs{};
@@ -1058,7 +1061,11 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             if (!L.gu2.w && (rc = eng_mat(c, lp.up, L.ffn, H, &L.u, true)) != 1) return bail(rc);
             if ((rc = eng_mat(c, lp.down, H, L.ffn, &L.d, true)) != 1) return bail(rc);
         }
+        if (lp.rope_factors && (L.mla || !(lp.rope_mscale > 0.0f) || !std::isfinite(lp.rope_mscale)))
+            return bail(0);  // YaRN on GQA layers only, with a positive mscale
+        L.rms = lp.rope_factors ? lp.rope_mscale : 1.0f;
         if (upload_f32(e, lp.norm_attn, H, &L.na) || upload_f32(e, lp.norm_ffn, H, &L.nf) ||
+            upload_f32(e, lp.rope_factors, L.hd / 2, &L.rf) ||
             upload_f32(e, lp.q_norm, L.hd, &L.qn) || upload_f32(e, lp.k_norm, L.hd, &L.kn) ||
             upload_f32(e, L.tp_attn ? (tp_bias.empty() ? nullptr : tp_bias.data()) : lp.qkv_bias, L.qd + 2 * L.kvd,
                        &L.bias))

@@ -52,6 +52,9 @@ class DenseConfig:
     first_moe: int = 0
     shared_ffn: int = 0
     shared_gate: bool = False
+    # YaRN RoPE on every layer (manifest v8 YarnSpec: factor, orig_ctx, beta_fast, beta_slow);
+    # empty = plain RoPE
+    yarn: tuple = ()
     # Q4_K_M mix: Q4_K everywhere, Q6_K for ffn_down and the output matrix
     dtypes: dict = field(default_factory=lambda: {"attn_q": DTYPE_Q4_K, "attn_k": DTYPE_Q4_K, "attn_v": DTYPE_Q4_K,
                                                   "attn_output": DTYPE_Q4_K, "ffn_gate": DTYPE_Q4_K,
@@ -77,6 +80,10 @@ QWEN25_3B = DenseConfig(n_layers=36, hidden=2048, heads=16, kv_heads=2, head_dim
                         ctx=4096)
 # a small model of the same structure, for parity tests against the CPU oracle
 TINY = DenseConfig(n_layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1024, ctx=160)
+# the same with YaRN (factor 16 over a 64-position original context: pairs 0-10 ramp, the
+# rest are divided by 16)
+TINY_YARN = DenseConfig(n_layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, ffn=1024, vocab=1024, ctx=160,
+                        theta=1e4, yarn=(16.0, 64, 32.0, 1.0))
 
 _ALL_Q4K = {k: DTYPE_Q4_K for k in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down",
                                     "output", "token_embd", "ffn_gate_inp", "attn_q_down", "attn_q_up",
@@ -177,6 +184,28 @@ def _f32(a: np.ndarray | None):
     return None if a is None else a.ctypes.data_as(c_f32p)
 
 
+def yarn_divisors(head_dim: int, theta: float, factor: float, orig_ctx: int, beta_fast: float,
+                  beta_slow: float) -> tuple[np.ndarray, float]:
+    """The per-pair frequency divisors and the cos/sin magnitude the reference hands its GPU
+    rope for a YaRN layer (yarn_factores with yarn_corr_dims and yarn_ramp,
+    crates/soso-llm-core/src/gemm.rs:1413-1446), in f32 as there: the ramp runs between the
+    corrected dims of beta_fast and beta_slow; divisor_i = 1 / (ramp_i + (1 - ramp_i) / factor);
+    mscale = 1 + 0.1 ln(factor)."""
+    f = np.float32
+
+    def dim(n_rot):
+        return f(head_dim) * np.log(f(orig_ctx) / (f(n_rot) * f(2.0) * f(np.pi))) / (f(2.0) * np.log(f(theta)))
+
+    low = f(max(np.floor(dim(beta_fast)), f(0.0)))
+    high = f(min(np.ceil(dim(beta_slow)), f(head_dim - 1)))
+    scale = f(1.0) / f(factor)
+    out = np.empty(head_dim // 2, np.float32)
+    for i in range(head_dim // 2):
+        ramp = f(1.0) - f(min(max((f(i) - low) / max(high - low, f(0.001)), f(0.0)), f(1.0)))
+        out[i] = f(1.0) / (scale * (f(1.0) - ramp) + ramp)
+    return out, float(f(f(1.0) + f(0.1) * np.log(f(factor))))
+
+
 class DecodeSession:
     """A prepared whole-token decode on one device (sb_decode_prepare)."""
 
@@ -206,6 +235,10 @@ class DecodeSession:
             lp = layers[l]
             lp.heads, lp.kv_heads, lp.head_dim = cfg.heads, cfg.kv_heads, cfg.head_dim
             lp.theta, lp.neox = cfg.theta, int(cfg.neox)
+            if cfg.yarn and not cfg.mla:
+                yf, lp.rope_mscale = yarn_divisors(cfg.head_dim, cfg.theta, *cfg.yarn)
+                self._keep.append(yf)
+                lp.rope_factors = _f32(yf)
             lp.q_norm = _f32(model.get(f"blk.{l}.attn_q_norm"))
             lp.k_norm = _f32(model.get(f"blk.{l}.attn_k_norm"))
             lp.qkv_bias = _f32(model.get(f"blk.{l}.qkv_bias"))

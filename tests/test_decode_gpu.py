@@ -59,6 +59,34 @@ def test_decode_token_logits_and_kv_rows(gpu, tiny):
             assert np.max(np.abs(v - vt)) <= 2e-3 * max(1.0, float(np.abs(vt).max()))
 
 
+@pytest.fixture(scope="module")
+def tiny_yarn():
+    cfg = decode.TINY_YARN
+    return cfg, decode.synth_model(cfg, "tiny_yarn")
+
+
+def test_yarn_greedy_and_logits_match_oracle(gpu, tiny_yarn):
+    """YaRN layers: the engine applies the reference's GPU form (gm_rope with yarn_factores
+    divisors), the oracle the reference's CPU form (rope_neox_yarn, layer.rs:1184-1189); the
+    two agree to f32 rounding of the angles at these positions."""
+    cfg, model = tiny_yarn
+    # a prompt whose greedy chain has no near-tie (top-2 logit gaps >= 0.046 at logit rms 1.1):
+    # the two RoPE forms differ by ~1e-5 relative, which a gap of ~1e-4 would not survive
+    prompt = synth.rng("prompt", "tiny_yarn2").integers(0, cfg.vocab, 16).astype(np.int32)
+    sess = decode.DecodeSession(cfg, model)
+    try:
+        got = sess.greedy(prompt, 40)
+        want, logits = DenseOracle(cfg, model).greedy(prompt, 40)
+        gaps = [float(np.sort(lg)[-1] - np.sort(lg)[-2]) for lg in logits]
+        assert np.array_equal(got, want), (np.nonzero(got != want)[0][:5], min(gaps))
+        orc = DenseOracle(cfg, model)
+        for pos, t in enumerate(synth.rng("toks", "tiny_yarn").integers(0, cfg.vocab, 8)):
+            e = orc.embed(int(t))
+            assert logits_close(sess.token(e, pos), orc.step(e, pos)) <= LOGIT_REL, pos
+    finally:
+        sess.close()
+
+
 def test_prepare_declines_unsupported_head_dim(gpu):
     cfg = decode.DenseConfig(n_layers=1, hidden=256, heads=4, kv_heads=2, head_dim=64, ffn=256, vocab=256, ctx=16)
     model = decode.synth_model(cfg, "hd64")

@@ -48,3 +48,13 @@ def test_inactive_yarn():
     got = oracle.rope_heads_div(x, heads, hd, pos, theta, True, np.ones(hd // 2, np.float32), 1.0)
     want = oracle.rope_heads(x, heads, hd, pos, theta, True)
     assert np.max(np.abs(got - want) / (1.0 + np.abs(want))) < 2e-5
+
+
+@pytest.mark.parametrize("factor,orig_ctx,beta_fast,beta_slow,theta", SPECS + [(16.0, 64, 32.0, 1.0, 1e4)])
+def test_product_divisors_equal_oracle(factor, orig_ctx, beta_fast, beta_slow, theta):
+    """The divisors the decode session hands the engine (host code of the product) are the
+    oracle's yarn_factores restatement, bit for bit."""
+    from soso_b200 import decode
+    a, ma = decode.yarn_divisors(128, theta, factor, orig_ctx, beta_fast, beta_slow)
+    b, mb = oracle.yarn_factors(128, theta, factor, orig_ctx, beta_fast, beta_slow)
+    assert np.array_equal(a, b) and ma == float(mb)
