@@ -209,6 +209,16 @@ int sb_decode_finish(sb_ctx *ctx);
  * (`sosomodel::dequant::row_bytes`, crates/sosomodel/src/dequant.rs:53-63). */
 size_t sbk_row_bytes(uint8_t dtype, size_t cols);
 
+/* The .som container of the reference's model directories (manifest.som, index.som,
+ * shards/): host functions, no device.  sb_crc32c: CRC-32C (Castagnoli) of n bytes, the
+ * checksum every .som header carries (sosomodel::crc32c, crates/sosomodel/src/lib.rs:32-34).
+ * sb_som_payload: 1 and the payload / its length / the version when the header's magic,
+ * length and CRC agree (parse_som, lib.rs:88-104; shard != 0: verify_shard,
+ * index.rs:118-139, payload at byte 64 from shard version 2), else 0. */
+uint32_t sb_crc32c(const void *data, size_t n);
+int sb_som_payload(const void *file, size_t file_len, int shard, const void **payload, size_t *len,
+                   uint32_t *version);
+
 /* y[rows] = W[rows x cols] . x[cols] for dtype Q8_0 / Q4_K / Q6_K / Q6_K_P.  Replaces
  * `gm_matvec_q4k` / `gm_matvec_q80` (lxdde/ports/nouveau/gemma_capa.cu:433,:501)
  * and the CPU `gemm::matvec_q4_k` / `matvec_q8_0` (crates/soso-llm-core/src/gemm.rs:295,:402).

@@ -369,3 +369,43 @@ def f32_to_f16_array(v: np.ndarray) -> np.ndarray:
     """f16.rs:10-37 elementwise (the reference KV-cache rounding)."""
     L = lib()
     return np.array([L.or_f32_to_f16(float(a)) for a in np.asarray(v, dtype=np.float32).ravel()], dtype=np.uint16)
+
+
+# ---- .som container writers (test infrastructure: the reference's writers restated, to build
+# files the product's reader must accept or reject)
+def crc32c_bitwise(data: bytes) -> int:
+    """CRC-32C one bit at a time: the published definition of the `crc` crate's CRC_32_ISCSI
+    (crc-catalog 2.5.0: reflected poly 0x1EDC6F41, init / xorout 0xFFFFFFFF), which
+    sosomodel::crc32c uses (crates/sosomodel/src/lib.rs:30-34)."""
+    crc = 0xFFFFFFFF
+    for b in bytes(data):
+        crc ^= b
+        for _ in range(8):
+            crc = (crc >> 1) ^ (0x82F63B78 if crc & 1 else 0)
+    return crc ^ 0xFFFFFFFF
+
+
+def pack_som(body: bytes, version: int, align: int) -> bytes:
+    """pack_som (lib.rs:72-85): magic, CRC-32C of body, version, u64 length, body, zeros to align."""
+    out = b"SOMODL01" + crc32c_bitwise(body).to_bytes(4, "little") + version.to_bytes(4, "little") + \
+        len(body).to_bytes(8, "little") + bytes(body)
+    return out + bytes(-len(out) % align)
+
+
+def pack_shard(data: bytes) -> bytes:
+    """pack_shard (index.rs:97-115): version-2 header, payload at byte 64, zeros to 4096."""
+    head = b"SOMODL01" + crc32c_bitwise(data).to_bytes(4, "little") + (2).to_bytes(4, "little") + \
+        len(data).to_bytes(8, "little")
+    out = head + bytes(64 - len(head)) + bytes(data)
+    return out + bytes(-len(out) % 4096)
+
+
+def serialize_index(entries) -> bytes:
+    """TensorIndex::serialize (index.rs:37-58); entries: (id, name, shard, offset, byte_len,
+    shape, dtype, quant) tuples."""
+    body = len(entries).to_bytes(4, "little")
+    for tid, name, shard, offset, byte_len, shape, dtype, quant in entries:
+        body += tid.to_bytes(4, "little") + name.encode() + b"\0" + shard.encode() + b"\0"
+        body += offset.to_bytes(8, "little") + byte_len.to_bytes(8, "little") + len(shape).to_bytes(4, "little")
+        body += b"".join(int(d).to_bytes(4, "little") for d in shape) + bytes([dtype, quant, 0, 0])
+    return pack_som(body, 1, 64)

@@ -128,6 +128,9 @@ SIGNATURES = {
     "sbk_matvec_q4k_noalloc": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p,
                                               ctypes.c_void_p]),
     "sbk_num_sms": (ctypes.c_int, [ctypes.c_int]),
+    "sb_crc32c": (ctypes.c_uint32, [ctypes.c_void_p, c_size]),
+    "sb_som_payload": (ctypes.c_int, [ctypes.c_void_p, c_size, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
+                                      ctypes.POINTER(c_size), ctypes.POINTER(ctypes.c_uint32)]),
     "sbk_matmul_ws_bytes": (c_size, [c_size, c_size]),
     "sbk_mla_ws_bytes": (c_size, [c_size, c_size]),
     "sbk_mla_absorb": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_uint8] + [ctypes.c_void_p] * 5 +

@@ -9,3 +9,4 @@
 #include "engine.cuh"
 #include "noalloc.cuh"
 #include "prefill.cuh"
+#include "som.cuh"

@@ -1,0 +1,163 @@
+"""Reader of the reference's model directories: ``manifest.som``, ``index.som`` and
+``shards/*`` (crates/sosomodel/src/layout.rs:3-6).
+
+Every .som file is a 24-byte header (magic ``SOMODL01``, CRC-32C of the payload, version,
+payload length) and the payload (lib.rs:70-104); a shard of version >= 2 puts its payload
+at byte 64 so that mmap'd weights are 64-byte aligned (index.rs:93-139).  The header
+checks and the CRC run in the library (``sb_som_payload``, ``sb_crc32c``).  The index is
+the tensor table (TensorIndex::parse, index.rs:61-91); a tensor's bytes are a slice of its
+shard's payload, handed to the decode plan (``SbMat`` views) without a copy.  The
+manifest's payload (model hyper-parameters, manifest.rs) is kept raw here: its fields are
+what ``decode.DenseConfig`` carries.
+"""
+from __future__ import annotations
+
+import ctypes
+import mmap
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import c_size, lib
+
+MANIFEST_FILE, INDEX_FILE, SHARDS_DIR = "manifest.som", "index.som", "shards"
+
+
+class SomError(ValueError):
+    """A .som file whose header, length, CRC or table does not hold together."""
+
+
+def payload(buf, shard: bool = False) -> tuple[int, np.ndarray]:
+    """(version, payload bytes as a uint8 view of `buf`) -- parse_som (lib.rs:88-104), or
+    verify_shard (index.rs:118-139) when `shard`; raises SomError like their Err(())."""
+    arr = np.frombuffer(buf, dtype=np.uint8)
+    p, n, v = ctypes.c_void_p(), c_size(), ctypes.c_uint32()
+    base = arr.ctypes.data if arr.size else None
+    if lib().sb_som_payload(base, arr.size, int(shard), ctypes.byref(p), ctypes.byref(n), ctypes.byref(v)) != 1:
+        raise SomError("not a .som file, or its length / CRC-32C does not match")
+    off = p.value - arr.ctypes.data
+    return int(v.value), arr[off:off + n.value]
+
+
+def crc32c(buf) -> int:
+    """CRC-32C of `buf` (sosomodel::crc32c, lib.rs:32-34)."""
+    arr = np.frombuffer(buf, dtype=np.uint8)
+    return int(lib().sb_crc32c(arr.ctypes.data if arr.size else None, arr.size))
+
+
+@dataclass(frozen=True)
+class TensorEntry:
+    """One row of index.som (TensorEntry, index.rs:14-24)."""
+    id: int
+    name: str
+    shard: str
+    offset: int
+    byte_len: int
+    shape: tuple
+    dtype: int
+    quant: int
+
+
+class _Cursor:
+    """Bounds-checked little-endian reads (Reader, lib.rs:106-147)."""
+
+    def __init__(self, b: bytes):
+        self.b, self.off = b, 0
+
+    def take(self, n: int) -> bytes:
+        if n < 0 or self.off + n > len(self.b):
+            raise SomError("truncated .som payload")
+        s = self.b[self.off:self.off + n]
+        self.off += n
+        return s
+
+    def u8(self) -> int:
+        return self.take(1)[0]
+
+    def u32(self) -> int:
+        return int.from_bytes(self.take(4), "little")
+
+    def u64(self) -> int:
+        return int.from_bytes(self.take(8), "little")
+
+    def cstr(self) -> str:
+        j = self.b.find(b"\0", self.off)
+        if j < 0:
+            raise SomError("unterminated string in .som payload")
+        try:
+            s = self.b[self.off:j].decode("utf-8")
+        except UnicodeDecodeError as e:
+            raise SomError("string in .som payload is not UTF-8") from e
+        self.off = j + 1
+        return s
+
+
+def parse_index(buf) -> list[TensorEntry]:
+    """TensorIndex::parse (index.rs:61-91): u32 count; per tensor u32 id, name NUL, shard NUL,
+    u64 offset, u64 byte_len, u32 ndim, ndim x u32, u8 dtype, u8 quant, 2 padding bytes."""
+    _, body = payload(buf)
+    r = _Cursor(body.tobytes())
+    out = []
+    for _ in range(r.u32()):
+        tid, name, shard = r.u32(), r.cstr(), r.cstr()
+        offset, byte_len = r.u64(), r.u64()
+        shape = tuple(r.u32() for _ in range(r.u32()))
+        dtype, quant = r.u8(), r.u8()
+        r.take(2)
+        out.append(TensorEntry(tid, name, shard, offset, byte_len, shape, dtype, quant))
+    return out
+
+
+class SomModel:
+    """A model directory: the index, the manifest payload, and each shard mapped once
+    (read-only) with its CRC checked on first use (``verify=False`` skips the check)."""
+
+    def __init__(self, path: str, verify: bool = True):
+        self.path, self.verify = path, verify
+        with open(os.path.join(path, MANIFEST_FILE), "rb") as f:
+            self.manifest_version, mp = payload(f.read())
+        self.manifest_payload = mp.tobytes()
+        with open(os.path.join(path, INDEX_FILE), "rb") as f:
+            self.entries = {e.name: e for e in parse_index(f.read())}
+        self._shards: dict[str, tuple] = {}
+
+    def names(self) -> list[str]:
+        return list(self.entries)
+
+    def _shard(self, shard: str) -> np.ndarray:
+        if shard not in self._shards:
+            if os.path.basename(shard) != shard or shard in ("", ".", ".."):
+                raise SomError(f"shard name {shard!r} leaves the shards directory")
+            with open(os.path.join(self.path, SHARDS_DIR, shard), "rb") as f:
+                mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+            raw = np.frombuffer(mm, dtype=np.uint8)
+            if self.verify:
+                _, body = payload(raw, shard=True)
+            else:  # header fields only
+                ver = int.from_bytes(raw[12:16].tobytes(), "little")
+                plen = int.from_bytes(raw[16:24].tobytes(), "little")
+                off = 64 if ver >= 2 else 24
+                if raw[:8].tobytes() != b"SOMODL01" or off + plen > raw.size:
+                    raise SomError(f"shard {shard}: bad header")
+                body = raw[off:off + plen]
+            self._shards[shard] = (mm, body)
+        return self._shards[shard][1]
+
+    def tensor(self, name: str) -> np.ndarray:
+        """The tensor's bytes (uint8 view into its mapped shard, no copy)."""
+        e = self.entries.get(name)
+        if e is None:
+            raise KeyError(name)
+        body = self._shard(e.shard)
+        if e.offset + e.byte_len > body.size:
+            raise SomError(f"{name}: bytes {e.offset}..{e.offset + e.byte_len} beyond its shard's payload")
+        return body[e.offset:e.offset + e.byte_len]
+
+    def close(self):
+        for mm, _ in self._shards.values():
+            try:
+                mm.close()
+            except BufferError:  # views still alive: the map goes with them
+                pass
+        self._shards.clear()

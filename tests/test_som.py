@@ -1,0 +1,154 @@
+"""The .som reader (soso_b200/som.py + sb_crc32c / sb_som_payload in the library), CPU only.
+
+Pinned against: the CRC-32C check value of the published algorithm ("123456789" ->
+0xE3069283; the `crc` crate's CRC_32_ISCSI, crc-catalog 2.5.0, which
+crates/sosomodel/src/lib.rs:30-34 uses) and a bitwise restatement; the reference's own
+tiny model headers (tests/golden/som_tiny, copied by make_som_fixture.py from
+rootfs/models/tiny); the reference's shard / index / truncation tests
+(crates/sosomodel/tests/roundtrip.rs:137-242), restated.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from soso_b200 import som
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "som_tiny")
+
+
+def test_crc32c_check_value_and_bitwise():
+    assert som.crc32c(b"123456789") == 0xE3069283
+    assert som.crc32c(b"") == 0
+    g = np.random.default_rng(5)
+    buf = g.integers(0, 256, 300, dtype=np.uint8).tobytes()
+    for start in range(0, 9):  # every alignment of the eight-byte steps
+        for n in (0, 1, 7, 8, 9, 15, 16, 17, 63, 64, 65, 200):
+            piece = buf[start:start + n]
+            assert som.crc32c(piece) == oracle.crc32c_bitwise(piece), (start, n)
+
+
+def test_reference_tiny_model_headers():
+    """The index and manifest the reference wrote: headers and CRCs agree, every entry is an
+    f32 tensor whose byte length is its shape's, and every shard it names is a file of the
+    model that holds those bytes."""
+    with open(os.path.join(GOLD, "index.som"), "rb") as f:
+        entries = som.parse_index(f.read())
+    with open(os.path.join(GOLD, "manifest.som"), "rb") as f:
+        version, body = som.payload(f.read())
+    assert version >= 1 and body.size > 0
+    shards = json.load(open(os.path.join(GOLD, "shards.json")))
+    assert len(entries) == 22 and len({e.name for e in entries}) == 22
+    assert sorted(e.id for e in entries) == list(range(22))
+    e0 = entries[0]
+    assert (e0.name, e0.shard, e0.offset, e0.byte_len, e0.shape, e0.dtype, e0.quant) == (
+        "L00.attn_q", "L00.attn_q.tensor", 0, 65536, (128, 128), 1, 0)
+    for e in entries:
+        assert e.dtype == 1 and e.quant == 0 and e.byte_len == 4 * int(np.prod(e.shape)), e
+        assert e.shard in shards and e.offset + e.byte_len <= shards[e.shard], e
+
+
+def test_shard_cases_of_the_reference():
+    """roundtrip.rs:137-151, :172-207: pack -> verify returns the payload; a flipped magic
+    byte is rejected; 600 payloads of 37 bytes verify whatever their CRC; the v2 payload
+    sits at byte 64 and the file is a multiple of 4096; trailing zeros are kept."""
+    p = oracle.pack_shard(bytes([1, 2, 3, 4]))
+    assert som.payload(p, shard=True)[1].tobytes() == bytes([1, 2, 3, 4])
+    bad = bytearray(p)
+    bad[0] ^= 0xFF
+    with pytest.raises(som.SomError):
+        som.payload(bytes(bad), shard=True)
+    for seed in range(600):
+        data = bytes(((seed * 31 + i) % (1 << 32)) % 251 for i in range(37))
+        assert som.payload(oracle.pack_shard(data), shard=True)[1].tobytes() == data, seed
+    data = bytes(range(100))
+    p = np.frombuffer(oracle.pack_shard(data), dtype=np.uint8)
+    v, body = som.payload(p, shard=True)
+    assert v == 2 and body.ctypes.data - p.ctypes.data == 64 and p.size % 4096 == 0 and body.tobytes() == data
+    assert som.payload(oracle.pack_shard(bytes([1, 2, 3, 0, 0, 0])), shard=True)[1].tobytes() == bytes([1, 2, 3, 0,
+                                                                                                        0, 0])
+    flip = bytearray(oracle.pack_shard(data))
+    flip[64 + 50] ^= 1  # a payload bit: the CRC no longer matches
+    with pytest.raises(som.SomError):
+        som.payload(bytes(flip), shard=True)
+
+
+def test_truncated_and_corrupt_headers_raise():
+    """roundtrip.rs:220-242: no truncation of an index or manifest is accepted, and a huge
+    payload length is rejected."""
+    idx = open(os.path.join(GOLD, "index.som"), "rb").read()
+    man = open(os.path.join(GOLD, "manifest.som"), "rb").read()
+    for data in (idx, man):
+        for cut in range(len(data)):
+            try:
+                som.payload(data[:cut])
+            except som.SomError:
+                continue
+            # a cut inside the zero padding after the payload is still a whole file
+            assert cut >= 24 + int.from_bytes(data[16:24], "little"), cut
+    evil = bytearray(man)
+    evil[16:24] = (2 ** 64 - 1).to_bytes(8, "little")
+    with pytest.raises(som.SomError):
+        som.payload(bytes(evil))
+    with pytest.raises(som.SomError):
+        som.payload(b"NOTSOM01" + man[8:])
+
+
+def test_model_directory_views(tmp_path):
+    """A model directory with the reference's tiny index and manifest and shards written by
+    the reference's pack_shard: every tensor comes back as the bytes written, as a view of
+    its mapped shard; a corrupted shard is refused on first use."""
+    for f in ("index.som", "manifest.som"):
+        (tmp_path / f).write_bytes(open(os.path.join(GOLD, f), "rb").read())
+    with open(os.path.join(GOLD, "index.som"), "rb") as f:
+        entries = som.parse_index(f.read())
+    (tmp_path / "shards").mkdir()
+    want = {}
+    g = np.random.default_rng(11)
+    for shard in sorted({e.shard for e in entries}):  # tensors may share a shard
+        mine = [e for e in entries if e.shard == shard]
+        raw = g.integers(0, 256, max(e.offset + e.byte_len for e in mine), dtype=np.uint8).tobytes()
+        for e in mine:
+            want[e.name] = raw[e.offset:e.offset + e.byte_len]
+        (tmp_path / "shards" / shard).write_bytes(oracle.pack_shard(raw))
+    m = som.SomModel(str(tmp_path))
+    try:
+        assert set(m.names()) == set(want)
+        for name, raw in want.items():
+            t = m.tensor(name)
+            assert t.dtype == np.uint8 and t.tobytes() == raw
+        with pytest.raises(KeyError):
+            m.tensor("no.such.tensor")
+    finally:
+        m.close()
+    victim = entries[3].shard
+    b = bytearray((tmp_path / "shards" / victim).read_bytes())
+    b[64 + 7] ^= 0x40
+    (tmp_path / "shards" / victim).write_bytes(bytes(b))
+    m = som.SomModel(str(tmp_path))
+    try:
+        with pytest.raises(som.SomError):
+            m.tensor(entries[3].name)
+        m2 = som.SomModel(str(tmp_path), verify=False)  # header-only checks load it
+        assert m2.tensor(entries[3].name).size == entries[3].byte_len
+        m2.close()
+    finally:
+        m.close()
+
+
+def test_index_roundtrip_of_the_reference_writer(tmp_path):
+    """index_roundtrip (roundtrip.rs:153-160) with the reference's serializer restated, and a
+    shard name that would leave the shards directory refused."""
+    data = oracle.serialize_index([(0, "w", "s.tensor", 0, 64, (4, 4), 1, 0),
+                                   (1, "blk.0.attn_q.weight", "s.tensor", 64, 144, (1, 256), 3, 2)])
+    es = som.parse_index(data)
+    assert [(e.id, e.name, e.shard, e.offset, e.byte_len, e.shape, e.dtype, e.quant) for e in es] == [
+        (0, "w", "s.tensor", 0, 64, (4, 4), 1, 0), (1, "blk.0.attn_q.weight", "s.tensor", 64, 144, (1, 256), 3, 2)]
+    (tmp_path / "index.som").write_bytes(oracle.serialize_index([(0, "w", "../index.som", 0, 4, (1,), 1, 0)]))
+    (tmp_path / "manifest.som").write_bytes(open(os.path.join(GOLD, "manifest.som"), "rb").read())
+    m = som.SomModel(str(tmp_path))
+    with pytest.raises(som.SomError):
+        m.tensor("w")
+    m.close()
