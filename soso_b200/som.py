@@ -6,9 +6,10 @@ payload length) and the payload (lib.rs:70-104); a shard of version >= 2 puts it
 at byte 64 so that mmap'd weights are 64-byte aligned (index.rs:93-139).  The header
 checks and the CRC run in the library (``sb_som_payload``, ``sb_crc32c``).  The index is
 the tensor table (TensorIndex::parse, index.rs:61-91); a tensor's bytes are a slice of its
-shard's payload, handed to the decode plan (``SbMat`` views) without a copy.  The
-manifest's payload (model hyper-parameters, manifest.rs) is kept raw here: its fields are
-what ``decode.DenseConfig`` carries.
+shard's payload, handed to the decode plan (``SbMat`` views) without a copy.  Of the
+manifest (manifest.rs) the leading fields every version shares are read
+(``parse_manifest_core``: sizes, heads, RoPE theta, RMS eps, expert counts); the raw
+payload is kept for the rest.
 """
 from __future__ import annotations
 
@@ -109,6 +110,50 @@ def parse_index(buf) -> list[TensorEntry]:
     return out
 
 
+@dataclass(frozen=True)
+class ManifestCore:
+    """The fields every manifest version starts with (Manifest::parse, manifest.rs:1021-1050):
+    v1 name .. max_seq; v2 adds kv_heads, rope_theta, rms_eps (v1: heads, 1e4, 1e-5);
+    v3 adds the expert counts (earlier: 0).  Later versions continue with per-layer specs
+    and extensions, which are not read here."""
+    version: int
+    name: str
+    vocab: int
+    hidden: int
+    n_layers: int
+    heads: int
+    ffn: int
+    max_seq: int
+    kv_heads: int
+    rope_theta: float
+    rms_eps: float
+    n_experts: int
+    experts_per_tok: int
+    moe_ffn: int
+
+
+def parse_manifest_core(buf) -> ManifestCore:
+    """The manifest's leading fields, with the reference's checks on them: heads and kv heads
+    non-zero and, before version 4, hidden % heads == 0 and heads % kv_heads == 0."""
+    version, body = payload(buf)
+    r = _Cursor(body.tobytes())
+    name = r.cstr()
+    vocab, hidden, n_layers, heads, ffn, max_seq = (r.u32() for _ in range(6))
+    if version >= 2:
+        kv_heads = r.u32()
+        theta = float(np.frombuffer(r.take(4), "<f4")[0])
+        eps = float(np.frombuffer(r.take(4), "<f4")[0])
+    else:
+        kv_heads, theta, eps = heads, 10000.0, float(np.float32(1e-5))
+    n_exp, per_tok, moe_ffn = (r.u32(), r.u32(), r.u32()) if version >= 3 else (0, 0, 0)
+    if heads == 0 or kv_heads == 0:
+        raise SomError("manifest: zero heads")
+    if version < 4 and (hidden % heads or heads % kv_heads):
+        raise SomError("manifest: heads do not divide the hidden size / kv heads")
+    return ManifestCore(version, name, vocab, hidden, n_layers, heads, ffn, max_seq, kv_heads, theta, eps, n_exp,
+                        per_tok, moe_ffn)
+
+
 class SomModel:
     """A model directory: the index, the manifest payload, and each shard mapped once
     (read-only) with its CRC checked on first use (``verify=False`` skips the check)."""
@@ -116,8 +161,10 @@ class SomModel:
     def __init__(self, path: str, verify: bool = True):
         self.path, self.verify = path, verify
         with open(os.path.join(path, MANIFEST_FILE), "rb") as f:
-            self.manifest_version, mp = payload(f.read())
+            raw = f.read()
+        self.manifest_version, mp = payload(raw)
         self.manifest_payload = mp.tobytes()
+        self.manifest = parse_manifest_core(raw)
         with open(os.path.join(path, INDEX_FILE), "rb") as f:
             self.entries = {e.name: e for e in parse_index(f.read())}
         self._shards: dict[str, tuple] = {}
@@ -130,7 +177,10 @@ class SomModel:
             if os.path.basename(shard) != shard or shard in ("", ".", ".."):
                 raise SomError(f"shard name {shard!r} leaves the shards directory")
             with open(os.path.join(self.path, SHARDS_DIR, shard), "rb") as f:
-                mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+                try:
+                    mm = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+                except ValueError as e:  # an empty file
+                    raise SomError(f"shard {shard}: empty file") from e
             raw = np.frombuffer(mm, dtype=np.uint8)
             if self.verify:
                 _, body = payload(raw, shard=True)

@@ -115,6 +115,7 @@ def test_model_directory_views(tmp_path):
         (tmp_path / "shards" / shard).write_bytes(oracle.pack_shard(raw))
     m = som.SomModel(str(tmp_path))
     try:
+        assert m.manifest.name == "tiny" and m.manifest.n_layers == 4
         assert set(m.names()) == set(want)
         for name, raw in want.items():
             t = m.tensor(name)
@@ -152,3 +153,19 @@ def test_index_roundtrip_of_the_reference_writer(tmp_path):
     with pytest.raises(som.SomError):
         m.tensor("w")
     m.close()
+
+
+def test_manifest_core_of_the_reference_tiny_model():
+    """Manifest::tiny (manifest.rs), the model rootfs/models/tiny was written from: vocab 256,
+    hidden 128, 4 layers of 4 heads, ffn 256, 128 positions; a version-1 manifest takes the
+    v1 defaults (kv heads = heads, theta 1e4, eps 1e-5, no experts)."""
+    mc = som.parse_manifest_core(open(os.path.join(GOLD, "manifest.som"), "rb").read())
+    assert (mc.vocab, mc.hidden, mc.n_layers, mc.heads, mc.ffn, mc.max_seq) == (256, 128, 4, 4, 256, 128)
+    assert (mc.kv_heads, mc.rope_theta, mc.n_experts, mc.experts_per_tok, mc.moe_ffn) == (4, 10000.0, 0, 0, 0)
+    assert mc.version == 1 and abs(mc.rms_eps - 1e-5) < 1e-12
+    # the reference's own index agrees with it: 4 layers of q/k/v at hidden x hidden, ffn_up at ffn x hidden
+    es = {e.name: e for e in som.parse_index(open(os.path.join(GOLD, "index.som"), "rb").read())}
+    for l in range(mc.n_layers):
+        assert es[f"L{l:02d}.attn_q"].shape == (mc.hidden, mc.hidden)
+        assert es[f"L{l:02d}.ffn_up"].shape in ((mc.ffn, mc.hidden), (mc.hidden, mc.ffn))
+    assert es["embed"].shape in ((mc.vocab, mc.hidden), (mc.hidden, mc.vocab))
