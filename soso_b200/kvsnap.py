@@ -1,0 +1,115 @@
+"""KV snapshots in the reference's portable format (crates/soso-llm-core/src/kvsnap.rs), so a
+prefix decoded here can be resumed by the reference and the other way round.
+
+Layout (little-endian): magic ``SOSOKV01``; a 32-byte profile (the fingerprint of weights,
+tokenizer and inference settings the snapshot belongs to); u32 token count n, u32 layer
+count, u32 hidden size; one u32 row width per layer; n u32 tokens; the f32 hidden vector;
+per layer the f16 K rows then the f16 V rows (n x width each, positions from 0); SHA-256 of
+everything before it.  ``decode`` makes the reference's checks in its order: length and
+identity first (nothing is allocated from an unchecked count), then the digest, then the
+row widths, token ids and finiteness.
+"""
+from __future__ import annotations
+
+import hashlib
+from dataclasses import dataclass
+
+import numpy as np
+
+MAGIC = b"SOSOKV01"
+HEADER = 8 + 32 + 4 + 4 + 4
+DIGEST = 32
+
+
+class KvSnapError(ValueError):
+    """kvsnap::Error: kind is "incompatible", "length", "integrity" or "non_finite"."""
+
+    def __init__(self, kind: str):
+        super().__init__(kind)
+        self.kind = kind
+
+
+@dataclass
+class Snapshot:
+    """Snapshot (kvsnap.rs:27-31): tokens, the hidden vector, per layer (K, V) f16 bits,
+    each n x width."""
+    tokens: np.ndarray
+    hidden: np.ndarray
+    layers: list
+
+
+def bytes_needed(tokens: int, hidden: int, dims) -> int:
+    """bytes_necesarios (kvsnap.rs:33-39)."""
+    return HEADER + 4 * tokens + 4 * len(dims) + 4 * hidden + 4 * tokens * int(sum(dims)) + DIGEST
+
+
+def _finite_f16(bits: np.ndarray) -> bool:
+    return not np.any((bits & 0x7C00) == 0x7C00)
+
+
+def encode(s: Snapshot, profile: bytes, dims, max_bytes: int) -> bytes:
+    """codificar (kvsnap.rs:43-72)."""
+    dims = [int(d) for d in dims]
+    tokens = np.asarray(s.tokens, dtype=np.uint32)
+    hidden = np.asarray(s.hidden, dtype=np.float32)
+    n = tokens.size
+    if len(profile) != 32:
+        raise KvSnapError("incompatible")
+    nbytes = bytes_needed(n, hidden.size, dims)
+    if n == 0 or n > 0xFFFFFFFF or hidden.size == 0 or not dims or len(s.layers) != len(dims) or nbytes > max_bytes:
+        raise KvSnapError("length")
+    if not np.all(np.isfinite(hidden)):
+        raise KvSnapError("non_finite")
+    rows = []
+    for (k, v), d in zip(s.layers, dims):
+        k = np.asarray(k, dtype=np.uint16).ravel()
+        v = np.asarray(v, dtype=np.uint16).ravel()
+        if d == 0 or d > 0xFFFFFFFF or k.size != n * d or v.size != n * d:
+            raise KvSnapError("length")
+        if not (_finite_f16(k) and _finite_f16(v)):
+            raise KvSnapError("non_finite")
+        rows += [k, v]
+    head = MAGIC + bytes(profile) + np.array([n, len(dims), hidden.size], "<u4").tobytes()
+    body = head + np.array(dims, "<u4").tobytes() + tokens.astype("<u4").tobytes() + hidden.astype("<f4").tobytes()
+    body += b"".join(r.astype("<u2").tobytes() for r in rows)
+    return body + hashlib.sha256(body).digest()
+
+
+def decode(data: bytes, profile: bytes, dims, max_tokens: int, vocab: int, hidden_dim: int,
+           max_bytes: int) -> Snapshot:
+    """decodificar (kvsnap.rs:76-125)."""
+    dims = [int(d) for d in dims]
+    b = bytes(data)
+    if len(b) < HEADER + DIGEST or len(b) > max_bytes:
+        raise KvSnapError("length")
+    if b[:8] != MAGIC or b[8:40] != bytes(profile):
+        raise KvSnapError("incompatible")
+    n, layers, hid = (int(x) for x in np.frombuffer(b, "<u4", 3, 40))
+    if (n == 0 or n > max_tokens or hidden_dim == 0 or not dims or layers != len(dims) or any(d == 0 for d in dims)
+            or hid != hidden_dim or bytes_needed(n, hidden_dim, dims) != len(b)):
+        raise KvSnapError("length")
+    end = len(b) - DIGEST
+    if hashlib.sha256(b[:end]).digest() != b[end:]:
+        raise KvSnapError("integrity")
+    off = HEADER
+    stored = np.frombuffer(b, "<u4", len(dims), off)
+    if [int(x) for x in stored] != dims:
+        raise KvSnapError("incompatible")
+    off += 4 * len(dims)
+    tokens = np.frombuffer(b, "<u4", n, off).astype(np.uint32)
+    if np.any(tokens >= vocab):
+        raise KvSnapError("incompatible")
+    off += 4 * n
+    hidden = np.frombuffer(b, "<f4", hidden_dim, off).astype(np.float32)
+    if not np.all(np.isfinite(hidden)):
+        raise KvSnapError("non_finite")
+    off += 4 * hidden_dim
+    out = []
+    for d in dims:
+        k = np.frombuffer(b, "<u2", n * d, off).astype(np.uint16)
+        v = np.frombuffer(b, "<u2", n * d, off + 2 * n * d).astype(np.uint16)
+        if not (_finite_f16(k) and _finite_f16(v)):
+            raise KvSnapError("non_finite")
+        out.append((k, v))
+        off += 4 * n * d
+    return Snapshot(tokens, hidden, out)
