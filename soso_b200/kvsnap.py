@@ -12,6 +12,7 @@ row widths, token ids and finiteness.
 from __future__ import annotations
 
 import hashlib
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -113,3 +114,68 @@ def decode(data: bytes, profile: bytes, dims, max_tokens: int, vocab: int, hidde
         out.append((k, v))
         off += 4 * n * d
     return Snapshot(tokens, hidden, out)
+
+
+def _field(h, b: bytes) -> None:
+    h.update(len(b).to_bytes(8, "little"))
+    h.update(b)
+
+
+def _file_sha256(path: str) -> bytes:
+    """hash_fichero (identidad_kv.rs:16-36): SHA-256 of a regular file that must not change
+    while it is read."""
+    st0 = os.stat(path)
+    if not os.path.isfile(path):
+        raise OSError(f"{path}: not a regular file")
+    h, total = hashlib.sha256(), 0
+    with open(path, "rb") as f:
+        while True:
+            chunk = f.read(1 << 20)
+            if not chunk:
+                break
+            total += len(chunk)
+            h.update(chunk)
+    st1 = os.stat(path)
+    if total != st0.st_size or st0.st_size != st1.st_size or st0.st_mtime_ns != st1.st_mtime_ns:
+        raise OSError(f"{path}: changed while its identity was computed")
+    return h.digest()
+
+
+def profile(model_dir: str, execution: bytes) -> bytes:
+    """The 32-byte snapshot profile of a model directory (identidad_kv::calcular,
+    crates/soso-llm-api/src/identidad_kv.rs:38-80): SHA-256 over length-prefixed fields --
+    the tag "soso-kv-perfil-v1", the execution identity (every option that changes the KV
+    values, and the engine version), then name and SHA-256 of manifest.som, index.som and
+    tokenizer.som, then name and SHA-256 of every shard the index names, in sorted order.
+    Shard paths that leave the shards directory are refused."""
+    from .som import parse_index
+    if not execution:
+        raise ValueError("missing execution identity")
+    h = hashlib.sha256()
+    _field(h, b"soso-kv-perfil-v1")
+    _field(h, bytes(execution))
+    with open(os.path.join(model_dir, "index.som"), "rb") as f:
+        index_bytes = f.read()
+    entries = parse_index(index_bytes)
+    for name in ("manifest.som", "index.som", "tokenizer.som"):
+        _field(h, name.encode())
+        digest = _file_sha256(os.path.join(model_dir, name))
+        if name == "index.som" and digest != hashlib.sha256(index_bytes).digest():
+            raise OSError("index.som changed while the identity was computed")
+        _field(h, digest)
+    shards = set()
+    for e in entries:
+        parts = e.shard.split("/")
+        if not e.shard or any(p in ("", ".", "..") for p in parts) or os.path.isabs(e.shard):
+            raise ValueError(f"invalid shard path {e.shard!r}")
+        shards.add(e.shard)
+    if not shards:
+        raise ValueError("index without shards")
+    root = os.path.realpath(os.path.join(model_dir, "shards"))
+    for name in sorted(shards, key=lambda n: n.encode()):
+        path = os.path.realpath(os.path.join(root, name))
+        if os.path.commonpath([root, path]) != root:
+            raise ValueError(f"shard {name!r} outside the shards directory")
+        _field(h, name.encode())
+        _field(h, _file_sha256(path))
+    return h.digest()

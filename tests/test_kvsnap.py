@@ -114,3 +114,40 @@ def test_round_trip_of_a_decode_prefix():
     assert np.array_equal(r.tokens, s.tokens) and np.array_equal(r.hidden, s.hidden)
     for (k, v), (k2, v2) in zip(layers, r.layers):
         assert np.array_equal(k, k2) and np.array_equal(v, v2)
+
+
+def test_profile_of_a_model_directory(tmp_path):
+    """identidad_kv::calcular: the fields in order, each length-prefixed; any byte of any
+    file it covers changes the profile; paths leaving shards/ are refused."""
+    import os
+    import oracle
+    gold = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "som_tiny")
+    from soso_b200 import som
+    idx = open(os.path.join(gold, "index.som"), "rb").read()
+    man = open(os.path.join(gold, "manifest.som"), "rb").read()
+    (tmp_path / "index.som").write_bytes(idx)
+    (tmp_path / "manifest.som").write_bytes(man)
+    (tmp_path / "tokenizer.som").write_bytes(b"tokenizer bytes")
+    (tmp_path / "shards").mkdir()
+    entries = som.parse_index(idx)
+    for sh in sorted({e.shard for e in entries}):
+        (tmp_path / "shards" / sh).write_bytes(oracle.pack_shard(sh.encode() * 3))
+    got = kvsnap.profile(str(tmp_path), b"engine v1, f16 KV")
+
+    def field(b):
+        return len(b).to_bytes(8, "little") + b
+    want = field(b"soso-kv-perfil-v1") + field(b"engine v1, f16 KV")
+    for name in ("manifest.som", "index.som", "tokenizer.som"):
+        want += field(name.encode()) + field(hashlib.sha256((tmp_path / name).read_bytes()).digest())
+    for sh in sorted({e.shard for e in entries}):
+        want += field(sh.encode()) + field(hashlib.sha256((tmp_path / "shards" / sh).read_bytes()).digest())
+    assert got == hashlib.sha256(want).digest()
+    assert kvsnap.profile(str(tmp_path), b"engine v2, f16 KV") != got
+    victim = tmp_path / "shards" / entries[5].shard
+    victim.write_bytes(victim.read_bytes()[:-1] + b"\x01")
+    assert kvsnap.profile(str(tmp_path), b"engine v1, f16 KV") != got
+    with pytest.raises(ValueError):
+        kvsnap.profile(str(tmp_path), b"")
+    (tmp_path / "index.som").write_bytes(oracle.serialize_index([(0, "w", "../manifest.som", 0, 4, (1,), 1, 0)]))
+    with pytest.raises(ValueError):
+        kvsnap.profile(str(tmp_path), b"engine v1")
