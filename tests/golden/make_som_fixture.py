@@ -8,7 +8,9 @@ import os
 import shutil
 import sys
 
-SRC = sys.argv[1] if len(sys.argv) > 1 else "/root/reference/rootfs/models/tiny"
+if len(sys.argv) != 2:
+    raise SystemExit("usage: make_som_fixture.py <reference checkout>/rootfs/models/tiny")
+SRC = sys.argv[1]
 DST = os.path.join(os.path.dirname(os.path.abspath(__file__)), "som_tiny")
 
 os.makedirs(DST, exist_ok=True)
