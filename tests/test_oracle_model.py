@@ -39,6 +39,24 @@ def test_tiny_mla_model_steps_are_finite_and_deterministic():
     assert np.array_equal(a, b) and all(np.isfinite(x).all() for x in la)
 
 
+def test_tiny_yarn_model_steps_are_deterministic_and_differ_from_plain_rope():
+    """The YaRN configuration takes the reference's CPU YaRN path (rope_neox_yarn on every
+    layer, layer.rs:1184-1189): deterministic, finite, and not the plain-RoPE model."""
+    import dataclasses
+    cfg = decode.TINY_YARN
+    model = decode.synth_model(cfg, "tiny_yarn")
+    prompt = synth.rng("prompt", "tiny_yarn2").integers(0, cfg.vocab, 4).astype(np.int32)
+    a, la = DenseOracle(cfg, model).greedy(prompt, 6)
+    b, lb = DenseOracle(cfg, model).greedy(prompt, 6)
+    assert np.array_equal(a, b) and all(np.array_equal(x, y) for x, y in zip(la, lb))
+    assert all(np.isfinite(x).all() for x in la)
+    _, lp = DenseOracle(dataclasses.replace(cfg, yarn=()), model).greedy(prompt, 6)
+    # position 0: q and k differ by the factor mscale only, and a softmax over one position is 1
+    # whatever the score, so the first logits agree; later positions attend differently
+    assert np.array_equal(la[0], lp[0])
+    assert not np.array_equal(la[-1], lp[-1])
+
+
 def test_mla_absorbed_form_equals_reexpansion():
     """The identity the MLA kernels rest on (f64, random data): q.(W_kn c) == (W_kn^T q).c and
     sum_t p_t (W_v c_t) == W_v (sum_t p_t c_t)."""
