@@ -409,3 +409,24 @@ def serialize_index(entries) -> bytes:
         body += offset.to_bytes(8, "little") + byte_len.to_bytes(8, "little") + len(shape).to_bytes(4, "little")
         body += b"".join(int(d).to_bytes(4, "little") for d in shape) + bytes([dtype, quant, 0, 0])
     return pack_som(body, 1, 64)
+
+
+def serialize_manifest_prefix(version: int, core: tuple, layers, prefetch, chat_template: str = "") -> bytes:
+    """Manifest::serialize up to the chat template (the mirror of Manifest::parse,
+    crates/sosomodel/src/manifest.rs:1021-1080), as a version-`version` .som file (4 <= version
+    <= 5): core = (name, vocab, hidden, n_layers, heads, ffn, max_seq, kv_heads, theta, eps,
+    n_experts, experts_per_tok, moe_ffn); layers = (attn kind, ffn kind, 13 u32) tuples;
+    prefetch = (layer, [shard names]) pairs."""
+    import struct
+    name, vocab, hidden, n_layers, heads, ffn, max_seq, kvh, theta, eps, ne, ept, mf = core
+    body = name.encode() + b"\0" + struct.pack("<6I", vocab, hidden, n_layers, heads, ffn, max_seq)
+    body += struct.pack("<Iff", kvh, theta, eps) + struct.pack("<3I", ne, ept, mf)
+    body += struct.pack("<I", len(layers))
+    for a, f, *vals in layers:
+        body += bytes([a, f, 0, 0]) + struct.pack("<13I", *vals)
+    body += struct.pack("<I", len(prefetch))
+    for layer, shards in prefetch:
+        body += struct.pack("<II", layer, len(shards)) + b"".join(n.encode() + b"\0" for n in shards)
+    if version >= 5:
+        body += chat_template.encode() + b"\0"
+    return pack_som(body, version, 64)

@@ -136,7 +136,10 @@ def parse_manifest_core(buf) -> ManifestCore:
     """The manifest's leading fields, with the reference's checks on them: heads and kv heads
     non-zero and, before version 4, hidden % heads == 0 and heads % kv_heads == 0."""
     version, body = payload(buf)
-    r = _Cursor(body.tobytes())
+    return _read_core(version, _Cursor(body.tobytes()))
+
+
+def _read_core(version: int, r: _Cursor) -> ManifestCore:
     name = r.cstr()
     vocab, hidden, n_layers, heads, ffn, max_seq = (r.u32() for _ in range(6))
     if version >= 2:
@@ -152,6 +155,70 @@ def parse_manifest_core(buf) -> ManifestCore:
         raise SomError("manifest: heads do not divide the hidden size / kv heads")
     return ManifestCore(version, name, vocab, hidden, n_layers, heads, ffn, max_seq, kv_heads, theta, eps, n_exp,
                         per_tok, moe_ffn)
+
+
+ATTN_KINDS = ("gqa", "mla", "kda", "gated", "gdn", "bidirectional", "cross")  # AttnKind, manifest.rs:10-35
+FFN_KINDS = ("dense", "moe", "latent_moe", "gelu_mlp")                          # FfnKind, manifest.rs:41-58
+
+
+@dataclass(frozen=True)
+class LayerSpec:
+    """One layer of a version >= 4 manifest (LayerSpec::parse, manifest.rs:346-368): the
+    attention and FFN kinds, then 13 u32 -- heads, kv heads, ffn width, the MLA ranks and
+    head widths, the expert counts and widths, flags."""
+    attn: str
+    ffn: str
+    heads: int
+    kv_heads: int
+    ffn_dim: int
+    kv_rank: int
+    q_rank: int
+    qk_rope: int
+    qk_nope: int
+    v_dim: int
+    n_experts: int
+    experts_per_tok: int
+    moe_ffn: int
+    n_shared: int
+    flags: int
+
+
+@dataclass(frozen=True)
+class ManifestPlan:
+    """The manifest up to the chat template (Manifest::parse, manifest.rs:1021-1080): the
+    leading fields, the per-layer specs (version >= 4; before that the globals describe every
+    layer), the per-layer prefetch lists of shard names, the chat template (version >= 5).
+    Version 6 and later extensions that follow are not read: ``rest`` holds their bytes."""
+    core: ManifestCore
+    layers: tuple
+    prefetch: tuple
+    chat_template: str
+    rest: bytes
+
+
+def parse_manifest(buf) -> ManifestPlan:
+    version, body = payload(buf)
+    r = _Cursor(body.tobytes())
+    core = _read_core(version, r)
+    layers = ()
+    if version >= 4:
+        n = r.u32()
+        if n != core.n_layers:
+            raise SomError("manifest: layer specs do not match the layer count")
+        specs = []
+        for _ in range(n):
+            a, f = r.u8(), r.u8()
+            r.take(2)
+            if a >= len(ATTN_KINDS) or f >= len(FFN_KINDS):
+                raise SomError("manifest: unknown attention or FFN kind")
+            specs.append(LayerSpec(ATTN_KINDS[a], FFN_KINDS[f], *(r.u32() for _ in range(13))))
+        layers = tuple(specs)
+    prefetch = []
+    for _ in range(r.u32()):
+        layer = r.u32()
+        prefetch.append((layer, tuple(r.cstr() for _ in range(r.u32()))))
+    template = r.cstr() if version >= 5 else ""
+    return ManifestPlan(core, layers, tuple(prefetch), template, r.b[r.off:])
 
 
 class SomModel:

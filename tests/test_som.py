@@ -169,3 +169,40 @@ def test_manifest_core_of_the_reference_tiny_model():
         assert es[f"L{l:02d}.attn_q"].shape == (mc.hidden, mc.hidden)
         assert es[f"L{l:02d}.ffn_up"].shape in ((mc.ffn, mc.hidden), (mc.hidden, mc.ffn))
     assert es["embed"].shape in ((mc.vocab, mc.hidden), (mc.hidden, mc.vocab))
+
+
+def test_manifest_prefetch_of_the_reference_tiny_model():
+    """The whole version-1 payload the reference wrote parses: the leading fields, then the
+    per-layer prefetch lists (layers 0-3, the five shard files each layer's tensors live in),
+    with no byte left over."""
+    m = som.parse_manifest(open(os.path.join(GOLD, "manifest.som"), "rb").read())
+    shards = json.load(open(os.path.join(GOLD, "shards.json")))
+    assert m.layers == () and m.chat_template == "" and m.rest == b""
+    assert [l for l, _ in m.prefetch] == [0, 1, 2, 3]
+    for l, names in m.prefetch:
+        assert names == tuple(f"L{l:02d}.{t}.tensor" for t in ("attn_q", "attn_k", "attn_v", "ffn_up", "ffn_down"))
+        assert all(n in shards for n in names)
+
+
+def test_manifest_layer_specs_round_trip():
+    """A version-5 manifest of a DeepSeek-V2-Lite-like model (an MLA layer with a dense FFN,
+    then MLA + MoE layers) written by the reference's serializer restated: the layer specs,
+    prefetch lists and chat template come back; unknown kinds and a spec count that differs
+    from the layer count are refused."""
+    import oracle
+    core = ("dsv2lite", 102400, 2048, 3, 16, 10944, 2048, 16, 1e4, 1e-6, 64, 6, 1408)
+    mla_dense = (1, 0, 16, 16, 10944, 512, 0, 64, 128, 128, 0, 0, 0, 0, 0)
+    mla_moe = (1, 1, 16, 16, 10944, 512, 0, 64, 128, 128, 64, 6, 1408, 2, 0)
+    pf = [(0, ["a.tensor", "b.tensor"]), (1, []), (2, ["c.tensor"])]
+    m = som.parse_manifest(oracle.serialize_manifest_prefix(5, core, [mla_dense, mla_moe, mla_moe], pf, "{{x}}"))
+    assert m.core.version == 5 and m.core.n_experts == 64 and abs(m.core.rms_eps - 1e-6) < 1e-12
+    assert [(l.attn, l.ffn) for l in m.layers] == [("mla", "dense"), ("mla", "moe"), ("mla", "moe")]
+    l1 = m.layers[1]
+    assert (l1.kv_rank, l1.qk_rope, l1.qk_nope, l1.v_dim, l1.n_experts, l1.experts_per_tok, l1.moe_ffn,
+            l1.n_shared) == (512, 64, 128, 128, 64, 6, 1408, 2)
+    assert m.prefetch == ((0, ("a.tensor", "b.tensor")), (1, ()), (2, ("c.tensor",)))
+    assert m.chat_template == "{{x}}" and m.rest == b""
+    with pytest.raises(som.SomError):
+        som.parse_manifest(oracle.serialize_manifest_prefix(5, core, [mla_dense, mla_moe, (9,) + mla_moe[1:]], pf))
+    with pytest.raises(som.SomError):
+        som.parse_manifest(oracle.serialize_manifest_prefix(5, core, [mla_dense, mla_moe], pf))
