@@ -3,8 +3,7 @@
  *
  * Drop-in boundary for demonodojo/soso's `trait GpuDispatch`
  * (crates/soso-llm-core/src/gpu.rs:338-737): a Rust `impl GpuDispatch` binds
- * these symbols with `extern "C"`.  Plain pointers and
- * sizes only.
+ * these symbols with `extern "C"`.  Plain pointers and sizes only.
  *
  * Two layers:
  *   sb_*   -- the GpuDispatch surface.  Host buffers, weights resident per key

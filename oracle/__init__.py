@@ -430,3 +430,28 @@ def serialize_manifest_prefix(version: int, core: tuple, layers, prefetch, chat_
     if version >= 5:
         body += chat_template.encode() + b"\0"
     return pack_som(body, version, 64)
+
+
+def serialize_manifest(version: int, core: tuple, layers, prefetch, chat_template: str = "", model_kind: int = 0,
+                       norm_kind: int = 0, audio=(0,) * 9, ext=None, kev=None) -> bytes:
+    """Manifest::serialize to its end (crates/sosomodel/src/manifest.rs:940-1019), as a
+    version-`version` .som file (5 <= version <= 9): the fields of serialize_manifest_prefix,
+    then the version-6 block (model kind u8, norm kind u8, u16 pad, nine u32 of AudioSpec),
+    the version-7 trailer ext = (embed_scale, logit_softcap, attn_scale, tied, [windows],
+    [rope thetas], yarn) with YaRN (factor f32, orig_ctx u32, beta_fast f32, beta_slow f32)
+    only from version 8, and the version-9 pointer head kev = (temperature f32, width u32)."""
+    import struct
+    out = serialize_manifest_prefix(min(version, 5), core, layers, prefetch, chat_template)
+    body = bytearray(out[24:24 + int.from_bytes(out[16:24], "little")])
+    if version >= 6:
+        body += bytes([model_kind, norm_kind, 0, 0]) + struct.pack("<9I", *audio)
+    if version >= 7:
+        es, cap, sc, tied, window, thetas, yarn = ext or (0.0, 0.0, 0.0, False, (), (), (0.0, 0, 0.0, 0.0))
+        body += struct.pack("<fffI", es, cap, sc, int(tied)) + struct.pack("<I", len(window))
+        body += b"".join(struct.pack("<I", w) for w in window) + struct.pack("<I", len(thetas))
+        body += b"".join(struct.pack("<f", t) for t in thetas)
+        if version >= 8:
+            body += struct.pack("<fIff", *yarn)
+    if version >= 9:
+        body += struct.pack("<fI", *kev)
+    return pack_som(bytes(body), version, 64)

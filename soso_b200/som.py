@@ -6,10 +6,11 @@ payload length) and the payload (lib.rs:70-104); a shard of version >= 2 puts it
 at byte 64 so that mmap'd weights are 64-byte aligned (index.rs:93-139).  The header
 checks and the CRC run in the library (``sb_som_payload``, ``sb_crc32c``).  The index is
 the tensor table (TensorIndex::parse, index.rs:61-91); a tensor's bytes are a slice of its
-shard's payload, handed to the decode plan (``SbMat`` views) without a copy.  Of the
-manifest (manifest.rs) the leading fields every version shares are read
-(``parse_manifest_core``: sizes, heads, RoPE theta, RMS eps, expert counts); the raw
-payload is kept for the rest.
+shard's payload, handed to the decode plan (``SbMat`` views) without a copy.  The
+manifest (manifest.rs) is read whole by ``parse_manifest`` (versions 1 to 9: the leading
+fields, per-layer specs, prefetch lists, chat template, model kind and audio spec, the
+extensions with YaRN, the pointer head); ``parse_manifest_core`` reads only the leading
+fields every version shares (sizes, heads, RoPE theta, RMS eps, expert counts).
 """
 from __future__ import annotations
 
@@ -81,6 +82,9 @@ class _Cursor:
 
     def u64(self) -> int:
         return int.from_bytes(self.take(8), "little")
+
+    def f32(self) -> float:
+        return float(np.frombuffer(self.take(4), "<f4")[0])
 
     def cstr(self) -> str:
         j = self.b.find(b"\0", self.off)
@@ -183,17 +187,47 @@ class LayerSpec:
     flags: int
 
 
+MODEL_KINDS = ("decoder", "asr_encoder_decoder", "decision")  # ModelKind, manifest.rs:80-95
+NORM_KINDS = ("rms", "layer")                                   # NormKind, manifest.rs:63-76
+
+
+@dataclass(frozen=True)
+class ManifestExt:
+    """Version 7 / 8 extensions (ManifestExt and YarnSpec, manifest.rs:111-161), every field
+    "no effect" by default: embedding scale (0 = none), logit soft cap (0 = none), attention
+    scale (0 = 1/sqrt(head_dim)), tied output matrix, per-layer window (0 = full) and RoPE base
+    (0 = the global one), and YaRN (factor, original context, beta_fast, beta_slow; active
+    when factor > 1 and the context > 0, YarnSpec::activa, manifest.rs:131-135)."""
+    embed_scale: float = 0.0
+    logit_softcap: float = 0.0
+    attn_scale: float = 0.0
+    tied_lm_head: bool = False
+    window: tuple = ()
+    rope_theta: tuple = ()
+    yarn: tuple = (0.0, 0, 0.0, 0.0)
+
+    def yarn_active(self) -> bool:
+        return self.yarn[0] > 1.0 and self.yarn[1] > 0
+
+
 @dataclass(frozen=True)
 class ManifestPlan:
-    """The manifest up to the chat template (Manifest::parse, manifest.rs:1021-1080): the
-    leading fields, the per-layer specs (version >= 4; before that the globals describe every
-    layer), the per-layer prefetch lists of shard names, the chat template (version >= 5).
-    Version 6 and later extensions that follow are not read: ``rest`` holds their bytes."""
+    """The whole manifest (Manifest::parse, manifest.rs:1021-1176): the leading fields, the
+    per-layer specs (version >= 4; before that the globals describe every layer), the
+    per-layer prefetch lists of shard names, the chat template (version >= 5), the model and
+    norm kinds and the audio spec (version >= 6), the extensions (versions 7 and 8) and the
+    pointer head (version 9: temperature, pointer width).  ``rest`` holds any bytes after
+    the last field the version defines (the reference ignores them)."""
     core: ManifestCore
     layers: tuple
     prefetch: tuple
     chat_template: str
     rest: bytes
+    model_kind: str = "decoder"
+    norm_kind: str = "rms"
+    audio: tuple = (0,) * 9
+    ext: ManifestExt = ManifestExt()
+    kev: tuple | None = None
 
 
 def parse_manifest(buf) -> ManifestPlan:
@@ -218,7 +252,29 @@ def parse_manifest(buf) -> ManifestPlan:
         layer = r.u32()
         prefetch.append((layer, tuple(r.cstr() for _ in range(r.u32()))))
     template = r.cstr() if version >= 5 else ""
-    return ManifestPlan(core, layers, tuple(prefetch), template, r.b[r.off:])
+    kinds = {}
+    if version >= 6:  # model kind, norm kind, u16 pad, AudioSpec (manifest.rs:1082-1100)
+        mk, nk = r.u8(), r.u8()
+        r.take(2)
+        if mk >= len(MODEL_KINDS) or nk >= len(NORM_KINDS):
+            raise SomError("manifest: unknown model or norm kind")
+        kinds = dict(model_kind=MODEL_KINDS[mk], norm_kind=NORM_KINDS[nk], audio=tuple(r.u32() for _ in range(9)))
+    if version >= 7:  # ManifestExt (manifest.rs:1101-1130): window / theta lists <= n_layers
+        es, cap, sc = r.f32(), r.f32(), r.f32()
+        tied = r.u32() != 0
+        n_w = r.u32()
+        if n_w > core.n_layers:
+            raise SomError("manifest: more windows than layers")
+        window = tuple(r.u32() for _ in range(n_w))
+        n_t = r.u32()
+        if n_t > core.n_layers:
+            raise SomError("manifest: more RoPE bases than layers")
+        thetas = tuple(r.f32() for _ in range(n_t))
+        yarn = (r.f32(), r.u32(), r.f32(), r.f32()) if version >= 8 else (0.0, 0, 0.0, 0.0)
+        kinds["ext"] = ManifestExt(es, cap, sc, tied, window, thetas, yarn)
+    if version >= 9:  # KevSpec (manifest.rs:1143-1150)
+        kinds["kev"] = (r.f32(), r.u32())
+    return ManifestPlan(core, layers, tuple(prefetch), template, r.b[r.off:], **kinds)
 
 
 class SomModel:

@@ -61,7 +61,31 @@ def _load(m: SomModel, path: str, ctx: int | None):
     kv_heads = s0.kv_heads or c.kv_heads
     if any((s.heads or c.heads, s.kv_heads or c.kv_heads, s.flags) != (heads, kv_heads, s0.flags) for s in specs):
         raise SomError("layers with different head counts or flags")
+    # Manifest::effective_head_dim (manifest.rs:453-465): the layer's v_head_dim when set
+    # (Qwen3-style GQA layers, MLA), else hidden / heads
+    head_dims = {(s.v_dim or c.hidden // heads) for s in specs}
+    if len(head_dims) != 1:
+        raise SomError(f"layers with different head widths {sorted(head_dims)}")
     moe = "moe" in ffns
+    dense_ffn = {(s.ffn_dim or c.ffn) for s, f in zip(specs, ffns) if f == "dense"}
+    if len(dense_ffn) > 1:
+        raise SomError(f"dense layers with different FFN widths {sorted(dense_ffn)}")
+    moe_specs = [s for s, f in zip(specs, ffns) if f == "moe"]
+    widths = {(s.n_experts or c.n_experts, s.experts_per_tok or c.experts_per_tok, s.moe_ffn or c.moe_ffn,
+               s.n_shared) for s in moe_specs}
+    if len(widths) > 1:
+        raise SomError("MoE layers with different expert counts or widths")
+    if mla and len({(s.q_rank, s.kv_rank, s.qk_nope, s.qk_rope, s.v_dim) for s in specs}) != 1:
+        raise SomError("MLA layers with different ranks or head widths")
+    ext = plan.ext
+    if ext.embed_scale not in (0.0, 1.0) or ext.logit_softcap != 0.0 or ext.attn_scale != 0.0:
+        raise SomError("manifest extensions (embedding scale, logit soft cap, attention scale) are not taken")
+    if any(ext.window) or any(t not in (0.0, c.rope_theta) for t in ext.rope_theta):
+        raise SomError("per-layer attention windows or RoPE bases are not taken")
+    if plan.model_kind != "decoder" or plan.norm_kind != "rms" or plan.kev is not None:
+        raise SomError(f"model kind {plan.model_kind} / norm {plan.norm_kind}: a decoder with RMSNorm is taken")
+    if ext.yarn_active() and mla:
+        raise SomError("YaRN on MLA layers is not taken")
     n_exp = (s0.n_experts or c.n_experts) if moe else 0
     n_shared = s0.n_shared if moe else 0
     if n_shared > 1:
@@ -108,11 +132,11 @@ def _load(m: SomModel, path: str, ctx: int | None):
             t[f"blk.{l}.attn_k_norm"] = _f32(m, L(l, "attn_k_norm"))
     t["output_norm"] = _f32(m, "output_norm")
     mat("token_embd", "embed", "token_embd")
-    mat("output", "lm_head" if "lm_head" in names else "embed", "output")
+    mat("output", "lm_head" if "lm_head" in names and not ext.tied_lm_head else "embed", "output")
 
-    head_dim = c.hidden // heads
+    head_dim = head_dims.pop()
     kw = dict(n_layers=c.n_layers, hidden=c.hidden, heads=heads, kv_heads=kv_heads, head_dim=head_dim,
-              ffn=(specs[0].ffn_dim or c.ffn) if "dense" in ffns else 0, vocab=c.vocab, ctx=ctx or c.max_seq,
+              ffn=dense_ffn.pop() if dense_ffn else 0, vocab=c.vocab, ctx=ctx or c.max_seq,
               theta=c.rope_theta, eps=c.rms_eps, neox=bool(s0.flags & FLAG_ROPE_NEOX),
               qkv_bias=any(k.endswith("qkv_bias") for k in t), qk_norm=bool(s0.flags & FLAG_QK_NORM) or any(k.endswith("attn_q_norm") for k in t),
               dtypes=dtypes)
@@ -123,6 +147,8 @@ def _load(m: SomModel, path: str, ctx: int | None):
         kw.update(n_exp=n_exp, top_k=s0.experts_per_tok or c.experts_per_tok, moe_ffn=s0.moe_ffn or c.moe_ffn,
                   first_moe=first_moe, shared_ffn=shared_ffn,
                   shared_gate=any(k.endswith("ffn_gate_inp_shexp") for k in t))
+    if ext.yarn_active():  # YaRN of every full-attention layer (manifest v8, YarnSpec)
+        kw.update(yarn=(float(ext.yarn[0]), int(ext.yarn[1]), float(ext.yarn[2]), float(ext.yarn[3])))
     return DenseConfig(**kw), t, m
 
 

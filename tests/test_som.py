@@ -206,3 +206,27 @@ def test_manifest_layer_specs_round_trip():
         som.parse_manifest(oracle.serialize_manifest_prefix(5, core, [mla_dense, mla_moe, (9,) + mla_moe[1:]], pf))
     with pytest.raises(som.SomError):
         som.parse_manifest(oracle.serialize_manifest_prefix(5, core, [mla_dense, mla_moe], pf))
+
+
+def test_manifest_versions_6_to_9_round_trip():
+    """The fields after the chat template (manifest.rs:1082-1150), written by the reference's
+    serializer restated: model and norm kinds with the audio spec (v6), the extensions (v7),
+    YaRN (v8) and the pointer head (v9) come back, with no byte left; more windows than
+    layers and an unknown model kind are refused."""
+    import oracle
+    core = ("m", 1024, 512, 2, 4, 1024, 160, 2, 1e4, 1e-6, 0, 0, 0)
+    specs = [(0, 0, 4, 2, 1024, 0, 0, 0, 0, 0, 0, 0, 0, 0, 8)] * 2
+    ext = (1.5, 30.0, 0.25, True, (0, 4096), (1e6, 0.0), (16.0, 8192, 32.0, 1.0))
+    m = som.parse_manifest(oracle.serialize_manifest(9, core, specs, [], "t", model_kind=2, norm_kind=1,
+                                                     audio=tuple(range(1, 10)), ext=ext, kev=(0.5, 256)))
+    assert (m.model_kind, m.norm_kind, m.audio) == ("decision", "layer", tuple(range(1, 10)))
+    assert m.ext.embed_scale == 1.5 and m.ext.logit_softcap == 30.0 and m.ext.attn_scale == 0.25
+    assert m.ext.tied_lm_head and m.ext.window == (0, 4096) and m.ext.rope_theta == (1e6, 0.0)
+    assert m.ext.yarn == (16.0, 8192, 32.0, 1.0) and m.ext.yarn_active()
+    assert m.kev == (0.5, 256) and m.rest == b""
+    m7 = som.parse_manifest(oracle.serialize_manifest(7, core, specs, [], ext=ext))
+    assert m7.ext.yarn == (0.0, 0, 0.0, 0.0) and not m7.ext.yarn_active() and m7.kev is None and m7.rest == b""
+    with pytest.raises(som.SomError):
+        som.parse_manifest(oracle.serialize_manifest(7, core, specs, [], ext=ext[:4] + ((0, 0, 0),) + ext[5:]))
+    with pytest.raises(som.SomError):
+        som.parse_manifest(oracle.serialize_manifest(6, core, specs, [], model_kind=3))

@@ -29,7 +29,7 @@ def som_name(key: str) -> str:
     return f"L{int(l):02d}.{rest}"
 
 
-def write_model(tmp, cfg, model, n_shared=0, version=5):
+def write_model(tmp, cfg, model, n_shared=0, version=5, v_dim=None, ext=None):
     (tmp / "shards").mkdir()
     entries = []
     H = cfg.hidden
@@ -61,12 +61,14 @@ def write_model(tmp, cfg, model, n_shared=0, version=5):
     for l in range(cfg.n_layers):
         moe = cfg.is_moe(l)
         specs.append((KIND_IDX["mla" if cfg.mla else "gqa"], KIND_IDX["moe" if moe else "dense"], cfg.heads,
-                      cfg.kv_heads, cfg.ffn, cfg.kv_rank, cfg.q_rank, cfg.qk_rope, cfg.qk_nope, cfg.v_dim,
+                      cfg.kv_heads, cfg.ffn, cfg.kv_rank, cfg.q_rank, cfg.qk_rope, cfg.qk_nope,
+                      cfg.v_dim if v_dim is None else v_dim,
                       cfg.n_exp if moe else 0, cfg.top_k if moe else 0, cfg.moe_ffn if moe else 0,
                       n_shared if moe else 0, flags))
     core = ("t", cfg.vocab, H, cfg.n_layers, cfg.heads, cfg.ffn, cfg.ctx, cfg.kv_heads, cfg.theta, cfg.eps,
             cfg.n_exp, cfg.top_k, cfg.moe_ffn)
-    (tmp / "manifest.som").write_bytes(oracle.serialize_manifest_prefix(version, core, specs, []))
+    (tmp / "manifest.som").write_bytes(oracle.serialize_manifest(version, core, specs, [], ext=ext) if version > 5
+                                       else oracle.serialize_manifest_prefix(version, core, specs, []))
     (tmp / "index.som").write_bytes(oracle.serialize_index(entries))
 
 
@@ -102,3 +104,40 @@ def test_refuses_what_the_engine_does_not_take(tmp_path):
     write_model(tmp_path, cfg, model, n_shared=2)  # two shared experts
     with pytest.raises(SomError):
         load_decode_model(str(tmp_path))
+
+
+def test_head_dim_from_the_layer_spec(tmp_path):
+    """Qwen3-style attention: head_dim 128 with hidden / heads = 64.  The layer spec's
+    v_head_dim gives the width (Manifest::effective_head_dim, manifest.rs:453-465), so the
+    q / k / v rows come back as heads x 128 and kv_heads x 128."""
+    cfg = dataclasses.replace(decode.TINY_MOE_NS, heads=8, kv_heads=2, head_dim=128)  # hidden 512 / 8 = 64
+    assert cfg.q_dim != cfg.hidden
+    model = decode.synth_model(cfg, "som_hd")
+    write_model(tmp_path, cfg, model, v_dim=cfg.head_dim)
+    got, t, m = load_decode_model(str(tmp_path))
+    try:
+        assert got.head_dim == 128 and got.q_dim == 1024 and got.kv_dim == 256
+        assert set(t) == set(model)
+    finally:
+        m.close()
+
+
+def test_manifest_extensions(tmp_path):
+    """A version-8 manifest with YaRN (factor 16 over a 64-position original context) loads
+    as the YaRN configuration; a version-7 manifest with a logit soft cap or a sliding
+    window, which the engine does not apply, is refused rather than loaded as something
+    else."""
+    cfg = decode.TINY
+    model = decode.synth_model(cfg, "som_ext")
+    yarn = (16.0, 64, 32.0, 1.0)
+    write_model(tmp_path, cfg, model, version=8, ext=(0.0, 0.0, 0.0, False, (), (), yarn))
+    got, t, m = load_decode_model(str(tmp_path))
+    m.close()
+    assert got.yarn == yarn
+    for i, (version, ext) in enumerate([(7, (0.0, 30.0, 0.0, False, (), (), (0.0, 0, 0.0, 0.0))),
+                                        (7, (0.0, 0.0, 0.0, False, (0, 512), (), (0.0, 0, 0.0, 0.0)))]):
+        d = tmp_path / f"r{i}"
+        d.mkdir()
+        write_model(d, cfg, model, version=version, ext=ext)
+        with pytest.raises(SomError):
+            load_decode_model(str(d))

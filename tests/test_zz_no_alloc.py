@@ -3,8 +3,11 @@
 For callers that cannot call cudaMalloc (fixed device-memory budgets, code that
 may run during a global-mode graph capture): sbk_matvec_q4k_noalloc takes its
 scratch from a fixed array in the library.  Checked here against the regular
-sbk_matvec on two calls in a row (the shared scratch must be left clean by the
-first call), and its size limit.  This file is collected last on purpose.
+sbk_matvec on two calls in a row of different shapes (the second call runs on
+the scratch the first one left behind), and its size limit.  Both entry points
+run the same kernel over the same grid and sum split rows in the same fixed
+order, so their outputs must agree bit for bit.  This file is collected last on
+purpose.
 """
 import ctypes
 
@@ -36,7 +39,9 @@ def test_noalloc_matches_regular_entry_point_twice():
         torch.cuda.synchronize()
         a, b = y_ref.cpu().numpy(), y_na.cpu().numpy()
         assert not np.isnan(b).any()
-        # same results as the regular entry point, within the matvec tolerance of the tests
+        # same results as the regular entry point: identical bits (same kernel, grid and
+        # summation order), and so within the matvec tolerance of the tests
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"call {call}: outputs differ"
         assert matvec_rel_err(b, a.astype(np.float64)) <= MATVEC_REL
         t = oracle.matvec_f64(DTYPE_Q4_K, w, rows, cols, x)
         ref = matvec_rel_err(oracle.matvec(DTYPE_Q4_K, w, rows, cols, x), t)
