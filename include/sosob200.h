@@ -70,12 +70,24 @@ typedef struct {
     float *out;
 } sb_matvec_op;
 
-/* Mirror of `GpuStats` (crates/soso-llm-core/src/gpu.rs:17-36), the fields this backend fills. */
+/* Mirror of `GpuStats` (crates/soso-llm-core/src/gpu.rs:17-36) without the cost model's
+ * per-stretch averages (ewma_ns / samples, sched.rs): launches, time and bytes of the host
+ * calls; the per-step transfers of the device-resident decode (embedding row up, position
+ * and control words up, logits down, new KV rows down, steps), as CudaGpu counts them
+ * (crates/soso-llm-api/src/cuda/decode.rs:790-937); expert-pool hits and misses (always 0:
+ * every expert is resident, nothing is streamed). */
 typedef struct {
     uint64_t launches;
     uint64_t total_ns;
     uint64_t bytes_up;
     uint64_t bytes_down;
+    uint64_t decode_embed_up;
+    uint64_t decode_control_up;
+    uint64_t decode_logits_down;
+    uint64_t decode_kv_down;
+    uint64_t decode_steps;
+    uint64_t stream_hits;
+    uint64_t stream_misses;
 } sb_stats;
 
 typedef struct sb_ctx sb_ctx;
@@ -185,6 +197,37 @@ int sb_decode_token(sb_ctx *ctx, const float *embed, size_t pos, float *logits, 
  * else the argmax of the previous step (runtime.rs:2021-2028).  tokens_out[i] = the
  * argmax produced at step i.  Needs plan.embed.  1 = done, 0 = not prepared, <0 = error. */
 int sb_decode_greedy(sb_ctx *ctx, const int32_t *prompt, size_t n_prompt, size_t pos, size_t n, int32_t *tokens_out);
+
+/* Mirror of `EstadoCapaDec` (gpu.rs:166-173) for the layers this backend runs (it has no
+ * Gated DeltaNet state): the host's copy of one layer's cache, rows from position 0 --
+ * K and V, f16 [rows][kv_heads*head_dim], of an attention layer (LayerKv, kv.rs:21-56), or
+ * the latent rows, f16 [rows][kv_rank], of an MLA layer in k with v NULL (kv.rs:293-315)
+ * -- and how many leading rows the device already holds. */
+typedef struct {
+    const uint16_t *k;
+    const uint16_t *v;
+    size_t *valid_rows;
+} sb_layer_state;
+/* `GpuDispatch::decode_subir_estado` (gpu.rs:664-668; CudaGpu's decode_subir_estado_impl,
+ * crates/soso-llm-api/src/cuda/decode.rs:629-660): for every layer the rows
+ * [min(*valid_rows, pos), pos) go up and *valid_rows becomes pos, so the next step can run
+ * at position pos.  An MLA layer's rope keys are formed again from its latent rows, exactly
+ * as the decode step forms them.  n_layers must be the plan's.  1 = done, 0 = not prepared
+ * (or a tensor-parallel engine), <0 = error. */
+int sb_decode_upload_state(sb_ctx *ctx, const sb_layer_state *layers, size_t n_layers, size_t pos);
+/* Rows [0, rows) of every layer's cache, in the sb_layer_state layout, down into k / v (v
+ * NULL for an MLA layer), and when hidden != NULL the hidden vector the last step left
+ * (f32[hidden], before the output norm: the Runtime::hidden that Runtime::exportar_kv stores
+ * with the rows, crates/soso-llm-core/src/runtime.rs:544-556).  The reference's
+ * decode_bajar_estado (gpu.rs:686-690) brings back only Gated DeltaNet state, because its
+ * host mirrors the KV rows through decode_token; steps run by sb_decode_greedy have no host
+ * mirror, so the rows come down here.  1 = done, 0 = not prepared (or tensor-parallel),
+ * <0 = error. */
+typedef struct {
+    uint16_t *k;
+    uint16_t *v;
+} sb_layer_rows;
+int sb_decode_download_state(sb_ctx *ctx, const sb_layer_rows *layers, size_t n_layers, size_t rows, float *hidden);
 
 /* ---- tensor-parallel groups (no counterpart in the reference, whose multi-machine mode
  * is a TCP layer pipeline, crates/soso-llm-core/src/pipeline.rs) -------------------------

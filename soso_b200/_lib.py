@@ -37,8 +37,17 @@ class SbkXSrc(ctypes.Structure):
 
 
 class SbStats(ctypes.Structure):
-    _fields_ = [("launches", ctypes.c_uint64), ("total_ns", ctypes.c_uint64), ("bytes_up", ctypes.c_uint64),
-                ("bytes_down", ctypes.c_uint64)]
+    _fields_ = [(n, ctypes.c_uint64) for n in ("launches", "total_ns", "bytes_up", "bytes_down", "decode_embed_up",
+                                               "decode_control_up", "decode_logits_down", "decode_kv_down",
+                                               "decode_steps", "stream_hits", "stream_misses")]
+
+
+class SbLayerState(ctypes.Structure):
+    _fields_ = [("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("valid_rows", ctypes.POINTER(ctypes.c_size_t))]
+
+
+class SbLayerRows(ctypes.Structure):
+    _fields_ = [("k", ctypes.c_void_p), ("v", ctypes.c_void_p)]
 
 
 class SbMat(ctypes.Structure):
@@ -92,6 +101,9 @@ SIGNATURES = {
     "sb_decode_finish": (ctypes.c_int, [ctypes.c_void_p]),
     "sb_decode_greedy": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), c_size, c_size, c_size,
                                         ctypes.POINTER(ctypes.c_int32)]),
+    "sb_decode_upload_state": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbLayerState), c_size, c_size]),
+    "sb_decode_download_state": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbLayerRows), c_size, c_size,
+                                                c_f32p]),
     "sbk_row_bytes": (c_size, [ctypes.c_uint8, c_size]),
     "sbk_q6k_pack": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p]),
     "sbk_q80_pad": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p]),

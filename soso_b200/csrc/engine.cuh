@@ -267,6 +267,7 @@ struct sb_engine {
     float eps = 0.0f;
     EngMat lm, emb;
     float *fnorm = nullptr;
+    float *hfin = nullptr;  // which residual buffer holds the hidden vector a step leaves (before the output norm)
     float *h = nullptr, *h2 = nullptr, *tmp = nullptr, *qkv = nullptr, *att = nullptr, *ob = nullptr, *gu = nullptr,
           *logits = nullptr;
     // MoE: router logits, chosen experts and weights, gate|up per choice, down outputs per choice
@@ -773,7 +774,10 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
         }
     }
     {
-        const sbk_xsrc xs = norm_src(e->fnorm, nullptr);
+        // the residual stream's last value goes to the other buffer on the way (the hidden
+        // vector of the step, Runtime::hidden)
+        const sbk_xsrc xs = norm_src(e->fnorm, ho);
+        e->hfin = ho;
         const EngMat *ms[1] = {&e->lm};
         float *ys[1] = {e->logits};
         const sb::grp::Wait w = wait_of(xprev);
@@ -1223,6 +1227,11 @@ extern "C" int sb_decode_token(sb_ctx *c, const float *embed, size_t pos, float 
     c->stats.launches += e->launches_per_token;
     c->stats.bytes_up += e->H * 4 + 4;
     c->stats.bytes_down += e->V * 4 + (kv_rows ? e->kv_rows_total * 2 : 0);
+    c->stats.decode_embed_up += e->H * 4;
+    c->stats.decode_control_up += 4;
+    c->stats.decode_logits_down += e->V * 4;
+    c->stats.decode_kv_down += kv_rows ? e->kv_rows_total * 2 : 0;
+    c->stats.decode_steps += 1;
     c->stats.total_ns += now_ns() - t0;
     return 1;
 }
@@ -1259,6 +1268,127 @@ extern "C" int sb_decode_greedy(sb_ctx *c, const int32_t *prompt, size_t n_promp
     if ((err = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", err);
     memcpy(tokens_out, hs + pb + 256, n * 4);
     c->stats.launches += e->launches_per_token * n;
+    c->stats.bytes_up += n_prompt * 4 + 16;
+    c->stats.bytes_down += n * 4;
+    c->stats.decode_control_up += n_prompt * 4 + 16;
+    c->stats.decode_steps += n;
+    c->stats.total_ns += now_ns() - t0;
+    return 1;
+}
+
+namespace sb {
+// f16 rows -> f32 (exact), for re-forming an MLA layer's rope keys from uploaded latent rows.
+__global__ void f16_to_f32_kernel(const uint16_t *__restrict__ src, float *__restrict__ dst, int n)
+{
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) dst[i] = f16_to_f32(src[i]);
+}
+}  // namespace sb
+
+extern "C" int sb_decode_upload_state(sb_ctx *c, const sb_layer_state *layers, size_t n_layers, size_t pos)
+{
+    if (!c) return fail("null context");
+    if (!layers) return fail("null argument");
+    std::lock_guard<std::mutex> lk(c->mu);
+    sb_engine *e = c->eng;
+    if (!e || e->tp || e->pending_finish) return 0;
+    if (n_layers != e->L.size()) return fail("sb_decode_upload_state: layer count differs from the plan's");
+    if (pos > e->ctx) return fail("sb_decode_upload_state: position beyond the prepared context");
+    cudaError_t err = cudaSetDevice(c->device);
+    if (err != cudaSuccess) return fail("cudaSetDevice", err);
+    const uint64_t t0 = now_ns();
+    int *tpos = nullptr;  // positions 0 .. pos-1 of the MLA rows to re-form
+    bool any_mla = false;
+    for (size_t l = 0; l < n_layers; l++) {
+        const sb_layer_state &st = layers[l];
+        const EngLayer &L = e->L[l];
+        if (!st.valid_rows || !st.k || (!L.mla && !st.v)) return fail("sb_decode_upload_state: layer without rows");
+        any_mla |= L.mla && std::min(*st.valid_rows, pos) < pos;
+    }
+    if (any_mla) {
+        std::vector<int> h(pos);
+        for (size_t t = 0; t < pos; t++) h[t] = (int)t;
+        if ((err = cudaMalloc(&tpos, std::max<size_t>(pos, 1) * 4)) != cudaSuccess) return fail("cudaMalloc", err);
+        if ((err = cudaMemcpy(tpos, h.data(), pos * 4, cudaMemcpyHostToDevice)) != cudaSuccess) {
+            cudaFree(tpos);
+            return fail("cudaMemcpy", err);
+        }
+    }
+    auto done = [&](int rc) {
+        if (tpos) {
+            cudaStreamSynchronize(c->stream);
+            cudaFree(tpos);
+        }
+        return rc;
+    };
+    for (size_t l = 0; l < n_layers; l++) {
+        const sb_layer_state &st = layers[l];
+        EngLayer &L = e->L[l];
+        const size_t v0 = std::min(*st.valid_rows, pos);
+        if (v0 < pos) {
+            const size_t w = L.mla ? L.kv_rank : L.kvd;  // f16 values a row
+            uint16_t *kd = L.mla ? L.latent : L.kc;
+            if ((err = cudaMemcpyAsync(kd + v0 * w, st.k + v0 * w, (pos - v0) * w * 2, cudaMemcpyHostToDevice,
+                                       c->stream)) != cudaSuccess)
+                return done(fail("cudaMemcpyAsync(k rows)", err));
+            if (!L.mla && (err = cudaMemcpyAsync(L.vc + v0 * w, st.v + v0 * w, (pos - v0) * w * 2,
+                                                 cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
+                return done(fail("cudaMemcpyAsync(v rows)", err));
+            c->stats.bytes_up += (pos - v0) * w * (L.mla ? 2 : 4);
+            if (L.mla) {
+                // the absorb step of each row again, on its own latent row (f16 -> f32 -> f16 is
+                // exact, so the cache keeps its bits): the row's rope keys as the step formed them
+                if ((err = cudaMemsetAsync(e->mq, 0, L.heads * (L.qk_nope + L.qk_rope) * 4, c->stream)) != cudaSuccess)
+                    return done(fail("cudaMemsetAsync", err));
+                for (size_t t = v0; t < pos; t++) {
+                    sb::f16_to_f32_kernel<<<1, 512, 0, c->stream>>>(L.latent + t * L.kv_rank, e->mc, (int)L.kv_rank);
+                    if ((err = cudaGetLastError()) != cudaSuccess) return done(fail("f16 rows launch", err));
+                    const int rc = sbk_mla_absorb(e->mq, e->mc, L.k_up.w, L.k_up.dt, L.latent, L.krope, e->mqt, e->mqr,
+                                                  tpos + t, L.heads, L.kvh, L.kv_rank, L.qk_nope, L.qk_rope, e->ctx,
+                                                  L.theta, 0, c->stream);
+                    if (rc) return done(fail("sbk_mla_absorb (state upload) failed (" + std::to_string(rc) + ")"));
+                    c->stats.launches += 2;
+                }
+            }
+        }
+    }
+    if ((err = cudaStreamSynchronize(c->stream)) != cudaSuccess) return done(fail("state upload", err));
+    for (size_t l = 0; l < n_layers; l++) *layers[l].valid_rows = pos;
+    c->stats.total_ns += now_ns() - t0;
+    return done(1);
+}
+
+extern "C" int sb_decode_download_state(sb_ctx *c, const sb_layer_rows *layers, size_t n_layers, size_t rows,
+                                        float *hidden)
+{
+    if (!c) return fail("null context");
+    if (!layers && n_layers) return fail("null argument");
+    std::lock_guard<std::mutex> lk(c->mu);
+    sb_engine *e = c->eng;
+    if (!e || e->tp || e->pending_finish) return 0;
+    if (n_layers != e->L.size()) return fail("sb_decode_download_state: layer count differs from the plan's");
+    if (rows > e->ctx) return fail("sb_decode_download_state: more rows than the prepared context");
+    cudaError_t err = cudaSetDevice(c->device);
+    if (err != cudaSuccess) return fail("cudaSetDevice", err);
+    const uint64_t t0 = now_ns();
+    for (size_t l = 0; l < n_layers; l++) {
+        const EngLayer &L = e->L[l];
+        const size_t w = L.mla ? L.kv_rank : L.kvd;
+        if (!layers[l].k || (!L.mla && !layers[l].v)) return fail("sb_decode_download_state: layer without rows");
+        if (!rows) continue;
+        if ((err = cudaMemcpyAsync(layers[l].k, L.mla ? L.latent : L.kc, rows * w * 2, cudaMemcpyDeviceToHost,
+                                   c->stream)) != cudaSuccess)
+            return fail("cudaMemcpyAsync(k rows)", err);
+        if (!L.mla && (err = cudaMemcpyAsync(layers[l].v, L.vc, rows * w * 2, cudaMemcpyDeviceToHost, c->stream)) !=
+                          cudaSuccess)
+            return fail("cudaMemcpyAsync(v rows)", err);
+        c->stats.bytes_down += rows * w * (L.mla ? 2 : 4);
+    }
+    if (hidden) {
+        if ((err = cudaMemcpyAsync(hidden, e->hfin, e->H * 4, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
+            return fail("cudaMemcpyAsync(hidden)", err);
+        c->stats.bytes_down += e->H * 4;
+    }
+    if ((err = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("state download", err);
     c->stats.total_ns += now_ns() - t0;
     return 1;
 }

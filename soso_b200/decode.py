@@ -14,8 +14,8 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import synth
-from ._lib import (SbDecodePlan, SbLayerPlan, SbMat, SbMlaPlan, SbMoePlan, SbView, SbError, c_f32p, c_u8p,
-                   last_error, lib)
+from ._lib import (SbDecodePlan, SbLayerPlan, SbLayerRows, SbLayerState, SbMat, SbMlaPlan, SbMoePlan, SbView,
+                   SbError, c_f32p, c_u8p, last_error, lib)
 from .formats import DTYPE_Q4_K, DTYPE_Q6_K, DTYPE_Q8_0
 
 
@@ -333,6 +333,46 @@ class DecodeSession:
         if rc != 1:
             raise SbError(f"sb_decode_greedy returned {rc}: {last_error()}")
         return out
+
+    def download_state(self, rows: int, hidden: bool = True):
+        """sb_decode_download_state: per layer (K, V) f16 bits [rows][kv_dim] (an MLA layer's
+        latent rows and None), and the hidden vector the last step left (before the output
+        norm)."""
+        cfg = self.cfg
+        out = [(np.empty((rows, cfg.kv_dim), np.uint16), None if cfg.mla else np.empty((rows, cfg.kv_dim), np.uint16))
+               for _ in range(cfg.n_layers)]
+        arr = (SbLayerRows * cfg.n_layers)()
+        for l, (k, v) in enumerate(out):
+            arr[l].k = k.ctypes.data
+            arr[l].v = v.ctypes.data if v is not None else None
+        h = np.empty(cfg.hidden, np.float32) if hidden else None
+        rc = lib().sb_decode_download_state(self.ctx, arr, cfg.n_layers, rows, _f32(h))
+        if rc != 1:
+            raise SbError(f"sb_decode_download_state returned {rc}: {last_error()}")
+        return out, h
+
+    def upload_state(self, layers, pos: int, valid=None) -> list:
+        """sb_decode_upload_state: layers = per layer (K, V) f16 bits with at least pos rows
+        (V None for MLA); valid = rows the device already holds per layer (default 0).
+        Returns the new valid-row counts (pos each)."""
+        cfg = self.cfg
+        arr = (SbLayerState * cfg.n_layers)()
+        counts = (ctypes.c_size_t * cfg.n_layers)(*(valid or [0] * cfg.n_layers))
+        keep = []
+        for l, (k, v) in enumerate(layers):
+            k = np.ascontiguousarray(k, dtype=np.uint16)
+            keep.append(k)
+            arr[l].k = k.ctypes.data
+            if v is not None:
+                v = np.ascontiguousarray(v, dtype=np.uint16)
+                keep.append(v)
+                arr[l].v = v.ctypes.data
+            arr[l].valid_rows = ctypes.cast(ctypes.addressof(counts) + l * ctypes.sizeof(ctypes.c_size_t),
+                                            ctypes.POINTER(ctypes.c_size_t))
+        rc = lib().sb_decode_upload_state(self.ctx, arr, cfg.n_layers, pos)
+        if rc != 1:
+            raise SbError(f"sb_decode_upload_state returned {rc}: {last_error()}")
+        return list(counts)
 
     def close(self):
         if self._own and self.ctx:

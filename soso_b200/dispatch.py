@@ -44,11 +44,20 @@ class MatvecOp:
 
 @dataclass
 class GpuStats:
-    """The `GpuStats` fields this backend fills (gpu.rs:17-36)."""
+    """The `GpuStats` fields this backend fills (gpu.rs:17-36): host-call launches, time and
+    bytes; the per-step transfers of the device-resident decode; expert-pool hits / misses
+    (always 0: every expert is resident)."""
     launches: int = 0
     total_ns: int = 0
     bytes_up: int = 0
     bytes_down: int = 0
+    decode_embed_up: int = 0
+    decode_control_up: int = 0
+    decode_logits_down: int = 0
+    decode_kv_down: int = 0
+    decode_steps: int = 0
+    stream_hits: int = 0
+    stream_misses: int = 0
 
 
 def _f32_arg(a: np.ndarray, n: int, name: str) -> np.ndarray:
@@ -159,7 +168,7 @@ class CudaGpu:
     def stats(self) -> GpuStats:
         s = SbStats()
         self._L.sb_get_stats(self._h, ctypes.byref(s))
-        return GpuStats(s.launches, s.total_ns, s.bytes_up, s.bytes_down)
+        return GpuStats(*(getattr(s, f) for f, _ in SbStats._fields_))
 
 
 def dtype_ofrecible(dtype: int) -> bool:

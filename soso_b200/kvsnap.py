@@ -179,3 +179,37 @@ def profile(model_dir: str, execution: bytes) -> bytes:
         _field(h, name.encode())
         _field(h, _file_sha256(path))
     return h.digest()
+
+
+def dims_of(cfg) -> list:
+    """The per-layer row widths a snapshot of this configuration carries (dimensiones_snapshot,
+    crates/soso-llm-core/src/runtime.rs:527-541): kv_heads x head_dim of every GQA layer.
+    The reference refuses MLA latent caches (and MoE models run with a planner), so do we."""
+    if getattr(cfg, "mla", False):
+        raise KvSnapError("incompatible")
+    return [cfg.kv_dim] * cfg.n_layers
+
+
+def export_session(session, tokens, profile: bytes, max_bytes: int) -> bytes:
+    """Runtime::exportar_kv (runtime.rs:544-556) over a decode session on the device: the
+    cached tokens are `tokens` (one per decoded position, from 0); the rows of those
+    positions of every layer and the hidden vector the last step left come down from the
+    device (sb_decode_download_state) and are encoded."""
+    tokens = np.asarray(tokens, dtype=np.uint32)
+    cfg = session.cfg
+    if tokens.size == 0 or tokens.size > cfg.ctx:
+        raise KvSnapError("incompatible")
+    layers, hidden = session.download_state(int(tokens.size))
+    return encode(Snapshot(tokens, hidden, [(k, v) for k, v in layers]), profile, dims_of(cfg), max_bytes)
+
+
+def import_session(session, image: bytes, profile: bytes, max_bytes: int) -> Snapshot:
+    """Runtime::importar_kv (runtime.rs:558-580) into a decode session on the device: every
+    check of `decode` first (a refused image changes nothing), then the rows go up
+    (sb_decode_upload_state at position len(tokens)); returns the snapshot, whose tokens and
+    hidden vector the caller keeps as the runtime does."""
+    cfg = session.cfg
+    snap = decode(image, profile, dims_of(cfg), cfg.ctx, cfg.vocab, cfg.hidden, max_bytes)
+    n = int(snap.tokens.size)
+    session.upload_state([(k.reshape(n, -1), v.reshape(n, -1)) for k, v in snap.layers], n)
+    return snap
