@@ -16,16 +16,23 @@ import oracle
 
 
 class DenseOracle:
-    def __init__(self, cfg, model: dict):
+    """threads > 0: the matvecs run the reference's AVX2 kernels (gemm.rs:806-894, restated in
+    cpu_baseline.c) on that many row strips (parallel.rs:22-31) -- the path the reference
+    takes on an AVX2 host -- instead of the scalar kernels; for models of full size."""
+
+    def __init__(self, cfg, model: dict, threads: int = 0):
         self.cfg = cfg
         self.m = model
+        self.threads = threads
         self.k = [np.zeros((cfg.ctx, cfg.kv_dim), np.uint16) for _ in range(cfg.n_layers)]
         self.v = [np.zeros((cfg.ctx, cfg.kv_dim), np.uint16) for _ in range(cfg.n_layers)]
         self._embd = None
-        self._mla_kv = [dict() for _ in range(cfg.n_layers)]  # (layer) t -> expanded (k, v) of latent row t
+        self._mla_kv = [dict() for _ in range(cfg.n_layers)]  # (layer) expanded K / V rows of the latent rows
 
     def _mv(self, name: str, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
         dt = self.cfg.dtypes[name.split(".")[-1]]  # by tensor kind (experts share their kind's dtype)
+        if self.threads:
+            return oracle.cpu_matvec(dt, self.m[name], rows, cols, x, threads=self.threads)
         return oracle.matvec(dt, self.m[name], rows, cols, x)
 
     def embed(self, token: int) -> np.ndarray:
@@ -115,28 +122,31 @@ class DenseOracle:
             q[s0:s0 + cfg.qk_rope] = oracle.rope_llama_n(q[s0:s0 + cfg.qk_rope], pos, cfg.theta, cfg.qk_rope)
         self.k[l][pos] = oracle.f32_to_f16_array(c)  # append_mla_latent (kv.rs:293-315)
         cache = self._mla_kv[l]
-        for t in range(pos + 1):
-            if t not in cache:
-                ct = self.k[l][t].view(np.float16).astype(np.float32)
-                kf = self._mv(p + "attn_k_up", ct, cfg.kv_heads * qk, cfg.kv_rank)
-                for g in range(cfg.kv_heads):
-                    s0 = g * qk + cfg.qk_nope
-                    kf[s0:s0 + cfg.qk_rope] = oracle.rope_llama_n(kf[s0:s0 + cfg.qk_rope], t, cfg.theta, cfg.qk_rope)
-                vf = self._mv(p + "attn_v_up", ct, cfg.kv_heads * cfg.v_dim, cfg.kv_rank)
-                cache[t] = (kf, vf)
+        if not cache:  # expanded rows of every cached position: K [ctx][kv_heads][qk], V [ctx][kv_heads][v_dim]
+            cache["k"] = np.zeros((cfg.ctx, cfg.kv_heads, qk), np.float32)
+            cache["v"] = np.zeros((cfg.ctx, cfg.kv_heads, cfg.v_dim), np.float32)
+            cache["n"] = 0
+        for t in range(cache["n"], pos + 1):
+            ct = self.k[l][t].view(np.float16).astype(np.float32)
+            kf = self._mv(p + "attn_k_up", ct, cfg.kv_heads * qk, cfg.kv_rank)
+            for g in range(cfg.kv_heads):
+                s0 = g * qk + cfg.qk_nope
+                kf[s0:s0 + cfg.qk_rope] = oracle.rope_llama_n(kf[s0:s0 + cfg.qk_rope], t, cfg.theta, cfg.qk_rope)
+            cache["k"][t] = kf.reshape(cfg.kv_heads, qk)
+            cache["v"][t] = self._mv(p + "attn_v_up", ct, cfg.kv_heads * cfg.v_dim, cfg.kv_rank).reshape(
+                cfg.kv_heads, cfg.v_dim)
+        cache["n"] = pos + 1
+        # softmax(q . k_t / sqrt(qk)) . v_t per head over t = 0..pos (attention_decode_mla_latent,
+        # attn.rs:306-404), f32 throughout
         inv = np.float32(1.0 / np.sqrt(np.float32(qk)))
         att = np.zeros(cfg.heads * cfg.v_dim, np.float32)
         for hh in range(cfg.heads):
             g = hh // group
             qh = q[hh * qk:(hh + 1) * qk]
-            lg = np.array([np.float32(np.dot(qh, cache[t][0][g * qk:(g + 1) * qk])) * inv for t in range(pos + 1)],
-                          np.float32)
+            lg = (cache["k"][:pos + 1, g, :] @ qh).astype(np.float32) * inv
             lg = np.exp(lg - lg.max()).astype(np.float32)
             lg = (lg / lg.sum()).astype(np.float32)
-            out = np.zeros(cfg.v_dim, np.float32)
-            for t in range(pos + 1):
-                out = (out + lg[t] * cache[t][1][g * cfg.v_dim:(g + 1) * cfg.v_dim]).astype(np.float32)
-            att[hh * cfg.v_dim:(hh + 1) * cfg.v_dim] = out
+            att[hh * cfg.v_dim:(hh + 1) * cfg.v_dim] = (lg @ cache["v"][:pos + 1, g, :]).astype(np.float32)
         return self._mv(p + "attn_output", att, H, cfg.q_dim)
 
     def _moe(self, p: str, xn: np.ndarray, l: int) -> np.ndarray:
