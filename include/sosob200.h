@@ -228,6 +228,29 @@ typedef struct {
     uint16_t *v;
 } sb_layer_rows;
 int sb_decode_download_state(sb_ctx *ctx, const sb_layer_rows *layers, size_t n_layers, size_t rows, float *hidden);
+/* The experts every MoE layer chose at the last decode step, in layer order, top_k IDs each
+ * in rank order (the order topk_softmax ranks them, crates/soso-llm-core/src/gemm.rs:77-91):
+ * a trace for checking a step against a CPU run, where a near-tie of two router logits can
+ * let the two sides pick different experts.  No counterpart in the reference.  idx holds
+ * at least the sum of the MoE layers' top_k.  1 = written, 0 = no decode prepared, <0 = error. */
+int sb_decode_routes(sb_ctx *ctx, int32_t *idx, size_t n);
+
+/* Block prefill of a prompt on the prepared model: tokens[0..n) at positions pos0 .. pos0+n-1
+ * through every layer at once -- the reference's prompt path over forward_layer_block
+ * (crates/soso-llm-core/src/layer.rs:1433) with its GPU offload of the block's matrix
+ * products, expert groups and attention (GpuDispatch::matmul / expertos_bloque /
+ * router_topk / atencion_prefill, gpu.rs:443-530) -- then the logits of the last token
+ * (runtime.rs:1976-2019).  Every matrix product is a tcgen05 GEMM over the n tokens with
+ * f16 operands and f32 sums (the precision of the reference's f16 mma.sync prefill,
+ * lxdde/ports/nouveau/matvec_iq.cu:731-816); a MoE layer groups the block's (token,
+ * choice) pairs by expert on the device and runs one grouped GEMM over every routed
+ * expert.  The KV caches of those positions are filled where the decode step puts them:
+ * decoding goes on with sb_decode_greedy / sb_decode_token at pos0 + n.  logits
+ * (host f32[vocab]) and next (the argmax, ties to the last index) may be NULL.  Needs
+ * plan.embed.  1 = done, 0 = not prepared, a tensor-parallel engine, or a plan with a
+ * layer the block path does not take (weight formats other than Q4_K / Q8_0 for the
+ * attention, router and expert matrices, widths not multiples of 64), <0 = error. */
+int sb_decode_prefill(sb_ctx *ctx, const int32_t *tokens, size_t n, size_t pos0, float *logits, int32_t *next);
 
 /* ---- tensor-parallel groups (no counterpart in the reference, whose multi-machine mode
  * is a TCP layer pipeline, crates/soso-llm-core/src/pipeline.rs) -------------------------

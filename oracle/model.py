@@ -43,12 +43,18 @@ class DenseOracle:
         row = self.m["token_embd"][token * rb:(token + 1) * rb]
         return oracle.dequant(cfg.dtypes["token_embd"], row, cfg.hidden).astype(np.float32)
 
-    def step(self, h: np.ndarray, pos: int) -> np.ndarray:
-        """One token from its embedding row at `pos`; returns the logits (and keeps K/V)."""
+    def step(self, h: np.ndarray, pos: int, routes: dict | None = None) -> np.ndarray:
+        """One token from its embedding row at `pos`; returns the logits (and keeps K/V).
+        routes: layer -> the experts another run chose there (rank order); where they differ
+        from this run's top-k the step follows them and records (layer, router logit gap)
+        in route_ties, so a comparison can tell a near-tie from a wrong choice."""
         cfg, m = self.cfg, self.m
+        self.force_routes = routes
+        self.route_ties = []
         H, qd, kvd, hd = cfg.hidden, cfg.q_dim, cfg.kv_dim, cfg.head_dim
         group = cfg.heads // cfg.kv_heads
         h = np.array(h, np.float32, copy=True)
+        self.route_gaps = []  # per MoE layer of this step
         for l in range(cfg.n_layers):
             p = f"blk.{l}."
             if getattr(cfg, "mla", False):
@@ -157,7 +163,27 @@ class DenseOracle:
         cfg, m, H = self.cfg, self.m, self.cfg.hidden
         logits = self._mv(p + "ffn_gate_inp", xn, cfg.n_exp, H)
         self.last_route = oracle.topk_softmax(logits, cfg.top_k)
+        # the routing margin: router logit gap between the k-th and (k+1)-th expert (a gap
+        # near the two sides' rounding difference lets either pick the other expert)
+        srt = np.sort(logits.astype(np.float64))
+        self.route_gaps.append(float(srt[-cfg.top_k] - srt[-cfg.top_k - 1]) if cfg.top_k < cfg.n_exp else np.inf)
         idx, wts = self.last_route
+        forced = self.force_routes.get(l) if self.force_routes else None
+        if forced is not None and set(int(e) for e in forced) != set(int(e) for e in idx):
+            # the other side chose differently: record how far its choice is from this side's
+            # k-th expert (router logit gap; a near-tie lets rounding pick either), and follow
+            # it, with this side's probabilities renormalised over the chosen set
+            lg = logits.astype(np.float64)
+            kth = float(min(lg[int(e)] for e in idx))
+            gap = max(kth - float(lg[int(e)]) for e in forced if int(e) not in set(int(i) for i in idx))
+            self.route_ties.append((l, gap))
+            m_ = np.float32(logits.max())
+            ex = np.exp((logits - m_).astype(np.float32)).astype(np.float32)
+            prob = (ex / np.float32(ex.sum(dtype=np.float32))).astype(np.float32)
+            idx = np.asarray(forced, np.int32)
+            w = prob[idx]
+            wts = (w / np.float32(w.sum(dtype=np.float32))).astype(np.float32)
+            self.last_route = (idx, wts)
         acc = np.zeros(H, np.float32)
         for e, w in zip(idx, wts):
             q = f"{p}E{int(e):03d}."

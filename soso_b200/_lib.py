@@ -104,6 +104,9 @@ SIGNATURES = {
     "sb_decode_upload_state": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbLayerState), c_size, c_size]),
     "sb_decode_download_state": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbLayerRows), c_size, c_size,
                                                 c_f32p]),
+    "sb_decode_routes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), c_size]),
+    "sb_decode_prefill": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), c_size, c_size, c_f32p,
+                                         ctypes.POINTER(ctypes.c_int32)]),
     "sbk_row_bytes": (c_size, [ctypes.c_uint8, c_size]),
     "sbk_q6k_pack": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p]),
     "sbk_q80_pad": (ctypes.c_int, [ctypes.c_void_p, c_size, c_size, ctypes.c_void_p, ctypes.c_void_p]),

@@ -544,13 +544,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1) attn_decode_kernel(const __gri
 // ------------------------------------------------------------------- router
 // gemm::topk_softmax (crates/soso-llm-core/src/gemm.rs:62-91): softmax over all
 // experts, stable sort by weight descending (ties keep the lower index first),
-// keep k, renormalise by their sum (in rank order).  One CTA.
+// keep k, renormalise by their sum (in rank order).  One CTA per token: CTA b routes
+// logits row b into idx / wts row b.
 __global__ void router_topk_kernel(const float *__restrict__ logits, int n, int k, int *__restrict__ idx,
                                    float *__restrict__ wts)
 {
     extern __shared__ float p[];
     __shared__ float red[32];
     griddep_wait();
+    logits += (size_t)blockIdx.x * n;
+    idx += (size_t)blockIdx.x * k;
+    wts += (size_t)blockIdx.x * k;
     const int tid = threadIdx.x;
     float m = -INFINITY;
     for (int i = tid; i < n; i += blockDim.x) m = fmaxf(m, logits[i]);
@@ -750,13 +754,15 @@ __global__ void argmax_gather_kernel(GatherArgs a)
 
 // -------------------------------------------------------------------- embed
 // Runtime::embed_token (runtime.rs:787-802): one row of the embedding table,
-// dequantised exactly (dequant.rs decoders).  Token id from device memory.
+// dequantised exactly (dequant.rs decoders).  Token id from device memory; CTA b
+// makes row b of out from tok[b] (one CTA: one token).
 __global__ void embed_kernel(const uint8_t *__restrict__ table, int dtype, int vocab, int h, const int *tok,
                              float *__restrict__ out)
 {
     griddep_launch();  // the next kernel reads the row only after its own wait
     griddep_wait();
-    const int t = *tok;
+    const int t = tok[blockIdx.x];
+    out += (size_t)blockIdx.x * h;
     if (t < 0 || t >= vocab) {
         if (threadIdx.x == 0) set_dev_error(0x63u);
         return;

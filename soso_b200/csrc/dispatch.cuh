@@ -60,6 +60,7 @@ constexpr size_t PREFILL_MIN_TOKENS = 16;  // sb_matmul: from this many tokens o
 
 struct sb_engine;                  // whole-token decode state (engine.cuh)
 void sb_engine_free(sb_engine *e);
+void sb_pf_free(void *p);          // its block-prefill state (prefill_engine.cuh)
 
 struct sb_ctx {
     int device = 0;

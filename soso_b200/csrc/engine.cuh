@@ -101,6 +101,7 @@ struct RouteArgs {
     int lo, hi;             // resident experts [lo, hi)
     int pairs;              // gate|up launches run one gate/up pair matrix per choice
     int xw;                 // floats between exchange slots: the down of choice r publishes at r * xw
+    int *trace;             // [k]: the chosen experts' IDs in rank order, kept for sb_decode_routes
 };
 
 __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
         for (int r = 0; r < a.k; r++) {
             a.wts[r] = t > 0.0f ? topw[r] / t : topw[r];
             a.idx[r] = topi[r];
+            a.trace[r] = topi[r];
         }
         if (a.has_shared) a.wts[a.k] = sg;
         int mo = 0;
@@ -273,6 +275,8 @@ struct sb_engine {
     // MoE: router logits, chosen experts and weights, gate|up per choice, down outputs per choice
     float *rlog = nullptr, *wts = nullptr, *egu = nullptr, *ys = nullptr;
     int *ridx = nullptr;
+    int *rtrace = nullptr;  // [layers][16]: the experts each MoE layer chose at the last step
+    void *pf = nullptr;     // block prefill state (prefill_engine.cuh)
     size_t moe_slots = 0, moe_ffn = 0, n_exp_max = 0;
     // MLA: q_down | kv_down outputs, q_up output, absorbed query, roped q slice, latent sums
     float *mcq = nullptr, *mc = nullptr, *mq = nullptr, *mqt = nullptr, *mqr = nullptr, *mcbar = nullptr;
@@ -303,6 +307,7 @@ struct sb_engine {
     }
     ~sb_engine()
     {
+        if (pf) sb_pf_free(pf);
         if (g_tok) cudaGraphExecDestroy(g_tok);
         if (g_greedy) cudaGraphExecDestroy(g_greedy);
         for (void *p : allocs) cudaFree(p);
@@ -572,7 +577,7 @@ int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, boo
     }
     sb::RouteArgs ra{e->rlog, (int)L.n_exp, (int)L.top_k, e->ridx, e->wts, L.sg, hc, L.nf, e->eps, (int)e->H,
                      L.has_sh ? 1 : 0, L.gu_b, L.dn_b, L.sel, L.maps, (int)L.ex_lo, (int)L.ex_hi, L.ex_pairs ? 1 : 0,
-                     sb::grp::XW};
+                     sb::grp::XW, e->rtrace + (&L - e->L.data()) * 16};
     if ((rc = sb::launch_k(sb::route_kernel, dim3(1), dim3(256), 0, 1, s, ra))) return rc;
     *n += 1;
     rc = gdt == SB_DTYPE_Q4_K ? launch_moe_batch<sb::tcmv::Q4K>(L.gu_b, L.sel, L.gu_smem, s)
@@ -1116,6 +1121,7 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         e->rlog = fbuf(e->n_exp_max);
         e->wts = fbuf(e->moe_slots);
         e->ridx = (int *)fbuf(e->moe_slots);
+        e->rtrace = (int *)fbuf(e->L.size() * 16);  // top_k <= 16 (checked above)
         e->moe_ffn = (e->moe_ffn + 63) & ~(size_t)63;
         e->egu = fbuf(2 * e->moe_slots * e->moe_ffn);
         e->ys = fbuf(e->moe_slots * H);
@@ -1390,5 +1396,28 @@ extern "C" int sb_decode_download_state(sb_ctx *c, const sb_layer_rows *layers, 
     }
     if ((err = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("state download", err);
     c->stats.total_ns += now_ns() - t0;
+    return 1;
+}
+
+extern "C" int sb_decode_routes(sb_ctx *c, int32_t *idx, size_t n)
+{
+    if (!c) return fail("null context");
+    if (!idx) return fail("null argument");
+    std::lock_guard<std::mutex> lk(c->mu);
+    sb_engine *e = c->eng;
+    if (!e || !e->rtrace) return 0;
+    size_t need = 0;
+    for (auto &L : e->L) need += L.moe ? L.top_k : 0;
+    if (n < need) return fail("sb_decode_routes: output shorter than the MoE layers' choices");
+    cudaError_t err = cudaSetDevice(c->device);
+    if (err != cudaSuccess) return fail("cudaSetDevice", err);
+    std::vector<int> t(e->L.size() * 16);
+    if ((err = cudaMemcpyAsync(t.data(), e->rtrace, t.size() * 4, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess ||
+        (err = cudaStreamSynchronize(c->stream)) != cudaSuccess)
+        return fail("sb_decode_routes", err);
+    size_t o = 0;
+    for (size_t l = 0; l < e->L.size(); l++)
+        if (e->L[l].moe)
+            for (size_t r = 0; r < e->L[l].top_k; r++) idx[o++] = t[l * 16 + r];
     return 1;
 }

@@ -1,0 +1,372 @@
+// pgemm.cuh -- the block-prefill GEMM on the sm_100a tensor cores, driven by a table of
+// output tiles so that one launch serves several matrices that read the same input (q|k|v,
+// q_down|kv_down) or the token groups of many experts (a MoE layer: every expert's rows
+// times the tokens routed to it).
+//
+//   Y[t][yoff + r] = sum_k X[t][k] . W_m[r][k]     for the tiles (m, rows, tokens) listed
+//
+// Replaces the reference's block-prefill GEMMs: iq_matmul_mma / iq_gateup_mma /
+// iq_down_mma (lxdde/ports/nouveau/matvec_iq.cu:731-816, :949-970; f16 mma.sync on weights
+// decoded to shared memory) and the grouped expert kernels mo_gateup_grp / mo_down_grp
+// (gemma_capa.cu:1174, :1223), behind GpuDispatch::matmul / expertos_bloque
+// (crates/soso-llm-core/src/gpu.rs:443-475).
+//
+// The machinery is the dense GEMM's (prefill.cuh): tcgen05.mma kind::f16 with the D tile
+// [128 weight rows x BN tokens] f32 in tensor memory, A = weight rows dequantised by eight
+// warps into 128-byte-swizzled K-major shared memory, B = X (16-bit, written by an earlier
+// kernel) by TMA with the 128-byte swizzle, raw weight blocks by TMA, a 3-stage ring.
+// New here: the weight formats are traits (Q4_K, and Q8_0 with 16-byte-aligned rows), the
+// token tile BN is 64 or 256 (a routed expert sees ~n*top_k/n_exp tokens), every CTA finds
+// its tile in a table (device-written for MoE: CTAs past the table's count leave at once),
+// and the epilogue stores f32, f16 (the next GEMM's operand) or, for a matrix of gate / up
+// 16-row group pairs, silu(gate) * up as f16 (swiglu_inplace, gemm.rs:210-226).
+#pragma once
+#include "prefill.cuh"
+
+namespace sb {
+namespace pg {
+
+constexpr int BM = pf::BM, BK = pf::BK, NST = pf::NST, NRAW = pf::NRAW, NDQ = pf::NDQ, THREADS = pf::THREADS;
+
+// One output tile: weight map `map` and output descriptor `out` of the launch's tables,
+// weight rows [row0, row0 + 128), X / Y rows [tok0, tok0 + ntok) with ntok <= BN.
+struct __align__(16) Tile {
+    int map, out, row0, tok0, ntok, pad0, pad1, pad2;
+};
+
+enum { OUT_F32 = 0, OUT_F16 = 1, OUT_SWIGLU16 = 2 };
+
+// Where matrix m's rows go: Y row t (a token, or a routed (token, choice) pair) at element
+// yoff of a row of ldy elements.  OUT_SWIGLU16: the matrix's rows are 16-row groups of gate
+// then up rows (its feature f = 16 (r / 32) + r % 16), Y gets rows / 2 features.
+struct __align__(16) Out {
+    void *y;
+    int rows, ldy, yoff, mode;
+};
+
+struct Launch {
+    const CUtensorMap *maps;  // weight maps (device memory, 64-byte aligned), by Tile::map
+    const Out *outs;          // output descriptors, by Tile::out
+    const Tile *tiles;        // [grid]
+    const int *n_tiles;       // tiles in use (device, written by an earlier kernel), or null: all
+    int cols;                 // K, the same for every matrix: a multiple of 64
+};
+
+// Weight formats: RAWB bytes of one row per 256 columns (the raw tile of a 4-stage block
+// column), and the dequantisation of 32 weights (columns 32h.. of stage p of the column)
+// into one 128-byte swizzled row of the stage tile.
+struct FQ4K {
+    static constexpr int RAWB = 144;  // one Q4_K block (crates/sosomodel/src/layout.rs:63-64)
+    template <bool F16>
+    __device__ __forceinline__ static void half16(const uint8_t *raw, int p, int h, uint8_t *row, int r)
+    {
+        pf::q4k_half_to_16<F16>(raw, p, h, row, r);
+    }
+};
+
+struct FQ80 {
+    static constexpr int RAWB = 288;  // eight .som Q8_0 blocks: f32 scale + 32 i8 (layout.rs:57-59)
+    // block 2p + h of the column: w_i = scale * q_i (dequant.rs:74-102), rounded once
+    template <bool F16>
+    __device__ __forceinline__ static void half16(const uint8_t *raw, int p, int h, uint8_t *row, int r)
+    {
+        const uint8_t *b = raw + (2 * p + h) * 36;
+        const float sc = *reinterpret_cast<const float *>(b);
+        const uint32_t *q = reinterpret_cast<const uint32_t *>(b + 4);
+#pragma unroll
+        for (int c = 0; c < 4; c++) {  // 8 weights -> one 16-byte chunk of the swizzled row
+            const uint32_t w0 = q[2 * c], w1 = q[2 * c + 1];
+            auto v = [&](uint32_t w, int k) { return sc * (float)(int8_t)(w >> (8 * k)); };
+            const uint4 out = make_uint4(pf::pack16<F16>(v(w0, 0), v(w0, 1)), pf::pack16<F16>(v(w0, 2), v(w0, 3)),
+                                         pf::pack16<F16>(v(w1, 0), v(w1, 1)), pf::pack16<F16>(v(w1, 2), v(w1, 3)));
+            const int chunk = 4 * h + c;
+            *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = out;
+        }
+    }
+};
+
+template <class W, int BN>
+struct Lay {
+    static constexpr int X_BYTES = BN * BK * 2;
+    static constexpr int W_BYTES = BM * BK * 2;
+    static constexpr int RAW_BYTES = BM * W::RAWB;
+    static constexpr size_t SMEM = 1024 + (size_t)NST * (X_BYTES + W_BYTES) + (size_t)NRAW * RAW_BYTES + 256;
+};
+
+template <int BN, bool F16>
+__host__ __device__ constexpr uint32_t idesc()
+{
+    return (1u << 4) | ((F16 ? 0u : 1u) << 7) | ((F16 ? 0u : 1u) << 10) | ((uint32_t)(BN >> 3) << 17) |
+           ((uint32_t)(BM >> 4) << 24);
+}
+
+template <int BN, bool F16>
+__device__ __forceinline__ void mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc)
+{
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc<BN, F16>()), "r"(acc)
+        : "memory");
+}
+
+template <class W, int BN, bool F16>
+__global__ void __launch_bounds__(THREADS, 1) pg_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const Launch a)
+{
+    using L = Lay<W, BN>;
+    griddep_wait();  // the tile table and X are written by earlier kernels
+    const int nt = a.n_tiles ? *a.n_tiles : (int)gridDim.x;
+    if ((int)blockIdx.x >= nt) {
+        griddep_launch();
+        return;
+    }
+    const Tile t = a.tiles[blockIdx.x];
+    const CUtensorMap *wmap = a.maps + t.map;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *b = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sx = b, *sw = b + NST * L::X_BYTES, *sraw = sw + NST * L::W_BYTES;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sraw + NRAW * L::RAW_BYTES);
+    uint64_t *x_full = bar, *w_full = bar + NST, *st_empty = bar + 2 * NST, *raw_full = bar + 3 * NST,
+             *raw_empty = bar + 3 * NST + NRAW, *acc_full = bar + 3 * NST + 2 * NRAW;
+    uint32_t *tmem_addr = reinterpret_cast<uint32_t *>(acc_full + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KS = a.cols / BK;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NST; i++) {
+            tcmv::mbar_init(&x_full[i], 1);
+            tcmv::mbar_init(&w_full[i], NDQ);
+            tcmv::mbar_init(&st_empty[i], 1);
+        }
+        for (int i = 0; i < NRAW; i++) {
+            tcmv::mbar_init(&raw_full[i], 1);
+            tcmv::mbar_init(&raw_empty[i], NDQ);
+        }
+        tcmv::mbar_init(acc_full, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(wmap) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         tcmv::smem_u32(tmem_addr)),
+                     "r"(BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    pf::fence_before_sync();
+    __syncthreads();
+    pf::fence_after_sync();
+    const uint32_t tmem = *tmem_addr;
+    bool failed = false;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint64_t pol = tcmv::l2_evict_first();
+            for (int ks = 0; ks < KS && !failed; ks++) {
+                const int st = ks % NST;
+                if (ks % 4 == 0) {  // a new raw block column
+                    const int rk = ks / 4, rs = rk % NRAW;
+                    if (rk >= NRAW && !tcmv::mbar_wait(&raw_empty[rs], ((rk / NRAW) - 1) & 1, pf::WAIT)) {
+                        failed = true;
+                        break;
+                    }
+                    tcmv::mbar_expect_tx_arrive(&raw_full[rs], (unsigned)L::RAW_BYTES);
+                    tcmv::tma_load_2d(sraw + rs * L::RAW_BYTES, wmap, rk * (W::RAWB / 8), t.row0, &raw_full[rs], pol);
+                }
+                if (ks >= NST && !tcmv::mbar_wait(&st_empty[st], ((ks / NST) - 1) & 1, pf::WAIT)) {
+                    failed = true;
+                    break;
+                }
+                tcmv::mbar_expect_tx_arrive(&x_full[st], (unsigned)L::X_BYTES);
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+                    "{%2, %3}], [%4];" ::"r"(tcmv::smem_u32(sx + st * L::X_BYTES)),
+                    "l"(&xmap), "r"(ks * BK), "r"(t.tok0), "r"(tcmv::smem_u32(&x_full[st]))
+                    : "memory");
+            }
+            if (failed) set_dev_error(0x81u);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int ks = 0; ks < KS; ks++) {
+                const int st = ks % NST;
+                const unsigned par = (ks / NST) & 1;
+                if (!tcmv::mbar_wait(&x_full[st], par, pf::WAIT) || !tcmv::mbar_wait(&w_full[st], par, pf::WAIT)) {
+                    failed = true;
+                    set_dev_error(0x82u);
+                    break;
+                }
+                pf::fence_after_sync();
+                const uint64_t ad = pf::sw128_desc(sw + st * L::W_BYTES), bd = pf::sw128_desc(sx + st * L::X_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; kk++)  // K16 slices: 32 bytes along the swizzled row
+                    mma<BN, F16>(tmem, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), (ks | kk) ? 1u : 0u);
+                pf::mma_commit(&st_empty[st]);
+            }
+            pf::mma_commit(acc_full);  // completion of every MMA issued above (even after a failure)
+        }
+        __syncwarp();
+    } else {
+        // dequantisers: thread t takes weight row t % 128, half t / 128 of every stage
+        const int r = (threadIdx.x - 64) & (BM - 1), hh = (threadIdx.x - 64) / BM;
+        for (int ks = 0; ks < KS && !failed; ks++) {
+            const int st = ks % NST, rk = ks / 4, rs = rk % NRAW, p = ks % 4;
+            if (p == 0 && !tcmv::mbar_wait(&raw_full[rs], (rk / NRAW) & 1, pf::WAIT)) failed = true;
+            if (!failed && ks >= NST && !tcmv::mbar_wait(&st_empty[st], ((ks / NST) - 1) & 1, pf::WAIT)) failed = true;
+            if (failed) {
+                set_dev_error(0x83u);
+                break;
+            }
+            W::template half16<F16>(sraw + rs * L::RAW_BYTES + r * W::RAWB, p, hh, sw + st * L::W_BYTES + r * 128, r);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
+            __syncwarp();
+            if (lane == 0) {
+                tcmv::mbar_arrive(&w_full[st]);
+                if (p == 3 || ks == KS - 1) tcmv::mbar_arrive(&raw_empty[rs]);
+            }
+        }
+        // epilogue: the accumulators of this warp's 32 lanes (weight rows)
+        if (tcmv::mbar_wait(acc_full, 0, pf::WAIT)) {
+            pf::fence_after_sync();
+            const Out o = a.outs[t.out];
+            const int q = warp & 3, rloc = 32 * q + lane, row = t.row0 + rloc;
+            const int c0 = ((warp - 2) / 4) * (BN / 2);  // the two warps of a lane quadrant split the tokens
+            for (int c = c0; c < c0 + BN / 2; c += 32) {
+                float v[32];
+                pf::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+                if (o.mode == OUT_SWIGLU16) {
+                    // lanes 0-15: gate rows of 16 features, lanes 16-31: their up rows
+                    const int f = ((t.row0 + 32 * q) >> 5) * 16 + (lane & 15);
+                    __half *y = reinterpret_cast<__half *>(o.y);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const float u = __shfl_down_sync(0xffffffffu, v[i], 16);
+                        const int tok = c + i;
+                        if (lane < 16 && tok < t.ntok && 2 * f < o.rows) {
+                            const float g = v[i];
+                            y[(size_t)(t.tok0 + tok) * o.ldy + o.yoff + f] = __float2half_rn(g / (1.0f + expf(-g)) * u);
+                        }
+                    }
+                } else if (row < o.rows) {
+                    if (o.mode == OUT_F16) {
+                        __half *y = reinterpret_cast<__half *>(o.y);
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            if (c + i < t.ntok) y[(size_t)(t.tok0 + c + i) * o.ldy + o.yoff + row] = __float2half_rn(v[i]);
+                    } else {
+                        float *y = reinterpret_cast<float *>(o.y);
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            if (c + i < t.ntok) y[(size_t)(t.tok0 + c + i) * o.ldy + o.yoff + row] = v[i];
+                    }
+                }
+            }
+        } else {
+            set_dev_error(0x84u);
+        }
+    }
+    pf::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        pf::fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+    }
+    griddep_launch();
+}
+
+// ------------------------------------------------------------------ host side
+
+// Weight map of a matrix: [rows][row bytes / 8] u64, box = 128 rows x one raw block column.
+// Q4_K rows as they are; Q8_0 rows padded to 16 bytes (SB_DTYPE_Q8_0_R).
+inline int make_wmap(CUtensorMap *m, uint8_t dtype, const void *w, int rows, int cols)
+{
+    tcmv::EncodeTiledFn fn = tcmv::encode_fn();
+    if (!fn) return -6;
+    cuuint64_t rb;
+    cuuint32_t bw;
+    if (dtype == SB_DTYPE_Q4_K) {
+        if (cols % 256) return -1;
+        rb = (cuuint64_t)(cols / 256) * 144, bw = FQ4K::RAWB / 8;
+    } else if (dtype == SB_DTYPE_Q8_0_R || (dtype == SB_DTYPE_Q8_0 && cols % 128 == 0)) {
+        if (cols % 32 || cols < 256) return -1;
+        rb = (cuuint64_t)(((size_t)cols / 32 * 36 + 15) & ~(size_t)15), bw = FQ80::RAWB / 8;
+    } else {
+        return -5;
+    }
+    if (((uintptr_t)w & 15) || rows < 1) return -2;
+    cuuint64_t dims[2] = {rb / 8, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {rb};
+    cuuint32_t box[2] = {bw, (cuuint32_t)BM};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -7;
+}
+
+// X map: nrows x cols 16-bit operands (row-major), box = BN rows x 64 columns, 128-byte swizzle.
+inline int make_xmap(CUtensorMap *m, const void *x, int nrows, int cols, int bn, bool f16)
+{
+    tcmv::EncodeTiledFn fn = tcmv::encode_fn();
+    if (!fn) return -6;
+    if (cols % BK || ((uintptr_t)x & 15) || nrows < 1) return -1;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)nrows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)bn};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                    const_cast<void *>(x), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -7;
+}
+
+template <class W, int BN, bool F16>
+inline int launch_t(const CUtensorMap &xmap, const Launch &a, int grid, int pdl, cudaStream_t s)
+{
+    static size_t smem_rec[64];
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        const int rc = tcmv::ensure_smem(pg_gemm_kernel<W, BN, F16>, Lay<W, BN>::SMEM, smem_rec);
+        if (rc) return rc;
+    }
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3((unsigned)grid);
+    c.blockDim = dim3(THREADS);
+    c.dynamicSmemBytes = Lay<W, BN>::SMEM;
+    c.stream = s;
+    c.attrs = at;
+    c.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&c, pg_gemm_kernel<W, BN, F16>, xmap, a) == cudaSuccess ? 0 : -4;
+}
+
+// One launch of the table-driven GEMM: weight format by dtype (Q4_K or padded Q8_0), BN 64
+// or 256, f16 operands (prec SBK_PREC_F16) or bf16.  grid = the table's length.
+inline int launch(uint8_t dtype, int bn, int prec, const CUtensorMap &xmap, const Launch &a, int grid, int pdl,
+                  cudaStream_t s)
+{
+    if (grid < 1 || a.cols % BK || a.cols < 256) return -1;
+    const bool q4k = dtype == SB_DTYPE_Q4_K, f16 = prec == SBK_PREC_F16;
+    if (!q4k && dtype != SB_DTYPE_Q8_0_R && dtype != SB_DTYPE_Q8_0) return -5;
+    if (q4k && a.cols % 256) return -1;
+#define PG_CASE(W, BN_, F)                                                                                             \
+    if ((bn == BN_) && (f16 == F)) return launch_t<W, BN_, F>(xmap, a, grid, pdl, s)
+    if (q4k) {
+        PG_CASE(FQ4K, 64, true);
+        PG_CASE(FQ4K, 256, true);
+        PG_CASE(FQ4K, 64, false);
+        PG_CASE(FQ4K, 256, false);
+    } else {
+        PG_CASE(FQ80, 64, true);
+        PG_CASE(FQ80, 256, true);
+        PG_CASE(FQ80, 64, false);
+        PG_CASE(FQ80, 256, false);
+    }
+#undef PG_CASE
+    return -1;
+}
+
+}  // namespace pg
+}  // namespace sb

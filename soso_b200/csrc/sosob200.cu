@@ -9,4 +9,6 @@
 #include "engine.cuh"
 #include "noalloc.cuh"
 #include "prefill.cuh"
+#include "block.cuh"
+#include "prefill_engine.cuh"
 #include "som.cuh"

@@ -374,6 +374,28 @@ class DecodeSession:
             raise SbError(f"sb_decode_upload_state returned {rc}: {last_error()}")
         return list(counts)
 
+    def prefill(self, tokens, pos: int = 0, logits: bool = True):
+        """sb_decode_prefill: the block of tokens at positions pos.., all layers at once on
+        the tensor cores; returns (logits of the last token or None, its argmax)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        lg = np.empty(self.cfg.vocab, np.float32) if logits else None
+        nxt = ctypes.c_int32(-1)
+        rc = lib().sb_decode_prefill(self.ctx, t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), t.size, pos,
+                                     _f32(lg), ctypes.byref(nxt))
+        if rc != 1:
+            raise SbError(f"sb_decode_prefill returned {rc}: {last_error()}")
+        return lg, int(nxt.value)
+
+    def routes(self) -> dict:
+        """sb_decode_routes: layer -> the experts its router chose at the last step (rank order)."""
+        cfg = self.cfg
+        moe = [l for l in range(cfg.n_layers) if cfg.is_moe(l)]
+        out = np.empty(max(1, len(moe) * cfg.top_k), np.int32)
+        rc = lib().sb_decode_routes(self.ctx, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), out.size)
+        if rc != 1:
+            raise SbError(f"sb_decode_routes returned {rc}: {last_error()}")
+        return {l: out[i * cfg.top_k:(i + 1) * cfg.top_k].copy() for i, l in enumerate(moe)}
+
     def close(self):
         if self._own and self.ctx:
             lib().sb_destroy(self.ctx)
