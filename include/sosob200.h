@@ -111,6 +111,48 @@ int sb_matmul(sb_ctx *ctx, const char *key, const sb_view *w, size_t rows, size_
 int sb_matvec_batch(sb_ctx *ctx, sb_matvec_op *ops, size_t nops, uint8_t *done);
 /* `GpuDispatch::rmsnorm` (gpu.rs:733-736): x *= rsqrt(mean(x^2) + eps) * w, in place. */
 int sb_rmsnorm(sb_ctx *ctx, float *x, const float *w, size_t n, float eps);
+/* `GpuDispatch::gemma_subir` (gpu.rs:364-368): make a tensor resident under its key (quantized
+ * matrices in their matvec form, F32 as they are) for the block calls below.  1 = resident,
+ * 0 = declined (dtype, shape; remembered), <0 = error. */
+int sb_upload(sb_ctx *ctx, const char *key, const sb_view *w, size_t rows, size_t cols);
+/* `GpuDispatch::router_topk` (gpu.rs:477-494): for each of n tokens xs[t] (h floats), router
+ * logits against the f32 matrix w [n_exp x h] (resident under key), softmax, stable top-k
+ * and renormalisation (topk_softmax, gemm.rs:62-91); idx / wts [n x top_k] in rank order.
+ * 1 = done, 0 = declined, <0 = error. */
+int sb_router_topk(sb_ctx *ctx, const char *key, const float *w, const float *xs, size_t n, size_t h, size_t n_exp,
+                   size_t top_k, int32_t *idx, float *wts);
+/* Mirror of `ExpertoBloque` (gpu.rs:175-187): one expert of a block, its three matrices
+ * (keys of ffn_gate, ffn_up, ffn_down; a view may be NULL or of dtype 0 when the caller
+ * expects the tensor resident already), the tokens (indices within the block) that chose
+ * it, whether it is a shared expert, and for each of those tokens its weight's index
+ * token * top_k + rank in `weights`. */
+typedef struct {
+    const char *keys[3];
+    const sb_view *views[3];
+    const uint32_t *tokens;
+    size_t n_tokens;
+    int shared;
+    const uint32_t *dests;
+} sb_expert_block;
+/* `GpuDispatch::expertos_bloque` (gpu.rs:457-475): the experts of a block of n tokens
+ * (xs [n x h]): per expert, for its tokens, down(silu(gate . x) * (up . x)) with gate / up
+ * [ffn x h] and down [h x ffn]; sum [n x h] receives per token the weighted sum, in rank
+ * order, of the experts resolved here (done[i] = 1), the others are the caller's.  The
+ * experts' tokens are grouped on the device: one tensor-core GEMM launch for every gate and
+ * up, one for the downs (f16 operands, f32 sums; Q4_K / Q8_0 matrices, h and ffn multiples
+ * of 64, at least 256).  1 = ran, 0 = declined (nothing done), <0 = error. */
+int sb_experts(sb_ctx *ctx, const float *xs, size_t n, size_t h, size_t ffn, size_t top_k, const float *weights,
+               sb_expert_block *exps, size_t n_exps, float *sum, uint8_t *done);
+/* `GpuDispatch::atencion_prefill` (gpu.rs:496-517): causal attention of a block of n tokens
+ * at positions seq_before .. seq_before + n - 1 on the device, over the layer's f16 KV rows
+ * mirrored from the host: k / v [seq_before + n][kv_heads * hd] with the block's rows
+ * already appended; *valid_rows = leading rows the device mirror already holds (the rest go
+ * up; set to seq_before + n).  q / out [n][heads * hd] (q roped).  Softmax of q.k / sqrt(hd)
+ * in f32 per query row (attn.rs:73-140).  1 = done, 0 = declined (hd a multiple of 32 up to
+ * 192, heads / kv_heads dividing 32), <0 = error. */
+int sb_attention_prefill(sb_ctx *ctx, uint32_t layer, const float *q, float *out, size_t n, size_t seq_before,
+                         size_t heads, size_t kv_heads, size_t hd, const uint16_t *k, const uint16_t *v,
+                         size_t *valid_rows);
 /* Number of resident weight tensors (`CudaGpu::residentes`, used by cuda_matvec.rs:138). */
 size_t sb_resident_count(const sb_ctx *ctx);
 /* `GpuDispatch::stats` (gpu.rs:350-352). */

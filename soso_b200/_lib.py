@@ -42,6 +42,12 @@ class SbStats(ctypes.Structure):
                                                "decode_steps", "stream_hits", "stream_misses")]
 
 
+class SbExpertBlock(ctypes.Structure):
+    _fields_ = [("keys", ctypes.c_char_p * 3), ("views", ctypes.POINTER(SbView) * 3),
+                ("tokens", ctypes.POINTER(ctypes.c_uint32)), ("n_tokens", c_size), ("shared", ctypes.c_int),
+                ("dests", ctypes.POINTER(ctypes.c_uint32))]
+
+
 class SbLayerState(ctypes.Structure):
     _fields_ = [("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("valid_rows", ctypes.POINTER(ctypes.c_size_t))]
 
@@ -91,6 +97,14 @@ SIGNATURES = {
     "sb_matvec_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbMatvecOp), c_size, c_u8p]),
     "sb_rmsnorm": (ctypes.c_int, [ctypes.c_void_p, c_f32p, c_f32p, c_size, ctypes.c_float]),
     "sb_resident_count": (c_size, [ctypes.c_void_p]),
+    "sb_upload": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(SbView), c_size, c_size]),
+    "sb_router_topk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, c_f32p, c_f32p, c_size, c_size, c_size, c_size,
+                                      ctypes.POINTER(ctypes.c_int32), c_f32p]),
+    "sb_experts": (ctypes.c_int, [ctypes.c_void_p, c_f32p, c_size, c_size, c_size, c_size, c_f32p,
+                                  ctypes.POINTER(SbExpertBlock), c_size, c_f32p, c_u8p]),
+    "sb_attention_prefill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, c_f32p, c_f32p, c_size, c_size, c_size,
+                                            c_size, c_size, ctypes.POINTER(ctypes.c_uint16),
+                                            ctypes.POINTER(ctypes.c_uint16), ctypes.POINTER(c_size)]),
     "sb_get_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbStats)]),
     "sb_last_error": (ctypes.c_char_p, []),
     "sb_decode_prepare": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbDecodePlan)]),

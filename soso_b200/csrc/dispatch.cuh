@@ -61,6 +61,8 @@ constexpr size_t PREFILL_MIN_TOKENS = 16;  // sb_matmul: from this many tokens o
 struct sb_engine;                  // whole-token decode state (engine.cuh)
 void sb_engine_free(sb_engine *e);
 void sb_pf_free(void *p);          // its block-prefill state (prefill_engine.cuh)
+struct sb_ctx;
+void sb_kv_mirror_free(const sb_ctx *c);  // KV mirrors of sb_attention_prefill (experts.cuh)
 
 struct sb_ctx {
     int device = 0;
@@ -216,6 +218,7 @@ extern "C" void sb_destroy(sb_ctx *c)
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
     if (c->eng) sb_engine_free(c->eng);
+    sb_kv_mirror_free(c);
     for (auto &kv : c->weights)
         if (kv.second.ptr) cudaFree(kv.second.ptr);
     if (c->scratch) cudaFree(c->scratch);

@@ -19,7 +19,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import SbError, SbMatvecOp, SbStats, SbView, c_f32p, c_u8p, last_error, lib
+from ._lib import SbError, SbExpertBlock, SbMatvecOp, SbStats, SbView, c_f32p, c_u8p, last_error, lib
 from .formats import DTYPE_F32, DTYPE_Q4_K, DTYPE_Q8_0
 
 
@@ -29,6 +29,19 @@ class TensorView:
     bytes: np.ndarray  # uint8, the tensor in its on-disk layout
     dtype: int
     elems: int
+
+
+@dataclass
+class ExpertoBloque:
+    """`ExpertoBloque` (crates/soso-llm-core/src/gpu.rs:175-187): the keys and views of an
+    expert's ffn_gate / ffn_up / ffn_down (a view may be None for a resident tensor), the
+    block's tokens that chose it, shared or routed, and each token's weight index
+    token * top_k + rank."""
+    claves: list
+    vistas: list
+    tokens: np.ndarray
+    compartido: bool
+    destinos: np.ndarray
 
 
 @dataclass
@@ -161,6 +174,69 @@ class CudaGpu:
         _f32_arg(weight, x.size, "weight")
         rc = self._L.sb_rmsnorm(self._h, x.ctypes.data_as(c_f32p), weight.ctypes.data_as(c_f32p), x.size, eps)
         return self._check(rc, "rmsnorm")
+
+    def gemma_subir(self, key: str, view: TensorView, rows: int, cols: int) -> bool:
+        """`gemma_subir` (gpu.rs:364-368): the tensor resident under its key."""
+        v = _view(view)
+        return self._check(self._L.sb_upload(self._h, key.encode(), ctypes.byref(v), rows, cols), f"upload({key})")
+
+    def router_topk(self, key: str, w: np.ndarray, xs: np.ndarray, n: int, h: int, n_exp: int, top_k: int,
+                    idx: np.ndarray, pesos: np.ndarray) -> bool:
+        """`router_topk` (gpu.rs:477-494): idx / pesos [n x top_k] in rank order."""
+        _f32_arg(w, n_exp * h, "w")
+        _f32_arg(xs, n * h, "xs")
+        _f32_arg(pesos, n * top_k, "pesos")
+        if idx.dtype != np.int32 or idx.size < n * top_k or not idx.flags.c_contiguous:
+            raise TypeError("idx must be a C-contiguous int32 array of n * top_k")
+        rc = self._L.sb_router_topk(self._h, key.encode(), w.ctypes.data_as(c_f32p), xs.ctypes.data_as(c_f32p), n, h,
+                                    n_exp, top_k, idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                    pesos.ctypes.data_as(c_f32p))
+        return self._check(rc, f"router_topk({key})")
+
+    def expertos_bloque(self, xs: np.ndarray, n: int, h: int, ffn: int, top_k: int, pesos: np.ndarray, exps: list,
+                        suma: np.ndarray, hecho: list) -> None:
+        """`expertos_bloque` (gpu.rs:457-475): exps = ExpertoBloque items; suma [n x h] gets the
+        weighted sum (rank order) of the experts resolved here, hecho[i] marks them."""
+        _f32_arg(xs, n * h, "xs")
+        _f32_arg(pesos, n * top_k, "pesos")
+        _f32_arg(suma, n * h, "suma")
+        arr = (SbExpertBlock * max(1, len(exps)))()
+        keep = []
+        for i, e in enumerate(exps):
+            keys = [k.encode() for k in e.claves]
+            views = [None if v is None else _view(v) for v in e.vistas]
+            toks = np.ascontiguousarray(e.tokens, dtype=np.uint32)
+            dest = np.ascontiguousarray(e.destinos, dtype=np.uint32)
+            keep += [keys, views, toks, dest]
+            arr[i].keys = (ctypes.c_char_p * 3)(*keys)
+            arr[i].views = (ctypes.POINTER(SbView) * 3)(*[ctypes.pointer(v) if v is not None else None for v in views])
+            arr[i].tokens = toks.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32))
+            arr[i].n_tokens = toks.size
+            arr[i].shared = int(e.compartido)
+            arr[i].dests = dest.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32))
+        done = (ctypes.c_uint8 * max(1, len(exps)))()
+        rc = self._L.sb_experts(self._h, xs.ctypes.data_as(c_f32p), n, h, ffn, top_k, pesos.ctypes.data_as(c_f32p),
+                                arr, len(exps), suma.ctypes.data_as(c_f32p), done)
+        self._check(rc, "expertos_bloque")
+        for i in range(len(exps)):
+            if done[i]:
+                hecho[i] = True
+
+    def atencion_prefill(self, capa: int, q: np.ndarray, out: np.ndarray, n: int, seq_antes: int, heads: int,
+                         kv_heads: int, hd: int, k: np.ndarray, v: np.ndarray, filas_validas: list) -> bool:
+        """`atencion_prefill` (gpu.rs:496-517): filas_validas = [rows the device mirrors]."""
+        _f32_arg(q, n * heads * hd, "q")
+        _f32_arg(out, n * heads * hd, "out")
+        kk = np.ascontiguousarray(k, dtype=np.uint16)
+        vv = np.ascontiguousarray(v, dtype=np.uint16)
+        fv = ctypes.c_size_t(filas_validas[0])
+        u16 = ctypes.POINTER(ctypes.c_uint16)
+        rc = self._L.sb_attention_prefill(self._h, capa, q.ctypes.data_as(c_f32p), out.ctypes.data_as(c_f32p), n,
+                                          seq_antes, heads, kv_heads, hd, kk.ctypes.data_as(u16),
+                                          vv.ctypes.data_as(u16), ctypes.byref(fv))
+        ok = self._check(rc, "atencion_prefill")
+        filas_validas[0] = fv.value
+        return ok
 
     def residentes(self) -> int:
         return int(self._L.sb_resident_count(self._h))
