@@ -177,7 +177,8 @@ def run_ours(args) -> None:
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        # (long enough for rank 0's one-GPU agreement run of a decode model while the others wait)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=480), device_id=dev)
 
     from soso_b200 import synth
     from soso_b200._lib import SbkMvOp, SbMatvecOp, SbView, c_f32p, c_u8p, last_error, lib
@@ -330,8 +331,19 @@ def run_ours(args) -> None:
         traffic = profile_traffic()
         h2d = sum(m[1] * 4 for m in mats)
         d2h = sum(m[0] * 4 for m in mats)
+        summary = {"q4k_GBps": round(value, 1), "q4k_frac": round(achieved / peaks["hbm_gbs"], 4)}
+        for k, v in extra.items():
+            if k.startswith("decode"):
+                summary[k + "_tok_s"] = v["tok_per_s"]
+                summary[k + "_frac"] = v["roofline"]["frac"]
+                if "prefill" in v:
+                    summary[k + "_prefill_ms"] = v["prefill"]["ms"]
+                    summary[k + "_prefill_frac"] = v["prefill"]["frac_of_bf16_peak"]
+                if "agreement_vs_1gpu" in v and v["agreement_vs_1gpu"]:
+                    summary[k + "_identical_vs_1gpu"] = v["agreement_vs_1gpu"]["identical_frac"]
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "summary": summary, "n_gpus": world,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "pct_of_peak": round(100.0 * value / world / peaks["hbm_gbs"], 1),
@@ -424,14 +436,33 @@ def decode_bench(device: int, rank: int, which: str = "dense", world: int = 1) -
     # under expert parallelism a rank makes only the experts it holds (same bytes as whole)
     model = decode.synth_model(cfg, seed, held=(rank, world) if group and cfg.n_exp else None)
     sess = decode.DecodeSession(cfg, model, device=device, group=group)
-    prompt = synth.rng("prompt", which, 0 if group else rank).integers(0, cfg.vocab, 128).astype(np.int32)
+    n_prompt = 512 if which == "mla" else 128  # configs[4]: a 512-token prefill, then decode
+    prompt = synth.rng("prompt", which, 0 if group else rank).integers(0, cfg.vocab, n_prompt).astype(np.int32)
     sess.greedy(prompt[:8], 8)  # warm
-    first = sess.greedy(prompt, 128)  # the prompt, one token per step
+    pf = None
+    if group is None:
+        # the prompt as one block on the tensor cores (sb_decode_prefill), timed over 3 runs
+        sess.prefill(prompt)  # warm: buffers and weight maps
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            _, nxt = sess.prefill(prompt, logits=False)
+            times.append(time.perf_counter() - t0)
+        ms = 1e3 * sorted(times)[1]
+        fl = prefill_flops(cfg, n_prompt)
+        tf = fl / (ms / 1e3) / 1e12
+        pf = {"tokens": n_prompt, "ms": round(ms, 3), "TFLOPs": round(tf, 1),
+              "frac_of_bf16_peak": round(tf / load_bf16_peak(), 4), "flops": int(fl),
+              "timing": "wall clock around sb_decode_prefill (tables and tokens up, every layer, last token's "
+                        "logits and argmax down), median of 3"}
+        first = np.array([nxt], np.int32)
+    else:
+        first = sess.greedy(prompt, n_prompt)[-1:]  # the prompt, one token per step
     n_gen = 256
     if group:
         group[2](b"go")  # start the timed region together
     t0 = time.perf_counter()
-    toks = sess.greedy(first[-1:], n_gen, pos=128)
+    toks = sess.greedy(first[-1:], n_gen, pos=n_prompt)
     dt = time.perf_counter() - t0
     if group:
         dt = max(float(v) for v in group[2](repr(dt).encode()))  # the slowest rank
@@ -440,12 +471,20 @@ def decode_bench(device: int, rank: int, which: str = "dense", world: int = 1) -
     # rope keys (f32) of an MLA layer
     kv_per_pos = (cfg.n_layers * (cfg.kv_rank * 2 + cfg.kv_heads * cfg.qk_rope * 4) if cfg.mla
                   else cfg.n_layers * 2 * cfg.kv_dim * 2)
-    avg_ctx = 128 + (n_gen + 1) / 2.0
+    avg_ctx = n_prompt + (n_gen + 1) / 2.0
     bytes_tok = weights + kv_per_pos * avg_ctx + cfg.hidden * 4
     peaks = load_peaks()
     hbm = peaks["hbm_gbs"] * (world if group else 1)  # a sharded model streams from every rank's HBM
     tps = n_gen / dt
     sess.close()
+    agree = None
+    if group:
+        # the same model and prompt unsharded on rank 0's GPU: token agreement of the split run,
+        # and at a first divergence the unsharded top-1 / top-2 gap (a tie or not)
+        full_toks = np.concatenate([first[-1:], toks])
+        agree = group_agreement(cfg, which, prompt, full_toks, device) if rank == 0 else None
+        agree = group[2](json.dumps(agree).encode())[0]
+        agree = json.loads(agree)
     desc = {"dense": "configs[2]: Qwen2.5-3B-style dense, 36 layers, hidden 2048, 16 q / 2 kv heads x 128, SwiGLU "
                      "11008, vocab 151936, Q4_K + Q6_K (ffn_down, output), fp16 KV ctx 4096",
             "moe": "configs[3]: Qwen3-30B-A3B-style MoE, 48 layers, hidden 2048, 32 q / 4 kv heads x 128, QK-norm, "
@@ -454,9 +493,9 @@ def decode_bench(device: int, rank: int, which: str = "dense", world: int = 1) -
                    "qk_nope 128 + qk_rope 64, v_head 128, q-LoRA 512 (synthesized), layer 0 dense FFN 10944, then "
                    "64 experts top-6 x 1408 + shared 2816, vocab 102400, Q4_K (down projections Q8_0), latent "
                    "f16 cache ctx 2048"}[which]
-    return {"config": desc,
+    out = {"tok_per_s": round(tps, 1), "config": desc,
             "data": "synthetic random-init weights (seeded), random prompt",
-            "prompt_tokens": 128, "generated_tokens": n_gen, "tok_per_s": round(tps, 1),
+            "prompt_tokens": n_prompt, "generated_tokens": n_gen,
             "ms_per_token": round(1e3 * dt / n_gen, 3), "bytes_per_token": int(bytes_tok),
             "roofline": {"bound": "hbm", "achieved_GBps": round(bytes_tok * tps / 1e9, 1),
                          "peak_GBps": hbm, "frac": round(bytes_tok * tps / 1e9 / hbm, 4),
@@ -465,6 +504,88 @@ def decode_bench(device: int, rank: int, which: str = "dense", world: int = 1) -
                       + ("; max over ranks" if group else ""),
             "parallelism": parallelism(cfg, world) if group else "1 GPU",
             "last_tokens": toks[-4:].tolist()}
+    if pf:
+        out["prefill"] = pf
+    if agree is not None:
+        out["agreement_vs_1gpu"] = agree
+    return out
+
+
+def prefill_flops(cfg, n: int) -> float:
+    """Useful FLOPs of a block prefill of n tokens from position 0: 2 x rows x cols per token
+    of every matrix a token goes through (its routed experts only), the MLA re-expansion of
+    the n latent rows, and the causal attention (heads x (dqk + dv) x 2 per (query, key))."""
+    H, fl = cfg.hidden, 0.0
+    for l in range(cfg.n_layers):
+        if cfg.mla:
+            qk = cfg.qk_nope + cfg.qk_rope
+            fl += 2 * n * (cfg.q_rank * H + cfg.kv_rank * H + cfg.heads * qk * cfg.q_rank + H * cfg.q_dim)
+            fl += 2 * n * (cfg.kv_heads * qk + cfg.kv_heads * cfg.v_dim) * cfg.kv_rank
+            fl += cfg.heads * (qk + cfg.v_dim) * n * (n + 1)
+        else:
+            fl += 2 * n * (cfg.q_dim + 2 * cfg.kv_dim) * H + 2 * n * H * cfg.q_dim
+            fl += cfg.heads * 2 * cfg.head_dim * n * (n + 1)
+        if cfg.is_moe(l):
+            fl += 2 * n * cfg.n_exp * H + 2 * n * cfg.top_k * 3 * cfg.moe_ffn * H + 2 * n * 3 * cfg.shared_ffn * H
+        else:
+            fl += 2 * n * 3 * cfg.ffn * H
+    return fl + 2 * cfg.vocab * H
+
+
+def load_bf16_peak() -> float:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f).get("bf16_tflops", 1590.0))
+    return 1590.0
+
+
+def group_agreement(cfg, which: str, prompt, split_toks, device: int) -> dict:
+    """The greedy chain of the split model against the same model on one GPU (rank 0's): the
+    share of identical generated tokens, the first step where they differ and, there, the
+    one-GPU top-1 / top-2 logit gap over the rms of the logits (a gap near the two runs'
+    rounding difference is a tie, which either run may break)."""
+    from soso_b200 import decode
+    model = decode.synth_model(cfg, f"{which}.0")  # every expert (the split run's rank 0 held its own)
+    s = decode.DecodeSession(cfg, model, device=device)
+    try:
+        one = s.greedy(prompt, len(prompt) + len(split_toks) - 1)[len(prompt) - 1:]
+        n = len(split_toks)
+        same = one[:n] == split_toks
+        first = None if same.all() else int(np.argmax(~same))
+        gap = None
+        if first is not None:
+            # teacher forced on the common prefix: the logits of the step where the runs part
+            orc_embed = decode_embed_rows(cfg, model)
+            fed = np.concatenate([prompt, split_toks[:first]])
+            for i, t in enumerate(fed):
+                lg = s.token(orc_embed(int(t)), i)
+            top = np.sort(lg.astype(np.float64))[-2:]
+            gap = float((top[1] - top[0]) / np.sqrt(np.mean(lg.astype(np.float64) ** 2)))
+        return {"tokens": n, "identical_frac": round(float(same.mean()), 4), "first_divergence": first,
+                "gap_at_divergence": gap}
+    finally:
+        s.close()
+
+
+def decode_embed_rows(cfg, model):
+    """The embedding row of a token (Runtime::embed_token), dequantised by the library's
+    embedding kernel (sbk_embed_row) on the current GPU."""
+    import torch
+
+    from soso_b200._lib import lib
+    table = torch.from_numpy(model["token_embd"]).cuda()
+    tok = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.empty(cfg.hidden, dtype=torch.float32, device="cuda")
+
+    def row(t: int) -> np.ndarray:
+        tok.fill_(t)
+        if lib().sbk_embed_row(table.data_ptr(), cfg.dtypes["token_embd"], cfg.vocab, cfg.hidden, tok.data_ptr(),
+                               out.data_ptr(), 0, torch.cuda.current_stream().cuda_stream):
+            raise RuntimeError("sbk_embed_row rejected")
+        torch.cuda.synchronize()
+        return out.cpu().numpy()
+    return row
 
 
 def q80_bench(dev) -> dict:
@@ -696,6 +817,23 @@ def run_decode_case(tokens: int) -> None:
     print(json.dumps({"case": "decode", "tokens": toks.tolist()}))
 
 
+def run_prefill_engine_case(launches: int) -> None:
+    """A 3-layer slice of configs[4] (MLA attention; the dense FFN layer, then two MoE layers)
+    through the block prefill: `launches` prefills of a 512-token prompt -- for ncu captures
+    of the table-driven GEMM (the grouped expert launches among them)."""
+    import dataclasses
+
+    from soso_b200 import decode, synth
+    cfg = dataclasses.replace(decode.DEEPSEEK_V2_LITE, n_layers=3)
+    sess = decode.DecodeSession(cfg, decode.synth_model(cfg, "ncu"))
+    prompt = synth.rng("ncu", "pf").integers(0, cfg.vocab, 512).astype(np.int32)
+    nxt = None
+    for _ in range(launches):
+        _, nxt = sess.prefill(prompt, logits=False)
+    sess.close()
+    print(json.dumps({"case": "prefill_engine", "prefills": launches, "next": nxt}))
+
+
 def run_decode_mla_case(tokens: int) -> None:
     """A 3-layer slice of configs[4] (MLA attention; a dense FFN, then two MoE layers) through
     the whole-token engine: `tokens` greedy steps after a 64-token prompt -- for ncu captures
@@ -747,7 +885,8 @@ def run_case(name: str, launches: int) -> None:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ncu-case", choices=sorted(NCU_CASES) + ["q4k_batch", "prefill", "decode", "decode_mla"], default=None)
+    ap.add_argument("--ncu-case", choices=sorted(NCU_CASES) + ["q4k_batch", "prefill", "decode", "decode_mla",
+                                                               "prefill_engine"], default=None)
     ap.add_argument("--launches", type=int, default=12)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -765,6 +904,9 @@ def main():
         return
     if args.ncu_case == "decode_mla":
         run_decode_mla_case(args.launches)
+        return
+    if args.ncu_case == "prefill_engine":
+        run_prefill_engine_case(args.launches)
         return
     if args.ncu_case == "decode":
         run_decode_case(args.launches)
