@@ -55,3 +55,32 @@ def test_mla_decode_token_logits_and_latent_rows(gpu, mla_model):
                 assert np.max(np.abs(got - want)) <= 2e-3 * max(1.0, float(np.abs(want).max())), (pos, l)
     finally:
         sess.close()
+
+
+# The reference's own MLA layout (forward_mla_attn, arch.rs:51-202, whose per-head q stride is
+# hidden / heads): qk_nope + qk_rope = hidden / heads = 128 and v_dim 128, one kv head shared
+# by the four query heads as in its parity model (tests/arch_ext.rs:156-178).  The oracle's
+# MLA is pinned to the reference's mla_oracle_attn_out on such dims
+# (tests/test_oracle_reference_cases.py); here the engine against the oracle.
+TINY_MLA_REF = decode.DenseConfig(n_layers=2, hidden=512, heads=4, kv_heads=1, head_dim=128, ffn=1024, vocab=1024,
+                                  ctx=96, theta=1e4, neox=False, qkv_bias=False, mla=True, q_rank=256, kv_rank=512,
+                                  qk_nope=64, qk_rope=64, v_dim=128, dtypes=dict(decode.TINY_MLA.dtypes))
+
+
+def test_mla_reference_stride_greedy_and_logits(gpu):
+    cfg = TINY_MLA_REF
+    assert cfg.qk_nope + cfg.qk_rope == cfg.hidden // cfg.heads
+    model = decode.synth_model(cfg, "mla_ref_stride")
+    prompt = synth.rng("prompt", "mla_ref").integers(0, cfg.vocab, 8).astype(np.int32)
+    sess = decode.DecodeSession(cfg, model)
+    try:
+        got = sess.greedy(prompt, 40)
+        orc = DenseOracle(cfg, model)
+        for pos, t in enumerate(synth.rng("toks", "mla_ref").integers(0, cfg.vocab, 10)):
+            e = orc.embed(int(t))
+            assert logits_close(sess.token(e, pos), orc.step(e, pos)) <= LOGIT_REL, pos
+    finally:
+        sess.close()
+    want, logits = DenseOracle(cfg, model).greedy(prompt, 40)
+    gaps = [float(np.sort(lg)[-1] - np.sort(lg)[-2]) for lg in logits]
+    assert np.array_equal(got, want), (np.nonzero(got != want)[0][:5], min(gaps))
