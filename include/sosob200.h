@@ -306,6 +306,13 @@ int sb_decode_prefill(sb_ctx *ctx, const int32_t *tokens, size_t n, size_t pos0,
  * of world > 1, sb_decode_prepare returns before its warm-up token: call
  * sb_decode_finish on every rank after a host barrier; only sb_decode_greedy runs. */
 size_t sb_group_handle_bytes(void);
+/* The consuming side of an exchange point on its own: wait, bounded by `limit` spins of about
+ * 100 ns, until the n counters cnt[0..n) (device memory) reach target; *ok (device int) = 1,
+ * or 0 when the limit ran out, which also leaves 0x91 in the device error word
+ * (sbk_take_device_error) -- how a rank learns that a peer never published, without a trap
+ * and with the context still usable.  limit <= 2^26 (the limit every exchange wait of the
+ * decode kernels uses).  No counterpart in the reference. */
+int sbk_exchange_wait(const unsigned *cnt, int n, unsigned target, unsigned limit, int *ok, void *stream);
 int sb_group_create(sb_ctx *ctx, int rank, int world, void *handle_out);
 int sb_group_open(sb_ctx *ctx, const void *handles /* world x sb_group_handle_bytes(), rank order */);
 int sb_decode_finish(sb_ctx *ctx);

@@ -169,6 +169,8 @@ SIGNATURES = {
     "sbk_matmul": (ctypes.c_int, [ctypes.c_uint8, ctypes.c_void_p, c_size, c_size, c_size, ctypes.c_void_p,
                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "sbk_take_device_error": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32)]),
+    "sbk_exchange_wait": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_uint, ctypes.c_void_p,
+                                         ctypes.c_void_p]),
 }
 
 _L = None

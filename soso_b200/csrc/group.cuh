@@ -61,12 +61,12 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p)
 
 // Bounded wait until cnt[s] >= target for s < n; false (and the device error word set)
 // if the limit ran out.
-__device__ inline bool wait_counts(const unsigned *cnt, int n, unsigned target)
+__device__ inline bool wait_counts(const unsigned *cnt, int n, unsigned target, unsigned limit = WAIT_LIMIT)
 {
     for (int s = 0; s < n; s++) {
         unsigned it = 0;
         while (ld_acquire_sys(cnt + s) < target) {
-            if (++it > WAIT_LIMIT) {
+            if (++it > limit) {
                 set_dev_error(0x91u);
                 return false;
             }
@@ -91,8 +91,26 @@ struct Wait {
     int per;                // counter increments per source per token (publisher CTAs)
 };
 
+// The consuming side of an exchange point on its own (one thread): the same bounded wait,
+// with the caller's spin limit; ok = 1 when every counter reached the target.
+__global__ void exchange_wait_kernel(const unsigned *cnt, int n, unsigned target, unsigned limit, int *ok)
+{
+    if (threadIdx.x == 0) *ok = wait_counts(cnt, n, target, limit) ? 1 : 0;
+}
+
 }  // namespace grp
 }  // namespace sb
+
+// Wait (bounded) for n exchange counters (device memory) to reach target, as a consuming
+// kernel does before it reads an exchange point; ok (device int) gets 1, or 0 when `limit`
+// spins ran out -- and then the device error word holds 0x91.  A wait that nothing
+// satisfies costs about limit x 100 ns.
+extern "C" int sbk_exchange_wait(const unsigned *cnt, int n, unsigned target, unsigned limit, int *ok, void *stream)
+{
+    if (!cnt || !ok || n < 1 || n > sb::grp::MAXG || !limit || limit > sb::grp::WAIT_LIMIT) return -1;
+    sb::grp::exchange_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(cnt, n, target, limit, ok);
+    return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
 
 struct sb_group {
     int rank = 0, world = 1;
