@@ -31,7 +31,7 @@ class DenseOracle:
 
     def _mv(self, name: str, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
         dt = self.cfg.dtypes[name.split(".")[-1]]  # by tensor kind (experts share their kind's dtype)
-        if self.threads:
+        if self.threads and dt != 1:  # (the AVX2 restatement has no f32 kernel: f32 matrices run scalar)
             return oracle.cpu_matvec(dt, self.m[name], rows, cols, x, threads=self.threads)
         return oracle.matvec(dt, self.m[name], rows, cols, x)
 

@@ -309,6 +309,24 @@ __global__ void mla_rope_rows_kernel(float *x, int heads, int qk_nope, int qk_ro
 // ---- MoE -----------------------------------------------------------------------------
 constexpr int MOE_MAXE = 1024, MOE_MAXK = 16;
 
+// Router logits of a block against an f32 matrix (the reference's router matvec,
+// layer.rs:1959-1972; mo_router_logits, gemma_capa.cu:517-538): one warp per
+// (expert, token), lanes over the hidden size, a fixed-order reduction.
+__global__ void router_logits_f32_kernel(const float *__restrict__ w, const float *__restrict__ xs,
+                                         float *__restrict__ out, int n_exp, int h)
+{
+    griddep_wait();
+    const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), t = blockIdx.y, lane = threadIdx.x & 31;
+    if (e < n_exp) {
+        const float *wr = w + (size_t)e * h, *x = xs + (size_t)t * h;
+        float acc = 0.0f;
+        for (int i = lane; i < h; i += 32) acc += wr[i] * x[i];
+        acc = warp_sum(acc);
+        if (lane == 0) out[(size_t)t * n_exp + e] = acc;
+    }
+    griddep_launch();
+}
+
 // Grouping of the block's routed pairs p = t * k + j by expert (idx from the router): slot
 // order is expert-major, within an expert arbitrary (every row of a GEMM is computed alone,
 // so the order changes no value).  Writes pair -> slot, slot -> token, and the two tile

@@ -104,6 +104,61 @@ struct RouteArgs {
     int *trace;             // [k]: the chosen experts' IDs in rank order, kept for sb_decode_routes
 };
 
+// The router of a MoE layer whose matrix is f32, as the reference stores ffn_gate_inp (its
+// router matvec, layer.rs:1959-1972, runs in f32), with the input formed as the fused matvec
+// forms it (XS_NORM): h = a + (res, or the weighted set of the previous MoE layer's outputs)
+// -> h_out (CTA 0), x = rmsnorm(h) * w (gemm.rs:93-100); logits[e] = W[e] . x.  Every CTA
+// forms x in shared memory itself and takes 8 experts, one per warp.
+struct RouterF32Args {
+    const float *a, *res, *ys, *yw;
+    int ny, ystride;
+    float *h_out;
+    const float *nw;
+    float eps;
+    const float *W;
+    float *logits;
+    int H, n_exp;
+};
+
+__global__ void __launch_bounds__(256) router_f32_kernel(RouterF32Args r)
+{
+    extern __shared__ float xs[];  // [H]
+    __shared__ float red[8];
+    griddep_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < r.H; i += blockDim.x) {
+        float v = r.a[i];
+        if (r.ny) {
+            float acc = 0.0f;
+            for (int k = 0; k < r.ny; k++) acc += __ldcg(r.ys + (size_t)k * r.ystride + i) * r.yw[k];
+            v = acc + v;
+        } else if (r.res) {
+            v += r.res[i];
+        }
+        xs[i] = v;
+        ss += v * v;
+        if (blockIdx.x == 0 && r.h_out) r.h_out[i] = v;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < 8; w++) tot += red[w];
+    const float scale = 1.0f / sqrtf(tot / (float)r.H + r.eps);
+    for (int i = threadIdx.x; i < r.H; i += blockDim.x) xs[i] = xs[i] * scale * r.nw[i];
+    __syncthreads();
+    const int e = blockIdx.x * 8 + warp;
+    if (e < r.n_exp) {
+        const float *wr = r.W + (size_t)e * r.H;
+        float acc = 0.0f;
+        for (int i = lane; i < r.H; i += 32) acc += wr[i] * xs[i];
+        acc = warp_sum(acc);
+        if (lane == 0) r.logits[e] = acc;
+    }
+    griddep_launch();
+}
+
 __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
 {
     __shared__ float p[1024];
@@ -722,7 +777,15 @@ int enqueue_token(sb_engine *e, cudaStream_t s, bool greedy)
         }
         if (L.moe) {
             // MoE FFN: h + attention output -> rmsnorm -> router logits; route; experts
-            {
+            if (L.router.dt == SB_DTYPE_F32) {  // (one GPU only: prepare declines it in a group)
+                const sbk_xsrc xs = norm_src(L.nf, ho);
+                sb::RouterF32Args ra{hc, xs.res, xs.ys, xs.yw, xs.ny, xs.ystride, ho, L.nf, e->eps,
+                                     (const float *)L.router.w, e->rlog, (int)e->H, (int)L.n_exp};
+                ENG_CHECK(sb::launch_k(sb::router_f32_kernel, dim3((unsigned)((L.n_exp + 7) / 8)), dim3(256),
+                                       e->H * 4, 1, s, ra));
+                std::swap(hc, ho);
+                consumed();
+            } else {
                 const sbk_xsrc xs = norm_src(L.nf, ho);
                 const EngMat *ms[1] = {&L.router};
                 float *ys[1] = {e->rlog};
@@ -970,7 +1033,18 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
             // the router on every rank; the experts resident here: all of them, or under
             // expert parallelism this rank's range of expert IDs (row_strip), and the shared
             // expert on rank l % world
-            if ((rc = eng_mat(c, mp.router, L.n_exp, H, &L.router, true)) != 1) return bail(rc);
+            if (mp.router.view.dtype == SB_DTYPE_F32) {
+                // an f32 router (as the reference stores it), one GPU only
+                if (g || H * 4 > 48 * 1024) return bail(0);
+                if (!mp.router.key || !mp.router.view.bytes || mp.router.view.len != L.n_exp * H * 4 ||
+                    mp.router.rows != L.n_exp || mp.router.cols != H)
+                    return bail(fail("decode plan: f32 router of an unexpected shape"));
+                Resident *r = nullptr;
+                if ((rc = c->resident(mp.router.key, &mp.router.view, L.n_exp, H, &r, false)) != 1) return bail(rc);
+                L.router = EngMat{r->ptr, SB_DTYPE_F32, L.n_exp, H};
+            } else if ((rc = eng_mat(c, mp.router, L.n_exp, H, &L.router, true)) != 1) {
+                return bail(rc);
+            }
             if (g) {
                 int lo, hi;
                 sb::row_strip((int)L.n_exp, g->rank, g->world, lo, hi);

@@ -11,24 +11,6 @@
 namespace sb {
 namespace blk {
 
-// Router logits of a block in f32 (the reference's router matvec over an f32 matrix,
-// layer.rs:1959-1972; mo_router_logits, gemma_capa.cu:517-538): one warp per
-// (expert, token), lanes over the hidden size, a fixed-order reduction.
-__global__ void router_logits_f32_kernel(const float *__restrict__ w, const float *__restrict__ xs,
-                                         float *__restrict__ out, int n_exp, int h)
-{
-    griddep_wait();
-    const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), t = blockIdx.y, lane = threadIdx.x & 31;
-    if (e < n_exp) {
-        const float *wr = w + (size_t)e * h, *x = xs + (size_t)t * h;
-        float acc = 0.0f;
-        for (int i = lane; i < h; i += 32) acc += wr[i] * x[i];
-        acc = warp_sum(acc);
-        if (lane == 0) out[(size_t)t * n_exp + e] = acc;
-    }
-    griddep_launch();
-}
-
 // silu(gate) * up of every slot as f16 operands of the down projection (swiglu_inplace,
 // gemm.rs:210-226): rows [slot][2 ffn] = gate | up.
 __global__ void swiglu16_rows_kernel(const float *__restrict__ gu, __half *__restrict__ act, int ffn, long long total)

@@ -126,7 +126,7 @@ int pf_state(sb_ctx *c, sb_engine *e, size_t n, PfState **out)
         if (L.moe) {
             nexp = std::max(nexp, L.n_exp), topk = std::max(topk, L.top_k), effn = std::max(effn, L.effn);
             if (L.sh_here) sffn = std::max(sffn, L.sh[0].rows / 2);
-            sg |= L.sg != nullptr;
+            sg |= L.sg != nullptr || L.router.dt == SB_DTYPE_F32;  // (x32: shared gate, f32 router)
         } else {
             ffn = std::max(ffn, L.ffn);
         }
@@ -424,8 +424,12 @@ int pf_layers(PfRun &r)
             continue;
         }
         // MoE FFN
-        PF_CHECK(norm(L.nf, L.sg ? st->x32 : nullptr));
-        {
+        const bool f32_router = L.router.dt == SB_DTYPE_F32;
+        PF_CHECK(norm(L.nf, L.sg || f32_router ? st->x32 : nullptr));
+        if (f32_router) {  // the router in f32, as the reference keeps it
+            PF_CHECK(r.k("router logits", blk::router_logits_f32_kernel, dim3((unsigned)((L.n_exp + 7) / 8), n),
+                         dim3(256), (const float *)L.router.w, (const float *)st->x32, st->rlog, (int)L.n_exp, H));
+        } else {
             const EngMat *ms[1] = {&L.router};
             const pg::Out os[1] = {{st->rlog, (int)L.n_exp, (int)L.n_exp, 0, pg::OUT_F32}};
             PF_CHECK(r.gemm(ms, os, 1, st->x16, cap, 0, n));
@@ -519,7 +523,8 @@ extern "C" int sb_decode_prefill(sb_ctx *c, const int32_t *tokens, size_t n, siz
         if (L.mla && (L.qk_nope + L.qk_rope) % 32) return 0;
         if (!L.mla && (L.hd % 32 || 32 % (L.heads / L.kvh))) return 0;
         if (L.moe) {
-            if (!L.ex_pairs || !pf_gemm_dtype(L.router.dt) || !pf_gemm_dtype(L.ex[0].dt) ||
+            if (!L.ex_pairs || !(pf_gemm_dtype(L.router.dt) || L.router.dt == SB_DTYPE_F32) ||
+                !pf_gemm_dtype(L.ex[0].dt) ||
                 !pf_gemm_dtype(L.ex[2].dt) || L.effn % 64 || (L.sh_here && (L.sh[0].rows / 2) % 64))
                 return 0;
         } else if (!L.gu2.w || !pf_gemm_dtype(L.gu2.dt) || L.ffn % 64) {

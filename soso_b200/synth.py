@@ -12,7 +12,7 @@ import zlib
 
 import numpy as np
 
-from .formats import DTYPE_Q4_K, DTYPE_Q6_K, DTYPE_Q8_0, row_bytes
+from .formats import DTYPE_F32, DTYPE_Q4_K, DTYPE_Q6_K, DTYPE_Q8_0, row_bytes
 
 
 def seed_of(*parts) -> int:
@@ -93,6 +93,8 @@ def model_weights(dtype: int, rows: int, cols: int, g: np.random.Generator, std:
     rb = row_bytes(dtype, cols)
     if rb is None:
         raise ValueError(f"cols={cols} is not a whole number of blocks for dtype {dtype}")
+    if dtype == DTYPE_F32:  # (an f32 matrix, as the reference keeps its routers: N(0, s^2))
+        return (g.standard_normal(rows * cols) * s).astype(np.float32).view(np.uint8)
     if dtype == DTYPE_Q4_K:
         nb = rows * cols // 256
         blk = np.empty((nb, 144), dtype=np.uint8)

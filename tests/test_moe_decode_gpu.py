@@ -21,9 +21,15 @@ def logits_close(g, t):
     return float((np.abs(g.astype(np.float64) - t) / np.maximum(np.abs(t), rms)).max())
 
 
-@pytest.fixture(scope="module", params=["TINY_MOE", "TINY_MOE_NS"])
+@pytest.fixture(scope="module", params=["TINY_MOE", "TINY_MOE_NS", "TINY_MOE_F32_ROUTER"])
 def moe_model(request):
-    cfg = getattr(decode, request.param)
+    if request.param == "TINY_MOE_F32_ROUTER":
+        # the router in f32, as the reference keeps ffn_gate_inp (its router matvec runs in f32)
+        import dataclasses
+        from soso_b200.formats import DTYPE_F32
+        cfg = dataclasses.replace(decode.TINY_MOE, dtypes=dict(decode.TINY_MOE.dtypes, ffn_gate_inp=DTYPE_F32))
+    else:
+        cfg = getattr(decode, request.param)
     return cfg, decode.synth_model(cfg, request.param.lower())
 
 

@@ -31,6 +31,8 @@ CONFIGS = {
     "dense_q6k_down": dataclasses.replace(decode.TINY, ctx=192),
     "moe_shared": dataclasses.replace(decode.TINY_MOE, dtypes=dict(decode.TINY_MOE_NS.dtypes), ctx=192),
     "moe": dataclasses.replace(decode.TINY_MOE_NS, ctx=192),
+    "moe_f32_router": dataclasses.replace(decode.TINY_MOE_NS, ctx=192,
+                                          dtypes=dict(decode.TINY_MOE_NS.dtypes, ffn_gate_inp=1)),
     "mla_moe": dataclasses.replace(decode.TINY_MLA, moe_ffn=256, ctx=192),
 }
 
