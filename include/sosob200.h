@@ -146,10 +146,11 @@ int sb_experts(sb_ctx *ctx, const float *xs, size_t n, size_t h, size_t ffn, siz
 /* `GpuDispatch::atencion_prefill` (gpu.rs:496-517): causal attention of a block of n tokens
  * at positions seq_before .. seq_before + n - 1 on the device, over the layer's f16 KV rows
  * mirrored from the host: k / v [seq_before + n][kv_heads * hd] with the block's rows
- * already appended; *valid_rows = leading rows the device mirror already holds (the rest go
- * up; set to seq_before + n).  q / out [n][heads * hd] (q roped).  Softmax of q.k / sqrt(hd)
- * in f32 per query row (attn.rs:73-140).  1 = done, 0 = declined (hd a multiple of 32 up to
- * 192, heads / kv_heads dividing 32), <0 = error. */
+ * already appended; *valid_rows = leading rows the device mirror already holds, counted up
+ * to seq_before (the rest go up; set to seq_before + n).  q / out [n][heads * hd] (q roped).
+ * Softmax of q.k / sqrt(hd) in f32 per query row (attn.rs:73-140), q.k exact to f32
+ * rounding, the softmax weights multiplied with V in f16.  1 = done, 0 = declined (hd not a
+ * multiple of 8 or above 256, heads / kv_heads above 64), <0 = error. */
 int sb_attention_prefill(sb_ctx *ctx, uint32_t layer, const float *q, float *out, size_t n, size_t seq_before,
                          size_t heads, size_t kv_heads, size_t hd, const uint16_t *k, const uint16_t *v,
                          size_t *valid_rows);

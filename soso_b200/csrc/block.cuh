@@ -6,10 +6,10 @@
 //                    f16 GEMM operands (and f32 when a shared-expert gate needs it)
 //   rope_kv_rows     bias, QK-norm, RoPE and the f16 K/V append of every token
 //                    (layer.rs:1146-1193, kv.rs:258-275): the decode step's math per row
-//   attn_prefill     causal GQA / MHA attention over the f16 rows, f32 throughout
+//   attn_prefill     causal GQA / MHA attention over the f16 rows on the tensor cores
 //                    (attention_decode_f16_tiled_scalar, attn.rs:73-140, per query row;
-//                    the reference's block kernel is attn_prefill_f16,
-//                    lxdde/ports/nouveau/matvec_iq.cu:507-628)
+//                    the reference's block kernels are attn_prefill_f16 and its mma form,
+//                    lxdde/ports/nouveau/matvec_iq.cu:507-628, :1477+)
 //   mla_*            the MLA latent rows (f16, kv.rs:293-315), RoPE of the q and the expanded
 //                    k rope slices (llama pairs, gemm.rs:1346) and the rope-key cache
 //   moe_*            routing of every token (topk_softmax, gemm.rs:62-91), grouping of the
@@ -138,11 +138,16 @@ __global__ void rope_kv_rows_kernel(RopeRowsArgs a)
 
 // ---- causal attention of a block of queries --------------------------------------
 // Query row (token t, head h) at position pos0 + t attends keys 0 .. pos0 + t of kv head
-// h / (heads / kv_heads): softmax(q.k / sqrt(dqk)) . v with the running maximum and sum of
-// the online softmax, in f32 over the f16 rows.  A CTA takes 32 query rows of one kv head
-// (32 / G tokens x the G heads of the group) and streams the keys through shared memory
-// 32 at a time; each of its 8 warps keeps 4 rows, the lanes splitting the dimensions.
-constexpr int AP_ROWS = 32, AP_KB = 32, AP_WARPS = 8, AP_MAXD = 192;
+// h / (heads / kv_heads): softmax(q.k / sqrt(dqk)) . v per row (attention_decode_f16_tiled_scalar,
+// attn.rs:73-140, over the f16 rows; the reference's block kernels are attn_prefill_f16 and its
+// mma.sync form, lxdde/ports/nouveau/matvec_iq.cu:507-628, :1477+).  On the tensor cores
+// (mma.sync m16n8k16, f32 accumulation): a CTA takes 64 query rows of one kv head (64 / G
+// tokens x the G heads of the group), each of its 4 warps 16 rows; keys stream through shared
+// memory 32 at a time (cp.async, two buffers).  S = Q K^T with q split into f16 hi + lo (22
+// significant bits, as the decode attention; K and V are f16 already), the causal mask, an
+// online softmax per row in f32 (running maximum and sum, the reference's order of
+// operations per key block), O += P V with P in f16.
+constexpr int AP_ROWS = 64, AP_KB = 32, AP_WARPS = 4, AP_MAXD = 256;
 
 struct AttnPrefillArgs {
     const float *q;      // [n][heads][dqk] (row stride ldq floats)
@@ -153,114 +158,236 @@ struct AttnPrefillArgs {
     float scale;
 };
 
-template <int DQ, int DV>  // dims per lane (dqk = 32 DQ, dv = 32 DV)
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tcmv::smem_u32(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b)
+{
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Shared memory of attn_prefill_kernel<KQ, NV, QS>: q hi / lo staging [2][64][QP] (kept for
+// the whole kernel when QS, else reused) and the key / value double buffers [2][32][QP],
+// [2][32][VP] (f16, row pitches padded by 16 bytes against bank conflicts).
+template <int KQ, int NV, bool QS>
+__host__ __device__ constexpr size_t attn_prefill_smem()
+{
+    constexpr size_t QP = 16 * KQ + 8, VP = 8 * NV + 8, qbytes = 2 * AP_ROWS * QP * 2,
+                     kvbytes = 2 * AP_KB * (QP + VP) * 2;
+    return QS ? qbytes + kvbytes : (qbytes > kvbytes ? qbytes : kvbytes);
+}
+
+// Widths up to 16 KQ (q, k) and 8 NV (v) that are multiples of 8: the columns past a.dqk /
+// a.dv are zero in shared memory and drop out of both products.  QS: the q fragments are
+// read from shared memory at every key block instead of being held in registers (the
+// 256-wide heads, whose q hi / lo and output accumulators would not fit in registers).
+template <int KQ, int NV, bool QS>
 __global__ void __launch_bounds__(AP_WARPS * 32) attn_prefill_kernel(AttnPrefillArgs a)
 {
-    __shared__ __align__(16) uint16_t ks[2][AP_KB][32 * DQ + 8];
-    __shared__ __align__(16) uint16_t vs[2][AP_KB][32 * DV + 8];
+    constexpr int DQ = 16 * KQ, DV = 8 * NV, QP = DQ + 8, VP = DV + 8;  // row pitches (f16)
+    extern __shared__ __align__(16) uint16_t ap_smem[];
+    uint16_t *qh = ap_smem, *ql = qh + AP_ROWS * QP;                   // q hi / lo
+    uint16_t *ks = QS ? ql + AP_ROWS * QP : ap_smem, *vs = ks + 2 * AP_KB * QP;
     griddep_wait();
-    const int G = a.heads / a.kv_heads, g = blockIdx.y;
-    const int tpc = AP_ROWS / G;  // tokens a CTA
-    const int t0 = blockIdx.x * tpc;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // this warp's 4 rows: r = 4 warp + j -> token t0 + r / G, head g G + r % G
-    float qv[4][DQ], acc[4][DV], m[4], l[4];
-    int lim[4];
-    bool live[4];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int r = 4 * warp + j, t = t0 + r / G, hh = g * G + r % G;
-        live[j] = t < a.n;
-        lim[j] = live[j] ? a.pos0 + t : -1;  // last key this row attends
-        m[j] = -INFINITY, l[j] = 0.0f;
-#pragma unroll
-        for (int d = 0; d < DQ; d++) qv[j][d] = live[j] ? a.q[(size_t)t * a.ldq + hh * a.dqk + lane * DQ + d] : 0.0f;
-#pragma unroll
-        for (int d = 0; d < DV; d++) acc[j][d] = 0.0f;
+    // the CTA's 64 rows: tpc tokens x the G query heads of kv head g (rows past tpc G idle)
+    const int G = a.heads / a.kv_heads, g = blockIdx.y, tpc = AP_ROWS / G, t0 = blockIdx.x * tpc;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+    // q of the CTA's rows -> f16 hi / lo in shared memory
+    for (int i = threadIdx.x; i < AP_ROWS * DQ; i += AP_WARPS * 32) {
+        const int r = i / DQ, d = i % DQ, t = t0 + r / G, hh = g * G + r % G;
+        const float x = r < tpc * G && t < a.n && d < a.dqk ? a.q[(size_t)t * a.ldq + hh * a.dqk + d] : 0.0f;
+        split_f16(x, qh[r * QP + d], ql[r * QP + d]);
     }
-    int tl = min(t0 + tpc, a.n) - 1;
-    const int kend = a.pos0 + tl + 1;  // keys the CTA needs
-    auto load = [&](int buf, int k0) {
-        // K rows: DQ*32 f16 = 4 DQ 16-byte pieces a row; V likewise
-        const int kp = 4 * DQ, vp = 4 * DV;
-        for (int i = threadIdx.x; i < AP_KB * (kp + vp); i += AP_WARPS * 32) {
-            const int row = i / (kp + vp), c = i % (kp + vp), key = k0 + row;
-            uint4 val = make_uint4(0, 0, 0, 0);
-            if (c < kp) {
-                if (key < kend) val = *reinterpret_cast<const uint4 *>(a.k + (size_t)key * a.ldk + g * a.dqk + 8 * c);
-                *reinterpret_cast<uint4 *>(&ks[buf][row][8 * c]) = val;
-            } else {
-                const int cv = c - kp;
-                if (key < kend) val = *reinterpret_cast<const uint4 *>(a.v + (size_t)key * a.ldv + g * a.dv + 8 * cv);
-                *reinterpret_cast<uint4 *>(&vs[buf][row][8 * cv]) = val;
-            }
-        }
-    };
-    const int nblk = (kend + AP_KB - 1) / AP_KB;
-    load(0, 0);
     __syncthreads();
+    const int mi = lane >> 3, mr = lane & 7;
+    const int qrow = 16 * warp + mr + (mi & 1) * 8, qcol = (mi >> 1) * 8;  // ldmatrix addresses
+    uint32_t fqh[QS ? 1 : KQ][4], fql[QS ? 1 : KQ][4];
+    if constexpr (!QS) {
+#pragma unroll
+        for (int s = 0; s < KQ; s++) {
+            ldsm_x4(fqh[s], qh + qrow * QP + 16 * s + qcol);
+            ldsm_x4(fql[s], ql + qrow * QP + 16 * s + qcol);
+        }
+        __syncthreads();  // the staging area becomes the key / value buffers
+    }
+    // this thread's two rows (gq, gq + 8 of the warp): their last key
+    int lim[2];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; h2++) {
+        const int r = 16 * warp + gq + 8 * h2, t = t0 + r / G;
+        lim[h2] = r < tpc * G && t < a.n ? a.pos0 + t : -1;
+    }
+    const int tl = min(t0 + tpc, a.n) - 1, kend = a.pos0 + tl + 1, nblk = (kend + AP_KB - 1) / AP_KB;
+    auto load = [&](int buf, int k0) {
+        constexpr int KC = DQ / 8, VC = DV / 8;  // 16-byte pieces a row
+        const int kc = a.dqk / 8, vc = a.dv / 8;
+        for (int i = threadIdx.x; i < AP_KB * (KC + VC); i += AP_WARPS * 32) {
+            const int row = i / (KC + VC), c = i % (KC + VC), key = k0 + row;
+            const bool ok = key < kend;
+            const int kk = ok ? key : 0;
+            if (c < KC)
+                cp_async16(ks + (buf * AP_KB + row) * QP + 8 * c,
+                           a.k + (size_t)kk * a.ldk + g * a.dqk + 8 * min(c, kc - 1), ok && c < kc);
+            else
+                cp_async16(vs + (buf * AP_KB + row) * VP + 8 * (c - KC),
+                           a.v + (size_t)kk * a.ldv + g * a.dv + 8 * min(c - KC, vc - 1), ok && c - KC < vc);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    float o[NV][4], m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int n = 0; n < NV; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    load(0, 0);
     for (int b = 0; b < nblk; b++) {
         const int buf = b & 1, k0 = b * AP_KB;
-        if (b + 1 < nblk) load(buf ^ 1, k0 + AP_KB);
-        for (int kk = 0; kk < AP_KB; kk++) {
-            const int key = k0 + kk;
-            float kvf[DQ], vvf[DV];
-#pragma unroll
-            for (int d = 0; d < DQ; d++) kvf[d] = __half2float(__ushort_as_half(ks[buf][kk][lane * DQ + d]));
-#pragma unroll
-            for (int d = 0; d < DV; d++) vvf[d] = __half2float(__ushort_as_half(vs[buf][kk][lane * DV + d]));
-            float s[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float p = 0.0f;
-#pragma unroll
-                for (int d = 0; d < DQ; d++) p += qv[j][d] * kvf[d];
-                s[j] = p;
-            }
-#pragma unroll
-            for (int o = 16; o; o >>= 1)
-#pragma unroll
-                for (int j = 0; j < 4; j++) s[j] += __shfl_xor_sync(0xffffffffu, s[j], o);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                if (key > lim[j]) continue;  // causal: uniform over the warp
-                const float sc = s[j] * a.scale;
-                const float mn = fmaxf(m[j], sc);
-                const float corr = expf(m[j] - mn), p = expf(sc - mn);
-                l[j] = l[j] * corr + p;
-#pragma unroll
-                for (int d = 0; d < DV; d++) acc[j][d] = acc[j][d] * corr + p * vvf[d];
-                m[j] = mn;
-            }
+        if (b + 1 < nblk) {
+            load(buf ^ 1, k0 + AP_KB);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
+        const uint16_t *kb = ks + buf * AP_KB * QP, *vb = vs + buf * AP_KB * VP;
+        // S = Q K^T for the block's 4 key tiles of 8
+        float sc[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll
+        for (int s = 0; s < KQ; s++) {
+            const int fs = QS ? 0 : s;
+            if constexpr (QS) {
+                ldsm_x4(fqh[0], qh + qrow * QP + 16 * s + qcol);
+                ldsm_x4(fql[0], ql + qrow * QP + 16 * s + qcol);
+            }
+#pragma unroll
+            for (int jp = 0; jp < 2; jp++) {
+                uint32_t bk[4];
+                ldsm_x4(bk, kb + (16 * jp + mr + (mi >> 1) * 8) * QP + 16 * s + (mi & 1) * 8);
+                tcmv::mma_f16(sc[2 * jp], fqh[fs][0], fqh[fs][1], fqh[fs][2], fqh[fs][3], bk[0], bk[1]);
+                tcmv::mma_f16(sc[2 * jp], fql[fs][0], fql[fs][1], fql[fs][2], fql[fs][3], bk[0], bk[1]);
+                tcmv::mma_f16(sc[2 * jp + 1], fqh[fs][0], fqh[fs][1], fqh[fs][2], fqh[fs][3], bk[2], bk[3]);
+                tcmv::mma_f16(sc[2 * jp + 1], fql[fs][0], fql[fs][1], fql[fs][2], fql[fs][3], bk[2], bk[3]);
+            }
+        }
+        // scale, causal mask, online softmax per row
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int key = k0 + 8 * j + 2 * tq + (e & 1), h2 = e >> 1;
+                float v = sc[j][e] * a.scale;
+                if (key > lim[h2]) v = -INFINITY;
+                sc[j][e] = v;
+                mx[h2] = fmaxf(mx[h2], v);
+            }
+        float corr[2];
+#pragma unroll
+        for (int h2 = 0; h2 < 2; h2++) {
+            mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 1));
+            mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 2));
+            const float mn = fmaxf(m[h2], mx[h2]);
+            corr[h2] = mn == -INFINITY ? 1.0f : expf(m[h2] - mn);
+            m[h2] = mn;
+        }
+        float rs[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int h2 = e >> 1;
+                const float p = m[h2] == -INFINITY ? 0.0f : expf(sc[j][e] - m[h2]);
+                sc[j][e] = p;
+                rs[h2] += p;
+            }
+#pragma unroll
+        for (int h2 = 0; h2 < 2; h2++) {
+            rs[h2] += __shfl_xor_sync(0xffffffffu, rs[h2], 1);
+            rs[h2] += __shfl_xor_sync(0xffffffffu, rs[h2], 2);
+            l[h2] = l[h2] * corr[h2] + rs[h2];
+        }
+#pragma unroll
+        for (int n = 0; n < NV; n++) o[n][0] *= corr[0], o[n][1] *= corr[0], o[n][2] *= corr[1], o[n][3] *= corr[1];
+        // O += P V, P as two k-steps of 16 keys
+#pragma unroll
+        for (int s2 = 0; s2 < 2; s2++) {
+            const uint32_t pa0 = pack_h2(sc[2 * s2][0], sc[2 * s2][1]), pa1 = pack_h2(sc[2 * s2][2], sc[2 * s2][3]);
+            const uint32_t pa2 = pack_h2(sc[2 * s2 + 1][0], sc[2 * s2 + 1][1]);
+            const uint32_t pa3 = pack_h2(sc[2 * s2 + 1][2], sc[2 * s2 + 1][3]);
+#pragma unroll
+            for (int n = 0; n < NV; n += 2) {
+                uint32_t bv[4];
+                ldsm_x4_t(bv, vb + (16 * s2 + mr + (mi & 1) * 8) * VP + 8 * n + (mi >> 1) * 8);
+                tcmv::mma_f16(o[n], pa0, pa1, pa2, pa3, bv[0], bv[1]);
+                tcmv::mma_f16(o[n + 1], pa0, pa1, pa2, pa3, bv[2], bv[3]);
+            }
+        }
+        __syncthreads();  // the buffer is refilled two blocks on
     }
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        if (!live[j]) continue;
-        const int r = 4 * warp + j, t = t0 + r / G, hh = g * G + r % G;
-        const float inv = l[j] > 0.0f ? 1.0f / l[j] : 0.0f;
+    for (int h2 = 0; h2 < 2; h2++) {
+        const int r = 16 * warp + gq + 8 * h2, t = t0 + r / G, hh = g * G + r % G;
+        if (r >= tpc * G || t >= a.n) continue;
+        const float inv = l[h2] > 0.0f ? 1.0f / l[h2] : 0.0f;
+        float *dst = a.out + (size_t)t * a.ldo + hh * a.dv + 2 * tq;
 #pragma unroll
-        for (int d = 0; d < DV; d++) a.out[(size_t)t * a.ldo + hh * a.dv + lane * DV + d] = acc[j][d] * inv;
+        for (int n = 0; n < NV; n++)
+            if (8 * n < a.dv)
+                *reinterpret_cast<float2 *>(dst + 8 * n) = make_float2(o[n][2 * h2] * inv, o[n][2 * h2 + 1] * inv);
     }
     griddep_launch();
 }
 
+template <int KQ, int NV, bool QS>
+inline int attn_prefill_launch(const AttnPrefillArgs &a, dim3 grid, cudaStream_t s)
+{
+    constexpr size_t smem = attn_prefill_smem<KQ, NV, QS>();
+    static size_t rec[64];
+    static std::mutex mu;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (tcmv::ensure_smem(attn_prefill_kernel<KQ, NV, QS>, smem, rec)) return -3;
+    }
+    return launch_k(attn_prefill_kernel<KQ, NV, QS>, grid, dim3(AP_WARPS * 32), smem, 1, s, a);
+}
+
+// The kernel width class of (q width, v width): 0 none, else a case of attn_prefill.
+inline int attn_prefill_class(int dqk, int dv)
+{
+    if (dqk < 8 || dv < 8 || dqk % 8 || dv % 8 || dqk > AP_MAXD || dv > AP_MAXD) return 0;
+    if (dqk <= 64 && dv <= 64) return 1;                // (4, 8)
+    if (dv <= 128) return dqk <= 96 ? 2 : dqk <= 128 ? 3 : dqk <= 192 ? 4 : 5;  // (6|8|12, 16), (16, 16) QS
+    return 6;                                           // (16, 32) QS
+}
+
+// Whether attn_prefill takes a (q width, v width, group) shape: widths multiples of 8 up to
+// 256 (the reference's block attention takes hd <= 256, group <= 16:
+// crates/soso-llm-api/src/cuda.rs:1562-1564), 1 <= group <= 64.
+inline bool attn_prefill_takes(int dqk, int dv, int group)
+{
+    return attn_prefill_class(dqk, dv) != 0 && group >= 1 && group <= AP_ROWS;
+}
+
 inline int attn_prefill(const AttnPrefillArgs &a, cudaStream_t s)
 {
-    if (a.heads % a.kv_heads || AP_ROWS % (a.heads / a.kv_heads) || a.dqk % 32 || a.dv % 32 ||
-        a.dqk > AP_MAXD || a.dv > AP_MAXD || a.n < 1)
+    if (a.kv_heads < 1 || a.heads % a.kv_heads || !attn_prefill_takes(a.dqk, a.dv, a.heads / a.kv_heads) ||
+        a.n < 1 || a.ldk % 8 || a.ldv % 8)
         return -1;
     const int tpc = AP_ROWS / (a.heads / a.kv_heads);
     const dim3 grid((unsigned)((a.n + tpc - 1) / tpc), (unsigned)a.kv_heads);
-    const int DQ = a.dqk / 32, DV = a.dv / 32;
-#define AP_CASE(Q, V) \
-    if (DQ == Q && DV == V) return launch_k(attn_prefill_kernel<Q, V>, grid, dim3(AP_WARPS * 32), 0, 1, s, a)
-    AP_CASE(4, 4);
-    AP_CASE(6, 4);
-    AP_CASE(2, 2);
-    AP_CASE(3, 4);
-#undef AP_CASE
+    switch (attn_prefill_class(a.dqk, a.dv)) {
+    case 1: return attn_prefill_launch<4, 8, false>(a, grid, s);    // head_dim 64
+    case 2: return attn_prefill_launch<6, 16, false>(a, grid, s);   // MLA: qk 96, v 128
+    case 3: return attn_prefill_launch<8, 16, false>(a, grid, s);   // head_dim 128
+    case 4: return attn_prefill_launch<12, 16, false>(a, grid, s);  // MLA: qk 192, v 128
+    case 5: return attn_prefill_launch<16, 16, true>(a, grid, s);
+    case 6: return attn_prefill_launch<16, 32, true>(a, grid, s);   // head_dim 256
+    }
     return -5;
 }
 

@@ -289,7 +289,9 @@ extern "C" int sb_attention_prefill(sb_ctx *c, uint32_t layer, const float *q, f
 {
     if (!c) return fail("null context");
     if (!q || !out || !k || !v || !valid_rows) return fail("null argument");
-    if (!n || !heads || !kv_heads || heads % kv_heads || hd % 32 || hd > 192 || 32 % (heads / kv_heads)) return 0;
+    if (!n || !heads || !kv_heads || heads % kv_heads ||
+        !sb::blk::attn_prefill_takes((int)hd, (int)hd, (int)(heads / kv_heads)))
+        return 0;
     std::lock_guard<std::mutex> lk(c->mu);
     const uint64_t t0 = now_ns();
     cudaError_t e = cudaSetDevice(c->device);
@@ -300,8 +302,15 @@ extern "C" int sb_attention_prefill(sb_ctx *c, uint32_t layer, const float *q, f
         std::lock_guard<std::mutex> g(g_kvm_mu);
         m = &g_kvm[c][layer];
     }
-    if (m->kv_dim && m->kv_dim != kvd) return fail("sb_attention_prefill: the layer's KV width changed");
-    size_t valid = std::min(*valid_rows, m->cap ? rows : 0);
+    if (m->kv_dim && m->kv_dim != kvd) {  // a new KV width for the layer: a new mirror
+        cudaStreamSynchronize(c->stream);
+        cudaFree(m->k);
+        cudaFree(m->v);
+        *m = sb_kv_mirror{};
+    }
+    // the caller's valid rows count up to seq_before: the block's own rows always go up
+    // (kv_espejo, crates/soso-llm-api/src/cuda.rs:1389-1416)
+    size_t valid = std::min(*valid_rows, m->cap ? seq_before : 0);
     if (rows > m->cap) {  // grow, keeping the rows the device holds
         const size_t cap = (rows + 4095) / 4096 * 4096;
         uint16_t *nk = nullptr, *nv = nullptr;

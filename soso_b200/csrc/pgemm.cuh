@@ -52,11 +52,13 @@ struct Launch {
     int cols;                 // K, the same for every matrix: a multiple of 64
 };
 
-// Weight formats: RAWB bytes of one row per 256 columns (the raw tile of a 4-stage block
-// column), and the dequantisation of 32 weights (columns 32h.. of stage p of the column)
-// into one 128-byte swizzled row of the stage tile.
+// Weight formats: RAWB bytes of one row per raw block column (SPR stages of 64 columns:
+// the unit the raw TMA ring moves), and the dequantisation of 32 weights (columns 32h.. of
+// stage p of the column) into one 128-byte swizzled row of the stage tile.  Both formats
+// keep a raw column at 144 bytes a row, so that at BN = 64 two CTAs fit on an SM.
 struct FQ4K {
     static constexpr int RAWB = 144;  // one Q4_K block (crates/sosomodel/src/layout.rs:63-64)
+    static constexpr int SPR = 4;     // 64-column stages per raw column (256 columns)
     template <bool F16>
     __device__ __forceinline__ static void half16(const uint8_t *raw, int p, int h, uint8_t *row, int r)
     {
@@ -65,7 +67,8 @@ struct FQ4K {
 };
 
 struct FQ80 {
-    static constexpr int RAWB = 288;  // eight .som Q8_0 blocks: f32 scale + 32 i8 (layout.rs:57-59)
+    static constexpr int RAWB = 144;  // four .som Q8_0 blocks: f32 scale + 32 i8 (layout.rs:57-59)
+    static constexpr int SPR = 2;     // 64-column stages per raw column (128 columns)
     // block 2p + h of the column: w_i = scale * q_i (dequant.rs:74-102), rounded once
     template <bool F16>
     __device__ __forceinline__ static void half16(const uint8_t *raw, int p, int h, uint8_t *row, int r)
@@ -76,7 +79,12 @@ struct FQ80 {
 #pragma unroll
         for (int c = 0; c < 4; c++) {  // 8 weights -> one 16-byte chunk of the swizzled row
             const uint32_t w0 = q[2 * c], w1 = q[2 * c + 1];
-            auto v = [&](uint32_t w, int k) { return sc * (float)(int8_t)(w >> (8 * k)); };
+            // the signed code as a float without an int -> float conversion: 2^23 + 128 + q has
+            // q + 128 in its low mantissa bits (the code's sign bit flipped), so the difference
+            // is q exactly
+            auto v = [&](uint32_t w, int k) {
+                return sc * (__uint_as_float(0x4B000000u | (((w >> (8 * k)) & 0xFFu) ^ 0x80u)) - 8388736.0f);
+            };
             const uint4 out = make_uint4(pf::pack16<F16>(v(w0, 0), v(w0, 1)), pf::pack16<F16>(v(w0, 2), v(w0, 3)),
                                          pf::pack16<F16>(v(w1, 0), v(w1, 1)), pf::pack16<F16>(v(w1, 2), v(w1, 3)));
             const int chunk = 4 * h + c;
@@ -111,7 +119,7 @@ __device__ __forceinline__ void mma(uint32_t d_tmem, uint64_t adesc, uint64_t bd
 }
 
 template <class W, int BN, bool F16>
-__global__ void __launch_bounds__(THREADS, 1) pg_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const Launch a)
+__global__ void __launch_bounds__(THREADS, BN == 64 ? 2 : 1) pg_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const Launch a)
 {
     using L = Lay<W, BN>;
     griddep_wait();  // the tile table and X are written by earlier kernels
@@ -163,8 +171,8 @@ __global__ void __launch_bounds__(THREADS, 1) pg_gemm_kernel(const __grid_consta
             const uint64_t pol = tcmv::l2_evict_first();
             for (int ks = 0; ks < KS && !failed; ks++) {
                 const int st = ks % NST;
-                if (ks % 4 == 0) {  // a new raw block column
-                    const int rk = ks / 4, rs = rk % NRAW;
+                if (ks % W::SPR == 0) {  // a new raw block column
+                    const int rk = ks / W::SPR, rs = rk % NRAW;
                     if (rk >= NRAW && !tcmv::mbar_wait(&raw_empty[rs], ((rk / NRAW) - 1) & 1, pf::WAIT)) {
                         failed = true;
                         break;
@@ -209,7 +217,7 @@ __global__ void __launch_bounds__(THREADS, 1) pg_gemm_kernel(const __grid_consta
         // dequantisers: thread t takes weight row t % 128, half t / 128 of every stage
         const int r = (threadIdx.x - 64) & (BM - 1), hh = (threadIdx.x - 64) / BM;
         for (int ks = 0; ks < KS && !failed; ks++) {
-            const int st = ks % NST, rk = ks / 4, rs = rk % NRAW, p = ks % 4;
+            const int st = ks % NST, rk = ks / W::SPR, rs = rk % NRAW, p = ks % W::SPR;
             if (p == 0 && !tcmv::mbar_wait(&raw_full[rs], (rk / NRAW) & 1, pf::WAIT)) failed = true;
             if (!failed && ks >= NST && !tcmv::mbar_wait(&st_empty[st], ((ks / NST) - 1) & 1, pf::WAIT)) failed = true;
             if (failed) {
@@ -221,7 +229,7 @@ __global__ void __launch_bounds__(THREADS, 1) pg_gemm_kernel(const __grid_consta
             __syncwarp();
             if (lane == 0) {
                 tcmv::mbar_arrive(&w_full[st]);
-                if (p == 3 || ks == KS - 1) tcmv::mbar_arrive(&raw_empty[rs]);
+                if (p == W::SPR - 1 || ks == KS - 1) tcmv::mbar_arrive(&raw_empty[rs]);
             }
         }
         // epilogue: the accumulators of this warp's 32 lanes (weight rows)
@@ -287,7 +295,7 @@ inline int make_wmap(CUtensorMap *m, uint8_t dtype, const void *w, int rows, int
         if (cols % 256) return -1;
         rb = (cuuint64_t)(cols / 256) * 144, bw = FQ4K::RAWB / 8;
     } else if (dtype == SB_DTYPE_Q8_0_R || (dtype == SB_DTYPE_Q8_0 && cols % 128 == 0)) {
-        if (cols % 32 || cols < 256) return -1;
+        if (cols % 32 || cols < 128) return -1;
         rb = (cuuint64_t)(((size_t)cols / 32 * 36 + 15) & ~(size_t)15), bw = FQ80::RAWB / 8;
     } else {
         return -5;

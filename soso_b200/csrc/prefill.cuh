@@ -174,8 +174,12 @@ __device__ __forceinline__ void q4k_half_to_16(const uint8_t *blk, int p, int h,
 #pragma unroll
             for (int wd = 0; wd < 4; wd++) {
                 const uint32_t v = h ? (qw[wd] >> 4) & 0x0F0F0F0Fu : qw[wd] & 0x0F0F0F0Fu;
-                const float q0 = (float)(v & 0xFF), q1 = (float)((v >> 8) & 0xFF), q2 = (float)((v >> 16) & 0xFF),
-                            q3 = (float)(v >> 24);
+                // the 4-bit codes as floats without int -> float conversions (a quarter-rate
+                // pipe): 2^23 + q has q in its low mantissa bits, minus 2^23 is q exactly
+                const float q0 = __uint_as_float(0x4B000000u | (v & 0xFFu)) - 8388608.0f;
+                const float q1 = __uint_as_float(0x4B000000u | ((v >> 8) & 0xFFu)) - 8388608.0f;
+                const float q2 = __uint_as_float(0x4B000000u | ((v >> 16) & 0xFFu)) - 8388608.0f;
+                const float q3 = __uint_as_float(0x4B000000u | (v >> 24)) - 8388608.0f;
                 out[2 * wd] = pack16<F16>(a * q0 - b, a * q1 - b);
                 out[2 * wd + 1] = pack16<F16>(a * q2 - b, a * q3 - b);
             }

@@ -520,8 +520,9 @@ extern "C" int sb_decode_prefill(sb_ctx *c, const int32_t *tokens, size_t n, siz
         else need[k++] = &L.q, need[k++] = &L.k, need[k++] = &L.v;
         for (int j = 0; j < k; j++)
             if (!pf_gemm_dtype(need[j]->dt) || need[j]->cols % 256) return 0;
-        if (L.mla && (L.qk_nope + L.qk_rope) % 32) return 0;
-        if (!L.mla && (L.hd % 32 || 32 % (L.heads / L.kvh))) return 0;
+        if (L.mla && !blk::attn_prefill_takes((int)(L.qk_nope + L.qk_rope), (int)L.v_dim, (int)(L.heads / L.kvh)))
+            return 0;
+        if (!L.mla && !blk::attn_prefill_takes((int)L.hd, (int)L.hd, (int)(L.heads / L.kvh))) return 0;
         if (L.moe) {
             if (!L.ex_pairs || !(pf_gemm_dtype(L.router.dt) || L.router.dt == SB_DTYPE_F32) ||
                 !pf_gemm_dtype(L.ex[0].dt) ||
