@@ -197,11 +197,36 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attn_prefill_kernel(AttnPrefill
     // the CTA's 64 rows: tpc tokens x the G query heads of kv head g (rows past tpc G idle)
     const int G = a.heads / a.kv_heads, g = blockIdx.y, tpc = AP_ROWS / G, t0 = blockIdx.x * tpc;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
-    // q of the CTA's rows -> f16 hi / lo in shared memory
-    for (int i = threadIdx.x; i < AP_ROWS * DQ; i += AP_WARPS * 32) {
-        const int r = i / DQ, d = i % DQ, t = t0 + r / G, hh = g * G + r % G;
-        const float x = r < tpc * G && t < a.n && d < a.dqk ? a.q[(size_t)t * a.ldq + hh * a.dqk + d] : 0.0f;
-        split_f16(x, qh[r * QP + d], ql[r * QP + d]);
+    // q of the CTA's rows -> f16 hi / lo in shared memory: 16-byte loads, a batch of them in
+    // flight before the first is used
+    {
+        constexpr int C4 = DQ / 4, PER = AP_ROWS * C4 / (AP_WARPS * 32), NB = PER % 8 == 0 ? 8 : 4;
+        static_assert(AP_ROWS * C4 % (AP_WARPS * 32) == 0 && PER % NB == 0, "q staging shape");
+#pragma unroll 1
+        for (int i0 = 0; i0 < PER; i0 += NB) {
+            float4 xv[NB];
+#pragma unroll
+            for (int u = 0; u < NB; u++) {
+                const int i = threadIdx.x + (i0 + u) * AP_WARPS * 32, r = i / C4, d = 4 * (i % C4);
+                const int t = t0 + r / G, hh = g * G + r % G;
+                xv[u] = r < tpc * G && t < a.n && d < a.dqk
+                            ? *reinterpret_cast<const float4 *>(a.q + (size_t)t * a.ldq + hh * a.dqk + d)
+                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < NB; u++) {
+                const int i = threadIdx.x + (i0 + u) * AP_WARPS * 32, r = i / C4, d = 4 * (i % C4);
+                uint16_t hi[4], lo[4];
+                split_f16(xv[u].x, hi[0], lo[0]);
+                split_f16(xv[u].y, hi[1], lo[1]);
+                split_f16(xv[u].z, hi[2], lo[2]);
+                split_f16(xv[u].w, hi[3], lo[3]);
+                *reinterpret_cast<uint2 *>(qh + r * QP + d) =
+                    make_uint2(hi[0] | ((uint32_t)hi[1] << 16), hi[2] | ((uint32_t)hi[3] << 16));
+                *reinterpret_cast<uint2 *>(ql + r * QP + d) =
+                    make_uint2(lo[0] | ((uint32_t)lo[1] << 16), lo[2] | ((uint32_t)lo[3] << 16));
+            }
+        }
     }
     __syncthreads();
     const int mi = lane >> 3, mr = lane & 7;
@@ -376,7 +401,7 @@ inline bool attn_prefill_takes(int dqk, int dv, int group)
 inline int attn_prefill(const AttnPrefillArgs &a, cudaStream_t s)
 {
     if (a.kv_heads < 1 || a.heads % a.kv_heads || !attn_prefill_takes(a.dqk, a.dv, a.heads / a.kv_heads) ||
-        a.n < 1 || a.ldk % 8 || a.ldv % 8)
+        a.n < 1 || a.ldk % 8 || a.ldv % 8 || a.ldq % 4 || ((uintptr_t)a.q & 15))
         return -1;
     const int tpc = AP_ROWS / (a.heads / a.kv_heads);
     const dim3 grid((unsigned)((a.n + tpc - 1) / tpc), (unsigned)a.kv_heads);

@@ -14,7 +14,8 @@
 // The machinery is the dense GEMM's (prefill.cuh): tcgen05.mma kind::f16 with the D tile
 // [128 weight rows x BN tokens] f32 in tensor memory, A = weight rows dequantised by eight
 // warps into 128-byte-swizzled K-major shared memory, B = X (16-bit, written by an earlier
-// kernel) by TMA with the 128-byte swizzle, raw weight blocks by TMA, a 3-stage ring.
+// kernel) by TMA with the 128-byte swizzle, a 3-stage ring; the raw weight block columns come
+// by TMA from a warp of their own, two columns ahead of the dequantisers.
 // New here: the weight formats are traits (Q4_K, and Q8_0 with 16-byte-aligned rows), the
 // token tile BN is 64 or 256 (a routed expert sees ~n*top_k/n_exp tokens), every CTA finds
 // its tile in a table (device-written for MoE: CTAs past the table's count leave at once),
@@ -26,7 +27,9 @@
 namespace sb {
 namespace pg {
 
-constexpr int BM = pf::BM, BK = pf::BK, NST = pf::NST, NRAW = pf::NRAW, NDQ = pf::NDQ, THREADS = pf::THREADS;
+constexpr int BM = pf::BM, BK = pf::BK, NST = pf::NST, NRAW = pf::NRAW, NDQ = pf::NDQ;
+// warp 0: X loads, warp 1: MMA issue, warps 2..9: dequantisers / epilogue, warp 10: raw weight loads
+constexpr int RAW_WARP = 2 + NDQ, THREADS = (RAW_WARP + 1) * 32;
 
 // One output tile: weight map `map` and output descriptor `out` of the launch's tables,
 // weight rows [row0, row0 + 128), X / Y rows [tok0, tok0 + ntok) with ntok <= BN.
@@ -74,19 +77,18 @@ struct FQ80 {
     __device__ __forceinline__ static void half16(const uint8_t *raw, int p, int h, uint8_t *row, int r)
     {
         const uint8_t *b = raw + (2 * p + h) * 36;
-        const float sc = *reinterpret_cast<const float *>(b);
+        const uint64_t sc2 = pf::dup2(*reinterpret_cast<const float *>(b)), nb2 = pf::dup2(-8388736.0f);
         const uint32_t *q = reinterpret_cast<const uint32_t *>(b + 4);
 #pragma unroll
         for (int c = 0; c < 4; c++) {  // 8 weights -> one 16-byte chunk of the swizzled row
-            const uint32_t w0 = q[2 * c], w1 = q[2 * c + 1];
-            // the signed code as a float without an int -> float conversion: 2^23 + 128 + q has
-            // q + 128 in its low mantissa bits (the code's sign bit flipped), so the difference
-            // is q exactly
-            auto v = [&](uint32_t w, int k) {
-                return sc * (__uint_as_float(0x4B000000u | (((w >> (8 * k)) & 0xFFu) ^ 0x80u)) - 8388736.0f);
+            // the codes' sign bits flipped: bytes q + 128, exact floats q after the bias
+            const uint32_t w0 = q[2 * c] ^ 0x80808080u, w1 = q[2 * c + 1] ^ 0x80808080u;
+            // scale * q, one rounding, two weights an instruction
+            auto v = [&](uint32_t w, uint32_t s0, uint32_t s1) {
+                return pf::pack16x2<F16>(pf::mul_f32x2(pf::codes2(w, s0, s1, nb2), sc2));
             };
-            const uint4 out = make_uint4(pf::pack16<F16>(v(w0, 0), v(w0, 1)), pf::pack16<F16>(v(w0, 2), v(w0, 3)),
-                                         pf::pack16<F16>(v(w1, 0), v(w1, 1)), pf::pack16<F16>(v(w1, 2), v(w1, 3)));
+            const uint4 out = make_uint4(v(w0, pf::SEL_B0, pf::SEL_B1), v(w0, pf::SEL_B2, pf::SEL_B3),
+                                         v(w1, pf::SEL_B0, pf::SEL_B1), v(w1, pf::SEL_B2, pf::SEL_B3));
             const int chunk = 4 * h + c;
             *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = out;
         }
@@ -168,18 +170,8 @@ __global__ void __launch_bounds__(THREADS, BN == 64 ? 2 : 1) pg_gemm_kernel(cons
 
     if (warp == 0) {
         if (lane == 0) {
-            const uint64_t pol = tcmv::l2_evict_first();
             for (int ks = 0; ks < KS && !failed; ks++) {
                 const int st = ks % NST;
-                if (ks % W::SPR == 0) {  // a new raw block column
-                    const int rk = ks / W::SPR, rs = rk % NRAW;
-                    if (rk >= NRAW && !tcmv::mbar_wait(&raw_empty[rs], ((rk / NRAW) - 1) & 1, pf::WAIT)) {
-                        failed = true;
-                        break;
-                    }
-                    tcmv::mbar_expect_tx_arrive(&raw_full[rs], (unsigned)L::RAW_BYTES);
-                    tcmv::tma_load_2d(sraw + rs * L::RAW_BYTES, wmap, rk * (W::RAWB / 8), t.row0, &raw_full[rs], pol);
-                }
                 if (ks >= NST && !tcmv::mbar_wait(&st_empty[st], ((ks / NST) - 1) & 1, pf::WAIT)) {
                     failed = true;
                     break;
@@ -193,6 +185,23 @@ __global__ void __launch_bounds__(THREADS, BN == 64 ? 2 : 1) pg_gemm_kernel(cons
             }
             if (failed) set_dev_error(0x81u);
         }
+    } else if (warp == RAW_WARP) {
+        // raw weight block columns, as far ahead as the raw ring allows (not paced by the X
+        // stages: a raw column comes from DRAM and feeds SPR stages)
+        if (lane == 0) {
+            const uint64_t pol = tcmv::l2_evict_first();
+            const int NRK = (KS + W::SPR - 1) / W::SPR;
+            for (int rk = 0; rk < NRK; rk++) {
+                const int rs = rk % NRAW;
+                if (rk >= NRAW && !tcmv::mbar_wait(&raw_empty[rs], ((rk / NRAW) - 1) & 1, pf::WAIT)) {
+                    set_dev_error(0x85u);
+                    break;
+                }
+                tcmv::mbar_expect_tx_arrive(&raw_full[rs], (unsigned)L::RAW_BYTES);
+                tcmv::tma_load_2d(sraw + rs * L::RAW_BYTES, wmap, rk * (W::RAWB / 8), t.row0, &raw_full[rs], pol);
+            }
+        }
+        __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
             for (int ks = 0; ks < KS; ks++) {

@@ -149,6 +149,56 @@ __device__ __forceinline__ uint32_t pack16(float a, float b)
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+// Codes as exact floats, two at a time: prmt puts byte j of v into the low mantissa byte of
+// 2^23 (0x4B000000), i.e. the float 2^23 + byte; one packed f32x2 add of -(2^23 + bias)
+// leaves byte - bias exactly (bias 128 for a signed byte whose sign bit was flipped).
+__device__ __forceinline__ uint32_t prmt_f(uint32_t v, uint32_t sel)
+{
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(v), "r"(0x4B000000u), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2(uint32_t lo, uint32_t hi)
+{
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+    return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// bytes (j0, j1) of v as floats minus the bias held (negated, twice) in nbias2
+__device__ __forceinline__ uint64_t codes2(uint32_t v, uint32_t sel0, uint32_t sel1, uint64_t nbias2)
+{
+    return add_f32x2(f2(prmt_f(v, sel0), prmt_f(v, sel1)), nbias2);
+}
+__device__ __forceinline__ uint64_t dup2(float x)
+{
+    return f2(__float_as_uint(x), __float_as_uint(x));
+}
+template <bool F16>
+__device__ __forceinline__ uint32_t pack16x2(uint64_t w)
+{
+    return pack16<F16>(__uint_as_float((uint32_t)w), __uint_as_float((uint32_t)(w >> 32)));
+}
+// prmt selectors: byte j of v, then bytes 4, 4, 7 of 0x4B000000 (0, 0, 0x4B)
+constexpr uint32_t SEL_B0 = 0x7440u, SEL_B1 = 0x7441u, SEL_B2 = 0x7442u, SEL_B3 = 0x7443u;
+
 // Q4_K, one byte pair p of the block in `blk` (144 bytes), nibble half h: the 32 weights of
 // sub-block 2p + h (h = 0: low nibbles, columns 0..31 of the stage; 1: high nibbles,
 // columns 32..63) as d*sc*q - dmin*m (crates/sosomodel/src/dequant.rs:150-248), rounded to
@@ -164,6 +214,7 @@ __device__ __forceinline__ void q4k_half_to_16(const uint8_t *blk, int p, int h,
     if (j < 4) s_ = sc[j] & 63, m_ = sc[j + 4] & 63;
     else s_ = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4), m_ = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
     const float a = d * (float)s_, b = dmin * (float)m_;
+    const uint64_t a2 = dup2(a), mb2 = dup2(-b), nb2 = dup2(-8388608.0f);
     const uint4 *q4 = reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
 #pragma unroll
     for (int half = 0; half < 2; half++) {  // 16 bytes -> weights 16*half .. +15 of the sub-block
@@ -174,14 +225,9 @@ __device__ __forceinline__ void q4k_half_to_16(const uint8_t *blk, int p, int h,
 #pragma unroll
             for (int wd = 0; wd < 4; wd++) {
                 const uint32_t v = h ? (qw[wd] >> 4) & 0x0F0F0F0Fu : qw[wd] & 0x0F0F0F0Fu;
-                // the 4-bit codes as floats without int -> float conversions (a quarter-rate
-                // pipe): 2^23 + q has q in its low mantissa bits, minus 2^23 is q exactly
-                const float q0 = __uint_as_float(0x4B000000u | (v & 0xFFu)) - 8388608.0f;
-                const float q1 = __uint_as_float(0x4B000000u | ((v >> 8) & 0xFFu)) - 8388608.0f;
-                const float q2 = __uint_as_float(0x4B000000u | ((v >> 16) & 0xFFu)) - 8388608.0f;
-                const float q3 = __uint_as_float(0x4B000000u | (v >> 24)) - 8388608.0f;
-                out[2 * wd] = pack16<F16>(a * q0 - b, a * q1 - b);
-                out[2 * wd + 1] = pack16<F16>(a * q2 - b, a * q3 - b);
+                // a * q - b with one rounding (q * a is exact), two weights an instruction
+                out[2 * wd] = pack16x2<F16>(fma_f32x2(codes2(v, SEL_B0, SEL_B1, nb2), a2, mb2));
+                out[2 * wd + 1] = pack16x2<F16>(fma_f32x2(codes2(v, SEL_B2, SEL_B3, nb2), a2, mb2));
             }
             // columns 32*h + 16*half .. +15 = 16-byte chunks c0, c0 + 1 of the 128-byte row
             const int c0 = 4 * h + 2 * half;

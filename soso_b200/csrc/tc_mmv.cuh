@@ -482,7 +482,7 @@ __global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_cons
 // With `sel` set, the batch is B[*sel], one of several prepared batches (the number of
 // routed experts this rank owns picks the one whose split fits).
 template <class F>
-__global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_dev_kernel(const Batch *__restrict__ B,
+__global__ void __launch_bounds__(F::THREADS, F::MINB) tc_mmv_dev_kernel(const Batch *__restrict__ B,
                                                                    const int *__restrict__ sel, Ws ws)
 {
     if (sel) {

@@ -34,6 +34,9 @@
 #ifndef SB_Q4K_NSTREAM
 #define SB_Q4K_NSTREAM 3  // consumer teams (build-time tuning knob)
 #endif
+#ifndef SB_Q4K_MINB
+#define SB_Q4K_MINB 1  // CTAs per SM the engine's matvec is compiled for (build-time tuning knob)
+#endif
 #include "tc_common.cuh"
 
 namespace sb {
@@ -46,6 +49,7 @@ struct Q4K {
     static constexpr int NSTREAM = SB_Q4K_NSTREAM;  // stages in compute at once (teams)
     static constexpr int NCW = NCONS * NSTREAM;
     static constexpr int THREADS = (NCW + 1) * 32;
+    static constexpr int MINB = SB_Q4K_MINB;
     static constexpr int NSLOT = SB_Q4K_NSLOT;  // a multiple of NSTREAM
     static constexpr int BOXW = SBLK * 18;  // u64 per box row (576 B)
     static constexpr int ROWB = BOXW * 8;

@@ -71,6 +71,7 @@ struct Q6KP {
     static constexpr int NSTREAM = SB_Q6K_NSTREAM;
     static constexpr int NCW = NCONS * NSTREAM;
     static constexpr int THREADS = (NCW + 1) * 32;
+    static constexpr int MINB = 1;
     static constexpr int NSLOT = SB_Q6K_NSLOT;  // a multiple of NSTREAM
     static constexpr int BOXW = 212;  // u64: one group (210) + 16 bytes
     static constexpr int ROWB = BOXW * 8;

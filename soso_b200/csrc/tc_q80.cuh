@@ -42,6 +42,7 @@ struct Q80 {
     static constexpr int NSTREAM = 3;
     static constexpr int NCW = NCONS * NSTREAM;
     static constexpr int THREADS = (NCW + 1) * 32;
+    static constexpr int MINB = 1;
     static constexpr int NSLOT = 9;       // a multiple of NSTREAM
     static constexpr int BOXW = SBLK * 18 + 2;  // u64 per box row: one stage (576 B) + 16 B, so that
                                                 // rows are 148 words apart and the 4-byte fragment loads
