@@ -421,7 +421,14 @@ static void *stream_ws(cudaStream_t s, size_t bytes)
     e.second = 0;
     size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
     if (cudaMalloc(&e.first, want) != cudaSuccess) return nullptr;
-    cudaMemset(e.first, 0, want);
+    // zeroed on the launching stream itself, so that the first kernel on it is ordered after
+    // the clear (a plain cudaMemset runs on the legacy stream, which a non-blocking stream
+    // does not wait for)
+    if (cudaMemsetAsync(e.first, 0, want, s) != cudaSuccess) {
+        cudaFree(e.first);
+        e.first = nullptr;
+        return nullptr;
+    }
     e.second = want;
     return e.first;
 }
