@@ -133,7 +133,9 @@ __global__ void __launch_bounds__(THREADS, BN == 64 ? 2 : 1) pg_gemm_kernel(cons
     const Tile t = a.tiles[blockIdx.x];
     const CUtensorMap *wmap = a.maps + t.map;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *b = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // aligned to 1024 by an offset from the shared array itself, so that the compiler keeps
+    // every access derived from it in the shared window (ld.shared, not generic loads)
+    uint8_t *b = smem_raw + ((1024u - (tcmv::smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t *sx = b, *sw = b + NST * L::X_BYTES, *sraw = sw + NST * L::W_BYTES;
     uint64_t *bar = reinterpret_cast<uint64_t *>(sraw + NRAW * L::RAW_BYTES);
     uint64_t *x_full = bar, *w_full = bar + NST, *st_empty = bar + 2 * NST, *raw_full = bar + 3 * NST,

@@ -54,9 +54,10 @@ constexpr int RAW_ROWB = 144;
 constexpr int RAW_BYTES = BM * RAW_ROWB;  // 18 KiB
 
 struct Smem {
-    uint8_t *x[NST];        // 1024-aligned
-    uint8_t *w[NST];        // 1024-aligned
-    uint8_t *raw[NRAW];
+    uint8_t *x0, *w0, *raw0;  // stage i at x0 + i X_BYTES, w0 + i W_BYTES (1024-aligned), raw0 + i RAW_BYTES
+    __device__ uint8_t *x(int i) const { return x0 + i * X_BYTES; }
+    __device__ uint8_t *w(int i) const { return w0 + i * W_BYTES; }
+    __device__ uint8_t *raw(int i) const { return raw0 + i * RAW_BYTES; }
     uint64_t *x_full, *w_full, *st_empty, *raw_full, *raw_empty, *acc_full;
     uint32_t *tmem_addr;
 };
@@ -66,12 +67,13 @@ inline size_t smem_bytes() { return 1024 + NST * (X_BYTES + W_BYTES) + NRAW * RA
 __device__ __forceinline__ Smem carve(uint8_t *raw_base)
 {
     Smem s;
-    uint8_t *b = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(raw_base) + 1023) & ~uintptr_t(1023));
-    for (int i = 0; i < NST; i++) s.x[i] = b + i * X_BYTES;
+    // aligned by an offset from the shared array, which keeps the accesses in the shared window
+    uint8_t *b = raw_base + ((1024u - (tcmv::smem_u32(raw_base) & 1023u)) & 1023u);
+    s.x0 = b;
     b += NST * X_BYTES;
-    for (int i = 0; i < NST; i++) s.w[i] = b + i * W_BYTES;
+    s.w0 = b;
     b += NST * W_BYTES;
-    for (int i = 0; i < NRAW; i++) s.raw[i] = b + i * RAW_BYTES;
+    s.raw0 = b;
     b += NRAW * RAW_BYTES;
     uint64_t *bar = reinterpret_cast<uint64_t *>(b);
     s.x_full = bar;
@@ -206,13 +208,18 @@ constexpr uint32_t SEL_B0 = 0x7440u, SEL_B1 = 0x7441u, SEL_B2 = 0x7442u, SEL_B3 
 template <bool F16>
 __device__ __forceinline__ void q4k_half_to_16(const uint8_t *blk, int p, int h, uint8_t *row, int r)
 {
-    const float d = __half2float(*reinterpret_cast<const __half *>(blk));
-    const float dmin = __half2float(*reinterpret_cast<const __half *>(blk + 2));
-    const uint8_t *sc = blk + 4;
+    // the block's 16-byte head in one load: d, dmin (f16), then the 12 packed scale bytes
+    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+    auto sc = [&](int k) {  // scale byte k (selects, not an indexed array: no local memory)
+        const uint32_t w = k < 4 ? hd.y : k < 8 ? hd.z : hd.w;
+        return (w >> (8 * (k & 3))) & 0xFFu;
+    };
     const int j = 2 * p + h;
     unsigned s_, m_;
-    if (j < 4) s_ = sc[j] & 63, m_ = sc[j + 4] & 63;
-    else s_ = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4), m_ = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    if (j < 4) s_ = sc(j) & 63, m_ = sc(j + 4) & 63;
+    else s_ = (sc(j + 4) & 15) | ((sc(j - 4) >> 6) << 4), m_ = (sc(j + 4) >> 4) | ((sc(j) >> 6) << 4);
     const float a = d * (float)s_, b = dmin * (float)m_;
     const uint64_t a2 = dup2(a), mb2 = dup2(-b), nb2 = dup2(-8388608.0f);
     const uint4 *q4 = reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
@@ -311,7 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         break;
                     }
                     tcmv::mbar_expect_tx_arrive(&s.raw_full[rs], (unsigned)RAW_BYTES);
-                    tcmv::tma_load_2d(s.raw[rs], &wmap, (rk + ks0 / 4) * (RAW_ROWB / 8), row0, &s.raw_full[rs], pol);
+                    tcmv::tma_load_2d(s.raw(rs), &wmap, (rk + ks0 / 4) * (RAW_ROWB / 8), row0, &s.raw_full[rs], pol);
                 }
                 if (ks >= NST && !tcmv::mbar_wait(&s.st_empty[st], ((ks / NST) - 1) & 1, WAIT)) {
                     failed = true;
@@ -320,7 +327,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tcmv::mbar_expect_tx_arrive(&s.x_full[st], (unsigned)X_BYTES);
                 asm volatile(
                     "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
-                    "{%2, %3}], [%4];" ::"r"(tcmv::smem_u32(s.x[st])),
+                    "{%2, %3}], [%4];" ::"r"(tcmv::smem_u32(s.x(st))),
                     "l"(&xmap), "r"((ks0 + ks) * BK), "r"(tok0), "r"(tcmv::smem_u32(&s.x_full[st]))
                     : "memory");
             }
@@ -337,7 +344,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     break;
                 }
                 fence_after_sync();
-                const uint64_t ad = sw128_desc(s.w[st]), bd = sw128_desc(s.x[st]);
+                const uint64_t ad = sw128_desc(s.w(st)), bd = sw128_desc(s.x(st));
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; kk++)  // K16 slices: 32 bytes along the swizzled row
                     mma_16bit<F16>(tmem, ad + (uint64_t)(2 * kk), bd + (uint64_t)(2 * kk), (ks | kk) ? 1u : 0u);
@@ -357,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 set_dev_error(0x73u);
                 break;
             }
-            q4k_half_to_16<F16>(s.raw[rs] + r * RAW_ROWB, p, hh, s.w[st] + r * 128, r);
+            q4k_half_to_16<F16>(s.raw(rs) + r * RAW_ROWB, p, hh, s.w(st) + r * 128, r);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
             __syncwarp();
             if (lane == 0) {

@@ -30,7 +30,11 @@ def test_decode_a_model_directory(tmp_path, which):
     cfg0 = getattr(decode, which)
     if cfg0.mla:
         cfg0 = dataclasses.replace(cfg0, head_dim=cfg0.hidden // cfg0.heads)
-    write_model(tmp_path, cfg0, decode.synth_model(cfg0, "somdec_" + which), n_shared=1 if cfg0.shared_ffn else 0)
+    # a head width other than hidden / heads travels in the layer spec's v_dim, as gguf2som
+    # writes it for such models (crates/gguf2som/src/lib.rs:804-808)
+    vd = cfg0.head_dim if not cfg0.mla and cfg0.head_dim != cfg0.hidden // cfg0.heads else None
+    write_model(tmp_path, cfg0, decode.synth_model(cfg0, "somdec_" + which), n_shared=1 if cfg0.shared_ffn else 0,
+                v_dim=vd)
     cfg, tensors, m = load_decode_model(str(tmp_path))
     try:
         prompt = synth.rng("somdec", which).integers(0, cfg.vocab, 24).astype(np.int32)
