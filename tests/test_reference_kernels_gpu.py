@@ -17,7 +17,8 @@ the kernels the drop-in replaces, checked for equal results and timed.
   weights and x to f16 the same way and sum in f32: within 1e-3 of the rms of Y.
 
 Each case prints one REFKERN line with both sides' times (CUDA events on the launching
-stream, after warm-up).  Nothing here asserts on speed.
+stream, after warm-up; the best of three runs, against other work on a shared GPU).
+Nothing here asserts on speed.
 """
 import ctypes
 import json
@@ -81,18 +82,22 @@ def refmod():
     m.close()
 
 
-def _time(fn, reps, warm=3):
+def _time(fn, reps, warm=3, trials=3):
+    """Seconds per call: the best of `trials` runs of `reps` calls, after `warm` calls."""
     import torch
     for _ in range(warm):
         fn()
     torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(reps):
-        fn()
-    b.record()
-    torch.cuda.synchronize()
-    return a.elapsed_time(b) / reps * 1e-3  # seconds per call
+    best = float("inf")
+    for _ in range(trials):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        best = min(best, a.elapsed_time(b) / reps * 1e-3)
+    return best
 
 
 def test_decode_matvec_vs_reference(refmod):
