@@ -476,13 +476,17 @@ def decode_bench(device: int, rank: int, which: str = "dense", world: int = 1) -
     peaks = load_peaks()
     hbm = peaks["hbm_gbs"] * (world if group else 1)  # a sharded model streams from every rank's HBM
     tps = n_gen / dt
+    split_routes = None
+    if group and rank == 0 and cfg.n_exp:
+        # the experts the split model's routers chose at every position, with their gaps
+        split_routes = [sess.route_trace(p) for p in range(n_prompt + n_gen)]
     sess.close()
     agree = None
     if group:
         # the same model and prompt unsharded on rank 0's GPU: token agreement of the split run,
         # and at a first divergence the unsharded top-1 / top-2 gap (a tie or not)
         full_toks = np.concatenate([first[-1:], toks])
-        agree = group_agreement(cfg, which, prompt, full_toks, device) if rank == 0 else None
+        agree = group_agreement(cfg, which, prompt, full_toks, device, split_routes) if rank == 0 else None
         agree = group[2](json.dumps(agree).encode())[0]
         agree = json.loads(agree)
     desc = {"dense": "configs[2]: Qwen2.5-3B-style dense, 36 layers, hidden 2048, 16 q / 2 kv heads x 128, SwiGLU "
@@ -540,19 +544,37 @@ def load_bf16_peak() -> float:
     return 1590.0
 
 
-def group_agreement(cfg, which: str, prompt, split_toks, device: int) -> dict:
+def group_agreement(cfg, which: str, prompt, split_toks, device: int, split_routes=None) -> dict:
     """The greedy chain of the split model against the same model on one GPU (rank 0's): the
     share of identical generated tokens, the first step where they differ and, there, the
     one-GPU top-1 / top-2 logit gap over the rms of the logits (a gap near the two runs'
-    rounding difference is a tie, which either run may break)."""
+    rounding difference is a tie, which either run may break).  For a MoE model also the first
+    position where the two runs' routers chose different experts, with both runs' router-logit
+    gaps between the k-th choice and the next expert there: a router near-tie broken the other
+    way changes that token's hidden state and, through the KV rows, every later step."""
     from soso_b200 import decode
     model = decode.synth_model(cfg, f"{which}.0")  # every expert (the split run's rank 0 held its own)
     s = decode.DecodeSession(cfg, model, device=device)
     try:
-        one = s.greedy(prompt, len(prompt) + len(split_toks) - 1)[len(prompt) - 1:]
+        P = len(prompt)
+        one = s.greedy(prompt, P + len(split_toks) - 1)[P - 1:]
         n = len(split_toks)
         same = one[:n] == split_toks
         first = None if same.all() else int(np.argmax(~same))
+        route = None
+        if split_routes is not None:
+            # positions run on the same tokens by both: the prompt, then the common prefix
+            last = P - 1 + (n - 1 if first is None else first)
+            for pos in range(min(last + 1, len(split_routes))):
+                ids1, gaps1 = s.route_trace(pos)
+                ids2, gaps2 = split_routes[pos]
+                diff = [l for l in ids1 if set(ids1[l].tolist()) != set(ids2[l].tolist())]
+                if diff:
+                    l = diff[0]
+                    route = {"position": pos, "layer": l, "layers_differing": len(diff),
+                             "router_gap_1gpu": round(gaps1[l], 6), "router_gap_split": round(gaps2[l], 6),
+                             "first_token_divergence_position": None if first is None else P - 1 + first}
+                    break
         gap = None
         if first is not None:
             # teacher forced on the common prefix: the logits of the step where the runs part
@@ -562,8 +584,11 @@ def group_agreement(cfg, which: str, prompt, split_toks, device: int) -> dict:
                 lg = s.token(orc_embed(int(t)), i)
             top = np.sort(lg.astype(np.float64))[-2:]
             gap = float((top[1] - top[0]) / np.sqrt(np.mean(lg.astype(np.float64) ** 2)))
-        return {"tokens": n, "identical_frac": round(float(same.mean()), 4), "first_divergence": first,
-                "gap_at_divergence": gap}
+        out = {"tokens": n, "identical_frac": round(float(same.mean()), 4), "first_divergence": first,
+               "gap_at_divergence": gap}
+        if split_routes is not None:
+            out["first_route_difference"] = route
+        return out
     finally:
         s.close()
 

@@ -277,6 +277,13 @@ int sb_decode_download_state(sb_ctx *ctx, const sb_layer_rows *layers, size_t n_
  * let the two sides pick different experts.  No counterpart in the reference.  idx holds
  * at least the sum of the MoE layers' top_k.  1 = written, 0 = no decode prepared, <0 = error. */
 int sb_decode_routes(sb_ctx *ctx, int32_t *idx, size_t n);
+/* The same for the decode step at position pos (any step run since sb_decode_prepare, by
+ * sb_decode_token or sb_decode_greedy, prompt steps included; positions the block prefill ran
+ * hold no trace), and, when gaps != NULL, per MoE layer the router-logit gap between its
+ * k-th choice and the best expert it did not choose (gaps holds at least the number of MoE
+ * layers): a small gap marks a near-tie that another summation order may break the other
+ * way.  No counterpart in the reference.  1 = written, 0 = no decode step yet, <0 = error. */
+int sb_decode_route_trace(sb_ctx *ctx, size_t pos, int32_t *idx, size_t n, float *gaps, size_t n_gaps);
 
 /* Block prefill of a prompt on the prepared model: tokens[0..n) at positions pos0 .. pos0+n-1
  * through every layer at once -- the reference's prompt path over forward_layer_block

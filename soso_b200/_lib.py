@@ -119,6 +119,8 @@ SIGNATURES = {
     "sb_decode_download_state": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbLayerRows), c_size, c_size,
                                                 c_f32p]),
     "sb_decode_routes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), c_size]),
+    "sb_decode_route_trace": (ctypes.c_int, [ctypes.c_void_p, c_size, ctypes.POINTER(ctypes.c_int32), c_size,
+                                             ctypes.POINTER(ctypes.c_float), c_size]),
     "sb_decode_prefill": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), c_size, c_size, c_f32p,
                                          ctypes.POINTER(ctypes.c_int32)]),
     "sbk_row_bytes": (c_size, [ctypes.c_uint8, c_size]),

@@ -101,8 +101,14 @@ struct RouteArgs {
     int lo, hi;             // resident experts [lo, hi)
     int pairs;              // gate|up launches run one gate/up pair matrix per choice
     int xw;                 // floats between exchange slots: the down of choice r publishes at r * xw
-    int *trace;             // [k]: the chosen experts' IDs in rank order, kept for sb_decode_routes
+    // route trace of this layer: row *pos of RT_W ints (the chosen IDs in rank order, then at
+    // RT_GAP the router-logit gap between the k-th and (k+1)-th choice, as float bits), rows
+    // trace_row ints apart; read by sb_decode_routes / sb_decode_route_trace
+    int *trace;
+    const int *pos;
+    int trace_row;
 };
+constexpr int RT_W = 17, RT_GAP = 16;
 
 // The router of a MoE layer whose matrix is f32, as the reference stores ffn_gate_inp (its
 // router matvec, layer.rs:1959-1972, runs in f32), with the input formed as the fused matvec
@@ -166,7 +172,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
     __shared__ float topw[64];
     __shared__ int topi[64];
     __shared__ int own[64];
-    __shared__ int s_m;
+    __shared__ int s_m, s_next;
     griddep_launch();  // the expert launches read the batches only after their own wait
     griddep_wait();
     const int tid = threadIdx.x, n = a.n_exp;
@@ -201,6 +207,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
             r += (u > v) || (u == v && j < i);
         }
         if (r < a.k) topi[r] = i, topw[r] = v;
+        if (r == a.k) s_next = i;  // the best expert not chosen: its logit gap goes in the trace
     }
     // shared expert gate: sigmoid(row . rmsnorm(h) * nw), the dot in warp 0
     float sg = 1.0f;
@@ -227,11 +234,13 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a)
     if (tid == 0) {
         float t = 0.0f;
         for (int r = 0; r < a.k; r++) t += topw[r];
+        int *tr = a.trace + (size_t)(*a.pos) * a.trace_row;
         for (int r = 0; r < a.k; r++) {
             a.wts[r] = t > 0.0f ? topw[r] / t : topw[r];
             a.idx[r] = topi[r];
-            a.trace[r] = topi[r];
+            tr[r] = topi[r];
         }
+        tr[RT_GAP] = __float_as_int(a.k < n ? a.logits[topi[a.k - 1]] - a.logits[s_next] : INFINITY);
         if (a.has_shared) a.wts[a.k] = sg;
         int mo = 0;
         for (int r = 0; r < a.k; r++)
@@ -330,7 +339,9 @@ struct sb_engine {
     // MoE: router logits, chosen experts and weights, gate|up per choice, down outputs per choice
     float *rlog = nullptr, *wts = nullptr, *egu = nullptr, *ys = nullptr;
     int *ridx = nullptr;
-    int *rtrace = nullptr;  // [layers][16]: the experts each MoE layer chose at the last step
+    int *rtrace = nullptr;  // [ctx][layers][RT_W]: per decode position, the experts each MoE layer chose
+    size_t last_pos = 0;    // position of the last decode step (host)
+    bool traced = false;    // a decode step ran since prepare
     void *pf = nullptr;     // block prefill state (prefill_engine.cuh)
     size_t moe_slots = 0, moe_ffn = 0, n_exp_max = 0;
     // MLA: q_down | kv_down outputs, q_up output, absorbed query, roped q slice, latent sums
@@ -632,7 +643,8 @@ int moe_dispatch(sb_engine *e, EngLayer &L, const float *hc, cudaStream_t s, boo
     }
     sb::RouteArgs ra{e->rlog, (int)L.n_exp, (int)L.top_k, e->ridx, e->wts, L.sg, hc, L.nf, e->eps, (int)e->H,
                      L.has_sh ? 1 : 0, L.gu_b, L.dn_b, L.sel, L.maps, (int)L.ex_lo, (int)L.ex_hi, L.ex_pairs ? 1 : 0,
-                     sb::grp::XW, e->rtrace + (&L - e->L.data()) * 16};
+                     sb::grp::XW, e->rtrace + (&L - e->L.data()) * sb::RT_W, e->ints,
+                     (int)(e->L.size() * sb::RT_W)};
     if ((rc = sb::launch_k(sb::route_kernel, dim3(1), dim3(256), 0, 1, s, ra))) return rc;
     *n += 1;
     rc = gdt == SB_DTYPE_Q4_K ? launch_moe_batch<sb::tcmv::Q4K>(L.gu_b, L.sel, L.gu_smem, s)
@@ -1195,7 +1207,7 @@ extern "C" int sb_decode_prepare(sb_ctx *c, const sb_decode_plan *p)
         e->rlog = fbuf(e->n_exp_max);
         e->wts = fbuf(e->moe_slots);
         e->ridx = (int *)fbuf(e->moe_slots);
-        e->rtrace = (int *)fbuf(e->L.size() * 16);  // top_k <= 16 (checked above)
+        e->rtrace = (int *)fbuf(e->ctx * e->L.size() * sb::RT_W);  // top_k <= 16 (checked above)
         e->moe_ffn = (e->moe_ffn + 63) & ~(size_t)63;
         e->egu = fbuf(2 * e->moe_slots * e->moe_ffn);
         e->ys = fbuf(e->moe_slots * H);
@@ -1304,6 +1316,7 @@ extern "C" int sb_decode_token(sb_ctx *c, const float *embed, size_t pos, float 
     if ((err = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", err);
     memcpy(logits, hs + hb + 256, e->V * 4);
     if (kv_rows) memcpy(kv_rows, hs + hb + 256 + lb, e->kv_rows_total * 2);
+    e->last_pos = pos, e->traced = true;
     c->stats.launches += e->launches_per_token;
     c->stats.bytes_up += e->H * 4 + 4;
     c->stats.bytes_down += e->V * 4 + (kv_rows ? e->kv_rows_total * 2 : 0);
@@ -1347,6 +1360,7 @@ extern "C" int sb_decode_greedy(sb_ctx *c, const int32_t *prompt, size_t n_promp
         return fail("cudaMemcpyAsync(tokens)", err);
     if ((err = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", err);
     memcpy(tokens_out, hs + pb + 256, n * 4);
+    e->last_pos = pos + n - 1, e->traced = true;
     c->stats.launches += e->launches_per_token * n;
     c->stats.bytes_up += n_prompt * 4 + 16;
     c->stats.bytes_down += n * 4;
@@ -1473,25 +1487,56 @@ extern "C" int sb_decode_download_state(sb_ctx *c, const sb_layer_rows *layers, 
     return 1;
 }
 
+namespace sb {
+// Row `pos` of the route trace: the chosen IDs of every MoE layer (layer order, rank order)
+// into idx, and when gaps != null the router-logit gap of each MoE layer into gaps.
+static int read_route_row(sb_ctx *c, sb_engine *e, size_t pos, int32_t *idx, size_t n, float *gaps, size_t n_gaps,
+                          const char *who)
+{
+    size_t need = 0, moe = 0;
+    for (auto &L : e->L) need += L.moe ? L.top_k : 0, moe += L.moe ? 1 : 0;
+    if (n < need) return fail(std::string(who) + ": output shorter than the MoE layers' choices");
+    if (gaps && n_gaps < moe) return fail(std::string(who) + ": gap output shorter than the MoE layers");
+    cudaError_t err = cudaSetDevice(c->device);
+    if (err != cudaSuccess) return fail("cudaSetDevice", err);
+    const size_t row = e->L.size() * RT_W;
+    std::vector<int> t(row);
+    if ((err = cudaMemcpyAsync(t.data(), e->rtrace + pos * row, row * 4, cudaMemcpyDeviceToHost, c->stream)) !=
+            cudaSuccess ||
+        (err = cudaStreamSynchronize(c->stream)) != cudaSuccess)
+        return fail(who, err);
+    size_t o = 0, g = 0;
+    for (size_t l = 0; l < e->L.size(); l++) {
+        if (!e->L[l].moe) continue;
+        for (size_t r = 0; r < e->L[l].top_k; r++) idx[o++] = t[l * RT_W + r];
+        if (gaps) {
+            int b = t[l * RT_W + RT_GAP];
+            float f;
+            memcpy(&f, &b, 4);
+            gaps[g++] = f;
+        }
+    }
+    return 1;
+}
+}  // namespace sb
+
 extern "C" int sb_decode_routes(sb_ctx *c, int32_t *idx, size_t n)
 {
     if (!c) return fail("null context");
     if (!idx) return fail("null argument");
     std::lock_guard<std::mutex> lk(c->mu);
     sb_engine *e = c->eng;
-    if (!e || !e->rtrace) return 0;
-    size_t need = 0;
-    for (auto &L : e->L) need += L.moe ? L.top_k : 0;
-    if (n < need) return fail("sb_decode_routes: output shorter than the MoE layers' choices");
-    cudaError_t err = cudaSetDevice(c->device);
-    if (err != cudaSuccess) return fail("cudaSetDevice", err);
-    std::vector<int> t(e->L.size() * 16);
-    if ((err = cudaMemcpyAsync(t.data(), e->rtrace, t.size() * 4, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess ||
-        (err = cudaStreamSynchronize(c->stream)) != cudaSuccess)
-        return fail("sb_decode_routes", err);
-    size_t o = 0;
-    for (size_t l = 0; l < e->L.size(); l++)
-        if (e->L[l].moe)
-            for (size_t r = 0; r < e->L[l].top_k; r++) idx[o++] = t[l * 16 + r];
-    return 1;
+    if (!e || !e->rtrace || !e->traced) return 0;
+    return sb::read_route_row(c, e, e->last_pos, idx, n, nullptr, 0, "sb_decode_routes");
+}
+
+extern "C" int sb_decode_route_trace(sb_ctx *c, size_t pos, int32_t *idx, size_t n, float *gaps, size_t n_gaps)
+{
+    if (!c) return fail("null context");
+    if (!idx) return fail("null argument");
+    std::lock_guard<std::mutex> lk(c->mu);
+    sb_engine *e = c->eng;
+    if (!e || !e->rtrace || !e->traced) return 0;
+    if (pos >= e->ctx) return fail("sb_decode_route_trace: position beyond the prepared context");
+    return sb::read_route_row(c, e, pos, idx, n, gaps, n_gaps, "sb_decode_route_trace");
 }

@@ -396,6 +396,21 @@ class DecodeSession:
             raise SbError(f"sb_decode_routes returned {rc}: {last_error()}")
         return {l: out[i * cfg.top_k:(i + 1) * cfg.top_k].copy() for i, l in enumerate(moe)}
 
+    def route_trace(self, pos: int) -> tuple[dict, dict]:
+        """sb_decode_route_trace: for the decode step at position pos, layer -> the experts
+        its router chose (rank order), and layer -> the router-logit gap between the k-th
+        choice and the best expert not chosen."""
+        cfg = self.cfg
+        moe = [l for l in range(cfg.n_layers) if cfg.is_moe(l)]
+        out = np.empty(max(1, len(moe) * cfg.top_k), np.int32)
+        gaps = np.empty(max(1, len(moe)), np.float32)
+        rc = lib().sb_decode_route_trace(self.ctx, pos, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), out.size,
+                                          gaps.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), gaps.size)
+        if rc != 1:
+            raise SbError(f"sb_decode_route_trace returned {rc}: {last_error()}")
+        return ({l: out[i * cfg.top_k:(i + 1) * cfg.top_k].copy() for i, l in enumerate(moe)},
+                {l: float(gaps[i]) for i, l in enumerate(moe)})
+
     def close(self):
         if self._own and self.ctx:
             lib().sb_destroy(self.ctx)

@@ -57,3 +57,35 @@ def test_moe_decode_token_logits(gpu, moe_model):
             assert logits_close(lg, orc.step(e, pos)) <= LOGIT_REL, pos
     finally:
         sess.close()
+
+
+def test_route_trace_per_position(gpu, moe_model):
+    """sb_decode_route_trace: the experts each MoE layer chose at every decode position, and the
+    router-logit gap between the k-th choice and the next expert, against the oracle's router
+    (topk_softmax, gemm.rs:62-91) teacher forced on the same tokens: the same experts wherever
+    the oracle's gap is not a near-tie, gaps within 1e-3; the last position's trace equals
+    sb_decode_routes."""
+    cfg, model = moe_model
+    sess = decode.DecodeSession(cfg, model)
+    orc = DenseOracle(cfg, model)
+    toks = synth.rng("toks", "moe_trace").integers(0, cfg.vocab, 12)
+    try:
+        want = []
+        for pos, t in enumerate(toks):
+            e = orc.embed(int(t))
+            sess.token(e, pos)
+            orc.step(e, pos)
+            want.append(list(orc.route_gaps))
+        last = sess.routes()
+        for pos in range(len(toks)):
+            ids, gaps = sess.route_trace(pos)
+            moe = sorted(ids)
+            assert len(moe) == len(want[pos])
+            for i, l in enumerate(moe):
+                assert abs(gaps[l] - want[pos][i]) <= 1e-3, (pos, l, gaps[l], want[pos][i])
+                assert gaps[l] >= 0.0
+            if pos == len(toks) - 1:
+                for l in moe:
+                    assert np.array_equal(ids[l], last[l])
+    finally:
+        sess.close()
