@@ -155,6 +155,52 @@ int sb_attention_prefill(sb_ctx *ctx, uint32_t layer, const float *q, float *out
                          size_t heads, size_t kv_heads, size_t hd, const uint16_t *k, const uint16_t *v,
                          size_t *valid_rows);
 /* Number of resident weight tensors (`CudaGpu::residentes`, used by cuda_matvec.rs:138). */
+/* Mirror of `MoeCapa` (gpu.rs:294-335) and its `MoeNormas` (:279-289): one MoE layer of a
+ * block of n tokens at positions pos0.. on the device (Qwen3-MoE-style: GQA with optional
+ * QK-norm, NeoX RoPE, softmax top-k router in f32, SwiGLU experts).  hidden [n][h] in and
+ * out (host); the attention matrices resident under key_q/k/v/o and the experts under
+ * `{prefix}.E{nn}.ffn_{gate,up,down}` (nn at least two digits), made resident by sb_upload
+ * (gemma_subir).  attn_norm / ffn_norm [h], q_norm / k_norm [head_dim] (qk_norm), router
+ * [n_exp x h] f32, rope_factors [head_dim / 2] or NULL: needed at a layer's first call, may
+ * be NULL after (sb_moe_ready).  cont: the input rows are the previous layer's output still
+ * on the device (sb_moe_pending), hidden is not read; chain: leave the output on the device
+ * for the next layer (hidden is not written; sb_moe_flush brings it down).  streamed != 0
+ * means the caller could supply experts on demand (ModoMoe::Flujo); this backend only runs
+ * layers whose experts are all resident.  evicted: KV rows dropped ahead of the layer's cache
+ * (0: sliding-window layers are declined). */
+typedef struct {
+    uint32_t layer;
+    size_t pos0, n;
+    float *hidden;
+    size_t h, heads, kv_heads, head_dim, ffn, n_exp, top_k, window, ctx_max;
+    float eps, theta, scale;
+    int qk_norm;
+    float rope_mscale;
+    int cont, chain;
+    const char *key_q, *key_k, *key_v, *key_o, *prefix;
+    const float *attn_norm, *q_norm, *k_norm, *ffn_norm, *router, *rope_factors;
+    int streamed;
+    size_t evicted;
+} sb_moe_layer_args;
+/* `GpuDispatch::moe_capa` (gpu.rs:424-429; CudaGpu's moe_ejecutar,
+ * crates/soso-llm-api/src/cuda/capa/moe.rs:316): the layer on the block path (tcgen05 GEMMs,
+ * the tensor-core prefill attention, experts grouped on the device), its f16 KV cache of
+ * ctx_max rows held on the device across calls (rows [0, pos0) must be there; a smaller pos0
+ * rewinds).  1 = done, 0 = declined (remembered: sb_moe_can turns 0), <0 = error. */
+int sb_moe_layer(sb_ctx *ctx, sb_moe_layer_args *args);
+/* `moe_lista` (gpu.rs:385-389): the layer's norms, router and expert tables are held. */
+int sb_moe_ready(sb_ctx *ctx, uint32_t layer);
+/* `moe_puede` (gpu.rs:379-383): 0 once the layer was declined or discarded. */
+int sb_moe_can(sb_ctx *ctx, uint32_t layer);
+/* `moe_pendiente` (gpu.rs:391-395): the device holds, not yet brought down, the output of
+ * that layer for n tokens from pos0. */
+int sb_moe_pending(sb_ctx *ctx, uint32_t layer, size_t pos0, size_t n);
+/* `moe_volcar` (gpu.rs:397-401): the pending output down into hidden (len floats, at least
+ * the pending rows), then no longer pending; nothing to do without one. */
+int sb_moe_flush(sb_ctx *ctx, float *hidden, size_t len);
+/* `moe_descartar` (gpu.rs:370-373): drop the layer's device state; not tried again. */
+int sb_moe_discard(sb_ctx *ctx, uint32_t layer);
+
 size_t sb_resident_count(const sb_ctx *ctx);
 /* `GpuDispatch::stats` (gpu.rs:350-352). */
 int sb_get_stats(const sb_ctx *ctx, sb_stats *out);

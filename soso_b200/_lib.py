@@ -48,6 +48,20 @@ class SbExpertBlock(ctypes.Structure):
                 ("dests", ctypes.POINTER(ctypes.c_uint32))]
 
 
+class SbMoeLayerArgs(ctypes.Structure):
+    """sb_moe_layer_args: the MoeCapa mirror (include/sosob200.h)."""
+    _fields_ = [("layer", ctypes.c_uint32), ("pos0", c_size), ("n", c_size), ("hidden", ctypes.c_void_p),
+                ("h", c_size), ("heads", c_size), ("kv_heads", c_size), ("head_dim", c_size), ("ffn", c_size),
+                ("n_exp", c_size), ("top_k", c_size), ("window", c_size), ("ctx_max", c_size),
+                ("eps", ctypes.c_float), ("theta", ctypes.c_float), ("scale", ctypes.c_float),
+                ("qk_norm", ctypes.c_int), ("rope_mscale", ctypes.c_float), ("cont", ctypes.c_int),
+                ("chain", ctypes.c_int), ("key_q", ctypes.c_char_p), ("key_k", ctypes.c_char_p),
+                ("key_v", ctypes.c_char_p), ("key_o", ctypes.c_char_p), ("prefix", ctypes.c_char_p),
+                ("attn_norm", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
+                ("ffn_norm", ctypes.c_void_p), ("router", ctypes.c_void_p), ("rope_factors", ctypes.c_void_p),
+                ("streamed", ctypes.c_int), ("evicted", c_size)]
+
+
 class SbLayerState(ctypes.Structure):
     _fields_ = [("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("valid_rows", ctypes.POINTER(ctypes.c_size_t))]
 
@@ -106,6 +120,12 @@ SIGNATURES = {
                                             c_size, c_size, ctypes.POINTER(ctypes.c_uint16),
                                             ctypes.POINTER(ctypes.c_uint16), ctypes.POINTER(c_size)]),
     "sb_get_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbStats)]),
+    "sb_moe_layer": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbMoeLayerArgs)]),
+    "sb_moe_ready": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32]),
+    "sb_moe_can": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32]),
+    "sb_moe_pending": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, c_size, c_size]),
+    "sb_moe_flush": (ctypes.c_int, [ctypes.c_void_p, c_f32p, c_size]),
+    "sb_moe_discard": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32]),
     "sb_last_error": (ctypes.c_char_p, []),
     "sb_decode_prepare": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(SbDecodePlan)]),
     "sb_decode_token": (ctypes.c_int, [ctypes.c_void_p, c_f32p, c_size, c_f32p, ctypes.POINTER(ctypes.c_uint16)]),

@@ -53,6 +53,16 @@ __global__ void norm16_rows_kernel(const float *__restrict__ a, const float *__r
     griddep_launch();
 }
 
+// out = a + b over count floats (a block's residual with its pending output).
+__global__ void add_rows_kernel(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ out,
+                                long long count)
+{
+    griddep_wait();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count; i += (long long)gridDim.x * blockDim.x)
+        out[i] = a[i] + b[i];
+    griddep_launch();
+}
+
 // f32 rows -> f16 rows (GEMM operands), 4 elements a thread.
 __global__ void to16_kernel(const float *__restrict__ x, __half *__restrict__ y, long long total4)
 {

@@ -63,6 +63,7 @@ void sb_engine_free(sb_engine *e);
 void sb_pf_free(void *p);          // its block-prefill state (prefill_engine.cuh)
 struct sb_ctx;
 void sb_kv_mirror_free(const sb_ctx *c);  // KV mirrors of sb_attention_prefill (experts.cuh)
+void sb_moe_free(const sb_ctx *c);        // MoE layers of sb_moe_layer (moe_layer.cuh)
 
 struct sb_ctx {
     int device = 0;
@@ -219,6 +220,7 @@ extern "C" void sb_destroy(sb_ctx *c)
     cudaStreamSynchronize(c->stream);
     if (c->eng) sb_engine_free(c->eng);
     sb_kv_mirror_free(c);
+    sb_moe_free(c);
     for (auto &kv : c->weights)
         if (kv.second.ptr) cudaFree(kv.second.ptr);
     if (c->scratch) cudaFree(c->scratch);

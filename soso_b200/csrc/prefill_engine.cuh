@@ -184,6 +184,10 @@ struct PfRun {
     pg::Tile *d_tiles = nullptr;
     pg::Out *d_outs = nullptr;
     size_t launches = 0;
+    // a block of hidden rows instead of the tokens' embeddings, and the rows the layers leave
+    // instead of the last token's logits (the layers of one call of sb_moe_layer)
+    const float *h_in = nullptr;
+    float *h_out = nullptr;
 
     int map_index(const EngMat &m)
     {
@@ -314,9 +318,14 @@ int pf_layers(PfRun &r)
     const int cap = (int)st->cap;
     float *hc = st->h0, *ho = st->h1;  // residual stream (current / other)
     const float *yp = nullptr;         // output of the last block, still to be added
-    // embedding rows of the tokens (Runtime::embed_token, runtime.rs:787-802)
-    PF_CHECK(r.k("embed", sb::embed_kernel, dim3(n), dim3(256), (const uint8_t *)e->emb.w, (int)e->emb.dt, (int)e->V,
-                 H, (const int *)st->tok, hc));
+    if (r.h_in) {  // the hidden rows the caller gave
+        if (!r.plan && cudaMemcpyAsync(hc, r.h_in, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, r.s) != cudaSuccess)
+            return fail("prefill: hidden rows copy");
+    } else {
+        // embedding rows of the tokens (Runtime::embed_token, runtime.rs:787-802)
+        PF_CHECK(r.k("embed", sb::embed_kernel, dim3(n), dim3(256), (const uint8_t *)e->emb.w, (int)e->emb.dt,
+                     (int)e->V, H, (const int *)st->tok, hc));
+    }
     auto norm = [&](const float *w, float *x32) -> int {
         PF_CHECK(r.k("norm", blk::norm16_rows_kernel, dim3(n), dim3(256), (const float *)hc, yp, yp ? ho : nullptr, w,
                      st->x16, x32, H, e->eps));
@@ -472,6 +481,13 @@ int pf_layers(PfRun &r)
         std::swap(hc, ho);
         yp = nullptr;
     }
+    if (r.h_out) {  // the hidden rows the layers leave, with a pending block output added
+        if (yp) return r.k("add rows", blk::add_rows_kernel, dim3(256), dim3(256), (const float *)hc, yp, r.h_out,
+                           (long long)n * H);
+        if (!r.plan && cudaMemcpyAsync(r.h_out, hc, (size_t)n * H * 4, cudaMemcpyDeviceToDevice, r.s) != cudaSuccess)
+            return fail("prefill: hidden rows copy");
+        return 0;
+    }
     // the last token: hidden vector (before the output norm) and logits
     {
         const size_t last = (size_t)(n - 1) * H;
@@ -495,6 +511,48 @@ int pf_layers(PfRun &r)
         }
     }
     return 0;
+}
+
+// The block path over engine e for n rows at positions pos0..: a planning pass (the dense
+// launches' tile tables and every output descriptor collected on the host, weight maps
+// built), one upload of the tables (and of the tokens, when given), then the pass that
+// launches.  Input: the tokens' embeddings, or h_in (device, n x H); output: the last token's
+// logits and argmax in the engine, or h_out (device, n x H).
+int pf_run(sb_ctx *c, sb_engine *e, size_t n, size_t pos0, const int32_t *tokens, const float *h_in, float *h_out,
+           PfRun *out)
+{
+    cudaError_t err = cudaSuccess;
+    PfState *st = nullptr;
+    int rc = pf_state(c, e, n, &st);
+    if (rc) return rc;
+    PfRun &r = *out;
+    r.c = c, r.e = e, r.st = st, r.s = c->stream, r.n = (int)n, r.pos0 = (int)pos0, r.h_in = h_in, r.h_out = h_out;
+    if ((rc = pf_layers(r))) return rc;  // plan
+    // tables up: dense tiles and output descriptors (grown as needed), then the tokens
+    const size_t tb = r.tiles.size() * sizeof(pg::Tile), ob = r.outs.size() * sizeof(pg::Out);
+    const size_t kb = tokens ? n * 4 : 0;
+    if (r.tiles.size() > st->tiles_cap) {
+        void *p = st->alloc(tb, &err);
+        if (err != cudaSuccess) return fail("cudaMalloc(prefill tiles)", err);
+        st->tiles = (pg::Tile *)p, st->tiles_cap = r.tiles.size();
+    }
+    if (r.outs.size() > st->outs_cap) {
+        void *p = st->alloc(ob, &err);
+        if (err != cudaSuccess) return fail("cudaMalloc(prefill outputs)", err);
+        st->outs = (pg::Out *)p, st->outs_cap = r.outs.size();
+    }
+    if (c->ensure_host_stage(tb + ob + kb + 1024)) return -1;
+    char *hs = (char *)c->host_stage;
+    memcpy(hs, r.tiles.data(), tb);
+    memcpy(hs + tb, r.outs.data(), ob);
+    if (kb) memcpy(hs + tb + ob, tokens, kb);
+    if ((tb && (err = cudaMemcpyAsync(st->tiles, hs, tb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess) ||
+        (ob && (err = cudaMemcpyAsync(st->outs, hs + tb, ob, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess) ||
+        (kb && (err = cudaMemcpyAsync(st->tok, hs + tb + ob, kb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess))
+        return fail("cudaMemcpyAsync(prefill tables)", err);
+    r.plan = false;
+    r.d_tiles = st->tiles, r.d_outs = st->outs;
+    return pf_layers(r);
 }
 
 }  // namespace
@@ -535,36 +593,11 @@ extern "C" int sb_decode_prefill(sb_ctx *c, const int32_t *tokens, size_t n, siz
     cudaError_t err = cudaSetDevice(c->device);
     if (err != cudaSuccess) return fail("cudaSetDevice", err);
     const uint64_t t0 = now_ns();
-    PfState *st = nullptr;
-    int rc = pf_state(c, e, n, &st);
-    if (rc) return rc;
     PfRun r;
-    r.c = c, r.e = e, r.st = st, r.s = c->stream, r.n = (int)n, r.pos0 = (int)pos0;
-    if ((rc = pf_layers(r))) return rc;  // plan
-    // tables up: dense tiles and output descriptors (grown as needed), then the tokens
+    int rc = pf_run(c, e, n, pos0, tokens, nullptr, nullptr, &r);
+    if (rc) return rc;
     const size_t tb = r.tiles.size() * sizeof(pg::Tile), ob = r.outs.size() * sizeof(pg::Out);
-    if (r.tiles.size() > st->tiles_cap) {
-        void *p = st->alloc(tb, &err);
-        if (err != cudaSuccess) return fail("cudaMalloc(prefill tiles)", err);
-        st->tiles = (pg::Tile *)p, st->tiles_cap = r.tiles.size();
-    }
-    if (r.outs.size() > st->outs_cap) {
-        void *p = st->alloc(ob, &err);
-        if (err != cudaSuccess) return fail("cudaMalloc(prefill outputs)", err);
-        st->outs = (pg::Out *)p, st->outs_cap = r.outs.size();
-    }
-    if (c->ensure_host_stage(tb + ob + n * 4 + 1024)) return -1;
-    char *hs = (char *)c->host_stage;
-    memcpy(hs, r.tiles.data(), tb);
-    memcpy(hs + tb, r.outs.data(), ob);
-    memcpy(hs + tb + ob, tokens, n * 4);
-    if ((tb && (err = cudaMemcpyAsync(st->tiles, hs, tb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess) ||
-        (err = cudaMemcpyAsync(st->outs, hs + tb, ob, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess ||
-        (err = cudaMemcpyAsync(st->tok, hs + tb + ob, n * 4, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
-        return fail("cudaMemcpyAsync(prefill tables)", err);
-    r.plan = false;
-    r.d_tiles = st->tiles, r.d_outs = st->outs;
-    if ((rc = pf_layers(r))) return rc;
+    char *hs;
     // the host's copy of the result: the next token and, when asked, the logits
     const size_t lb = (e->V * 4 + 255) & ~(size_t)255;
     if (c->ensure_host_stage(lb + 256)) return -1;

@@ -19,7 +19,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import SbError, SbExpertBlock, SbMatvecOp, SbStats, SbView, c_f32p, c_u8p, last_error, lib
+from ._lib import (SbError, SbExpertBlock, SbMatvecOp, SbMoeLayerArgs, SbStats, SbView, c_f32p, c_u8p, last_error,
+                   lib)
 from .formats import DTYPE_F32, DTYPE_Q4_K, DTYPE_Q8_0
 
 
@@ -53,6 +54,53 @@ class MatvecOp:
     cols: int
     x: np.ndarray
     out: np.ndarray
+
+
+@dataclass
+class MoeNormas:
+    """`MoeNormas` (crates/soso-llm-core/src/gpu.rs:279-289): what a MoE layer sends once."""
+    attn_norm: np.ndarray
+    q_norm: np.ndarray
+    k_norm: np.ndarray
+    ffn_norm: np.ndarray
+    router: np.ndarray  # [n_exp x h] f32
+    rope_factores: np.ndarray | None = None
+
+
+@dataclass
+class MoeCapa:
+    """`MoeCapa` (crates/soso-llm-core/src/gpu.rs:294-335): one MoE layer of a block of n
+    tokens; `hidden` [n x h] f32 in and out.  `flujo` stands for the reference's expert
+    provider (streamed experts), which this backend does not take: every expert must be
+    resident (gemma_subir)."""
+    layer: int
+    pos0: int
+    n: int
+    hidden: np.ndarray
+    h: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    n_exp: int
+    top_k: int
+    ventana: int
+    ctx_max: int
+    eps: float
+    theta: float
+    escala: float
+    qk_norm: bool
+    rope_mscale: float
+    continuar: bool
+    encadenar: bool
+    clave_q: str
+    clave_k: str
+    clave_v: str
+    clave_o: str
+    prefijo: str
+    normas: MoeNormas | None = None
+    flujo: object = None
+    expulsadas: int = 0
 
 
 @dataclass
@@ -237,6 +285,57 @@ class CudaGpu:
         ok = self._check(rc, "atencion_prefill")
         filas_validas[0] = fv.value
         return ok
+
+    def moe_capa(self, capa: MoeCapa) -> bool:
+        """`moe_capa` (gpu.rs:424-429): the whole layer on the device."""
+        _f32_arg(capa.hidden, capa.n * capa.h, "hidden")
+        keep = []
+
+        def f32(a, n, name):
+            if a is None:
+                return None
+            arr = np.ascontiguousarray(a, dtype=np.float32)
+            if arr.size != n:
+                raise ValueError(f"{name}: {arr.size} values, want {n}")
+            keep.append(arr)
+            return arr.ctypes.data
+        nm = capa.normas
+        a = SbMoeLayerArgs()
+        a.layer, a.pos0, a.n, a.hidden = capa.layer, capa.pos0, capa.n, capa.hidden.ctypes.data
+        a.h, a.heads, a.kv_heads, a.head_dim = capa.h, capa.heads, capa.kv_heads, capa.head_dim
+        a.ffn, a.n_exp, a.top_k, a.window, a.ctx_max = capa.ffn, capa.n_exp, capa.top_k, capa.ventana, capa.ctx_max
+        a.eps, a.theta, a.scale, a.qk_norm = capa.eps, capa.theta, capa.escala, int(capa.qk_norm)
+        a.rope_mscale, a.cont, a.chain = capa.rope_mscale, int(capa.continuar), int(capa.encadenar)
+        a.key_q, a.key_k, a.key_v = capa.clave_q.encode(), capa.clave_k.encode(), capa.clave_v.encode()
+        a.key_o, a.prefix = capa.clave_o.encode(), capa.prefijo.encode()
+        if nm is not None:
+            a.attn_norm = f32(nm.attn_norm, capa.h, "attn_norm")
+            a.ffn_norm = f32(nm.ffn_norm, capa.h, "ffn_norm")
+            a.q_norm = f32(nm.q_norm, capa.head_dim, "q_norm") if capa.qk_norm else None
+            a.k_norm = f32(nm.k_norm, capa.head_dim, "k_norm") if capa.qk_norm else None
+            a.router = f32(nm.router, capa.n_exp * capa.h, "router")
+            a.rope_factors = f32(nm.rope_factores, capa.head_dim // 2, "rope_factores")
+        a.streamed = int(capa.flujo is not None)
+        ok = self._check(self._L.sb_moe_layer(self._h, ctypes.byref(a)), "moe_capa")
+        capa.expulsadas = int(a.evicted)
+        return ok
+
+    def moe_lista(self, layer: int) -> bool:
+        return self._check(self._L.sb_moe_ready(self._h, layer), "moe_lista")
+
+    def moe_puede(self, layer: int) -> bool:
+        return self._check(self._L.sb_moe_can(self._h, layer), "moe_puede")
+
+    def moe_pendiente(self, layer: int, pos0: int, n: int) -> bool:
+        return self._check(self._L.sb_moe_pending(self._h, layer, pos0, n), "moe_pendiente")
+
+    def moe_volcar(self, hidden: np.ndarray) -> None:
+        if hidden.dtype != np.float32 or not hidden.flags.c_contiguous:
+            raise ValueError("hidden: contiguous float32 wanted")
+        self._check(self._L.sb_moe_flush(self._h, hidden.ctypes.data_as(c_f32p), hidden.size), "moe_volcar")
+
+    def moe_descartar(self, layer: int) -> None:
+        self._check(self._L.sb_moe_discard(self._h, layer), "moe_descartar")
 
     def residentes(self) -> int:
         return int(self._L.sb_resident_count(self._h))
