@@ -61,10 +61,15 @@ def setup():
     gpu.close()
 
 
-def _capa(cfg, model, layer, pos0, hidden, normas=True, **kw):
-    p = f"blk.{layer}."
+def _f32(a):
+    a = np.ascontiguousarray(a)
+    return a.view(np.float32) if a.dtype == np.uint8 else a.astype(np.float32)
+
+
+def _capa(cfg, model, layer, pos0, hidden, normas=True, src=None, **kw):
+    p = f"blk.{layer if src is None else src}."
     nm = MoeNormas(model[p + "attn_norm"], model[p + "attn_q_norm"], model[p + "attn_k_norm"], model[p + "ffn_norm"],
-                   np.asarray(model[p + "ffn_gate_inp"], np.float32)) if normas else None
+                   _f32(model[p + "ffn_gate_inp"])) if normas else None
     args = dict(layer=layer, pos0=pos0, n=hidden.shape[0], hidden=hidden, h=cfg.hidden, heads=cfg.heads,
                 kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, ffn=cfg.moe_ffn, n_exp=cfg.n_exp, top_k=cfg.top_k,
                 ventana=0, ctx_max=cfg.ctx, eps=cfg.eps, theta=cfg.theta,
@@ -162,7 +167,7 @@ def test_moe_capa_chained_layers(setup):
 def test_moe_capa_declines_sliding_window(setup):
     cfg, model, gpu = setup
     h = np.zeros((4, cfg.hidden), np.float32)
-    capa = _capa(cfg, model, 7, 0, h, ventana=64, clave_q="L00.attn_q", clave_k="L00.attn_k", clave_v="L00.attn_v",
+    capa = _capa(cfg, model, 7, 0, h, src=0, ventana=64, clave_q="L00.attn_q", clave_k="L00.attn_k", clave_v="L00.attn_v",
                  clave_o="L00.attn_output", prefijo="L00")
     assert gpu.moe_puede(7)
     assert not gpu.moe_capa(capa)
