@@ -81,7 +81,8 @@ struct sb_ctx {
     int ensure_host_stage(size_t bytes)
     {
         if (bytes <= host_stage_bytes) return 0;
-        if (host_stage) cudaFreeHost(host_stage);
+        // copies still queued may read or write the old buffer: let them finish first
+        if (host_stage) cudaDeviceSynchronize(), cudaFreeHost(host_stage);
         host_stage = nullptr;
         host_stage_bytes = 0;
         size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;

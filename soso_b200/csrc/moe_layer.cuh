@@ -221,9 +221,9 @@ extern "C" int sb_moe_layer(sb_ctx *c, sb_moe_layer_args *a)
     const int in = a->cont ? mc.out_buf : 1 - mc.out_buf, out = 1 - in;
     size_t up = 0;
     if (!a->cont) {
-        if (c->ensure_host_stage(n * H * 4)) return -1;
-        memcpy(c->host_stage, a->hidden, n * H * 4);
-        if ((err = cudaMemcpyAsync(mc.buf[in], c->host_stage, n * H * 4, cudaMemcpyHostToDevice, c->stream)) !=
+        // straight from the caller's (pageable) rows: the copy has read them when the call
+        // returns, so the staging buffer is free for the tables the block path uploads next
+        if ((err = cudaMemcpyAsync(mc.buf[in], a->hidden, n * H * 4, cudaMemcpyHostToDevice, c->stream)) !=
             cudaSuccess)
             return fail("cudaMemcpyAsync(hidden rows)", err);
         up = n * H * 4;
