@@ -87,11 +87,16 @@ void sb_pf_free(void *p) { delete reinterpret_cast<PfState *>(p); }
 
 namespace {
 
-// token tile width: the small one unless the large one still gives every SM a tile
+// Token tile width.  A tile's time is set by dequantising its 128 x K weights (the same for
+// both widths); the small tile fits two CTAs an SM, the large one takes ~1.5x as long (four
+// times the MMAs and X) but dequantises each weight once per 256 tokens instead of 64.  Take
+// the width whose waves of tiles end first.
 int pick_bn(int rows_total, int ntok, int sms)
 {
     const int rt = (rows_total + pg::BM - 1) / pg::BM;
-    return rt * ((ntok + PF_BN_LARGE - 1) / PF_BN_LARGE) >= sms ? PF_BN_LARGE : PF_BN_SMALL;
+    const int w64 = (rt * ((ntok + PF_BN_SMALL - 1) / PF_BN_SMALL) + 2 * sms - 1) / (2 * sms);
+    const int w256 = (rt * ((ntok + PF_BN_LARGE - 1) / PF_BN_LARGE) + sms - 1) / sms;
+    return 3 * w256 < 2 * w64 ? PF_BN_LARGE : PF_BN_SMALL;
 }
 
 // Grow the prefill buffers to n tokens (all sized from the engine's plan).
