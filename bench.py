@@ -340,7 +340,12 @@ def run_ours(args) -> None:
                     summary[k + "_prefill_ms"] = v["prefill"]["ms"]
                     summary[k + "_prefill_frac"] = v["prefill"]["frac_of_bf16_peak"]
                 if "agreement_vs_1gpu" in v and v["agreement_vs_1gpu"]:
-                    summary[k + "_identical_vs_1gpu"] = v["agreement_vs_1gpu"]["identical_frac"]
+                    ag = v["agreement_vs_1gpu"]
+                    summary[k + "_identical_vs_1gpu"] = ag["identical_frac"]
+                    rd = ag.get("first_route_difference")
+                    if rd:  # [position, router-logit gap there (whole run), first token divergence position]
+                        summary[k + "_route_tie"] = [rd["position"], rd["router_gap_1gpu"],
+                                                     rd["first_token_divergence_position"]]
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "summary": summary, "n_gpus": world,
             "steps": args.steps,
