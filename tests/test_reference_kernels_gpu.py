@@ -16,6 +16,12 @@ the kernels the drop-in replaces, checked for equal results and timed.
   configs[4]'s dense gate shape (10944x2048) and a 512-token block.  Both round the decoded
   weights and x to f16 the same way and sum in f32: within 1e-3 of the rms of Y.
 
+* decode attention: `mo_attn_split` + `mo_attn_combine` (gemma_capa.cu:765-926, launched
+  as atencion_split_dev does: grid (ceil(positions / 256), kv heads), 256 threads, then
+  (heads), 128 threads: cuda/capa.rs:787-845) against sbk_attn_decode, configs[2]'s 16 query
+  / 2 kv heads x 128 over a 4096-row f16 cache, at positions 200, 1000 and 4000.  Results
+  within 1e-3 of the output's largest magnitude (both f32 softmax over f16 K / V).
+
 Each case prints one REFKERN line with both sides' times (CUDA events on the launching
 stream, after warm-up; the best of three runs, against other work on a shared GPU).
 Nothing here asserts on speed.
@@ -32,8 +38,9 @@ from soso_b200._lib import SbkMvOp, lib
 from soso_b200.formats import DTYPE_Q4_K, row_bytes
 
 pytestmark = pytest.mark.gpu
-CUBIN = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
-                     "matvec_iq.cubin")
+REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref")
+CUBIN = os.path.join(REF, "matvec_iq.cubin")
+CUBIN_CAPA = os.path.join(REF, "gemma_capa.cubin")
 Q4K_CODE = 1002  # the reference's decoder code for Q4_K (crates/soso-llm-api/src/cuda.rs:39-44)
 
 
@@ -59,9 +66,10 @@ class _Module:
     def launch(self, name, grid, block, smem, stream, args):
         vals = []
         for kind, v in args:
-            vals.append({"p": ctypes.c_uint64, "i": ctypes.c_int32, "l": ctypes.c_int64}[kind](v))
+            vals.append({"p": ctypes.c_uint64, "i": ctypes.c_int32, "l": ctypes.c_int64, "f": ctypes.c_float}[kind](v))
         params = (ctypes.c_void_p * len(vals))(*[ctypes.cast(ctypes.pointer(v), ctypes.c_void_p) for v in vals])
-        rc = self.cu.cuLaunchKernel(self.fn(name), ctypes.c_uint(grid[0]), ctypes.c_uint(grid[1]), ctypes.c_uint(1),
+        rc = self.cu.cuLaunchKernel(self.fn(name), ctypes.c_uint(grid[0]), ctypes.c_uint(grid[1]),
+                                    ctypes.c_uint(grid[2] if len(grid) > 2 else 1),
                                     ctypes.c_uint(block), ctypes.c_uint(1), ctypes.c_uint(1), ctypes.c_uint(smem),
                                     ctypes.c_void_p(stream), params, None)
         assert rc == 0, f"cuLaunchKernel({name}) {rc}"
@@ -77,6 +85,18 @@ def refmod():
     import torch
     torch.zeros(1, device="cuda")  # torch's primary context current on this thread
     m = _Module(CUBIN)
+    yield m
+    torch.cuda.synchronize()
+    m.close()
+
+
+@pytest.fixture(scope="module")
+def capamod():
+    if not os.path.exists(CUBIN_CAPA):
+        pytest.skip("oracle/_ref/gemma_capa.cubin not built (needs the reference checkout at build time)")
+    import torch
+    torch.zeros(1, device="cuda")
+    m = _Module(CUBIN_CAPA)
     yield m
     torch.cuda.synchronize()
     m.close()
@@ -189,3 +209,50 @@ def test_prefill_gemm_vs_reference(refmod):
         "reference_cvt_f16_iq_matmul_mma_h": {"us": round(t_ref * 1e6, 1), "TFLOPs": round(flops / t_ref / 1e12, 1)},
         "sbk_matmul_f16": {"us": round(t_our * 1e6, 1), "TFLOPs": round(flops / t_our / 1e12, 1)},
         "speedup_vs_reference": round(t_ref / t_our, 2)}))
+
+
+def test_decode_attention_vs_reference(capamod):
+    import torch
+    s = torch.cuda.current_stream()
+    heads, kvh, hd, ctx = 16, 2, 128, 4096
+    kvd = kvh * hd
+    g = np.random.default_rng(7)
+    kc = torch.from_numpy(g.standard_normal((ctx, kvd)).astype(np.float16).view(np.int16)).cuda()
+    vc = torch.from_numpy(g.standard_normal((ctx, kvd)).astype(np.float16).view(np.int16)).cuda()
+    q = torch.from_numpy(g.standard_normal(heads * hd).astype(np.float32)).cuda()
+    L = lib()
+    ws = torch.zeros(int(L.sbk_attn_ws_bytes(heads, kvh, hd, ctx)), dtype=torch.uint8, device="cuda")
+    out_ref = torch.empty(heads * hd, device="cuda")
+    out_our = torch.empty(heads * hd, device="cuda")
+    S_max = (ctx + 255) // 256
+    parcial = torch.empty(kvh * S_max * 8 * hd, device="cuda")
+    ml = torch.empty(kvh * S_max * 8 * 2, device="cuda")
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
+    rows = []
+    for pos in (200, 1000, 4000):
+        S = (pos + 1 + 255) // 256
+        dpos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+
+        def ref():
+            capamod.launch("mo_attn_split", (S, kvh, 1), 256, 0, s.cuda_stream,
+                           [("p", q.data_ptr()), ("p", kc.data_ptr()), ("p", vc.data_ptr()), ("p", parcial.data_ptr()),
+                            ("p", ml.data_ptr()), ("i", heads), ("i", kvh), ("i", kvd), ("i", pos), ("i", 0),
+                            ("f", scale), ("i", S), ("p", 0)])
+            capamod.launch("mo_attn_combine", (heads, 1), 128, 0, s.cuda_stream,
+                           [("p", parcial.data_ptr()), ("p", ml.data_ptr()), ("p", out_ref.data_ptr()), ("i", heads),
+                            ("i", kvh), ("i", S)])
+
+        def ours():
+            assert L.sbk_attn_decode(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out_our.data_ptr(), dpos.data_ptr(),
+                                     heads, kvh, hd, ctx, ws.data_ptr(), 0, s.cuda_stream) == 0
+
+        ref()
+        ours()
+        torch.cuda.synchronize()
+        a, b = out_ref.cpu().numpy(), out_our.cpu().numpy()
+        assert float(np.abs(a - b).max()) <= 1e-3 * float(np.abs(a).max()), pos
+        t_ref, t_our = _time(ref, 20), _time(ours, 20)
+        rows.append({"position": pos, "reference_mo_attn_split_combine_us": round(t_ref * 1e6, 2),
+                     "sbk_attn_decode_us": round(t_our * 1e6, 2), "speedup": round(t_ref / t_our, 2)})
+    print("REFKERN " + json.dumps({"case": "GQA decode attention, 16 q / 2 kv heads x 128, f16 cache of 4096 rows "
+                                           "(launch after launch on one stream)", "positions": rows}))
