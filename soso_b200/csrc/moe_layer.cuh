@@ -63,7 +63,7 @@ MoeCtxState &moe_state(const sb_ctx *c)
 }
 
 // a resident tensor (sb_upload) by key, as a GEMM operand of rows x cols
-int moe_mat(sb_ctx *c, const std::string &key, size_t rows, size_t cols, EngMat *out)
+int moe_mat(sb_ctx *c, const std::string &key, size_t rows, size_t cols, EngMat *out, bool grouped = false)
 {
     auto it = c->weights.find(key);
     if (it == c->weights.end() || !it->second.ok) return 0;
@@ -71,7 +71,7 @@ int moe_mat(sb_ctx *c, const std::string &key, size_t rows, size_t cols, EngMat 
     if (!sbk_row_bytes(r.dtype, cols) || r.bytes != rows * sbk_row_bytes(r.dtype, cols))
         return fail("sb_moe_layer: '" + key + "' is not a " + std::to_string(rows) + " x " + std::to_string(cols) +
                     " matrix");
-    if (!pf_gemm_dtype(r.dev_dtype)) return 0;
+    if (!(grouped ? pf_group_dtype(r.dev_dtype) : pf_gemm_dtype(r.dev_dtype))) return 0;
     *out = EngMat{r.ptr, r.dev_dtype, rows, cols};
     return 1;
 }
@@ -118,9 +118,9 @@ int moe_build(sb_ctx *c, const sb_moe_layer_args &a, MoeLayerState *ls)
     L.ex.resize(3 * a.n_exp);
     for (size_t x = 0; x < a.n_exp; x++) {
         EngMat g, u, d;
-        if ((rc = moe_mat(c, expert_key(a.prefix, x, "ffn_gate"), a.ffn, a.h, &g)) != 1 ||
-            (rc = moe_mat(c, expert_key(a.prefix, x, "ffn_up"), a.ffn, a.h, &u)) != 1 ||
-            (rc = moe_mat(c, expert_key(a.prefix, x, "ffn_down"), a.h, a.ffn, &d)) != 1)
+        if ((rc = moe_mat(c, expert_key(a.prefix, x, "ffn_gate"), a.ffn, a.h, &g, true)) != 1 ||
+            (rc = moe_mat(c, expert_key(a.prefix, x, "ffn_up"), a.ffn, a.h, &u, true)) != 1 ||
+            (rc = moe_mat(c, expert_key(a.prefix, x, "ffn_down"), a.h, a.ffn, &d, true)) != 1)
             return rc;
         if (g.dt != u.dt || (x && (g.dt != L.ex[0].dt || d.dt != L.ex[2].dt))) return 0;  // one format a kind
         if (d.dt == SB_DTYPE_Q4_K ? a.ffn % 256 != 0 : a.ffn < 256) return 0;  // the down GEMM's K

@@ -59,7 +59,23 @@ struct Launch {
 // the unit the raw TMA ring moves), and the dequantisation of 32 weights (columns 32h.. of
 // stage p of the column) into one 128-byte swizzled row of the stage tile.  Both formats
 // keep a raw column at 144 bytes a row, so that at BN = 64 two CTAs fit on an SM.
-struct FQ4K {
+// Formats held row-interleaved (a raw column is one box of 128 rows x RAWB bytes, one map).
+template <class W>
+struct RowRaw {
+    static constexpr int NMAP = 1;
+    __device__ __forceinline__ static void load_raw(uint8_t *slot, const CUtensorMap *maps, int rk, int row0, int,
+                                                    uint64_t *bar, uint64_t pol)
+    {
+        tcmv::tma_load_2d(slot, maps, rk * (W::RAWB / 8), row0, bar, pol);
+    }
+    template <bool F16>
+    __device__ __forceinline__ static void dq(const uint8_t *slot, int r, int, int p, int h, uint8_t *row)
+    {
+        W::template half16<F16>(slot + r * W::RAWB, p, h, row, r);
+    }
+};
+
+struct FQ4K : RowRaw<FQ4K> {
     static constexpr int RAWB = 144;  // one Q4_K block (crates/sosomodel/src/layout.rs:63-64)
     static constexpr int SPR = 4;     // 64-column stages per raw column (256 columns)
     template <bool F16>
@@ -69,7 +85,7 @@ struct FQ4K {
     }
 };
 
-struct FQ80 {
+struct FQ80 : RowRaw<FQ80> {
     static constexpr int RAWB = 144;  // four .som Q8_0 blocks: f32 scale + 32 i8 (layout.rs:57-59)
     static constexpr int SPR = 2;     // 64-column stages per raw column (128 columns)
     // block 2p + h of the column: w_i = scale * q_i (dequant.rs:74-102), rounded once
@@ -91,6 +107,62 @@ struct FQ80 {
                                          v(w1, pf::SEL_B0, pf::SEL_B1), v(w1, pf::SEL_B2, pf::SEL_B3));
             const int chunk = 4 * h + c;
             *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = out;
+        }
+    }
+};
+
+// Q6_K rows repacked on upload into groups of 8 blocks laid out as planes -- [ql 8x128]
+// [qh 8x64][sc 8x16][d 8x2] = 1680 bytes, a last group of m < 8 blocks the same way with m,
+// padded to 16 bytes (SB_DTYPE_Q6_K_P) -- so a raw column here is half a block (128 columns,
+// half n of block b): four boxes of 128 rows, one map each (box widths differ), landing as
+// planes in the slot: ql[64n..] 64 B, qh[32n..] 32 B, the block's 16 scales, the group's d
+// values (16 B).  Weight 32k + l of half n (GGML dequantize_row_q6_K, restated in
+// crates/gguf2som/src/lib.rs:1639-1661): code = ((ql[64n + l + 32 (k & 1)] >> 4 (k >> 1)) &
+// 15) | (((qh[32n + l] >> 2k) & 3) << 4), w = (d * sc[8n + 2k + l / 16]) * (code - 32) in
+// f32 (d * sc is exact), then rounded to the operand type.
+struct FQ6KP {
+    static constexpr int RAWB = 128;  // bytes a row of the four planes
+    static constexpr int SPR = 2;     // 64-column stages per raw column (128 columns)
+    static constexpr int NMAP = 4;
+    static constexpr int QL = 0, QH = 64 * BM, SC = 96 * BM, DD = 112 * BM;  // plane offsets in the slot
+    __device__ __forceinline__ static void load_raw(uint8_t *slot, const CUtensorMap *maps, int rk, int row0,
+                                                    int nb, uint64_t *bar, uint64_t pol)
+    {
+        const int b = rk >> 1, n = rk & 1, gi = b >> 3, w = b & 7, m = min(8, nb - 8 * gi), g0 = gi * 1680;
+        // byte offsets / 8 (u64 columns of the row): all multiples of 16 bytes
+        tcmv::tma_load_2d(slot + QL, maps + 0, (g0 + 128 * w + 64 * n) / 8, row0, bar, pol);
+        tcmv::tma_load_2d(slot + QH, maps + 1, (g0 + 128 * m + 64 * w + 32 * n) / 8, row0, bar, pol);
+        tcmv::tma_load_2d(slot + SC, maps + 2, (g0 + 192 * m + 16 * w) / 8, row0, bar, pol);
+        tcmv::tma_load_2d(slot + DD, maps + 3, (g0 + 208 * m) / 8, row0, bar, pol);
+    }
+    template <bool F16>
+    __device__ __forceinline__ static void dq(const uint8_t *slot, int r, int rk, int p, int h, uint8_t *row)
+    {
+        const int n = rk & 1, w = (rk >> 1) & 7, k = 2 * p + h;
+        const uint4 *ql = reinterpret_cast<const uint4 *>(slot + QL + r * 64 + 32 * (k & 1));
+        const uint4 *qh = reinterpret_cast<const uint4 *>(slot + QH + r * 32);
+        const uint32_t scw = *reinterpret_cast<const uint32_t *>(slot + SC + r * 16 + 8 * n + 2 * k - ((2 * k) & 2));
+        const int sh = (2 * k) & 2;  // the two scales at byte 8n + 2k: in the word at 8n + 2k - sh, bytes sh, sh+1
+        const float d = __half2float(*reinterpret_cast<const __half *>(slot + DD + r * 16 + 2 * w));
+        const float s0 = d * (float)(int8_t)((scw >> (8 * sh)) & 0xFFu);
+        const float s1 = d * (float)(int8_t)((scw >> (8 * sh + 8)) & 0xFFu);
+        const uint64_t nb2 = pf::dup2(-8388640.0f);  // -(2^23 + 32): codes 0..63 -> code - 32 exactly
+        const int lsh = 4 * (k >> 1), hsh = 2 * k;
+        const uint4 l0 = ql[0], l1 = ql[1], h0 = qh[0], h1 = qh[1];
+        const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int c = 0; c < 4; c++) {  // 8 weights -> one 16-byte chunk of the swizzled row
+            const uint64_t sc2 = pf::dup2(c < 2 ? s0 : s1);  // l < 16: scale 8n + 2k, else 8n + 2k + 1
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const uint32_t code = ((lw[2 * c + j] >> lsh) & 0x0F0F0F0Fu) | (((hw[2 * c + j] >> hsh) & 0x03030303u) << 4);
+                o[2 * j] = pf::pack16x2<F16>(pf::mul_f32x2(pf::codes2(code, pf::SEL_B0, pf::SEL_B1, nb2), sc2));
+                o[2 * j + 1] = pf::pack16x2<F16>(pf::mul_f32x2(pf::codes2(code, pf::SEL_B2, pf::SEL_B3, nb2), sc2));
+            }
+            const int chunk = 4 * h + c;
+            *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
 };
@@ -155,7 +227,7 @@ __global__ void __launch_bounds__(THREADS, BN == 64 ? 2 : 1) pg_gemm_kernel(cons
         }
         tcmv::mbar_init(acc_full, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(wmap) : "memory");
+        for (int i = 0; i < W::NMAP; i++) asm volatile("prefetch.tensormap [%0];" ::"l"(wmap + i) : "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -200,7 +272,7 @@ __global__ void __launch_bounds__(THREADS, BN == 64 ? 2 : 1) pg_gemm_kernel(cons
                     break;
                 }
                 tcmv::mbar_expect_tx_arrive(&raw_full[rs], (unsigned)L::RAW_BYTES);
-                tcmv::tma_load_2d(sraw + rs * L::RAW_BYTES, wmap, rk * (W::RAWB / 8), t.row0, &raw_full[rs], pol);
+                W::load_raw(sraw + rs * L::RAW_BYTES, wmap, rk, t.row0, a.cols / 256, &raw_full[rs], pol);
             }
         }
         __syncwarp();
@@ -235,7 +307,7 @@ __global__ void __launch_bounds__(THREADS, BN == 64 ? 2 : 1) pg_gemm_kernel(cons
                 set_dev_error(0x83u);
                 break;
             }
-            W::template half16<F16>(sraw + rs * L::RAW_BYTES + r * W::RAWB, p, hh, sw + st * L::W_BYTES + r * 128, r);
+            W::template dq<F16>(sraw + rs * L::RAW_BYTES, r, rk, p, hh, sw + st * L::W_BYTES + r * 128);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
             __syncwarp();
             if (lane == 0) {
@@ -322,6 +394,33 @@ inline int make_wmap(CUtensorMap *m, uint8_t dtype, const void *w, int rows, int
     return r == CUDA_SUCCESS ? 0 : -7;
 }
 
+// The weight maps of a matrix for the GEMM: one (row-interleaved formats), or four of the
+// packed Q6_K rows (SB_DTYPE_Q6_K_P: the ql, qh, sc and d boxes of a half-block raw column,
+// FQ6KP).  Returns the number of maps written to m[], or < 0.
+inline int make_wmaps(CUtensorMap *m, uint8_t dtype, const void *w, int rows, int cols)
+{
+    if (dtype != SB_DTYPE_Q6_K_P) {
+        const int rc = make_wmap(m, dtype, w, rows, cols);
+        return rc ? rc : 1;
+    }
+    tcmv::EncodeTiledFn fn = tcmv::encode_fn();
+    if (!fn) return -6;
+    if (cols % 256 || cols < 256 || ((uintptr_t)w & 15) || rows < 1) return -1;
+    const cuuint64_t rb = (cuuint64_t)tcmv::q6k_packed_row_bytes((size_t)cols);
+    const cuuint32_t widths[4] = {64 / 8, 32 / 8, 16 / 8, 16 / 8};
+    for (int i = 0; i < 4; i++) {
+        cuuint64_t dims[2] = {rb / 8, (cuuint64_t)rows};
+        cuuint64_t strides[1] = {rb};
+        cuuint32_t box[2] = {widths[i], (cuuint32_t)BM};
+        cuuint32_t es[2] = {1, 1};
+        if (fn(&m[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void *>(w), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return -7;
+    }
+    return 4;
+}
+
 // X map: nrows x cols 16-bit operands (row-major), box = BN rows x 64 columns, 128-byte swizzle.
 inline int make_xmap(CUtensorMap *m, const void *x, int nrows, int cols, int bn, bool f16)
 {
@@ -368,6 +467,12 @@ inline int launch(uint8_t dtype, int bn, int prec, const CUtensorMap &xmap, cons
 {
     if (grid < 1 || a.cols % BK || a.cols < 256) return -1;
     const bool q4k = dtype == SB_DTYPE_Q4_K, f16 = prec == SBK_PREC_F16;
+    if (dtype == SB_DTYPE_Q6_K_P) {  // (f16 operands: the block prefill's)
+        if (a.cols % 256 || !f16) return -1;
+        if (bn == 64) return launch_t<FQ6KP, 64, true>(xmap, a, grid, pdl, s);
+        if (bn == 256) return launch_t<FQ6KP, 256, true>(xmap, a, grid, pdl, s);
+        return -1;
+    }
     if (!q4k && dtype != SB_DTYPE_Q8_0_R && dtype != SB_DTYPE_Q8_0) return -5;
     if (q4k && a.cols % 256) return -1;
 #define PG_CASE(W, BN_, F)                                                                                             \

@@ -79,7 +79,13 @@ struct PfState {
 
 constexpr int PF_BN_SMALL = 64, PF_BN_LARGE = 256;
 
-bool pf_gemm_dtype(uint8_t dt) { return dt == SB_DTYPE_Q4_K || dt == SB_DTYPE_Q8_0_R || dt == SB_DTYPE_Q8_0; }
+// formats of the dense GEMM launches (Q6_K as repacked for the matvec, four maps a matrix),
+// and of the grouped expert launches (one map an expert)
+bool pf_gemm_dtype(uint8_t dt)
+{
+    return dt == SB_DTYPE_Q4_K || dt == SB_DTYPE_Q8_0_R || dt == SB_DTYPE_Q8_0 || dt == SB_DTYPE_Q6_K_P;
+}
+bool pf_group_dtype(uint8_t dt) { return dt == SB_DTYPE_Q4_K || dt == SB_DTYPE_Q8_0_R || dt == SB_DTYPE_Q8_0; }
 
 }  // namespace
 
@@ -161,7 +167,7 @@ int pf_state(sb_ctx *c, sb_engine *e, size_t n, PfState **out)
         st->t_gu = (pg::Tile *)st->alloc(st->cap_gu * sizeof(pg::Tile), &err);
         st->t_dn = (pg::Tile *)st->alloc(st->cap_dn * sizeof(pg::Tile), &err);
     }
-    st->maps_cap = 64 + e->L.size() * (16 + 2 * nexp);
+    st->maps_cap = 64 + e->L.size() * (40 + 2 * nexp);  // (a Q6_K matrix takes four maps)
     st->maps = (CUtensorMap *)st->alloc(st->maps_cap * sizeof(CUtensorMap), &err);
     if (err != cudaSuccess) {
         delete st;
@@ -198,12 +204,15 @@ struct PfRun {
     {
         auto it = st->map_of.find(m.w);
         if (it != st->map_of.end()) return it->second;
-        if (st->maps_n >= st->maps_cap) return -1;
-        CUtensorMap h;
-        if (pg::make_wmap(&h, m.dt, m.w, (int)m.rows, (int)m.cols)) return -1;
-        if (cudaMemcpy(st->maps + st->maps_n, &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess) return -1;
-        st->map_of[m.w] = (int)st->maps_n;
-        return (int)st->maps_n++;
+        CUtensorMap h[4];
+        const int nm = pg::make_wmaps(h, m.dt, m.w, (int)m.rows, (int)m.cols);
+        if (nm < 1 || st->maps_n + nm > st->maps_cap) return -1;
+        if (cudaMemcpy(st->maps + st->maps_n, h, nm * sizeof(CUtensorMap), cudaMemcpyHostToDevice) != cudaSuccess)
+            return -1;
+        const int first = (int)st->maps_n;
+        st->map_of[m.w] = first;
+        st->maps_n += nm;
+        return first;
     }
 
     // a contiguous block of maps for a list of matrices (the experts of a layer), built once
@@ -588,8 +597,8 @@ extern "C" int sb_decode_prefill(sb_ctx *c, const int32_t *tokens, size_t n, siz
         if (!L.mla && !blk::attn_prefill_takes((int)L.hd, (int)L.hd, (int)(L.heads / L.kvh))) return 0;
         if (L.moe) {
             if (!L.ex_pairs || !(pf_gemm_dtype(L.router.dt) || L.router.dt == SB_DTYPE_F32) ||
-                !pf_gemm_dtype(L.ex[0].dt) ||
-                !pf_gemm_dtype(L.ex[2].dt) || L.effn % 64 || (L.sh_here && (L.sh[0].rows / 2) % 64))
+                !pf_group_dtype(L.ex[0].dt) ||
+                !pf_group_dtype(L.ex[2].dt) || L.effn % 64 || (L.sh_here && (L.sh[0].rows / 2) % 64))
                 return 0;
         } else if (!L.gu2.w || !pf_gemm_dtype(L.gu2.dt) || L.ffn % 64) {
             return 0;
