@@ -344,8 +344,8 @@ int sb_decode_route_trace(sb_ctx *ctx, size_t pos, int32_t *idx, size_t n, float
  * decoding goes on with sb_decode_greedy / sb_decode_token at pos0 + n.  logits
  * (host f32[vocab]) and next (the argmax, ties to the last index) may be NULL.  Needs
  * plan.embed.  1 = done, 0 = not prepared, a tensor-parallel engine, or a plan with a
- * layer the block path does not take (weight formats other than Q4_K / Q8_0 for the
- * attention, router and expert matrices, widths not multiples of 64), <0 = error. */
+ * layer the block path does not take (expert matrices other than Q4_K / Q8_0, other
+ * matrices other than Q4_K / Q8_0 / Q6_K, widths not multiples of 64), <0 = error. */
 int sb_decode_prefill(sb_ctx *ctx, const int32_t *tokens, size_t n, size_t pos0, float *logits, int32_t *next);
 
 /* ---- tensor-parallel groups (no counterpart in the reference, whose multi-machine mode
