@@ -113,3 +113,23 @@ def test_prefill_declines_what_it_does_not_take():
             sess.prefill(np.arange(8, dtype=np.int32))
     finally:
         sess.close()
+
+
+@pytest.mark.parametrize("which,n", [("moe", 1), ("moe", 2), ("moe", 64), ("moe", 65), ("dense_q6k_down", 1),
+                                     ("dense_q6k_down", 129), ("mla_moe", 1), ("mla_moe", 150), ("moe_shared", 191)])
+def test_prefill_block_sizes(which, n):
+    """Blocks of 1 token, of a tile width and one past it, and up to the context: the last
+    token's logits against the oracle run over the same tokens one at a time."""
+    cfg = CONFIGS[which]
+    model = decode.synth_model(cfg, f"pf_n_{which}")
+    prompt = synth.rng("pf_n", which, n).integers(0, cfg.vocab, n).astype(np.int32)
+    sess = decode.DecodeSession(cfg, model)
+    try:
+        lg, nxt = sess.prefill(prompt)
+    finally:
+        sess.close()
+    orc = DenseOracle(cfg, model)
+    for i, t in enumerate(prompt):
+        want = orc.step(orc.embed(int(t)), i)
+    assert _rel(lg, want) <= LOGIT_REL, (which, n)
+    assert nxt == oracle.argmax(want) or _gap(want) < TIE
