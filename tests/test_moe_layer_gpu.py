@@ -173,3 +173,22 @@ def test_moe_capa_declines_sliding_window(setup):
     assert not gpu.moe_capa(capa)
     assert not gpu.moe_puede(7)
     assert not gpu.moe_capa(capa)
+
+
+@pytest.mark.parametrize("n", [1, 3, 100])
+def test_moe_capa_block_sizes(setup, n):
+    """One token, a few, and most of the context in a block, then one more token after it."""
+    cfg, model, gpu = setup
+    g = synth.rng("moe_capa", "n", n)
+    a = g.standard_normal((n, cfg.hidden)).astype(np.float32)
+    b = g.standard_normal((1, cfg.hidden)).astype(np.float32)
+    ref = _Ref(cfg, model)
+    want_a, gaps_a = ref.layer(1, a, 0)
+    want_b, gaps_b = ref.layer(1, b, n)
+    ha, hb = a.copy(), b.copy()
+    assert gpu.moe_capa(_capa(cfg, model, 1, 0, ha))
+    assert gpu.moe_capa(_capa(cfg, model, 1, n, hb, normas=False))
+    if (gaps_a >= ROUTE_TIE).any():
+        _check(ha[gaps_a >= ROUTE_TIE], want_a[gaps_a >= ROUTE_TIE], a[gaps_a >= ROUTE_TIE], gaps_a[gaps_a >= ROUTE_TIE])
+    if gaps_b[0] >= ROUTE_TIE:
+        _check(hb, want_b, b, gaps_b)
