@@ -184,40 +184,47 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b)
 // Shared memory of attn_prefill_kernel<KQ, NV, QS>: q hi / lo staging [2][64][QP] (kept for
 // the whole kernel when QS, else reused) and the key / value double buffers [2][32][QP],
 // [2][32][VP] (f16, row pitches padded by 16 bytes against bank conflicts).
-template <int KQ, int NV, bool QS>
+template <int KQ, int NV, bool QS, int KS>
 __host__ __device__ constexpr size_t attn_prefill_smem()
 {
     constexpr size_t QP = 16 * KQ + 8, VP = 8 * NV + 8, qbytes = 2 * AP_ROWS * QP * 2,
-                     kvbytes = 2 * AP_KB * (QP + VP) * 2;
-    return QS ? qbytes + kvbytes : (qbytes > kvbytes ? qbytes : kvbytes);
+                     kvbytes = 2 * KS * AP_KB * (QP + VP) * 2, merge = AP_ROWS * (8 * NV + 2) * 4;
+    constexpr size_t a = QS ? qbytes + kvbytes : (qbytes > kvbytes ? qbytes : kvbytes);
+    return a > merge ? a : merge;
 }
 
 // Widths up to 16 KQ (q, k) and 8 NV (v) that are multiples of 8: the columns past a.dqk /
 // a.dv are zero in shared memory and drop out of both products.  QS: the q fragments are
 // read from shared memory at every key block instead of being held in registers (the
 // 256-wide heads, whose q hi / lo and output accumulators would not fit in registers).
-template <int KQ, int NV, bool QS>
-__global__ void __launch_bounds__(AP_WARPS * 32) attn_prefill_kernel(AttnPrefillArgs a)
+// KS = 2: eight warps, the keys of each 64-key stage split between two groups of four (one
+// online softmax each, merged at the end), so that twice the warps hide the MMA and load
+// latencies of a CTA's 64 rows.
+template <int KQ, int NV, bool QS, int KS>
+__global__ void __launch_bounds__(KS *AP_WARPS * 32) attn_prefill_kernel(AttnPrefillArgs a)
 {
     constexpr int DQ = 16 * KQ, DV = 8 * NV, QP = DQ + 8, VP = DV + 8;  // row pitches (f16)
+    constexpr int NT = KS * AP_WARPS * 32, SKEYS = KS * AP_KB;         // threads, keys a stage
     extern __shared__ __align__(16) uint16_t ap_smem[];
     uint16_t *qh = ap_smem, *ql = qh + AP_ROWS * QP;                   // q hi / lo
-    uint16_t *ks = QS ? ql + AP_ROWS * QP : ap_smem, *vs = ks + 2 * AP_KB * QP;
+    uint16_t *ks = QS ? ql + AP_ROWS * QP : ap_smem, *vs = ks + 2 * SKEYS * QP;
     griddep_wait();
     // the CTA's 64 rows: tpc tokens x the G query heads of kv head g (rows past tpc G idle)
     const int G = a.heads / a.kv_heads, g = blockIdx.y, tpc = AP_ROWS / G, t0 = blockIdx.x * tpc;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gq = lane >> 2, tq = lane & 3;
+    const int rw = warp % AP_WARPS, kh = warp / AP_WARPS;  // row group, key group
     // q of the CTA's rows -> f16 hi / lo in shared memory: 16-byte loads, a batch of them in
     // flight before the first is used
     {
-        constexpr int C4 = DQ / 4, PER = AP_ROWS * C4 / (AP_WARPS * 32), NB = PER % 8 == 0 ? 8 : 4;
-        static_assert(AP_ROWS * C4 % (AP_WARPS * 32) == 0 && PER % NB == 0, "q staging shape");
+        constexpr int C4 = DQ / 4, PER = AP_ROWS * C4 / NT;
+        constexpr int NB = PER % 8 == 0 ? 8 : PER % 4 == 0 ? 4 : PER % 2 == 0 ? 2 : 1;
+        static_assert(AP_ROWS * C4 % NT == 0 && PER % NB == 0, "q staging shape");
 #pragma unroll 1
         for (int i0 = 0; i0 < PER; i0 += NB) {
             float4 xv[NB];
 #pragma unroll
             for (int u = 0; u < NB; u++) {
-                const int i = threadIdx.x + (i0 + u) * AP_WARPS * 32, r = i / C4, d = 4 * (i % C4);
+                const int i = threadIdx.x + (i0 + u) * NT, r = i / C4, d = 4 * (i % C4);
                 const int t = t0 + r / G, hh = g * G + r % G;
                 xv[u] = r < tpc * G && t < a.n && d < a.dqk
                             ? *reinterpret_cast<const float4 *>(a.q + (size_t)t * a.ldq + hh * a.dqk + d)
@@ -225,7 +232,7 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attn_prefill_kernel(AttnPrefill
             }
 #pragma unroll
             for (int u = 0; u < NB; u++) {
-                const int i = threadIdx.x + (i0 + u) * AP_WARPS * 32, r = i / C4, d = 4 * (i % C4);
+                const int i = threadIdx.x + (i0 + u) * NT, r = i / C4, d = 4 * (i % C4);
                 uint16_t hi[4], lo[4];
                 split_f16(xv[u].x, hi[0], lo[0]);
                 split_f16(xv[u].y, hi[1], lo[1]);
@@ -240,7 +247,7 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attn_prefill_kernel(AttnPrefill
     }
     __syncthreads();
     const int mi = lane >> 3, mr = lane & 7;
-    const int qrow = 16 * warp + mr + (mi & 1) * 8, qcol = (mi >> 1) * 8;  // ldmatrix addresses
+    const int qrow = 16 * rw + mr + (mi & 1) * 8, qcol = (mi >> 1) * 8;  // ldmatrix addresses
     uint32_t fqh[QS ? 1 : KQ][4], fql[QS ? 1 : KQ][4];
     if constexpr (!QS) {
 #pragma unroll
@@ -254,22 +261,22 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attn_prefill_kernel(AttnPrefill
     int lim[2];
 #pragma unroll
     for (int h2 = 0; h2 < 2; h2++) {
-        const int r = 16 * warp + gq + 8 * h2, t = t0 + r / G;
+        const int r = 16 * rw + gq + 8 * h2, t = t0 + r / G;
         lim[h2] = r < tpc * G && t < a.n ? a.pos0 + t : -1;
     }
-    const int tl = min(t0 + tpc, a.n) - 1, kend = a.pos0 + tl + 1, nblk = (kend + AP_KB - 1) / AP_KB;
+    const int tl = min(t0 + tpc, a.n) - 1, kend = a.pos0 + tl + 1, nstg = (kend + SKEYS - 1) / SKEYS;
     auto load = [&](int buf, int k0) {
         constexpr int KC = DQ / 8, VC = DV / 8;  // 16-byte pieces a row
         const int kc = a.dqk / 8, vc = a.dv / 8;
-        for (int i = threadIdx.x; i < AP_KB * (KC + VC); i += AP_WARPS * 32) {
+        for (int i = threadIdx.x; i < SKEYS * (KC + VC); i += NT) {
             const int row = i / (KC + VC), c = i % (KC + VC), key = k0 + row;
             const bool ok = key < kend;
             const int kk = ok ? key : 0;
             if (c < KC)
-                cp_async16(ks + (buf * AP_KB + row) * QP + 8 * c,
+                cp_async16(ks + (buf * SKEYS + row) * QP + 8 * c,
                            a.k + (size_t)kk * a.ldk + g * a.dqk + 8 * min(c, kc - 1), ok && c < kc);
             else
-                cp_async16(vs + (buf * AP_KB + row) * VP + 8 * (c - KC),
+                cp_async16(vs + (buf * SKEYS + row) * VP + 8 * (c - KC),
                            a.v + (size_t)kk * a.ldv + g * a.dv + 8 * min(c - KC, vc - 1), ok && c - KC < vc);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
@@ -278,16 +285,16 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attn_prefill_kernel(AttnPrefill
 #pragma unroll
     for (int n = 0; n < NV; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
     load(0, 0);
-    for (int b = 0; b < nblk; b++) {
-        const int buf = b & 1, k0 = b * AP_KB;
-        if (b + 1 < nblk) {
-            load(buf ^ 1, k0 + AP_KB);
+    for (int b = 0; b < nstg; b++) {
+        const int buf = b & 1, k0 = b * SKEYS + kh * AP_KB;  // this key group's 32 keys of the stage
+        if (b + 1 < nstg) {
+            load(buf ^ 1, (b + 1) * SKEYS);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
-        const uint16_t *kb = ks + buf * AP_KB * QP, *vb = vs + buf * AP_KB * VP;
+        const uint16_t *kb = ks + (buf * SKEYS + kh * AP_KB) * QP, *vb = vs + (buf * SKEYS + kh * AP_KB) * VP;
         // S = Q K^T for the block's 4 key tiles of 8
         float sc[4][4];
 #pragma unroll
@@ -362,11 +369,44 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attn_prefill_kernel(AttnPrefill
                 tcmv::mma_f16(o[n + 1], pa0, pa1, pa2, pa3, bv[2], bv[3]);
             }
         }
-        __syncthreads();  // the buffer is refilled two blocks on
+        __syncthreads();  // the buffer is refilled two stages on
+    }
+    if constexpr (KS == 2) {
+        // key group 1 hands its (m, l, o) of every row to group 0 through shared memory (the
+        // key / value buffers are free now), which merges the two softmax halves
+        float *mo = reinterpret_cast<float *>(ap_smem), *ml = mo + AP_ROWS * DV;
+        if (kh == 1) {
+#pragma unroll
+            for (int h2 = 0; h2 < 2; h2++) {
+                const int r = 16 * rw + gq + 8 * h2;
+#pragma unroll
+                for (int n = 0; n < NV; n++)
+                    *reinterpret_cast<float2 *>(mo + r * DV + 8 * n + 2 * tq) = make_float2(o[n][2 * h2], o[n][2 * h2 + 1]);
+                if (tq == 0) ml[2 * r] = m[h2], ml[2 * r + 1] = l[h2];
+            }
+        }
+        __syncthreads();
+        if (kh == 1) {
+            griddep_launch();
+            return;
+        }
+#pragma unroll
+        for (int h2 = 0; h2 < 2; h2++) {
+            const int r = 16 * rw + gq + 8 * h2;
+            const float m1 = ml[2 * r], l1 = ml[2 * r + 1], mm = fmaxf(m[h2], m1);
+            const float c0 = m[h2] == -INFINITY ? 0.0f : expf(m[h2] - mm), c1 = m1 == -INFINITY ? 0.0f : expf(m1 - mm);
+            l[h2] = l[h2] * c0 + l1 * c1;
+#pragma unroll
+            for (int n = 0; n < NV; n++) {
+                const float2 u = *reinterpret_cast<const float2 *>(mo + r * DV + 8 * n + 2 * tq);
+                o[n][2 * h2] = o[n][2 * h2] * c0 + u.x * c1;
+                o[n][2 * h2 + 1] = o[n][2 * h2 + 1] * c0 + u.y * c1;
+            }
+        }
     }
 #pragma unroll
     for (int h2 = 0; h2 < 2; h2++) {
-        const int r = 16 * warp + gq + 8 * h2, t = t0 + r / G, hh = g * G + r % G;
+        const int r = 16 * rw + gq + 8 * h2, t = t0 + r / G, hh = g * G + r % G;
         if (r >= tpc * G || t >= a.n) continue;
         const float inv = l[h2] > 0.0f ? 1.0f / l[h2] : 0.0f;
         float *dst = a.out + (size_t)t * a.ldo + hh * a.dv + 2 * tq;
@@ -378,17 +418,17 @@ __global__ void __launch_bounds__(AP_WARPS * 32) attn_prefill_kernel(AttnPrefill
     griddep_launch();
 }
 
-template <int KQ, int NV, bool QS>
+template <int KQ, int NV, bool QS, int KS = QS ? 1 : 2>
 inline int attn_prefill_launch(const AttnPrefillArgs &a, dim3 grid, cudaStream_t s)
 {
-    constexpr size_t smem = attn_prefill_smem<KQ, NV, QS>();
+    constexpr size_t smem = attn_prefill_smem<KQ, NV, QS, KS>();
     static size_t rec[64];
     static std::mutex mu;
     {
         std::lock_guard<std::mutex> lk(mu);
-        if (tcmv::ensure_smem(attn_prefill_kernel<KQ, NV, QS>, smem, rec)) return -3;
+        if (tcmv::ensure_smem(attn_prefill_kernel<KQ, NV, QS, KS>, smem, rec)) return -3;
     }
-    return launch_k(attn_prefill_kernel<KQ, NV, QS>, grid, dim3(AP_WARPS * 32), smem, 1, s, a);
+    return launch_k(attn_prefill_kernel<KQ, NV, QS, KS>, grid, dim3(KS * AP_WARPS * 32), smem, 1, s, a);
 }
 
 // The kernel width class of (q width, v width): 0 none, else a case of attn_prefill.
