@@ -73,6 +73,12 @@ struct RowRaw {
     {
         W::template half16<F16>(slot + r * W::RAWB, p, h, row, r);
     }
+    // the whole 64-column stage of row r
+    template <bool F16>
+    __device__ __forceinline__ static void dq_row(const uint8_t *slot, int r, int, int p, uint8_t *row)
+    {
+        W::template row16<F16>(slot + r * W::RAWB, p, row, r);
+    }
 };
 
 struct FQ4K : RowRaw<FQ4K> {
@@ -82,6 +88,11 @@ struct FQ4K : RowRaw<FQ4K> {
     __device__ __forceinline__ static void half16(const uint8_t *raw, int p, int h, uint8_t *row, int r)
     {
         pf::q4k_half_to_16<F16>(raw, p, h, row, r);
+    }
+    template <bool F16>
+    __device__ __forceinline__ static void row16(const uint8_t *raw, int p, uint8_t *row, int r)
+    {
+        pf::q4k_row_to_16<F16>(raw, p, row, r);
     }
 };
 
@@ -108,6 +119,12 @@ struct FQ80 : RowRaw<FQ80> {
             const int chunk = 4 * h + c;
             *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = out;
         }
+    }
+    template <bool F16>
+    __device__ __forceinline__ static void row16(const uint8_t *raw, int p, uint8_t *row, int r)
+    {
+        half16<F16>(raw, p, 0, row, r);
+        half16<F16>(raw, p, 1, row, r);
     }
 };
 
@@ -165,6 +182,42 @@ struct FQ6KP {
             *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
+    // both 32-column chunks k = 2p, 2p + 1 of the stage: the qh bytes, the scale word and d
+    // loaded once
+    template <bool F16>
+    __device__ __forceinline__ static void dq_row(const uint8_t *slot, int r, int rk, int p, uint8_t *row)
+    {
+        const int n = rk & 1, w = (rk >> 1) & 7;
+        const uint4 *ql = reinterpret_cast<const uint4 *>(slot + QL + r * 64);
+        const uint4 *qh = reinterpret_cast<const uint4 *>(slot + QH + r * 32);
+        const uint32_t scw = *reinterpret_cast<const uint32_t *>(slot + SC + r * 16 + 8 * n + 4 * p);
+        const float d = __half2float(*reinterpret_cast<const __half *>(slot + DD + r * 16 + 2 * w));
+        const uint64_t nb2 = pf::dup2(-8388640.0f);
+        const uint4 h0 = qh[0], h1 = qh[1];
+        const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int h = 0; h < 2; h++) {  // k = 2p + h: ql bytes 32h.., scales at bytes 2h, 2h + 1 of scw
+            const uint4 l0 = ql[2 * h], l1 = ql[2 * h + 1];
+            const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+            const float s0 = d * (float)(int8_t)((scw >> (16 * h)) & 0xFFu);
+            const float s1 = d * (float)(int8_t)((scw >> (16 * h + 8)) & 0xFFu);
+            const int lsh = 4 * p, hsh = 2 * (2 * p + h);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                const uint64_t sc2 = pf::dup2(c < 2 ? s0 : s1);
+                uint32_t o[4];
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const uint32_t code =
+                        ((lw[2 * c + j] >> lsh) & 0x0F0F0F0Fu) | (((hw[2 * c + j] >> hsh) & 0x03030303u) << 4);
+                    o[2 * j] = pf::pack16x2<F16>(pf::mul_f32x2(pf::codes2(code, pf::SEL_B0, pf::SEL_B1, nb2), sc2));
+                    o[2 * j + 1] = pf::pack16x2<F16>(pf::mul_f32x2(pf::codes2(code, pf::SEL_B2, pf::SEL_B3, nb2), sc2));
+                }
+                const int chunk = 4 * h + c;
+                *reinterpret_cast<uint4 *>(row + ((chunk ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        }
+    }
 };
 
 template <class W, int BN>
@@ -218,7 +271,7 @@ __global__ void __launch_bounds__(THREADS, BN == 64 ? 2 : 1) pg_gemm_kernel(cons
     if (threadIdx.x == 0) {
         for (int i = 0; i < NST; i++) {
             tcmv::mbar_init(&x_full[i], 1);
-            tcmv::mbar_init(&w_full[i], NDQ);
+            tcmv::mbar_init(&w_full[i], NDQ / 2);  // a stage is one group's (four warps)
             tcmv::mbar_init(&st_empty[i], 1);
         }
         for (int i = 0; i < NRAW; i++) {
@@ -297,22 +350,26 @@ __global__ void __launch_bounds__(THREADS, BN == 64 ? 2 : 1) pg_gemm_kernel(cons
         }
         __syncwarp();
     } else {
-        // dequantisers: thread t takes weight row t % 128, half t / 128 of every stage
-        const int r = (threadIdx.x - 64) & (BM - 1), hh = (threadIdx.x - 64) / BM;
-        for (int ks = 0; ks < KS && !failed; ks++) {
+        // dequantisers: two groups of four warps take the even and the odd stages; thread t of
+        // a group takes weight row t % 128 of its stages, the whole 64 columns (the halves share
+        // their code bytes and block head).  A group releases a raw column after its last stage
+        // in it (both groups have stages in every raw column but a last, partial one, whose
+        // release nobody waits for).
+        const int r = (threadIdx.x - 64) & (BM - 1), grp = (threadIdx.x - 64) / BM;
+        for (int ks = grp; ks < KS && !failed; ks += 2) {
             const int st = ks % NST, rk = ks / W::SPR, rs = rk % NRAW, p = ks % W::SPR;
-            if (p == 0 && !tcmv::mbar_wait(&raw_full[rs], (rk / NRAW) & 1, pf::WAIT)) failed = true;
+            if (p < 2 && !tcmv::mbar_wait(&raw_full[rs], (rk / NRAW) & 1, pf::WAIT)) failed = true;
             if (!failed && ks >= NST && !tcmv::mbar_wait(&st_empty[st], ((ks / NST) - 1) & 1, pf::WAIT)) failed = true;
             if (failed) {
                 set_dev_error(0x83u);
                 break;
             }
-            W::template dq<F16>(sraw + rs * L::RAW_BYTES, r, rk, p, hh, sw + st * L::W_BYTES + r * 128);
+            W::template dq_row<F16>(sraw + rs * L::RAW_BYTES, r, rk, p, sw + st * L::W_BYTES + r * 128);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> MMA reads
             __syncwarp();
             if (lane == 0) {
                 tcmv::mbar_arrive(&w_full[st]);
-                if (p == W::SPR - 1 || ks == KS - 1) tcmv::mbar_arrive(&raw_empty[rs]);
+                if (ks + 2 >= (rk + 1) * W::SPR || ks + 2 >= KS) tcmv::mbar_arrive(&raw_empty[rs]);
             }
         }
         // epilogue: the accumulators of this warp's 32 lanes (weight rows)

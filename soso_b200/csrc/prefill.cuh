@@ -248,6 +248,54 @@ __device__ __forceinline__ void q4k_half_to_16(const uint8_t *blk, int p, int h,
     }
 }
 
+// Q4_K, both sub-blocks 2p (low nibbles: columns 0..31 of the stage) and 2p + 1 (high
+// nibbles: 32..63) of byte pair p -- one load of the block head and of the 32 code bytes
+// they share -- into the whole 128-byte swizzled row.
+template <bool F16>
+__device__ __forceinline__ void q4k_row_to_16(const uint8_t *blk, int p, uint8_t *row, int r)
+{
+    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+    const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+    auto sc = [&](int k) {
+        const uint32_t w = k < 4 ? hd.y : k < 8 ? hd.z : hd.w;
+        return (w >> (8 * (k & 3))) & 0xFFu;
+    };
+    uint64_t a2[2], mb2[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int j = 2 * p + h;
+        unsigned s_, m_;
+        if (j < 4) s_ = sc(j) & 63, m_ = sc(j + 4) & 63;
+        else s_ = (sc(j + 4) & 15) | ((sc(j - 4) >> 6) << 4), m_ = (sc(j + 4) >> 4) | ((sc(j) >> 6) << 4);
+        a2[h] = dup2(d * (float)s_), mb2[h] = dup2(-(dmin * (float)m_));
+    }
+    const uint64_t nb2 = dup2(-8388608.0f);
+    const uint4 *q4 = reinterpret_cast<const uint4 *>(blk + 16 + 32 * p);
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+        const uint4 qv = q4[half];
+        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            uint32_t out[8];
+#pragma unroll
+            for (int wd = 0; wd < 4; wd++) {
+                const uint32_t v = h ? (qw[wd] >> 4) & 0x0F0F0F0Fu : qw[wd] & 0x0F0F0F0Fu;
+                out[2 * wd] = pack16x2<F16>(fma_f32x2(codes2(v, SEL_B0, SEL_B1, nb2), a2[h], mb2[h]));
+                out[2 * wd + 1] = pack16x2<F16>(fma_f32x2(codes2(v, SEL_B2, SEL_B3, nb2), a2[h], mb2[h]));
+            }
+            const int c0 = 4 * h + 2 * half;
+#pragma unroll
+            for (int cc = 0; cc < 2; cc++) {
+                const int c = c0 + cc;
+                *reinterpret_cast<uint4 *>(row + ((c ^ (r & 7)) << 4)) =
+                    make_uint4(out[4 * cc], out[4 * cc + 1], out[4 * cc + 2], out[4 * cc + 3]);
+            }
+        }
+    }
+}
+
 struct Args {
     int rows, cols, n;
     float *y;      // [n][rows]
