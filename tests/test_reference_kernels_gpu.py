@@ -4,7 +4,8 @@ checkout is given), run beside this library's kernels on the same inputs on the 
 the kernels the drop-in replaces, checked for equal results and timed.
 
 * decode matvec: `dec_matvec` with the Q4_K decoder (code 1002, matvec_iq.cu:1930-1975), as
-  the reference's resident decode graph launches it (grid ceil(rows / 16), 256 threads,
+  the reference's resident decode graph launches it, and `gm_matvec_q4k` (gemma_capa.cu:433,
+  the whole-layer path's matvec; grid ceil(rows / 8), cuda.rs:817-840) (grid ceil(rows / 16), 256 threads,
   (cols + cols / 32 + 1) floats of shared memory: crates/soso-llm-api/src/cuda/decode.rs:
   729-741), one launch per matrix, against sbk_matvec (one launch per matrix, PDL chain)
   and sbk_matvec_batch (the matrices in one launch), on configs[1]'s shapes (11008x4096
@@ -120,7 +121,7 @@ def _time(fn, reps, warm=3, trials=3):
     return best
 
 
-def test_decode_matvec_vs_reference(refmod):
+def test_decode_matvec_vs_reference(refmod, capamod):
     import torch
     s = torch.cuda.current_stream()
     g = synth.rng("refkern", "q4k")
@@ -152,19 +153,32 @@ def test_decode_matvec_vs_reference(refmod):
     def ours_batch():
         assert L.sbk_matvec_batch(DTYPE_Q4_K, batch, len(mats), 1, s.cuda_stream) == 0
 
+    ys_gm = [torch.empty(r, device="cuda") for _, r, _ in mats]
+
+    def ref_gm():  # the Gemma-layer path's Q4_K matvec (gemma_capa.cu:433; grid ceil(rows / 8), cuda.rs:817-840)
+        for (w, rows, cols), y in zip(mats, ys_gm):
+            capamod.launch("gm_matvec_q4k", ((rows + 7) // 8, 1), 256, 0, s.cuda_stream,
+                           [("p", w.data_ptr()), ("p", x.data_ptr()), ("p", y.data_ptr()), ("i", rows), ("i", cols)])
+
     ref()
+    ref_gm()
     ours_batch()
     torch.cuda.synchronize()
+    for (w, rows, cols), yr, yo in zip(mats, ys_gm, ys_our):
+        yr, yo = yr.cpu().numpy().astype(np.float64), yo.cpu().numpy().astype(np.float64)
+        assert float(np.abs(yr - yo).max()) <= 1e-3 * float(np.sqrt(np.mean(yo ** 2))), (rows, cols)
     for (w, rows, cols), yr, yo in zip(mats, ys_ref, ys_our):
         yr, yo = yr.cpu().numpy().astype(np.float64), yo.cpu().numpy().astype(np.float64)
         rms = float(np.sqrt(np.mean(yo ** 2)))
         assert float(np.abs(yr - yo).max()) <= 1e-3 * rms, (rows, cols)
     nbytes = sum(w.numel() for w, _, _ in mats)
     t_ref, t_each, t_batch = _time(ref, 10), _time(ours_each, 10), _time(ours_batch, 10)
+    t_gm = _time(ref_gm, 10)
     print("REFKERN " + json.dumps({
         "case": "Q4_K decode matvec, configs[1] shapes (8 x 11008x4096 + 8 x 4096x4096, x f32)",
         "bytes": nbytes,
         "reference_dec_matvec": {"us": round(t_ref * 1e6, 1), "GBps": round(nbytes / t_ref / 1e9, 1)},
+        "reference_gm_matvec_q4k": {"us": round(t_gm * 1e6, 1), "GBps": round(nbytes / t_gm / 1e9, 1)},
         "sbk_matvec_per_matrix": {"us": round(t_each * 1e6, 1), "GBps": round(nbytes / t_each / 1e9, 1)},
         "sbk_matvec_batch": {"us": round(t_batch * 1e6, 1), "GBps": round(nbytes / t_batch / 1e9, 1)},
         "speedup_batch_vs_reference": round(t_ref / t_batch, 2)}))
