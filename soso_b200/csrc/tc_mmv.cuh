@@ -472,7 +472,7 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
 }
 
 template <class F>
-__global__ void __launch_bounds__(F::THREADS, 1) tc_mmv_kernel(const __grid_constant__ Batch B, Ws ws)
+__global__ void __launch_bounds__(F::THREADS, F::MINB) tc_mmv_kernel(const __grid_constant__ Batch B, Ws ws)
 {
     tc_mmv_body<F, false>(B, ws);
 }

@@ -35,15 +35,25 @@ __global__ void q80_pad_kernel(const uint8_t *__restrict__ src, long long rows, 
     dst[i] = o < rb ? src[r * rb + o] : 0;
 }
 
+#ifndef SB_Q80_NSTREAM
+#define SB_Q80_NSTREAM 3  // consumer teams (build-time tuning knob)
+#endif
+#ifndef SB_Q80_NSLOT
+#define SB_Q80_NSLOT 9  // ring slots, a multiple of the teams (build-time tuning knob)
+#endif
+#ifndef SB_Q80_MINB
+#define SB_Q80_MINB 1  // CTAs per SM the kernels are compiled for (build-time tuning knob)
+#endif
+
 struct Q80 {
     static constexpr uint8_t DTYPE = 15;  // SB_DTYPE_Q8_0_R (also reads SB_DTYPE_Q8_0 rows whose width is a multiple of 128)
     static constexpr int SBLK = 4;        // units (4 blocks, 128 weights) per stage
     static constexpr int NCONS = 4;
-    static constexpr int NSTREAM = 3;
+    static constexpr int NSTREAM = SB_Q80_NSTREAM;
     static constexpr int NCW = NCONS * NSTREAM;
     static constexpr int THREADS = (NCW + 1) * 32;
-    static constexpr int MINB = 1;
-    static constexpr int NSLOT = 9;       // a multiple of NSTREAM
+    static constexpr int MINB = SB_Q80_MINB;
+    static constexpr int NSLOT = SB_Q80_NSLOT;  // a multiple of NSTREAM
     static constexpr int BOXW = SBLK * 18 + 2;  // u64 per box row: one stage (576 B) + 16 B, so that
                                                 // rows are 148 words apart and the 4-byte fragment loads
                                                 // of a warp hit 32 distinct banks
