@@ -25,6 +25,9 @@
 // matvec_lote, crates/soso-llm-core/src/gpu.rs:694-701: several matvecs, one
 // wait); their stages are numbered one after another, so the batch streams as one.
 #pragma once
+#ifndef SB_GROUP_SLACK
+#define SB_GROUP_SLACK 8  // stages a busiest CTA may take beyond the even split to avoid cut groups (build-time knob)
+#endif
 #include <cstring>
 
 #include "tc_q4k.cuh"
@@ -730,9 +733,10 @@ inline int build_batch(const MatOpX *ops, int n, int cnt_cap, int grid, const XS
     for (int i = 0; i < n; i++)
         if ((uintptr_t)ops[i].xb & 15) return -2;
     // Whole groups per CTA when that costs at most one stage more on the busiest CTA
-    // and the stream-K split is short (latency-bound): no cross-CTA fix-up at all.
+    // and the stream-K split is short (latency-bound), or at most SB_GROUP_SLACK stages more
+    // (a stage streams in well under the cross-CTA fix-up's round trip): no fix-up at all.
     const int smax = (st + grid - 1) / grid, gmax = group_split_max(b, grid);
-    b.split_groups = gmax <= smax || (gmax <= smax + 1 && smax <= 4);
+    b.split_groups = gmax <= smax || (gmax <= smax + 1 && smax <= 4) || gmax <= smax + SB_GROUP_SLACK;
     b.pair_split = ops[0].pairs;
     if (b.pair_split) b.split_groups = 1;  // a pair's two groups finish in one CTA
     size_t smem = batch_smem<F>(plain, n, grid, &b.max_cols, &b.max_groups);
