@@ -616,10 +616,7 @@ int launch_moe_batch(sb::tcmv::Batch *b, const int *sel, size_t smem, cudaStream
     const int grid = sb::num_sms_cached();
     void *ws = sb::stream_ws(s, ws_bytes(grid));
     if (!ws) return -3;
-    Ws w;
-    w.cnt = reinterpret_cast<unsigned *>(ws);
-    w.part = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(ws) + ws_part_off());
-    return launch_dev_batch<F>(b, sel, smem, w, grid, 1, s);
+    return launch_dev_batch<F>(b, sel, smem, ws_of(ws), grid, 1, s);
 }
 
 // The MoE FFN after its router matvec: route, expert gate|up, expert downs.  pub: where the

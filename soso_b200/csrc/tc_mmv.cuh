@@ -71,6 +71,14 @@ struct Batch {
     MatDesc d[MAXB];
 };
 
+// Shared memory of the consumers besides the ring.
+struct Work {
+    uint8_t *prep;  // the prepared x of the current segment
+    uint8_t *zero;  // 64 B of zeros
+    float *part;    // [groups of this CTA][NCW][16]
+    float *red;     // [64]
+};
+
 template <class F>
 struct Smem {
     uint8_t *ring;    // NSLOT * SLOTB
@@ -80,6 +88,7 @@ struct Smem {
     float *red;       // [64]: the sum of squares of an XS_NORM input, per unit or per consumer warp
     uint64_t *full;   // [NSLOT]
     uint64_t *empty;  // [NSLOT]
+    __device__ Work work() const { return Work{prep, zero, part, red}; }
 };
 
 template <class F>
@@ -133,7 +142,7 @@ __device__ __forceinline__ int owner_of(int unit, int total, int n)
 constexpr int PREP_U = SB_PREP_U;
 
 template <class F>
-__device__ __forceinline__ void prep_segment(XLoad &X, int cols, float *h_out, float eps, const Smem<F> &s, int cwg,
+__device__ __forceinline__ void prep_segment(XLoad &X, int cols, float *h_out, float eps, const Work &s, int cwg,
                                              int lane)
 {
     constexpr int NCW = F::NCW, XPL = F::XPL;
@@ -219,16 +228,216 @@ __device__ __forceinline__ void prep_segment(XLoad &X, int cols, float *h_out, f
     }
 }
 
+// One format's ring of weight stages: NS slots of F::SLOTB bytes, a full barrier (the
+// producer's TMA completion) and an empty barrier (the consumer team's release) per slot.
+struct Ring {
+    uint8_t *slot;
+    uint64_t *full, *empty;
+};
+
+// The producer (one thread): TMA copies of this CTA's nst stages of batch B (its range
+// starts at global stage st0, in matrix m_first) into ring r, stage k into slot k % NS;
+// stage k >= NS first waits for the release of stage k - NS.  Returns the number of
+// stages copied: nst, or fewer if a wait ran out.
+template <class F, int NS>
+__device__ __forceinline__ int produce(const Batch &B, const Ring &r, int st0, int m_first, int nst, uint64_t pol)
+{
+    int mi = m_first, slot = 0;
+    unsigned phase = 0;  // parity of the empty-barrier phase to wait for
+    const MatDesc *d = &B.d[mi];
+    const CUtensorMap *mp = d->mapp ? d->mapp : &d->map;
+    int G = (st0 - d->st_begin) / d->spg, j = (st0 - d->st_begin) - G * d->spg;
+    int mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
+    asm volatile("prefetch.tensormap [%0];" ::"l"(mp) : "memory");
+    for (int k = 0; k < nst; k++) {
+        if (st0 + k == mend) {  // next matrix of the batch
+            d = &B.d[++mi];
+            mp = d->mapp ? d->mapp : &d->map;
+            G = 0, j = 0;
+            mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
+            asm volatile("prefetch.tensormap [%0];" ::"l"(mp) : "memory");
+        }
+        if (k >= NS && !mbar_wait(&r.empty[slot], phase)) return k;
+        mbar_expect_tx_arrive(&r.full[slot], (unsigned)F::SLOTB);  // full box, zero-filled past the ends
+        tma_load_2d(r.slot + slot * F::SLOTB, mp, F::stage_x(j), G * 16, &r.full[slot], pol);
+        if (++j == d->spg) j = 0, G++;
+        if (++slot == NS) {
+            slot = 0;
+            if (k >= NS) phase ^= 1u;  // stages 2*NS.. wait for the second use of a slot, ...
+        }
+    }
+    return nst;
+}
+
+// Wait (bounded) until the TMA copies of the last issued stages, max(0, n - NS)..n-1, have
+// landed: a CTA that gives up must not leave while copies into its shared memory are in flight.
+template <int NS>
+__device__ __forceinline__ void drain(const Ring &r, int n)
+{
+    for (int k = n > NS ? n - NS : 0; k < n; k++) mbar_wait(&r.full[k % NS], (unsigned)(k / NS) & 1u);
+}
+
+// The consumers of batch B (warp cwg of F::NCW, named barrier 1 among them): this CTA's
+// stages (cr: first stage, end stage, first and last matrix) from ring r, every segment's
+// x prepared first, rows written in the segment epilogue (cut groups' pieces to ws).
+template <class F, int NS>
+__device__ __forceinline__ void consume(const Batch &B, const Ring &r, const Work &s, Ws ws, int4 cr, int cwg,
+                                        int lane, bool &failed)
+{
+    constexpr int NCW = F::NCW, NSTREAM = F::NSTREAM;
+    static_assert(NS % NSTREAM == 0, "a ring slot must belong to one consumer team");
+    const int st0 = cr.x, st1 = cr.y, m_first = cr.z, m_last = cr.w;
+    const int nst = st1 - st0;
+    const int team = cwg / F::NCONS, cw = cwg % F::NCONS, g = lane >> 2, t = lane & 3;
+    const typename F::Lane L = F::lane_setup(g, t);
+    {
+        // this CTA's first matrix descriptor into the constant cache while the previous
+        // kernel finishes (the asm keeps the load before the wait)
+        const float *x_first = nst > 0 ? B.d[m_first].x : nullptr;
+        asm volatile("" ::"l"(x_first));
+    }
+    griddep_wait();  // x of every matrix is written by the previous kernel
+    if (B.wait.n) {  // the input's residual set comes from every rank of the group
+        if (cwg == 0 && lane == 0)
+            if (!grp::wait_counts(B.wait.cnt, B.wait.n, *B.wait.epoch * (unsigned)B.wait.per)) failed = true;
+        asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+    }
+    const float *prev_x = nullptr;
+    int prev_cols = 0;
+    for (int mi = m_first; mi <= m_last && nst > 0; mi++) {
+        const MatDesc &d = B.d[mi];
+        const int nb = F::units(d.cols), spg = d.spg;
+        const int mtot = spg * ((d.rows + 15) >> 4);
+        const int ka = max(st0, d.st_begin) - st0, kb = min(st1, d.st_begin + mtot) - st0;  // CTA-local stages
+        const int gs0 = (ka + st0 - d.st_begin) / spg, gs1 = (kb - 1 + st0 - d.st_begin) / spg;
+        const int ng = gs1 - gs0 + 1;
+        // x -> prep (unless the previous segment prepared the same x) and a clean
+        // partial table for this segment
+        if (d.x != prev_x || d.cols != prev_cols) {
+            XLoad X;
+            X.a = reinterpret_cast<const float4 *>(d.x);
+            X.b = reinterpret_cast<const float4 *>(d.xb ? d.xb : B.xs.b);
+            X.w = reinterpret_cast<const float4 *>(B.xs.w);
+            X.ys = reinterpret_cast<const float4 *>(B.xs.ys);
+            X.scale = 1.0f;
+            X.mode = B.xs.mode;
+            X.ny = B.xs.mode == XS_NORM ? B.xs.ny : 0;
+            X.ys4 = B.xs.ystride / 4;
+            for (int k = 0; k < X.ny; k++) X.yw[k] = B.xs.yw[k];
+            prep_segment<F>(X, d.cols, blockIdx.x == 0 ? B.xs.h_out : nullptr, B.xs.eps, s, cwg, lane);
+            prev_x = d.x;
+            prev_cols = d.cols;
+        }
+        for (int i = cwg * 32 + lane; i < ng * NCW * 16; i += NCW * 32) s.part[i] = 0.0f;
+        asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+        const typename F::Seg S = F::seg_setup(L, s.prep, s.zero, nb, d.cols);
+        float acc0 = 0.0f, acc1 = 0.0f;
+        int cur = -1;
+        // Team j takes the CTA-local stages k with k % NSTREAM == j in every segment, so
+        // (NS a multiple of NSTREAM) each ring slot is only ever read by one team.  That
+        // team waited for the slot's previous phase itself, so a parity wait can never
+        // mistake the phase before an unfinished one for the awaited phase.
+        const int k0 = ka + (team - ka % NSTREAM + NSTREAM) % NSTREAM;
+        int slot = k0 % NS, G = (k0 + st0 - d.st_begin) / spg, j = (k0 + st0 - d.st_begin) - G * spg;
+        unsigned parity = (k0 / NS) & 1;
+        auto flush = [&]() {
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+            if (t == 0) {
+                float *p = s.part + ((cur - gs0) * NCW + cwg) * 16;
+                p[g] = acc0;
+                p[g + 8] = acc1;
+            }
+        };
+        for (int k = k0; k < kb && !failed; k += NSTREAM) {
+            if (k != k0) {  // advance by NSTREAM stages
+                slot += NSTREAM;
+                if (slot >= NS) slot -= NS, parity ^= 1u;
+                j += NSTREAM;
+                while (j >= spg) j -= spg, G++;
+            }
+            if (!mbar_wait(&r.full[slot], parity)) {
+                failed = true;
+                set_dev_error(0x52u);
+                break;
+            }
+            if (G != cur) {
+                if (cur >= 0) flush();
+                cur = G;
+                acc0 = acc1 = 0.0f;
+            }
+            const int blk = j * F::SBLK + cw;
+            if (blk < nb) {
+                F::block(L, S, r.slot + slot * F::SLOTB, cw, blk, nb, &r.empty[slot], acc0, acc1);
+            } else {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&r.empty[slot]);
+            }
+        }
+        if (cur >= 0) flush();
+        asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+        // segment epilogue: sum the consumer warps' pieces per group (fixed order)
+        const bool head_cut = mi == m_first && (st0 - d.st_begin) % spg != 0;
+        const bool tail_cut = mi == m_last && (st1 - d.st_begin) % spg != 0 && st1 < d.st_begin + mtot;
+        if (d.pairs) {
+            // gate/up group pairs (whole in this CTA): y = silu(gate) * up (gemm.rs:210-226,
+            // the same f32 steps as the XS_SWIGLU input form)
+            for (int i = cwg * 32 + lane; i < (ng >> 1) * 16; i += NCW * 32) {
+                const int pl = i >> 4, rr = i & 15, row = ((gs0 >> 1) + pl) * 16 + rr;
+                float vg = 0.0f, vu = 0.0f;
+                for (int w = 0; w < NCW; w++) {
+                    vg += s.part[(2 * pl * NCW + w) * 16 + rr];
+                    vu += s.part[((2 * pl + 1) * NCW + w) * 16 + rr];
+                }
+                if (2 * row < d.rows) d.y[row] = vg / (1.0f + expf(-vg)) * vu;
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+            continue;
+        }
+        for (int i = cwg * 32 + lane; i < ng * 16; i += NCW * 32) {
+            const int gl = i >> 4, rr = i & 15, row = (gs0 + gl) * 16 + rr;
+            float v = 0.0f;
+            for (int w = 0; w < NCW; w++) v += s.part[(gl * NCW + w) * 16 + rr];
+            const bool cut = (gl == 0 && head_cut) || (gl == ng - 1 && tail_cut);
+            if (!cut) {
+                if (row < d.rows) {
+                    d.y[row] = v;
+                    for (int p = 0; p < B.pub.n; p++) B.pub.dst[p][d.pub_off + row] = v;
+                }
+            } else {
+                // side 0: the group holding this CTA's first stage, side 1: any other (its last)
+                const int ga = d.st_begin + (gs0 + gl) * spg;
+                ws.part[(blockIdx.x * 2 + ((st0 >= ga && st0 < ga + spg) ? 0 : 1)) * 16 + rr] = v;
+                __threadfence();
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
+    }
+}
+
+// Every row this CTA owns is in the peers' exchange areas: count the CTA there (all CTAs
+// count, so the consumers' target is epoch * grid whatever the split).  All threads.
+__device__ __forceinline__ void publish_count(const Batch &B)
+{
+    if (B.pub.n) {
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x < B.pub.n) atomicAdd_system(B.pub.cnt[threadIdx.x], 1u);
+    }
+}
+
 template <class F, bool DEV>
 __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
 {
     // A batch in device memory may have been written by the previous kernel (the expert
     // choice): everyone, the producer included, waits for it before reading the batch.
     if (DEV) griddep_wait();
-    constexpr int NCW = F::NCW, NSLOT = F::NSLOT, NSTREAM = F::NSTREAM;
-    static_assert(NSLOT % NSTREAM == 0, "a ring slot must belong to one consumer team");
+    constexpr int NSLOT = F::NSLOT;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<F> s = carve<F>(smem_raw, B.max_cols, B.max_groups);
+    const Ring ring{s.ring, s.full, s.empty};
     const int4 cr = B.cta[blockIdx.x];  // (built on the host: fill_cta)
     const int st0 = cr.x, st1 = cr.y, m_first = cr.z, m_last = cr.w;
     const int nst = st1 - st0;
@@ -248,184 +457,24 @@ __device__ __forceinline__ void tc_mmv_body(const Batch &B, Ws ws)
     griddep_launch();
 
     bool failed = false;
+    int issued = 0;
     if (warp == 0) {
         // ---------------- producer: weights do not depend on the previous kernel, so the
         // whole stream runs without griddepcontrol.wait
         if (lane == 0 && nst > 0) {
-            int mi = m_first, slot = 0;
-            unsigned phase = 0;  // parity of the empty-barrier phase to wait for
-            const uint64_t pol = l2_evict_first();
-            const MatDesc *d = &B.d[mi];
-            const CUtensorMap *mp = d->mapp ? d->mapp : &d->map;
-            int ls = st0 - d->st_begin, G = ls / d->spg, j = ls - G * d->spg;
-            int mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
-            asm volatile("prefetch.tensormap [%0];" ::"l"(mp) : "memory");
-            for (int k = 0; k < nst; k++) {
-                if (st0 + k == mend) {  // next matrix of the batch
-                    d = &B.d[++mi];
-                    mp = d->mapp ? d->mapp : &d->map;
-                    G = 0, j = 0;
-                    mend = d->st_begin + d->spg * ((d->rows + 15) >> 4);
-                    asm volatile("prefetch.tensormap [%0];" ::"l"(mp) : "memory");
-                }
-                if (k >= NSLOT && !mbar_wait(&s.empty[slot], phase)) {
-                    failed = true;
-                    break;
-                }
-                mbar_expect_tx_arrive(&s.full[slot], (unsigned)F::SLOTB);  // full box, zero-filled past the ends
-                tma_load_2d(s.ring + slot * F::SLOTB, mp, F::stage_x(j), G * 16, &s.full[slot], pol);
-                if (++j == d->spg) j = 0, G++;
-                if (++slot == NSLOT) {
-                    slot = 0;
-                    if (k >= NSLOT) phase ^= 1u;  // stages 2*NSLOT.. wait for the second use of a slot, ...
-                }
+            issued = produce<F, NSLOT>(B, ring, st0, m_first, nst, l2_evict_first());
+            if (issued < nst) {
+                failed = true;
+                set_dev_error(0x51u);
             }
-            if (failed) set_dev_error(0x51u);
         }
         __syncwarp();
     } else {
-        // ---------------- consumers
-        const int cwg = warp - 1;  // 0 .. NCW-1
-        const int team = cwg / F::NCONS, cw = cwg % F::NCONS, g = lane >> 2, t = lane & 3;
-        const typename F::Lane L = F::lane_setup(g, t);
-        {
-            // this CTA's first matrix descriptor into the constant cache while the previous
-            // kernel finishes (the asm keeps the load before the wait)
-            const float *x_first = nst > 0 ? B.d[m_first].x : nullptr;
-            asm volatile("" ::"l"(x_first));
-        }
-        griddep_wait();  // x of every matrix is written by the previous kernel
-        if (B.wait.n) {  // the input's residual set comes from every rank of the group
-            if (cwg == 0 && lane == 0)
-                if (!grp::wait_counts(B.wait.cnt, B.wait.n, *B.wait.epoch * (unsigned)B.wait.per)) failed = true;
-            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-        }
-        const float *prev_x = nullptr;
-        int prev_cols = 0;
-        for (int mi = m_first; mi <= m_last && nst > 0; mi++) {
-            const MatDesc &d = B.d[mi];
-            const int nb = F::units(d.cols), spg = d.spg;
-            const int mtot = spg * ((d.rows + 15) >> 4);
-            const int ka = max(st0, d.st_begin) - st0, kb = min(st1, d.st_begin + mtot) - st0;  // CTA-local stages
-            const int gs0 = (ka + st0 - d.st_begin) / spg, gs1 = (kb - 1 + st0 - d.st_begin) / spg;
-            const int ng = gs1 - gs0 + 1;
-            // x -> prep (unless the previous segment prepared the same x) and a clean
-            // partial table for this segment
-            if (d.x != prev_x || d.cols != prev_cols) {
-                XLoad X;
-                X.a = reinterpret_cast<const float4 *>(d.x);
-                X.b = reinterpret_cast<const float4 *>(d.xb ? d.xb : B.xs.b);
-                X.w = reinterpret_cast<const float4 *>(B.xs.w);
-                X.ys = reinterpret_cast<const float4 *>(B.xs.ys);
-                X.scale = 1.0f;
-                X.mode = B.xs.mode;
-                X.ny = B.xs.mode == XS_NORM ? B.xs.ny : 0;
-                X.ys4 = B.xs.ystride / 4;
-                for (int k = 0; k < X.ny; k++) X.yw[k] = B.xs.yw[k];
-                prep_segment<F>(X, d.cols, blockIdx.x == 0 ? B.xs.h_out : nullptr, B.xs.eps, s, cwg, lane);
-                prev_x = d.x;
-                prev_cols = d.cols;
-            }
-            for (int i = cwg * 32 + lane; i < ng * NCW * 16; i += NCW * 32) s.part[i] = 0.0f;
-            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-            const typename F::Seg S = F::seg_setup(L, s.prep, s.zero, nb, d.cols);
-            float acc0 = 0.0f, acc1 = 0.0f;
-            int cur = -1;
-            // Team j takes the CTA-local stages k with k % NSTREAM == j in every segment, so
-            // (NSLOT a multiple of NSTREAM) each ring slot is only ever read by one team.  That
-            // team waited for the slot's previous phase itself, so a parity wait can never
-            // mistake the phase before an unfinished one for the awaited phase.
-            const int k0 = ka + (team - ka % NSTREAM + NSTREAM) % NSTREAM;
-            int slot = k0 % NSLOT, G = (k0 + st0 - d.st_begin) / spg, j = (k0 + st0 - d.st_begin) - G * spg;
-            unsigned parity = (k0 / NSLOT) & 1;
-            auto flush = [&]() {
-                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-                acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-                acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
-                if (t == 0) {
-                    float *p = s.part + ((cur - gs0) * NCW + cwg) * 16;
-                    p[g] = acc0;
-                    p[g + 8] = acc1;
-                }
-            };
-            for (int k = k0; k < kb && !failed; k += NSTREAM) {
-                if (k != k0) {  // advance by NSTREAM stages
-                    slot += NSTREAM;
-                    if (slot >= NSLOT) slot -= NSLOT, parity ^= 1u;
-                    j += NSTREAM;
-                    while (j >= spg) j -= spg, G++;
-                }
-                if (!mbar_wait(&s.full[slot], parity)) {
-                    failed = true;
-                    set_dev_error(0x52u);
-                    break;
-                }
-                if (G != cur) {
-                    if (cur >= 0) flush();
-                    cur = G;
-                    acc0 = acc1 = 0.0f;
-                }
-                const int blk = j * F::SBLK + cw;
-                if (blk < nb) {
-                    F::block(L, S, s.ring + slot * F::SLOTB, cw, blk, nb, &s.empty[slot], acc0, acc1);
-                } else {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&s.empty[slot]);
-                }
-            }
-            if (cur >= 0) flush();
-            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-            // segment epilogue: sum the consumer warps' pieces per group (fixed order)
-            const bool head_cut = mi == m_first && (st0 - d.st_begin) % spg != 0;
-            const bool tail_cut = mi == m_last && (st1 - d.st_begin) % spg != 0 && st1 < d.st_begin + mtot;
-            if (d.pairs) {
-                // gate/up group pairs (whole in this CTA): y = silu(gate) * up (gemm.rs:210-226,
-                // the same f32 steps as the XS_SWIGLU input form)
-                for (int i = cwg * 32 + lane; i < (ng >> 1) * 16; i += NCW * 32) {
-                    const int pl = i >> 4, r = i & 15, row = ((gs0 >> 1) + pl) * 16 + r;
-                    float vg = 0.0f, vu = 0.0f;
-                    for (int w = 0; w < NCW; w++) {
-                        vg += s.part[(2 * pl * NCW + w) * 16 + r];
-                        vu += s.part[((2 * pl + 1) * NCW + w) * 16 + r];
-                    }
-                    if (2 * row < d.rows) d.y[row] = vg / (1.0f + expf(-vg)) * vu;
-                }
-                asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-                continue;
-            }
-            for (int i = cwg * 32 + lane; i < ng * 16; i += NCW * 32) {
-                const int gl = i >> 4, r = i & 15, row = (gs0 + gl) * 16 + r;
-                float v = 0.0f;
-                for (int w = 0; w < NCW; w++) v += s.part[(gl * NCW + w) * 16 + r];
-                const bool cut = (gl == 0 && head_cut) || (gl == ng - 1 && tail_cut);
-                if (!cut) {
-                    if (row < d.rows) {
-                        d.y[row] = v;
-                        for (int p = 0; p < B.pub.n; p++) B.pub.dst[p][d.pub_off + row] = v;
-                    }
-                } else {
-                    // side 0: the group holding this CTA's first stage, side 1: any other (its last)
-                    const int ga = d.st_begin + (gs0 + gl) * spg;
-                    ws.part[(blockIdx.x * 2 + ((st0 >= ga && st0 < ga + spg) ? 0 : 1)) * 16 + r] = v;
-                    __threadfence();
-                }
-            }
-            asm volatile("bar.sync 1, %0;" ::"r"(NCW * 32) : "memory");
-        }
+        consume<F, NSLOT>(B, ring, s.work(), ws, cr, warp - 1, lane, failed);
     }
-    if (failed) {
-        // let every TMA copy issued into this CTA's shared memory land before exiting (bounded)
-        if (warp == 0 && lane == 0)
-            for (int k = nst > NSLOT ? nst - NSLOT : 0; k < nst; k++) mbar_wait(&s.full[k % NSLOT], (k / NSLOT) & 1);
-    }
-    if (B.pub.n) {
-        // every row this CTA owns is in the peers' areas: count the CTA (all CTAs count,
-        // so the consumers' target is epoch * grid whatever the split)
-        __threadfence_system();
-        __syncthreads();
-        if (threadIdx.x < B.pub.n) atomicAdd_system(B.pub.cnt[threadIdx.x], 1u);
-    }
+    // let every TMA copy issued into this CTA's shared memory land before exiting (bounded)
+    if (failed && warp == 0 && lane == 0) drain<NSLOT>(ring, issued);
+    publish_count(B);
     if (B.split_groups) return;  // whole groups: every row is final in the CTA that formed it
     __syncthreads();
     if (nst <= 0) return;
@@ -503,6 +552,14 @@ __global__ void __launch_bounds__(F::THREADS, F::MINB) tc_mmv_dev_kernel(const B
 // [part: grid*2*16 f32].  Zeroed once when allocated; the kernel leaves it zeroed.
 inline size_t ws_part_off() { return (size_t)CNT_MAX * 4; }
 inline size_t ws_bytes(int grid) { return ws_part_off() + (size_t)grid * 2 * 16 * 4 + 256; }
+inline Ws ws_of(void *p)
+{
+    uint8_t *b = reinterpret_cast<uint8_t *>(p);
+    Ws w;
+    w.cnt = reinterpret_cast<unsigned *>(b);
+    w.part = reinterpret_cast<float *>(b + ws_part_off());
+    return w;
+}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -866,11 +923,7 @@ inline int launch_batch(const MatOp *ops, int n, void *ws, int grid, int pdl, cu
                         const XSrc *xs = nullptr, const grp::Pub *pub = nullptr, const grp::Wait *wait = nullptr,
                         bool pairs = false)
 {
-    uint8_t *wsb = reinterpret_cast<uint8_t *>(ws);
-    Ws wsd;
-    wsd.cnt = reinterpret_cast<unsigned *>(wsb);
-    wsd.part = reinterpret_cast<float *>(wsb + ws_part_off());
-    return launch_batch_ws<F>(ops, n, wsd, CNT_MAX, grid, pdl, stream, xs, pub, wait, pairs);
+    return launch_batch_ws<F>(ops, n, ws_of(ws), CNT_MAX, grid, pdl, stream, xs, pub, wait, pairs);
 }
 
 // Repack GGML Q6_K rows (reference layout) into the packed layout of tc_q6k.cuh.
