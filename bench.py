@@ -376,6 +376,9 @@ def run_ours(args) -> None:
             line[k] = v
         if cpu:
             line["cpu_baseline"] = cpu
+        # the same summary again as the line's last key: a reader that keeps only the end of a
+        # long line still sees every config's tokens/s, roofline fraction and agreement
+        line["summary_tail"] = summary
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
