@@ -101,8 +101,7 @@ __device__ __forceinline__ float bits_f(uint32_t u) { return __uint_as_float(u);
 
 constexpr float TWO_P60 = 1152921504606846976.0f;  // 2^60
 
-// Sum over the 8-lane group that contains this lane.  The mask names only the
-// group, so groups of one warp may call it at different times.
+// Sum over the warp (a butterfly: every lane ends with the same sum).
 __device__ __forceinline__ float warp_sum(float v)
 {
 #pragma unroll
@@ -110,6 +109,8 @@ __device__ __forceinline__ float warp_sum(float v)
     return v;
 }
 
+// Sum over the 8-lane group that contains this lane.  The mask names only the
+// group, so groups of one warp may call it at different times.
 __device__ __forceinline__ float warp8_sum(float v)
 {
     const unsigned m = 0xffu << (threadIdx.x & 24);
