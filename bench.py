@@ -850,6 +850,19 @@ def run_decode_case(tokens: int) -> None:
     print(json.dumps({"case": "decode", "tokens": toks.tolist()}))
 
 
+def run_decode_moe_case(tokens: int) -> None:
+    """A 4-layer slice of configs[3] (the MoE decoder: 128 experts, top-8) through the
+    whole-token engine: `tokens` greedy steps after an 8-token prompt -- for an ncu launch list."""
+    import dataclasses
+
+    from soso_b200 import decode
+    cfg = dataclasses.replace(decode.QWEN3_30B_A3B, n_layers=4)
+    sess = decode.DecodeSession(cfg, decode.synth_model(cfg, "ncu"))
+    toks = sess.greedy(np.arange(8, dtype=np.int32), tokens)
+    sess.close()
+    print(json.dumps({"case": "decode_moe", "tokens": toks[-4:].tolist()}))
+
+
 def run_prefill_engine_case(launches: int) -> None:
     """A 3-layer slice of configs[4] (MLA attention; the dense FFN layer, then two MoE layers)
     through the block prefill: `launches` prefills of a 512-token prompt -- for ncu captures
@@ -919,7 +932,7 @@ def run_case(name: str, launches: int) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ncu-case", choices=sorted(NCU_CASES) + ["q4k_batch", "prefill", "decode", "decode_mla",
-                                                               "prefill_engine"], default=None)
+                                                               "decode_moe", "prefill_engine"], default=None)
     ap.add_argument("--launches", type=int, default=12)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -937,6 +950,9 @@ def main():
         return
     if args.ncu_case == "decode_mla":
         run_decode_mla_case(args.launches)
+        return
+    if args.ncu_case == "decode_moe":
+        run_decode_moe_case(args.launches)
         return
     if args.ncu_case == "prefill_engine":
         run_prefill_engine_case(args.launches)
