@@ -9,10 +9,15 @@
 // :275-282).  Unlike the reference there is no silent fallback in here: a
 // declined op returns 0 and the caller decides.
 #pragma once
+#include <algorithm>
+#include <atomic>
 #include <chrono>
+#include <condition_variable>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -61,6 +66,95 @@ constexpr size_t PREFILL_MIN_TOKENS = 16;  // sb_matmul: from this many tokens o
 struct sb_engine;                  // whole-token decode state (engine.cuh)
 void sb_engine_free(sb_engine *e);
 void sb_pf_free(void *p);          // its block-prefill state (prefill_engine.cuh)
+// The host copies of a call between the caller's (pageable) buffers and the pinned staging
+// buffer, spread over a few threads: one thread copies at ~10 GB/s, which for a batch of
+// matvecs (1.5 MB of x and y for the configs[1] sweep) takes longer than the kernels.  The
+// calling thread takes part 0 of the bytes, the workers the rest; workers spin for a short
+// while after a job (calls tend to come back to back) and then sleep.
+struct HostCopy {
+    void *dst;
+    const void *src;
+    size_t n;
+};
+
+class CopyPool {
+  public:
+    explicit CopyPool(int workers)
+    {
+        for (int i = 0; i < workers; i++) th_.emplace_back([this, i] { loop(i + 1); });
+    }
+    ~CopyPool()
+    {
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            stop_.store(true);
+        }
+        cv_.notify_all();
+        for (auto &t : th_) t.join();
+    }
+    // All copies done when it returns.
+    void run(const std::vector<HostCopy> &c)
+    {
+        size_t total = 0;
+        for (const HostCopy &h : c) total += h.n;
+        if (th_.empty() || total < (128u << 10)) {
+            for (const HostCopy &h : c) memcpy(h.dst, h.src, h.n);
+            return;
+        }
+        jobs_ = c.data(), njobs_ = c.size(), total_ = total;
+        left_.store((int)th_.size(), std::memory_order_relaxed);
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            gen_.fetch_add(1, std::memory_order_release);
+        }
+        cv_.notify_all();
+        part(0);
+        while (left_.load(std::memory_order_acquire) > 0) std::this_thread::yield();
+    }
+
+  private:
+    // bytes [total * p / parts, total * (p + 1) / parts) of the copies, in list order
+    void part(int p)
+    {
+        const size_t parts = th_.size() + 1, b0 = total_ * p / parts, b1 = total_ * (p + 1) / parts;
+        size_t at = 0;
+        for (size_t i = 0; i < njobs_ && at < b1; i++) {
+            const HostCopy &h = jobs_[i];
+            const size_t s = std::max(at, b0), e = std::min(at + h.n, b1);
+            if (s < e) memcpy((char *)h.dst + (s - at), (const char *)h.src + (s - at), e - s);
+            at += h.n;
+        }
+    }
+    void loop(int id)
+    {
+        unsigned seen = 0;
+        for (;;) {
+            unsigned g = gen_.load(std::memory_order_acquire);
+            for (int spin = 0; g == seen && spin < 4000 && !stop_.load(); spin++) {
+                std::this_thread::yield();
+                g = gen_.load(std::memory_order_acquire);
+            }
+            if (g == seen) {
+                std::unique_lock<std::mutex> lk(mu_);
+                cv_.wait(lk, [&] { return stop_.load() || gen_.load(std::memory_order_acquire) != seen; });
+                if (stop_.load()) return;
+                g = gen_.load(std::memory_order_acquire);
+            }
+            seen = g;
+            part(id);
+            left_.fetch_sub(1, std::memory_order_release);
+        }
+    }
+    std::vector<std::thread> th_;
+    std::mutex mu_;
+    std::condition_variable cv_;
+    std::atomic<unsigned> gen_{0};
+    std::atomic<int> left_{0};
+    std::atomic<bool> stop_{false};
+    const HostCopy *jobs_ = nullptr;
+    size_t njobs_ = 0, total_ = 0;
+};
+
 struct sb_ctx;
 void sb_kv_mirror_free(const sb_ctx *c);  // KV mirrors of sb_attention_prefill (experts.cuh)
 void sb_moe_free(const sb_ctx *c);        // MoE layers of sb_moe_layer (moe_layer.cuh)
@@ -77,6 +171,16 @@ struct sb_ctx {
     size_t host_stage_bytes = 0;
     sb_stats stats = {};
     sb_group *grp = nullptr;  // tensor-parallel group (sb_group_create / sb_group_open)
+    std::unique_ptr<CopyPool> pool;  // host copies of the calls (made at the first large one)
+
+    void copy(const std::vector<HostCopy> &c)
+    {
+        if (!pool) {
+            const unsigned hw = std::thread::hardware_concurrency();
+            pool.reset(new CopyPool((int)std::min(3u, hw > 2 ? hw / 2 - 1 : 0u)));
+        }
+        pool->run(c);
+    }
 
     int ensure_host_stage(size_t bytes)
     {
@@ -399,8 +503,10 @@ extern "C" int sb_matvec_batch(sb_ctx *c, sb_matvec_op *ops, size_t nops, uint8_
     // the outputs come down in one copy (a pageable copy per op costs far more than the op)
     if (c->ensure_scratch(xend + yb) || c->ensure_host_stage(xend + yb)) return -1;
     char *base = (char *)c->scratch, *hs = (char *)c->host_stage;
+    std::vector<HostCopy> cp;
     for (size_t i = 0; i < nops; i++)
-        if (res[i]) memcpy(hs + xo[i], ops[i].x, ops[i].cols * 4);
+        if (res[i]) cp.push_back(HostCopy{hs + xo[i], ops[i].x, ops[i].cols * 4});
+    c->copy(cp);
     if ((e = cudaMemcpyAsync(base, hs, xend, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(x)", e);
     // the kernels grouped by dtype (one launch per batch of Q4_K matrices), one wait
@@ -426,8 +532,10 @@ extern "C" int sb_matvec_batch(sb_ctx *c, sb_matvec_op *ops, size_t nops, uint8_
     if ((e = cudaMemcpyAsync(hs + xend, base + xend, yb, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(out)", e);
     if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", e);
+    cp.clear();
     for (size_t i = 0; i < nops; i++)
-        if (res[i]) memcpy(ops[i].out, hs + yo[i], ops[i].rows * 4);
+        if (res[i]) cp.push_back(HostCopy{ops[i].out, hs + yo[i], ops[i].rows * 4});
+    c->copy(cp);
     for (size_t i = 0; i < nops; i++) done[i] = res[i] ? 1 : 0;
     c->stats.total_ns += now_ns() - t0;
     return 1;
