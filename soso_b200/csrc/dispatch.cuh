@@ -436,7 +436,7 @@ static int run_matvecs(sb_ctx *c, const char *key, const sb_view *w, size_t rows
     if (c->ensure_scratch(yoff + wsb) || c->ensure_host_stage(xoff + yb)) return -1;
     float *dx = (float *)c->scratch, *dy = (float *)((char *)c->scratch + xoff);
     char *hs = (char *)c->host_stage;
-    memcpy(hs, x, xb);
+    c->copy({HostCopy{hs, x, xb}});
     if ((e = cudaMemcpyAsync(dx, hs, xb, cudaMemcpyHostToDevice, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(x)", e);
     if (gemm) {
@@ -454,7 +454,7 @@ static int run_matvecs(sb_ctx *c, const char *key, const sb_view *w, size_t rows
     if ((e = cudaMemcpyAsync(hs + xoff, dy, yb, cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(out)", e);
     if ((e = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", e);
-    memcpy(out, hs + xoff, yb);
+    c->copy({HostCopy{out, hs + xoff, yb}});
     c->stats.bytes_up += xb;
     c->stats.bytes_down += yb;
     c->stats.total_ns += now_ns() - t0;

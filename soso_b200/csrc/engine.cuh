@@ -1311,8 +1311,9 @@ extern "C" int sb_decode_token(sb_ctx *c, const float *embed, size_t pos, float 
                                           cudaMemcpyDeviceToHost, c->stream)) != cudaSuccess)
         return fail("cudaMemcpyAsync(kv rows)", err);
     if ((err = cudaStreamSynchronize(c->stream)) != cudaSuccess) return fail("cudaStreamSynchronize", err);
-    memcpy(logits, hs + hb + 256, e->V * 4);
-    if (kv_rows) memcpy(kv_rows, hs + hb + 256 + lb, e->kv_rows_total * 2);
+    std::vector<HostCopy> cp{HostCopy{logits, hs + hb + 256, e->V * 4}};
+    if (kv_rows) cp.push_back(HostCopy{kv_rows, hs + hb + 256 + lb, e->kv_rows_total * 2});
+    c->copy(cp);
     e->last_pos = pos, e->traced = true;
     c->stats.launches += e->launches_per_token;
     c->stats.bytes_up += e->H * 4 + 4;
